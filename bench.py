@@ -1,0 +1,331 @@
+"""Decode benchmark: Llama-3-8B-shaped Q8_0, batch 1.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+A step is one batch-1 greedy decode token (one pass of the quantized forward
+over one token). Setup (untimed): a seeded random-init GGUF with the config-4
+shape is written (cached in $YL_BENCH_DIR, default /tmp), loaded through the
+C-ABI, and a 512-token random prompt is prefilled. Then W warm-up steps and K
+timed steps continue the sequence from position 512.
+
+  value  device-resident greedy loop (one CUDA graph launch per token, token
+         fed back on device), CUDA events on the launching stream, barrier +
+         synchronize on both sides, max over ranks.
+  e2e    the same metric through the reference-facing call yl_forward_x
+         (Transformer::forward_x): host token id in, host logits + greedy id
+         out every step (pinned buffers), timed on the host.
+  roofline  the dominant kernel (Q8_0 gate/up matvec, 4096 -> 2x14336) timed
+         alone with CUDA events, cycling through the 32 layers' weights so no
+         launch reuses L2; algorithmic bytes / duration vs measured HBM peak.
+  cpu_baseline  the CPU oracle (C++ restatement of the reference CPU path) on
+         a bounded sample of the same decode, all host cores.
+
+With N > 1 (torchrun), each rank runs an independent replica of the batch-1
+decode on its own GPU (no data-path collective); value = all ranks' tokens /
+max time.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+PKG = "yallma3-mini-inference_b200"
+PROMPT_LEN = 512
+CONFIG = "c4"
+
+
+def measured_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "src": "measured"}
+    return {"hbm_gbs": 6650.0, "src": "fallback"}
+
+
+def bytes_per_token(cfg: dict, seq: float) -> float:
+    """Algorithmic HBM bytes of one decode token: weights in file format
+    (Q8_0 = 34/32 B per element), lm_head, f32 KV reads at length seq and the
+    new K/V row writes."""
+    d, f, L, V = cfg["dim"], cfg["hidden_dim"], cfg["n_layers"], cfg["vocab_size"]
+    hd = d // cfg["n_heads"]
+    kvd = hd * cfg["n_kv_heads"]
+    per_layer = d * d + 2 * d * kvd + d * d + 3 * d * f
+    b = 34.0 / 32.0
+    return L * per_layer * b + V * d * b + L * (2 * seq * kvd * 4) + L * (2 * kvd * 4)
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], 0.0, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for ln in self.lines:
+            p = [x.strip() for x in ln.split(",")]
+            if len(p) < 9:
+                continue
+            try:
+                sm.append(float(p[1]))
+                mx = max(mx, float(p[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, p[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def ensure_model(yl, rank: int, world: int, dist) -> str:
+    cache = Path(os.environ.get("YL_BENCH_DIR", tempfile.gettempdir()))
+    path = cache / "yl_bench_c4_q8_0.gguf"
+    ok = path.with_suffix(".ok")
+    if rank == 0 and not ok.exists():
+        t = time.time()
+        yl.synth_preset(CONFIG, str(path))
+        ok.write_text(str(time.time() - t))
+    if world > 1:
+        dist.barrier()
+    return str(path)
+
+
+def time_dominant_matvec(yl, torch, model, cfg: dict, iters: int) -> dict:
+    """Q8_0 gate/up matvec (rows 2*ffn, K = dim) alone, cycling over layers."""
+    L, d, f = cfg["n_layers"], cfg["dim"], cfg["hidden_dim"]
+    ws = [model.weight(layer, 4) for layer in range(L)]
+    x = (torch.randn(d, device="cuda") * 1.0).contiguous()
+    xa = yl.new_workspace_buffer(yl.WeightFormat.Q8_0, d, 32)
+    yl.quantize(yl.WeightFormat.Q8_0, xa, x, d, 32)
+    out = torch.empty(2 * f, device="cuda")
+    st = torch.cuda.current_stream()
+    for i in range(2 * L):
+        yl.matmul(out, xa, ws[i % L], d, 2 * f, 32, batch=1, accumulate=False)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for i in range(iters):
+        yl.matmul(out, xa, ws[i % L], d, 2 * f, 32, batch=1, accumulate=False)
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / iters
+    nbytes = 2 * f * d * 34 / 32 + d + d / 32 * 4 + 2 * f * 4
+    return {"ms": ms, "bytes": nbytes, "gbs": nbytes / (ms * 1e-3) / 1e9}
+
+
+def cpu_baseline(path: str, cfg: dict, n_tokens: int, threads: int) -> dict:
+    """Oracle decode of n_tokens at positions 512.. with a seeded KV prefix."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import pyoracle as orc
+    orc.set_threads(threads)
+    t0 = time.time()
+    m = orc.Model(path, 4096)
+    load_s = time.time() - t0
+    s = m.create_session()
+    k, v = s.kv()
+    sh = m.shape
+    kvd = sh.n_kv_heads * sh.head_size
+    rng = np.random.default_rng(0)
+    for layer in range(sh.n_layers):
+        base = layer * sh.ctx_len * kvd
+        k[base:base + PROMPT_LEN * kvd] = rng.standard_normal(PROMPT_LEN * kvd).astype(np.float32)
+        v[base:base + PROMPT_LEN * kvd] = rng.standard_normal(PROMPT_LEN * kvd).astype(np.float32)
+    tok = 1
+    m.forward_x([tok], PROMPT_LEN, s)  # warm-up (page-in)
+    t = time.perf_counter()
+    for i in range(n_tokens):
+        lg = m.forward_x([tok], PROMPT_LEN + 1 + i, s)
+        tok = orc.argmax(lg)
+    dt = time.perf_counter() - t
+    return {"value": n_tokens / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{n_tokens} batch-1 decode tokens of config 4 at positions {PROMPT_LEN + 1}.. "
+                      f"(KV prefix 0..{PROMPT_LEN - 1} seeded instead of a CPU prefill), "
+                      f"oracle load {load_s:.0f}s untimed"}
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    yl = importlib.import_module(PKG)
+    cfg = yl.PRESETS[CONFIG]
+    cache = Path(os.environ.get("YL_BENCH_DIR", tempfile.gettempdir()))
+    path = cache / "yl_bench_c4_q8_0.gguf"
+    if not path.with_suffix(".ok").exists():
+        yl.synth_preset(CONFIG, str(path))
+        path.with_suffix(".ok").write_text("ok")
+    steps = max(1, min(args.steps, 8))
+    threads = os.cpu_count() or 1
+    cb = cpu_baseline(str(path), cfg, steps, threads)
+    line = {"impl": "reference", "metric": "decode tokens/s (Llama-3-8B-shape Q8_0, batch 1)",
+            "value": cb["value"], "unit": "tokens/s", "n_gpus": args.gpus, "steps": steps, "warmup": 1,
+            "ms_per_step": 1000.0 / cb["value"], "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8 dot / f32 accumulate", "data": "synthetic",
+            "config": {"workload": "config 4: Llama-3-8B-shaped Q8_0, prompt 512, batch-1 greedy decode",
+                       "global_batch": 1, "seq_len": PROMPT_LEN, "parallelism": "cpu"},
+            "cpu_baseline": cb,
+            "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--e2e-steps", type=int, default=128)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-tokens", type=int, default=3)
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    args.warmup = max(3, args.warmup)
+
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
+    yl = importlib.import_module(PKG)
+    cfg = yl.PRESETS[CONFIG]
+    path = ensure_model(yl, rank, world, dist)
+    t0 = time.time()
+    model = yl.load_transformer(path, max_ctx_len=4096)
+    load_s = time.time() - t0
+    sess = model.create_session()
+    prompt = yl.prompt_ids(cfg["vocab_size"], PROMPT_LEN, cfg["seed"] + 1000)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    _, tok = model.forward_x_full(prompt, 0, sess, want_logits=False)
+    prefill_s = time.perf_counter() - t0
+    pos = PROMPT_LEN
+    # warm-up through the device graph
+    ids = model.decode_greedy(sess, tok, pos, args.warmup)
+    pos += args.warmup
+    tok = int(ids[-1])
+    stream = torch.cuda.current_stream()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record(stream)
+        model.decode_greedy(sess, tok, pos, args.steps, stream=stream, sync=False)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    pos += args.steps
+    tok = 1
+    # e2e through the reference-facing call (host in / host out)
+    e2e_steps = min(args.e2e_steps, args.steps)
+    logits = torch.empty(cfg["vocab_size"], dtype=torch.float32).pin_memory().numpy()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for i in range(e2e_steps):
+        _, tok = model.forward_x_full([tok], pos + i, sess, want_logits=True, logits_out=logits)
+    e2e_s = time.perf_counter() - t0
+    if world > 1:
+        t = torch.tensor([e2e_s], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    # dominant kernel roofline
+    mv = time_dominant_matvec(yl, torch, model, cfg, 96)
+    peaks = measured_peaks()
+    seq_avg = PROMPT_LEN + args.warmup + args.steps / 2.0
+    btok = bytes_per_token(cfg, seq_avg)
+    tokps = world * args.steps / (ms * 1e-3)
+    line = {
+        "metric": "decode tokens/s (Llama-3-8B-shape Q8_0, batch 1)",
+        "value": tokps, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int8 dot / f32 accumulate", "data": "synthetic",
+        "config": {"workload": "config 4: Llama-3-8B-shaped Q8_0 (random-init, seed 3), prompt 512, "
+                               "batch-1 greedy decode from position 512",
+                   "model": "llama-3-8b-shape-q8_0", "global_batch": world, "seq_len": PROMPT_LEN,
+                   "parallelism": "replicas" if world > 1 else "single",
+                   "l2": "weights 8.1 GB per token > 126 MB L2 (no flush needed)"},
+        "e2e": {"value": world * e2e_steps / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": 16,
+                "d2h_bytes_per_step": 4 * cfg["vocab_size"] + 4,
+                "call": "yl_forward_x (Transformer::forward_x), logits + greedy id to host"},
+        "roofline": {"bound": "hbm", "kernel": "mv_kernel<Q8,NT=1> gate/up 28672x4096",
+                     "achieved": mv["gbs"], "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": mv["gbs"] / peaks["hbm_gbs"], "peak_src": peaks["src"], "traffic": None,
+                     "algorithmic_bytes": mv["bytes"], "launch_ms": mv["ms"]},
+        "step_roofline": {"bytes_per_token": btok, "achieved_gbs": btok / (ms / args.steps * 1e-3) / 1e9,
+                          "frac": btok / (ms / args.steps * 1e-3) / 1e9 / peaks["hbm_gbs"]},
+        "gpu_launches": model.decode_step_launches() * args.steps,
+        "clocks": clk.summary(),
+        "prefill": {"tokens": PROMPT_LEN, "s": prefill_s, "tokens_per_s": PROMPT_LEN / prefill_s},
+        "load_s": load_s,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        del model, sess
+        torch.cuda.empty_cache()
+        line["cpu_baseline"] = cpu_baseline(path, cfg, args.cpu_tokens, os.cpu_count() or 1)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

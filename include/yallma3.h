@@ -1,0 +1,218 @@
+/*
+ * yallma3_b200 — C-ABI of the B200-native quantized-weight forward path.
+ *
+ * This header is the drop-in boundary for yallma3-mini-inference's hot path.
+ * Each entry point names the reference item it replaces (path:line inside the
+ * reference project). All entry points are plain C: pointers and sizes only,
+ * no C++ or torch types. Device pointers are CUDA global-memory addresses on
+ * the current device; `stream` is a cudaStream_t passed as void* (NULL = the
+ * legacy default stream).
+ *
+ * Errors: every function that can fail returns int (YL_OK = 0, negative =
+ * error) and never aborts; yl_last_error() returns a thread-local message for
+ * the last failure on the calling thread. (The reference panics across its
+ * FFI; lib.rs:135-152 only returns false for load failures.)
+ *
+ * Threading: a yl_model may be shared by many threads (the reference's
+ * `Transformer: Send + Sync`, transformer.rs:19). A yl_session is used by one
+ * thread at a time (the reference passes `&mut InferenceSession`).
+ */
+#ifndef YALLMA3_B200_H
+#define YALLMA3_B200_H
+
+#include <stdbool.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------- */
+enum yl_status {
+  YL_OK = 0,
+  YL_ERR_ARG = -1,         /* bad argument (null pointer, size, range) */
+  YL_ERR_IO = -2,          /* file cannot be opened / read */
+  YL_ERR_FORMAT = -3,      /* malformed file, or format/variant mismatch
+                              (the reference panics: weight_type.rs:141,157) */
+  YL_ERR_CUDA = -4,        /* CUDA runtime error */
+  YL_ERR_OOM = -5,         /* device allocation failed */
+  YL_ERR_RANGE = -6,       /* position beyond the session's ctx_len */
+  YL_ERR_TIMEOUT = -7,     /* a bounded device wait expired */
+  YL_ERR_UNSUPPORTED = -8, /* valid request the device path does not support */
+  YL_ERR_COMM = -9         /* tensor-parallel communicator error */
+};
+
+/* WeightFormat (weight_type.rs:70-75). */
+enum yl_weight_format { YL_Q8_0 = 0, YL_Q4_0 = 1, YL_F16 = 2 };
+
+/* Scale element type of a yl_qtensor. */
+enum yl_scale_type { YL_SCALE_F32 = 0, YL_SCALE_F16 = 1 };
+
+/* Q4_0 decode semantics (see DESIGN.md "Resolved deviations"). */
+enum yl_q4_mode { YL_Q4_GGML = 0 };
+
+/* RoPE variants: util.rs:653-718 `rope_gguf` (pairs 2k,2k+1) and
+ * util.rs:589-635 `rope` (pairs j, j+hd/2, llama3 frequency scaling). */
+enum yl_rope_mode { YL_ROPE_GGUF = 0, YL_ROPE_LLAMA3 = 1 };
+
+const char* yl_last_error(void);
+/* Library version string, e.g. "yallma3_b200 0.1 sm_100a". */
+const char* yl_version(void);
+
+/* ---- quantized tensors (weight_type.rs:77-120, quantization.rs:23-27) ----
+ *
+ * Two kinds share one struct:
+ *  - activation tensors (rows == 0): the reference's flat containers.
+ *    Q8_0 / Q4_0: `quant` int8[len], `scale` f32[len/gs]. F16 format keeps
+ *    activations unquantized: `quant` f32[len], `scale` NULL
+ *    (F16Kernel::quantize copies, forward.rs:78-81).
+ *  - weight tensors (rows > 0, cols = row length): the repacked HBM layout.
+ *    Q8_0: `quant` int8 [rows][cols]; Q4_0: `quant` GGML nibbles
+ *    [rows][cols/2] (byte j of a block: low nibble = element j, high nibble =
+ *    element j+16, value (q-8)*d); F16: `quant` f16 [rows][cols].
+ *    `scale` [rows][scale_stride] of f16 (or f32), scale_stride padded so that
+ *    every row starts on a 16-byte boundary.
+ * Memory is owned by the library when allocated with yl_qtensor_alloc*.
+ */
+typedef struct yl_qtensor {
+  int32_t fmt;         /* yl_weight_format */
+  int32_t scale_type;  /* yl_scale_type */
+  uint64_t len;        /* element count */
+  uint64_t gs;         /* group size (32 on the device path) */
+  uint64_t rows, cols; /* weights: matrix shape; activations: 0, 0 */
+  uint64_t scale_stride;
+  void* quant;
+  void* scale;
+  int32_t owned;       /* 1 if freed by yl_qtensor_free */
+  int32_t _pad;
+} yl_qtensor;
+
+/* new_workspace_buffer (weight_type.rs:161-173): zeroed activation tensor. */
+int yl_qtensor_alloc(int fmt, uint64_t len, uint64_t gs, yl_qtensor* out);
+/* Weight tensor [rows][cols] in the repacked layout (zeroed). */
+int yl_qtensor_alloc_weight(int fmt, int scale_type, uint64_t rows, uint64_t cols, uint64_t gs,
+                            yl_qtensor* out);
+int yl_qtensor_free(yl_qtensor* t);
+/* Copy host data in the reference container layout into `t`:
+ *  Q8_0/Q4_0 activation or weight: q int8[len] (for Q4_0 weights: signed
+ *  values q-8 in [-8,7]), scales f32[len/gs]; F16: values f32[len] (weights
+ *  are rounded to f16; activations stay f32), scales NULL. Weight scales are
+ *  stored as f16 when t->scale_type == YL_SCALE_F16 (exact only if every scale
+ *  is an f16 value, as for GGUF weights). */
+int yl_qtensor_upload(yl_qtensor* t, const int8_t* q, const float* scales, const float* values);
+/* Inverse of yl_qtensor_upload (host buffers sized as above). */
+int yl_qtensor_download(const yl_qtensor* t, int8_t* q, float* scales, float* values);
+
+/* quantization.rs:29-52 `quantize`: per group of gs, scale = absmax/127 (f32),
+ * q = round-half-away(x/scale) saturated to int8, NaN -> 0. Bit-exact with the
+ * reference. x, q, scale are device pointers; floor(n/gs) groups are written. */
+int yl_quantize_q8_0(const float* x, int8_t* q, float* scale, uint64_t n, uint32_t gs, void* stream);
+/* weight_type.rs:129-143 `quantize(fmt, dst, x, n, gs)`: format dispatch into
+ * an activation tensor (YL_ERR_FORMAT on a variant mismatch). */
+int yl_quantize(int fmt, yl_qtensor* dst, const float* x, uint64_t n, uint32_t gs, void* stream);
+/* weight_type.rs:145-159 `matmul(out, x, w, n, o, gs)` with the batch made
+ * explicit (the reference infers it as out.len()/o). out: device f32
+ * [batch][o]. accumulate = 1 reproduces the reference's store semantics
+ * exactly (columns < 4*floor(o/4) add into out, the rest overwrite,
+ * weight_type.rs:243-276); accumulate = 0 overwrites every column. */
+int yl_matmul(float* out, const yl_qtensor* x, const yl_qtensor* w, uint64_t n, uint64_t o, uint64_t gs,
+              uint64_t batch, int accumulate, void* stream);
+
+/* ---- model and sessions (transformer.rs:19-69, lib.rs:107-133) ---------- */
+typedef struct yl_model yl_model;
+typedef struct yl_session yl_session;
+
+/* TransformerShape (base_transformer.rs:25-44) plus the device-path switches. */
+typedef struct yl_shape {
+  uint32_t dim, hidden_dim, n_heads, head_size, n_kv_heads, vocab_size, n_layers, ctx_len;
+  float rms_norm_eps, rope_theta;
+  uint32_t group_size;
+  float rope_freq_scale, rope_ext_factor, rope_attn_factor;
+  uint32_t rope_original_ctx_len;
+  float attention_scale;
+  int32_t weight_format; /* yl_weight_format */
+  int32_t rope_mode;     /* yl_rope_mode */
+  int32_t untied_lm_head;
+  int32_t tp_rank, tp_size;
+  int32_t _pad;
+} yl_shape;
+
+/* lib.rs:107-133 `load_transformer(path, sequential, max_ctx_len, fmt_override)`.
+ * Dispatch by extension: .gguf (architecture must be "llama"). fmt_override
+ * = -1 keeps general.file_type; `sequential` selects nothing on the device
+ * path (kept for signature parity). Weights are parsed on the host, repacked
+ * and uploaded to the current CUDA device. */
+int yl_load_transformer(const char* path, int sequential, uint32_t max_ctx_len, int fmt_override,
+                        yl_model** out);
+int yl_model_free(yl_model* m);
+const char* yl_model_name(const yl_model* m);            /* Transformer::name */
+uint64_t yl_model_vocab_size(const yl_model* m);         /* Transformer::vocab_size */
+uint32_t yl_model_max_ctx_len(const yl_model* m);        /* Transformer::max_ctx_len */
+uint32_t yl_model_eos_token(const yl_model* m);          /* Transformer::eos_token */
+uint32_t yl_model_bos_token(const yl_model* m);          /* Transformer::bos_token */
+int yl_model_shape(const yl_model* m, yl_shape* out);
+/* Bytes of device memory the model's weights occupy. */
+uint64_t yl_model_device_bytes(const yl_model* m);
+/* base_transformer.rs:129-161: host f32 copies; out-of-range ids give zeros. */
+int yl_get_embeddings(const yl_model* m, uint32_t token, float* out);
+int yl_get_embeddings_batch(const yl_model* m, const uint32_t* tokens, uint64_t n, float* out);
+/* Device view of one weight matrix: which = 0 wq, 1 wk, 2 wv, 3 wo, 4 w1 (gate),
+ * 5 w2 (down), 6 w3 (up), 7 lm_head (tied embedding or output.weight).
+ * The view aliases model memory (owned = 0). */
+int yl_model_weight(const yl_model* m, uint32_t layer, int which, yl_qtensor* out);
+
+/* InferenceSession (base_transformer.rs:78-105): device KV cache f32
+ * [n_layers][ctx_len][kv_dim] for keys and values, zeroed. */
+int yl_create_session(const yl_model* m, yl_session** out);
+int yl_session_reset(yl_session* s);
+int yl_session_free(yl_session* s);
+uint32_t yl_session_pos(const yl_session* s);
+int yl_session_set_pos(yl_session* s, uint32_t pos);
+/* Device pointers of the session's KV cache (for inspection). */
+int yl_session_kv(const yl_session* s, float** key_cache, float** value_cache, uint64_t* elems);
+
+/* Transformer::forward_x (transformer.rs:44-53; forward.rs:282-297).
+ * tokens: host array of n ids at positions start_pos..start_pos+n-1. Writes the
+ * last token's logits to logits_out (host, vocab floats) and/or its greedy id
+ * (sampler.rs:67-79 semantics: lowest index among equal maxima) to
+ * argmax_out; either may be NULL. Like the reference, the caller advances the
+ * session position; this call does not. */
+int yl_forward_x(const yl_model* m, yl_session* s, const uint32_t* tokens, uint64_t n, uint32_t start_pos,
+                 float* logits_out, uint32_t* argmax_out);
+/* Device-resident greedy decode: n_steps batch-1 steps starting with
+ * `first_token` at `start_pos`, each step feeding its argmax to the next,
+ * without host round trips (one CUDA graph launch per step). tokens_out:
+ * host array of n_steps ids (NULL allowed). Runs on `stream`; returns after
+ * enqueueing when sync == 0 (tokens_out must then be NULL). */
+int yl_decode_greedy(const yl_model* m, yl_session* s, uint32_t first_token, uint32_t start_pos,
+                     uint32_t n_steps, uint32_t* tokens_out, void* stream, int sync);
+/* Number of kernel launches one batch-1 decode step issues. */
+int yl_decode_step_launches(const yl_model* m, uint32_t* out);
+
+/* ---- reference FFI (lib.rs:135-152) -------------------------------------- */
+/* Loads into a process-global slot (guarded by a mutex here; `static mut` in
+ * the reference). Returns false on any error. */
+bool load_transformer_ffi(const char* model_path);
+
+/* ---- synthetic model files (test and bench inputs) ----------------------- */
+typedef struct yl_synth_config {
+  uint32_t dim, hidden_dim, n_layers, n_heads, n_kv_heads, vocab_size, context_length;
+  float rope_theta, rms_norm_eps;
+  int32_t weight_format; /* yl_weight_format */
+  int32_t tied;          /* 0 writes output.weight */
+  int32_t llama3_scaling;
+  float llama3_factor, llama3_low, llama3_high;
+  uint32_t llama3_orig_ctx;
+  uint64_t seed;
+  float weight_std;
+  int32_t threads;
+} yl_synth_config;
+/* Writes a GGUF v3 llama model with weights ~ N(0, weight_std) from a
+ * counter-based generator (seeded), norms = 1.0, a dummy token list. */
+int yl_synth_write_gguf(const char* path, const yl_synth_config* cfg);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* YALLMA3_B200_H */

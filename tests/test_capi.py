@@ -1,0 +1,100 @@
+"""CPU: the C-ABI library loads, exports every function include/yallma3.h
+declares, and rejects bad inputs with status codes (no GPU needed)."""
+from __future__ import annotations
+
+import ctypes as C
+import re
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def declared_functions() -> list[str]:
+    src = (ROOT / "include" / "yallma3.h").read_text()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    names = re.findall(r"^\s*(?:const\s+)?[A-Za-z_][A-Za-z0-9_]*\s*\**\s*([A-Za-z_][A-Za-z0-9_]*)\s*\(", src, re.M)
+    return sorted(set(n for n in names if n not in {"if", "return", "sizeof"}))
+
+
+def test_header_symbols_exported(yl):
+    lib = yl.raw_lib()
+    names = declared_functions()
+    assert "yl_matmul" in names and "load_transformer_ffi" in names and "yl_forward_x" in names
+    missing = [n for n in names if not hasattr(lib, n)]
+    assert not missing, missing
+    # the Python mirror binds every declared function
+    assert set(names) <= set(yl.EXPORTED), set(names) - set(yl.EXPORTED)
+
+
+def test_version(yl):
+    assert "sm_100a" in yl.version()
+
+
+def test_load_errors_without_gpu(yl, tmp_path):
+    with pytest.raises(yl.YlError) as e:
+        yl.load_transformer(str(tmp_path / "missing.gguf"))
+    assert e.value.code == -2  # YL_ERR_IO
+    with pytest.raises(yl.YlError) as e:
+        yl.load_transformer(str(tmp_path / "model.bin"))
+    assert e.value.code == -1  # unsupported extension (lib.rs:131)
+    with pytest.raises(yl.YlError) as e:
+        yl.load_transformer(str(tmp_path / "model.safetensors"))
+    assert e.value.code == -8
+    bad = tmp_path / "bad.gguf"
+    bad.write_bytes(b"NOTGGUF" + bytes(64))
+    with pytest.raises(yl.YlError) as e:
+        yl.load_transformer(str(bad))
+    assert e.value.code == -3 and "magic" in str(e.value)
+    v2 = tmp_path / "v2.gguf"
+    v2.write_bytes(b"GGUF" + (2).to_bytes(4, "little") + bytes(16))
+    with pytest.raises(yl.YlError) as e:
+        yl.load_transformer(str(v2))
+    assert e.value.code == -3 and "version 3" in str(e.value)
+
+
+def test_truncated_gguf_rejected(yl, tmp_path, model_factory):
+    data = Path(model_factory("tiny")).read_bytes()
+    t = tmp_path / "trunc.gguf"
+    t.write_bytes(data[:200])
+    with pytest.raises(yl.YlError) as e:
+        yl.load_transformer(str(t))
+    assert e.value.code == -3
+
+
+def test_ffi_returns_false_on_error(yl, tmp_path):
+    assert yl.load_transformer_ffi(None) is False
+    assert yl.load_transformer_ffi(str(tmp_path / "nope.gguf")) is False
+
+
+def test_null_arguments(yl):
+    lib = yl.raw_lib()
+    assert lib.yl_matmul(None, None, None, 0, 0, 32, 0, 0, None) == -1
+    assert lib.yl_quantize_q8_0(None, None, None, 64, 16, None) == -8  # group size 16 unsupported on device
+    assert lib.yl_model_vocab_size(None) == 0
+
+
+def test_synth_gguf_parsed_by_oracle(yl, orc, model_factory):
+    for preset, fmt in (("tiny", 0), ("tiny128", 0)):
+        m = orc.Model(model_factory(preset), 4096)
+        cfg = yl.PRESETS[preset]
+        assert m.shape.dim == cfg["dim"] and m.shape.vocab_size == cfg["vocab_size"]
+        assert m.shape.head_size == cfg["dim"] // cfg["n_heads"]
+        assert m.shape.untied_lm_head == (0 if cfg["tied"] else 1)
+        assert m.shape.weight_format == fmt
+
+
+def test_synth_deterministic(yl, tmp_path):
+    a = yl.synth_preset("tiny", str(tmp_path / "a.gguf"), threads=1)
+    b = yl.synth_preset("tiny", str(tmp_path / "b.gguf"), threads=7)
+    assert Path(a).read_bytes() == Path(b).read_bytes()
+    c = yl.synth_preset("tiny", str(tmp_path / "c.gguf"), seed=99)
+    assert Path(a).read_bytes() != Path(c).read_bytes()
+
+
+def test_synth_weight_statistics(yl, orc, model_factory):
+    m = orc.Model(model_factory("tiny128"), 512)
+    e = np.concatenate([m.get_embeddings(t) for t in range(64)])
+    assert abs(float(e.std()) - 0.02) < 0.002 and abs(float(e.mean())) < 0.002

@@ -1,0 +1,133 @@
+"""GPU parity of the full forward (Transformer::forward_x) against the CPU
+oracle on seeded synthetic GGUF models.
+
+Bar: logits within 1e-2 * max|logit| of the oracle at
+every step; greedy token ids identical over the whole run."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_TOL = 1e-2
+
+
+def close_logits(got: np.ndarray, ref: np.ndarray) -> float:
+    return float(np.max(np.abs(got - ref)) / max(1e-30, float(np.max(np.abs(ref)))))
+
+
+def run_pair(yl, orc, path, prompt, n_gen, max_ctx, fmt_override=None):
+    """Prefill `prompt`, then greedy-decode n_gen tokens on device and oracle.
+    Returns per-step relative logit errors and both id sequences."""
+    gm = yl.load_transformer(path, max_ctx_len=max_ctx, fmt_override=fmt_override)
+    om = orc.Model(path, max_ctx, -1 if fmt_override is None else int(fmt_override))
+    gs, os_ = gm.create_session(), om.create_session()
+    errs, gids, oids = [], [], []
+    lg, am = gm.forward_x_full(prompt, 0, gs)
+    lo = om.forward_x(prompt, 0, os_)
+    errs.append(close_logits(lg, lo))
+    gid, oid = am, orc.argmax(lo)
+    assert gid == int(np.argmax(lg)) or lg[gid] == lg.max()
+    pos = len(prompt)
+    for _ in range(n_gen):
+        gids.append(gid)
+        oids.append(oid)
+        lg, am = gm.forward_x_full([gid], pos, gs)
+        lo = om.forward_x([oid], pos, os_)
+        errs.append(close_logits(lg, lo))
+        gid, oid = am, orc.argmax(lo)
+        pos += 1
+    return errs, gids, oids, gm, gs
+
+
+@pytest.mark.parametrize("preset,over", [
+    ("tiny", {}),
+    ("tiny128", {}),
+    ("tiny", {"weight_format": 1}),
+    ("tiny", {"weight_format": 2}),
+    ("tiny", {"llama3_scaling": True, "rope_theta": 5e5, "context_length": 131072}),
+    ("tiny128", {"weight_format": 1, "tied": True}),
+])
+def test_tiny_models_match_oracle(yl, orc, model_factory, preset, over):
+    path = model_factory(preset, **over)
+    vocab = yl.PRESETS[preset]["vocab_size"]
+    prompt = yl.prompt_ids(vocab, 9, 1234).tolist()
+    errs, gids, oids, _, _ = run_pair(yl, orc, path, prompt, 24, 256)
+    assert max(errs) < LOGIT_TOL, errs
+    assert gids == oids
+
+
+def test_decode_graph_matches_host_loop(yl, orc, model_factory):
+    path = model_factory("tiny128")
+    gm = yl.load_transformer(path, max_ctx_len=512)
+    prompt = yl.prompt_ids(1000, 12, 5).tolist()
+    s1 = gm.create_session()
+    _, first = gm.forward_x_full(prompt, 0, s1, want_logits=False)
+    dev_ids = gm.decode_greedy(s1, first, len(prompt), 40)
+    s2 = gm.create_session()
+    _, tok = gm.forward_x_full(prompt, 0, s2, want_logits=False)
+    host_ids = []
+    for i in range(40):
+        _, nxt = gm.forward_x_full([tok], len(prompt) + i, s2, want_logits=False)
+        host_ids.append(nxt)
+        tok = nxt
+    assert dev_ids.tolist() == host_ids
+
+
+def test_prefill_equals_stepwise_on_device(yl, model_factory):
+    path = model_factory("tiny")
+    gm = yl.load_transformer(path, max_ctx_len=256)
+    toks = [3, 17, 99, 5, 250, 1, 77, 200, 12, 9]
+    a, _ = gm.forward_x_full(toks, 0, gm.create_session())
+    s = gm.create_session()
+    for i, t in enumerate(toks):
+        b, _ = gm.forward_x_full([t], i, s)
+    assert close_logits(a, b) < 1e-4
+
+
+def test_c1_smollm_shape_128_steps(yl, orc, model_factory):
+    """SmolLM2-135M shape, Q8_0, seed 0, prompt of 16 random
+    ids, 128 greedy steps, max_ctx 512."""
+    path = model_factory("c1")
+    prompt = yl.prompt_ids(49152, 16, 1000).tolist()
+    errs, gids, oids, _, _ = run_pair(yl, orc, path, prompt, 128, 512)
+    assert max(errs) < LOGIT_TOL, max(errs)
+    assert gids == oids
+
+
+def test_embeddings_match_oracle(yl, orc, model_factory):
+    path = model_factory("tiny128")
+    gm = yl.load_transformer(path, max_ctx_len=512)
+    om = orc.Model(path, 512)
+    for t in (0, 5, 999, 1000, 123456):
+        assert np.array_equal(gm.get_embeddings(t), om.get_embeddings(t))
+    batch = gm.get_embeddings_batch([1, 2, 5000])
+    assert np.all(batch[2] == 0) and np.array_equal(batch[1], om.get_embeddings(2))
+
+
+def test_forward_errors(yl, model_factory):
+    path = model_factory("tiny")
+    gm = yl.load_transformer(path, max_ctx_len=16)
+    s = gm.create_session()
+    with pytest.raises(yl.YlError) as e:
+        gm.forward_x([1] * 4, 14, s)
+    assert e.value.code == -6
+    with pytest.raises(yl.YlError) as e:
+        gm.forward_x([], 0, s)
+    assert e.value.code == -1
+    assert gm.name() == "TransformerLlamaGguf" and gm.vocab_size() == 512 and gm.max_ctx_len() == 16
+
+
+def test_session_reset_restores_results(yl, model_factory):
+    gm = yl.load_transformer(model_factory("tiny"), max_ctx_len=64)
+    s = gm.create_session()
+    a = gm.forward_x([4, 5, 6], 0, s)
+    gm.forward_x([7, 8], 3, s)
+    s.reset()
+    b = gm.forward_x([4, 5, 6], 0, s)
+    assert np.array_equal(a, b)
+
+
+def test_ffi_load(yl, model_factory):
+    assert yl.load_transformer_ffi(model_factory("tiny")) is True

@@ -1,0 +1,461 @@
+"""Python mirror of the reference's API for the quantized forward path.
+
+The reference crate (yallma3-mini-inference) exposes, for this path:
+  * weight_type.rs:70-173  WeightFormat, QuantizedTensor, quantize, matmul,
+                           new_workspace_buffer
+  * quantization.rs:23-52  MutableQuantizedTensorQ8, quantize
+  * transformer.rs:19-69   the Transformer trait (load_model, name, vocab_size,
+                           get_embeddings[_batch], forward_x, create_session,
+                           max_ctx_len, eos_token, bos_token)
+  * base_transformer.rs:78-105  InferenceSession (caller advances `pos`)
+  * lib.rs:107-152         load_transformer, load_transformer_ffi
+This module keeps those names and argument meanings and forwards every call to
+the C-ABI of libyallma3_b200.so (include/yallma3.h), which runs the sm_100a
+kernels. There is no CPU fallback: without the built library, importing this
+module raises. Where the reference panics (format/variant mismatch), these
+functions raise YlError.
+
+Device tensors are passed as torch CUDA tensors (or raw integer device
+addresses); torch is only the allocator here.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import enum
+import os
+from pathlib import Path
+from typing import Optional, Sequence
+
+import numpy as np
+
+_PKG = Path(__file__).resolve().parent
+LIB_PATH = _PKG / "libyallma3_b200.so"
+
+if not LIB_PATH.exists():
+    raise ImportError(f"{LIB_PATH} is not built; run `python {_PKG / 'build.py'}` (nvcc, sm_100a)")
+
+_lib = C.CDLL(str(LIB_PATH))
+
+# ---------------------------------------------------------------- structs --
+
+
+class QTensorC(C.Structure):
+    _fields_ = [("fmt", C.c_int32), ("scale_type", C.c_int32), ("len", C.c_uint64), ("gs", C.c_uint64),
+                ("rows", C.c_uint64), ("cols", C.c_uint64), ("scale_stride", C.c_uint64),
+                ("quant", C.c_void_p), ("scale", C.c_void_p), ("owned", C.c_int32), ("_pad", C.c_int32)]
+
+
+class ShapeC(C.Structure):
+    _fields_ = [(n, C.c_uint32) for n in ("dim", "hidden_dim", "n_heads", "head_size", "n_kv_heads", "vocab_size",
+                                          "n_layers", "ctx_len")] + [
+        ("rms_norm_eps", C.c_float), ("rope_theta", C.c_float), ("group_size", C.c_uint32),
+        ("rope_freq_scale", C.c_float), ("rope_ext_factor", C.c_float), ("rope_attn_factor", C.c_float),
+        ("rope_original_ctx_len", C.c_uint32), ("attention_scale", C.c_float), ("weight_format", C.c_int32),
+        ("rope_mode", C.c_int32), ("untied_lm_head", C.c_int32), ("tp_rank", C.c_int32), ("tp_size", C.c_int32),
+        ("_pad", C.c_int32)]
+
+
+class SynthC(C.Structure):
+    _fields_ = [(n, C.c_uint32) for n in ("dim", "hidden_dim", "n_layers", "n_heads", "n_kv_heads", "vocab_size",
+                                          "context_length")] + [
+        ("rope_theta", C.c_float), ("rms_norm_eps", C.c_float), ("weight_format", C.c_int32),
+        ("tied", C.c_int32), ("llama3_scaling", C.c_int32), ("llama3_factor", C.c_float),
+        ("llama3_low", C.c_float), ("llama3_high", C.c_float), ("llama3_orig_ctx", C.c_uint32),
+        ("seed", C.c_uint64), ("weight_std", C.c_float), ("threads", C.c_int32)]
+
+
+_P = C.c_void_p
+_sigs = {
+    "yl_last_error": (C.c_char_p, []),
+    "yl_version": (C.c_char_p, []),
+    "yl_qtensor_alloc": (C.c_int, [C.c_int, C.c_uint64, C.c_uint64, C.POINTER(QTensorC)]),
+    "yl_qtensor_alloc_weight": (C.c_int, [C.c_int, C.c_int, C.c_uint64, C.c_uint64, C.c_uint64,
+                                          C.POINTER(QTensorC)]),
+    "yl_qtensor_free": (C.c_int, [C.POINTER(QTensorC)]),
+    "yl_qtensor_upload": (C.c_int, [C.POINTER(QTensorC), _P, _P, _P]),
+    "yl_qtensor_download": (C.c_int, [C.POINTER(QTensorC), _P, _P, _P]),
+    "yl_quantize_q8_0": (C.c_int, [_P, _P, _P, C.c_uint64, C.c_uint32, _P]),
+    "yl_quantize": (C.c_int, [C.c_int, C.POINTER(QTensorC), _P, C.c_uint64, C.c_uint32, _P]),
+    "yl_matmul": (C.c_int, [_P, C.POINTER(QTensorC), C.POINTER(QTensorC), C.c_uint64, C.c_uint64, C.c_uint64,
+                            C.c_uint64, C.c_int, _P]),
+    "yl_load_transformer": (C.c_int, [C.c_char_p, C.c_int, C.c_uint32, C.c_int, C.POINTER(_P)]),
+    "yl_model_free": (C.c_int, [_P]),
+    "yl_model_name": (C.c_char_p, [_P]),
+    "yl_model_vocab_size": (C.c_uint64, [_P]),
+    "yl_model_max_ctx_len": (C.c_uint32, [_P]),
+    "yl_model_eos_token": (C.c_uint32, [_P]),
+    "yl_model_bos_token": (C.c_uint32, [_P]),
+    "yl_model_shape": (C.c_int, [_P, C.POINTER(ShapeC)]),
+    "yl_model_device_bytes": (C.c_uint64, [_P]),
+    "yl_get_embeddings": (C.c_int, [_P, C.c_uint32, _P]),
+    "yl_get_embeddings_batch": (C.c_int, [_P, _P, C.c_uint64, _P]),
+    "yl_model_weight": (C.c_int, [_P, C.c_uint32, C.c_int, C.POINTER(QTensorC)]),
+    "yl_create_session": (C.c_int, [_P, C.POINTER(_P)]),
+    "yl_session_reset": (C.c_int, [_P]),
+    "yl_session_free": (C.c_int, [_P]),
+    "yl_session_pos": (C.c_uint32, [_P]),
+    "yl_session_set_pos": (C.c_int, [_P, C.c_uint32]),
+    "yl_session_kv": (C.c_int, [_P, C.POINTER(_P), C.POINTER(_P), C.POINTER(C.c_uint64)]),
+    "yl_forward_x": (C.c_int, [_P, _P, _P, C.c_uint64, C.c_uint32, _P, _P]),
+    "yl_decode_greedy": (C.c_int, [_P, _P, C.c_uint32, C.c_uint32, C.c_uint32, _P, _P, C.c_int]),
+    "yl_decode_step_launches": (C.c_int, [_P, C.POINTER(C.c_uint32)]),
+    "load_transformer_ffi": (C.c_bool, [C.c_char_p]),
+    "yl_synth_write_gguf": (C.c_int, [C.c_char_p, C.POINTER(SynthC)]),
+}
+for _name, (_res, _args) in _sigs.items():
+    _f = getattr(_lib, _name)
+    _f.restype = _res
+    _f.argtypes = _args
+
+EXPORTED = tuple(_sigs)
+
+# ------------------------------------------------------------------ errors --
+
+STATUS = {0: "YL_OK", -1: "YL_ERR_ARG", -2: "YL_ERR_IO", -3: "YL_ERR_FORMAT", -4: "YL_ERR_CUDA",
+          -5: "YL_ERR_OOM", -6: "YL_ERR_RANGE", -7: "YL_ERR_TIMEOUT", -8: "YL_ERR_UNSUPPORTED", -9: "YL_ERR_COMM"}
+
+
+class YlError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"{STATUS.get(code, code)}: {msg}")
+        self.code = code
+
+
+def _check(rc: int) -> None:
+    if rc != 0:
+        raise YlError(rc, _lib.yl_last_error().decode(errors="replace"))
+
+
+def last_error() -> str:
+    return _lib.yl_last_error().decode(errors="replace")
+
+
+def version() -> str:
+    return _lib.yl_version().decode()
+
+
+def raw_lib() -> C.CDLL:
+    """The loaded C library (for direct C-ABI calls in tests and benchmarks)."""
+    return _lib
+
+
+def _ptr(t) -> Optional[int]:
+    if t is None:
+        return None
+    if isinstance(t, int):
+        return t
+    if hasattr(t, "data_ptr"):
+        return t.data_ptr()
+    if isinstance(t, np.ndarray):
+        return t.ctypes.data
+    raise TypeError(f"cannot take a pointer of {type(t)}")
+
+
+def _stream(stream) -> Optional[int]:
+    if stream is None:
+        try:
+            import torch
+            if torch.cuda.is_available():
+                return torch.cuda.current_stream().cuda_stream
+        except ImportError:
+            pass
+        return None
+    return stream if isinstance(stream, int) else stream.cuda_stream
+
+
+# ------------------------------------------------------ weight_type.rs ---
+
+class WeightFormat(enum.IntEnum):
+    """weight_type.rs:70-75"""
+    Q8_0 = 0
+    Q4_0 = 1
+    F16 = 2
+
+
+class QuantType(enum.IntEnum):
+    """quantization.rs:15-21"""
+    NONE = 0
+    Q8_0 = 1
+    Q4_0 = 2
+    F16 = 3
+
+
+SCALE_F32, SCALE_F16 = 0, 1
+
+
+class QuantizedTensor:
+    """A device-resident QuantizedTensor (weight_type.rs:83-103).
+
+    Activation tensors (the reference's flat containers) come from
+    `new_workspace_buffer`; weight matrices (repacked HBM layout) from
+    `QuantizedTensor.weight`. Views of model weights are not owned."""
+
+    def __init__(self, c: QTensorC):
+        self.c = c
+
+    @staticmethod
+    def weight(fmt: WeightFormat, rows: int, cols: int, gs: int = 32, scale_type: int = SCALE_F16):
+        c = QTensorC()
+        _check(_lib.yl_qtensor_alloc_weight(int(fmt), scale_type, rows, cols, gs, C.byref(c)))
+        return QuantizedTensor(c)
+
+    @property
+    def fmt(self) -> WeightFormat:
+        return WeightFormat(self.c.fmt)
+
+    @property
+    def len(self) -> int:
+        return self.c.len
+
+    def upload(self, quant_vals=None, scale_factor=None, values=None) -> "QuantizedTensor":
+        """Host data in the reference container layout (numpy): int8 values and
+        f32 scales per group (Q4_0 weights: signed q-8), or f32 values (F16)."""
+        q = None if quant_vals is None else np.ascontiguousarray(quant_vals, dtype=np.int8)
+        s = None if scale_factor is None else np.ascontiguousarray(scale_factor, dtype=np.float32)
+        v = None if values is None else np.ascontiguousarray(values, dtype=np.float32)
+        _check(_lib.yl_qtensor_upload(C.byref(self.c), _ptr(q), _ptr(s), _ptr(v)))
+        return self
+
+    def download(self):
+        n = self.c.len
+        if self.c.fmt == WeightFormat.F16:
+            v = np.empty(n, np.float32)
+            _check(_lib.yl_qtensor_download(C.byref(self.c), None, None, _ptr(v)))
+            return v
+        q = np.empty(n, np.int8)
+        s = np.empty(n // self.c.gs, np.float32)
+        _check(_lib.yl_qtensor_download(C.byref(self.c), _ptr(q), _ptr(s), None))
+        return q, s
+
+    def free(self) -> None:
+        if self.c.owned and self.c.quant:
+            _lib.yl_qtensor_free(C.byref(self.c))
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+def new_workspace_buffer(fmt: WeightFormat, len: int, gs: int) -> QuantizedTensor:
+    """weight_type.rs:161-173"""
+    c = QTensorC()
+    _check(_lib.yl_qtensor_alloc(int(fmt), len, gs, C.byref(c)))
+    return QuantizedTensor(c)
+
+
+def quantize(fmt: WeightFormat, dst: QuantizedTensor, x, n: int, gs: int, stream=None) -> None:
+    """weight_type.rs:129-143: quantize n values of device tensor `x` into `dst`."""
+    _check(_lib.yl_quantize(int(fmt), C.byref(dst.c), _ptr(x), n, gs, _stream(stream)))
+
+
+def quantize_q8_0(x, q, scale, n: int, gs: int = 32, stream=None) -> None:
+    """quantization.rs:29-52 on device pointers / tensors (bit-exact)."""
+    _check(_lib.yl_quantize_q8_0(_ptr(x), _ptr(q), _ptr(scale), n, gs, _stream(stream)))
+
+
+def matmul(out, x: QuantizedTensor, w: QuantizedTensor, n: int, o: int, gs: int, batch: Optional[int] = None,
+           accumulate: bool = True, stream=None) -> None:
+    """weight_type.rs:145-159. batch defaults to out.numel() // o like the
+    reference. accumulate=True reproduces the reference's `+=` on the first
+    4*floor(o/4) columns."""
+    if batch is None:
+        batch = out.numel() // o
+    _check(_lib.yl_matmul(_ptr(out), C.byref(x.c), C.byref(w.c), n, o, gs, batch, 1 if accumulate else 0,
+                          _stream(stream)))
+
+
+# -------------------------------------------------- transformer.rs ---
+
+class InferenceSession:
+    """base_transformer.rs:78-105: device KV cache; the caller advances pos."""
+
+    def __init__(self, handle: int, model: "Transformer"):
+        self._h = handle
+        self._model = model
+        self.pos = 0
+
+    def reset(self) -> None:
+        _check(_lib.yl_session_reset(self._h))
+        self.pos = 0
+
+    def kv_cache(self):
+        k, v, n = _P(), _P(), C.c_uint64()
+        _check(_lib.yl_session_kv(self._h, C.byref(k), C.byref(v), C.byref(n)))
+        return k.value, v.value, n.value
+
+    def close(self) -> None:
+        if self._h:
+            _lib.yl_session_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Transformer:
+    """The Transformer trait (transformer.rs:19-69) over a device model."""
+
+    def __init__(self, handle: int):
+        self._h = handle
+
+    @classmethod
+    def load_model(cls, model_path: str, max_ctx_len: int = 0xFFFFFFFF) -> "Transformer":
+        return load_transformer(model_path, False, max_ctx_len, None)
+
+    def name(self) -> str:
+        return _lib.yl_model_name(self._h).decode()
+
+    def vocab_size(self) -> int:
+        return int(_lib.yl_model_vocab_size(self._h))
+
+    def max_ctx_len(self) -> int:
+        return int(_lib.yl_model_max_ctx_len(self._h))
+
+    def eos_token(self) -> int:
+        return int(_lib.yl_model_eos_token(self._h))
+
+    def bos_token(self) -> int:
+        return int(_lib.yl_model_bos_token(self._h))
+
+    def tokenizer(self):
+        return None
+
+    def shape(self) -> ShapeC:
+        s = ShapeC()
+        _check(_lib.yl_model_shape(self._h, C.byref(s)))
+        return s
+
+    def device_bytes(self) -> int:
+        return int(_lib.yl_model_device_bytes(self._h))
+
+    def get_embeddings(self, token: int) -> np.ndarray:
+        out = np.empty(self.shape().dim, np.float32)
+        _check(_lib.yl_get_embeddings(self._h, token, _ptr(out)))
+        return out
+
+    def get_embeddings_batch(self, tokens: Sequence[int]) -> list:
+        t = np.ascontiguousarray(tokens, dtype=np.uint32)
+        d = self.shape().dim
+        out = np.empty((len(t), d), np.float32)
+        _check(_lib.yl_get_embeddings_batch(self._h, _ptr(t), len(t), _ptr(out)))
+        return [row for row in out]
+
+    def create_session(self) -> InferenceSession:
+        h = _P()
+        _check(_lib.yl_create_session(self._h, C.byref(h)))
+        return InferenceSession(h.value, self)
+
+    def forward_x(self, tokens: Sequence[int], start_pos: int, session: InferenceSession) -> np.ndarray:
+        """Logits of the last token (length vocab_size), like forward.rs:261-279."""
+        logits, _ = self.forward_x_full(tokens, start_pos, session, want_logits=True)
+        return logits
+
+    def forward_x_full(self, tokens, start_pos: int, session: InferenceSession, want_logits: bool = True,
+                       logits_out: Optional[np.ndarray] = None):
+        t = np.ascontiguousarray(tokens, dtype=np.uint32)
+        logits = None
+        if want_logits:
+            logits = logits_out if logits_out is not None else np.empty(self.vocab_size(), np.float32)
+        am = np.zeros(1, np.uint32)
+        _check(_lib.yl_forward_x(self._h, session._h, _ptr(t), len(t), start_pos, _ptr(logits), _ptr(am)))
+        return logits, int(am[0])
+
+    def decode_greedy(self, session: InferenceSession, first_token: int, start_pos: int, n_steps: int,
+                      stream=None, sync: bool = True) -> Optional[np.ndarray]:
+        """n_steps device-resident greedy steps (one CUDA graph launch each)."""
+        out = np.empty(n_steps, np.uint32) if sync else None
+        _check(_lib.yl_decode_greedy(self._h, session._h, first_token, start_pos, n_steps, _ptr(out),
+                                     _stream(stream) if stream is not None else None, 1 if sync else 0))
+        return out
+
+    def decode_step_launches(self) -> int:
+        n = C.c_uint32()
+        _check(_lib.yl_decode_step_launches(self._h, C.byref(n)))
+        return n.value
+
+    def weight(self, layer: int, which: int) -> QuantizedTensor:
+        c = QTensorC()
+        _check(_lib.yl_model_weight(self._h, layer, which, C.byref(c)))
+        return QuantizedTensor(c)
+
+    def close(self) -> None:
+        if self._h:
+            _lib.yl_model_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def load_transformer(model_path: str, sequential: bool = False, max_ctx_len: int = 0xFFFFFFFF,
+                     fmt_override: Optional[WeightFormat] = None) -> Transformer:
+    """lib.rs:107-133"""
+    h = _P()
+    _check(_lib.yl_load_transformer(str(model_path).encode(), 1 if sequential else 0, max_ctx_len,
+                                    -1 if fmt_override is None else int(fmt_override), C.byref(h)))
+    return Transformer(h.value)
+
+
+def load_transformer_ffi(model_path: Optional[str]) -> bool:
+    """lib.rs:135-152"""
+    return bool(_lib.load_transformer_ffi(None if model_path is None else str(model_path).encode()))
+
+
+# -------------------------------------------------- synthetic models ---
+
+# C1 SmolLM2-135M-shaped, C2/C3 Llama-3.2-1B-shaped (Q8_0 /
+# Q4_0), C4 Llama-3-8B-shaped (untied lm_head); plus tiny shapes for tests.
+PRESETS = {
+    "c1": dict(dim=576, hidden_dim=1536, n_layers=30, n_heads=9, n_kv_heads=3, vocab_size=49152,
+               context_length=2048, rope_theta=1e5, rms_norm_eps=1e-5, weight_format=WeightFormat.Q8_0, tied=True,
+               seed=0),
+    "c2": dict(dim=2048, hidden_dim=8192, n_layers=16, n_heads=32, n_kv_heads=8, vocab_size=128256,
+               context_length=131072, rope_theta=5e5, rms_norm_eps=1e-5, weight_format=WeightFormat.Q8_0, tied=True,
+               llama3_scaling=True, seed=1),
+    "c3": dict(dim=2048, hidden_dim=8192, n_layers=16, n_heads=32, n_kv_heads=8, vocab_size=128256,
+               context_length=131072, rope_theta=5e5, rms_norm_eps=1e-5, weight_format=WeightFormat.Q4_0, tied=True,
+               llama3_scaling=True, seed=2),
+    "c4": dict(dim=4096, hidden_dim=14336, n_layers=32, n_heads=32, n_kv_heads=8, vocab_size=128256,
+               context_length=8192, rope_theta=5e5, rms_norm_eps=1e-5, weight_format=WeightFormat.Q8_0, tied=False,
+               seed=3),
+    "tiny": dict(dim=256, hidden_dim=512, n_layers=2, n_heads=4, n_kv_heads=2, vocab_size=512, context_length=256,
+                 rope_theta=1e4, rms_norm_eps=1e-5, weight_format=WeightFormat.Q8_0, tied=True, seed=7),
+    "tiny128": dict(dim=512, hidden_dim=1024, n_layers=2, n_heads=4, n_kv_heads=1, vocab_size=1000,
+                    context_length=512, rope_theta=5e5, rms_norm_eps=1e-5, weight_format=WeightFormat.Q8_0,
+                    tied=False, seed=8),
+}
+
+
+def synth_write_gguf(path: str, dim: int, hidden_dim: int, n_layers: int, n_heads: int, n_kv_heads: int,
+                     vocab_size: int, context_length: int = 4096, rope_theta: float = 1e4, rms_norm_eps: float = 1e-5,
+                     weight_format: WeightFormat = WeightFormat.Q8_0, tied: bool = True, llama3_scaling: bool = False,
+                     llama3_factor: float = 32.0, llama3_low: float = 1.0, llama3_high: float = 4.0,
+                     llama3_orig_ctx: int = 8192, seed: int = 0, weight_std: float = 0.02, threads: int = 0) -> str:
+    """Writes a seeded random-init LLaMA GGUF v3 (weights ~ N(0, weight_std))."""
+    c = SynthC(dim=dim, hidden_dim=hidden_dim, n_layers=n_layers, n_heads=n_heads, n_kv_heads=n_kv_heads,
+               vocab_size=vocab_size, context_length=context_length, rope_theta=rope_theta,
+               rms_norm_eps=rms_norm_eps, weight_format=int(weight_format), tied=1 if tied else 0,
+               llama3_scaling=1 if llama3_scaling else 0, llama3_factor=llama3_factor, llama3_low=llama3_low,
+               llama3_high=llama3_high, llama3_orig_ctx=llama3_orig_ctx, seed=seed, weight_std=weight_std,
+               threads=threads)
+    _check(_lib.yl_synth_write_gguf(str(path).encode(), C.byref(c)))
+    return str(path)
+
+
+def synth_preset(name: str, path: str, **overrides) -> str:
+    cfg = dict(PRESETS[name])
+    cfg.update(overrides)
+    return synth_write_gguf(path, **cfg)
+
+
+def prompt_ids(vocab: int, n: int, seed: int) -> np.ndarray:
+    """Uniform random prompt ids (seeded)."""
+    return np.random.default_rng(seed).integers(0, vocab, size=n, dtype=np.uint32)

@@ -1,0 +1,484 @@
+// extern "C" entry points declared in include/yallma3.h.
+#include <algorithm>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "model.h"
+
+struct yl_model {
+  yl::Model* m;
+};
+struct yl_session {
+  yl::Session* s;
+};
+
+namespace yl {
+namespace {
+thread_local std::string g_last_error;
+}
+void set_error(const std::string& msg) { g_last_error = msg; }
+int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+}  // namespace yl
+
+using namespace yl;
+
+extern "C" {
+
+const char* yl_last_error(void) { return g_last_error.c_str(); }
+const char* yl_version(void) { return "yallma3_b200 0.1 sm_100a"; }
+
+// ------------------------------- qtensors --------------------------------
+
+static uint64_t w_row_bytes(int fmt, uint64_t cols) {
+  return fmt == YL_Q8_0 ? cols : fmt == YL_Q4_0 ? cols / 2 : cols * 2;
+}
+
+int yl_qtensor_alloc(int fmt, uint64_t len, uint64_t gs, yl_qtensor* out) {
+  if (!out || gs == 0) return fail(YL_ERR_ARG, "null output or zero group size");
+  if (fmt != YL_Q8_0 && fmt != YL_Q4_0 && fmt != YL_F16) return fail(YL_ERR_ARG, "unknown format");
+  yl_qtensor t{};
+  t.fmt = fmt;
+  t.scale_type = YL_SCALE_F32;
+  t.len = len;
+  t.gs = gs;
+  t.owned = 1;
+  const uint64_t qbytes = fmt == YL_F16 ? len * 4 : len;
+  YL_CUDA_TRY(cudaMalloc(&t.quant, std::max<uint64_t>(qbytes, 16)));
+  YL_CUDA_TRY(cudaMemset(t.quant, 0, std::max<uint64_t>(qbytes, 16)));
+  if (fmt != YL_F16) {
+    YL_CUDA_TRY(cudaMalloc(&t.scale, std::max<uint64_t>(len / gs * 4, 16)));
+    YL_CUDA_TRY(cudaMemset(t.scale, 0, std::max<uint64_t>(len / gs * 4, 16)));
+  }
+  *out = t;
+  return YL_OK;
+}
+
+int yl_qtensor_alloc_weight(int fmt, int scale_type, uint64_t rows, uint64_t cols, uint64_t gs, yl_qtensor* out) {
+  if (!out) return fail(YL_ERR_ARG, "null output");
+  if (fmt != YL_Q8_0 && fmt != YL_Q4_0 && fmt != YL_F16) return fail(YL_ERR_ARG, "unknown format");
+  if (gs != 32) return fail(YL_ERR_UNSUPPORTED, "device weights use group size 32");
+  if (rows == 0 || cols == 0 || cols % 32) return fail(YL_ERR_ARG, "cols must be a non-zero multiple of 32");
+  if (rows > 0xFFFFFFFFull || cols > 0x3FFFFFFFull) return fail(YL_ERR_ARG, "shape too large");
+  yl_qtensor t{};
+  t.fmt = fmt;
+  t.scale_type = scale_type == YL_SCALE_F16 ? YL_SCALE_F16 : YL_SCALE_F32;
+  t.len = rows * cols;
+  t.gs = gs;
+  t.rows = rows;
+  t.cols = cols;
+  t.owned = 1;
+  const uint64_t rb = w_row_bytes(fmt, cols);
+  YL_CUDA_TRY(cudaMalloc(&t.quant, rows * rb));
+  YL_CUDA_TRY(cudaMemset(t.quant, 0, rows * rb));
+  if (fmt != YL_F16) {
+    const uint64_t ssz = t.scale_type == YL_SCALE_F16 ? 2 : 4;
+    t.scale_stride = round_up(cols / 32 * ssz, 16) / ssz;
+    YL_CUDA_TRY(cudaMalloc(&t.scale, rows * t.scale_stride * ssz));
+    YL_CUDA_TRY(cudaMemset(t.scale, 0, rows * t.scale_stride * ssz));
+  }
+  *out = t;
+  return YL_OK;
+}
+
+int yl_qtensor_free(yl_qtensor* t) {
+  if (!t) return fail(YL_ERR_ARG, "null tensor");
+  if (t->owned) {
+    if (t->quant) cudaFree(t->quant);
+    if (t->scale) cudaFree(t->scale);
+  }
+  t->quant = t->scale = nullptr;
+  return YL_OK;
+}
+
+int yl_qtensor_upload(yl_qtensor* t, const int8_t* q, const float* scales, const float* values) {
+  if (!t || !t->quant) return fail(YL_ERR_ARG, "null tensor");
+  if (t->rows == 0) {  // activation container
+    if (t->fmt == YL_F16) {
+      if (!values) return fail(YL_ERR_ARG, "F16 activations need values");
+      YL_CUDA_TRY(cudaMemcpy(t->quant, values, t->len * 4, cudaMemcpyHostToDevice));
+    } else {
+      if (!q || !scales) return fail(YL_ERR_ARG, "quantized activations need q and scales");
+      YL_CUDA_TRY(cudaMemcpy(t->quant, q, t->len, cudaMemcpyHostToDevice));
+      YL_CUDA_TRY(cudaMemcpy(t->scale, scales, t->len / t->gs * 4, cudaMemcpyHostToDevice));
+    }
+    return YL_OK;
+  }
+  const uint64_t rows = t->rows, cols = t->cols, nb = cols / 32, rb = w_row_bytes(t->fmt, cols);
+  std::vector<uint8_t> hq(rows * rb);
+  if (t->fmt == YL_F16) {
+    if (!values) return fail(YL_ERR_ARG, "F16 weights need values");
+    uint16_t* h = (uint16_t*)hq.data();
+    for (uint64_t i = 0; i < rows * cols; ++i) h[i] = f32_to_f16(values[i]);
+    YL_CUDA_TRY(cudaMemcpy(t->quant, hq.data(), hq.size(), cudaMemcpyHostToDevice));
+    return YL_OK;
+  }
+  if (!q || !scales) return fail(YL_ERR_ARG, "quantized weights need q and scales");
+  for (uint64_t r = 0; r < rows; ++r) {
+    const int8_t* src = q + r * cols;
+    uint8_t* dst = hq.data() + r * rb;
+    if (t->fmt == YL_Q8_0) {
+      memcpy(dst, src, cols);
+    } else {  // Q4_0: signed values q-8 in [-8, 7] -> GGML nibbles
+      for (uint64_t b = 0; b < nb; ++b)
+        for (int j = 0; j < 16; ++j) {
+          int lo = src[b * 32 + j] + 8, hi = src[b * 32 + 16 + j] + 8;
+          if (lo < 0 || lo > 15 || hi < 0 || hi > 15) return fail(YL_ERR_ARG, "Q4_0 value out of [-8, 7]");
+          dst[b * 16 + j] = (uint8_t)(lo | (hi << 4));
+        }
+    }
+  }
+  YL_CUDA_TRY(cudaMemcpy(t->quant, hq.data(), hq.size(), cudaMemcpyHostToDevice));
+  const uint64_t ssz = t->scale_type == YL_SCALE_F16 ? 2 : 4;
+  std::vector<uint8_t> hs(rows * t->scale_stride * ssz, 0);
+  for (uint64_t r = 0; r < rows; ++r)
+    for (uint64_t b = 0; b < nb; ++b) {
+      const float sv = scales[r * nb + b];
+      if (ssz == 2) ((uint16_t*)hs.data())[r * t->scale_stride + b] = f32_to_f16(sv);
+      else ((float*)hs.data())[r * t->scale_stride + b] = sv;
+    }
+  YL_CUDA_TRY(cudaMemcpy(t->scale, hs.data(), hs.size(), cudaMemcpyHostToDevice));
+  return YL_OK;
+}
+
+int yl_qtensor_download(const yl_qtensor* t, int8_t* q, float* scales, float* values) {
+  if (!t || !t->quant) return fail(YL_ERR_ARG, "null tensor");
+  if (t->rows == 0) {
+    if (t->fmt == YL_F16) {
+      if (values) YL_CUDA_TRY(cudaMemcpy(values, t->quant, t->len * 4, cudaMemcpyDeviceToHost));
+    } else {
+      if (q) YL_CUDA_TRY(cudaMemcpy(q, t->quant, t->len, cudaMemcpyDeviceToHost));
+      if (scales) YL_CUDA_TRY(cudaMemcpy(scales, t->scale, t->len / t->gs * 4, cudaMemcpyDeviceToHost));
+    }
+    return YL_OK;
+  }
+  const uint64_t rows = t->rows, cols = t->cols, nb = cols / 32, rb = w_row_bytes(t->fmt, cols);
+  std::vector<uint8_t> hq(rows * rb);
+  YL_CUDA_TRY(cudaMemcpy(hq.data(), t->quant, hq.size(), cudaMemcpyDeviceToHost));
+  if (t->fmt == YL_F16) {
+    if (values)
+      for (uint64_t i = 0; i < rows * cols; ++i) values[i] = f16_to_f32(((uint16_t*)hq.data())[i]);
+    return YL_OK;
+  }
+  if (q)
+    for (uint64_t r = 0; r < rows; ++r) {
+      const uint8_t* src = hq.data() + r * rb;
+      int8_t* dst = q + r * cols;
+      if (t->fmt == YL_Q8_0) memcpy(dst, src, cols);
+      else
+        for (uint64_t b = 0; b < nb; ++b)
+          for (int j = 0; j < 16; ++j) {
+            dst[b * 32 + j] = (int8_t)((src[b * 16 + j] & 0xF) - 8);
+            dst[b * 32 + 16 + j] = (int8_t)((src[b * 16 + j] >> 4) - 8);
+          }
+    }
+  if (scales) {
+    const uint64_t ssz = t->scale_type == YL_SCALE_F16 ? 2 : 4;
+    std::vector<uint8_t> hs(rows * t->scale_stride * ssz);
+    YL_CUDA_TRY(cudaMemcpy(hs.data(), t->scale, hs.size(), cudaMemcpyDeviceToHost));
+    for (uint64_t r = 0; r < rows; ++r)
+      for (uint64_t b = 0; b < nb; ++b)
+        scales[r * nb + b] = ssz == 2 ? f16_to_f32(((uint16_t*)hs.data())[r * t->scale_stride + b])
+                                      : ((float*)hs.data())[r * t->scale_stride + b];
+  }
+  return YL_OK;
+}
+
+// ------------------------------- quantize / matmul -----------------------
+
+int yl_quantize_q8_0(const float* x, int8_t* q, float* scale, uint64_t n, uint32_t gs, void* stream) {
+  if (gs != 32) return fail(YL_ERR_UNSUPPORTED, "the device quantizer uses group size 32");
+  if (n / gs == 0) return YL_OK;
+  if (!x || !q || !scale) return fail(YL_ERR_ARG, "null pointer");
+  k::LaunchCfg lc;
+  lc.stream = (cudaStream_t)stream;
+  cudaError_t e = k::quantize_q8(x, q, scale, n / gs, lc);
+  if (e != cudaSuccess) return fail(YL_ERR_CUDA, std::string("quantize: ") + cudaGetErrorString(e));
+  return YL_OK;
+}
+
+int yl_quantize(int fmt, yl_qtensor* dst, const float* x, uint64_t n, uint32_t gs, void* stream) {
+  if (!dst || !x) return fail(YL_ERR_ARG, "null pointer");
+  if (dst->fmt != fmt || dst->rows != 0) return fail(YL_ERR_FORMAT, "quantize: format/variant mismatch");
+  if (n > dst->len) return fail(YL_ERR_ARG, "n exceeds the destination length");
+  if (fmt == YL_F16) {  // F16Kernel::quantize copies (forward.rs:78-81)
+    YL_CUDA_TRY(cudaMemcpyAsync(dst->quant, x, n * 4, cudaMemcpyDeviceToDevice, (cudaStream_t)stream));
+    return YL_OK;
+  }
+  // Q8_0, and Q4_0 activations quantized as Q8_0 (GGML semantics)
+  return yl_quantize_q8_0(x, (int8_t*)dst->quant, (float*)dst->scale, n, gs, stream);
+}
+
+int yl_matmul(float* out, const yl_qtensor* x, const yl_qtensor* w, uint64_t n, uint64_t o, uint64_t gs,
+              uint64_t batch, int accumulate, void* stream) {
+  if (!out || !x || !w) return fail(YL_ERR_ARG, "null pointer");
+  if (x->fmt != w->fmt) return fail(YL_ERR_FORMAT, "matmul: format/variant mismatch or mixed formats");
+  if (w->rows == 0) return fail(YL_ERR_ARG, "w must be a weight tensor (yl_qtensor_alloc_weight)");
+  if (x->rows != 0) return fail(YL_ERR_ARG, "x must be an activation tensor");
+  if (w->rows != o || w->cols != n) return fail(YL_ERR_ARG, "w shape does not match (o, n)");
+  if (gs != 32 || w->gs != 32) return fail(YL_ERR_UNSUPPORTED, "device matmul uses group size 32");
+  if (batch * n > x->len) return fail(YL_ERR_ARG, "x is shorter than batch * n");
+  if (batch == 0 || o == 0) return YL_OK;
+  DevWeight dw;
+  dw.fmt = w->fmt;
+  dw.sf16 = w->scale_type == YL_SCALE_F16;
+  dw.rows = (uint32_t)o;
+  dw.cols = (uint32_t)n;
+  dw.row_bytes = (uint32_t)w_row_bytes(w->fmt, n);
+  dw.scale_row_bytes = w->fmt == YL_F16 ? 0 : (uint32_t)(w->scale_stride * (dw.sf16 ? 2 : 4));
+  dw.q = (uint8_t*)w->quant;
+  dw.s = (uint8_t*)w->scale;
+  const bool f32act = w->fmt == YL_F16;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return run_matvec(dw, f32act, f32act ? nullptr : (const int8_t*)x->quant, f32act ? nullptr : (const float*)x->scale,
+                    f32act ? (const float*)x->quant : nullptr, n, n / 32, (uint32_t)batch, out, o,
+                    accumulate ? k::EPI_QUIRK : k::EPI_STORE, (uint32_t)(o / 4 * 4), nullptr, (cudaStream_t)stream,
+                    false, sms);
+}
+
+// ------------------------------- model -----------------------------------
+
+int yl_load_transformer(const char* path, int sequential, uint32_t max_ctx_len, int fmt_override, yl_model** out) {
+  (void)sequential;
+  if (!path || !out) return fail(YL_ERR_ARG, "null argument");
+  std::string p(path);
+  const size_t dot = p.rfind('.');
+  const std::string ext = dot == std::string::npos ? "" : p.substr(dot + 1);
+  if (ext != "gguf") {
+    if (ext == "safetensors" || ext == "lmrs")
+      return fail(YL_ERR_UNSUPPORTED, "the device path loads .gguf files; " + ext + " upload is not built yet");
+    return fail(YL_ERR_ARG, "Unsupported model extension for path: " + p);
+  }
+  if (fmt_override < -1 || fmt_override > YL_F16) return fail(YL_ERR_ARG, "bad format override");
+  Model* m = nullptr;
+  int rc = model_load_gguf(path, max_ctx_len, fmt_override, &m);
+  if (rc) return rc;
+  *out = new yl_model{m};
+  return YL_OK;
+}
+
+int yl_model_free(yl_model* m) {
+  if (!m) return fail(YL_ERR_ARG, "null model");
+  delete m->m;
+  delete m;
+  return YL_OK;
+}
+const char* yl_model_name(const yl_model* m) { return m ? m->m->name.c_str() : ""; }
+uint64_t yl_model_vocab_size(const yl_model* m) { return m ? m->m->shape.vocab_size : 0; }
+uint32_t yl_model_max_ctx_len(const yl_model* m) { return m ? m->m->shape.ctx_len : 2048; }
+uint32_t yl_model_eos_token(const yl_model* m) { return m ? m->m->eos : 0; }
+uint32_t yl_model_bos_token(const yl_model* m) { return m ? m->m->bos : 0; }
+int yl_model_shape(const yl_model* m, yl_shape* out) {
+  if (!m || !out) return fail(YL_ERR_ARG, "null argument");
+  *out = m->m->shape;
+  return YL_OK;
+}
+uint64_t yl_model_device_bytes(const yl_model* m) { return m ? m->m->device_bytes : 0; }
+
+int yl_get_embeddings_batch(const yl_model* m, const uint32_t* tokens, uint64_t n, float* out) {
+  if (!m || (!tokens && n) || (!out && n)) return fail(YL_ERR_ARG, "null argument");
+  if (n == 0) return YL_OK;
+  const Model* mm = m->m;
+  const uint32_t d = mm->shape.dim;
+  YL_CUDA_TRY(cudaSetDevice(mm->device));
+  uint32_t* tk = nullptr;
+  float* x = nullptr;
+  YL_CUDA_TRY(cudaMalloc(&tk, n * 4));
+  cudaError_t e = cudaMalloc(&x, n * d * 4ull);
+  if (e == cudaSuccess) e = cudaMemcpy(tk, tokens, n * 4, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) {
+    k::LaunchCfg lc;
+    e = k::embed(mm->emb.fmt == YL_Q8_0 ? k::FMT_Q8 : mm->emb.fmt == YL_Q4_0 ? k::FMT_Q4 : k::FMT_F16, mm->emb.q,
+                 mm->emb.s, mm->emb.row_bytes, mm->emb.scale_row_bytes, d, mm->shape.vocab_size, tk, nullptr,
+                 (uint32_t)n, x, lc);
+  }
+  if (e == cudaSuccess) e = cudaMemcpy(out, x, n * d * 4ull, cudaMemcpyDeviceToHost);
+  cudaFree(tk);
+  cudaFree(x);
+  if (e != cudaSuccess) return fail(YL_ERR_CUDA, std::string("get_embeddings: ") + cudaGetErrorString(e));
+  return YL_OK;
+}
+int yl_get_embeddings(const yl_model* m, uint32_t token, float* out) {
+  return yl_get_embeddings_batch(m, &token, 1, out);
+}
+
+int yl_model_weight(const yl_model* m, uint32_t layer, int which, yl_qtensor* out) {
+  if (!m || !out) return fail(YL_ERR_ARG, "null argument");
+  const Model* mm = m->m;
+  const DevWeight* w = nullptr;
+  yl_qtensor t{};
+  if (which == 7) {
+    w = &mm->lm;
+  } else {
+    if (layer >= mm->layers.size() || which < 0 || which > 6) return fail(YL_ERR_ARG, "bad layer or weight id");
+    const Layer& L = mm->layers[layer];
+    switch (which) {
+      case 0: case 1: case 2: w = &L.wqkv; break;
+      case 3: w = &L.wo; break;
+      case 4: case 6: w = &L.w13; break;
+      case 5: w = &L.w2; break;
+    }
+  }
+  t.fmt = w->fmt;
+  t.scale_type = YL_SCALE_F16;
+  t.gs = 32;
+  t.cols = w->cols;
+  t.scale_stride = w->scale_row_bytes / 2;
+  t.owned = 0;
+  uint64_t r0 = 0, nr = w->rows, stride = 1;
+  const yl_shape& s = mm->shape;
+  const uint64_t att = (uint64_t)s.n_heads * s.head_size, kvd = (uint64_t)s.n_kv_heads * s.head_size;
+  if (which == 0) nr = att;
+  if (which == 1) { r0 = att; nr = kvd; }
+  if (which == 2) { r0 = att + kvd; nr = kvd; }
+  if (which == 4 || which == 6) {
+    // gate/up rows are interleaved in HBM; expose the fused pair matrix
+    r0 = 0;
+    nr = w->rows;
+    stride = 1;
+  }
+  (void)stride;
+  t.rows = nr;
+  t.len = nr * w->cols;
+  t.quant = w->q + r0 * w->row_bytes;
+  t.scale = w->s ? w->s + r0 * w->scale_row_bytes : nullptr;
+  *out = t;
+  return YL_OK;
+}
+
+// ------------------------------- sessions --------------------------------
+
+int yl_create_session(const yl_model* m, yl_session** out) {
+  if (!m || !out) return fail(YL_ERR_ARG, "null argument");
+  Session* s = nullptr;
+  int rc = session_create(m->m, &s);
+  if (rc) return rc;
+  *out = new yl_session{s};
+  return YL_OK;
+}
+int yl_session_reset(yl_session* s) {
+  if (!s) return fail(YL_ERR_ARG, "null session");
+  return session_reset(s->s);
+}
+int yl_session_free(yl_session* s) {
+  if (!s) return fail(YL_ERR_ARG, "null session");
+  delete s->s;
+  delete s;
+  return YL_OK;
+}
+uint32_t yl_session_pos(const yl_session* s) { return s ? s->s->pos : 0; }
+int yl_session_set_pos(yl_session* s, uint32_t pos) {
+  if (!s) return fail(YL_ERR_ARG, "null session");
+  if (pos > s->s->m->shape.ctx_len) return fail(YL_ERR_RANGE, "position beyond ctx_len");
+  s->s->pos = pos;
+  return YL_OK;
+}
+int yl_session_kv(const yl_session* s, float** key_cache, float** value_cache, uint64_t* elems) {
+  if (!s) return fail(YL_ERR_ARG, "null session");
+  if (key_cache) *key_cache = s->s->kcache;
+  if (value_cache) *value_cache = s->s->vcache;
+  if (elems) *elems = s->s->kv_elems;
+  return YL_OK;
+}
+
+static int check_err(Session* s) {
+  int herr = 0;
+  YL_CUDA_TRY(cudaMemcpy(&herr, s->err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (herr) {
+    cudaMemset(s->err, 0, sizeof(int));
+    return fail(YL_ERR_TIMEOUT, "a bounded device wait expired (error word " + std::to_string(herr) + ")");
+  }
+  return YL_OK;
+}
+
+int yl_forward_x(const yl_model* m, yl_session* sp, const uint32_t* tokens, uint64_t n, uint32_t start_pos,
+                 float* logits_out, uint32_t* argmax_out) {
+  if (!m || !sp || (!tokens && n)) return fail(YL_ERR_ARG, "null argument");
+  if (sp->s->m != m->m) return fail(YL_ERR_ARG, "session belongs to another model");
+  Session* s = sp->s;
+  const yl_shape& sh = m->m->shape;
+  if (n == 0) return fail(YL_ERR_ARG, "empty token batch");
+  if ((uint64_t)start_pos + n > sh.ctx_len) return fail(YL_ERR_RANGE, "position beyond ctx_len");
+  YL_CUDA_TRY(cudaSetDevice(s->device));
+  int rc;
+  if (n == 1) {  // batch-1 step through the captured decode graph
+    if ((rc = ensure_decode_graph(s))) return rc;
+    s->state_h->pos = (int32_t)start_pos;
+    s->state_h->token = (int32_t)tokens[0];
+    s->state_h->next = 0;
+    s->state_h->steps = 0;
+    YL_CUDA_TRY(cudaMemcpyAsync(s->state, s->state_h, sizeof(k::StepState), cudaMemcpyHostToDevice, s->stream));
+    YL_CUDA_TRY(cudaGraphLaunch(s->graph, s->stream));
+  } else {
+    if ((rc = forward(s, tokens, (uint32_t)n, start_pos))) return rc;
+  }
+  if (logits_out)
+    YL_CUDA_TRY(cudaMemcpyAsync(s->logits_h, s->logits, (uint64_t)sh.vocab_size * 4, cudaMemcpyDeviceToHost, s->stream));
+  YL_CUDA_TRY(cudaMemcpyAsync(s->hist_h, s->hist, 4, cudaMemcpyDeviceToHost, s->stream));
+  YL_CUDA_TRY(cudaStreamSynchronize(s->stream));
+  if ((rc = check_err(s))) return rc;
+  if (logits_out) memcpy(logits_out, s->logits_h, (uint64_t)sh.vocab_size * 4);
+  if (argmax_out) *argmax_out = s->hist_h[0];
+  return YL_OK;
+}
+
+int yl_decode_greedy(const yl_model* m, yl_session* sp, uint32_t first_token, uint32_t start_pos, uint32_t n_steps,
+                     uint32_t* tokens_out, void* stream, int sync) {
+  if (!m || !sp) return fail(YL_ERR_ARG, "null argument");
+  Session* s = sp->s;
+  const yl_shape& sh = m->m->shape;
+  if ((uint64_t)start_pos + n_steps > sh.ctx_len) return fail(YL_ERR_RANGE, "position beyond ctx_len");
+  if (!sync && tokens_out) return fail(YL_ERR_ARG, "tokens_out needs sync");
+  if (n_steps == 0) return YL_OK;
+  YL_CUDA_TRY(cudaSetDevice(s->device));
+  int rc;
+  if ((rc = ensure_decode_graph(s))) return rc;
+  cudaStream_t st = stream ? (cudaStream_t)stream : s->stream;
+  s->state_h->pos = (int32_t)start_pos;
+  s->state_h->token = (int32_t)first_token;
+  s->state_h->next = 0;
+  s->state_h->steps = 0;
+  YL_CUDA_TRY(cudaMemcpyAsync(s->state, s->state_h, sizeof(k::StepState), cudaMemcpyHostToDevice, st));
+  for (uint32_t i = 0; i < n_steps; ++i) YL_CUDA_TRY(cudaGraphLaunch(s->graph, st));
+  if (!sync) return YL_OK;
+  if (tokens_out)
+    YL_CUDA_TRY(cudaMemcpyAsync(s->hist_h, s->hist, (uint64_t)n_steps * 4, cudaMemcpyDeviceToHost, st));
+  YL_CUDA_TRY(cudaStreamSynchronize(st));
+  if ((rc = check_err(s))) return rc;
+  if (tokens_out) memcpy(tokens_out, s->hist_h, (uint64_t)n_steps * 4);
+  return YL_OK;
+}
+
+int yl_decode_step_launches(const yl_model* m, uint32_t* out) {
+  if (!m || !out) return fail(YL_ERR_ARG, "null argument");
+  const yl_shape& s = m->m->shape;
+  // per layer: norm, qkv, rope, attention (+combine), wo, norm, w13, quant (Q formats), w2
+  const uint32_t per_layer = 8 + (s.weight_format == YL_F16 ? 0 : 1);
+  uint32_t ns = (2 * (uint32_t)m->m->num_sms + s.n_kv_heads - 1) / s.n_kv_heads;
+  ns = std::max(1u, std::min(64u, ns));
+  *out = 1 + s.n_layers * (per_layer + (ns > 1 ? 1 : 0)) + 3;
+  return YL_OK;
+}
+
+// ------------------------------- reference FFI ---------------------------
+
+static std::mutex g_ffi_mu;
+static yl_model* g_current = nullptr;  // CURRENT_TRANSFORMER (lib.rs:48)
+
+bool load_transformer_ffi(const char* model_path) {
+  if (!model_path) return false;
+  yl_model* m = nullptr;
+  // lib.rs:143: load_transformer(path, false, u32::MAX, None)
+  if (yl_load_transformer(model_path, 0, 0xFFFFFFFFu, -1, &m) != YL_OK) return false;
+  std::lock_guard<std::mutex> lk(g_ffi_mu);
+  if (g_current) yl_model_free(g_current);
+  g_current = m;
+  return true;
+}
+
+}  // extern "C"

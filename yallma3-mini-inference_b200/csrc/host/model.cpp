@@ -1,0 +1,773 @@
+// GGUF loading (transformer_llama_gguf.rs:183-655) into the repacked HBM
+// layout, sessions (base_transformer.rs:78-105) and the device forward
+// (forward.rs:119-297) with a CUDA-graph batch-1 decode step.
+#include "model.h"
+
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdlib>
+#include <functional>
+#include <map>
+#include <memory>
+#include <thread>
+
+namespace yl {
+
+namespace {
+
+struct GVal {
+  uint32_t type = 0;
+  uint64_t u = 0;
+  int64_t i = 0;
+  double f = 0;
+  std::string str;
+  uint64_t arr_len = 0;
+  uint32_t arr_type = 0;
+};
+
+struct Cursor {
+  const uint8_t* p;
+  size_t size, off;
+  bool ok = true;
+  uint64_t rd(size_t k) {
+    if (off + k > size) { ok = false; return 0; }
+    uint64_t v = 0;
+    memcpy(&v, p + off, k);
+    off += k;
+    return v;
+  }
+  std::string str() {
+    uint64_t n = rd(8);
+    if (!ok || off + n > size) { ok = false; return ""; }
+    std::string s((const char*)p + off, n);
+    off += n;
+    return s;
+  }
+  void skip_str() {
+    uint64_t n = rd(8);
+    if (!ok || off + n > size) { ok = false; return; }
+    off += n;
+  }
+  // GGUF value of type t (transformer_llama_gguf.rs:80-107). Arrays keep only
+  // their length and element type (the token list is counted, not stored).
+  GVal value(uint32_t t, int depth = 0) {
+    GVal v;
+    v.type = t;
+    switch (t) {
+      case 0: v.u = rd(1); break;
+      case 1: v.i = (int8_t)rd(1); break;
+      case 2: v.u = rd(2); break;
+      case 3: v.i = (int16_t)rd(2); break;
+      case 4: v.u = rd(4); break;
+      case 5: v.i = (int32_t)rd(4); break;
+      case 6: { uint32_t b = (uint32_t)rd(4); float f; memcpy(&f, &b, 4); v.f = f; break; }
+      case 7: v.u = rd(1) != 0; break;
+      case 8: v.str = str(); break;
+      case 9: {
+        v.arr_type = (uint32_t)rd(4);
+        v.arr_len = rd(8);
+        if (depth > 1) { ok = false; break; }
+        for (uint64_t k = 0; k < v.arr_len && ok; ++k) {
+          if (v.arr_type == 8) skip_str();
+          else value(v.arr_type, depth + 1);
+        }
+        break;
+      }
+      case 10: v.u = rd(8); break;
+      case 11: v.i = (int64_t)rd(8); break;
+      case 12: { uint64_t b = rd(8); double d; memcpy(&d, &b, 8); v.f = d; break; }
+      default: ok = false;
+    }
+    return v;
+  }
+};
+
+struct TInfo {
+  std::string name;
+  uint32_t type = 0;  // GGML type
+  uint64_t off = 0;   // absolute file offset
+  uint64_t ne0 = 0, ne1 = 1;
+  uint64_t n = 0;
+};
+
+struct Mapped {
+  void* p = MAP_FAILED;
+  size_t size = 0;
+  ~Mapped() { if (p != MAP_FAILED) munmap(p, size); }
+};
+
+bool meta_u(const std::map<std::string, GVal>& m, const char* k, uint64_t* out) {
+  auto it = m.find(k);
+  if (it == m.end() || !(it->second.type == 4 || it->second.type == 10)) return false;
+  *out = it->second.u;
+  return true;
+}
+bool meta_f(const std::map<std::string, GVal>& m, const char* k, float* out) {
+  auto it = m.find(k);
+  if (it == m.end() || !(it->second.type == 6 || it->second.type == 12)) return false;
+  *out = (float)it->second.f;
+  return true;
+}
+uint32_t meta_id(const std::map<std::string, GVal>& m, const char* k, uint32_t dflt) {
+  auto it = m.find(k);
+  if (it == m.end()) return dflt;
+  switch (it->second.type) {
+    case 4: case 10: return (uint32_t)it->second.u;
+    case 5: case 11: return (uint32_t)it->second.i;
+  }
+  return dflt;
+}
+
+int parallel_for(uint64_t n, const std::function<void(uint64_t, uint64_t)>& fn) {
+  unsigned nt = std::max(1u, std::min(32u, std::thread::hardware_concurrency()));
+  if (n < 4096) nt = 1;
+  std::vector<std::thread> th;
+  uint64_t per = (n + nt - 1) / nt;
+  for (unsigned k = 0; k < nt; ++k) {
+    uint64_t a = k * per, b = std::min(n, a + per);
+    if (a >= b) break;
+    th.emplace_back(fn, a, b);
+  }
+  for (auto& t : th) t.join();
+  return 0;
+}
+
+// Repacks `nrows` rows coming from (possibly several) GGUF tensors into one
+// device weight. src_row(r) returns the file address of logical row r.
+struct Uploader {
+  Model* m;
+  uint8_t* stage = nullptr;
+  size_t stage_bytes = 0;
+  ~Uploader() { if (stage) cudaFreeHost(stage); }
+  int alloc(size_t bytes, void** out) {
+    void* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, std::max<size_t>(bytes, 256));
+    if (e != cudaSuccess) return fail(YL_ERR_OOM, std::string("cudaMalloc: ") + cudaGetErrorString(e));
+    m->allocs.push_back(p);
+    m->device_bytes += bytes;
+    *out = p;
+    return YL_OK;
+  }
+  int ensure_stage(size_t bytes) {
+    if (bytes <= stage_bytes) return YL_OK;
+    if (stage) cudaFreeHost(stage);
+    stage = nullptr;
+    YL_CUDA_TRY(cudaMallocHost(&stage, bytes));
+    stage_bytes = bytes;
+    return YL_OK;
+  }
+  // ggml_type: 8 Q8_0, 2 Q4_0, 1 F16
+  int weight(uint32_t ggml_type, uint32_t rows, uint32_t cols, const std::function<const uint8_t*(uint32_t)>& src_row,
+             DevWeight* w) {
+    if (cols % 32) return fail(YL_ERR_FORMAT, "row length must be a multiple of 32");
+    w->rows = rows;
+    w->cols = cols;
+    w->sf16 = true;
+    const uint32_t nb = cols / 32;
+    uint32_t src_row_bytes;
+    if (ggml_type == 8) { w->fmt = YL_Q8_0; w->row_bytes = cols; src_row_bytes = nb * 34; }
+    else if (ggml_type == 2) { w->fmt = YL_Q4_0; w->row_bytes = cols / 2; src_row_bytes = nb * 18; }
+    else if (ggml_type == 1) { w->fmt = YL_F16; w->row_bytes = cols * 2; src_row_bytes = cols * 2; }
+    else return fail(YL_ERR_FORMAT, "unsupported tensor type " + std::to_string(ggml_type));
+    (void)src_row_bytes;
+    w->scale_row_bytes = w->fmt == YL_F16 ? 0 : (uint32_t)round_up(nb * 2, 16);
+    void* q;
+    int rc = alloc((size_t)rows * w->row_bytes, &q);
+    if (rc) return rc;
+    w->q = (uint8_t*)q;
+    if (w->scale_row_bytes) {
+      void* s;
+      rc = alloc((size_t)rows * w->scale_row_bytes, &s);
+      if (rc) return rc;
+      w->s = (uint8_t*)s;
+    }
+    const size_t per_row = (size_t)w->row_bytes + w->scale_row_bytes;
+    const uint32_t chunk_rows = (uint32_t)std::max<size_t>(1, (64u << 20) / per_row);
+    rc = ensure_stage((size_t)chunk_rows * per_row);
+    if (rc) return rc;
+    for (uint32_t r0 = 0; r0 < rows; r0 += chunk_rows) {
+      const uint32_t nr = std::min(chunk_rows, rows - r0);
+      uint8_t* sq = stage;
+      uint8_t* ss = stage + (size_t)nr * w->row_bytes;
+      parallel_for(nr, [&](uint64_t a, uint64_t b) {
+        for (uint64_t r = a; r < b; ++r) {
+          const uint8_t* src = src_row(r0 + (uint32_t)r);
+          uint8_t* dq = sq + r * w->row_bytes;
+          if (w->fmt == YL_F16) {
+            memcpy(dq, src, w->row_bytes);
+            continue;
+          }
+          uint8_t* ds = ss + r * w->scale_row_bytes;
+          memset(ds, 0, w->scale_row_bytes);
+          const uint32_t bsz = w->fmt == YL_Q8_0 ? 34 : 18, qb = w->fmt == YL_Q8_0 ? 32 : 16;
+          for (uint32_t b = 0; b < nb; ++b) {
+            const uint8_t* blk = src + (size_t)b * bsz;
+            ds[2 * b] = blk[0];
+            ds[2 * b + 1] = blk[1];
+            memcpy(dq + (size_t)b * qb, blk + 2, qb);
+          }
+        }
+      });
+      YL_CUDA_TRY(cudaMemcpy(w->q + (size_t)r0 * w->row_bytes, sq, (size_t)nr * w->row_bytes, cudaMemcpyHostToDevice));
+      if (w->scale_row_bytes)
+        YL_CUDA_TRY(cudaMemcpy(w->s + (size_t)r0 * w->scale_row_bytes, ss, (size_t)nr * w->scale_row_bytes,
+                               cudaMemcpyHostToDevice));
+    }
+    return YL_OK;
+  }
+  int f32(const float* src, uint64_t n, float** out) {
+    void* p;
+    int rc = alloc(n * 4, &p);
+    if (rc) return rc;
+    YL_CUDA_TRY(cudaMemcpy(p, src, n * 4, cudaMemcpyHostToDevice));
+    *out = (float*)p;
+    return YL_OK;
+  }
+};
+
+// RoPE (cos, sin) table per (position, pair), by the reference formulas:
+// util.rs:653-718 (rope_gguf, theta iterated by *= theta_scale) or
+// util.rs:589-635 (rope with llama3 frequency scaling).
+void rope_table(const yl_shape& s, float llama3_factor, float llama3_low, float llama3_high, float old_ctx,
+                std::vector<float2>* out) {
+  const uint32_t hs = s.head_size, half = hs / 2;
+  out->assign((size_t)s.ctx_len * half, float2{0.f, 0.f});
+  if (s.rope_mode == YL_ROPE_GGUF) {
+    const float theta_scale = powf(s.rope_theta, -2.0f / (float)hs);
+    const float n_ctx_orig = (float)s.rope_original_ctx_len;
+    const float beta_fast = 32.0f, beta_slow = 1.0f;
+    float corr_start = fmaf(logf(n_ctx_orig / (beta_fast * 2.0f * (float)M_PI)), (float)hs, 0.0f) /
+                       (2.0f * logf(s.rope_theta));
+    corr_start = fmaxf(floorf(corr_start), 0.0f);
+    const float corr_end = fmaf(logf(n_ctx_orig / (beta_slow * 2.0f * (float)M_PI)), (float)hs, 0.0f) /
+                           (2.0f * logf(s.rope_theta));
+    const float corr_dims_1 = fminf(corr_start, corr_end) + fminf(corr_end, (float)half) - fmaxf(corr_start, 0.0f);
+    parallel_for(s.ctx_len, [&](uint64_t a, uint64_t b) {
+      for (uint64_t pos = a; pos < b; ++pos) {
+        float theta = (float)pos;
+        for (uint32_t kp = 0; kp < half; ++kp) {
+          const float theta_interp = s.rope_freq_scale * theta / 1.0f;
+          float t = theta_interp;
+          if (s.rope_ext_factor != 0.0f) {
+            const float y = ((float)(kp * 2) * 0.5f - corr_start) / fmaxf(corr_dims_1 - corr_start, 0.001f);
+            const float ramp = (1.0f - fminf(1.0f, fmaxf(y, 0.0f))) * s.rope_ext_factor;
+            t = theta_interp * (1.0f - ramp) + theta / 1.0f * ramp;
+          }
+          (*out)[pos * half + kp] = float2{cosf(t) * s.rope_attn_factor, sinf(t) * s.rope_attn_factor};
+          theta = theta * theta_scale;
+        }
+      }
+    });
+  } else {
+    const float low_wl = old_ctx / llama3_low, high_wl = old_ctx / llama3_high;
+    std::vector<float> freq(half);
+    for (uint32_t j = 0; j < half; ++j) {
+      float f = powf(s.rope_theta, -((float)(j * 2)) / (float)hs);
+      const float wl = (2.0f * (float)M_PI) / f;
+      if (wl > low_wl) {
+        f = f / llama3_factor;
+      } else if (wl <= low_wl && wl >= high_wl) {
+        const float sm = (old_ctx / wl - llama3_low) / (llama3_high - llama3_low);
+        f = (1.0f - sm) * f / llama3_factor + sm * f;
+      }
+      freq[j] = f;
+    }
+    parallel_for(s.ctx_len, [&](uint64_t a, uint64_t b) {
+      for (uint64_t pos = a; pos < b; ++pos)
+        for (uint32_t j = 0; j < half; ++j) {
+          const float v = (float)pos * freq[j];
+          (*out)[pos * half + j] = float2{cosf(v), sinf(v)};
+        }
+    });
+  }
+}
+
+}  // namespace
+
+Model::~Model() {
+  for (void* p : allocs) cudaFree(p);
+}
+
+const Tunables& tunables() {
+  static Tunables t = [] {
+    Tunables x;
+    if (const char* e = getenv("YL_MV_KC_BYTES")) x.kc_bytes = (uint32_t)atoi(e);
+    if (const char* e = getenv("YL_MV_SMEM")) x.smem = (uint32_t)atoi(e);
+    if (const char* e = getenv("YL_PDL")) x.pdl = atoi(e) != 0;
+    if (const char* e = getenv("YL_MV_GRID_MULT")) x.grid_mult = std::max(1, atoi(e));
+    return x;
+  }();
+  return t;
+}
+
+int model_load_gguf(const char* path, uint32_t max_ctx_len, int fmt_override, Model** out) {
+  int fd = open(path, O_RDONLY);
+  if (fd < 0) return fail(YL_ERR_IO, std::string("cannot open ") + path);
+  struct stat stt;
+  if (fstat(fd, &stt) != 0) { close(fd); return fail(YL_ERR_IO, "fstat failed"); }
+  Mapped mp;
+  mp.size = (size_t)stt.st_size;
+  mp.p = mmap(nullptr, mp.size, PROT_READ, MAP_PRIVATE, fd, 0);
+  close(fd);
+  if (mp.p == MAP_FAILED) return fail(YL_ERR_IO, "mmap failed");
+  madvise(mp.p, mp.size, MADV_SEQUENTIAL);
+  const uint8_t* base = (const uint8_t*)mp.p;
+  Cursor c{base, mp.size, 0};
+  if (c.rd(4) != 0x46554747u) return fail(YL_ERR_FORMAT, "Not a GGUF file (bad magic)");
+  const uint64_t version = c.rd(4);
+  if (version != 3) return fail(YL_ERR_FORMAT, "Only GGUF version 3 is supported, got " + std::to_string(version));
+  const uint64_t n_tensors = c.rd(8), n_kv = c.rd(8);
+  std::map<std::string, GVal> meta;
+  for (uint64_t i = 0; i < n_kv && c.ok; ++i) {
+    std::string key = c.str();
+    uint32_t t = (uint32_t)c.rd(4);
+    meta[key] = c.value(t);
+  }
+  if (!c.ok) return fail(YL_ERR_FORMAT, "truncated GGUF metadata");
+  auto arch = meta.find("general.architecture");
+  if (arch == meta.end() || arch->second.str != "llama")
+    return fail(YL_ERR_FORMAT, "Unsupported GGUF architecture (must be 'llama')");
+
+  std::unique_ptr<Model> m(new Model());
+  m->path = path;
+  yl_shape& s = m->shape;
+  uint64_t v;
+  if (!meta_u(meta, "llama.embedding_length", &v)) return fail(YL_ERR_FORMAT, "Missing llama.embedding_length");
+  s.dim = (uint32_t)v;
+  if (!meta_u(meta, "llama.feed_forward_length", &v)) return fail(YL_ERR_FORMAT, "Missing llama.feed_forward_length");
+  s.hidden_dim = (uint32_t)v;
+  if (!meta_u(meta, "llama.block_count", &v)) return fail(YL_ERR_FORMAT, "Missing llama.block_count");
+  s.n_layers = (uint32_t)v;
+  if (!meta_u(meta, "llama.attention.head_count", &v)) return fail(YL_ERR_FORMAT, "Missing head_count");
+  s.n_heads = (uint32_t)v;
+  s.n_kv_heads = meta_u(meta, "llama.attention.head_count_kv", &v) ? (uint32_t)v : s.n_heads;
+  if (!meta_f(meta, "llama.attention.layer_norm_rms_epsilon", &s.rms_norm_eps))
+    return fail(YL_ERR_FORMAT, "Missing layer_norm_rms_epsilon");
+  const uint64_t file_type = meta_u(meta, "general.file_type", &v) ? v : 7;
+  if (!meta_f(meta, "llama.rope.freq_base", &s.rope_theta)) s.rope_theta = 10000.0f;
+  if (!meta_u(meta, "llama.context_length", &v)) return fail(YL_ERR_FORMAT, "Missing llama.context_length");
+  const uint32_t seq_len = (uint32_t)v;
+  if (s.n_heads == 0 || s.dim % s.n_heads) return fail(YL_ERR_FORMAT, "dim must be divisible by n_heads");
+  s.head_size = s.dim / s.n_heads;
+  s.ctx_len = std::min(seq_len, max_ctx_len);
+  auto toks = meta.find("tokenizer.ggml.tokens");
+  if (toks == meta.end() || toks->second.type != 9) return fail(YL_ERR_FORMAT, "tokenizer.ggml.tokens not found");
+  s.vocab_size = (uint32_t)toks->second.arr_len;
+  float raw = 1.0f;
+  if (!meta_f(meta, "llama.rope.scaling.factor", &raw)) raw = 1.0f;
+  s.rope_freq_scale = raw != 0.0f ? 1.0f / raw : 1.0f;
+  if (!meta_f(meta, "llama.rope.scaling.ext_factor", &s.rope_ext_factor)) s.rope_ext_factor = 0.0f;
+  if (!meta_f(meta, "llama.rope.scaling.attn_factor", &s.rope_attn_factor)) s.rope_attn_factor = 1.0f;
+  s.rope_original_ctx_len = meta_u(meta, "llama.rope.scaling.original_context_length", &v) ? (uint32_t)v : seq_len;
+  if (!meta_f(meta, "llama.attention.scale", &s.attention_scale)) s.attention_scale = 0.0f;
+  s.group_size = 32;
+  auto sct = meta.find("llama.rope.scaling.type");
+  s.rope_mode = (sct != meta.end() && sct->second.str == "llama3") ? YL_ROPE_LLAMA3 : YL_ROPE_GGUF;
+  float l3_factor = 32.0f, l3_low = 1.0f, l3_high = 4.0f;
+  meta_f(meta, "llama.rope.scaling.factor", &l3_factor);
+  meta_f(meta, "llama.rope.scaling.low_freq_factor", &l3_low);
+  meta_f(meta, "llama.rope.scaling.high_freq_factor", &l3_high);
+  int fmt;
+  if (fmt_override >= 0) fmt = fmt_override;
+  else if (file_type == 1) fmt = YL_F16;
+  else if (file_type == 2) fmt = YL_Q4_0;
+  else if (file_type == 7) fmt = YL_Q8_0;
+  else return fail(YL_ERR_FORMAT, "Unsupported GGUF file_type " + std::to_string(file_type));
+  s.weight_format = fmt;
+  s.tp_rank = 0;
+  s.tp_size = 1;
+  m->bos = meta_id(meta, "tokenizer.ggml.bos_token_id", 128000u);
+  m->eos = meta_id(meta, "tokenizer.ggml.eos_token_id", 128009u);
+  if (s.dim % 32 || s.hidden_dim % 32 || s.head_size % 32 || s.n_kv_heads == 0 || s.n_heads % s.n_kv_heads)
+    return fail(YL_ERR_UNSUPPORTED, "device path needs dim, ffn and head_size multiples of 32 and GQA grouping");
+  if (s.head_size != 64 && s.head_size != 128) return fail(YL_ERR_UNSUPPORTED, "head_size must be 64 or 128");
+  if (s.n_heads / s.n_kv_heads > 8) return fail(YL_ERR_UNSUPPORTED, "more than 8 query heads per KV head");
+  if (s.ctx_len == 0) return fail(YL_ERR_ARG, "ctx_len is 0");
+
+  std::map<std::string, TInfo> tmap;
+  for (uint64_t i = 0; i < n_tensors && c.ok; ++i) {
+    TInfo ti;
+    ti.name = c.str();
+    const uint32_t nd = (uint32_t)c.rd(4);
+    ti.n = 1;
+    for (uint32_t d = 0; d < nd; ++d) {
+      uint64_t e = c.rd(8);
+      if (d == 0) ti.ne0 = e;
+      else if (d == 1) ti.ne1 = e;
+      ti.n *= e;
+    }
+    ti.type = (uint32_t)c.rd(4);
+    ti.off = c.rd(8);
+    tmap[ti.name] = ti;
+  }
+  if (!c.ok) return fail(YL_ERR_FORMAT, "truncated tensor infos");
+  const uint64_t alignment = meta_u(meta, "general.alignment", &v) ? v : 32;
+  if (alignment == 0 || (alignment & (alignment - 1))) return fail(YL_ERR_FORMAT, "GGUF alignment must be a power of 2");
+  const uint64_t data_start = (c.off + alignment - 1) / alignment * alignment;
+  for (auto& kv : tmap) kv.second.off += data_start;
+  auto bytes_of = [](uint32_t type, uint64_t n) -> uint64_t {
+    switch (type) {
+      case 0: return n * 4;
+      case 1: return n * 2;
+      case 2: return n / 32 * 18;
+      case 8: return n / 32 * 34;
+    }
+    return 0;
+  };
+  for (auto& kv : tmap) {
+    const uint64_t nb = bytes_of(kv.second.type, kv.second.n);
+    if (nb == 0 || kv.second.off + nb > mp.size) return fail(YL_ERR_FORMAT, "tensor out of file bounds: " + kv.first);
+  }
+  auto get = [&](const std::string& nm, const TInfo** out_ti) -> int {
+    auto it = tmap.find(nm);
+    if (it == tmap.end()) return fail(YL_ERR_FORMAT, "Missing tensor: " + nm);
+    *out_ti = &it->second;
+    return YL_OK;
+  };
+  const uint32_t want_type = fmt == YL_Q8_0 ? 8 : fmt == YL_Q4_0 ? 2 : 1;
+
+  YL_CUDA_TRY(cudaGetDevice(&m->device));
+  YL_CUDA_TRY(cudaDeviceGetAttribute(&m->num_sms, cudaDevAttrMultiProcessorCount, m->device));
+  Uploader up{m.get()};
+  const uint32_t d = s.dim, att = s.n_heads * s.head_size, kvd = s.n_kv_heads * s.head_size, f = s.hidden_dim;
+  int rc;
+  auto row_ptr = [&](const TInfo* ti, uint32_t cols, uint32_t r) {
+    return base + ti->off + bytes_of(ti->type, (uint64_t)r * cols);
+  };
+  auto check = [&](const TInfo* ti, uint64_t rows, uint64_t cols) -> int {
+    if (ti->type != want_type) return fail(YL_ERR_FORMAT, "format/variant mismatch in " + ti->name);
+    if (ti->n != rows * cols) return fail(YL_ERR_FORMAT, "unexpected element count in " + ti->name);
+    return YL_OK;
+  };
+  const TInfo* te;
+  if ((rc = get("token_embd.weight", &te))) return rc;
+  if (te->n != (uint64_t)s.vocab_size * d) return fail(YL_ERR_FORMAT, "token_embd.weight shape mismatch");
+  if ((rc = up.weight(te->type, s.vocab_size, d, [&](uint32_t r) { return row_ptr(te, d, r); }, &m->emb))) return rc;
+  m->lm = m->emb;
+  auto out_it = tmap.find("output.weight");
+  if (out_it != tmap.end()) {  // untied lm_head (resolved deviation D2)
+    const TInfo* to = &out_it->second;
+    if (to->n != (uint64_t)s.vocab_size * d) return fail(YL_ERR_FORMAT, "output.weight shape mismatch");
+    if ((rc = up.weight(to->type, s.vocab_size, d, [&](uint32_t r) { return row_ptr(to, d, r); }, &m->lm))) return rc;
+    s.untied_lm_head = 1;
+  }
+  auto f32t = [&](const std::string& nm, uint64_t n, float** dst) -> int {
+    const TInfo* t;
+    int r = get(nm, &t);
+    if (r) return r;
+    if (t->type != 0 || t->n != n) return fail(YL_ERR_FORMAT, "Expected F32 tensor " + nm);
+    return up.f32((const float*)(base + t->off), n, dst);
+  };
+  if ((rc = f32t("output_norm.weight", d, &m->rms_final))) return rc;
+  m->layers.resize(s.n_layers);
+  for (uint32_t l = 0; l < s.n_layers; ++l) {
+    const std::string p = "blk." + std::to_string(l) + ".";
+    Layer& L = m->layers[l];
+    if ((rc = f32t(p + "attn_norm.weight", d, &L.rms_att))) return rc;
+    if ((rc = f32t(p + "ffn_norm.weight", d, &L.rms_ffn))) return rc;
+    const TInfo *tq, *tk, *tv, *to, *tg, *tu, *tdn;
+    if ((rc = get(p + "attn_q.weight", &tq)) || (rc = get(p + "attn_k.weight", &tk)) ||
+        (rc = get(p + "attn_v.weight", &tv)) || (rc = get(p + "attn_output.weight", &to)) ||
+        (rc = get(p + "ffn_gate.weight", &tg)) || (rc = get(p + "ffn_up.weight", &tu)) ||
+        (rc = get(p + "ffn_down.weight", &tdn)))
+      return rc;
+    if ((rc = check(tq, att, d)) || (rc = check(tk, kvd, d)) || (rc = check(tv, kvd, d)) || (rc = check(to, d, att)) ||
+        (rc = check(tg, f, d)) || (rc = check(tu, f, d)) || (rc = check(tdn, d, f)))
+      return rc;
+    rc = up.weight(want_type, att + 2 * kvd, d, [&](uint32_t r) {
+      if (r < att) return row_ptr(tq, d, r);
+      if (r < att + kvd) return row_ptr(tk, d, r - att);
+      return row_ptr(tv, d, r - att - kvd);
+    }, &L.wqkv);
+    if (rc) return rc;
+    if ((rc = up.weight(want_type, d, att, [&](uint32_t r) { return row_ptr(to, att, r); }, &L.wo))) return rc;
+    rc = up.weight(want_type, 2 * f, d, [&](uint32_t r) { return (r & 1) ? row_ptr(tu, d, r / 2) : row_ptr(tg, d, r / 2); },
+                   &L.w13);
+    if (rc) return rc;
+    if ((rc = up.weight(want_type, d, f, [&](uint32_t r) { return row_ptr(tdn, f, r); }, &L.w2))) return rc;
+  }
+  std::vector<float2> cs;
+  rope_table(s, l3_factor, l3_low, l3_high, (float)s.rope_original_ctx_len, &cs);
+  void* csd;
+  if ((rc = up.alloc(cs.size() * sizeof(float2), &csd))) return rc;
+  YL_CUDA_TRY(cudaMemcpy(csd, cs.data(), cs.size() * sizeof(float2), cudaMemcpyHostToDevice));
+  m->rope_cs = (float2*)csd;
+  m->attn_scale = s.attention_scale != 0.0f ? s.attention_scale : 1.0f / sqrtf((float)s.head_size);
+  *out = m.release();
+  return YL_OK;
+}
+
+// ------------------------------ sessions ---------------------------------
+
+Session::~Session() {
+  if (graph) cudaGraphExecDestroy(graph);
+  if (stream) cudaStreamDestroy(stream);
+  for (void* p : allocs) cudaFree(p);
+  if (state_h) cudaFreeHost(state_h);
+  if (logits_h) cudaFreeHost(logits_h);
+  if (hist_h) cudaFreeHost(hist_h);
+}
+
+namespace {
+int salloc(Session* s, size_t bytes, void** out) {
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, std::max<size_t>(bytes, 256));
+  if (e != cudaSuccess) return fail(YL_ERR_OOM, std::string("cudaMalloc: ") + cudaGetErrorString(e));
+  s->allocs.push_back(p);
+  *out = p;
+  return YL_OK;
+}
+
+// Grows the per-token workspace to hold `n` tokens.
+int ensure_cap(Session* s, uint32_t n) {
+  if (n <= s->cap) return YL_OK;
+  const yl_shape& sh = s->m->shape;
+  const uint64_t att = (uint64_t)sh.n_heads * sh.head_size, kvd = (uint64_t)sh.n_kv_heads * sh.head_size;
+  const uint64_t wmax = std::max<uint64_t>({sh.dim, att, sh.hidden_dim});
+  const uint32_t cap = std::max(n, 8u);
+  void* p;
+  int rc;
+  if ((rc = salloc(s, cap * sh.dim * 4ull, &p))) return rc;
+  s->x = (float*)p;
+  if ((rc = salloc(s, cap * wmax * 4ull, &p))) return rc;
+  s->xf = (float*)p;
+  if ((rc = salloc(s, cap * wmax, &p))) return rc;
+  s->xq = (int8_t*)p;
+  if ((rc = salloc(s, cap * (wmax / 32) * 4ull, &p))) return rc;
+  s->xs = (float*)p;
+  if ((rc = salloc(s, cap * (att + 2 * kvd) * 4ull, &p))) return rc;
+  s->qkv = (float*)p;
+  if ((rc = salloc(s, cap * att * 4ull, &p))) return rc;
+  s->q = (float*)p;
+  if ((rc = salloc(s, cap * (uint64_t)sh.hidden_dim * 4ull, &p))) return rc;
+  s->h = (float*)p;
+  if ((rc = salloc(s, cap * 4ull, &p))) return rc;
+  s->tok = (uint32_t*)p;
+  s->cap = cap;
+  return YL_OK;
+}
+}  // namespace
+
+int session_create(const Model* m, Session** out) {
+  std::unique_ptr<Session> s(new Session());
+  s->m = m;
+  s->device = m->device;
+  YL_CUDA_TRY(cudaSetDevice(m->device));
+  YL_CUDA_TRY(cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking));
+  const yl_shape& sh = m->shape;
+  const uint64_t kvd = (uint64_t)sh.n_kv_heads * sh.head_size;
+  s->kv_elems = (uint64_t)sh.n_layers * sh.ctx_len * kvd;
+  void* p;
+  int rc;
+  if ((rc = salloc(s.get(), s->kv_elems * 4, &p))) return rc;
+  s->kcache = (float*)p;
+  if ((rc = salloc(s.get(), s->kv_elems * 4, &p))) return rc;
+  s->vcache = (float*)p;
+  YL_CUDA_TRY(cudaMemset(s->kcache, 0, s->kv_elems * 4));
+  YL_CUDA_TRY(cudaMemset(s->vcache, 0, s->kv_elems * 4));
+  if ((rc = salloc(s.get(), (uint64_t)sh.vocab_size * 4, &p))) return rc;
+  s->logits = (float*)p;
+  // decode split count: enough CTAs to cover the SMs twice
+  uint32_t ns = (2 * (uint32_t)m->num_sms + sh.n_kv_heads - 1) / sh.n_kv_heads;
+  s->n_splits = std::max(1u, std::min(64u, ns));
+  if ((rc = salloc(s.get(), (uint64_t)sh.n_heads * s->n_splits * (sh.head_size + 2) * 4, &p))) return rc;
+  s->part = (float*)p;
+  if ((rc = salloc(s.get(), ((uint64_t)sh.ctx_len + 1) * 4, &p))) return rc;
+  s->hist = (uint32_t*)p;
+  if ((rc = salloc(s.get(), sizeof(k::StepState), &p))) return rc;
+  s->state = (k::StepState*)p;
+  if ((rc = salloc(s.get(), sizeof(int), &p))) return rc;
+  s->err = (int*)p;
+  YL_CUDA_TRY(cudaMemset(s->err, 0, sizeof(int)));
+  YL_CUDA_TRY(cudaMemset(s->state, 0, sizeof(k::StepState)));
+  YL_CUDA_TRY(cudaMallocHost(&s->state_h, sizeof(k::StepState)));
+  YL_CUDA_TRY(cudaMallocHost(&s->logits_h, (uint64_t)sh.vocab_size * 4));
+  YL_CUDA_TRY(cudaMallocHost(&s->hist_h, ((uint64_t)sh.ctx_len + 1) * 4));
+  if ((rc = ensure_cap(s.get(), 8))) return rc;
+  *out = s.release();
+  return YL_OK;
+}
+
+int session_reset(Session* s) {
+  YL_CUDA_TRY(cudaSetDevice(s->device));
+  YL_CUDA_TRY(cudaMemsetAsync(s->kcache, 0, s->kv_elems * 4, s->stream));
+  YL_CUDA_TRY(cudaMemsetAsync(s->vcache, 0, s->kv_elems * 4, s->stream));
+  YL_CUDA_TRY(cudaStreamSynchronize(s->stream));
+  s->pos = 0;
+  return YL_OK;
+}
+
+// ------------------------------ forward ------------------------------------
+
+int run_matvec(const DevWeight& w, bool f32act, const int8_t* xq, const float* xs, const float* xf, uint64_t x_stride,
+               uint64_t xs_stride, uint32_t ntok, float* out, uint64_t out_stride, int epi, uint32_t quirk_cols,
+               int* err, cudaStream_t st, bool pdl, int num_sms) {
+  const Tunables& tu = tunables();
+  int fmt;
+  uint32_t kc;
+  if (w.fmt == YL_Q8_0) { fmt = f32act ? k::FMT_Q8F : k::FMT_Q8; kc = tu.kc_bytes; }
+  else if (w.fmt == YL_Q4_0) { fmt = f32act ? k::FMT_Q4F : k::FMT_Q4; kc = tu.kc_bytes * 2; }
+  else { fmt = k::FMT_F16; kc = tu.kc_bytes / 2; }
+  kc = std::max<uint32_t>(256, kc / 256 * 256);
+  k::LaunchCfg lc;
+  lc.stream = st;
+  lc.pdl = pdl;
+  lc.grid = (uint32_t)num_sms * tu.grid_mult;
+  lc.smem_budget = tu.smem;
+  for (uint32_t t0 = 0; t0 < ntok; t0 += 8) {
+    k::MvArgs a{};
+    a.wq = w.q;
+    a.ws = w.s;
+    a.rows = w.rows;
+    a.K = w.cols;
+    a.row_bytes = w.row_bytes;
+    a.scale_row_bytes = w.scale_row_bytes;
+    a.kc = std::min<uint32_t>(kc, (uint32_t)round_up(w.cols, 256));
+    a.xq = xq ? xq + t0 * x_stride : nullptr;
+    a.xs = xs ? xs + t0 * xs_stride : nullptr;
+    a.xf = xf ? xf + t0 * x_stride : nullptr;
+    a.x_tok_stride = x_stride;
+    a.xs_tok_stride = xs_stride;
+    a.ntok = std::min(8u, ntok - t0);
+    a.out = out + t0 * out_stride;
+    a.out_tok_stride = out_stride;
+    a.quirk_cols = quirk_cols;
+    a.err = err;
+    cudaError_t e = k::matvec(a, fmt, w.sf16, epi, lc);
+    if (e != cudaSuccess) return fail(YL_ERR_CUDA, std::string("matvec launch: ") + cudaGetErrorString(e));
+  }
+  return YL_OK;
+}
+
+namespace {
+
+// Enqueues the full forward for n tokens (already on device in s->tok unless
+// from_state). from_state: batch-1 step whose token/pos live in s->state
+// (graph capture). pdl: launch with programmatic dependent launch.
+int enqueue_forward(Session* s, uint32_t n, uint32_t start_pos, bool from_state, bool pdl, uint32_t* launches) {
+  const Model* m = s->m;
+  const yl_shape& sh = m->shape;
+  const uint32_t d = sh.dim, att = sh.n_heads * sh.head_size, kvd = sh.n_kv_heads * sh.head_size, f = sh.hidden_dim;
+  const uint64_t wmax = std::max<uint64_t>({d, att, f});
+  const bool f32act = sh.weight_format == YL_F16;
+  const k::StepState* st = from_state ? s->state : nullptr;
+  k::LaunchCfg lc;
+  lc.stream = s->stream;
+  lc.pdl = pdl;
+  uint32_t nl = 0;
+  cudaError_t e;
+  int rc;
+#define YL_LAUNCH(expr)                                                                   \
+  do {                                                                                    \
+    e = (expr);                                                                           \
+    if (e != cudaSuccess) return fail(YL_ERR_CUDA, std::string(#expr) + ": " + cudaGetErrorString(e)); \
+    ++nl;                                                                                 \
+  } while (0)
+#define YL_MV(...)                                  \
+  do {                                              \
+    if ((rc = run_matvec(__VA_ARGS__))) return rc;  \
+    nl += (n + 7) / 8;                              \
+  } while (0)
+
+  YL_LAUNCH(k::embed(m->emb.fmt == YL_Q8_0 ? k::FMT_Q8 : m->emb.fmt == YL_Q4_0 ? k::FMT_Q4 : k::FMT_F16, m->emb.q,
+                     m->emb.s, m->emb.row_bytes, m->emb.scale_row_bytes, d, sh.vocab_size, s->tok, st, n, s->x, lc));
+  const uint32_t n_splits = n == 1 ? s->n_splits : 1;
+  for (uint32_t l = 0; l < sh.n_layers; ++l) {
+    const Layer& L = m->layers[l];
+    float* kc = s->kcache + (uint64_t)l * sh.ctx_len * kvd;
+    float* vc = s->vcache + (uint64_t)l * sh.ctx_len * kvd;
+    // attention block (forward.rs:154-204)
+    YL_LAUNCH(k::rmsnorm_quant(s->x, L.rms_att, n, d, sh.rms_norm_eps, f32act ? nullptr : s->xq, s->xs,
+                               f32act ? s->xf : nullptr, lc));
+    YL_MV(L.wqkv, f32act, s->xq, s->xs, s->xf, d, d / 32, n, s->qkv, att + 2 * kvd, k::EPI_STORE, 0, s->err, s->stream,
+          pdl, m->num_sms);
+    YL_LAUNCH(k::rope_kv(s->qkv, n, sh.n_heads, sh.n_kv_heads, sh.head_size, sh.rope_mode, m->rope_cs, sh.ctx_len, st,
+                         start_pos, s->q, kc, vc, lc));
+    k::AttnArgs aa{};
+    aa.q = s->q;
+    aa.kcache = kc;
+    aa.vcache = vc;
+    aa.ntok = n;
+    aa.n_heads = sh.n_heads;
+    aa.n_kv_heads = sh.n_kv_heads;
+    aa.head_size = sh.head_size;
+    aa.kv_dim = kvd;
+    aa.state = st;
+    aa.pos0 = start_pos;
+    aa.scale = m->attn_scale;
+    aa.n_splits = n_splits;
+    aa.part = s->part;
+    aa.out = f32act ? s->xf : nullptr;
+    aa.q8 = f32act ? nullptr : s->xq;
+    aa.s8 = s->xs;
+    YL_LAUNCH(k::attention(aa, lc));
+    if (n_splits > 1) ++nl;
+    YL_MV(L.wo, f32act, s->xq, s->xs, s->xf, att, att / 32, n, s->x, d, k::EPI_ADD, 0, s->err, s->stream, pdl,
+          m->num_sms);
+    // feed-forward block (forward.rs:206-253)
+    YL_LAUNCH(k::rmsnorm_quant(s->x, L.rms_ffn, n, d, sh.rms_norm_eps, f32act ? nullptr : s->xq, s->xs,
+                               f32act ? s->xf : nullptr, lc));
+    YL_MV(L.w13, f32act, s->xq, s->xs, s->xf, d, d / 32, n, s->h, f, k::EPI_SWIGLU, 0, s->err, s->stream, pdl,
+          m->num_sms);
+    // F16Kernel::quantize is a copy (forward.rs:78-81): the F16 path reads h directly
+    if (!f32act) YL_LAUNCH(k::quantize_q8(s->h, s->xq, s->xs, (uint64_t)n * f / 32, lc));
+    YL_MV(L.w2, f32act, s->xq, s->xs, f32act ? s->h : s->xf, f, f / 32, n, s->x, d, k::EPI_ADD, 0, s->err, s->stream,
+          pdl, m->num_sms);
+  }
+  // final norm on the last token, lm_head, greedy id (forward.rs:256-279)
+  const float* xlast = s->x + (uint64_t)(n - 1) * d;
+  YL_LAUNCH(k::rmsnorm_quant(xlast, m->rms_final, 1, d, sh.rms_norm_eps, nullptr, nullptr, s->xf, lc));
+  {
+    const DevWeight& lm = m->lm;
+    if ((rc = run_matvec(lm, true, nullptr, nullptr, s->xf, d, 0, 1, s->logits, sh.vocab_size, k::EPI_STORE, 0, s->err,
+                         s->stream, pdl, m->num_sms)))
+      return rc;
+    ++nl;
+  }
+  YL_LAUNCH(k::argmax(s->logits, sh.vocab_size, s->hist, from_state ? s->state : nullptr, lc));
+#undef YL_LAUNCH
+#undef YL_MV
+  if (launches) *launches = nl;
+  return YL_OK;
+}
+
+}  // namespace
+
+int forward(Session* s, const uint32_t* tokens_host, uint32_t n, uint32_t start_pos) {
+  const yl_shape& sh = s->m->shape;
+  if (n == 0) return fail(YL_ERR_ARG, "empty token batch");
+  if ((uint64_t)start_pos + n > sh.ctx_len) return fail(YL_ERR_RANGE, "position beyond ctx_len");
+  YL_CUDA_TRY(cudaSetDevice(s->device));
+  int rc = ensure_cap(s, n);
+  if (rc) return rc;
+  YL_CUDA_TRY(cudaMemcpyAsync(s->tok, tokens_host, (uint64_t)n * 4, cudaMemcpyHostToDevice, s->stream));
+  rc = enqueue_forward(s, n, start_pos, false, tunables().pdl, nullptr);
+  if (rc) return rc;
+  return YL_OK;
+}
+
+int ensure_decode_graph(Session* s) {
+  if (s->graph) return YL_OK;
+  YL_CUDA_TRY(cudaSetDevice(s->device));
+  int rc = ensure_cap(s, 8);
+  if (rc) return rc;
+  cudaGraph_t g = nullptr;
+  YL_CUDA_TRY(cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal));
+  uint32_t nl = 0;
+  rc = enqueue_forward(s, 1, 0, true, tunables().pdl, &nl);
+  cudaError_t e = cudaStreamEndCapture(s->stream, &g);
+  if (rc) { if (g) cudaGraphDestroy(g); return rc; }
+  if (e != cudaSuccess) return fail(YL_ERR_CUDA, std::string("graph capture: ") + cudaGetErrorString(e));
+  e = cudaGraphInstantiate(&s->graph, g, 0);
+  cudaGraphDestroy(g);
+  if (e != cudaSuccess) { s->graph = nullptr; return fail(YL_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(e)); }
+  s->graph_launches = nl;
+  return YL_OK;
+}
+
+}  // namespace yl

@@ -1,0 +1,107 @@
+// Host-side model/session objects of the device path.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../kernels/kernels.h"
+#include "common.h"
+
+namespace yl {
+
+// One repacked weight matrix in HBM: quants [rows][row_bytes] and (for
+// quantized formats) scales [rows][scale_row_bytes], rows 16-byte aligned.
+struct DevWeight {
+  int fmt = YL_Q8_0;  // yl_weight_format
+  bool sf16 = true;   // scale element type
+  uint32_t rows = 0, cols = 0;
+  uint32_t row_bytes = 0, scale_row_bytes = 0;
+  uint8_t* q = nullptr;
+  uint8_t* s = nullptr;
+};
+
+struct Layer {
+  DevWeight wqkv;  // rows: q (att_dim) | k (kv_dim) | v (kv_dim)
+  DevWeight wo;
+  DevWeight w13;   // rows interleaved: gate j at 2j, up j at 2j+1
+  DevWeight w2;
+  float* rms_att = nullptr;
+  float* rms_ffn = nullptr;
+};
+
+struct Model {
+  yl_shape shape{};
+  std::string name = "TransformerLlamaGguf";
+  std::string path;
+  int device = 0;
+  int num_sms = 148;
+  uint32_t bos = 0, eos = 0;
+  float attn_scale = 0.f;
+  DevWeight emb;
+  DevWeight lm;  // aliases emb when tied
+  std::vector<Layer> layers;
+  float* rms_final = nullptr;
+  float2* rope_cs = nullptr;  // [ctx_len][head_size/2] (cos, sin)
+  std::vector<void*> allocs;
+  uint64_t device_bytes = 0;
+  ~Model();
+};
+
+struct Session {
+  const Model* m = nullptr;
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  float* kcache = nullptr;
+  float* vcache = nullptr;
+  uint64_t kv_elems = 0;  // per cache
+  uint32_t pos = 0;
+  // workspace sized for `cap` tokens
+  uint32_t cap = 0;
+  float* x = nullptr;     // residual stream [cap][dim]
+  float* xf = nullptr;    // f32 activations [cap][max(dim,att,ffn)] (F16 format) / final norm
+  int8_t* xq = nullptr;   // [cap][max(dim,att,ffn)]
+  float* xs = nullptr;    // [cap][max/32]
+  float* qkv = nullptr;   // [cap][att + 2 kv]
+  float* q = nullptr;     // [cap][att]
+  float* h = nullptr;     // [cap][ffn]
+  uint32_t* tok = nullptr;  // [cap]
+  float* logits = nullptr;  // [vocab]
+  float* part = nullptr;    // attention split partials (decode)
+  uint32_t* hist = nullptr; // [ctx_len] greedy ids of device steps
+  k::StepState* state = nullptr;
+  int* err = nullptr;
+  // pinned host staging
+  k::StepState* state_h = nullptr;
+  float* logits_h = nullptr;
+  uint32_t* hist_h = nullptr;
+  uint32_t n_splits = 1;
+  cudaGraphExec_t graph = nullptr;
+  uint32_t graph_launches = 0;
+  std::vector<void*> allocs;
+  ~Session();
+};
+
+int model_load_gguf(const char* path, uint32_t max_ctx_len, int fmt_override, Model** out);
+int session_create(const Model* m, Session** out);
+int session_reset(Session* s);
+// General forward over n tokens (prefill or decode); last-token logits stay in
+// s->logits (device), greedy id in s->hist[0].
+int forward(Session* s, const uint32_t* tokens_host, uint32_t n, uint32_t start_pos);
+// One batch-1 step through the captured graph (state already set on device).
+int ensure_decode_graph(Session* s);
+// Tunables read once from the environment (YL_MV_KC_BYTES, YL_MV_SMEM, YL_PDL).
+struct Tunables {
+  uint32_t kc_bytes = 2048;
+  uint32_t smem = 100 * 1024;
+  bool pdl = true;
+  uint32_t grid_mult = 1;
+};
+const Tunables& tunables();
+// Launches the matvec for `ntok` tokens (groups of 8) with activations x*.
+int run_matvec(const DevWeight& w, bool f32act, const int8_t* xq, const float* xs, const float* xf,
+               uint64_t x_stride, uint64_t xs_stride, uint32_t ntok, float* out, uint64_t out_stride, int epi,
+               uint32_t quirk_cols, int* err, cudaStream_t st, bool pdl, int num_sms);
+
+}  // namespace yl

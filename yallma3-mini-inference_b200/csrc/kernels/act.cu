@@ -1,0 +1,178 @@
+// Activation-side kernels: the bit-exact Q8_0 quantizer, fused RMSNorm +
+// quantize, embedding gather and the greedy argmax.
+#include <float.h>
+
+#include "device.cuh"
+#include "kernels.h"
+
+namespace yl {
+namespace k {
+using namespace yl::dev;
+
+// quantization.rs:29-52, one warp per 32-element block.
+__global__ void __launch_bounds__(256) quantize_q8_kernel(const float* __restrict__ x, int8_t* __restrict__ q,
+                                                          float* __restrict__ s, uint64_t nblocks) {
+  grid_dep_launch();
+  grid_dep_wait();
+  const uint64_t b = (uint64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (b >= nblocks) return;
+  float sc;
+  const int8_t v = quant_q8_lane(x[b * 32 + lane], &sc);
+  q[b * 32 + lane] = v;
+  if (lane == 0) s[b] = sc;
+}
+
+cudaError_t quantize_q8(const float* x, int8_t* q, float* s, uint64_t nblocks, const LaunchCfg& lc) {
+  if (nblocks == 0) return cudaSuccess;
+  return launch_kernel(quantize_q8_kernel, dim3((unsigned)((nblocks + 7) / 8)), dim3(256), 0, lc, x, q, s, nblocks);
+}
+
+// util.rs:389-426: ss = sum x^2; ss /= n; ss += eps; ss = 1/sqrt(ss);
+// y = w * (ss * x); then the Q8_0 quantizer on y (forward.rs:155-160). The
+// sum-of-squares order differs from the reference's 8-lane fold (f32
+// rounding only); everything after it is the same sequence of IEEE ops.
+__global__ void __launch_bounds__(256) rmsnorm_quant_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                                            uint32_t dim, float eps, int8_t* __restrict__ q,
+                                                            float* __restrict__ s, float* __restrict__ y) {
+  grid_dep_launch();
+  grid_dep_wait();
+  __shared__ float red[8];
+  const uint32_t t = blockIdx.x;
+  const float* xr = x + (uint64_t)t * dim;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float ss = 0.0f;
+  for (uint32_t i = threadIdx.x * 4; i < dim; i += 256 * 4) {
+    const float4 v = *reinterpret_cast<const float4*>(xr + i);
+    ss = fmaf(v.x, v.x, ss);
+    ss = fmaf(v.y, v.y, ss);
+    ss = fmaf(v.z, v.z, ss);
+    ss = fmaf(v.w, v.w, ss);
+  }
+  ss = warp_sum(ss);
+  if (lane == 0) red[warp] = ss;
+  __syncthreads();
+  float tot = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) tot += red[i];
+  float r = __fdiv_rn(tot, (float)dim);
+  r = __fadd_rn(r, eps);
+  r = __fdiv_rn(1.0f, __fsqrt_rn(r));
+  const uint32_t nb = dim / 32;
+  for (uint32_t b = warp; b < nb; b += 8) {
+    const uint32_t k = b * 32 + lane;
+    const float yv = __fmul_rn(w[k], __fmul_rn(r, xr[k]));
+    if (y) y[(uint64_t)t * dim + k] = yv;
+    if (q) {
+      float sc;
+      const int8_t qv = quant_q8_lane(yv, &sc);
+      q[(uint64_t)t * dim + k] = qv;
+      if (lane == 0) s[(uint64_t)t * nb + b] = sc;
+    }
+  }
+}
+
+cudaError_t rmsnorm_quant(const float* x, const float* w, uint32_t ntok, uint32_t dim, float eps, int8_t* q,
+                          float* s, float* y, const LaunchCfg& lc) {
+  if (ntok == 0) return cudaSuccess;
+  return launch_kernel(rmsnorm_quant_kernel, dim3(ntok), dim3(256), 0, lc, x, w, dim, eps, q, s, y);
+}
+
+// Embedding gather: x[t][k] = value of row tokens[t] (exact: int8 * f16 scale
+// fits in f32), zeros for ids >= vocab (base_transformer.rs:148-158).
+__global__ void __launch_bounds__(256) embed_kernel(int fmt, const uint8_t* __restrict__ wq,
+                                                    const uint8_t* __restrict__ ws, uint32_t row_bytes,
+                                                    uint32_t scale_row_bytes, uint32_t dim, uint32_t vocab,
+                                                    const uint32_t* __restrict__ tokens, const StepState* state,
+                                                    float* __restrict__ x) {
+  grid_dep_launch();
+  grid_dep_wait();
+  const uint32_t t = blockIdx.y;
+  const uint32_t k = blockIdx.x * 256 + threadIdx.x;
+  if (k >= dim) return;
+  const uint32_t id = state ? (uint32_t)state->token : tokens[t];
+  float v = 0.0f;
+  if (id < vocab) {
+    const uint8_t* row = wq + (uint64_t)id * row_bytes;
+    if (fmt == FMT_F16) {
+      v = __half2float(reinterpret_cast<const __half*>(row)[k]);
+    } else {
+      const float sc = __half2float(reinterpret_cast<const __half*>(ws + (uint64_t)id * scale_row_bytes)[k / 32]);
+      int qv;
+      if (fmt == FMT_Q8) {
+        qv = (int8_t)row[k];
+      } else {
+        const uint32_t j = k & 31;
+        const uint8_t byte = row[(k / 32) * 16 + (j & 15)];
+        qv = (int)(j < 16 ? (byte & 0xF) : (byte >> 4)) - 8;
+      }
+      v = __fmul_rn((float)qv, sc);
+    }
+  }
+  x[(uint64_t)t * dim + k] = v;
+}
+
+cudaError_t embed(int fmt, const uint8_t* wq, const uint8_t* ws, uint32_t row_bytes, uint32_t scale_row_bytes,
+                  uint32_t dim, uint32_t vocab, const uint32_t* tokens, const StepState* state, uint32_t ntok,
+                  float* x, const LaunchCfg& lc) {
+  if (ntok == 0) return cudaSuccess;
+  return launch_kernel(embed_kernel, dim3((dim + 255) / 256, ntok), dim3(256), 0, lc, fmt, wq, ws, row_bytes,
+                       scale_row_bytes, dim, vocab, tokens, state, x);
+}
+
+// sampler.rs:67-79: index of the first strictly-greatest value. NaNs never
+// win; if logits[0] is NaN the reference returns 0 (nothing compares greater).
+__device__ __forceinline__ bool better(float v, uint32_t i, float bv, uint32_t bi) {
+  return v > bv || (v == bv && i < bi);
+}
+
+__global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ logits, uint32_t n,
+                                                      uint32_t* __restrict__ out, StepState* state) {
+  grid_dep_launch();
+  grid_dep_wait();
+  __shared__ float sv[32];
+  __shared__ uint32_t si[32];
+  float bv = -INFINITY;
+  uint32_t bi = 0xFFFFFFFFu;
+  for (uint32_t i = threadIdx.x; i < n; i += 1024) {
+    const float v = logits[i];
+    if (v == v && better(v, i, bv, bi)) { bv = v; bi = i; }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(FULL, bv, o);
+    const uint32_t oi = __shfl_xor_sync(FULL, bi, o);
+    if (better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) { sv[warp] = bv; si[warp] = bi; }
+  __syncthreads();
+  if (warp == 0) {
+    bv = sv[lane];
+    bi = si[lane];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(FULL, bv, o);
+      const uint32_t oi = __shfl_xor_sync(FULL, bi, o);
+      if (better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+    }
+    if (lane == 0) {
+      uint32_t r = bi == 0xFFFFFFFFu ? 0u : bi;
+      if (logits[0] != logits[0]) r = 0;
+      if (out) out[state ? state->steps : 0] = r;
+      if (state) {
+        state->next = (int32_t)r;
+        state->token = (int32_t)r;
+        state->pos += 1;
+        state->steps += 1;
+      }
+    }
+  }
+}
+
+cudaError_t argmax(const float* logits, uint32_t n, uint32_t* out, StepState* state, const LaunchCfg& lc) {
+  return launch_kernel(argmax_kernel, dim3(1), dim3(1024), 0, lc, logits, n, out, state);
+}
+
+}  // namespace k
+}  // namespace yl

@@ -1,0 +1,134 @@
+// Device helpers shared by the sm_100a kernels: PTX wrappers (mbarrier, 1-D
+// bulk async copies, programmatic dependent launch), bounded waits, and the
+// bit-exact Q8_0 block quantizer.
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace yl {
+namespace dev {
+
+constexpr unsigned FULL = 0xFFFFFFFFu;
+
+// Error word codes written by kernels into their `err` argument.
+enum : int { ERR_NONE = 0, ERR_WAIT_TIMEOUT = 1, ERR_BAD_ARG = 2 };
+
+// ---- programmatic dependent launch -------------------------------------
+// Wait until the preceding kernel in the stream has completed and its writes
+// are visible. A no-op when the kernel was launched without the PDL attribute.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Allow the next kernel in the stream to be scheduled (it still waits in
+// grid_dep_wait() for this grid to finish before reading our outputs).
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// ---- time ----------------------------------------------------------------
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// ---- mbarrier --------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_fence_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: gives up after `limit_ns` and records ERR_WAIT_TIMEOUT.
+// Returns false on timeout so the caller can stop issuing work.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err,
+                                          uint64_t limit_ns = 2000000000ull) {
+  if (mbar_try_wait(bar, parity)) return true;
+  uint64_t t0 = global_ns();
+  for (uint32_t it = 0;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 255u) == 255u && global_ns() - t0 > limit_ns) {
+      if (err) atomicExch(err, ERR_WAIT_TIMEOUT);
+      return false;
+    }
+  }
+}
+
+// ---- 1-D bulk async copy global -> shared (TMA, non-tensor) --------------
+// Both addresses 16-byte aligned, size a multiple of 16. Completion is
+// signalled on `bar` as transaction bytes. Weights are streamed once per
+// step, so they are marked evict-first in L2.
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+__device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src, uint32_t bytes, uint64_t* bar,
+                                         uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], "
+      "%4;" ::"r"(smem_u32(dst_smem)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+// ---- named barrier over a subset of warps ---------------------------------
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// ---- integer dot ----------------------------------------------------------
+__device__ __forceinline__ int dp4a(int a, int b, int c) { return __dp4a(a, b, c); }
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(FULL, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(FULL, v, o));
+  return v;
+}
+
+// ---- Q8_0 quantization of one 32-element block by one warp ----------------
+// quantization.rs:29-52: wmax = max |x| (NaN never wins the `>` scan, the
+// scan starts from 0), scale = wmax / 127 (IEEE f32 division),
+// q = round-half-away-from-zero(x / scale) converted like Rust `as i8`
+// (saturating, NaN -> 0). Lane i holds element i; returns lane i's int8, the
+// scale is returned in every lane.
+__device__ __forceinline__ int8_t rust_as_i8(float v) {
+  if (v != v) return 0;
+  if (v >= 127.0f) return 127;
+  if (v <= -128.0f) return -128;
+  return (int8_t)(int)v;
+}
+__device__ __forceinline__ int8_t quant_q8_lane(float x, float* scale_out) {
+  float a = fabsf(x);
+  a = (a > 0.0f) ? a : 0.0f;  // NaN -> 0 so it never becomes the max
+  float wmax = warp_max(a);
+  float scale = __fdiv_rn(wmax, 127.0f);
+  *scale_out = scale;
+  return rust_as_i8(roundf(__fdiv_rn(x, scale)));
+}
+
+}  // namespace dev
+}  // namespace yl

@@ -1,0 +1,117 @@
+// Host-visible interface of the device kernels (launch wrappers + argument
+// structs). Every wrapper enqueues on lc.stream and returns the launch error;
+// with lc.pdl set the launch carries the programmatic-stream-serialization
+// attribute so the kernel may start while its predecessor drains (each kernel
+// calls griddepcontrol.wait before touching data the predecessor produced).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace yl {
+namespace k {
+
+enum Fmt : int { FMT_Q8 = 0, FMT_Q4 = 1, FMT_F16 = 2, FMT_Q8F = 3, FMT_Q4F = 4 };
+enum Epi : int { EPI_STORE = 0, EPI_ADD = 1, EPI_QUIRK = 2, EPI_SWIGLU = 3 };
+
+struct LaunchCfg {
+  cudaStream_t stream = nullptr;
+  bool pdl = false;
+  uint32_t grid = 0;              // 0 = kernel default (number of SMs)
+  uint32_t smem_budget = 100 * 1024;
+};
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_kernel(void (*kern)(KArgs...), dim3 grid, dim3 block, uint32_t smem, const LaunchCfg& lc,
+                                 Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = lc.stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = lc.pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
+// ---- matvec -------------------------------------------------------------
+struct MvArgs {
+  const uint8_t* wq;        // weight quants (row-major, row_bytes per row)
+  const uint8_t* ws;        // weight scales (row stride scale_row_bytes), null for F16
+  uint32_t rows, K;
+  uint32_t row_bytes, scale_row_bytes;
+  uint32_t kc;              // K-chunk per stage (elements, multiple of 256)
+  int stages;               // set by the launcher
+  const int8_t* xq;         // int8 activations [ntok][x_tok_stride]
+  const float* xs;          // activation scales [ntok][xs_tok_stride]
+  const float* xf;          // f32 activations [ntok][x_tok_stride] (F16 / lm_head)
+  uint64_t x_tok_stride, xs_tok_stride;
+  uint32_t ntok;            // tokens in this pass (<= 8)
+  float* out;
+  uint64_t out_tok_stride;
+  uint32_t quirk_cols;      // EPI_QUIRK: columns below this add, the rest store
+  int* err;
+};
+// fmt: FMT_*; scale_f16: weight scale type. Chooses NT from a.ntok.
+cudaError_t matvec(const MvArgs& a, int fmt, bool scale_f16, int epi, const LaunchCfg& lc);
+
+// ---- activations ------------------------------------------------------------
+// Bit-exact Q8_0 quantization of nblocks 32-element blocks (warp per block).
+cudaError_t quantize_q8(const float* x, int8_t* q, float* s, uint64_t nblocks, const LaunchCfg& lc);
+// RMSNorm (util.rs:389-426) of ntok rows of `dim`, then Q8_0 quantization of
+// the normalized rows into q/s (if q != null) and/or the f32 rows into y.
+cudaError_t rmsnorm_quant(const float* x, const float* w, uint32_t ntok, uint32_t dim, float eps, int8_t* q,
+                          float* s, float* y, const LaunchCfg& lc);
+
+// Embedding rows (base_transformer.rs:143-161 over the dequantized table of
+// transformer_llama_gguf.rs:453-489): x[t] = row(tokens[t]) as f32, zeros for
+// out-of-range ids. tokens: device ids; if tok_from_state, tokens[0] is read
+// from state->token.
+struct StepState {
+  int32_t pos;    // position of the token being processed
+  int32_t token;  // token id being processed
+  int32_t next;   // greedy id produced by this step
+  int32_t steps;  // number of device steps executed
+};
+cudaError_t embed(int fmt, const uint8_t* wq, const uint8_t* ws, uint32_t row_bytes, uint32_t scale_row_bytes,
+                  uint32_t dim, uint32_t vocab, const uint32_t* tokens, const StepState* state, uint32_t ntok,
+                  float* x, const LaunchCfg& lc);
+
+// RoPE + KV-cache write. qkv: [ntok][att_dim + 2 kv_dim] (q | k | v) from the
+// fused projection; q_out: [ntok][att_dim] rotated; k/v rows go to
+// kcache/vcache [ctx][kv_dim] (layer base) at positions pos0 + t. pos0 comes
+// from state->pos when state != null. cs: cos/sin table [ctx][head_size/2].
+cudaError_t rope_kv(const float* qkv, uint32_t ntok, uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_size,
+                    int rope_mode, const float2* cs, uint32_t ctx_len, const StepState* state, uint32_t pos0,
+                    float* q_out, float* kcache, float* vcache, const LaunchCfg& lc);
+
+// Causal GQA attention (forward.rs:299-400) for ntok queries at positions
+// pos0..pos0+ntok-1 over kcache/vcache [ctx][kv_dim]. Split-sequence with
+// partials in `part` when n_splits > 1; the combine also quantizes the output
+// per 32-block into q/s (Q8_0) and/or writes f32 into out.
+struct AttnArgs {
+  const float* q;
+  const float* kcache;
+  const float* vcache;
+  uint32_t ntok, n_heads, n_kv_heads, head_size, kv_dim;
+  const StepState* state;
+  uint32_t pos0;
+  float scale;
+  uint32_t n_splits;
+  float* part;  // [ntok][n_heads][n_splits][head_size + 2]
+  float* out;   // [ntok][n_heads*head_size] f32 (nullable)
+  int8_t* q8;   // [ntok][n_heads*head_size] (nullable)
+  float* s8;    // [ntok][n_heads*head_size/32]
+};
+cudaError_t attention(const AttnArgs& a, const LaunchCfg& lc);
+
+// Greedy argmax over n logits (sampler.rs:67-79: the lowest index among equal
+// maxima). Writes out[0]; with state != null also state->next/token/pos/steps
+// for the device-resident decode loop.
+cudaError_t argmax(const float* logits, uint32_t n, uint32_t* out, StepState* state, const LaunchCfg& lc);
+
+// Copies state->token/pos from a host-written staging struct (graph input).
+}  // namespace k
+}  // namespace yl
