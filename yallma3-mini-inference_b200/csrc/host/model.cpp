@@ -619,7 +619,10 @@ int run_matvec(const DevWeight& w, bool f32act, const int8_t* xq, const float* x
   lc.pdl = pdl;
   lc.grid = (uint32_t)num_sms * tu.grid_mult;
   lc.smem_budget = tu.smem;
-  for (uint32_t t0 = 0; t0 < ntok; t0 += 8) {
+  const uint32_t kc_eff = std::min<uint32_t>(kc, (uint32_t)round_up(w.cols, 256));
+  const uint32_t group = k::matvec_max_ntok(fmt, w.cols, kc_eff, epi);
+  if (group == 0) return fail(YL_ERR_UNSUPPORTED, "matvec row length too large for shared memory");
+  for (uint32_t t0 = 0; t0 < ntok; t0 += group) {
     k::MvArgs a{};
     a.wq = w.q;
     a.ws = w.s;
@@ -627,13 +630,13 @@ int run_matvec(const DevWeight& w, bool f32act, const int8_t* xq, const float* x
     a.K = w.cols;
     a.row_bytes = w.row_bytes;
     a.scale_row_bytes = w.scale_row_bytes;
-    a.kc = std::min<uint32_t>(kc, (uint32_t)round_up(w.cols, 256));
+    a.kc = kc_eff;
     a.xq = xq ? xq + t0 * x_stride : nullptr;
     a.xs = xs ? xs + t0 * xs_stride : nullptr;
     a.xf = xf ? xf + t0 * x_stride : nullptr;
     a.x_tok_stride = x_stride;
     a.xs_tok_stride = xs_stride;
-    a.ntok = std::min(8u, ntok - t0);
+    a.ntok = std::min(group, ntok - t0);
     a.out = out + t0 * out_stride;
     a.out_tok_stride = out_stride;
     a.quirk_cols = quirk_cols;
@@ -671,7 +674,7 @@ int enqueue_forward(Session* s, uint32_t n, uint32_t start_pos, bool from_state,
 #define YL_MV(...)                                  \
   do {                                              \
     if ((rc = run_matvec(__VA_ARGS__))) return rc;  \
-    nl += (n + 7) / 8;                              \
+    nl += 1;                                        \
   } while (0)
 
   YL_LAUNCH(k::embed(m->emb.fmt == YL_Q8_0 ? k::FMT_Q8 : m->emb.fmt == YL_Q4_0 ? k::FMT_Q4 : k::FMT_F16, m->emb.q,

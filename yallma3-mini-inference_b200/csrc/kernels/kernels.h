@@ -56,6 +56,9 @@ struct MvArgs {
 };
 // fmt: FMT_*; scale_f16: weight scale type. Chooses NT from a.ntok.
 cudaError_t matvec(const MvArgs& a, int fmt, bool scale_f16, int epi, const LaunchCfg& lc);
+// Largest tokens-per-pass (1, 2, 4 or 8) whose shared-memory layout fits with
+// at least two ring stages.
+uint32_t matvec_max_ntok(int fmt, uint32_t K, uint32_t kc, int epi);
 
 // ---- activations ------------------------------------------------------------
 // Bit-exact Q8_0 quantization of nblocks 32-element blocks (warp per block).

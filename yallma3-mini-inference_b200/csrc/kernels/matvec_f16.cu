@@ -7,6 +7,28 @@ namespace k {
 cudaError_t matvec_q8(const MvArgs& a, int fmt, bool sf16, int epi, const LaunchCfg& lc);
 cudaError_t matvec_q4(const MvArgs& a, int fmt, bool sf16, int epi, const LaunchCfg& lc);
 
+template <int FMT>
+static uint32_t max_ntok_fmt(uint32_t K, uint32_t kc, int rpw) {
+  const uint32_t lim = 227u * 1024u;
+  if (mv_layout<FMT, 8>(K, kc, rpw, 2).total <= lim) return 8;
+  if (mv_layout<FMT, 4>(K, kc, rpw, 2).total <= lim) return 4;
+  if (mv_layout<FMT, 2>(K, kc, rpw, 2).total <= lim) return 2;
+  if (mv_layout<FMT, 1>(K, kc, rpw, 2).total <= lim) return 1;
+  return 0;
+}
+
+uint32_t matvec_max_ntok(int fmt, uint32_t K, uint32_t kc, int epi) {
+  const int rpw = epi == EPI_SWIGLU ? 2 : 1;
+  switch (fmt) {
+    case FMT_Q8: return max_ntok_fmt<FMT_Q8>(K, kc, rpw);
+    case FMT_Q8F: return max_ntok_fmt<FMT_Q8F>(K, kc, rpw);
+    case FMT_Q4: return max_ntok_fmt<FMT_Q4>(K, kc, rpw);
+    case FMT_Q4F: return max_ntok_fmt<FMT_Q4F>(K, kc, rpw);
+    case FMT_F16: return max_ntok_fmt<FMT_F16>(K, kc, rpw);
+  }
+  return 0;
+}
+
 cudaError_t matvec(const MvArgs& a, int fmt, bool sf16, int epi, const LaunchCfg& lc) {
   if (a.K % 32 || a.kc % 256 || a.kc == 0 || a.ntok == 0 || a.ntok > 8) return cudaErrorInvalidValue;
   switch (fmt) {
