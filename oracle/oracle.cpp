@@ -27,6 +27,7 @@
 namespace {
 
 thread_local std::string g_err;
+int g_probe = 0;
 
 /* Rust `f as i8`: saturating, NaN -> 0. */
 inline int8_t rust_f32_as_i8(float v) {
@@ -92,6 +93,7 @@ float orc_f16_to_f32(uint16_t h) {
 }
 
 void orc_set_threads(int n) { if (n > 0) omp_set_num_threads(n); }
+void orc_set_probe(int flags) { g_probe = flags; }
 int orc_get_threads(void) { return omp_get_max_threads(); }
 
 /* quantization.rs:29-52 */
@@ -251,6 +253,11 @@ void orc_rmsnorm(float* o, const float* x, const float* weight, size_t size, flo
       lanes[l] = lanes[l] + p;
     }
   float ss = reduce_add8(lanes);
+  if (g_probe & 1) {
+    double sd = 0.0;
+    for (size_t i = 0; i < n_simd * 8; ++i) sd += (double)x[i] * (double)x[i];
+    ss = (float)sd;
+  }
   ss = ss / (float)size;
   ss = ss + eps;
   ss = 1.0f / sqrtf(ss);

@@ -54,6 +54,12 @@ typedef struct orc_shape {
 
 /* ---- numeric kernels ---------------------------------------------------- */
 void orc_set_threads(int n);
+/* Sensitivity probe (test infrastructure): flags != 0 perturbs the oracle by
+ * at most one rounding step. Bit 0: the rmsnorm sum of squares is accumulated
+ * in double instead of the reference's 8-lane f32 fold. Used only to measure
+ * how far a model's logits move under a 1-ulp change (how sensitive a test
+ * model is to activation-quantization flips); 0 = the faithful restatement. */
+void orc_set_probe(int flags);
 int orc_get_threads(void);
 
 void orc_quantize_q8(int8_t* q, float* scale, const float* x, size_t n, uint32_t gs);

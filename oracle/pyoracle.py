@@ -45,6 +45,7 @@ def lib() -> C.CDLL:
         sig = {
             "orc_set_threads": (None, [C.c_int]),
             "orc_get_threads": (C.c_int, []),
+            "orc_set_probe": (None, [C.c_int]),
             "orc_quantize_q8": (None, [P, P, P, C.c_size_t, C.c_uint32]),
             "orc_quantize_q4_ref": (None, [P, P, P, C.c_size_t, C.c_uint32]),
             "orc_matmul_q8_slices": (None, [P, C.c_size_t, P, P, P, P, C.c_size_t, C.c_size_t, C.c_size_t]),
@@ -86,6 +87,12 @@ def _p(a: np.ndarray) -> int:
 
 def set_threads(n: int) -> None:
     lib().orc_set_threads(n)
+
+
+def set_probe(flags: int) -> None:
+    """0 = faithful restatement; 1 = rmsnorm sum of squares in f64 (a 1-ulp
+    perturbation used to measure a test model's sensitivity)."""
+    lib().orc_set_probe(flags)
 
 
 def quantize_q8(x: np.ndarray, gs: int = 32):

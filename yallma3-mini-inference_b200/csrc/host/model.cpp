@@ -546,6 +546,10 @@ int ensure_cap(Session* s, uint32_t n) {
   s->q = (float*)p;
   if ((rc = salloc(s, cap * (uint64_t)sh.hidden_dim * 4ull, &p))) return rc;
   s->h = (float*)p;
+  if ((rc = salloc(s, cap * (uint64_t)sh.hidden_dim, &p))) return rc;
+  s->hq = (int8_t*)p;
+  if ((rc = salloc(s, cap * (uint64_t)(sh.hidden_dim / 32) * 4ull, &p))) return rc;
+  s->hs = (float*)p;
   if ((rc = salloc(s, cap * 4ull, &p))) return rc;
   s->tok = (uint32_t*)p;
   s->cap = cap;
@@ -579,6 +583,17 @@ int session_create(const Model* m, Session** out) {
   s->part = (float*)p;
   if ((rc = salloc(s.get(), ((uint64_t)sh.ctx_len + 1) * 4, &p))) return rc;
   s->hist = (uint32_t*)p;
+  if ((rc = salloc(s.get(), (uint64_t)sh.n_kv_heads * 4, &p))) return rc;
+  s->att_count = (unsigned int*)p;
+  YL_CUDA_TRY(cudaMemset(s->att_count, 0, (uint64_t)sh.n_kv_heads * 4));
+  const uint64_t am_slots = (uint64_t)m->num_sms * 8;
+  if ((rc = salloc(s.get(), am_slots * 4, &p))) return rc;
+  s->am_val = (float*)p;
+  if ((rc = salloc(s.get(), am_slots * 4, &p))) return rc;
+  s->am_idx = (uint32_t*)p;
+  if ((rc = salloc(s.get(), sizeof(unsigned int), &p))) return rc;
+  s->am_count = (unsigned int*)p;
+  YL_CUDA_TRY(cudaMemset(s->am_count, 0, sizeof(unsigned int)));
   if ((rc = salloc(s.get(), sizeof(k::StepState), &p))) return rc;
   s->state = (k::StepState*)p;
   if ((rc = salloc(s.get(), sizeof(int), &p))) return rc;
@@ -607,6 +622,14 @@ int session_reset(Session* s) {
 int run_matvec(const DevWeight& w, bool f32act, const int8_t* xq, const float* xs, const float* xf, uint64_t x_stride,
                uint64_t xs_stride, uint32_t ntok, float* out, uint64_t out_stride, int epi, uint32_t quirk_cols,
                int* err, cudaStream_t st, bool pdl, int num_sms) {
+  return run_matvec_ex(w, f32act, xq, xs, xf, x_stride, xs_stride, ntok, out, out_stride, epi, quirk_cols, err, st,
+                       pdl, num_sms, MvExtra(), nullptr);
+}
+
+int run_matvec_ex(const DevWeight& w, bool f32act, const int8_t* xq, const float* xs, const float* xf,
+                  uint64_t x_stride, uint64_t xs_stride, uint32_t ntok, float* out, uint64_t out_stride, int epi,
+                  uint32_t quirk_cols, int* err, cudaStream_t st, bool pdl, int num_sms, const MvExtra& ex,
+                  uint32_t* launches) {
   const Tunables& tu = tunables();
   int fmt;
   uint32_t kc;
@@ -641,8 +664,20 @@ int run_matvec(const DevWeight& w, bool f32act, const int8_t* xq, const float* x
     a.out_tok_stride = out_stride;
     a.quirk_cols = quirk_cols;
     a.err = err;
+    a.pro = ex.pro;
+    a.xres = ex.xres ? ex.xres + t0 * x_stride : nullptr;
+    a.norm_w = ex.norm_w;
+    a.eps = ex.eps;
+    a.hq = ex.hq ? ex.hq + t0 * (uint64_t)(w.rows / 2) : nullptr;
+    a.hs = ex.hs ? ex.hs + t0 * (uint64_t)(w.rows / 64) : nullptr;
+    a.am_val = ex.am_val;
+    a.am_idx = ex.am_idx;
+    a.am_count = ex.am_count;
+    a.am_out = ex.am_out;
+    a.state = ex.state;
     cudaError_t e = k::matvec(a, fmt, w.sf16, epi, lc);
     if (e != cudaSuccess) return fail(YL_ERR_CUDA, std::string("matvec launch: ") + cudaGetErrorString(e));
+    if (launches) ++*launches;
   }
   return YL_OK;
 }
@@ -656,7 +691,6 @@ int enqueue_forward(Session* s, uint32_t n, uint32_t start_pos, bool from_state,
   const Model* m = s->m;
   const yl_shape& sh = m->shape;
   const uint32_t d = sh.dim, att = sh.n_heads * sh.head_size, kvd = sh.n_kv_heads * sh.head_size, f = sh.hidden_dim;
-  const uint64_t wmax = std::max<uint64_t>({d, att, f});
   const bool f32act = sh.weight_format == YL_F16;
   const k::StepState* st = from_state ? s->state : nullptr;
   k::LaunchCfg lc;
@@ -679,60 +713,101 @@ int enqueue_forward(Session* s, uint32_t n, uint32_t start_pos, bool from_state,
 
   YL_LAUNCH(k::embed(m->emb.fmt == YL_Q8_0 ? k::FMT_Q8 : m->emb.fmt == YL_Q4_0 ? k::FMT_Q4 : k::FMT_F16, m->emb.q,
                      m->emb.s, m->emb.row_bytes, m->emb.scale_row_bytes, d, sh.vocab_size, s->tok, st, n, s->x, lc));
-  const uint32_t n_splits = n == 1 ? s->n_splits : 1;
+  const bool decode = n == 1;
+  MvExtra norm;
+  norm.pro = k::PRO_NORM;
+  norm.xres = s->x;
+  norm.eps = sh.rms_norm_eps;
   for (uint32_t l = 0; l < sh.n_layers; ++l) {
     const Layer& L = m->layers[l];
     float* kc = s->kcache + (uint64_t)l * sh.ctx_len * kvd;
     float* vc = s->vcache + (uint64_t)l * sh.ctx_len * kvd;
-    // attention block (forward.rs:154-204)
-    YL_LAUNCH(k::rmsnorm_quant(s->x, L.rms_att, n, d, sh.rms_norm_eps, f32act ? nullptr : s->xq, s->xs,
-                               f32act ? s->xf : nullptr, lc));
-    YL_MV(L.wqkv, f32act, s->xq, s->xs, s->xf, d, d / 32, n, s->qkv, att + 2 * kvd, k::EPI_STORE, 0, s->err, s->stream,
-          pdl, m->num_sms);
-    YL_LAUNCH(k::rope_kv(s->qkv, n, sh.n_heads, sh.n_kv_heads, sh.head_size, sh.rope_mode, m->rope_cs, sh.ctx_len, st,
-                         start_pos, s->q, kc, vc, lc));
-    k::AttnArgs aa{};
-    aa.q = s->q;
-    aa.kcache = kc;
-    aa.vcache = vc;
-    aa.ntok = n;
-    aa.n_heads = sh.n_heads;
-    aa.n_kv_heads = sh.n_kv_heads;
-    aa.head_size = sh.head_size;
-    aa.kv_dim = kvd;
-    aa.state = st;
-    aa.pos0 = start_pos;
-    aa.scale = m->attn_scale;
-    aa.n_splits = n_splits;
-    aa.part = s->part;
-    aa.out = f32act ? s->xf : nullptr;
-    aa.q8 = f32act ? nullptr : s->xq;
-    aa.s8 = s->xs;
-    YL_LAUNCH(k::attention(aa, lc));
-    if (n_splits > 1) ++nl;
+    // ---- attention block (forward.rs:154-204) ----
+    // RMSNorm + quantize fused into the QKV projection's prologue
+    norm.norm_w = L.rms_att;
+    norm.hq = nullptr;
+    norm.hs = nullptr;
+    if ((rc = run_matvec_ex(L.wqkv, f32act, nullptr, nullptr, nullptr, d, d / 32, n, s->qkv, att + 2 * kvd,
+                            k::EPI_STORE, 0, s->err, s->stream, pdl, m->num_sms, norm, &nl)))
+      return rc;
+    if (decode) {
+      // RoPE, KV write, split attention, merge and quantize in one kernel
+      k::AttnDecodeArgs ad{};
+      ad.qkv = s->qkv;
+      ad.cs = m->rope_cs;
+      ad.rope_mode = sh.rope_mode;
+      ad.kcache = kc;
+      ad.vcache = vc;
+      ad.n_heads = sh.n_heads;
+      ad.n_kv_heads = sh.n_kv_heads;
+      ad.head_size = sh.head_size;
+      ad.kv_dim = kvd;
+      ad.state = st;
+      ad.pos0 = start_pos;
+      ad.scale = m->attn_scale;
+      ad.n_splits = s->n_splits;
+      ad.part = s->part;
+      ad.count = s->att_count;
+      ad.out = f32act ? s->xf : nullptr;
+      ad.q8 = f32act ? nullptr : s->xq;
+      ad.s8 = s->xs;
+      YL_LAUNCH(k::attention_decode(ad, lc));
+    } else {
+      YL_LAUNCH(k::rope_kv(s->qkv, n, sh.n_heads, sh.n_kv_heads, sh.head_size, sh.rope_mode, m->rope_cs, sh.ctx_len,
+                           st, start_pos, s->q, kc, vc, lc));
+      k::AttnArgs aa{};
+      aa.q = s->q;
+      aa.kcache = kc;
+      aa.vcache = vc;
+      aa.ntok = n;
+      aa.n_heads = sh.n_heads;
+      aa.n_kv_heads = sh.n_kv_heads;
+      aa.head_size = sh.head_size;
+      aa.kv_dim = kvd;
+      aa.state = st;
+      aa.pos0 = start_pos;
+      aa.scale = m->attn_scale;
+      aa.n_splits = 1;
+      aa.part = s->part;
+      aa.out = f32act ? s->xf : nullptr;
+      aa.q8 = f32act ? nullptr : s->xq;
+      aa.s8 = s->xs;
+      YL_LAUNCH(k::attention(aa, lc));
+    }
+    // wo projection + residual add
     YL_MV(L.wo, f32act, s->xq, s->xs, s->xf, att, att / 32, n, s->x, d, k::EPI_ADD, 0, s->err, s->stream, pdl,
           m->num_sms);
-    // feed-forward block (forward.rs:206-253)
-    YL_LAUNCH(k::rmsnorm_quant(s->x, L.rms_ffn, n, d, sh.rms_norm_eps, f32act ? nullptr : s->xq, s->xs,
-                               f32act ? s->xf : nullptr, lc));
-    YL_MV(L.w13, f32act, s->xq, s->xs, s->xf, d, d / 32, n, s->h, f, k::EPI_SWIGLU, 0, s->err, s->stream, pdl,
-          m->num_sms);
-    // F16Kernel::quantize is a copy (forward.rs:78-81): the F16 path reads h directly
-    if (!f32act) YL_LAUNCH(k::quantize_q8(s->h, s->xq, s->xs, (uint64_t)n * f / 32, lc));
-    YL_MV(L.w2, f32act, s->xq, s->xs, f32act ? s->h : s->xf, f, f / 32, n, s->x, d, k::EPI_ADD, 0, s->err, s->stream,
-          pdl, m->num_sms);
-  }
-  // final norm on the last token, lm_head, greedy id (forward.rs:256-279)
-  const float* xlast = s->x + (uint64_t)(n - 1) * d;
-  YL_LAUNCH(k::rmsnorm_quant(xlast, m->rms_final, 1, d, sh.rms_norm_eps, nullptr, nullptr, s->xf, lc));
-  {
-    const DevWeight& lm = m->lm;
-    if ((rc = run_matvec(lm, true, nullptr, nullptr, s->xf, d, 0, 1, s->logits, sh.vocab_size, k::EPI_STORE, 0, s->err,
-                         s->stream, pdl, m->num_sms)))
+    // ---- feed-forward block (forward.rs:206-253) ----
+    // RMSNorm + quantize in the prologue; SwiGLU (and, for quantized
+    // formats, the Q8_0 quantization of h) in the epilogue. F16Kernel's
+    // quantize is a copy (forward.rs:78-81), so the F16 path keeps h in f32.
+    norm.norm_w = L.rms_ffn;
+    norm.hq = f32act ? nullptr : s->hq;
+    norm.hs = f32act ? nullptr : s->hs;
+    if ((rc = run_matvec_ex(L.w13, f32act, nullptr, nullptr, nullptr, d, d / 32, n, s->h, f,
+                            f32act ? k::EPI_SWIGLU : k::EPI_SWIGLU_Q8, 0, s->err, s->stream, pdl, m->num_sms, norm,
+                            &nl)))
       return rc;
-    ++nl;
+    YL_MV(L.w2, f32act, s->hq, s->hs, s->h, f, f / 32, n, s->x, d, k::EPI_ADD, 0, s->err, s->stream, pdl,
+          m->num_sms);
   }
-  YL_LAUNCH(k::argmax(s->logits, sh.vocab_size, s->hist, from_state ? s->state : nullptr, lc));
+  // final norm (prologue), lm_head on the last token and greedy id
+  // (forward.rs:256-279, sampler.rs:67-79)
+  {
+    MvExtra fin;
+    fin.pro = k::PRO_NORM;
+    fin.xres = s->x + (uint64_t)(n - 1) * d;
+    fin.norm_w = m->rms_final;
+    fin.eps = sh.rms_norm_eps;
+    fin.am_val = s->am_val;
+    fin.am_idx = s->am_idx;
+    fin.am_count = s->am_count;
+    fin.am_out = s->hist;
+    fin.state = from_state ? s->state : nullptr;
+    if ((rc = run_matvec_ex(m->lm, true, nullptr, nullptr, nullptr, d, 0, 1, s->logits, sh.vocab_size, k::EPI_ARGMAX,
+                            0, s->err, s->stream, pdl, m->num_sms, fin, &nl)))
+      return rc;
+  }
 #undef YL_LAUNCH
 #undef YL_MV
   if (launches) *launches = nl;

@@ -66,9 +66,15 @@ struct Session {
   float* qkv = nullptr;   // [cap][att + 2 kv]
   float* q = nullptr;     // [cap][att]
   float* h = nullptr;     // [cap][ffn]
+  int8_t* hq = nullptr;   // [cap][ffn] quantized h (SwiGLU epilogue)
+  float* hs = nullptr;    // [cap][ffn/32]
   uint32_t* tok = nullptr;  // [cap]
   float* logits = nullptr;  // [vocab]
   float* part = nullptr;    // attention split partials (decode)
+  unsigned int* att_count = nullptr;  // [n_kv_heads] arrival counters (zero between launches)
+  float* am_val = nullptr;            // lm_head per-CTA winners
+  uint32_t* am_idx = nullptr;
+  unsigned int* am_count = nullptr;
   uint32_t* hist = nullptr; // [ctx_len] greedy ids of device steps
   k::StepState* state = nullptr;
   int* err = nullptr;
@@ -103,5 +109,23 @@ const Tunables& tunables();
 int run_matvec(const DevWeight& w, bool f32act, const int8_t* xq, const float* xs, const float* xf,
                uint64_t x_stride, uint64_t xs_stride, uint32_t ntok, float* out, uint64_t out_stride, int epi,
                uint32_t quirk_cols, int* err, cudaStream_t st, bool pdl, int num_sms);
+// Optional prologue / epilogue operands of run_matvec_ex.
+struct MvExtra {
+  int pro = 0;                 // k::PRO_*
+  const float* xres = nullptr; // PRO_NORM: residual rows (stride x_stride)
+  const float* norm_w = nullptr;
+  float eps = 0.f;
+  int8_t* hq = nullptr;        // EPI_SWIGLU_Q8 outputs
+  float* hs = nullptr;
+  float* am_val = nullptr;     // EPI_ARGMAX scratch / outputs
+  uint32_t* am_idx = nullptr;
+  unsigned int* am_count = nullptr;
+  uint32_t* am_out = nullptr;
+  k::StepState* state = nullptr;
+};
+int run_matvec_ex(const DevWeight& w, bool f32act, const int8_t* xq, const float* xs, const float* xf,
+                  uint64_t x_stride, uint64_t xs_stride, uint32_t ntok, float* out, uint64_t out_stride, int epi,
+                  uint32_t quirk_cols, int* err, cudaStream_t st, bool pdl, int num_sms, const MvExtra& ex,
+                  uint32_t* launches);
 
 }  // namespace yl

@@ -11,7 +11,16 @@ namespace yl {
 namespace k {
 
 enum Fmt : int { FMT_Q8 = 0, FMT_Q4 = 1, FMT_F16 = 2, FMT_Q8F = 3, FMT_Q4F = 4 };
-enum Epi : int { EPI_STORE = 0, EPI_ADD = 1, EPI_QUIRK = 2, EPI_SWIGLU = 3 };
+// EPI_SWIGLU_Q8: SwiGLU on (gate, up) row pairs, f32 h stored and h quantized
+// to Q8_0 blocks (for the next matvec). EPI_ARGMAX: store + greedy id over
+// all rows (last CTA to finish reduces the per-CTA winners).
+enum Epi : int { EPI_STORE = 0, EPI_ADD = 1, EPI_QUIRK = 2, EPI_SWIGLU = 3, EPI_SWIGLU_Q8 = 4, EPI_ARGMAX = 5 };
+// Activation prologue: PRO_LOAD reads prepared activations; PRO_NORM computes
+// RMSNorm of the f32 residual rows (util.rs:389-426) and quantizes them
+// (quantization.rs:29-52) into shared memory (f32 for f32-activation formats).
+enum Pro : int { PRO_LOAD = 0, PRO_NORM = 1 };
+
+struct StepState;
 
 struct LaunchCfg {
   cudaStream_t stream = nullptr;
@@ -53,6 +62,21 @@ struct MvArgs {
   uint64_t out_tok_stride;
   uint32_t quirk_cols;      // EPI_QUIRK: columns below this add, the rest store
   int* err;
+  // PRO_NORM: f32 residual rows [ntok][x_tok_stride] and the norm weight
+  int pro;
+  const float* xres;
+  const float* norm_w;
+  float eps;
+  // EPI_SWIGLU_Q8: quantized h [ntok][rows/2] + scales [ntok][rows/64]
+  int8_t* hq;
+  float* hs;
+  // EPI_ARGMAX: per-CTA winners, arrival counter (zero between launches),
+  // output id slot (hist[state->steps] or hist[0]) and the step state
+  float* am_val;
+  uint32_t* am_idx;
+  unsigned int* am_count;
+  uint32_t* am_out;
+  StepState* state;
 };
 // fmt: FMT_*; scale_f16: weight scale type. Chooses NT from a.ntok.
 cudaError_t matvec(const MvArgs& a, int fmt, bool scale_f16, int epi, const LaunchCfg& lc);
@@ -109,6 +133,30 @@ struct AttnArgs {
   float* s8;    // [ntok][n_heads*head_size/32]
 };
 cudaError_t attention(const AttnArgs& a, const LaunchCfg& lc);
+
+// Batch-1 decode attention with RoPE and the KV-cache write fused in:
+// q and the new k/v rows are taken unrotated from `qkv` ([att | k | v]),
+// rotated with cs[pos], the new k/v rows written at `pos`, then the split
+// partials are merged by the last CTA of each KV head (arrival counters in
+// `count`, zero between launches), which also quantizes the output.
+struct AttnDecodeArgs {
+  const float* qkv;
+  const float2* cs;  // [ctx][head_size/2]
+  int rope_mode;
+  float* kcache;
+  float* vcache;
+  uint32_t n_heads, n_kv_heads, head_size, kv_dim;
+  const StepState* state;
+  uint32_t pos0;
+  float scale;
+  uint32_t n_splits;
+  float* part;            // [n_heads][n_splits][head_size + 2]
+  unsigned int* count;    // [n_kv_heads]
+  float* out;             // [n_heads*head_size] f32 (nullable)
+  int8_t* q8;             // (nullable)
+  float* s8;
+};
+cudaError_t attention_decode(const AttnDecodeArgs& a, const LaunchCfg& lc);
 
 // Greedy argmax over n logits (sampler.rs:67-79: the lowest index among equal
 // maxima). Writes out[0]; with state != null also state->next/token/pos/steps

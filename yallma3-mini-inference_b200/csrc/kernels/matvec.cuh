@@ -11,14 +11,17 @@
 //    range of weight rows into a shared-memory ring with 1-D bulk async copies
 //    (cp.async.bulk, TMA engine) completing on mbarriers; weights are marked
 //    evict-first in L2;
-//  * 8 consumer warps read the ring with 128-bit conflict-free shared loads and
-//    do dp4a block dots (exact int32 per 32-element block) and the f32 scale
-//    fold; warp w owns RPW rows of every stage;
+//  * 8 consumer warps read the ring with 128-bit conflict-free shared loads,
+//    four independent chunks in flight per lane, and do dp4a block dots (exact
+//    int32 per 32-element block) and the f32 scale fold;
 //  * the producer starts streaming before griddepcontrol.wait, so under
-//    programmatic dependent launch the weight fetch of this kernel overlaps the
-//    tail of the previous kernel; consumers wait for the activations only.
-//  * epilogues: store, residual add, the reference's `+=` quirk, and SwiGLU on
-//    interleaved (gate, up) row pairs.
+//    programmatic dependent launch the weight fetch overlaps the tail of the
+//    previous kernel; consumers wait for the activations only;
+//  * prologue PRO_NORM fuses the RMSNorm + Q8_0 quantization of the residual
+//    stream (each CTA normalizes the row itself, a few KB from L2);
+//  * epilogues: store, residual add, the reference's `+=` quirk, SwiGLU on
+//    interleaved (gate, up) row pairs (optionally quantizing h per 32-block),
+//    and logits + greedy argmax.
 #pragma once
 #include "device.cuh"
 #include "kernels.h"
@@ -28,6 +31,7 @@ namespace k {
 
 constexpr int MV_NCW = 8;                   // consumer warps
 constexpr int MV_THREADS = 32 * (1 + MV_NCW);
+constexpr int MV_U = 4;                     // 16-byte chunks in flight per lane
 
 template <int FMT>
 __host__ __device__ constexpr uint32_t mv_qbytes(uint32_t kn) {
@@ -39,17 +43,19 @@ template <int FMT>
 __host__ __device__ constexpr bool mv_f32_act() {
   return FMT == FMT_F16 || FMT == FMT_Q8F || FMT == FMT_Q4F;
 }
+__host__ __device__ constexpr bool mv_swiglu(int epi) { return epi == EPI_SWIGLU || epi == EPI_SWIGLU_Q8; }
 
 // Shared-memory layout, computed identically on host and device.
 struct MvLayout {
-  uint32_t bar_off, x_off, xs_off, xsum_off, ring_off;
+  uint32_t bar_off, red_off, x_off, xs_off, xsum_off, ring_off;
   uint32_t stage_q_row, stage_s_row, stage_bytes, total;
 };
 template <int FMT, int NT>
 __host__ __device__ inline MvLayout mv_layout(uint32_t K, uint32_t kc, int rpw, int stages) {
   MvLayout L;
-  L.bar_off = 0;
-  uint32_t off = 256;
+  L.bar_off = 0;       // 2 x 8 mbarriers
+  L.red_off = 128;     // reductions / argmax / h staging ([2][8][32] floats)
+  uint32_t off = 128 + 2048 + 128;
   L.x_off = off;
   if (mv_f32_act<FMT>()) {
     off += NT * K * 4;
@@ -83,6 +89,315 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
   return __fmul_rn(s, u);
 }
 
+// int8 -> f32 for 4 packed bytes without the (quarter-rate) I2F unit:
+// 0x4B000000 | (b ^ 0x80) is the float 2^23 + b + 128, exact.
+__device__ __forceinline__ void i8x4_to_f32(uint32_t w, float& f0, float& f1, float& f2, float& f3) {
+  const uint32_t u = w ^ 0x80808080u;
+  f0 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7650)) - 8388736.0f;
+  f1 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7651)) - 8388736.0f;
+  f2 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7652)) - 8388736.0f;
+  f3 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7653)) - 8388736.0f;
+}
+
+__device__ __forceinline__ bool am_better(float v, uint32_t i, float bv, uint32_t bi) {
+  return v > bv || (v == bv && i < bi);
+}
+
+// ---------------------------------------------------------------------------
+// Prologue: stage the activations of NT tokens into shared memory.
+template <int FMT, int NT>
+__device__ __forceinline__ void mv_stage_x(const MvArgs& a, const MvLayout& L, uint8_t* smem, int cw, int lane) {
+  using namespace yl::dev;
+  const uint32_t K = a.K, nb = K / 32;
+  const int ctid = cw * 32 + lane;
+  float* red = reinterpret_cast<float*>(smem + L.red_off);
+  if (a.pro == PRO_NORM) {
+    for (int t = 0; t < NT; ++t) {
+      const bool valid = t < (int)a.ntok;
+      const float* xr = a.xres + (uint64_t)t * a.x_tok_stride;
+      // sum of squares, same order as rmsnorm_quant_kernel (256 threads, float4)
+      float ss = 0.0f;
+      if (valid)
+        for (uint32_t i = ctid * 4; i < K; i += MV_NCW * 32 * 4) {
+          const float4 v = *reinterpret_cast<const float4*>(xr + i);
+          ss = fmaf(v.x, v.x, ss);
+          ss = fmaf(v.y, v.y, ss);
+          ss = fmaf(v.z, v.z, ss);
+          ss = fmaf(v.w, v.w, ss);
+        }
+      ss = warp_sum(ss);
+      if (lane == 0) red[cw] = ss;
+      named_bar_sync(1, MV_NCW * 32);
+      float tot = 0.0f;
+#pragma unroll
+      for (int i = 0; i < MV_NCW; ++i) tot += red[i];
+      float r = __fdiv_rn(tot, (float)K);
+      r = __fadd_rn(r, a.eps);
+      r = __fdiv_rn(1.0f, __fsqrt_rn(r));
+      named_bar_sync(1, MV_NCW * 32);  // red[] reused by the next token
+      if (mv_f32_act<FMT>()) {
+        float* xf = reinterpret_cast<float*>(smem + L.x_off) + t * K;
+        for (uint32_t k = ctid; k < K; k += MV_NCW * 32)
+          xf[k] = valid ? __fmul_rn(a.norm_w[k], __fmul_rn(r, xr[k])) : 0.0f;
+      } else {
+        int8_t* xq = reinterpret_cast<int8_t*>(smem + L.x_off) + t * K;
+        float* xs = reinterpret_cast<float*>(smem + L.xs_off) + t * nb;
+        int* xsum = reinterpret_cast<int*>(smem + L.xsum_off) + t * nb;
+        for (uint32_t b = cw; b < nb; b += MV_NCW) {
+          const uint32_t k = b * 32 + lane;
+          const float y = valid ? __fmul_rn(a.norm_w[k], __fmul_rn(r, xr[k])) : 0.0f;
+          float sc;
+          const int8_t q = quant_q8_lane(y, &sc);
+          if (FMT == FMT_Q4) {
+            const uint32_t off = (lane < 16) ? b * 16 + lane : nb * 16 + b * 16 + (lane - 16);
+            xq[off] = q;
+            int s = (int)q;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(FULL, s, o);
+            if (lane == 0) xsum[b] = s;
+          } else {
+            xq[k] = q;
+          }
+          if (lane == 0) xs[b] = sc;
+        }
+      }
+    }
+    return;
+  }
+  if (mv_f32_act<FMT>()) {
+    float* xf = reinterpret_cast<float*>(smem + L.x_off);
+    for (int t = 0; t < NT; ++t) {
+      const float4* src = reinterpret_cast<const float4*>(a.xf + (uint64_t)t * a.x_tok_stride);
+      float4* dst = reinterpret_cast<float4*>(xf + t * K);
+      const bool valid = t < (int)a.ntok;
+      for (uint32_t i = ctid; i < K / 4; i += MV_NCW * 32) dst[i] = valid ? src[i] : make_float4(0, 0, 0, 0);
+    }
+    return;
+  }
+  int8_t* xq = reinterpret_cast<int8_t*>(smem + L.x_off);
+  float* xs = reinterpret_cast<float*>(smem + L.xs_off);
+  int* xsum = reinterpret_cast<int*>(smem + L.xsum_off);
+  for (int t = 0; t < NT; ++t) {
+    const bool valid = t < (int)a.ntok;
+    const int4* src = reinterpret_cast<const int4*>(a.xq + (uint64_t)t * a.x_tok_stride);
+    if (FMT == FMT_Q4) {
+      // split layout: first 16 bytes of every block, then the second halves,
+      // so a lane reading one block's halves hits consecutive 16-byte slots
+      for (uint32_t b = ctid; b < nb; b += MV_NCW * 32) {
+        int4 lo = valid ? src[2 * b] : make_int4(0, 0, 0, 0);
+        int4 hi = valid ? src[2 * b + 1] : make_int4(0, 0, 0, 0);
+        reinterpret_cast<int4*>(xq + t * K)[b] = lo;
+        reinterpret_cast<int4*>(xq + t * K)[nb + b] = hi;
+        int s = dp4a(lo.x, 0x01010101, 0);
+        s = dp4a(lo.y, 0x01010101, s);
+        s = dp4a(lo.z, 0x01010101, s);
+        s = dp4a(lo.w, 0x01010101, s);
+        s = dp4a(hi.x, 0x01010101, s);
+        s = dp4a(hi.y, 0x01010101, s);
+        s = dp4a(hi.z, 0x01010101, s);
+        s = dp4a(hi.w, 0x01010101, s);
+        xsum[t * nb + b] = s;
+      }
+    } else {
+      for (uint32_t i = ctid; i < K / 16; i += MV_NCW * 32)
+        reinterpret_cast<int4*>(xq + t * K)[i] = valid ? src[i] : make_int4(0, 0, 0, 0);
+    }
+    const float* ssrc = a.xs + (uint64_t)t * a.xs_tok_stride;
+    for (uint32_t i = ctid; i < nb; i += MV_NCW * 32) xs[t * nb + i] = valid ? ssrc[i] : 0.0f;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// One row's chunk [k0, k0+kn) from the stage, accumulated into acc[NT].
+template <int FMT, int NT, bool SF16>
+__device__ __forceinline__ void mv_row_chunk(const uint8_t* wrow, const uint8_t* srow, const uint8_t* smem,
+                                             const MvLayout& L, uint32_t K, uint32_t k0, uint32_t kn, int lane,
+                                             float (&acc)[NT]) {
+  using namespace yl::dev;
+  if (FMT == FMT_Q8) {
+    const int8_t* xq = reinterpret_cast<const int8_t*>(smem + L.x_off);
+    const float* xs = reinterpret_cast<const float*>(smem + L.xs_off);
+    const uint32_t nck = kn / 16;  // 16-byte chunks, two per block
+    for (uint32_t c0 = 0; c0 < nck; c0 += 32 * MV_U) {
+      int4 w[MV_U];
+      float wsc[MV_U];
+      bool v[MV_U];
+#pragma unroll
+      for (int u = 0; u < MV_U; ++u) {
+        const uint32_t c = c0 + u * 32 + lane;
+        v[u] = c < nck;
+        w[u] = v[u] ? *reinterpret_cast<const int4*>(wrow + 16 * c) : make_int4(0, 0, 0, 0);
+        wsc[u] = v[u] ? ld_scale<SF16>(srow, c >> 1) : 0.0f;
+      }
+#pragma unroll
+      for (int t = 0; t < NT; ++t) {
+        int s[MV_U];
+#pragma unroll
+        for (int u = 0; u < MV_U; ++u) {
+          const uint32_t c = c0 + u * 32 + lane;
+          const int4 x = v[u] ? *reinterpret_cast<const int4*>(xq + t * K + k0 + 16 * c) : make_int4(0, 0, 0, 0);
+          int d = dp4a(w[u].x, x.x, 0);
+          d = dp4a(w[u].y, x.y, d);
+          d = dp4a(w[u].z, x.z, d);
+          s[u] = dp4a(w[u].w, x.w, d);
+        }
+#pragma unroll
+        for (int u = 0; u < MV_U; ++u) s[u] += __shfl_xor_sync(FULL, s[u], 1);  // exact block dot
+#pragma unroll
+        for (int u = 0; u < MV_U; ++u) {
+          const uint32_t c = c0 + u * 32 + lane;
+          if (v[u] && !(lane & 1)) {
+            const float p = __fmul_rn(__fmul_rn((float)s[u], wsc[u]), xs[t * (K / 32) + (k0 >> 5) + (c >> 1)]);
+            acc[t] = __fadd_rn(acc[t], p);
+          }
+        }
+      }
+    }
+  } else if (FMT == FMT_Q4) {
+    const int8_t* xq = reinterpret_cast<const int8_t*>(smem + L.x_off);
+    const float* xs = reinterpret_cast<const float*>(smem + L.xs_off);
+    const int* xsum = reinterpret_cast<const int*>(smem + L.xsum_off);
+    const uint32_t nb = K / 32, nbk = kn / 32;  // one 16-byte chunk per block
+    for (uint32_t b0 = 0; b0 < nbk; b0 += 32 * 2) {
+      int4 w[2];
+      float wsc[2];
+      bool v[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const uint32_t b = b0 + u * 32 + lane;
+        v[u] = b < nbk;
+        w[u] = v[u] ? *reinterpret_cast<const int4*>(wrow + 16 * b) : make_int4(0, 0, 0, 0);
+        wsc[u] = v[u] ? ld_scale<SF16>(srow, b) : 0.0f;
+      }
+#pragma unroll
+      for (int t = 0; t < NT; ++t) {
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          if (!v[u]) continue;
+          const uint32_t kb = (k0 >> 5) + b0 + u * 32 + lane;
+          const int4 xl = reinterpret_cast<const int4*>(xq + t * K)[kb];
+          const int4 xh = reinterpret_cast<const int4*>(xq + t * K)[nb + kb];
+          int s = dp4a(w[u].x & 0x0F0F0F0F, xl.x, 0);
+          s = dp4a(w[u].y & 0x0F0F0F0F, xl.y, s);
+          s = dp4a(w[u].z & 0x0F0F0F0F, xl.z, s);
+          s = dp4a(w[u].w & 0x0F0F0F0F, xl.w, s);
+          s = dp4a((w[u].x >> 4) & 0x0F0F0F0F, xh.x, s);
+          s = dp4a((w[u].y >> 4) & 0x0F0F0F0F, xh.y, s);
+          s = dp4a((w[u].z >> 4) & 0x0F0F0F0F, xh.z, s);
+          s = dp4a((w[u].w >> 4) & 0x0F0F0F0F, xh.w, s);
+          s -= 8 * xsum[t * nb + kb];  // sum (q-8)*x exactly
+          const float p = __fmul_rn(__fmul_rn((float)s, wsc[u]), xs[t * nb + kb]);
+          acc[t] = __fadd_rn(acc[t], p);
+        }
+      }
+    }
+  } else if (FMT == FMT_F16) {
+    const float* xf = reinterpret_cast<const float*>(smem + L.x_off);
+    const uint32_t nck = kn / 8;  // 8 halves per 16-byte chunk
+    for (uint32_t c0 = 0; c0 < nck; c0 += 32 * 2) {
+      int4 w[2];
+      bool v[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const uint32_t c = c0 + u * 32 + lane;
+        v[u] = c < nck;
+        w[u] = v[u] ? *reinterpret_cast<const int4*>(wrow + 16 * c) : make_int4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        if (!v[u]) continue;
+        const uint32_t c = c0 + u * 32 + lane;
+        const __half2* h2 = reinterpret_cast<const __half2*>(&w[u]);
+        float wf[8];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = __half22float2(h2[j]);
+          wf[2 * j] = f.x;
+          wf[2 * j + 1] = f.y;
+        }
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+          const float4 x0 = *reinterpret_cast<const float4*>(xf + t * K + k0 + 8 * c);
+          const float4 x1 = *reinterpret_cast<const float4*>(xf + t * K + k0 + 8 * c + 4);
+          float s = acc[t];
+          s = __fadd_rn(s, __fmul_rn(x0.x, wf[0]));
+          s = __fadd_rn(s, __fmul_rn(x0.y, wf[1]));
+          s = __fadd_rn(s, __fmul_rn(x0.z, wf[2]));
+          s = __fadd_rn(s, __fmul_rn(x0.w, wf[3]));
+          s = __fadd_rn(s, __fmul_rn(x1.x, wf[4]));
+          s = __fadd_rn(s, __fmul_rn(x1.y, wf[5]));
+          s = __fadd_rn(s, __fmul_rn(x1.z, wf[6]));
+          s = __fadd_rn(s, __fmul_rn(x1.w, wf[7]));
+          acc[t] = s;
+        }
+      }
+    }
+  } else if (FMT == FMT_Q8F) {  // Q8_0 weights, f32 activations (lm_head)
+    const float* xf = reinterpret_cast<const float*>(smem + L.x_off);
+    const uint32_t nck = kn / 16;
+    for (uint32_t c0 = 0; c0 < nck; c0 += 32 * 2) {
+      int4 w[2];
+      float wsc[2];
+      bool v[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const uint32_t c = c0 + u * 32 + lane;
+        v[u] = c < nck;
+        w[u] = v[u] ? *reinterpret_cast<const int4*>(wrow + 16 * c) : make_int4(0, 0, 0, 0);
+        wsc[u] = v[u] ? ld_scale<SF16>(srow, c >> 1) : 0.0f;
+      }
+#pragma unroll
+      for (int t = 0; t < NT; ++t) {
+        float s[2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const uint32_t c = c0 + u * 32 + lane;
+          s[u] = 0.0f;
+          if (v[u]) {
+            const float4* xp = reinterpret_cast<const float4*>(xf + t * K + k0 + 16 * c);
+            const uint32_t wv[4] = {(uint32_t)w[u].x, (uint32_t)w[u].y, (uint32_t)w[u].z, (uint32_t)w[u].w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float4 x = xp[j];
+              float f0, f1, f2, f3;
+              i8x4_to_f32(wv[j], f0, f1, f2, f3);
+              s[u] = fmaf(x.x, f0, s[u]);
+              s[u] = fmaf(x.y, f1, s[u]);
+              s[u] = fmaf(x.z, f2, s[u]);
+              s[u] = fmaf(x.w, f3, s[u]);
+            }
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 2; ++u) s[u] += __shfl_xor_sync(FULL, s[u], 1);
+#pragma unroll
+        for (int u = 0; u < 2; ++u)
+          if (v[u] && !(lane & 1)) acc[t] = fmaf(s[u], wsc[u], acc[t]);
+      }
+    }
+  } else {  // FMT_Q4F
+    const float* xf = reinterpret_cast<const float*>(smem + L.x_off);
+    const uint32_t nbk = kn / 32;
+    for (uint32_t b = lane; b < nbk; b += 32) {
+      const int4 w = *reinterpret_cast<const int4*>(wrow + 16 * b);
+      const float wsc = ld_scale<SF16>(srow, b);
+      const uint8_t* wb = reinterpret_cast<const uint8_t*>(&w);
+#pragma unroll
+      for (int t = 0; t < NT; ++t) {
+        const float* xp = xf + t * K + k0 + 32 * b;
+        float s = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          s = fmaf(xp[j], (float)((int)(wb[j] & 0xF) - 8), s);
+          s = fmaf(xp[j + 16], (float)((int)(wb[j] >> 4) - 8), s);
+        }
+        acc[t] = fmaf(s, wsc, acc[t]);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 template <int FMT, int NT, int EPI, bool SF16, int RPW>
 __global__ void __launch_bounds__(MV_THREADS, 1) mv_kernel(MvArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -94,8 +409,9 @@ __global__ void __launch_bounds__(MV_THREADS, 1) mv_kernel(MvArgs a) {
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar_off);
   uint64_t* empty = full + S;
 
-  // Row range of this CTA (row pairs for SwiGLU so gate/up stay together).
-  const uint32_t unit = (EPI == EPI_SWIGLU) ? 2u : 1u;
+  // Row range of this CTA: row pairs for SwiGLU (gate/up together), 64-row
+  // units when h is quantized here (32 pairs = one Q8_0 block of h).
+  const uint32_t unit = EPI == EPI_SWIGLU_Q8 ? 64u : (EPI == EPI_SWIGLU ? 2u : 1u);
   const uint64_t units = a.rows / unit;
   const uint32_t r_begin = (uint32_t)(units * blockIdx.x / gridDim.x) * unit;
   const uint32_t r_end = (uint32_t)(units * (blockIdx.x + 1) / gridDim.x) * unit;
@@ -152,52 +468,8 @@ __global__ void __launch_bounds__(MV_THREADS, 1) mv_kernel(MvArgs a) {
 
   // ---------------- consumers ----------------
   const int cw = warp - 1;
-  const int ctid = threadIdx.x - 32;
   grid_dep_wait();
-
-  // Stage the activations into shared memory.
-  if (mv_f32_act<FMT>()) {
-    float* xf = reinterpret_cast<float*>(smem + L.x_off);
-    for (int t = 0; t < NT; ++t) {
-      const float4* src = reinterpret_cast<const float4*>(a.xf + (uint64_t)t * a.x_tok_stride);
-      float4* dst = reinterpret_cast<float4*>(xf + t * K);
-      const bool valid = t < (int)a.ntok;
-      for (uint32_t i = ctid; i < K / 4; i += MV_NCW * 32) dst[i] = valid ? src[i] : make_float4(0, 0, 0, 0);
-    }
-  } else {
-    int8_t* xq = reinterpret_cast<int8_t*>(smem + L.x_off);
-    float* xs = reinterpret_cast<float*>(smem + L.xs_off);
-    int* xsum = reinterpret_cast<int*>(smem + L.xsum_off);
-    const uint32_t nb = K / 32;
-    for (int t = 0; t < NT; ++t) {
-      const bool valid = t < (int)a.ntok;
-      const int4* src = reinterpret_cast<const int4*>(a.xq + (uint64_t)t * a.x_tok_stride);
-      if (FMT == FMT_Q4) {
-        // split layout: first 16 bytes of every block, then the second halves,
-        // so a lane reading one block's halves hits consecutive 16-byte slots
-        for (uint32_t b = ctid; b < nb; b += MV_NCW * 32) {
-          int4 lo = valid ? src[2 * b] : make_int4(0, 0, 0, 0);
-          int4 hi = valid ? src[2 * b + 1] : make_int4(0, 0, 0, 0);
-          reinterpret_cast<int4*>(xq + t * K)[b] = lo;
-          reinterpret_cast<int4*>(xq + t * K)[nb + b] = hi;
-          int s = dp4a(lo.x, 0x01010101, 0);
-          s = dp4a(lo.y, 0x01010101, s);
-          s = dp4a(lo.z, 0x01010101, s);
-          s = dp4a(lo.w, 0x01010101, s);
-          s = dp4a(hi.x, 0x01010101, s);
-          s = dp4a(hi.y, 0x01010101, s);
-          s = dp4a(hi.z, 0x01010101, s);
-          s = dp4a(hi.w, 0x01010101, s);
-          xsum[t * nb + b] = s;
-        }
-      } else {
-        for (uint32_t i = ctid; i < K / 16; i += MV_NCW * 32)
-          reinterpret_cast<int4*>(xq + t * K)[i] = valid ? src[i] : make_int4(0, 0, 0, 0);
-      }
-      const float* ssrc = a.xs + (uint64_t)t * a.xs_tok_stride;
-      for (uint32_t i = ctid; i < nb; i += MV_NCW * 32) xs[t * nb + i] = valid ? ssrc[i] : 0.0f;
-    }
-  }
+  mv_stage_x<FMT, NT>(a, L, smem, cw, lane);
   named_bar_sync(1, MV_NCW * 32);
 
   float acc[RPW][NT];
@@ -205,12 +477,17 @@ __global__ void __launch_bounds__(MV_THREADS, 1) mv_kernel(MvArgs a) {
   for (int r = 0; r < RPW; ++r)
 #pragma unroll
     for (int t = 0; t < NT; ++t) acc[r][t] = 0.0f;
+  float am_v = -INFINITY;  // EPI_ARGMAX: this warp's best (lane 0)
+  uint32_t am_i = 0xFFFFFFFFu;
+  float* hbuf = reinterpret_cast<float*>(smem + L.red_off);  // EPI_SWIGLU_Q8: [2][NT][32]
 
+  // After a wait timeout the warp stops waiting and computing ("dead") but
+  // keeps walking the loop so every named barrier below is still reached.
+  bool dead = false;
   for (uint32_t it = 0; it < n_it; ++it) {
     const int slot = it % S;
     const uint32_t ph = (it / S) & 1;
-    const bool ok = mbar_wait(&full[slot], ph, a.err);
-    if (!ok) break;
+    if (!dead && !mbar_wait(&full[slot], ph, a.err)) dead = true;
     const uint32_t rs = it / nch, ch = it % nch;
     const uint32_t row0 = r_begin + rs * RS;
     const uint32_t k0 = ch * kc, kn = min(kc, K - k0);
@@ -218,180 +495,140 @@ __global__ void __launch_bounds__(MV_THREADS, 1) mv_kernel(MvArgs a) {
 #pragma unroll
     for (int rr = 0; rr < RPW; ++rr) {
       const uint32_t rl = cw * RPW + rr;
-      if (!ok || row0 + rl >= r_end) continue;
-      const uint8_t* wrow = stage + rl * L.stage_q_row;
-      const uint8_t* srow = stage + RS * L.stage_q_row + rl * L.stage_s_row;
-      if (FMT == FMT_Q8) {
-        const int8_t* xq = reinterpret_cast<const int8_t*>(smem + L.x_off);
-        const float* xs = reinterpret_cast<const float*>(smem + L.xs_off);
-        const uint32_t nck = kn / 16;  // 16-byte chunks, two per block
-        for (uint32_t c0 = 0; c0 < nck; c0 += 32) {
-          const uint32_t c = c0 + lane;
-          const bool v = c < nck;
-          const int4 w = v ? *reinterpret_cast<const int4*>(wrow + 16 * c) : make_int4(0, 0, 0, 0);
-          const float wsc = v ? ld_scale<SF16>(srow, c >> 1) : 0.0f;
-          const uint32_t kb = (k0 >> 5) + (c >> 1);
+      if (dead || row0 + rl >= r_end) continue;
+      mv_row_chunk<FMT, NT, SF16>(stage + rl * L.stage_q_row, stage + RS * L.stage_q_row + rl * L.stage_s_row, smem,
+                                  L, K, k0, kn, lane, acc[rr]);
+    }
+    __syncwarp();
+    if (lane == 0 && !dead) mbar_arrive(&empty[slot]);
+    if (ch != nch - 1) continue;
+
+    // ---- epilogue for this warp's rows of the finished row set ----
 #pragma unroll
-          for (int t = 0; t < NT; ++t) {
-            int4 x = v ? *reinterpret_cast<const int4*>(xq + t * K + k0 + 16 * c) : make_int4(0, 0, 0, 0);
-            int s = dp4a(w.x, x.x, 0);
-            s = dp4a(w.y, x.y, s);
-            s = dp4a(w.z, x.z, s);
-            s = dp4a(w.w, x.w, s);
-            s += __shfl_xor_sync(FULL, s, 1);  // exact int32 dot of the whole block
-            if (v && !(lane & 1)) {
-              float p = __fmul_rn(__fmul_rn((float)s, wsc), xs[t * (K / 32) + kb]);
-              acc[rr][t] = __fadd_rn(acc[rr][t], p);
-            }
+    for (int t = 0; t < NT; ++t)
+#pragma unroll
+      for (int rr = 0; rr < RPW; ++rr) acc[rr][t] = warp_sum(acc[rr][t]);
+    if (mv_swiglu(EPI)) {
+      const uint32_t r = row0 + cw * RPW;  // gate row (even), up row = r + 1
+      const bool have = r + 1 < r_end;
+      float hv[NT];
+#pragma unroll
+      for (int t = 0; t < NT; ++t) hv[t] = have ? silu_mul(acc[0][t], acc[1][t]) : 0.0f;
+      if (lane == 0 && have) {
+#pragma unroll
+        for (int t = 0; t < NT; ++t)
+          if (t < (int)a.ntok) a.out[(uint64_t)t * a.out_tok_stride + r / 2] = hv[t];
+      }
+      if (EPI == EPI_SWIGLU_Q8) {
+        // rows [row0, row0+16) give h [row0/2, row0/2 + 8); a block of 32 h
+        // completes every 64 rows (4 row sets); double-buffered staging
+        const uint32_t j = (r - r_begin) / 2;  // h index within the CTA
+        const uint32_t blk = j / 32, jj = j % 32;
+        float* hb = hbuf + (blk & 1) * NT * 32;
+        if (lane == 0 && have)
+#pragma unroll
+          for (int t = 0; t < NT; ++t) hb[t * 32 + jj] = hv[t];
+        if (((rs + 1) * RS) % 64 == 0 || row0 + RS >= r_end) {
+          named_bar_sync(2, MV_NCW * 32);
+          const uint32_t jb = (r_begin / 2) + blk * 32;  // first h of the block
+          if (cw < NT && cw < (int)a.ntok) {
+            const int t = cw;
+            float sc;
+            const int8_t qv = quant_q8_lane(hb[t * 32 + lane], &sc);
+            const uint64_t hk = (uint64_t)t * (a.rows / 2) + jb + lane;
+            a.hq[hk] = qv;
+            if (lane == 0) a.hs[hk / 32] = sc;
           }
         }
-      } else if (FMT == FMT_Q4) {
-        const int8_t* xq = reinterpret_cast<const int8_t*>(smem + L.x_off);
-        const float* xs = reinterpret_cast<const float*>(smem + L.xs_off);
-        const int* xsum = reinterpret_cast<const int*>(smem + L.xsum_off);
-        const uint32_t nb = K / 32, nbk = kn / 32;  // one 16-byte chunk per block
-        for (uint32_t b0 = 0; b0 < nbk; b0 += 32) {
-          const uint32_t b = b0 + lane;
-          if (b >= nbk) break;
-          const int4 w = *reinterpret_cast<const int4*>(wrow + 16 * b);
-          const float wsc = ld_scale<SF16>(srow, b);
-          const uint32_t kb = (k0 >> 5) + b;
-          const int wl[4] = {w.x & 0x0F0F0F0F, w.y & 0x0F0F0F0F, w.z & 0x0F0F0F0F, w.w & 0x0F0F0F0F};
-          const int wh[4] = {(w.x >> 4) & 0x0F0F0F0F, (w.y >> 4) & 0x0F0F0F0F, (w.z >> 4) & 0x0F0F0F0F,
-                             (w.w >> 4) & 0x0F0F0F0F};
+      }
+    } else {
 #pragma unroll
-          for (int t = 0; t < NT; ++t) {
-            const int4 xl = reinterpret_cast<const int4*>(xq + t * K)[kb];
-            const int4 xh = reinterpret_cast<const int4*>(xq + t * K)[nb + kb];
-            int s = dp4a(wl[0], xl.x, 0);
-            s = dp4a(wl[1], xl.y, s);
-            s = dp4a(wl[2], xl.z, s);
-            s = dp4a(wl[3], xl.w, s);
-            s = dp4a(wh[0], xh.x, s);
-            s = dp4a(wh[1], xh.y, s);
-            s = dp4a(wh[2], xh.z, s);
-            s = dp4a(wh[3], xh.w, s);
-            s -= 8 * xsum[t * nb + kb];  // sum (q-8)*x exactly
-            float p = __fmul_rn(__fmul_rn((float)s, wsc), xs[t * nb + kb]);
-            acc[rr][t] = __fadd_rn(acc[rr][t], p);
+      for (int rr = 0; rr < RPW; ++rr) {
+        const uint32_t r = row0 + cw * RPW + rr;
+        if (r >= r_end) continue;
+        if (EPI == EPI_ARGMAX) {
+          const float v = acc[rr][0];
+          if (v == v && am_better(v, r, am_v, am_i)) {
+            am_v = v;
+            am_i = r;
           }
         }
-      } else if (FMT == FMT_F16) {
-        const float* xf = reinterpret_cast<const float*>(smem + L.x_off);
-        const uint32_t nck = kn / 8;  // 8 halves per 16-byte chunk
-        for (uint32_t c = lane; c < nck; c += 32) {
-          const int4 w = *reinterpret_cast<const int4*>(wrow + 16 * c);
-          const __half2* h2 = reinterpret_cast<const __half2*>(&w);
-          float wf[8];
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            float2 f = __half22float2(h2[j]);
-            wf[2 * j] = f.x;
-            wf[2 * j + 1] = f.y;
-          }
+        if (lane == 0) {
 #pragma unroll
           for (int t = 0; t < NT; ++t) {
-            const float4 x0 = *reinterpret_cast<const float4*>(xf + t * K + k0 + 8 * c);
-            const float4 x1 = *reinterpret_cast<const float4*>(xf + t * K + k0 + 8 * c + 4);
-            float s = acc[rr][t];
-            s = __fadd_rn(s, __fmul_rn(x0.x, wf[0]));
-            s = __fadd_rn(s, __fmul_rn(x0.y, wf[1]));
-            s = __fadd_rn(s, __fmul_rn(x0.z, wf[2]));
-            s = __fadd_rn(s, __fmul_rn(x0.w, wf[3]));
-            s = __fadd_rn(s, __fmul_rn(x1.x, wf[4]));
-            s = __fadd_rn(s, __fmul_rn(x1.y, wf[5]));
-            s = __fadd_rn(s, __fmul_rn(x1.z, wf[6]));
-            s = __fadd_rn(s, __fmul_rn(x1.w, wf[7]));
-            acc[rr][t] = s;
-          }
-        }
-      } else {  // FMT_Q8F / FMT_Q4F: quantized weights, f32 activations (lm_head)
-        const float* xf = reinterpret_cast<const float*>(smem + L.x_off);
-        if (FMT == FMT_Q8F) {
-          const uint32_t nck = kn / 16;
-          for (uint32_t c0 = 0; c0 < nck; c0 += 32) {
-            const uint32_t c = c0 + lane;
-            const bool v = c < nck;
-            const int4 w = v ? *reinterpret_cast<const int4*>(wrow + 16 * c) : make_int4(0, 0, 0, 0);
-            const float wsc = v ? ld_scale<SF16>(srow, c >> 1) : 0.0f;
-            const int8_t* wb = reinterpret_cast<const int8_t*>(&w);
-#pragma unroll
-            for (int t = 0; t < NT; ++t) {
-              float s = 0.0f;
-              if (v) {
-                const float4* xp = reinterpret_cast<const float4*>(xf + t * K + k0 + 16 * c);
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                  const float4 x = xp[j];
-                  s = fmaf(x.x, (float)wb[4 * j + 0], s);
-                  s = fmaf(x.y, (float)wb[4 * j + 1], s);
-                  s = fmaf(x.z, (float)wb[4 * j + 2], s);
-                  s = fmaf(x.w, (float)wb[4 * j + 3], s);
-                }
-              }
-              s += __shfl_xor_sync(FULL, s, 1);
-              if (v && !(lane & 1)) acc[rr][t] = fmaf(s, wsc, acc[rr][t]);
-            }
-          }
-        } else {
-          const uint32_t nbk = kn / 32;
-          for (uint32_t b = lane; b < nbk; b += 32) {
-            const int4 w = *reinterpret_cast<const int4*>(wrow + 16 * b);
-            const float wsc = ld_scale<SF16>(srow, b);
-            const uint8_t* wb = reinterpret_cast<const uint8_t*>(&w);
-#pragma unroll
-            for (int t = 0; t < NT; ++t) {
-              const float* xp = xf + t * K + k0 + 32 * b;
-              float s = 0.0f;
-#pragma unroll
-              for (int j = 0; j < 16; ++j) {
-                s = fmaf(xp[j], (float)((int)(wb[j] & 0xF) - 8), s);
-                s = fmaf(xp[j + 16], (float)((int)(wb[j] >> 4) - 8), s);
-              }
-              acc[rr][t] = fmaf(s, wsc, acc[rr][t]);
-            }
+            if (t >= (int)a.ntok) continue;
+            float* o = a.out + (uint64_t)t * a.out_tok_stride + r;
+            if (EPI == EPI_STORE || EPI == EPI_ARGMAX) *o = acc[rr][t];
+            else if (EPI == EPI_ADD) *o = __fadd_rn(*o, acc[rr][t]);
+            else *o = (r < a.quirk_cols) ? __fadd_rn(*o, acc[rr][t]) : acc[rr][t];
           }
         }
       }
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[slot]);
+#pragma unroll
+    for (int t = 0; t < NT; ++t)
+#pragma unroll
+      for (int rr = 0; rr < RPW; ++rr) acc[rr][t] = 0.0f;
+  }
 
-    if (ch == nch - 1) {
-      // Epilogue for this warp's rows of the finished row set.
+  if (EPI == EPI_ARGMAX) {
+    // CTA winner -> global slot; the last CTA to arrive reduces all slots
+    // (sampler.rs:67-79: lowest index among equal maxima; NaN never wins).
+    float* rv = reinterpret_cast<float*>(smem + L.red_off);
+    uint32_t* ri = reinterpret_cast<uint32_t*>(smem + L.red_off + 64);
+    __shared__ int is_last;
+    if (lane == 0) {
+      rv[cw] = am_v;
+      ri[cw] = am_i;
+    }
+    named_bar_sync(1, MV_NCW * 32);
+    if (cw == 0) {
+      float bv = lane < MV_NCW ? rv[lane] : -INFINITY;
+      uint32_t bi = lane < MV_NCW ? ri[lane] : 0xFFFFFFFFu;
 #pragma unroll
-      for (int t = 0; t < NT; ++t) {
-#pragma unroll
-        for (int rr = 0; rr < RPW; ++rr) acc[rr][t] = warp_sum(acc[rr][t]);
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(FULL, bv, o);
+        const uint32_t oi = __shfl_xor_sync(FULL, bi, o);
+        if (am_better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
       }
-      if (lane == 0 && ok) {
-        if (EPI == EPI_SWIGLU) {
-          const uint32_t r = row0 + cw * RPW;  // gate row (even), up row = r + 1
-          if (r + 1 < r_end) {
+      if (lane == 0) {
+        a.am_val[blockIdx.x] = bv;
+        a.am_idx[blockIdx.x] = bi;
+        __threadfence();
+        const unsigned prev = atomicAdd(a.am_count, 1u);
+        is_last = prev == gridDim.x - 1;
+      }
+      __syncwarp();
+      if (__shfl_sync(FULL, lane == 0 ? is_last : 0, 0)) {
+        __threadfence();
+        bv = -INFINITY;
+        bi = 0xFFFFFFFFu;
+        for (uint32_t i = lane; i < gridDim.x; i += 32) {
+          const float v = __ldcg(a.am_val + i);
+          const uint32_t ix = __ldcg(a.am_idx + i);
+          if (am_better(v, ix, bv, bi)) { bv = v; bi = ix; }
+        }
 #pragma unroll
-            for (int t = 0; t < NT; ++t)
-              if (t < (int)a.ntok) a.out[(uint64_t)t * a.out_tok_stride + r / 2] = silu_mul(acc[0][t], acc[1][t]);
+        for (int o = 16; o > 0; o >>= 1) {
+          const float ov = __shfl_xor_sync(FULL, bv, o);
+          const uint32_t oi = __shfl_xor_sync(FULL, bi, o);
+          if (am_better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+        }
+        if (lane == 0) {
+          uint32_t res = bi == 0xFFFFFFFFu ? 0u : bi;
+          const float l0 = __ldcg(a.out);
+          if (l0 != l0) res = 0;  // reference: a NaN first logit is never beaten
+          StepState* st = a.state;
+          if (a.am_out) a.am_out[st ? st->steps : 0] = res;
+          if (st) {
+            st->next = (int32_t)res;
+            st->token = (int32_t)res;
+            st->pos += 1;
+            st->steps += 1;
           }
-        } else {
-#pragma unroll
-          for (int rr = 0; rr < RPW; ++rr) {
-            const uint32_t r = row0 + cw * RPW + rr;
-            if (r >= r_end) continue;
-#pragma unroll
-            for (int t = 0; t < NT; ++t) {
-              if (t >= (int)a.ntok) continue;
-              float* o = a.out + (uint64_t)t * a.out_tok_stride + r;
-              if (EPI == EPI_STORE) *o = acc[rr][t];
-              else if (EPI == EPI_ADD) *o = __fadd_rn(*o, acc[rr][t]);
-              else *o = (r < a.quirk_cols) ? __fadd_rn(*o, acc[rr][t]) : acc[rr][t];
-            }
-          }
+          *a.am_count = 0u;  // ready for the next launch
         }
       }
-#pragma unroll
-      for (int t = 0; t < NT; ++t)
-#pragma unroll
-        for (int rr = 0; rr < RPW; ++rr) acc[rr][t] = 0.0f;
     }
   }
 }
@@ -401,8 +638,7 @@ template <int FMT, bool SF16>
 cudaError_t mv_launch(const MvArgs& a0, int epi, const LaunchCfg& lc) {
   MvArgs a = a0;
   const int nt = a.ntok <= 1 ? 1 : a.ntok <= 2 ? 2 : a.ntok <= 4 ? 4 : 8;
-  const int rpw = epi == EPI_SWIGLU ? 2 : 1;
-  // Stage count from the shared-memory budget.
+  const int rpw = mv_swiglu(epi) ? 2 : 1;
   MvLayout L0;
   switch (nt) {
     case 1: L0 = mv_layout<FMT, 1>(a.K, a.kc, rpw, 0); break;
@@ -416,25 +652,29 @@ cudaError_t mv_launch(const MvArgs& a0, int epi, const LaunchCfg& lc) {
   a.stages = stages;
   const uint32_t smem = L0.total + stages * L0.stage_bytes;
   if (smem > 227u * 1024u) return cudaErrorInvalidConfiguration;
+  if (epi == EPI_ARGMAX && nt != 1) return cudaErrorInvalidValue;
+  if (epi == EPI_SWIGLU_Q8 && (a.rows % 64 || mv_f32_act<FMT>())) return cudaErrorInvalidValue;
   void (*kern)(MvArgs) = nullptr;
 #define YL_MV_CASE(NT_, EPI_, RPW_) \
   if (nt == NT_ && epi == EPI_) kern = mv_kernel<FMT, NT_, EPI_, SF16, RPW_>;
-#define YL_MV_NT(NT_)                   \
-  YL_MV_CASE(NT_, EPI_STORE, 1)         \
-  YL_MV_CASE(NT_, EPI_ADD, 1)           \
-  YL_MV_CASE(NT_, EPI_QUIRK, 1)         \
-  if (!mv_f32_act<FMT>() || FMT == FMT_F16) { YL_MV_CASE(NT_, EPI_SWIGLU, 2) }
+#define YL_MV_NT(NT_)                                           \
+  YL_MV_CASE(NT_, EPI_STORE, 1)                                 \
+  YL_MV_CASE(NT_, EPI_ADD, 1)                                   \
+  YL_MV_CASE(NT_, EPI_QUIRK, 1)                                 \
+  if (!mv_f32_act<FMT>() || FMT == FMT_F16) { YL_MV_CASE(NT_, EPI_SWIGLU, 2) } \
+  if (!mv_f32_act<FMT>()) { YL_MV_CASE(NT_, EPI_SWIGLU_Q8, 2) }
   YL_MV_NT(1)
   YL_MV_NT(2)
   YL_MV_NT(4)
   YL_MV_NT(8)
+  if (mv_f32_act<FMT>()) { YL_MV_CASE(1, EPI_ARGMAX, 1) }
 #undef YL_MV_NT
 #undef YL_MV_CASE
   if (!kern) return cudaErrorInvalidValue;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   uint32_t grid = lc.grid ? lc.grid : 148;
-  const uint32_t unit = epi == EPI_SWIGLU ? 2 : 1;
+  const uint32_t unit = epi == EPI_SWIGLU_Q8 ? 64 : (epi == EPI_SWIGLU ? 2 : 1);
   if (grid > a.rows / unit) grid = (uint32_t)(a.rows / unit);
   if (grid == 0) return cudaSuccess;
   return launch_kernel(kern, dim3(grid), dim3(MV_THREADS), smem, lc, a);
