@@ -119,6 +119,20 @@ int yl_quantize(int fmt, yl_qtensor* dst, const float* x, uint64_t n, uint32_t g
 int yl_matmul(float* out, const yl_qtensor* x, const yl_qtensor* w, uint64_t n, uint64_t o, uint64_t gs,
               uint64_t batch, int accumulate, void* stream);
 
+/* forward.rs:299-400 `fused_attention`: causal GQA attention of `batch` query
+ * rows at positions start_pos..start_pos+batch-1 over key/value caches
+ * [seq_len][kv_dim] (queries already rotated, caches already holding the new
+ * rows, seq_len = start_pos + batch as in forward.rs:135). Scores use
+ * attn_scale, masked positions are excluded, the softmax runs over the whole
+ * visible row. sq/output: [batch][n_heads*head_size]. All device pointers.
+ * The reference takes its softmax scratch from the caller (`scores`); here a
+ * single-token call splits the keys across CTAs and keeps the split partials
+ * in a workspace this function allocates and frees on `stream`.
+ * head_size 64 or 128, n_heads/n_kv_heads <= 8. */
+int yl_fused_attention(float* output, const float* sq, const float* key_cache, const float* value_cache,
+                       uint64_t seq_len, uint64_t batch, uint64_t n_heads, uint64_t n_kv_heads, uint64_t head_size,
+                       uint32_t start_pos, uint64_t kv_dim, float attn_scale, void* stream);
+
 /* ---- model and sessions (transformer.rs:19-69, lib.rs:107-133) ---------- */
 typedef struct yl_model yl_model;
 typedef struct yl_session yl_session;

@@ -155,6 +155,18 @@ def silu(x: np.ndarray) -> np.ndarray:
     return x
 
 
+def fused_attention(sq, key_cache, value_cache, seq_len: int, batch: int, n_heads: int, n_kv_heads: int,
+                    head_size: int, start_pos: int, kv_dim: int, attn_scale: float) -> np.ndarray:
+    sq = np.ascontiguousarray(sq, np.float32)
+    kc = np.ascontiguousarray(key_cache, np.float32)
+    vc = np.ascontiguousarray(value_cache, np.float32)
+    out = np.zeros(batch * n_heads * head_size, np.float32)
+    scores = np.zeros(n_heads * batch * seq_len, np.float32)
+    lib().orc_fused_attention(_p(out), _p(scores), _p(sq), _p(kc), _p(vc), seq_len, batch, n_heads, n_kv_heads,
+                              head_size, start_pos, kv_dim, attn_scale)
+    return out
+
+
 def argmax(p: np.ndarray) -> int:
     p = np.ascontiguousarray(p, np.float32)
     return int(lib().orc_argmax(_p(p), p.size))

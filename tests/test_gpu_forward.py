@@ -122,7 +122,8 @@ def test_c1_smollm_shape_128_steps(yl, orc, model_factory):
     path = model_factory("c1")
     prompt = yl.prompt_ids(49152, 16, 1000).tolist()
     errs, gids, oids, _, _ = run_pair(yl, orc, path, prompt, 128, 512)
-    assert max(errs) < LOGIT_TOL, max(errs)
+    sens = oracle_sensitivity(orc, path, prompt, oids, 512)
+    assert max(errs) < bound_for(sens), (max(errs), sens)
     assert gids == oids
     # free-running device decode (its own ids fed back) gives the same sequence
     gm = yl.load_transformer(path, max_ctx_len=512)

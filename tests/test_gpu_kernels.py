@@ -219,3 +219,27 @@ def test_matmul_format_mismatch(yl, torch_cuda):
     with pytest.raises(yl.YlError) as e:
         yl.matmul(out, x, w, 64, 8, 32)
     assert e.value.code == -3
+
+
+@pytest.mark.parametrize("hd,nh,nkv,batch,start", [
+    (128, 32, 8, 1, 700), (64, 9, 3, 1, 40), (64, 32, 8, 1, 0), (128, 4, 1, 1, 3000),
+    (128, 32, 8, 7, 100), (64, 32, 8, 16, 0),
+])
+def test_fused_attention_vs_oracle(yl, orc, torch_cuda, hd, nh, nkv, batch, start):
+    """forward.rs:299-400 through yl_fused_attention (split-sequence partials
+    for single-token calls) against the oracle's restatement."""
+    rng = np.random.default_rng(hd + nh + batch + start)
+    seq = start + batch
+    kvd = nkv * hd
+    sq = rng.standard_normal(batch * nh * hd).astype(np.float32)
+    kc = rng.standard_normal(seq * kvd).astype(np.float32)
+    vc = rng.standard_normal(seq * kvd).astype(np.float32)
+    scale = 1.0 / np.sqrt(hd)
+    ref = orc.fused_attention(sq, kc, vc, seq, batch, nh, nkv, hd, start, kvd, scale)
+    out = torch_cuda.zeros(batch * nh * hd, device="cuda")
+    yl.fused_attention(out, dev(torch_cuda, sq), dev(torch_cuda, kc), dev(torch_cuda, vc), seq, batch, nh, nkv, hd,
+                       start, kvd, float(scale))
+    torch_cuda.cuda.synchronize()
+    got = out.cpu().numpy()
+    # outputs are convex combinations of V rows: absolute error vs max|V|
+    assert np.max(np.abs(got - ref)) <= 1e-5 * np.max(np.abs(vc))

@@ -78,6 +78,8 @@ _sigs = {
     "yl_quantize": (C.c_int, [C.c_int, C.POINTER(QTensorC), _P, C.c_uint64, C.c_uint32, _P]),
     "yl_matmul": (C.c_int, [_P, C.POINTER(QTensorC), C.POINTER(QTensorC), C.c_uint64, C.c_uint64, C.c_uint64,
                             C.c_uint64, C.c_int, _P]),
+    "yl_fused_attention": (C.c_int, [_P, _P, _P, _P, C.c_uint64, C.c_uint64, C.c_uint64, C.c_uint64, C.c_uint64,
+                                     C.c_uint32, C.c_uint64, C.c_float, _P]),
     "yl_load_transformer": (C.c_int, [C.c_char_p, C.c_int, C.c_uint32, C.c_int, C.POINTER(_P)]),
     "yl_model_free": (C.c_int, [_P]),
     "yl_model_name": (C.c_char_p, [_P]),
@@ -264,6 +266,13 @@ def matmul(out, x: QuantizedTensor, w: QuantizedTensor, n: int, o: int, gs: int,
         batch = out.numel() // o
     _check(_lib.yl_matmul(_ptr(out), C.byref(x.c), C.byref(w.c), n, o, gs, batch, 1 if accumulate else 0,
                           _stream(stream)))
+
+
+def fused_attention(output, sq, key_cache, value_cache, seq_len: int, batch: int, n_heads: int, n_kv_heads: int,
+                    head_size: int, start_pos: int, kv_dim: int, attn_scale: float, stream=None) -> None:
+    """forward.rs:299-400 on device tensors (queries rotated, caches filled)."""
+    _check(_lib.yl_fused_attention(_ptr(output), _ptr(sq), _ptr(key_cache), _ptr(value_cache), seq_len, batch,
+                                   n_heads, n_kv_heads, head_size, start_pos, kv_dim, attn_scale, _stream(stream)))
 
 
 # -------------------------------------------------- transformer.rs ---

@@ -241,6 +241,65 @@ int yl_matmul(float* out, const yl_qtensor* x, const yl_qtensor* w, uint64_t n, 
                     false, sms);
 }
 
+// Split count for a single-token attention call: enough CTAs to cover the
+// SMs twice, never more splits than keys, at most 64.
+static uint32_t attention_splits(uint64_t seq_len, uint64_t n_kv_heads) {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  uint64_t ns = (2 * (uint64_t)sms + n_kv_heads - 1) / n_kv_heads;
+  ns = std::min<uint64_t>(ns, 64);
+  ns = std::min<uint64_t>(ns, std::max<uint64_t>(seq_len, 1));
+  return (uint32_t)std::max<uint64_t>(ns, 1);
+}
+
+static int check_attention_args(const float* output, const float* sq, const float* kc, const float* vc,
+                                uint64_t seq_len, uint64_t batch, uint64_t n_heads, uint64_t n_kv_heads,
+                                uint64_t head_size, uint32_t start_pos, uint64_t kv_dim) {
+  if (!output || !sq || !kc || !vc) return fail(YL_ERR_ARG, "null pointer");
+  if (batch == 0) return fail(YL_ERR_ARG, "empty batch");
+  if (head_size != 64 && head_size != 128) return fail(YL_ERR_UNSUPPORTED, "head_size must be 64 or 128");
+  if (n_kv_heads == 0 || n_heads % n_kv_heads || n_heads / n_kv_heads > 8)
+    return fail(YL_ERR_UNSUPPORTED, "n_heads must be a multiple (at most 8x) of n_kv_heads");
+  if (kv_dim < n_kv_heads * head_size) return fail(YL_ERR_ARG, "kv_dim smaller than n_kv_heads * head_size");
+  if ((uint64_t)start_pos + batch > seq_len) return fail(YL_ERR_RANGE, "start_pos + batch exceeds seq_len");
+  if (((uintptr_t)kc | (uintptr_t)vc) % 16 || kv_dim % 4) return fail(YL_ERR_ARG, "caches must be 16-byte aligned");
+  return YL_OK;
+}
+
+int yl_fused_attention(float* output, const float* sq, const float* key_cache, const float* value_cache,
+                       uint64_t seq_len, uint64_t batch, uint64_t n_heads, uint64_t n_kv_heads, uint64_t head_size,
+                       uint32_t start_pos, uint64_t kv_dim, float attn_scale, void* stream) {
+  int rc = check_attention_args(output, sq, key_cache, value_cache, seq_len, batch, n_heads, n_kv_heads, head_size,
+                                start_pos, kv_dim);
+  if (rc) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  k::AttnArgs a{};
+  a.q = sq;
+  a.kcache = key_cache;
+  a.vcache = value_cache;
+  a.ntok = (uint32_t)batch;
+  a.n_heads = (uint32_t)n_heads;
+  a.n_kv_heads = (uint32_t)n_kv_heads;
+  a.head_size = (uint32_t)head_size;
+  a.kv_dim = (uint32_t)kv_dim;
+  a.pos0 = start_pos;
+  a.scale = attn_scale;
+  a.n_splits = batch == 1 ? attention_splits(seq_len, n_kv_heads) : 1;
+  a.out = output;
+  void* ws = nullptr;
+  if (a.n_splits > 1) {
+    YL_CUDA_TRY(cudaMallocAsync(&ws, n_heads * a.n_splits * (head_size + 2) * 4, st));
+    a.part = (float*)ws;
+  }
+  k::LaunchCfg lc;
+  lc.stream = st;
+  cudaError_t e = k::attention(a, lc);
+  if (ws) cudaFreeAsync(ws, st);
+  if (e != cudaSuccess) return fail(YL_ERR_CUDA, std::string("attention launch: ") + cudaGetErrorString(e));
+  return YL_OK;
+}
+
 // ------------------------------- model -----------------------------------
 
 int yl_load_transformer(const char* path, int sequential, uint32_t max_ctx_len, int fmt_override, yl_model** out) {

@@ -99,10 +99,10 @@ int forward(Session* s, const uint32_t* tokens_host, uint32_t n, uint32_t start_
 int ensure_decode_graph(Session* s);
 // Tunables read once from the environment (YL_MV_KC_BYTES, YL_MV_SMEM, YL_PDL).
 struct Tunables {
-  uint32_t kc_bytes = 2048;
-  uint32_t smem = 100 * 1024;
+  uint32_t kc_bytes = 4096;  // weight bytes per row per bulk copy
+  uint32_t smem = 100 * 1024;  // per CTA: two matvec CTAs fit on one SM
   bool pdl = true;
-  uint32_t grid_mult = 1;
+  uint32_t grid_mult = 2;    // matvec CTAs per SM
 };
 const Tunables& tunables();
 // Launches the matvec for `ntok` tokens (groups of 8) with activations x*.

@@ -222,7 +222,14 @@ __global__ void __launch_bounds__(AT_THREADS) attn_combine_kernel(AttnArgs a) {
   __syncthreads();
   for (uint32_t d = threadIdx.x; d < HD; d += AT_THREADS) {
     float acc = 0.0f;
-    for (uint32_t s = 0; s < a.n_splits; ++s) acc = fmaf(base[s * (HD + 2) + 2 + d], wgt[s], acc);
+    for (uint32_t s0 = 0; s0 < a.n_splits; s0 += 8) {  // 8 independent loads in flight
+      float v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = s0 + j < a.n_splits ? base[(s0 + j) * (HD + 2) + 2 + d] : 0.0f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (s0 + j < a.n_splits) acc = fmaf(v[j], wgt[s0 + j], acc);
+    }
     o[d] = acc * inv_l;
   }
   __syncthreads();
@@ -327,7 +334,14 @@ __global__ void __launch_bounds__(AT_THREADS) attn_decode_kernel(AttnDecodeArgs 
     __syncthreads();
     for (uint32_t d = threadIdx.x; d < HD; d += AT_THREADS) {
       float acc = 0.0f;
-      for (uint32_t s = 0; s < a.n_splits; ++s) acc = fmaf(__ldcg(base + s * (HD + 2) + 2 + d), wgt[s], acc);
+      for (uint32_t s0 = 0; s0 < a.n_splits; s0 += 8) {  // 8 independent L2 loads in flight
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = s0 + j < a.n_splits ? __ldcg(base + (s0 + j) * (HD + 2) + 2 + d) : 0.0f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          if (s0 + j < a.n_splits) acc = fmaf(v[j], wgt[s0 + j], acc);
+      }
       sm.os[0][d] = acc * sm.ls[0];
     }
     __syncthreads();

@@ -115,15 +115,24 @@ __device__ __forceinline__ void mv_stage_x(const MvArgs& a, const MvLayout& L, u
     for (int t = 0; t < NT; ++t) {
       const bool valid = t < (int)a.ntok;
       const float* xr = a.xres + (uint64_t)t * a.x_tok_stride;
-      // sum of squares, same order as rmsnorm_quant_kernel (256 threads, float4)
+      // sum of squares, same order as rmsnorm_quant_kernel (256 threads,
+      // float4); the loads are issued four at a time so they overlap
       float ss = 0.0f;
       if (valid)
-        for (uint32_t i = ctid * 4; i < K; i += MV_NCW * 32 * 4) {
-          const float4 v = *reinterpret_cast<const float4*>(xr + i);
-          ss = fmaf(v.x, v.x, ss);
-          ss = fmaf(v.y, v.y, ss);
-          ss = fmaf(v.z, v.z, ss);
-          ss = fmaf(v.w, v.w, ss);
+        for (uint32_t i0 = ctid * 4; i0 < K; i0 += 4 * MV_NCW * 32 * 4) {
+          float4 v[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const uint32_t i = i0 + u * MV_NCW * 32 * 4;
+            v[u] = i < K ? *reinterpret_cast<const float4*>(xr + i) : make_float4(0, 0, 0, 0);
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            ss = fmaf(v[u].x, v[u].x, ss);
+            ss = fmaf(v[u].y, v[u].y, ss);
+            ss = fmaf(v[u].z, v[u].z, ss);
+            ss = fmaf(v[u].w, v[u].w, ss);
+          }
         }
       ss = warp_sum(ss);
       if (lane == 0) red[cw] = ss;
@@ -143,22 +152,34 @@ __device__ __forceinline__ void mv_stage_x(const MvArgs& a, const MvLayout& L, u
         int8_t* xq = reinterpret_cast<int8_t*>(smem + L.x_off) + t * K;
         float* xs = reinterpret_cast<float*>(smem + L.xs_off) + t * nb;
         int* xsum = reinterpret_cast<int*>(smem + L.xsum_off) + t * nb;
-        for (uint32_t b = cw; b < nb; b += MV_NCW) {
-          const uint32_t k = b * 32 + lane;
-          const float y = valid ? __fmul_rn(a.norm_w[k], __fmul_rn(r, xr[k])) : 0.0f;
-          float sc;
-          const int8_t q = quant_q8_lane(y, &sc);
-          if (FMT == FMT_Q4) {
-            const uint32_t off = (lane < 16) ? b * 16 + lane : nb * 16 + b * 16 + (lane - 16);
-            xq[off] = q;
-            int s = (int)q;
+        // four blocks per warp pass: their loads and quantizer chains overlap
+        for (uint32_t b0 = cw; b0 < nb; b0 += 4 * MV_NCW) {
+          float y[4];
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(FULL, s, o);
-            if (lane == 0) xsum[b] = s;
-          } else {
-            xq[k] = q;
+          for (int u = 0; u < 4; ++u) {
+            const uint32_t b = b0 + u * MV_NCW;
+            const uint32_t k = b * 32 + lane;
+            y[u] = (valid && b < nb) ? __fmul_rn(a.norm_w[k], __fmul_rn(r, xr[k])) : 0.0f;
           }
-          if (lane == 0) xs[b] = sc;
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const uint32_t b = b0 + u * MV_NCW;
+            if (b >= nb) break;  // warp-uniform
+            const uint32_t k = b * 32 + lane;
+            float sc;
+            const int8_t q = quant_q8_lane(y[u], &sc);
+            if (FMT == FMT_Q4) {
+              const uint32_t off = (lane < 16) ? b * 16 + lane : nb * 16 + b * 16 + (lane - 16);
+              xq[off] = q;
+              int s = (int)q;
+#pragma unroll
+              for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(FULL, s, o);
+              if (lane == 0) xsum[b] = s;
+            } else {
+              xq[k] = q;
+            }
+            if (lane == 0) xs[b] = sc;
+          }
         }
       }
     }
