@@ -133,6 +133,24 @@ int yl_fused_attention(float* output, const float* sq, const float* key_cache, c
                        uint64_t seq_len, uint64_t batch, uint64_t n_heads, uint64_t n_kv_heads, uint64_t head_size,
                        uint32_t start_pos, uint64_t kv_dim, float attn_scale, void* stream);
 
+/* No counterpart in the reference: an addition of this library.
+ * yl_fused_attention without any allocation, for callers that cannot call
+ * cudaMalloc or cudaMallocAsync where attention runs (an engine whose memory
+ * manager owns all device memory, or a latency-critical loop that must not
+ * risk the allocator's implicit synchronization or out-of-memory failures).
+ * Same arguments and result as yl_fused_attention; the split partials live in
+ * a fixed device array of YL_ATTN_STATIC_BYTES (1 MiB) that every GPU loading
+ * this library holds until the process exits. A call whose partials would not
+ * fit (n_heads * splits * (head_size + 2) * 4 bytes) fails with
+ * YL_ERR_UNSUPPORTED. The first call on a device resolves the array's device
+ * address (cudaGetSymbolAddress), so make that first call before any stream
+ * capture. All calls share the array: calls that overlap on the GPU (other
+ * streams, other threads) race on it; serialize them. */
+#define YL_ATTN_STATIC_BYTES (1u << 20)
+int yl_fused_attention_static(float* output, const float* sq, const float* key_cache, const float* value_cache,
+                              uint64_t seq_len, uint64_t batch, uint64_t n_heads, uint64_t n_kv_heads,
+                              uint64_t head_size, uint32_t start_pos, uint64_t kv_dim, float attn_scale, void* stream);
+
 /* ---- model and sessions (transformer.rs:19-69, lib.rs:107-133) ---------- */
 typedef struct yl_model yl_model;
 typedef struct yl_session yl_session;

@@ -80,6 +80,8 @@ _sigs = {
                             C.c_uint64, C.c_int, _P]),
     "yl_fused_attention": (C.c_int, [_P, _P, _P, _P, C.c_uint64, C.c_uint64, C.c_uint64, C.c_uint64, C.c_uint64,
                                      C.c_uint32, C.c_uint64, C.c_float, _P]),
+    "yl_fused_attention_static": (C.c_int, [_P, _P, _P, _P, C.c_uint64, C.c_uint64, C.c_uint64, C.c_uint64,
+                                            C.c_uint64, C.c_uint32, C.c_uint64, C.c_float, _P]),
     "yl_load_transformer": (C.c_int, [C.c_char_p, C.c_int, C.c_uint32, C.c_int, C.POINTER(_P)]),
     "yl_model_free": (C.c_int, [_P]),
     "yl_model_name": (C.c_char_p, [_P]),
