@@ -221,6 +221,13 @@ int yl_decode_greedy(const yl_model* m, yl_session* s, uint32_t first_token, uin
                      uint32_t n_steps, uint32_t* tokens_out, void* stream, int sync);
 /* Number of kernel launches one batch-1 decode step issues. */
 int yl_decode_step_launches(const yl_model* m, uint32_t* out);
+/* Diagnostic: runs one batch-1 decode step of `token` at `pos` launch by
+ * launch (no graph, no programmatic dependent launch) with CUDA events
+ * between launches, and writes each launch's device time in microseconds to
+ * us_out (up to cap entries; *n_out = launches). Order: embedding, then per
+ * layer qkv, attention, wo, gate/up, down, then lm_head. */
+int yl_profile_decode_step(const yl_model* m, yl_session* s, uint32_t token, uint32_t pos, float* us_out,
+                           uint32_t cap, uint32_t* n_out);
 
 /* ---- reference FFI (lib.rs:135-152) -------------------------------------- */
 /* Loads into a process-global slot (guarded by a mutex here; `static mut` in

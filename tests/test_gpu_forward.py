@@ -25,13 +25,14 @@ def run_pair(yl, orc, path, prompt, n_gen, max_ctx, fmt_override=None):
     gm = yl.load_transformer(path, max_ctx_len=max_ctx, fmt_override=fmt_override)
     om = orc.Model(path, max_ctx, -1 if fmt_override is None else int(fmt_override))
     gs, os_ = gm.create_session(), om.create_session()
-    errs, gids, oids = [], [], []
+    errs, gids, oids, olg = [], [], [], []
     lg, am = gm.forward_x_full(prompt, 0, gs)
     lo = om.forward_x(prompt, 0, os_)
     assert lg[am] == lg.max() and int(np.argmax(lg)) == am  # lowest index among maxima
     errs.append(close_logits(lg, lo))
     gids.append(am)
     oids.append(orc.argmax(lo))
+    olg.append(lo)
     pos = len(prompt)
     for _ in range(n_gen):
         tok = oids[-1]
@@ -40,8 +41,24 @@ def run_pair(yl, orc, path, prompt, n_gen, max_ctx, fmt_override=None):
         errs.append(close_logits(lg, lo))
         gids.append(am)
         oids.append(orc.argmax(lo))
+        olg.append(lo)
         pos += 1
+    run_pair.oracle_logits = olg
     return errs, gids, oids, gm, gs
+
+
+def assert_ids_match(gids, oids, olg, bound):
+    """Greedy ids must be identical, except at a certified near-tie: a step
+    where the oracle's own logit margin between its choice and ours is within
+    the logit deviation bound (no implementation that is not bit-identical to
+    the oracle can order such a pair reliably). Returns the near-tie steps."""
+    flips = [k for k in range(len(oids)) if gids[k] != oids[k]]
+    for k in flips:
+        lo = olg[k]
+        margin = float(lo[oids[k]] - lo[gids[k]]) / float(np.max(np.abs(lo)))
+        assert 0.0 <= margin <= bound, (k, oids[k], gids[k], margin, bound)
+    assert len(flips) <= max(1, len(oids) // 32), flips
+    return flips
 
 
 def oracle_sensitivity(orc, path, prompt, ids, max_ctx) -> float:
@@ -83,9 +100,10 @@ def test_tiny_models_match_oracle(yl, orc, model_factory, preset, over):
     vocab = yl.PRESETS[preset]["vocab_size"]
     prompt = yl.prompt_ids(vocab, 9, 1234).tolist()
     errs, gids, oids, _, _ = run_pair(yl, orc, path, prompt, 24, 256)
+    olg = run_pair.oracle_logits
     sens = oracle_sensitivity(orc, path, prompt, oids, 256)
     assert max(errs) < bound_for(sens), (errs, sens)
-    assert gids == oids
+    assert_ids_match(gids, oids, olg, bound_for(sens))
 
 
 def test_decode_graph_matches_host_loop(yl, orc, model_factory):
@@ -105,6 +123,32 @@ def test_decode_graph_matches_host_loop(yl, orc, model_factory):
     assert dev_ids.tolist() == host_ids
 
 
+@pytest.mark.parametrize("preset", ["tiny", "tiny128"])
+def test_long_context_decode_matches_oracle(yl, orc, model_factory, preset):
+    """Decode past 16 x 64 positions: every split of the decode attention
+    walks several key tiles (online softmax across tiles), and the graph path
+    (keys fetched before the wait on the projection) equals the host loop."""
+    path = model_factory(preset, context_length=2048)
+    vocab = yl.PRESETS[preset]["vocab_size"]
+    prompt = yl.prompt_ids(vocab, 1500, 77).tolist()
+    errs, gids, oids, _, _ = run_pair(yl, orc, path, prompt, 6, 2048)
+    olg = run_pair.oracle_logits
+    sens = oracle_sensitivity(orc, path, prompt, oids, 2048)
+    assert max(errs) < bound_for(sens), (errs, sens)
+    assert_ids_match(gids, oids, olg, bound_for(sens))
+    gm = yl.load_transformer(path, max_ctx_len=2048)
+    s1 = gm.create_session()
+    _, first = gm.forward_x_full(prompt, 0, s1, want_logits=False)
+    dev_ids = gm.decode_greedy(s1, first, len(prompt), 24).tolist()
+    s2 = gm.create_session()
+    _, tok = gm.forward_x_full(prompt, 0, s2, want_logits=False)
+    host_ids = []
+    for i in range(24):
+        _, tok = gm.forward_x_full([tok], len(prompt) + i, s2, want_logits=False)
+        host_ids.append(tok)
+    assert dev_ids == host_ids
+
+
 def test_prefill_equals_stepwise_on_device(yl, model_factory):
     path = model_factory("tiny")
     gm = yl.load_transformer(path, max_ctx_len=256)
@@ -122,16 +166,19 @@ def test_c1_smollm_shape_128_steps(yl, orc, model_factory):
     path = model_factory("c1")
     prompt = yl.prompt_ids(49152, 16, 1000).tolist()
     errs, gids, oids, _, _ = run_pair(yl, orc, path, prompt, 128, 512)
+    olg = run_pair.oracle_logits
     sens = oracle_sensitivity(orc, path, prompt, oids, 512)
     assert max(errs) < bound_for(sens), (max(errs), sens)
-    assert gids == oids
-    # free-running device decode (its own ids fed back) gives the same sequence
+    flips = assert_ids_match(gids, oids, olg, bound_for(sens))
+    # free-running device decode (its own ids fed back) follows the oracle's
+    # sequence up to the first near-tie
     gm = yl.load_transformer(path, max_ctx_len=512)
     s = gm.create_session()
     _, first = gm.forward_x_full(prompt, 0, s, want_logits=False)
-    assert first == oids[0]
-    dev = gm.decode_greedy(s, first, len(prompt), 128)
-    assert dev.tolist() == oids[1:]
+    assert first == gids[0]
+    dev = gm.decode_greedy(s, first, len(prompt), 128).tolist()
+    upto = flips[0] if flips else 128
+    assert dev[:upto] == gids[1:upto + 1]
 
 
 def test_embeddings_match_oracle(yl, orc, model_factory):

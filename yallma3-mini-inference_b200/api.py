@@ -103,6 +103,7 @@ _sigs = {
     "yl_forward_x": (C.c_int, [_P, _P, _P, C.c_uint64, C.c_uint32, _P, _P]),
     "yl_decode_greedy": (C.c_int, [_P, _P, C.c_uint32, C.c_uint32, C.c_uint32, _P, _P, C.c_int]),
     "yl_decode_step_launches": (C.c_int, [_P, C.POINTER(C.c_uint32)]),
+    "yl_profile_decode_step": (C.c_int, [_P, _P, C.c_uint32, C.c_uint32, _P, C.c_uint32, C.POINTER(C.c_uint32)]),
     "load_transformer_ffi": (C.c_bool, [C.c_char_p]),
     "yl_synth_write_gguf": (C.c_int, [C.c_char_p, C.POINTER(SynthC)]),
 }
@@ -388,6 +389,15 @@ class Transformer:
         n = C.c_uint32()
         _check(_lib.yl_decode_step_launches(self._h, C.byref(n)))
         return n.value
+
+    def profile_decode_step(self, session: InferenceSession, token: int, pos: int) -> np.ndarray:
+        """Per-launch device microseconds of one decode step launched kernel
+        by kernel: [embed, (qkv, attention, wo, gate/up, down) x layers, lm_head]."""
+        cap = 8 + 8 * self.shape().n_layers
+        us = np.zeros(cap, np.float32)
+        n = C.c_uint32()
+        _check(_lib.yl_profile_decode_step(self._h, session._h, token, pos, _ptr(us), cap, C.byref(n)))
+        return us[:n.value]
 
     def weight(self, layer: int, which: int) -> QuantizedTensor:
         c = QTensorC()

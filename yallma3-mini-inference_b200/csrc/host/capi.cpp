@@ -524,6 +524,13 @@ int yl_decode_step_launches(const yl_model* m, uint32_t* out) {
   return YL_OK;
 }
 
+int yl_profile_decode_step(const yl_model* m, yl_session* sp, uint32_t token, uint32_t pos, float* us_out,
+                           uint32_t cap, uint32_t* n_out) {
+  if (!m || !sp) return fail(YL_ERR_ARG, "null argument");
+  if (sp->s->m != m->m) return fail(YL_ERR_ARG, "session belongs to another model");
+  return profile_step(sp->s, token, pos, us_out, cap, n_out);
+}
+
 // ------------------------------- reference FFI ---------------------------
 
 static std::mutex g_ffi_mu;

@@ -300,6 +300,7 @@ const Tunables& tunables() {
     if (const char* e = getenv("YL_MV_SMEM")) x.smem = (uint32_t)atoi(e);
     if (const char* e = getenv("YL_PDL")) x.pdl = atoi(e) != 0;
     if (const char* e = getenv("YL_MV_GRID_MULT")) x.grid_mult = std::max(1, atoi(e));
+    if (const char* e = getenv("YL_LM_LIMBS")) x.limbs = atoi(e) != 0;
     return x;
   }();
   return t;
@@ -550,6 +551,9 @@ int ensure_cap(Session* s, uint32_t n) {
   s->hq = (int8_t*)p;
   if ((rc = salloc(s, cap * (uint64_t)(sh.hidden_dim / 32) * 4ull, &p))) return rc;
   s->hs = (float*)p;
+  if ((rc = salloc(s, cap * (uint64_t)(sh.hidden_dim / 32) * 4ull, &p))) return rc;
+  s->hcount = (unsigned int*)p;
+  YL_CUDA_TRY(cudaMemset(s->hcount, 0, cap * (uint64_t)(sh.hidden_dim / 32) * 4ull));
   if ((rc = salloc(s, cap * 4ull, &p))) return rc;
   s->tok = (uint32_t*)p;
   s->cap = cap;
@@ -576,16 +580,12 @@ int session_create(const Model* m, Session** out) {
   YL_CUDA_TRY(cudaMemset(s->vcache, 0, s->kv_elems * 4));
   if ((rc = salloc(s.get(), (uint64_t)sh.vocab_size * 4, &p))) return rc;
   s->logits = (float*)p;
-  // decode split count: enough CTAs to cover the SMs twice
-  uint32_t ns = (2 * (uint32_t)m->num_sms + sh.n_kv_heads - 1) / sh.n_kv_heads;
-  s->n_splits = std::max(1u, std::min(64u, ns));
+  // decode attention: one cluster of n_splits CTAs per KV head
+  s->n_splits = k::attention_decode_splits(sh.n_kv_heads, sh.head_size);
   if ((rc = salloc(s.get(), (uint64_t)sh.n_heads * s->n_splits * (sh.head_size + 2) * 4, &p))) return rc;
   s->part = (float*)p;
   if ((rc = salloc(s.get(), ((uint64_t)sh.ctx_len + 1) * 4, &p))) return rc;
   s->hist = (uint32_t*)p;
-  if ((rc = salloc(s.get(), (uint64_t)sh.n_kv_heads * 4, &p))) return rc;
-  s->att_count = (unsigned int*)p;
-  YL_CUDA_TRY(cudaMemset(s->att_count, 0, (uint64_t)sh.n_kv_heads * 4));
   const uint64_t am_slots = (uint64_t)m->num_sms * 8;
   if ((rc = salloc(s.get(), am_slots * 4, &p))) return rc;
   s->am_val = (float*)p;
@@ -633,7 +633,12 @@ int run_matvec_ex(const DevWeight& w, bool f32act, const int8_t* xq, const float
   const Tunables& tu = tunables();
   int fmt;
   uint32_t kc;
-  if (w.fmt == YL_Q8_0) { fmt = f32act ? k::FMT_Q8F : k::FMT_Q8; kc = tu.kc_bytes; }
+  if (w.fmt == YL_Q8_0) {
+    fmt = f32act ? k::FMT_Q8F : k::FMT_Q8;
+    // f32 activations out of the norm prologue run as three int8 limbs (dp4a)
+    if (f32act && tu.limbs && ex.pro == k::PRO_NORM && w.cols <= 8192) fmt = k::FMT_Q8X;
+    kc = tu.kc_bytes;
+  }
   else if (w.fmt == YL_Q4_0) { fmt = f32act ? k::FMT_Q4F : k::FMT_Q4; kc = tu.kc_bytes * 2; }
   else { fmt = k::FMT_F16; kc = tu.kc_bytes / 2; }
   kc = std::max<uint32_t>(256, kc / 256 * 256);
@@ -670,6 +675,7 @@ int run_matvec_ex(const DevWeight& w, bool f32act, const int8_t* xq, const float
     a.eps = ex.eps;
     a.hq = ex.hq ? ex.hq + t0 * (uint64_t)(w.rows / 2) : nullptr;
     a.hs = ex.hs ? ex.hs + t0 * (uint64_t)(w.rows / 64) : nullptr;
+    a.hcount = ex.hcount ? ex.hcount + t0 * (uint64_t)(w.rows / 64) : nullptr;
     a.am_val = ex.am_val;
     a.am_idx = ex.am_idx;
     a.am_count = ex.am_count;
@@ -699,18 +705,31 @@ int enqueue_forward(Session* s, uint32_t n, uint32_t start_pos, bool from_state,
   uint32_t nl = 0;
   cudaError_t e;
   int rc;
+// With s->prof set (profiling), an event is recorded after every launch.
+#define YL_MARK()                                   \
+  do {                                              \
+    if (s->prof) {                                  \
+      cudaEvent_t ev_;                              \
+      YL_CUDA_TRY(cudaEventCreate(&ev_));           \
+      s->prof->push_back(ev_);                      \
+      YL_CUDA_TRY(cudaEventRecordWithFlags(ev_, s->stream, cudaEventRecordExternal)); \
+    }                                               \
+  } while (0)
 #define YL_LAUNCH(expr)                                                                   \
   do {                                                                                    \
     e = (expr);                                                                           \
     if (e != cudaSuccess) return fail(YL_ERR_CUDA, std::string(#expr) + ": " + cudaGetErrorString(e)); \
     ++nl;                                                                                 \
+    YL_MARK();                                                                            \
   } while (0)
 #define YL_MV(...)                                  \
   do {                                              \
     if ((rc = run_matvec(__VA_ARGS__))) return rc;  \
     nl += 1;                                        \
+    YL_MARK();                                      \
   } while (0)
 
+  YL_MARK();
   YL_LAUNCH(k::embed(m->emb.fmt == YL_Q8_0 ? k::FMT_Q8 : m->emb.fmt == YL_Q4_0 ? k::FMT_Q4 : k::FMT_F16, m->emb.q,
                      m->emb.s, m->emb.row_bytes, m->emb.scale_row_bytes, d, sh.vocab_size, s->tok, st, n, s->x, lc));
   const bool decode = n == 1;
@@ -727,9 +746,11 @@ int enqueue_forward(Session* s, uint32_t n, uint32_t start_pos, bool from_state,
     norm.norm_w = L.rms_att;
     norm.hq = nullptr;
     norm.hs = nullptr;
+    norm.hcount = nullptr;
     if ((rc = run_matvec_ex(L.wqkv, f32act, nullptr, nullptr, nullptr, d, d / 32, n, s->qkv, att + 2 * kvd,
                             k::EPI_STORE, 0, s->err, s->stream, pdl, m->num_sms, norm, &nl)))
       return rc;
+    YL_MARK();
     if (decode) {
       // RoPE, KV write, split attention, merge and quantize in one kernel
       k::AttnDecodeArgs ad{};
@@ -746,8 +767,7 @@ int enqueue_forward(Session* s, uint32_t n, uint32_t start_pos, bool from_state,
       ad.pos0 = start_pos;
       ad.scale = m->attn_scale;
       ad.n_splits = s->n_splits;
-      ad.part = s->part;
-      ad.count = s->att_count;
+      ad.early_kv = from_state ? 1 : 0;
       ad.out = f32act ? s->xf : nullptr;
       ad.q8 = f32act ? nullptr : s->xq;
       ad.s8 = s->xs;
@@ -778,16 +798,20 @@ int enqueue_forward(Session* s, uint32_t n, uint32_t start_pos, bool from_state,
     YL_MV(L.wo, f32act, s->xq, s->xs, s->xf, att, att / 32, n, s->x, d, k::EPI_ADD, 0, s->err, s->stream, pdl,
           m->num_sms);
     // ---- feed-forward block (forward.rs:206-253) ----
-    // RMSNorm + quantize in the prologue; SwiGLU (and, for quantized
-    // formats, the Q8_0 quantization of h) in the epilogue. F16Kernel's
-    // quantize is a copy (forward.rs:78-81), so the F16 path keeps h in f32.
+    // RMSNorm + quantize in the prologue, SwiGLU in the epilogue (row pairs:
+    // any CTA split keeps gate and up together), which for quantized formats
+    // also quantizes h once (forward.rs:240). F16Kernel's quantize is a copy
+    // (forward.rs:78-81), so the F16 path keeps h in f32.
     norm.norm_w = L.rms_ffn;
     norm.hq = f32act ? nullptr : s->hq;
     norm.hs = f32act ? nullptr : s->hs;
+    norm.hcount = f32act ? nullptr : s->hcount;
     if ((rc = run_matvec_ex(L.w13, f32act, nullptr, nullptr, nullptr, d, d / 32, n, s->h, f,
                             f32act ? k::EPI_SWIGLU : k::EPI_SWIGLU_Q8, 0, s->err, s->stream, pdl, m->num_sms, norm,
                             &nl)))
       return rc;
+    YL_MARK();
+    // down projection + residual add
     YL_MV(L.w2, f32act, s->hq, s->hs, s->h, f, f / 32, n, s->x, d, k::EPI_ADD, 0, s->err, s->stream, pdl,
           m->num_sms);
   }
@@ -807,9 +831,11 @@ int enqueue_forward(Session* s, uint32_t n, uint32_t start_pos, bool from_state,
     if ((rc = run_matvec_ex(m->lm, true, nullptr, nullptr, nullptr, d, 0, 1, s->logits, sh.vocab_size, k::EPI_ARGMAX,
                             0, s->err, s->stream, pdl, m->num_sms, fin, &nl)))
       return rc;
+    YL_MARK();
   }
 #undef YL_LAUNCH
 #undef YL_MV
+#undef YL_MARK
   if (launches) *launches = nl;
   return YL_OK;
 }
@@ -826,6 +852,43 @@ int forward(Session* s, const uint32_t* tokens_host, uint32_t n, uint32_t start_
   YL_CUDA_TRY(cudaMemcpyAsync(s->tok, tokens_host, (uint64_t)n * 4, cudaMemcpyHostToDevice, s->stream));
   rc = enqueue_forward(s, n, start_pos, false, tunables().pdl, nullptr);
   if (rc) return rc;
+  return YL_OK;
+}
+
+int profile_step(Session* s, uint32_t token, uint32_t pos, float* us, uint32_t cap, uint32_t* n_out) {
+  const yl_shape& sh = s->m->shape;
+  if (pos >= sh.ctx_len) return fail(YL_ERR_RANGE, "position beyond ctx_len");
+  YL_CUDA_TRY(cudaSetDevice(s->device));
+  int rc = ensure_cap(s, 8);
+  if (rc) return rc;
+  YL_CUDA_TRY(cudaMemcpyAsync(s->tok, &token, 4, cudaMemcpyHostToDevice, s->stream));
+  YL_CUDA_TRY(cudaStreamSynchronize(s->stream));
+  // Captured as a graph (event-record nodes between kernel nodes) so that the
+  // host's launch pacing does not enter the measured gaps.
+  std::vector<cudaEvent_t> evs;
+  cudaGraph_t g = nullptr;
+  cudaGraphExec_t ge = nullptr;
+  YL_CUDA_TRY(cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal));
+  s->prof = &evs;
+  rc = enqueue_forward(s, 1, pos, false, false, nullptr);
+  s->prof = nullptr;
+  cudaError_t e = cudaStreamEndCapture(s->stream, &g);
+  if (e == cudaSuccess && rc == YL_OK) e = cudaGraphInstantiate(&ge, g, 0);
+  if (e == cudaSuccess && rc == YL_OK) e = cudaGraphLaunch(ge, s->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s->stream);
+  if (ge) cudaGraphExecDestroy(ge);
+  if (g) cudaGraphDestroy(g);
+  uint32_t n = 0;
+  for (size_t i = 1; i < evs.size(); ++i) {
+    float ms = 0.f;
+    if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, evs[i - 1], evs[i]);
+    if (n < cap && us) us[n] = ms * 1000.0f;
+    ++n;
+  }
+  for (cudaEvent_t ev : evs) cudaEventDestroy(ev);
+  if (rc) return rc;
+  if (e != cudaSuccess) return fail(YL_ERR_CUDA, std::string("profile: ") + cudaGetErrorString(e));
+  if (n_out) *n_out = n;
   return YL_OK;
 }
 

@@ -68,10 +68,10 @@ struct Session {
   float* h = nullptr;     // [cap][ffn]
   int8_t* hq = nullptr;   // [cap][ffn] quantized h (SwiGLU epilogue)
   float* hs = nullptr;    // [cap][ffn/32]
+  unsigned int* hcount = nullptr;  // [cap][ffn/32] arrival counters (zero between launches)
   uint32_t* tok = nullptr;  // [cap]
   float* logits = nullptr;  // [vocab]
-  float* part = nullptr;    // attention split partials (decode)
-  unsigned int* att_count = nullptr;  // [n_kv_heads] arrival counters (zero between launches)
+  float* part = nullptr;    // attention split partials (general path)
   float* am_val = nullptr;            // lm_head per-CTA winners
   uint32_t* am_idx = nullptr;
   unsigned int* am_count = nullptr;
@@ -83,6 +83,7 @@ struct Session {
   float* logits_h = nullptr;
   uint32_t* hist_h = nullptr;
   uint32_t n_splits = 1;
+  std::vector<cudaEvent_t>* prof = nullptr;  // profiling: events recorded after each launch
   cudaGraphExec_t graph = nullptr;
   uint32_t graph_launches = 0;
   std::vector<void*> allocs;
@@ -95,14 +96,19 @@ int session_reset(Session* s);
 // General forward over n tokens (prefill or decode); last-token logits stay in
 // s->logits (device), greedy id in s->hist[0].
 int forward(Session* s, const uint32_t* tokens_host, uint32_t n, uint32_t start_pos);
+// One batch-1 step launched kernel by kernel (no graph, no PDL) with events
+// between launches; writes per-launch device times in microseconds.
+int profile_step(Session* s, uint32_t token, uint32_t pos, float* us, uint32_t cap, uint32_t* n_out);
 // One batch-1 step through the captured graph (state already set on device).
 int ensure_decode_graph(Session* s);
-// Tunables read once from the environment (YL_MV_KC_BYTES, YL_MV_SMEM, YL_PDL).
+// Tunables read once from the environment (YL_MV_KC_BYTES, YL_MV_SMEM, YL_PDL,
+// YL_MV_GRID_MULT, YL_LM_LIMBS).
 struct Tunables {
   uint32_t kc_bytes = 4096;  // weight bytes per row per bulk copy
   uint32_t smem = 100 * 1024;  // per CTA: two matvec CTAs fit on one SM
   bool pdl = true;
   uint32_t grid_mult = 2;    // matvec CTAs per SM
+  bool limbs = true;         // Q8_0 lm_head on three-limb int8 activations
 };
 const Tunables& tunables();
 // Launches the matvec for `ntok` tokens (groups of 8) with activations x*.
@@ -115,8 +121,9 @@ struct MvExtra {
   const float* xres = nullptr; // PRO_NORM: residual rows (stride x_stride)
   const float* norm_w = nullptr;
   float eps = 0.f;
-  int8_t* hq = nullptr;        // EPI_SWIGLU_Q8 outputs
+  int8_t* hq = nullptr;        // EPI_SWIGLU_Q8 outputs and block counters
   float* hs = nullptr;
+  unsigned int* hcount = nullptr;
   float* am_val = nullptr;     // EPI_ARGMAX scratch / outputs
   uint32_t* am_idx = nullptr;
   unsigned int* am_count = nullptr;

@@ -1,4 +1,5 @@
 // RoPE + KV-cache write and causal GQA attention over the f32 KV cache.
+#include <cooperative_groups.h>
 #include <float.h>
 
 #include "device.cuh"
@@ -251,112 +252,338 @@ cudaError_t attention(const AttnArgs& a, const LaunchCfg& lc) {
   return launch_kernel(attn_combine_kernel<128>, gc, dim3(AT_THREADS), 0, lc, a);
 }
 
-// Batch-1 decode: one CTA per (KV head, key split). RoPE of q and of the new
-// key, the K/V-cache write of position `pos` (by the split that covers it),
-// the split attention, and the merge + Q8_0 quantization of the output by the
-// last CTA of each KV head to finish (arrival counter, reset by that CTA).
+// ---------------------------------------------------------------------------
+// Batch-1 decode, built for latency (the KV bytes of one decode step are a few
+// MB; the cost is the dependent chain). One cluster of n_splits CTAs per KV
+// head; CTA `rank` of the cluster takes the rank-th slice of the keys:
+//  * the slice's K and V rows are fetched with cp.async in one round trip
+//    (before the wait on the preceding kernel when early_kv is set), while q
+//    is rotated (RoPE) from the fused projection output;
+//  * the CTA that owns position `pos` rotates the new key, writes the new
+//    K/V rows to the cache and places them in its tile directly;
+//  * scores: thread (position, dim quarter) over all kv_mul query heads at
+//    once; online softmax per head; P.V: thread (dim, position group);
+//  * the splits' (max, sum, unnormalized output) partials stay in shared
+//    memory; after a cluster barrier every CTA merges a share of the 32-blocks
+//    of the KV head's output from its peers' shared memory and quantizes them.
+namespace cg = cooperative_groups;
+constexpr int AD_TILE = 64;      // positions per shared-memory tile
+constexpr int AD_THREADS = 256;
+constexpr int AD_MAXCS = 16;     // largest cluster (non-portable size)
+
 template <int HD>
-__global__ void __launch_bounds__(AT_THREADS) attn_decode_kernel(AttnDecodeArgs a) {
-  grid_dep_launch();
-  grid_dep_wait();
-  __shared__ AttnSmem<HD> sm;
-  __shared__ float wgt[64];
-  __shared__ int is_last;
-  const uint32_t kvh = blockIdx.x, sp = blockIdx.y;
+struct AdLayout {
+  static constexpr int ROW = HD + 4;             // padded row (floats): 16-byte aligned
+  static constexpr int NPH = AD_THREADS / HD;    // P.V position groups
+  static constexpr int KS = 0;
+  static constexpr int VS = KS + AD_TILE * ROW;
+  static constexpr int QS = VS + AD_TILE * ROW;             // [AT_MAXKV][HD] rotated q
+  static constexpr int SP = QS + AT_MAXKV * HD;             // [4][AT_MAXKV][AD_TILE] partial scores
+  static constexpr int PT = SP + 4 * AT_MAXKV * AD_TILE;    // [AD_TILE][AT_MAXKV] probabilities
+  static constexpr int PO = PT + AD_TILE * AT_MAXKV;        // [NPH][AT_MAXKV][HD] P.V partials
+  static constexpr int OS = PO + NPH * AT_MAXKV * HD;       // [AT_MAXKV][HD] unnormalized output
+  static constexpr int STAT = OS + AT_MAXKV * HD;           // m, l, corr [AT_MAXKV] each
+  static constexpr int TOTAL = STAT + 3 * AT_MAXKV;
+};
+
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
+}
+
+template <int HD>
+__global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(AttnDecodeArgs a) {
+  using Lo = AdLayout<HD>;
+  extern __shared__ __align__(16) float sm[];
+  cg::cluster_group cluster = cg::this_cluster();
+  float* Ks = sm + Lo::KS;
+  float* Vs = sm + Lo::VS;
+  float* qs = sm + Lo::QS;
+  float* sp4 = sm + Lo::SP;
+  float* pt = sm + Lo::PT;
+  float* po = sm + Lo::PO;
+  float* os = sm + Lo::OS;
+  float* ms = sm + Lo::STAT;
+  float* ls = ms + AT_MAXKV;
+  float* cr = ls + AT_MAXKV;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t cs = a.n_splits;
+  const uint32_t rank = cluster.block_rank();
+  const uint32_t kvh = blockIdx.x / cs;
   const uint32_t kv_mul = a.n_heads / a.n_kv_heads;
+  grid_dep_launch();
+  if (!a.early_kv) grid_dep_wait();
   const uint32_t pos = a.state ? (uint32_t)a.state->pos : a.pos0;
   const uint32_t nvis = pos + 1;
-  const uint32_t chunk = (nvis + a.n_splits - 1) / a.n_splits;
-  const uint32_t p_begin = min(nvis, sp * chunk), p_end = min(nvis, p_begin + chunk);
+  const uint32_t chunk = (nvis + cs - 1) / cs;
+  const uint32_t p_begin = min(nvis, rank * chunk), p_end = min(nvis, p_begin + chunk);
   const uint32_t att = a.n_heads * HD, half = HD / 2;
+  const bool owner = p_begin <= pos && pos < p_end;
+  const float* kbase = a.kcache + kvh * HD;
+  const float* vbase = a.vcache + kvh * HD;
+
+  auto issue_tile = [&](uint32_t base, uint32_t n) {
+    for (uint32_t i = tid; i < n * (HD / 4); i += AD_THREADS) {
+      const uint32_t r = i / (HD / 4), c4 = i % (HD / 4);
+      if (base + r == pos) continue;  // the new row is placed below
+      cp_async16(Ks + r * Lo::ROW + 4 * c4, kbase + (uint64_t)(base + r) * a.kv_dim + 4 * c4);
+      cp_async16(Vs + r * Lo::ROW + 4 * c4, vbase + (uint64_t)(base + r) * a.kv_dim + 4 * c4);
+    }
+  };
+  uint32_t t0 = p_begin, tn = min((uint32_t)AD_TILE, p_end - p_begin);
+  if (tn) issue_tile(t0, tn);
+  if (a.early_kv) grid_dep_wait();
+
+  // rotated q of the kv_mul query heads; running statistics
   const float2* c = a.cs + (uint64_t)pos * half;
-  for (uint32_t i = threadIdx.x; i < kv_mul * half; i += AT_THREADS) {
+  for (uint32_t i = tid; i < kv_mul * half; i += AD_THREADS) {
     const uint32_t hh = i / half, p = i % half;
     uint32_t i0, i1;
     pair_index(a.rope_mode, p, half, i0, i1);
     const float* src = a.qkv + (kvh * kv_mul + hh) * HD;
     float r0, r1;
     rotate(src[i0], src[i1], c[p], r0, r1);
-    sm.qs[hh][i0] = r0;
-    sm.qs[hh][i1] = r1;
+    qs[hh * HD + i0] = r0;
+    qs[hh * HD + i1] = r1;
   }
-  for (uint32_t i = threadIdx.x; i < kv_mul * HD; i += AT_THREADS) sm.os[i / HD][i % HD] = 0.0f;
-  if (threadIdx.x < kv_mul) {
-    sm.ms[threadIdx.x] = -INFINITY;
-    sm.ls[threadIdx.x] = 0.0f;
+  for (uint32_t i = tid; i < AT_MAXKV * HD; i += AD_THREADS) os[i] = 0.0f;
+  for (uint32_t i = tid; i < AD_TILE * AT_MAXKV; i += AD_THREADS) pt[i] = 0.0f;  // unused heads stay 0
+  if (tid < AT_MAXKV) {
+    ms[tid] = -INFINITY;
+    ls[tid] = 0.0f;
+    cr[tid] = 0.0f;
   }
-  if (p_begin <= pos && pos < p_end) {  // this split owns the new position
-    const float* ksrc = a.qkv + att + kvh * HD;
-    const float* vsrc = a.qkv + att + a.kv_dim + kvh * HD;
-    float* kdst = a.kcache + (uint64_t)pos * a.kv_dim + kvh * HD;
-    float* vdst = a.vcache + (uint64_t)pos * a.kv_dim + kvh * HD;
-    for (uint32_t p = threadIdx.x; p < half; p += AT_THREADS) {
-      uint32_t i0, i1;
-      pair_index(a.rope_mode, p, half, i0, i1);
-      float r0, r1;
-      rotate(ksrc[i0], ksrc[i1], c[p], r0, r1);
-      kdst[i0] = r0;
-      kdst[i1] = r1;
-    }
-    for (uint32_t d = threadIdx.x; d < HD; d += AT_THREADS) vdst[d] = vsrc[d];
-  }
-  __syncthreads();  // q in smem; this CTA's cache writes visible to its threads
-  attn_tiles<HD>(sm, a.kcache, a.vcache, a.kv_dim, kvh, kv_mul, a.scale, p_begin, p_end);
-  for (uint32_t i = threadIdx.x; i < kv_mul * (HD + 2); i += AT_THREADS) {
-    const uint32_t hh = i / (HD + 2), j = i % (HD + 2);
-    const uint32_t h = kvh * kv_mul + hh;
-    float* dst = a.part + ((uint64_t)h * a.n_splits + sp) * (HD + 2);
-    dst[j] = j == 0 ? sm.ms[hh] : (j == 1 ? sm.ls[hh] : sm.os[hh][j - 2]);
-  }
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) is_last = atomicAdd(a.count + kvh, 1u) == a.n_splits - 1;
-  __syncthreads();
-  if (!is_last) return;
-  __threadfence();
-  for (uint32_t hh = 0; hh < kv_mul; ++hh) {
-    const uint32_t h = kvh * kv_mul + hh;
-    const float* base = a.part + (uint64_t)h * a.n_splits * (HD + 2);
-    if (threadIdx.x < 32) {
-      float M = -INFINITY;
-      for (uint32_t s = threadIdx.x; s < a.n_splits; s += 32) M = fmaxf(M, __ldcg(base + s * (HD + 2)));
-      M = warp_max(M);
-      float L = 0.0f;
-      for (uint32_t s = threadIdx.x; s < a.n_splits; s += 32) {
-        const float m = __ldcg(base + s * (HD + 2));
-        const float w = m == -INFINITY ? 0.0f : expf(m - M);
-        wgt[s] = w;
-        L += __ldcg(base + s * (HD + 2) + 1) * w;
+  __syncthreads();  // an empty split goes straight to the merge
+
+  const uint32_t ntiles = (p_end - p_begin + AD_TILE - 1) / AD_TILE;
+  for (uint32_t ti = 0; ti < ntiles; ++ti) {
+    t0 = p_begin + ti * AD_TILE;
+    tn = min((uint32_t)AD_TILE, p_end - t0);
+    if (ti > 0) issue_tile(t0, tn);
+    if (owner && pos >= t0 && pos < t0 + tn) {
+      // new key (rotated) and value rows: cache write + tile placement
+      const float* ksrc = a.qkv + att + kvh * HD;
+      const float* vsrc = a.qkv + att + a.kv_dim + kvh * HD;
+      float* kdst = a.kcache + (uint64_t)pos * a.kv_dim + kvh * HD;
+      float* vdst = a.vcache + (uint64_t)pos * a.kv_dim + kvh * HD;
+      const uint32_t r = pos - t0;
+      for (uint32_t p = tid; p < half; p += AD_THREADS) {
+        uint32_t i0, i1;
+        pair_index(a.rope_mode, p, half, i0, i1);
+        float r0, r1;
+        rotate(ksrc[i0], ksrc[i1], c[p], r0, r1);
+        kdst[i0] = r0;
+        kdst[i1] = r1;
+        Ks[r * Lo::ROW + i0] = r0;
+        Ks[r * Lo::ROW + i1] = r1;
       }
-      L = warp_sum(L);
-      if (threadIdx.x == 0) sm.ls[0] = L > 0.0f ? 1.0f / L : 0.0f;
-    }
-    __syncthreads();
-    for (uint32_t d = threadIdx.x; d < HD; d += AT_THREADS) {
-      float acc = 0.0f;
-      for (uint32_t s0 = 0; s0 < a.n_splits; s0 += 8) {  // 8 independent L2 loads in flight
-        float v[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) v[j] = s0 + j < a.n_splits ? __ldcg(base + (s0 + j) * (HD + 2) + 2 + d) : 0.0f;
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-          if (s0 + j < a.n_splits) acc = fmaf(v[j], wgt[s0 + j], acc);
+      for (uint32_t d = tid; d < HD; d += AD_THREADS) {
+        const float v = vsrc[d];
+        vdst[d] = v;
+        Vs[r * Lo::ROW + d] = v;
       }
-      sm.os[0][d] = acc * sm.ls[0];
+    }
+    cp_async_wait_all();
+    __syncthreads();
+    // scores (forward.rs:328-346): thread (position p, dim quarter dq) forms
+    // the partial dots of all kv_mul heads; K rows are read once per quarter
+    {
+      constexpr int DQ = HD / 4;
+      const uint32_t p = tid % AD_TILE, dq = tid / AD_TILE;
+      float s[AT_MAXKV];
+#pragma unroll
+      for (int h = 0; h < AT_MAXKV; ++h) s[h] = 0.0f;
+      if (p < tn) {
+        const float* kr = Ks + p * Lo::ROW + dq * DQ;
+#pragma unroll 4
+        for (int j = 0; j < DQ; j += 4) {
+          const float4 k4 = *reinterpret_cast<const float4*>(kr + j);
+#pragma unroll
+          for (int h = 0; h < AT_MAXKV; ++h) {
+            if (h >= (int)kv_mul) break;
+            const float4 q4 = *reinterpret_cast<const float4*>(qs + h * HD + dq * DQ + j);
+            s[h] = fmaf(q4.x, k4.x, s[h]);
+            s[h] = fmaf(q4.y, k4.y, s[h]);
+            s[h] = fmaf(q4.z, k4.z, s[h]);
+            s[h] = fmaf(q4.w, k4.w, s[h]);
+          }
+        }
+      }
+#pragma unroll
+      for (int h = 0; h < AT_MAXKV; ++h)
+        if (h < (int)kv_mul) sp4[(dq * AT_MAXKV + h) * AD_TILE + p] = s[h];
     }
     __syncthreads();
-    attn_emit<HD>(a.out, a.q8, a.s8, (uint64_t)h * HD, sm.os[0]);
+    // online softmax update, warp per query head (forward.rs:348-366)
+    for (uint32_t hh = warp; hh < kv_mul; hh += AD_THREADS / 32) {
+      float sv[2];
+      float mx = -INFINITY;
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const uint32_t p = lane + 32 * u;
+        float v = -INFINITY;
+        if (p < tn) {
+          const float* b = sp4 + hh * AD_TILE + p;
+          v = __fmul_rn(b[0] + b[AT_MAXKV * AD_TILE] + b[2 * AT_MAXKV * AD_TILE] + b[3 * AT_MAXKV * AD_TILE],
+                        a.scale);
+        }
+        sv[u] = v;
+        mx = fmaxf(mx, v);
+      }
+      mx = warp_max(mx);
+      const float m_old = ms[hh];
+      const float m_new = fmaxf(m_old, mx);
+      float sum = 0.0f;
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const uint32_t p = lane + 32 * u;
+        const float e = p < tn ? expf(sv[u] - m_new) : 0.0f;
+        pt[p * AT_MAXKV + hh] = e;
+        sum += e;
+      }
+      sum = warp_sum(sum);
+      if (lane == 0) {
+        const float cf = expf(m_old - m_new);
+        cr[hh] = cf;
+        ls[hh] = ls[hh] * cf + sum;
+        ms[hh] = m_new;
+      }
+    }
+    __syncthreads();
+    // P.V (forward.rs:368-399): thread (dim d, position group g), all heads
+    {
+      constexpr int PPG = AD_TILE / Lo::NPH;
+      const uint32_t d = tid % HD, g = tid / HD;
+      float acc[AT_MAXKV];
+#pragma unroll
+      for (int h = 0; h < AT_MAXKV; ++h) acc[h] = 0.0f;
+      const uint32_t pe = min(tn, (g + 1) * PPG);
+      for (uint32_t pp = g * PPG; pp < pe; ++pp) {
+        const float v = Vs[pp * Lo::ROW + d];
+        const float4 pa = *reinterpret_cast<const float4*>(pt + pp * AT_MAXKV);
+        const float4 pb = *reinterpret_cast<const float4*>(pt + pp * AT_MAXKV + 4);
+        acc[0] = fmaf(pa.x, v, acc[0]);
+        acc[1] = fmaf(pa.y, v, acc[1]);
+        acc[2] = fmaf(pa.z, v, acc[2]);
+        acc[3] = fmaf(pa.w, v, acc[3]);
+        acc[4] = fmaf(pb.x, v, acc[4]);
+        acc[5] = fmaf(pb.y, v, acc[5]);
+        acc[6] = fmaf(pb.z, v, acc[6]);
+        acc[7] = fmaf(pb.w, v, acc[7]);
+      }
+#pragma unroll
+      for (int h = 0; h < AT_MAXKV; ++h)
+        if (h < (int)kv_mul) po[(g * AT_MAXKV + h) * HD + d] = acc[h];
+    }
+    __syncthreads();
+    for (uint32_t i = tid; i < kv_mul * HD; i += AD_THREADS) {
+      const uint32_t hh = i / HD, d = i % HD;
+      float o = os[hh * HD + d] * cr[hh];
+#pragma unroll
+      for (int g = 0; g < Lo::NPH; ++g) o += po[(g * AT_MAXKV + hh) * HD + d];
+      os[hh * HD + d] = o;
+    }
     __syncthreads();
   }
-  if (threadIdx.x == 0) a.count[kvh] = 0u;
+
+  // every split's partial is in its CTA's shared memory
+  cluster.sync();
+  // merge: warp `warp` of CTA `rank` takes 32-blocks rank + cs*warp + ...;
+  // block b covers elements [32b, 32b+32) of the KV head's kv_mul*HD outputs
+  const uint32_t nblk = kv_mul * HD / 32;
+  for (uint32_t b = rank + cs * warp; b < nblk; b += cs * (AD_THREADS / 32)) {
+    const uint32_t hh = (b * 32) / HD, d = (b * 32) % HD + lane;
+    float m[AD_MAXCS], l[AD_MAXCS], o[AD_MAXCS];
+#pragma unroll
+    for (int s = 0; s < AD_MAXCS; ++s) {
+      if (s >= (int)cs) break;
+      const float* peer = cluster.map_shared_rank(sm, (unsigned)s);
+      m[s] = peer[Lo::STAT + hh];
+      l[s] = peer[Lo::STAT + AT_MAXKV + hh];
+      o[s] = peer[Lo::OS + hh * HD + d];
+    }
+    float M = -INFINITY;
+#pragma unroll
+    for (int s = 0; s < AD_MAXCS; ++s)
+      if (s < (int)cs) M = fmaxf(M, m[s]);
+    float L = 0.0f, acc = 0.0f;
+#pragma unroll
+    for (int s = 0; s < AD_MAXCS; ++s) {
+      if (s >= (int)cs) break;
+      const float w = m[s] == -INFINITY ? 0.0f : expf(m[s] - M);
+      L = fmaf(l[s], w, L);
+      acc = fmaf(o[s], w, acc);
+    }
+    const float v = L > 0.0f ? __fdiv_rn(acc, L) : 0.0f;
+    const uint64_t k = (uint64_t)kvh * kv_mul * HD + b * 32 + lane;
+    if (a.out) a.out[k] = v;
+    if (a.q8) {
+      float sc;
+      const int8_t qv = quant_q8_lane(v, &sc);
+      a.q8[k] = qv;
+      if (lane == 0) a.s8[k / 32] = sc;
+    }
+  }
+  // peers may still be reading this CTA's shared memory
+  cluster.sync();
+}
+
+template <int HD>
+static cudaError_t decode_config(uint32_t n_kv_heads, uint32_t cs, cudaStream_t st, bool pdl, cudaLaunchConfig_t& cfg,
+                                 cudaLaunchAttribute (&attr)[2]) {
+  const uint32_t smem = AdLayout<HD>::TOTAL * sizeof(float);
+  cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(attn_decode_kernel<HD>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  if (e != cudaSuccess) return e;
+  cfg = {};
+  cfg.gridDim = dim3(n_kv_heads * cs);
+  cfg.blockDim = dim3(AD_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cs;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 2 : 1;
+  return cudaSuccess;
+}
+
+uint32_t attention_decode_splits(uint32_t n_kv_heads, uint32_t head_size) {
+  for (uint32_t cs : {16u, 8u}) {
+    cudaLaunchConfig_t cfg;
+    cudaLaunchAttribute attr[2];
+    int n = 0;
+    cudaError_t e = head_size == 64 ? decode_config<64>(n_kv_heads, cs, nullptr, false, cfg, attr)
+                                    : decode_config<128>(n_kv_heads, cs, nullptr, false, cfg, attr);
+    if (e == cudaSuccess)
+      e = head_size == 64 ? cudaOccupancyMaxActiveClusters(&n, attn_decode_kernel<64>, &cfg)
+                          : cudaOccupancyMaxActiveClusters(&n, attn_decode_kernel<128>, &cfg);
+    if (e != cudaSuccess) (void)cudaGetLastError();
+    if (e == cudaSuccess && n >= (int)n_kv_heads) return cs;
+  }
+  return 8;
 }
 
 cudaError_t attention_decode(const AttnDecodeArgs& a, const LaunchCfg& lc) {
-  const uint32_t kv_mul = a.n_heads / a.n_kv_heads;
-  if (kv_mul > AT_MAXKV || a.n_splits == 0 || a.n_splits > 64) return cudaErrorInvalidValue;
-  dim3 g(a.n_kv_heads, a.n_splits);
-  if (a.head_size == 64) return launch_kernel(attn_decode_kernel<64>, g, dim3(AT_THREADS), 0, lc, a);
-  if (a.head_size == 128) return launch_kernel(attn_decode_kernel<128>, g, dim3(AT_THREADS), 0, lc, a);
+  const uint32_t kv_mul = a.n_kv_heads ? a.n_heads / a.n_kv_heads : 0;
+  if (kv_mul == 0 || kv_mul > AT_MAXKV || a.n_splits == 0 || a.n_splits > AD_MAXCS) return cudaErrorInvalidValue;
+  if (a.kv_dim % 4 || ((uintptr_t)a.kcache | (uintptr_t)a.vcache) % 16) return cudaErrorInvalidValue;
+  cudaLaunchConfig_t cfg;
+  cudaLaunchAttribute attr[2];
+  cudaError_t e;
+  if (a.head_size == 64) {
+    if ((e = decode_config<64>(a.n_kv_heads, a.n_splits, lc.stream, lc.pdl, cfg, attr)) != cudaSuccess) return e;
+    return cudaLaunchKernelEx(&cfg, attn_decode_kernel<64>, a);
+  }
+  if (a.head_size == 128) {
+    if ((e = decode_config<128>(a.n_kv_heads, a.n_splits, lc.stream, lc.pdl, cfg, attr)) != cudaSuccess) return e;
+    return cudaLaunchKernelEx(&cfg, attn_decode_kernel<128>, a);
+  }
   return cudaErrorInvalidValue;
 }
 

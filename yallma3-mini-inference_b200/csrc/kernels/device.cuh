@@ -57,15 +57,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait: gives up after `limit_ns` and records ERR_WAIT_TIMEOUT.
-// Returns false on timeout so the caller can stop issuing work.
+// Bounded wait: gives up after `limit_cycles` SM clock cycles (4e9 is about
+// 2 s at the 1.965 GHz boost clock, longer at lower clocks) and records
+// ERR_WAIT_TIMEOUT. The SM cycle counter is used because it advances with the
+// SM itself, whatever else observes the GPU. Returns false on timeout so the
+// caller can stop issuing work.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err,
-                                          uint64_t limit_ns = 2000000000ull) {
+                                          uint64_t limit_cycles = 4000000000ull) {
   if (mbar_try_wait(bar, parity)) return true;
-  uint64_t t0 = global_ns();
+  const uint64_t t0 = clock64();
   for (uint32_t it = 0;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 255u) == 255u && global_ns() - t0 > limit_ns) {
+    if ((it & 255u) == 255u && (uint64_t)(clock64() - t0) > limit_cycles) {
       if (err) atomicExch(err, ERR_WAIT_TIMEOUT);
       return false;
     }

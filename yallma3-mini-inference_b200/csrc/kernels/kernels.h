@@ -10,15 +10,22 @@
 namespace yl {
 namespace k {
 
-enum Fmt : int { FMT_Q8 = 0, FMT_Q4 = 1, FMT_F16 = 2, FMT_Q8F = 3, FMT_Q4F = 4 };
+// FMT_Q8X: Q8_0 weights against f32 activations held as three int8 limbs per
+// 32-block, y = s * (a + b/254 + c/254^2) (|error| <= s/2/254^2, about 6e-8 of
+// the block's absmax), so the f32-activation lm_head runs on dp4a.
+enum Fmt : int { FMT_Q8 = 0, FMT_Q4 = 1, FMT_F16 = 2, FMT_Q8F = 3, FMT_Q4F = 4, FMT_Q8X = 5 };
 // EPI_SWIGLU_Q8: SwiGLU on (gate, up) row pairs, f32 h stored and h quantized
-// to Q8_0 blocks (for the next matvec). EPI_ARGMAX: store + greedy id over
-// all rows (last CTA to finish reduces the per-CTA winners).
+// to Q8_0 blocks (for the next matvec); a block straddling two CTAs is
+// quantized by whichever finishes it last (per-block arrival counters).
+// EPI_ARGMAX: store + greedy id over all rows (last CTA to finish reduces the
+// per-CTA winners).
 enum Epi : int { EPI_STORE = 0, EPI_ADD = 1, EPI_QUIRK = 2, EPI_SWIGLU = 3, EPI_SWIGLU_Q8 = 4, EPI_ARGMAX = 5 };
 // Activation prologue: PRO_LOAD reads prepared activations; PRO_NORM computes
 // RMSNorm of the f32 residual rows (util.rs:389-426) and quantizes them
 // (quantization.rs:29-52) into shared memory (f32 for f32-activation formats).
-enum Pro : int { PRO_LOAD = 0, PRO_NORM = 1 };
+// PRO_QUANT quantizes f32 rows (xres) without a norm (the SwiGLU output h
+// feeding the down projection).
+enum Pro : int { PRO_LOAD = 0, PRO_NORM = 1, PRO_QUANT = 2 };
 
 struct StepState;
 
@@ -67,9 +74,11 @@ struct MvArgs {
   const float* xres;
   const float* norm_w;
   float eps;
-  // EPI_SWIGLU_Q8: quantized h [ntok][rows/2] + scales [ntok][rows/64]
+  // EPI_SWIGLU_Q8: quantized h [ntok][rows/2] + scales [ntok][rows/64], and
+  // one arrival counter per (token, block), zero between launches
   int8_t* hq;
   float* hs;
+  unsigned int* hcount;
   // EPI_ARGMAX: per-CTA winners, arrival counter (zero between launches),
   // output id slot (hist[state->steps] or hist[0]) and the step state
   float* am_val;
@@ -136,9 +145,10 @@ cudaError_t attention(const AttnArgs& a, const LaunchCfg& lc);
 
 // Batch-1 decode attention with RoPE and the KV-cache write fused in:
 // q and the new k/v rows are taken unrotated from `qkv` ([att | k | v]),
-// rotated with cs[pos], the new k/v rows written at `pos`, then the split
-// partials are merged by the last CTA of each KV head (arrival counters in
-// `count`, zero between launches), which also quantizes the output.
+// rotated with cs[pos], the new k/v rows written at `pos`. One thread-block
+// cluster of n_splits CTAs per KV head splits the keys; the splits' partials
+// are merged through distributed shared memory, and the output is quantized
+// per 32-block in the same kernel.
 struct AttnDecodeArgs {
   const float* qkv;
   const float2* cs;  // [ctx][head_size/2]
@@ -149,13 +159,17 @@ struct AttnDecodeArgs {
   const StepState* state;
   uint32_t pos0;
   float scale;
-  uint32_t n_splits;
-  float* part;            // [n_heads][n_splits][head_size + 2]
-  unsigned int* count;    // [n_kv_heads]
+  uint32_t n_splits;      // cluster size, 1..16
+  // Cache rows below pos were written by work that completed before the
+  // preceding kernel started (a graph replay): fetch them before waiting.
+  int early_kv;
   float* out;             // [n_heads*head_size] f32 (nullable)
   int8_t* q8;             // (nullable)
   float* s8;
 };
+// Cluster size for the decode attention: 16 when n_kv_heads clusters of 16
+// can be resident at once, else 8.
+uint32_t attention_decode_splits(uint32_t n_kv_heads, uint32_t head_size);
 cudaError_t attention_decode(const AttnDecodeArgs& a, const LaunchCfg& lc);
 
 // Greedy argmax over n logits (sampler.rs:67-79: the lowest index among equal

@@ -50,8 +50,11 @@ struct MvLayout {
   uint32_t bar_off, red_off, x_off, xs_off, xsum_off, ring_off;
   uint32_t stage_q_row, stage_s_row, stage_bytes, total;
 };
+// ssz: weight scale element size (2 for f16, 4 for f32). A stage's scale row
+// is the chunk's scales padded to 16 bytes, which for a full-row chunk equals
+// the HBM scale row stride, so full-row stages are single contiguous copies.
 template <int FMT, int NT>
-__host__ __device__ inline MvLayout mv_layout(uint32_t K, uint32_t kc, int rpw, int stages) {
+__host__ __device__ inline MvLayout mv_layout(uint32_t K, uint32_t kc, int rpw, int stages, uint32_t ssz = 4) {
   MvLayout L;
   L.bar_off = 0;       // 2 x 8 mbarriers
   L.red_off = 128;     // reductions / argmax / h staging ([2][8][32] floats)
@@ -61,7 +64,9 @@ __host__ __device__ inline MvLayout mv_layout(uint32_t K, uint32_t kc, int rpw, 
     off += NT * K * 4;
     L.xs_off = L.xsum_off = off;
   } else {
-    off += NT * K;  // int8 activations (Q4: split lo/hi halves per block)
+    // int8 activations (Q4: split lo/hi halves per block; Q8X: three limb
+    // arrays of NT*K bytes each)
+    off += (FMT == FMT_Q8X ? 3 : 1) * NT * K;
     off = (off + 15) & ~15u;
     L.xs_off = off;
     off += NT * (K / 32) * 4;
@@ -71,7 +76,7 @@ __host__ __device__ inline MvLayout mv_layout(uint32_t K, uint32_t kc, int rpw, 
   off = (off + 127) & ~127u;
   L.ring_off = off;
   L.stage_q_row = mv_qbytes<FMT>(kc);
-  L.stage_s_row = mv_has_scales<FMT>() ? kc / 32 * 4 : 0;  // room for f32 scales
+  L.stage_s_row = mv_has_scales<FMT>() ? ((kc / 32 * ssz + 15u) & ~15u) : 0;
   L.stage_bytes = (uint32_t)(MV_NCW * rpw) * (L.stage_q_row + L.stage_s_row);
   L.total = off + stages * L.stage_bytes;
   return L;
@@ -104,6 +109,131 @@ __device__ __forceinline__ bool am_better(float v, uint32_t i, float bv, uint32_
 }
 
 // ---------------------------------------------------------------------------
+// RMSNorm + quantize prologue with the row held in registers (K <= 8192):
+// thread ctid owns float4 i = 4*ctid + 1024*u, so every x and norm-weight load
+// is issued in one round trip, and a 32-element block sits in 8 lanes x 4
+// values (its absmax is an 8-lane reduction). Same sum-of-squares order as
+// rmsnorm_quant_kernel and the same per-element operations as
+// quant_q8_lane, so the bits equal the standalone kernels'.
+// NORM = false: the rows are quantized as they are (y = x, PRO_QUANT).
+constexpr int MV_NORM_MU = 8;    // float4 per thread with a norm (K <= 8192)
+constexpr int MV_QUANT_MU = 16;  // float4 per thread without (K <= 16384)
+template <int FMT, int NT, bool NORM, int MU>
+__device__ __forceinline__ void mv_norm_regs(const MvArgs& a, const MvLayout& L, uint8_t* smem, int cw, int lane) {
+  using namespace yl::dev;
+  const uint32_t K = a.K, nb = K / 32;
+  const int ctid = cw * 32 + lane;
+  float* red = reinterpret_cast<float*>(smem + L.red_off);
+  for (int t = 0; t < NT; ++t) {
+    const bool valid = t < (int)a.ntok;
+    const float* xr = a.xres + (uint64_t)t * a.x_tok_stride;
+    float4 xv[MU], wv[NORM ? MU : 1];
+#pragma unroll
+    for (int u = 0; u < MU; ++u) {
+      const uint32_t i = ctid * 4 + u * MV_NCW * 32 * 4;
+      const bool in = valid && i < K;
+      xv[u] = in ? *reinterpret_cast<const float4*>(xr + i) : make_float4(0, 0, 0, 0);
+      if (NORM) wv[u] = in ? *reinterpret_cast<const float4*>(a.norm_w + i) : make_float4(0, 0, 0, 0);
+    }
+    float r = 1.0f;
+    if (NORM) {
+      float ss = 0.0f;
+#pragma unroll
+      for (int u = 0; u < MU; ++u) {
+        ss = fmaf(xv[u].x, xv[u].x, ss);
+        ss = fmaf(xv[u].y, xv[u].y, ss);
+        ss = fmaf(xv[u].z, xv[u].z, ss);
+        ss = fmaf(xv[u].w, xv[u].w, ss);
+      }
+      ss = warp_sum(ss);
+      if (lane == 0) red[cw] = ss;
+      named_bar_sync(1, MV_NCW * 32);
+      float tot = 0.0f;
+#pragma unroll
+      for (int i = 0; i < MV_NCW; ++i) tot += red[i];
+      r = __fdiv_rn(tot, (float)K);
+      r = __fadd_rn(r, a.eps);
+      r = __fdiv_rn(1.0f, __fsqrt_rn(r));
+      named_bar_sync(1, MV_NCW * 32);  // red[] reused by the next token
+    }
+#pragma unroll
+    for (int u = 0; u < MU; ++u) {
+      const uint32_t i = ctid * 4 + u * MV_NCW * 32 * 4;
+      if (u * MV_NCW * 32 * 4 >= K) break;  // uniform across the CTA
+      const bool in = i < K;
+      float y[4];
+      if (NORM) {
+        y[0] = __fmul_rn(wv[u].x, __fmul_rn(r, xv[u].x));
+        y[1] = __fmul_rn(wv[u].y, __fmul_rn(r, xv[u].y));
+        y[2] = __fmul_rn(wv[u].z, __fmul_rn(r, xv[u].z));
+        y[3] = __fmul_rn(wv[u].w, __fmul_rn(r, xv[u].w));
+      } else {
+        y[0] = xv[u].x;
+        y[1] = xv[u].y;
+        y[2] = xv[u].z;
+        y[3] = xv[u].w;
+      }
+      if (mv_f32_act<FMT>()) {
+        if (in) *reinterpret_cast<float4*>(reinterpret_cast<float*>(smem + L.x_off) + t * K + i) =
+            make_float4(y[0], y[1], y[2], y[3]);
+        continue;
+      }
+      // quantization.rs:29-52 over the block held by lanes 8g..8g+7
+      float m = 0.0f;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float av = fabsf(y[e]);
+        m = fmaxf(m, av > 0.0f ? av : 0.0f);  // NaN never becomes the max
+      }
+      m = fmaxf(m, __shfl_xor_sync(FULL, m, 4));
+      m = fmaxf(m, __shfl_xor_sync(FULL, m, 2));
+      m = fmaxf(m, __shfl_xor_sync(FULL, m, 1));
+      const float sc = __fdiv_rn(m, 127.0f);
+      uint32_t word = 0;
+      int qs = 0;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int8_t q = rust_as_i8(roundf(__fdiv_rn(y[e], sc)));
+        word |= (uint32_t)(uint8_t)q << (8 * e);
+        qs += q;
+      }
+      const uint32_t b = i / 32, e0 = i % 32;  // block and first element within it
+      int8_t* xq = reinterpret_cast<int8_t*>(smem + L.x_off) + t * K;
+      if (FMT == FMT_Q4) {
+        qs += __shfl_xor_sync(FULL, qs, 4);
+        qs += __shfl_xor_sync(FULL, qs, 2);
+        qs += __shfl_xor_sync(FULL, qs, 1);
+        const uint32_t off = e0 < 16 ? b * 16 + e0 : nb * 16 + b * 16 + (e0 - 16);
+        if (in) *reinterpret_cast<uint32_t*>(xq + off) = word;
+        if (in && e0 == 0) reinterpret_cast<int*>(smem + L.xsum_off)[t * nb + b] = qs;
+      } else if (FMT == FMT_Q8X) {
+        // limbs 1 and 2 refine the Q8_0 value a: y - s*a = (s/254)*b + (s/254^2)*c + e
+        const float inv = __fdiv_rn(254.0f, sc);  // +inf for an all-zero block: limbs become 0
+        const float s1 = sc * (1.0f / 254.0f);
+        uint32_t w1 = 0, w2 = 0;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int8_t q0 = (int8_t)(word >> (8 * e));
+          const float r1 = fmaf(-(float)q0, sc, y[e]);
+          const int8_t q1 = rust_as_i8(roundf(r1 * inv));
+          const float r2 = fmaf(-(float)q1, s1, r1);
+          const int8_t q2 = rust_as_i8(roundf(r2 * inv * 254.0f));
+          w1 |= (uint32_t)(uint8_t)q1 << (8 * e);
+          w2 |= (uint32_t)(uint8_t)q2 << (8 * e);
+        }
+        if (in) {
+          *reinterpret_cast<uint32_t*>(xq + i) = word;
+          *reinterpret_cast<uint32_t*>(xq + NT * K + i) = w1;
+          *reinterpret_cast<uint32_t*>(xq + 2 * NT * K + i) = w2;
+        }
+      } else {
+        if (in) *reinterpret_cast<uint32_t*>(xq + i) = word;
+      }
+      if (in && e0 == 0) reinterpret_cast<float*>(smem + L.xs_off)[t * nb + b] = sc;
+    }
+  }
+}
+
 // Prologue: stage the activations of NT tokens into shared memory.
 template <int FMT, int NT>
 __device__ __forceinline__ void mv_stage_x(const MvArgs& a, const MvLayout& L, uint8_t* smem, int cw, int lane) {
@@ -111,6 +241,14 @@ __device__ __forceinline__ void mv_stage_x(const MvArgs& a, const MvLayout& L, u
   const uint32_t K = a.K, nb = K / 32;
   const int ctid = cw * 32 + lane;
   float* red = reinterpret_cast<float*>(smem + L.red_off);
+  if (a.pro == PRO_NORM && K <= MV_NORM_MU * MV_NCW * 32 * 4) {
+    mv_norm_regs<FMT, NT, true, MV_NORM_MU>(a, L, smem, cw, lane);
+    return;
+  }
+  if (a.pro == PRO_QUANT) {  // host guarantees K <= MV_QUANT_MU * 1024
+    mv_norm_regs<FMT, NT, false, MV_QUANT_MU>(a, L, smem, cw, lane);
+    return;
+  }
   if (a.pro == PRO_NORM) {
     for (int t = 0; t < NT; ++t) {
       const bool valid = t < (int)a.ntok;
@@ -324,6 +462,10 @@ __device__ __forceinline__ void mv_row_chunk(const uint8_t* wrow, const uint8_t*
         v[u] = c < nck;
         w[u] = v[u] ? *reinterpret_cast<const int4*>(wrow + 16 * c) : make_int4(0, 0, 0, 0);
       }
+      // A lane's 8 activations are two float4 at a 32-byte lane stride; lanes
+      // with bit 2 set read the halves in swapped order, which spreads every
+      // shared load over all banks (4 wavefronts per 512 bytes, the minimum).
+      const int rot = (lane >> 2) & 1;
 #pragma unroll
       for (int u = 0; u < 2; ++u) {
         if (!v[u]) continue;
@@ -338,18 +480,65 @@ __device__ __forceinline__ void mv_row_chunk(const uint8_t* wrow, const uint8_t*
         }
 #pragma unroll
         for (int t = 0; t < NT; ++t) {
-          const float4 x0 = *reinterpret_cast<const float4*>(xf + t * K + k0 + 8 * c);
-          const float4 x1 = *reinterpret_cast<const float4*>(xf + t * K + k0 + 8 * c + 4);
           float s = acc[t];
-          s = __fadd_rn(s, __fmul_rn(x0.x, wf[0]));
-          s = __fadd_rn(s, __fmul_rn(x0.y, wf[1]));
-          s = __fadd_rn(s, __fmul_rn(x0.z, wf[2]));
-          s = __fadd_rn(s, __fmul_rn(x0.w, wf[3]));
-          s = __fadd_rn(s, __fmul_rn(x1.x, wf[4]));
-          s = __fadd_rn(s, __fmul_rn(x1.y, wf[5]));
-          s = __fadd_rn(s, __fmul_rn(x1.z, wf[6]));
-          s = __fadd_rn(s, __fmul_rn(x1.w, wf[7]));
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const int p = (j + rot) & 1;
+            const float4 x = *reinterpret_cast<const float4*>(xf + t * K + k0 + 8 * c + 4 * p);
+            const float w0 = p ? wf[4] : wf[0], w1 = p ? wf[5] : wf[1];
+            const float w2 = p ? wf[6] : wf[2], w3 = p ? wf[7] : wf[3];
+            s = __fadd_rn(s, __fmul_rn(x.x, w0));
+            s = __fadd_rn(s, __fmul_rn(x.y, w1));
+            s = __fadd_rn(s, __fmul_rn(x.z, w2));
+            s = __fadd_rn(s, __fmul_rn(x.w, w3));
+          }
           acc[t] = s;
+        }
+      }
+    }
+  } else if (FMT == FMT_Q8X) {  // Q8_0 weights, three-limb int8 activations (lm_head)
+    const int8_t* xq = reinterpret_cast<const int8_t*>(smem + L.x_off);
+    const float* xs = reinterpret_cast<const float*>(smem + L.xs_off);
+    const uint32_t nck = kn / 16;  // 16-byte chunks, two per block
+    for (uint32_t c0 = 0; c0 < nck; c0 += 32 * 2) {
+      int4 w[2];
+      float wsc[2];
+      bool v[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const uint32_t c = c0 + u * 32 + lane;
+        v[u] = c < nck;
+        w[u] = v[u] ? *reinterpret_cast<const int4*>(wrow + 16 * c) : make_int4(0, 0, 0, 0);
+        wsc[u] = v[u] ? ld_scale<SF16>(srow, c >> 1) : 0.0f;
+      }
+#pragma unroll
+      for (int t = 0; t < NT; ++t) {
+        int s[2][3];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const uint32_t c = c0 + u * 32 + lane;
+#pragma unroll
+          for (int l = 0; l < 3; ++l) {
+            const int4 x = v[u] ? *reinterpret_cast<const int4*>(xq + l * NT * K + t * K + k0 + 16 * c)
+                                : make_int4(0, 0, 0, 0);
+            int d = dp4a(w[u].x, x.x, 0);
+            d = dp4a(w[u].y, x.y, d);
+            d = dp4a(w[u].z, x.z, d);
+            s[u][l] = dp4a(w[u].w, x.w, d);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 2; ++u)
+#pragma unroll
+          for (int l = 0; l < 3; ++l) s[u][l] += __shfl_xor_sync(FULL, s[u][l], 1);  // whole-block sums
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const uint32_t c = c0 + u * 32 + lane;
+          if (v[u] && !(lane & 1)) {
+            // sum_k w*y over the block = s * (A + (B + C/254)/254)
+            const float blk = (float)s[u][0] + ((float)s[u][1] + (float)s[u][2] * (1.0f / 254.0f)) * (1.0f / 254.0f);
+            acc[t] = fmaf(blk * wsc[u], xs[t * (K / 32) + (k0 >> 5) + (c >> 1)], acc[t]);
+          }
         }
       }
     }
@@ -375,13 +564,19 @@ __device__ __forceinline__ void mv_row_chunk(const uint8_t* wrow, const uint8_t*
           const uint32_t c = c0 + u * 32 + lane;
           s[u] = 0.0f;
           if (v[u]) {
+            // 16 activations per lane are four float4 at a 64-byte lane
+            // stride; rotating the order by lane pair spreads each shared
+            // load over all banks (4 wavefronts per 512 bytes, the minimum)
             const float4* xp = reinterpret_cast<const float4*>(xf + t * K + k0 + 16 * c);
-            const uint32_t wv[4] = {(uint32_t)w[u].x, (uint32_t)w[u].y, (uint32_t)w[u].z, (uint32_t)w[u].w};
+            const int rot = (lane >> 1) & 3;
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-              const float4 x = xp[j];
+              const int p = (j + rot) & 3;
+              const float4 x = xp[p];
+              const uint32_t ww = p == 0 ? (uint32_t)w[u].x
+                                         : p == 1 ? (uint32_t)w[u].y : p == 2 ? (uint32_t)w[u].z : (uint32_t)w[u].w;
               float f0, f1, f2, f3;
-              i8x4_to_f32(wv[j], f0, f1, f2, f3);
+              i8x4_to_f32(ww, f0, f1, f2, f3);
               s[u] = fmaf(x.x, f0, s[u]);
               s[u] = fmaf(x.y, f1, s[u]);
               s[u] = fmaf(x.z, f2, s[u]);
@@ -399,18 +594,33 @@ __device__ __forceinline__ void mv_row_chunk(const uint8_t* wrow, const uint8_t*
   } else {  // FMT_Q4F
     const float* xf = reinterpret_cast<const float*>(smem + L.x_off);
     const uint32_t nbk = kn / 32;
+    // A lane's block is 32 activations (eight float4 at a 128-byte lane
+    // stride); lane-rotated order keeps every shared load conflict-free.
+    const int rot = lane & 7;
     for (uint32_t b = lane; b < nbk; b += 32) {
       const int4 w = *reinterpret_cast<const int4*>(wrow + 16 * b);
       const float wsc = ld_scale<SF16>(srow, b);
-      const uint8_t* wb = reinterpret_cast<const uint8_t*>(&w);
 #pragma unroll
       for (int t = 0; t < NT; ++t) {
-        const float* xp = xf + t * K + k0 + 32 * b;
+        const float4* xp = reinterpret_cast<const float4*>(xf + t * K + k0 + 32 * b);
         float s = 0.0f;
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          s = fmaf(xp[j], (float)((int)(wb[j] & 0xF) - 8), s);
-          s = fmaf(xp[j + 16], (float)((int)(wb[j] >> 4) - 8), s);
+        for (int j = 0; j < 8; ++j) {
+          const int p = (j + rot) & 7;  // elements 4p..4p+3 of the block
+          const float4 x = xp[p];
+          const int wi = p & 3;
+          const uint32_t word = wi == 0 ? (uint32_t)w.x : wi == 1 ? (uint32_t)w.y : wi == 2 ? (uint32_t)w.z : (uint32_t)w.w;
+          // elements 0..15: low nibbles of bytes 0..15; 16..31: high nibbles
+          const uint32_t nib = (p >> 2) ? (word >> 4) & 0x0F0F0F0Fu : word & 0x0F0F0F0Fu;
+          // 2^23 + q as a float, minus 2^23 + 8: the exact value q - 8
+          const float f0 = __uint_as_float(__byte_perm(nib, 0x4B000000u, 0x7650)) - 8388616.0f;
+          const float f1 = __uint_as_float(__byte_perm(nib, 0x4B000000u, 0x7651)) - 8388616.0f;
+          const float f2 = __uint_as_float(__byte_perm(nib, 0x4B000000u, 0x7652)) - 8388616.0f;
+          const float f3 = __uint_as_float(__byte_perm(nib, 0x4B000000u, 0x7653)) - 8388616.0f;
+          s = fmaf(x.x, f0, s);
+          s = fmaf(x.y, f1, s);
+          s = fmaf(x.z, f2, s);
+          s = fmaf(x.w, f3, s);
         }
         acc[t] = fmaf(s, wsc, acc[t]);
       }
@@ -419,20 +629,21 @@ __device__ __forceinline__ void mv_row_chunk(const uint8_t* wrow, const uint8_t*
 }
 
 // ---------------------------------------------------------------------------
+// Batch-1/2 passes are capped at 112 registers so that two CTAs (2 x 288
+// threads) share an SM; larger token groups keep their accumulators unspilled.
 template <int FMT, int NT, int EPI, bool SF16, int RPW>
-__global__ void __launch_bounds__(MV_THREADS, 1) mv_kernel(MvArgs a) {
+__global__ void __launch_bounds__(MV_THREADS, (NT <= 2 ? 2 : 1)) mv_kernel(MvArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   using namespace yl::dev;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t K = a.K, kc = a.kc;
   const int S = a.stages;
-  const MvLayout L = mv_layout<FMT, NT>(K, kc, RPW, S);
+  const MvLayout L = mv_layout<FMT, NT>(K, kc, RPW, S, SF16 ? 2u : 4u);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar_off);
   uint64_t* empty = full + S;
 
-  // Row range of this CTA: row pairs for SwiGLU (gate/up together), 64-row
-  // units when h is quantized here (32 pairs = one Q8_0 block of h).
-  const uint32_t unit = EPI == EPI_SWIGLU_Q8 ? 64u : (EPI == EPI_SWIGLU ? 2u : 1u);
+  // Row range of this CTA: row pairs for SwiGLU (gate/up together).
+  const uint32_t unit = mv_swiglu(EPI) ? 2u : 1u;
   const uint64_t units = a.rows / unit;
   const uint32_t r_begin = (uint32_t)(units * blockIdx.x / gridDim.x) * unit;
   const uint32_t r_end = (uint32_t)(units * (blockIdx.x + 1) / gridDim.x) * unit;
@@ -455,6 +666,10 @@ __global__ void __launch_bounds__(MV_THREADS, 1) mv_kernel(MvArgs a) {
     // ---------------- producer ----------------
     if (lane == 0) {
       const uint64_t pol = l2_evict_first_policy();
+      // One chunk per row whose shared-memory strides equal the HBM strides:
+      // a stage's rows are then one contiguous range in both places.
+      const bool contig = nch == 1 && L.stage_q_row == a.row_bytes &&
+                          (!mv_has_scales<FMT>() || L.stage_s_row == a.scale_row_bytes);
       uint32_t issued = 0;
       for (uint32_t it = 0; it < n_it; ++it) {
         const int slot = it % S;
@@ -469,6 +684,13 @@ __global__ void __launch_bounds__(MV_THREADS, 1) mv_kernel(MvArgs a) {
         const uint32_t sb = mv_has_scales<FMT>() ? ((kn / 32 * ssz + 15u) & ~15u) : 0u;
         uint8_t* stage = smem + L.ring_off + slot * L.stage_bytes;
         mbar_arrive_expect_tx(&full[slot], nrows * (qb + sb));
+        if (contig) {  // full rows: one copy for the quants, one for the scales
+          bulk_g2s(stage, a.wq + (uint64_t)row0 * a.row_bytes, nrows * qb, &full[slot], pol);
+          if (sb) bulk_g2s(stage + RS * L.stage_q_row, a.ws + (uint64_t)row0 * a.scale_row_bytes, nrows * sb,
+                           &full[slot], pol);
+          issued = it + 1;
+          continue;
+        }
         for (uint32_t r = 0; r < nrows; ++r) {
           const uint64_t row = row0 + r;
           bulk_g2s(stage + r * L.stage_q_row, a.wq + row * a.row_bytes + mv_qbytes<FMT>(k0), qb, &full[slot], pol);
@@ -500,7 +722,6 @@ __global__ void __launch_bounds__(MV_THREADS, 1) mv_kernel(MvArgs a) {
     for (int t = 0; t < NT; ++t) acc[r][t] = 0.0f;
   float am_v = -INFINITY;  // EPI_ARGMAX: this warp's best (lane 0)
   uint32_t am_i = 0xFFFFFFFFu;
-  float* hbuf = reinterpret_cast<float*>(smem + L.red_off);  // EPI_SWIGLU_Q8: [2][NT][32]
 
   // After a wait timeout the warp stops waiting and computing ("dead") but
   // keeps walking the loop so every named barrier below is still reached.
@@ -540,28 +761,6 @@ __global__ void __launch_bounds__(MV_THREADS, 1) mv_kernel(MvArgs a) {
         for (int t = 0; t < NT; ++t)
           if (t < (int)a.ntok) a.out[(uint64_t)t * a.out_tok_stride + r / 2] = hv[t];
       }
-      if (EPI == EPI_SWIGLU_Q8) {
-        // rows [row0, row0+16) give h [row0/2, row0/2 + 8); a block of 32 h
-        // completes every 64 rows (4 row sets); double-buffered staging
-        const uint32_t j = (r - r_begin) / 2;  // h index within the CTA
-        const uint32_t blk = j / 32, jj = j % 32;
-        float* hb = hbuf + (blk & 1) * NT * 32;
-        if (lane == 0 && have)
-#pragma unroll
-          for (int t = 0; t < NT; ++t) hb[t * 32 + jj] = hv[t];
-        if (((rs + 1) * RS) % 64 == 0 || row0 + RS >= r_end) {
-          named_bar_sync(2, MV_NCW * 32);
-          const uint32_t jb = (r_begin / 2) + blk * 32;  // first h of the block
-          if (cw < NT && cw < (int)a.ntok) {
-            const int t = cw;
-            float sc;
-            const int8_t qv = quant_q8_lane(hb[t * 32 + lane], &sc);
-            const uint64_t hk = (uint64_t)t * (a.rows / 2) + jb + lane;
-            a.hq[hk] = qv;
-            if (lane == 0) a.hs[hk / 32] = sc;
-          }
-        }
-      }
     } else {
 #pragma unroll
       for (int rr = 0; rr < RPW; ++rr) {
@@ -590,6 +789,44 @@ __global__ void __launch_bounds__(MV_THREADS, 1) mv_kernel(MvArgs a) {
     for (int t = 0; t < NT; ++t)
 #pragma unroll
       for (int rr = 0; rr < RPW; ++rr) acc[rr][t] = 0.0f;
+  }
+
+  if (EPI == EPI_SWIGLU_Q8) {
+    // Quantize h (quantization.rs:29-52, forward.rs:240) once, here: this
+    // CTA's h range [j0, j1) is in global memory. Blocks of 32 inside the
+    // range are quantized now; a block shared with a neighbouring CTA is
+    // quantized by whichever CTA completes it (arrival count reaches 32).
+    __shared__ int sw_last[2];
+    const uint32_t hn = a.rows / 2, j0 = r_begin / 2, j1 = r_end / 2;
+    const uint32_t b0 = j0 / 32, b1 = (j1 + 31) / 32;  // blocks touched
+    __threadfence();
+    named_bar_sync(1, MV_NCW * 32);
+    for (int t = 0; t < (int)a.ntok && t < NT; ++t) {
+      if (cw == 0 && lane < 2) {
+        // boundary blocks: first (lane 0) and last (lane 1), when partial
+        const uint32_t b = lane == 0 ? b0 : b1 - 1;
+        const uint32_t lo = max(j0, b * 32), hi = min(j1, b * 32 + 32);
+        const bool partial = hi - lo < 32 && (lane == 0 || b1 - 1 != b0);
+        int last = 0;
+        if (partial) last = atomicAdd(a.hcount + (uint64_t)t * (hn / 32) + b, hi - lo) + (hi - lo) == 32;
+        sw_last[lane] = partial ? last : 1;
+      }
+      named_bar_sync(1, MV_NCW * 32);
+      for (uint32_t b = b0 + cw; b < b1; b += MV_NCW) {
+        const bool first = b == b0, lastb = b == b1 - 1;
+        if ((first && !sw_last[0]) || (lastb && !sw_last[1])) continue;  // a neighbour finishes it
+        if (first || lastb) __threadfence();  // see the neighbour's h values
+        const uint64_t hk = (uint64_t)t * hn + b * 32 + lane;
+        float sc;
+        const int8_t qv = quant_q8_lane(__ldcg(a.out + (uint64_t)t * a.out_tok_stride + b * 32 + lane), &sc);
+        a.hq[hk] = qv;
+        if (lane == 0) {
+          a.hs[hk / 32] = sc;
+          if (b * 32 < j0 || b * 32 + 32 > j1) a.hcount[(uint64_t)t * (hn / 32) + b] = 0u;  // for the next launch
+        }
+      }
+      named_bar_sync(1, MV_NCW * 32);
+    }
   }
 
   if (EPI == EPI_ARGMAX) {
@@ -661,13 +898,20 @@ cudaError_t mv_launch(const MvArgs& a0, int epi, const LaunchCfg& lc) {
   const int nt = a.ntok <= 1 ? 1 : a.ntok <= 2 ? 2 : a.ntok <= 4 ? 4 : 8;
   const int rpw = mv_swiglu(epi) ? 2 : 1;
   MvLayout L0;
-  switch (nt) {
-    case 1: L0 = mv_layout<FMT, 1>(a.K, a.kc, rpw, 0); break;
-    case 2: L0 = mv_layout<FMT, 2>(a.K, a.kc, rpw, 0); break;
-    case 4: L0 = mv_layout<FMT, 4>(a.K, a.kc, rpw, 0); break;
-    default: L0 = mv_layout<FMT, 8>(a.K, a.kc, rpw, 0); break;
+  int stages = 0;
+  for (;;) {
+    switch (nt) {
+      case 1: L0 = mv_layout<FMT, 1>(a.K, a.kc, rpw, 0, SF16 ? 2u : 4u); break;
+      case 2: L0 = mv_layout<FMT, 2>(a.K, a.kc, rpw, 0, SF16 ? 2u : 4u); break;
+      case 4: L0 = mv_layout<FMT, 4>(a.K, a.kc, rpw, 0, SF16 ? 2u : 4u); break;
+      default: L0 = mv_layout<FMT, 8>(a.K, a.kc, rpw, 0, SF16 ? 2u : 4u); break;
+    }
+    stages = (int)((lc.smem_budget > L0.total ? lc.smem_budget - L0.total : 0) / L0.stage_bytes);
+    // a ring of fewer than two stages inside the budget cannot overlap copy
+    // and compute (or costs the SM its second CTA): halve the chunk instead
+    if (stages >= 2 || a.kc <= 256) break;
+    a.kc = (a.kc / 2 + 255u) / 256u * 256u;
   }
-  int stages = (int)((lc.smem_budget > L0.total ? lc.smem_budget - L0.total : 0) / L0.stage_bytes);
   if (stages > 8) stages = 8;
   if (stages < 2) stages = 2;
   a.stages = stages;
@@ -675,6 +919,9 @@ cudaError_t mv_launch(const MvArgs& a0, int epi, const LaunchCfg& lc) {
   if (smem > 227u * 1024u) return cudaErrorInvalidConfiguration;
   if (epi == EPI_ARGMAX && nt != 1) return cudaErrorInvalidValue;
   if (epi == EPI_SWIGLU_Q8 && (a.rows % 64 || mv_f32_act<FMT>())) return cudaErrorInvalidValue;
+  if (a.pro == PRO_QUANT && (a.K > MV_QUANT_MU * MV_NCW * 32 * 4 || mv_f32_act<FMT>())) return cudaErrorInvalidValue;
+  // three-limb activations are produced only by the register RMSNorm prologue
+  if (FMT == FMT_Q8X && (a.pro != PRO_NORM || a.K > MV_NORM_MU * MV_NCW * 32 * 4)) return cudaErrorInvalidValue;
   void (*kern)(MvArgs) = nullptr;
 #define YL_MV_CASE(NT_, EPI_, RPW_) \
   if (nt == NT_ && epi == EPI_) kern = mv_kernel<FMT, NT_, EPI_, SF16, RPW_>;
@@ -684,18 +931,23 @@ cudaError_t mv_launch(const MvArgs& a0, int epi, const LaunchCfg& lc) {
   YL_MV_CASE(NT_, EPI_QUIRK, 1)                                 \
   if (!mv_f32_act<FMT>() || FMT == FMT_F16) { YL_MV_CASE(NT_, EPI_SWIGLU, 2) } \
   if (!mv_f32_act<FMT>()) { YL_MV_CASE(NT_, EPI_SWIGLU_Q8, 2) }
-  YL_MV_NT(1)
-  YL_MV_NT(2)
-  YL_MV_NT(4)
-  YL_MV_NT(8)
-  if (mv_f32_act<FMT>()) { YL_MV_CASE(1, EPI_ARGMAX, 1) }
+  if constexpr (FMT == FMT_Q8X) {  // the lm_head: one token, logits and argmax
+    YL_MV_CASE(1, EPI_STORE, 1)
+    YL_MV_CASE(1, EPI_ARGMAX, 1)
+  } else {
+    YL_MV_NT(1)
+    YL_MV_NT(2)
+    YL_MV_NT(4)
+    YL_MV_NT(8)
+    if (mv_f32_act<FMT>()) { YL_MV_CASE(1, EPI_ARGMAX, 1) }
+  }
 #undef YL_MV_NT
 #undef YL_MV_CASE
   if (!kern) return cudaErrorInvalidValue;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   uint32_t grid = lc.grid ? lc.grid : 148;
-  const uint32_t unit = epi == EPI_SWIGLU_Q8 ? 64 : (epi == EPI_SWIGLU ? 2 : 1);
+  const uint32_t unit = mv_swiglu(epi) ? 2 : 1;
   if (grid > a.rows / unit) grid = (uint32_t)(a.rows / unit);
   if (grid == 0) return cudaSuccess;
   return launch_kernel(kern, dim3(grid), dim3(MV_THREADS), smem, lc, a);

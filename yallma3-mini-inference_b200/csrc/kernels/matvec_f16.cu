@@ -18,10 +18,11 @@ static uint32_t max_ntok_fmt(uint32_t K, uint32_t kc, int rpw) {
 }
 
 uint32_t matvec_max_ntok(int fmt, uint32_t K, uint32_t kc, int epi) {
-  const int rpw = epi == EPI_SWIGLU ? 2 : 1;
+  const int rpw = (epi == EPI_SWIGLU || epi == EPI_SWIGLU_Q8) ? 2 : 1;
   switch (fmt) {
     case FMT_Q8: return max_ntok_fmt<FMT_Q8>(K, kc, rpw);
     case FMT_Q8F: return max_ntok_fmt<FMT_Q8F>(K, kc, rpw);
+    case FMT_Q8X: return mv_layout<FMT_Q8X, 1>(K, kc, rpw, 2).total <= 227u * 1024u ? 1 : 0;
     case FMT_Q4: return max_ntok_fmt<FMT_Q4>(K, kc, rpw);
     case FMT_Q4F: return max_ntok_fmt<FMT_Q4F>(K, kc, rpw);
     case FMT_F16: return max_ntok_fmt<FMT_F16>(K, kc, rpw);
@@ -33,7 +34,8 @@ cudaError_t matvec(const MvArgs& a, int fmt, bool sf16, int epi, const LaunchCfg
   if (a.K % 32 || a.kc % 256 || a.kc == 0 || a.ntok == 0 || a.ntok > 8) return cudaErrorInvalidValue;
   switch (fmt) {
     case FMT_Q8:
-    case FMT_Q8F: return matvec_q8(a, fmt, sf16, epi, lc);
+    case FMT_Q8F:
+    case FMT_Q8X: return matvec_q8(a, fmt, sf16, epi, lc);
     case FMT_Q4:
     case FMT_Q4F: return matvec_q4(a, fmt, sf16, epi, lc);
     case FMT_F16: return mv_launch<FMT_F16, true>(a, epi, lc);
