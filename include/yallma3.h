@@ -228,6 +228,15 @@ int yl_decode_step_launches(const yl_model* m, uint32_t* out);
  * layer qkv, attention, wo, gate/up, down, then lm_head. */
 int yl_profile_decode_step(const yl_model* m, yl_session* s, uint32_t token, uint32_t pos, float* us_out,
                            uint32_t cap, uint32_t* n_out);
+/* Diagnostic: runs one batch-1 decode step of `token` at `pos` exactly as the
+ * decode graph does (one graph, programmatic dependent launch) while every
+ * matvec and attention CTA stamps the GPU's nanosecond global timer at four
+ * points: out[launch * 4096 + cta * 4 + i], i = entry, prologue done (wait
+ * released for attention), first weight stage ready (attention: partials
+ * visible), done. Launch order as yl_profile_decode_step; the embedding launch
+ * (index 0) is not stamped. Writes up to cap values; *n_launches = launches. */
+int yl_trace_decode_step(const yl_model* m, yl_session* s, uint32_t token, uint32_t pos, uint64_t* out,
+                         uint64_t cap, uint32_t* n_launches);
 
 /* ---- reference FFI (lib.rs:135-152) -------------------------------------- */
 /* Loads into a process-global slot (guarded by a mutex here; `static mut` in

@@ -104,6 +104,7 @@ _sigs = {
     "yl_decode_greedy": (C.c_int, [_P, _P, C.c_uint32, C.c_uint32, C.c_uint32, _P, _P, C.c_int]),
     "yl_decode_step_launches": (C.c_int, [_P, C.POINTER(C.c_uint32)]),
     "yl_profile_decode_step": (C.c_int, [_P, _P, C.c_uint32, C.c_uint32, _P, C.c_uint32, C.POINTER(C.c_uint32)]),
+    "yl_trace_decode_step": (C.c_int, [_P, _P, C.c_uint32, C.c_uint32, _P, C.c_uint64, C.POINTER(C.c_uint32)]),
     "load_transformer_ffi": (C.c_bool, [C.c_char_p]),
     "yl_synth_write_gguf": (C.c_int, [C.c_char_p, C.POINTER(SynthC)]),
 }
@@ -398,6 +399,17 @@ class Transformer:
         n = C.c_uint32()
         _check(_lib.yl_profile_decode_step(self._h, session._h, token, pos, _ptr(us), cap, C.byref(n)))
         return us[:n.value]
+
+    def trace_decode_step(self, session: InferenceSession, token: int, pos: int) -> np.ndarray:
+        """Global-timer stamps (ns) of one decode step run as the decode graph
+        runs it: array [launch][cta][4] = (entry, prologue done / wait
+        released, first stage ready / partials visible, done); zeros where a
+        launch has fewer CTAs or is not stamped (the embedding)."""
+        n_max = 5 * self.shape().n_layers + 4
+        out = np.zeros(n_max * 4096, np.uint64)
+        n = C.c_uint32()
+        _check(_lib.yl_trace_decode_step(self._h, session._h, token, pos, _ptr(out), out.size, C.byref(n)))
+        return out[: n.value * 4096].reshape(n.value, 1024, 4)
 
     def weight(self, layer: int, which: int) -> QuantizedTensor:
         c = QTensorC()

@@ -531,6 +531,13 @@ int yl_profile_decode_step(const yl_model* m, yl_session* sp, uint32_t token, ui
   return profile_step(sp->s, token, pos, us_out, cap, n_out);
 }
 
+int yl_trace_decode_step(const yl_model* m, yl_session* sp, uint32_t token, uint32_t pos, uint64_t* out,
+                         uint64_t cap, uint32_t* n_launches) {
+  if (!m || !sp) return fail(YL_ERR_ARG, "null argument");
+  if (sp->s->m != m->m) return fail(YL_ERR_ARG, "session belongs to another model");
+  return trace_step(sp->s, token, pos, out, cap, n_launches);
+}
+
 // ------------------------------- reference FFI ---------------------------
 
 static std::mutex g_ffi_mu;

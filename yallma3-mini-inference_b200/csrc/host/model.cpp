@@ -681,6 +681,7 @@ int run_matvec_ex(const DevWeight& w, bool f32act, const int8_t* xq, const float
     a.am_count = ex.am_count;
     a.am_out = ex.am_out;
     a.state = ex.state;
+    a.trace = ex.trace;
     cudaError_t e = k::matvec(a, fmt, w.sf16, epi, lc);
     if (e != cudaSuccess) return fail(YL_ERR_CUDA, std::string("matvec launch: ") + cudaGetErrorString(e));
     if (launches) ++*launches;
@@ -722,11 +723,15 @@ int enqueue_forward(Session* s, uint32_t n, uint32_t start_pos, bool from_state,
     ++nl;                                                                                 \
     YL_MARK();                                                                            \
   } while (0)
-#define YL_MV(...)                                  \
-  do {                                              \
-    if ((rc = run_matvec(__VA_ARGS__))) return rc;  \
-    nl += 1;                                        \
-    YL_MARK();                                      \
+// timeline stamps of the launch about to be enqueued (launch index nl)
+#define YL_TRACE() (s->trace_on ? s->trace + (uint64_t)nl * TRACE_STRIDE : nullptr)
+  MvExtra plain;
+#define YL_MV(...)                                                   \
+  do {                                                               \
+    plain.trace = YL_TRACE();                                        \
+    if ((rc = run_matvec_ex(__VA_ARGS__, plain, nullptr))) return rc; \
+    nl += 1;                                                         \
+    YL_MARK();                                                       \
   } while (0)
 
   YL_MARK();
@@ -747,6 +752,7 @@ int enqueue_forward(Session* s, uint32_t n, uint32_t start_pos, bool from_state,
     norm.hq = nullptr;
     norm.hs = nullptr;
     norm.hcount = nullptr;
+    norm.trace = YL_TRACE();
     if ((rc = run_matvec_ex(L.wqkv, f32act, nullptr, nullptr, nullptr, d, d / 32, n, s->qkv, att + 2 * kvd,
                             k::EPI_STORE, 0, s->err, s->stream, pdl, m->num_sms, norm, &nl)))
       return rc;
@@ -768,6 +774,7 @@ int enqueue_forward(Session* s, uint32_t n, uint32_t start_pos, bool from_state,
       ad.scale = m->attn_scale;
       ad.n_splits = s->n_splits;
       ad.early_kv = from_state ? 1 : 0;
+      ad.trace = YL_TRACE();
       ad.out = f32act ? s->xf : nullptr;
       ad.q8 = f32act ? nullptr : s->xq;
       ad.s8 = s->xs;
@@ -806,6 +813,7 @@ int enqueue_forward(Session* s, uint32_t n, uint32_t start_pos, bool from_state,
     norm.hq = f32act ? nullptr : s->hq;
     norm.hs = f32act ? nullptr : s->hs;
     norm.hcount = f32act ? nullptr : s->hcount;
+    norm.trace = YL_TRACE();
     if ((rc = run_matvec_ex(L.w13, f32act, nullptr, nullptr, nullptr, d, d / 32, n, s->h, f,
                             f32act ? k::EPI_SWIGLU : k::EPI_SWIGLU_Q8, 0, s->err, s->stream, pdl, m->num_sms, norm,
                             &nl)))
@@ -828,6 +836,7 @@ int enqueue_forward(Session* s, uint32_t n, uint32_t start_pos, bool from_state,
     fin.am_count = s->am_count;
     fin.am_out = s->hist;
     fin.state = from_state ? s->state : nullptr;
+    fin.trace = YL_TRACE();
     if ((rc = run_matvec_ex(m->lm, true, nullptr, nullptr, nullptr, d, 0, 1, s->logits, sh.vocab_size, k::EPI_ARGMAX,
                             0, s->err, s->stream, pdl, m->num_sms, fin, &nl)))
       return rc;
@@ -836,6 +845,7 @@ int enqueue_forward(Session* s, uint32_t n, uint32_t start_pos, bool from_state,
 #undef YL_LAUNCH
 #undef YL_MV
 #undef YL_MARK
+#undef YL_TRACE
   if (launches) *launches = nl;
   return YL_OK;
 }
@@ -889,6 +899,46 @@ int profile_step(Session* s, uint32_t token, uint32_t pos, float* us, uint32_t c
   if (rc) return rc;
   if (e != cudaSuccess) return fail(YL_ERR_CUDA, std::string("profile: ") + cudaGetErrorString(e));
   if (n_out) *n_out = n;
+  return YL_OK;
+}
+
+int trace_step(Session* s, uint32_t token, uint32_t pos, uint64_t* out, uint64_t cap, uint32_t* n_launches) {
+  const yl_shape& sh = s->m->shape;
+  if (pos >= sh.ctx_len) return fail(YL_ERR_RANGE, "position beyond ctx_len");
+  YL_CUDA_TRY(cudaSetDevice(s->device));
+  int rc = ensure_cap(s, 8);
+  if (rc) return rc;
+  const uint64_t n_max = 5ull * sh.n_layers + 4;
+  if (!s->trace) {
+    void* p = nullptr;
+    if ((rc = salloc(s, n_max * TRACE_STRIDE * 8, &p))) return rc;
+    s->trace = (uint64_t*)p;
+  }
+  YL_CUDA_TRY(cudaMemsetAsync(s->trace, 0, n_max * TRACE_STRIDE * 8, s->stream));
+  s->state_h->pos = (int32_t)pos;
+  s->state_h->token = (int32_t)token;
+  s->state_h->next = 0;
+  s->state_h->steps = 0;
+  YL_CUDA_TRY(cudaMemcpyAsync(s->state, s->state_h, sizeof(k::StepState), cudaMemcpyHostToDevice, s->stream));
+  YL_CUDA_TRY(cudaStreamSynchronize(s->stream));
+  cudaGraph_t g = nullptr;
+  cudaGraphExec_t ge = nullptr;
+  uint32_t nl = 0;
+  YL_CUDA_TRY(cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal));
+  s->trace_on = true;
+  rc = enqueue_forward(s, 1, 0, true, tunables().pdl, &nl);
+  s->trace_on = false;
+  cudaError_t e = cudaStreamEndCapture(s->stream, &g);
+  if (e == cudaSuccess && rc == YL_OK) e = cudaGraphInstantiate(&ge, g, 0);
+  if (e == cudaSuccess && rc == YL_OK) e = cudaGraphLaunch(ge, s->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s->stream);
+  if (ge) cudaGraphExecDestroy(ge);
+  if (g) cudaGraphDestroy(g);
+  if (rc) return rc;
+  if (e != cudaSuccess) return fail(YL_ERR_CUDA, std::string("trace: ") + cudaGetErrorString(e));
+  const uint64_t n = std::min<uint64_t>(cap, (uint64_t)nl * TRACE_STRIDE);
+  if (out && n) YL_CUDA_TRY(cudaMemcpy(out, s->trace, n * 8, cudaMemcpyDeviceToHost));
+  if (n_launches) *n_launches = nl;
   return YL_OK;
 }
 

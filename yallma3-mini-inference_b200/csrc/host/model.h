@@ -84,6 +84,8 @@ struct Session {
   uint32_t* hist_h = nullptr;
   uint32_t n_splits = 1;
   std::vector<cudaEvent_t>* prof = nullptr;  // profiling: events recorded after each launch
+  uint64_t* trace = nullptr;  // timeline tracing: [launch][TRACE_STRIDE] stamps
+  bool trace_on = false;
   cudaGraphExec_t graph = nullptr;
   uint32_t graph_launches = 0;
   std::vector<void*> allocs;
@@ -101,6 +103,11 @@ int forward(Session* s, const uint32_t* tokens_host, uint32_t n, uint32_t start_
 int profile_step(Session* s, uint32_t token, uint32_t pos, float* us, uint32_t cap, uint32_t* n_out);
 // One batch-1 step through the captured graph (state already set on device).
 int ensure_decode_graph(Session* s);
+// One batch-1 step captured exactly like the decode graph (PDL, state on the
+// device) with every matvec / attention CTA stamping globaltimer at fixed
+// points: out[launch * TRACE_STRIDE + cta * 4 + i].
+constexpr uint32_t TRACE_STRIDE = 4 * 1024;
+int trace_step(Session* s, uint32_t token, uint32_t pos, uint64_t* out, uint64_t cap, uint32_t* n_launches);
 // Tunables read once from the environment (YL_MV_KC_BYTES, YL_MV_SMEM, YL_PDL,
 // YL_MV_GRID_MULT, YL_LM_LIMBS).
 struct Tunables {
@@ -129,6 +136,7 @@ struct MvExtra {
   unsigned int* am_count = nullptr;
   uint32_t* am_out = nullptr;
   k::StepState* state = nullptr;
+  uint64_t* trace = nullptr;   // timeline stamps of this launch (nullable)
 };
 int run_matvec_ex(const DevWeight& w, bool f32act, const int8_t* xq, const float* xs, const float* xf,
                   uint64_t x_stride, uint64_t xs_stride, uint32_t ntok, float* out, uint64_t out_stride, int epi,

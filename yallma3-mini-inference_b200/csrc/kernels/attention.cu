@@ -313,6 +313,8 @@ __global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(AttnDecodeArgs 
   const uint32_t rank = cluster.block_rank();
   const uint32_t kvh = blockIdx.x / cs;
   const uint32_t kv_mul = a.n_heads / a.n_kv_heads;
+  uint64_t* const trace = a.trace ? a.trace + (uint64_t)blockIdx.x * 4 : nullptr;
+  if (trace && tid == 0) trace[0] = globaltimer();
   grid_dep_launch();
   if (!a.early_kv) grid_dep_wait();
   const uint32_t pos = a.state ? (uint32_t)a.state->pos : a.pos0;
@@ -335,6 +337,7 @@ __global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(AttnDecodeArgs 
   uint32_t t0 = p_begin, tn = min((uint32_t)AD_TILE, p_end - p_begin);
   if (tn) issue_tile(t0, tn);
   if (a.early_kv) grid_dep_wait();
+  if (trace && tid == 0) trace[1] = globaltimer();
 
   // rotated q of the kv_mul query heads; running statistics
   const float2* c = a.cs + (uint64_t)pos * half;
@@ -490,6 +493,7 @@ __global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(AttnDecodeArgs 
 
   // every split's partial is in its CTA's shared memory
   cluster.sync();
+  if (trace && tid == 0) trace[2] = globaltimer();
   // merge: warp `warp` of CTA `rank` takes 32-blocks rank + cs*warp + ...;
   // block b covers elements [32b, 32b+32) of the KV head's kv_mul*HD outputs
   const uint32_t nblk = kv_mul * HD / 32;
@@ -528,6 +532,7 @@ __global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(AttnDecodeArgs 
   }
   // peers may still be reading this CTA's shared memory
   cluster.sync();
+  if (trace && tid == 0) trace[3] = globaltimer();
 }
 
 template <int HD>

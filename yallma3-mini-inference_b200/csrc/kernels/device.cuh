@@ -20,6 +20,12 @@ enum : int { ERR_NONE = 0, ERR_WAIT_TIMEOUT = 1, ERR_BAD_ARG = 2 };
 __device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 // Allow the next kernel in the stream to be scheduled (it still waits in
 // grid_dep_wait() for this grid to finish before reading our outputs).
+// Global nanosecond timer (timeline tracing of the decode step).
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
 __device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 // ---- time ----------------------------------------------------------------

@@ -86,6 +86,9 @@ struct MvArgs {
   unsigned int* am_count;
   uint32_t* am_out;
   StepState* state;
+  // timeline tracing (nullable): per CTA [entry, prologue done, first stage
+  // ready, consumers done] in globaltimer nanoseconds
+  uint64_t* trace;
 };
 // fmt: FMT_*; scale_f16: weight scale type. Chooses NT from a.ntok.
 cudaError_t matvec(const MvArgs& a, int fmt, bool scale_f16, int epi, const LaunchCfg& lc);
@@ -166,6 +169,9 @@ struct AttnDecodeArgs {
   float* out;             // [n_heads*head_size] f32 (nullable)
   int8_t* q8;             // (nullable)
   float* s8;
+  // timeline tracing (nullable): per CTA [entry, wait released, partials
+  // visible, done] in globaltimer nanoseconds
+  uint64_t* trace;
 };
 // Cluster size for the decode attention: 16 when n_kv_heads clusters of 16
 // can be resident at once, else 8.

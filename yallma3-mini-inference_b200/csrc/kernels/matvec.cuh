@@ -652,6 +652,8 @@ __global__ void __launch_bounds__(MV_THREADS, (NT <= 2 ? 2 : 1)) mv_kernel(MvArg
   const uint32_t nrs = (r_end - r_begin + RS - 1) / RS;
   const uint32_t n_it = nrs * nch;
 
+  uint64_t* const trace = a.trace ? a.trace + (uint64_t)blockIdx.x * 4 : nullptr;
+  if (trace && threadIdx.x == 0) trace[0] = globaltimer();
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
@@ -714,6 +716,7 @@ __global__ void __launch_bounds__(MV_THREADS, (NT <= 2 ? 2 : 1)) mv_kernel(MvArg
   grid_dep_wait();
   mv_stage_x<FMT, NT>(a, L, smem, cw, lane);
   named_bar_sync(1, MV_NCW * 32);
+  if (trace && threadIdx.x == 32) trace[1] = globaltimer();
 
   float acc[RPW][NT];
 #pragma unroll
@@ -730,6 +733,7 @@ __global__ void __launch_bounds__(MV_THREADS, (NT <= 2 ? 2 : 1)) mv_kernel(MvArg
     const int slot = it % S;
     const uint32_t ph = (it / S) & 1;
     if (!dead && !mbar_wait(&full[slot], ph, a.err)) dead = true;
+    if (trace && it == 0 && threadIdx.x == 32) trace[2] = globaltimer();
     const uint32_t rs = it / nch, ch = it % nch;
     const uint32_t row0 = r_begin + rs * RS;
     const uint32_t k0 = ch * kc, kn = min(kc, K - k0);
@@ -889,6 +893,7 @@ __global__ void __launch_bounds__(MV_THREADS, (NT <= 2 ? 2 : 1)) mv_kernel(MvArg
       }
     }
   }
+  if (trace && threadIdx.x == 32) trace[3] = globaltimer();
 }
 
 // Host-side launcher for one (FMT, SF16) family; NT and EPI dispatched here.
