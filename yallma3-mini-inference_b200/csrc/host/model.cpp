@@ -641,6 +641,7 @@ int run_matvec_ex(const DevWeight& w, bool f32act, const int8_t* xq, const float
   }
   else if (w.fmt == YL_Q4_0) { fmt = f32act ? k::FMT_Q4F : k::FMT_Q4; kc = tu.kc_bytes * 2; }
   else { fmt = k::FMT_F16; kc = tu.kc_bytes / 2; }
+  if (tu.kc_bytes == 0) kc = (uint32_t)round_up(w.cols, 256);  // whole rows
   kc = std::max<uint32_t>(256, kc / 256 * 256);
   k::LaunchCfg lc;
   lc.stream = st;

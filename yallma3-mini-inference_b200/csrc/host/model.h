@@ -109,7 +109,7 @@ int ensure_decode_graph(Session* s);
 constexpr uint32_t TRACE_STRIDE = 4 * 1024;
 int trace_step(Session* s, uint32_t token, uint32_t pos, uint64_t* out, uint64_t cap, uint32_t* n_launches);
 // Tunables read once from the environment (YL_MV_KC_BYTES, YL_MV_SMEM, YL_PDL,
-// YL_MV_GRID_MULT, YL_LM_LIMBS).
+// YL_MV_GRID_MULT, YL_LM_LIMBS; YL_MV_KC_BYTES=0 streams whole rows).
 struct Tunables {
   uint32_t kc_bytes = 4096;  // weight bytes per row per bulk copy
   uint32_t smem = 100 * 1024;  // per CTA: two matvec CTAs fit on one SM

@@ -44,6 +44,10 @@ __host__ __device__ constexpr bool mv_f32_act() {
   return FMT == FMT_F16 || FMT == FMT_Q8F || FMT == FMT_Q4F;
 }
 __host__ __device__ constexpr bool mv_swiglu(int epi) { return epi == EPI_SWIGLU || epi == EPI_SWIGLU_Q8; }
+// Consumer groups: SwiGLU stages hold row pairs (twice the bytes of a row), so
+// its ring is split into two groups of four warps to keep two stages in the
+// budget; every other epilogue uses one group of eight warps.
+__host__ __device__ constexpr int mv_groups(int epi) { return mv_swiglu(epi) ? 2 : 1; }
 
 // Shared-memory layout, computed identically on host and device.
 struct MvLayout {
@@ -53,12 +57,15 @@ struct MvLayout {
 // ssz: weight scale element size (2 for f16, 4 for f32). A stage's scale row
 // is the chunk's scales padded to 16 bytes, which for a full-row chunk equals
 // the HBM scale row stride, so full-row stages are single contiguous copies.
+// groups: consumer groups; a stage holds the rows of one group (MV_NCW/groups
+// warps x rpw rows each).
 template <int FMT, int NT>
-__host__ __device__ inline MvLayout mv_layout(uint32_t K, uint32_t kc, int rpw, int stages, uint32_t ssz = 4) {
+__host__ __device__ inline MvLayout mv_layout(uint32_t K, uint32_t kc, int rpw, int stages, uint32_t ssz = 4,
+                                             int groups = 1) {
   MvLayout L;
-  L.bar_off = 0;       // 2 x 8 mbarriers
-  L.red_off = 128;     // reductions / argmax / h staging ([2][8][32] floats)
-  uint32_t off = 128 + 2048 + 128;
+  L.bar_off = 0;       // 2 x 16 mbarriers
+  L.red_off = 256;     // reductions / argmax / h staging ([2][8][32] floats)
+  uint32_t off = 256 + 2048 + 128;
   L.x_off = off;
   if (mv_f32_act<FMT>()) {
     off += NT * K * 4;
@@ -77,7 +84,7 @@ __host__ __device__ inline MvLayout mv_layout(uint32_t K, uint32_t kc, int rpw, 
   L.ring_off = off;
   L.stage_q_row = mv_qbytes<FMT>(kc);
   L.stage_s_row = mv_has_scales<FMT>() ? ((kc / 32 * ssz + 15u) & ~15u) : 0;
-  L.stage_bytes = (uint32_t)(MV_NCW * rpw) * (L.stage_q_row + L.stage_s_row);
+  L.stage_bytes = (uint32_t)(MV_NCW / groups * rpw) * (L.stage_q_row + L.stage_s_row);
   L.total = off + stages * L.stage_bytes;
   return L;
 }
@@ -102,6 +109,12 @@ __device__ __forceinline__ void i8x4_to_f32(uint32_t w, float& f0, float& f1, fl
   f1 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7651)) - 8388736.0f;
   f2 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7652)) - 8388736.0f;
   f3 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7653)) - 8388736.0f;
+}
+
+// Exact int -> f32 for |v| < 2^22 on the integer and FMA pipes (the I2F unit
+// runs at a quarter of their rate): 0x4B400000 + v is the float 1.5*2^23 + v.
+__device__ __forceinline__ float small_i2f(int v) {
+  return __int_as_float(0x4B400000 + v) - 12582912.0f;
 }
 
 __device__ __forceinline__ bool am_better(float v, uint32_t i, float bv, uint32_t bi) {
@@ -527,18 +540,15 @@ __device__ __forceinline__ void mv_row_chunk(const uint8_t* wrow, const uint8_t*
             s[u][l] = dp4a(w[u].w, x.w, d);
           }
         }
-#pragma unroll
-        for (int u = 0; u < 2; ++u)
-#pragma unroll
-          for (int l = 0; l < 3; ++l) s[u][l] += __shfl_xor_sync(FULL, s[u][l], 1);  // whole-block sums
+        // per lane: this half-block's w.y / s = A + (B + C/254)/254 (|A|,|B|,|C|
+        // < 2^22, exact in f32), then one shuffle completes the block
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
           const uint32_t c = c0 + u * 32 + lane;
-          if (v[u] && !(lane & 1)) {
-            // sum_k w*y over the block = s * (A + (B + C/254)/254)
-            const float blk = (float)s[u][0] + ((float)s[u][1] + (float)s[u][2] * (1.0f / 254.0f)) * (1.0f / 254.0f);
-            acc[t] = fmaf(blk * wsc[u], xs[t * (K / 32) + (k0 >> 5) + (c >> 1)], acc[t]);
-          }
+          float blk = small_i2f(s[u][0]) +
+                      fmaf(small_i2f(s[u][2]), 1.0f / 254.0f, small_i2f(s[u][1])) * (1.0f / 254.0f);
+          blk += __shfl_xor_sync(FULL, blk, 1);
+          if (v[u] && !(lane & 1)) acc[t] = fmaf(blk * wsc[u], xs[t * (K / 32) + (k0 >> 5) + (c >> 1)], acc[t]);
         }
       }
     }
@@ -638,7 +648,8 @@ __global__ void __launch_bounds__(MV_THREADS, (NT <= 2 ? 2 : 1)) mv_kernel(MvArg
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t K = a.K, kc = a.kc;
   const int S = a.stages;
-  const MvLayout L = mv_layout<FMT, NT>(K, kc, RPW, S, SF16 ? 2u : 4u);
+  constexpr int G = mv_groups(EPI);
+  const MvLayout L = mv_layout<FMT, NT>(K, kc, RPW, S, SF16 ? 2u : 4u, G);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar_off);
   uint64_t* empty = full + S;
 
@@ -647,17 +658,26 @@ __global__ void __launch_bounds__(MV_THREADS, (NT <= 2 ? 2 : 1)) mv_kernel(MvArg
   const uint64_t units = a.rows / unit;
   const uint32_t r_begin = (uint32_t)(units * blockIdx.x / gridDim.x) * unit;
   const uint32_t r_end = (uint32_t)(units * (blockIdx.x + 1) / gridDim.x) * unit;
-  const uint32_t RS = MV_NCW * RPW;
+  // Stages carry row sets of RS rows (one consumer group's rows) and K-chunks.
+  // Stage order: round p, chunk ch, group g (row set p*G + g), so consecutive
+  // stages go to different groups and all groups consume concurrently; the
+  // producer and every consumer walk the same nest and count stages in q.
+  constexpr int WPG = MV_NCW / G;  // warps per group
+  if (S % G != 0 || S > 16) {  // the launcher never plans this (parity aliasing)
+    if (threadIdx.x == 0 && a.err) atomicExch(a.err, 1);
+    return;
+  }
+  const uint32_t RS = WPG * RPW;
   const uint32_t nch = (K + kc - 1) / kc;
   const uint32_t nrs = (r_end - r_begin + RS - 1) / RS;
-  const uint32_t n_it = nrs * nch;
+  const uint32_t nrounds = (nrs + G - 1) / G;
 
   uint64_t* const trace = a.trace ? a.trace + (uint64_t)blockIdx.x * 4 : nullptr;
   if (trace && threadIdx.x == 0) trace[0] = globaltimer();
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], MV_NCW);
+      mbar_init(&empty[s], WPG);
     }
     mbar_fence_init();
   }
@@ -672,12 +692,17 @@ __global__ void __launch_bounds__(MV_THREADS, (NT <= 2 ? 2 : 1)) mv_kernel(MvArg
       // a stage's rows are then one contiguous range in both places.
       const bool contig = nch == 1 && L.stage_q_row == a.row_bytes &&
                           (!mv_has_scales<FMT>() || L.stage_s_row == a.scale_row_bytes);
-      uint32_t issued = 0;
-      for (uint32_t it = 0; it < n_it; ++it) {
-        const int slot = it % S;
-        const uint32_t ph = (it / S) & 1;
-        if (!mbar_wait(&empty[slot], ph ^ 1, a.err)) break;
-        const uint32_t rs = it / nch, ch = it % nch;
+      uint32_t issued = 0, q = 0;
+      bool ok = true;
+      for (uint32_t p = 0; ok && p < nrounds; ++p)
+      for (uint32_t ch = 0; ok && ch < nch; ++ch)
+      for (int g = 0; g < G; ++g) {
+        const uint32_t rs = p * G + g;
+        if (rs >= nrs) break;
+        const int slot = q % S;
+        const uint32_t ph = (q / S) & 1;
+        ++q;
+        if (!mbar_wait(&empty[slot], ph ^ 1, a.err)) { ok = false; break; }
         const uint32_t row0 = r_begin + rs * RS;
         const uint32_t nrows = min(RS, r_end - row0);
         const uint32_t k0 = ch * kc, kn = min(kc, K - k0);
@@ -690,7 +715,7 @@ __global__ void __launch_bounds__(MV_THREADS, (NT <= 2 ? 2 : 1)) mv_kernel(MvArg
           bulk_g2s(stage, a.wq + (uint64_t)row0 * a.row_bytes, nrows * qb, &full[slot], pol);
           if (sb) bulk_g2s(stage + RS * L.stage_q_row, a.ws + (uint64_t)row0 * a.scale_row_bytes, nrows * sb,
                            &full[slot], pol);
-          issued = it + 1;
+          issued = q;
           continue;
         }
         for (uint32_t r = 0; r < nrows; ++r) {
@@ -700,7 +725,7 @@ __global__ void __launch_bounds__(MV_THREADS, (NT <= 2 ? 2 : 1)) mv_kernel(MvArg
             bulk_g2s(stage + RS * L.stage_q_row + r * L.stage_s_row,
                      a.ws + row * a.scale_row_bytes + (k0 / 32) * ssz, sb, &full[slot], pol);
         }
-        issued = it + 1;
+        issued = q;
       }
       // Drain: no bulk copy may still target this CTA's shared memory at exit.
       // In a healthy run every issued stage was consumed, so this returns at once.
@@ -729,18 +754,25 @@ __global__ void __launch_bounds__(MV_THREADS, (NT <= 2 ? 2 : 1)) mv_kernel(MvArg
   // After a wait timeout the warp stops waiting and computing ("dead") but
   // keeps walking the loop so every named barrier below is still reached.
   bool dead = false;
-  for (uint32_t it = 0; it < n_it; ++it) {
-    const int slot = it % S;
-    const uint32_t ph = (it / S) & 1;
+  const int grp = cw / WPG, wi = cw % WPG;
+  uint32_t q = 0;
+  for (uint32_t p = 0; p < nrounds; ++p)
+  for (uint32_t ch = 0; ch < nch; ++ch)
+  for (int g = 0; g < G; ++g) {
+    const uint32_t rs = p * G + g;
+    if (rs >= nrs) break;
+    const int slot = q % S;
+    const uint32_t ph = (q / S) & 1;
+    ++q;
+    if (g != grp) continue;
     if (!dead && !mbar_wait(&full[slot], ph, a.err)) dead = true;
-    if (trace && it == 0 && threadIdx.x == 32) trace[2] = globaltimer();
-    const uint32_t rs = it / nch, ch = it % nch;
+    if (trace && q == 1 && threadIdx.x == 32) trace[2] = globaltimer();
     const uint32_t row0 = r_begin + rs * RS;
     const uint32_t k0 = ch * kc, kn = min(kc, K - k0);
     const uint8_t* stage = smem + L.ring_off + slot * L.stage_bytes;
 #pragma unroll
     for (int rr = 0; rr < RPW; ++rr) {
-      const uint32_t rl = cw * RPW + rr;
+      const uint32_t rl = wi * RPW + rr;
       if (dead || row0 + rl >= r_end) continue;
       mv_row_chunk<FMT, NT, SF16>(stage + rl * L.stage_q_row, stage + RS * L.stage_q_row + rl * L.stage_s_row, smem,
                                   L, K, k0, kn, lane, acc[rr]);
@@ -755,7 +787,7 @@ __global__ void __launch_bounds__(MV_THREADS, (NT <= 2 ? 2 : 1)) mv_kernel(MvArg
 #pragma unroll
       for (int rr = 0; rr < RPW; ++rr) acc[rr][t] = warp_sum(acc[rr][t]);
     if (mv_swiglu(EPI)) {
-      const uint32_t r = row0 + cw * RPW;  // gate row (even), up row = r + 1
+      const uint32_t r = row0 + wi * RPW;  // gate row (even), up row = r + 1
       const bool have = r + 1 < r_end;
       float hv[NT];
 #pragma unroll
@@ -768,7 +800,7 @@ __global__ void __launch_bounds__(MV_THREADS, (NT <= 2 ? 2 : 1)) mv_kernel(MvArg
     } else {
 #pragma unroll
       for (int rr = 0; rr < RPW; ++rr) {
-        const uint32_t r = row0 + cw * RPW + rr;
+        const uint32_t r = row0 + wi * RPW + rr;
         if (r >= r_end) continue;
         if (EPI == EPI_ARGMAX) {
           const float v = acc[rr][0];
@@ -904,21 +936,31 @@ cudaError_t mv_launch(const MvArgs& a0, int epi, const LaunchCfg& lc) {
   const int rpw = mv_swiglu(epi) ? 2 : 1;
   MvLayout L0;
   int stages = 0;
-  for (;;) {
+  auto layout = [&](int g) {
     switch (nt) {
-      case 1: L0 = mv_layout<FMT, 1>(a.K, a.kc, rpw, 0, SF16 ? 2u : 4u); break;
-      case 2: L0 = mv_layout<FMT, 2>(a.K, a.kc, rpw, 0, SF16 ? 2u : 4u); break;
-      case 4: L0 = mv_layout<FMT, 4>(a.K, a.kc, rpw, 0, SF16 ? 2u : 4u); break;
-      default: L0 = mv_layout<FMT, 8>(a.K, a.kc, rpw, 0, SF16 ? 2u : 4u); break;
+      case 1: return mv_layout<FMT, 1>(a.K, a.kc, rpw, 0, SF16 ? 2u : 4u, g);
+      case 2: return mv_layout<FMT, 2>(a.K, a.kc, rpw, 0, SF16 ? 2u : 4u, g);
+      case 4: return mv_layout<FMT, 4>(a.K, a.kc, rpw, 0, SF16 ? 2u : 4u, g);
+      default: return mv_layout<FMT, 8>(a.K, a.kc, rpw, 0, SF16 ? 2u : 4u, g);
     }
+  };
+  // Ring plan. The stage count S must be a multiple of the group count G:
+  // then slot s always serves group s % G, every wait on a slot is exactly one
+  // phase after that group's previous use of it, and the mbarrier parity is
+  // unambiguous (with S % G != 0 a group could pass a wait on the completion
+  // of a phase two uses back, i.e. on another group's stage).
+  const int G = mv_groups(epi);
+  for (;;) {
+    L0 = layout(G);
     stages = (int)((lc.smem_budget > L0.total ? lc.smem_budget - L0.total : 0) / L0.stage_bytes);
+    stages = (stages > 16 ? 16 : stages) / G * G;
     // a ring of fewer than two stages inside the budget cannot overlap copy
     // and compute (or costs the SM its second CTA): halve the chunk instead
     if (stages >= 2 || a.kc <= 256) break;
     a.kc = (a.kc / 2 + 255u) / 256u * 256u;
   }
-  if (stages > 8) stages = 8;
-  if (stages < 2) stages = 2;
+  if (stages < 2) stages = 2;  // activations fill the budget (large token groups)
+  if (stages % G || stages > 16) return cudaErrorInvalidConfiguration;
   a.stages = stages;
   const uint32_t smem = L0.total + stages * L0.stage_bytes;
   if (smem > 227u * 1024u) return cudaErrorInvalidConfiguration;

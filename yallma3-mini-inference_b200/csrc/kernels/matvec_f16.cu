@@ -10,10 +10,11 @@ cudaError_t matvec_q4(const MvArgs& a, int fmt, bool sf16, int epi, const Launch
 template <int FMT>
 static uint32_t max_ntok_fmt(uint32_t K, uint32_t kc, int rpw) {
   const uint32_t lim = 227u * 1024u;
-  if (mv_layout<FMT, 8>(K, kc, rpw, 2).total <= lim) return 8;
-  if (mv_layout<FMT, 4>(K, kc, rpw, 2).total <= lim) return 4;
-  if (mv_layout<FMT, 2>(K, kc, rpw, 2).total <= lim) return 2;
-  if (mv_layout<FMT, 1>(K, kc, rpw, 2).total <= lim) return 1;
+  const int g = rpw == 2 ? 2 : 1;  // mv_groups of the SwiGLU / other epilogues
+  if (mv_layout<FMT, 8>(K, kc, rpw, 2, 4, g).total <= lim) return 8;
+  if (mv_layout<FMT, 4>(K, kc, rpw, 2, 4, g).total <= lim) return 4;
+  if (mv_layout<FMT, 2>(K, kc, rpw, 2, 4, g).total <= lim) return 2;
+  if (mv_layout<FMT, 1>(K, kc, rpw, 2, 4, g).total <= lim) return 1;
   return 0;
 }
 
