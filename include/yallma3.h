@@ -231,9 +231,9 @@ int yl_profile_decode_step(const yl_model* m, yl_session* s, uint32_t token, uin
 /* Diagnostic: runs one batch-1 decode step of `token` at `pos` exactly as the
  * decode graph does (one graph, programmatic dependent launch) while every
  * matvec and attention CTA stamps the GPU's nanosecond global timer at four
- * points: out[launch * 4096 + cta * 4 + i], i = entry, prologue done (wait
- * released for attention), first weight stage ready (attention: partials
- * visible), done. Launch order as yl_profile_decode_step; the embedding launch
+ * points: out[launch * 4096 + cta * 4 + i], i = entry, activations staged
+ * (attention: wait released), wait on the preceding kernel released
+ * (attention: partials visible), done. Launch order as yl_profile_decode_step; the embedding launch
  * (index 0) is not stamped. Writes up to cap values; *n_launches = launches. */
 int yl_trace_decode_step(const yl_model* m, yl_session* s, uint32_t token, uint32_t pos, uint64_t* out,
                          uint64_t cap, uint32_t* n_launches);

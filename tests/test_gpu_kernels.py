@@ -42,6 +42,27 @@ def test_quantizer_random_bit_exact(yl, orc, torch_cuda, n):
     assert np.array_equal(s.view(np.uint32), so.view(np.uint32))
 
 
+def test_quantizer_half_ties_bit_exact(yl, orc, torch_cuda):
+    """Blocks whose quotients x/scale sit on, or a few ulps either side of,
+    half-integers: the device rounds x*(1/scale) and must fall back to the
+    exact quotient exactly where the two could round differently."""
+    rng = np.random.default_rng(7)
+    blocks = []
+    for amax in (127.0, 3.0, 0.7, 1e-3, 4.5e4, 1.0e-30):
+        sc = np.float32(np.float32(amax) / np.float32(127.0))
+        for _ in range(64):
+            k = rng.integers(-126, 126, 31) + 0.5
+            x = (k * np.float64(sc)).astype(np.float32)
+            ulps = rng.integers(-4, 5, 31).astype(np.int32)
+            x = (x.view(np.int32) + ulps).view(np.float32)
+            blocks.append(np.concatenate([[np.float32(amax)], x]).astype(np.float32))
+    x = np.concatenate(blocks)
+    q, s = gpu_quantize(yl, torch_cuda, x)
+    qo, so = orc.quantize_q8(x)
+    assert np.array_equal(s.view(np.uint32), so.view(np.uint32))
+    assert np.array_equal(q, qo)
+
+
 def test_quantize_dispatch_errors(yl, torch_cuda):
     x = torch_cuda.zeros(64, device="cuda")
     dst = yl.new_workspace_buffer(yl.WeightFormat.Q8_0, 64, 32)

@@ -402,8 +402,8 @@ class Transformer:
 
     def trace_decode_step(self, session: InferenceSession, token: int, pos: int) -> np.ndarray:
         """Global-timer stamps (ns) of one decode step run as the decode graph
-        runs it: array [launch][cta][4] = (entry, prologue done / wait
-        released, first stage ready / partials visible, done); zeros where a
+        runs it: array [launch][cta][4] = (entry, activations staged / wait
+        released, wait released / partials visible, done); zeros where a
         launch has fewer CTAs or is not stamped (the embedding)."""
         n_max = 5 * self.shape().n_layers + 4
         out = np.zeros(n_max * 4096, np.uint64)

@@ -86,8 +86,8 @@ struct MvArgs {
   unsigned int* am_count;
   uint32_t* am_out;
   StepState* state;
-  // timeline tracing (nullable): per CTA [entry, prologue done, first stage
-  // ready, consumers done] in globaltimer nanoseconds
+  // timeline tracing (nullable): per CTA [entry, prologue done, wait
+  // released, consumers done] in globaltimer nanoseconds
   uint64_t* trace;
 };
 // fmt: FMT_*; scale_f16: weight scale type. Chooses NT from a.ntok.

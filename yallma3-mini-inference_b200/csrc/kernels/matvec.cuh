@@ -202,11 +202,12 @@ __device__ __forceinline__ void mv_norm_regs(const MvArgs& a, const MvLayout& L,
       m = fmaxf(m, __shfl_xor_sync(FULL, m, 2));
       m = fmaxf(m, __shfl_xor_sync(FULL, m, 1));
       const float sc = __fdiv_rn(m, 127.0f);
+      const float isc = __frcp_rn(sc);
       uint32_t word = 0;
       int qs = 0;
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const int8_t q = rust_as_i8(roundf(__fdiv_rn(y[e], sc)));
+        const int8_t q = rust_as_i8(round_quot(y[e], sc, isc));
         word |= (uint32_t)(uint8_t)q << (8 * e);
         qs += q;
       }
@@ -739,6 +740,7 @@ __global__ void __launch_bounds__(MV_THREADS, (NT <= 2 ? 2 : 1)) mv_kernel(MvArg
   // ---------------- consumers ----------------
   const int cw = warp - 1;
   grid_dep_wait();
+  if (trace && threadIdx.x == 32) trace[2] = globaltimer();
   mv_stage_x<FMT, NT>(a, L, smem, cw, lane);
   named_bar_sync(1, MV_NCW * 32);
   if (trace && threadIdx.x == 32) trace[1] = globaltimer();
@@ -766,7 +768,6 @@ __global__ void __launch_bounds__(MV_THREADS, (NT <= 2 ? 2 : 1)) mv_kernel(MvArg
     ++q;
     if (g != grp) continue;
     if (!dead && !mbar_wait(&full[slot], ph, a.err)) dead = true;
-    if (trace && q == 1 && threadIdx.x == 32) trace[2] = globaltimer();
     const uint32_t row0 = r_begin + rs * RS;
     const uint32_t k0 = ch * kc, kn = min(kc, K - k0);
     const uint8_t* stage = smem + L.ring_off + slot * L.stage_bytes;
