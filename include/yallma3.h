@@ -230,11 +230,13 @@ int yl_profile_decode_step(const yl_model* m, yl_session* s, uint32_t token, uin
                            uint32_t cap, uint32_t* n_out);
 /* Diagnostic: runs one batch-1 decode step of `token` at `pos` exactly as the
  * decode graph does (one graph, programmatic dependent launch) while every
- * matvec and attention CTA stamps the GPU's nanosecond global timer at four
- * points: out[launch * 4096 + cta * 4 + i], i = entry, activations staged
- * (attention: wait released), wait on the preceding kernel released
- * (attention: partials visible), done. Launch order as yl_profile_decode_step; the embedding launch
- * (index 0) is not stamped. Writes up to cap values; *n_launches = launches. */
+ * matvec and attention CTA stamps the GPU's nanosecond global timer:
+ * out[launch * 8192 + cta * 8 + i], i = 0 entry, 1 activations staged
+ * (attention: wait released), 2 wait on the preceding kernel released
+ * (attention: partials visible), 3 done; RMSNorm prologues also 4 first
+ * token's rows loaded, 5 norm factor ready, 6 warp 0's rows quantized, 7 the
+ * last warp's (0 where not stamped). Launch order as yl_profile_decode_step;
+ * the embedding launch (index 0) is not stamped. Writes up to cap values; *n_launches = launches. */
 int yl_trace_decode_step(const yl_model* m, yl_session* s, uint32_t token, uint32_t pos, uint64_t* out,
                          uint64_t cap, uint32_t* n_launches);
 

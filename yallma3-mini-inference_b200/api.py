@@ -402,14 +402,15 @@ class Transformer:
 
     def trace_decode_step(self, session: InferenceSession, token: int, pos: int) -> np.ndarray:
         """Global-timer stamps (ns) of one decode step run as the decode graph
-        runs it: array [launch][cta][4] = (entry, activations staged / wait
-        released, wait released / partials visible, done); zeros where a
-        launch has fewer CTAs or is not stamped (the embedding)."""
+        runs it: array [launch][cta][8] = (entry, activations staged / wait
+        released, wait released / partials visible, done, rows loaded, norm
+        factor ready, -, -); zeros where a launch has fewer CTAs or a point
+        is not stamped (the embedding launch has none)."""
         n_max = 5 * self.shape().n_layers + 4
-        out = np.zeros(n_max * 4096, np.uint64)
+        out = np.zeros(n_max * 8192, np.uint64)
         n = C.c_uint32()
         _check(_lib.yl_trace_decode_step(self._h, session._h, token, pos, _ptr(out), out.size, C.byref(n)))
-        return out[: n.value * 4096].reshape(n.value, 1024, 4)
+        return out[: n.value * 8192].reshape(n.value, 1024, 8)
 
     def weight(self, layer: int, which: int) -> QuantizedTensor:
         c = QTensorC()

@@ -105,8 +105,8 @@ int profile_step(Session* s, uint32_t token, uint32_t pos, float* us, uint32_t c
 int ensure_decode_graph(Session* s);
 // One batch-1 step captured exactly like the decode graph (PDL, state on the
 // device) with every matvec / attention CTA stamping globaltimer at fixed
-// points: out[launch * TRACE_STRIDE + cta * 4 + i].
-constexpr uint32_t TRACE_STRIDE = 4 * 1024;
+// points: out[launch * TRACE_STRIDE + cta * 8 + i].
+constexpr uint32_t TRACE_STRIDE = 8 * 1024;
 int trace_step(Session* s, uint32_t token, uint32_t pos, uint64_t* out, uint64_t cap, uint32_t* n_launches);
 // Tunables read once from the environment (YL_MV_KC_BYTES, YL_MV_SMEM, YL_PDL,
 // YL_MV_GRID_MULT, YL_LM_LIMBS; YL_MV_KC_BYTES=0 streams whole rows).

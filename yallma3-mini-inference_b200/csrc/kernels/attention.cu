@@ -313,7 +313,7 @@ __global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(AttnDecodeArgs 
   const uint32_t rank = cluster.block_rank();
   const uint32_t kvh = blockIdx.x / cs;
   const uint32_t kv_mul = a.n_heads / a.n_kv_heads;
-  uint64_t* const trace = a.trace ? a.trace + (uint64_t)blockIdx.x * 4 : nullptr;
+  uint64_t* const trace = a.trace ? a.trace + (uint64_t)blockIdx.x * 8 : nullptr;
   if (trace && tid == 0) trace[0] = globaltimer();
   grid_dep_launch();
   if (!a.early_kv) grid_dep_wait();

@@ -125,10 +125,10 @@ __device__ __forceinline__ float warp_max(float v) {
 // (saturating, NaN -> 0). Lane i holds element i; returns lane i's int8, the
 // scale is returned in every lane.
 __device__ __forceinline__ int8_t rust_as_i8(float v) {
-  if (v != v) return 0;
-  if (v >= 127.0f) return 127;
-  if (v <= -128.0f) return -128;
-  return (int8_t)(int)v;
+  // the device float -> int conversion truncates, saturates and maps NaN to
+  // 0, which with a clamp to [-128, 127] is exactly Rust's `as i8`
+  const int i = __float2int_rz(v);
+  return (int8_t)max(-128, min(127, i));
 }
 // roundf(x / d) with the quotient correctly rounded to f32 (the quantizer's
 // `(x / scale).round()`), from one multiply by inv = 1/d (correctly rounded).

@@ -86,8 +86,10 @@ struct MvArgs {
   unsigned int* am_count;
   uint32_t* am_out;
   StepState* state;
-  // timeline tracing (nullable): per CTA [entry, prologue done, wait
-  // released, consumers done] in globaltimer nanoseconds
+  // timeline tracing (nullable): 8 slots per CTA in globaltimer nanoseconds:
+  // entry, activations staged, wait released, consumers done, and for the
+  // RMSNorm prologue: first token's rows loaded, norm factor ready, warp 0's
+  // and the last warp's rows quantized
   uint64_t* trace;
 };
 // fmt: FMT_*; scale_f16: weight scale type. Chooses NT from a.ntok.
@@ -169,8 +171,8 @@ struct AttnDecodeArgs {
   float* out;             // [n_heads*head_size] f32 (nullable)
   int8_t* q8;             // (nullable)
   float* s8;
-  // timeline tracing (nullable): per CTA [entry, wait released, partials
-  // visible, done] in globaltimer nanoseconds
+  // timeline tracing (nullable): 8 slots per CTA in globaltimer nanoseconds:
+  // entry, wait released, partials visible, done
   uint64_t* trace;
 };
 // Cluster size for the decode attention: 16 when n_kv_heads clusters of 16

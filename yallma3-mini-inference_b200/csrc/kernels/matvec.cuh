@@ -159,6 +159,7 @@ __device__ __forceinline__ void mv_norm_regs(const MvArgs& a, const MvLayout& L,
         ss = fmaf(xv[u].w, xv[u].w, ss);
       }
       ss = warp_sum(ss);
+      if (a.trace && t == 0 && ctid == 0) a.trace[(uint64_t)blockIdx.x * 8 + 4] = globaltimer();
       if (lane == 0) red[cw] = ss;
       named_bar_sync(1, MV_NCW * 32);
       float tot = 0.0f;
@@ -168,82 +169,105 @@ __device__ __forceinline__ void mv_norm_regs(const MvArgs& a, const MvLayout& L,
       r = __fadd_rn(r, a.eps);
       r = __fdiv_rn(1.0f, __fsqrt_rn(r));
       named_bar_sync(1, MV_NCW * 32);  // red[] reused by the next token
+      if (a.trace && t == 0 && ctid == 0) a.trace[(uint64_t)blockIdx.x * 8 + 5] = globaltimer();
     }
+    // y = w * (r * x) in place
 #pragma unroll
     for (int u = 0; u < MU; ++u) {
-      const uint32_t i = ctid * 4 + u * MV_NCW * 32 * 4;
-      if (u * MV_NCW * 32 * 4 >= K) break;  // uniform across the CTA
-      const bool in = i < K;
-      float y[4];
       if (NORM) {
-        y[0] = __fmul_rn(wv[u].x, __fmul_rn(r, xv[u].x));
-        y[1] = __fmul_rn(wv[u].y, __fmul_rn(r, xv[u].y));
-        y[2] = __fmul_rn(wv[u].z, __fmul_rn(r, xv[u].z));
-        y[3] = __fmul_rn(wv[u].w, __fmul_rn(r, xv[u].w));
-      } else {
-        y[0] = xv[u].x;
-        y[1] = xv[u].y;
-        y[2] = xv[u].z;
-        y[3] = xv[u].w;
+        xv[u].x = __fmul_rn(wv[u].x, __fmul_rn(r, xv[u].x));
+        xv[u].y = __fmul_rn(wv[u].y, __fmul_rn(r, xv[u].y));
+        xv[u].z = __fmul_rn(wv[u].z, __fmul_rn(r, xv[u].z));
+        xv[u].w = __fmul_rn(wv[u].w, __fmul_rn(r, xv[u].w));
       }
-      if (mv_f32_act<FMT>()) {
-        if (in) *reinterpret_cast<float4*>(reinterpret_cast<float*>(smem + L.x_off) + t * K + i) =
-            make_float4(y[0], y[1], y[2], y[3]);
-        continue;
-      }
-      // quantization.rs:29-52 over the block held by lanes 8g..8g+7
-      float m = 0.0f;
+    }
+    if (mv_f32_act<FMT>()) {
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float av = fabsf(y[e]);
-        m = fmaxf(m, av > 0.0f ? av : 0.0f);  // NaN never becomes the max
+      for (int u = 0; u < MU; ++u) {
+        const uint32_t i = ctid * 4 + u * MV_NCW * 32 * 4;
+        if (i < K) *reinterpret_cast<float4*>(reinterpret_cast<float*>(smem + L.x_off) + t * K + i) = xv[u];
       }
-      m = fmaxf(m, __shfl_xor_sync(FULL, m, 4));
-      m = fmaxf(m, __shfl_xor_sync(FULL, m, 2));
-      m = fmaxf(m, __shfl_xor_sync(FULL, m, 1));
-      const float sc = __fdiv_rn(m, 127.0f);
-      const float isc = __frcp_rn(sc);
-      uint32_t word = 0;
-      int qs = 0;
+      continue;
+    }
+    // quantization.rs:29-52 over the blocks held by lanes 8g..8g+7, four
+    // slots at a time with every step interleaved across the slots (the
+    // shuffle, divide and rounding chains overlap instead of running in turn)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int8_t q = rust_as_i8(round_quot(y[e], sc, isc));
-        word |= (uint32_t)(uint8_t)q << (8 * e);
-        qs += q;
+    for (int u0 = 0; u0 < MU; u0 += 4) {
+      if (u0 * MV_NCW * 32 * 4 >= K) break;  // uniform across the CTA
+      float m[4], sc[4], isc[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float4 y = xv[u0 + j];
+        float mm = 0.0f;
+        mm = fmaxf(mm, fabsf(y.x) > 0.0f ? fabsf(y.x) : 0.0f);  // NaN never becomes the max
+        mm = fmaxf(mm, fabsf(y.y) > 0.0f ? fabsf(y.y) : 0.0f);
+        mm = fmaxf(mm, fabsf(y.z) > 0.0f ? fabsf(y.z) : 0.0f);
+        mm = fmaxf(mm, fabsf(y.w) > 0.0f ? fabsf(y.w) : 0.0f);
+        m[j] = mm;
       }
-      const uint32_t b = i / 32, e0 = i % 32;  // block and first element within it
-      int8_t* xq = reinterpret_cast<int8_t*>(smem + L.x_off) + t * K;
-      if (FMT == FMT_Q4) {
-        qs += __shfl_xor_sync(FULL, qs, 4);
-        qs += __shfl_xor_sync(FULL, qs, 2);
-        qs += __shfl_xor_sync(FULL, qs, 1);
-        const uint32_t off = e0 < 16 ? b * 16 + e0 : nb * 16 + b * 16 + (e0 - 16);
-        if (in) *reinterpret_cast<uint32_t*>(xq + off) = word;
-        if (in && e0 == 0) reinterpret_cast<int*>(smem + L.xsum_off)[t * nb + b] = qs;
-      } else if (FMT == FMT_Q8X) {
-        // limbs 1 and 2 refine the Q8_0 value a: y - s*a = (s/254)*b + (s/254^2)*c + e
-        const float inv = __fdiv_rn(254.0f, sc);  // +inf for an all-zero block: limbs become 0
-        const float s1 = sc * (1.0f / 254.0f);
-        uint32_t w1 = 0, w2 = 0;
+#pragma unroll
+      for (int o = 4; o > 0; o >>= 1)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) m[j] = fmaxf(m[j], __shfl_xor_sync(FULL, m[j], o));
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        sc[j] = __fdiv_rn(m[j], 127.0f);
+        isc[j] = __frcp_rn(sc[j]);
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int u = u0 + j;
+        const uint32_t i = ctid * 4 + u * MV_NCW * 32 * 4;
+        const bool in = i < K;
+        const float y[4] = {xv[u].x, xv[u].y, xv[u].z, xv[u].w};
+        uint32_t word = 0;
+        int qs = 0;
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const int8_t q0 = (int8_t)(word >> (8 * e));
-          const float r1 = fmaf(-(float)q0, sc, y[e]);
-          const int8_t q1 = rust_as_i8(roundf(r1 * inv));
-          const float r2 = fmaf(-(float)q1, s1, r1);
-          const int8_t q2 = rust_as_i8(roundf(r2 * inv * 254.0f));
-          w1 |= (uint32_t)(uint8_t)q1 << (8 * e);
-          w2 |= (uint32_t)(uint8_t)q2 << (8 * e);
+          const int8_t q = rust_as_i8(round_quot(y[e], sc[j], isc[j]));
+          word |= (uint32_t)(uint8_t)q << (8 * e);
+          qs += q;
         }
-        if (in) {
-          *reinterpret_cast<uint32_t*>(xq + i) = word;
-          *reinterpret_cast<uint32_t*>(xq + NT * K + i) = w1;
-          *reinterpret_cast<uint32_t*>(xq + 2 * NT * K + i) = w2;
+        const uint32_t b = i / 32, e0 = i % 32;  // block and first element within it
+        int8_t* xq = reinterpret_cast<int8_t*>(smem + L.x_off) + t * K;
+        if (FMT == FMT_Q4) {
+          qs += __shfl_xor_sync(FULL, qs, 4);
+          qs += __shfl_xor_sync(FULL, qs, 2);
+          qs += __shfl_xor_sync(FULL, qs, 1);
+          const uint32_t off = e0 < 16 ? b * 16 + e0 : nb * 16 + b * 16 + (e0 - 16);
+          if (in) *reinterpret_cast<uint32_t*>(xq + off) = word;
+          if (in && e0 == 0) reinterpret_cast<int*>(smem + L.xsum_off)[t * nb + b] = qs;
+        } else if (FMT == FMT_Q8X) {
+          // limbs 1 and 2 refine the Q8_0 value a: y - s*a = (s/254)*b + (s/254^2)*c + e
+          const float inv = __fdiv_rn(254.0f, sc[j]);  // +inf for an all-zero block: limbs become 0
+          const float s1 = sc[j] * (1.0f / 254.0f);
+          uint32_t w1 = 0, w2 = 0;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int8_t q0 = (int8_t)(word >> (8 * e));
+            const float r1 = fmaf(-(float)q0, sc[j], y[e]);
+            const int8_t q1 = rust_as_i8(roundf(r1 * inv));
+            const float r2 = fmaf(-(float)q1, s1, r1);
+            const int8_t q2 = rust_as_i8(roundf(r2 * inv * 254.0f));
+            w1 |= (uint32_t)(uint8_t)q1 << (8 * e);
+            w2 |= (uint32_t)(uint8_t)q2 << (8 * e);
+          }
+          if (in) {
+            *reinterpret_cast<uint32_t*>(xq + i) = word;
+            *reinterpret_cast<uint32_t*>(xq + NT * K + i) = w1;
+            *reinterpret_cast<uint32_t*>(xq + 2 * NT * K + i) = w2;
+          }
+        } else {
+          if (in) *reinterpret_cast<uint32_t*>(xq + i) = word;
         }
-      } else {
-        if (in) *reinterpret_cast<uint32_t*>(xq + i) = word;
+        if (in && e0 == 0) reinterpret_cast<float*>(smem + L.xs_off)[t * nb + b] = sc[j];
       }
-      if (in && e0 == 0) reinterpret_cast<float*>(smem + L.xs_off)[t * nb + b] = sc;
+    }
+    if (a.trace && t == 0 && lane == 0) {  // this warp's rows quantized: warp 0, and the last warp
+      const unsigned long long now = globaltimer();
+      if (cw == 0) a.trace[(uint64_t)blockIdx.x * 8 + 6] = now;
+      atomicMax(reinterpret_cast<unsigned long long*>(a.trace + (uint64_t)blockIdx.x * 8 + 7), now);
     }
   }
 }
@@ -255,6 +279,10 @@ __device__ __forceinline__ void mv_stage_x(const MvArgs& a, const MvLayout& L, u
   const uint32_t K = a.K, nb = K / 32;
   const int ctid = cw * 32 + lane;
   float* red = reinterpret_cast<float*>(smem + L.red_off);
+  if (a.pro == PRO_NORM && K <= 4 * MV_NCW * 32 * 4) {  // K <= 4096: four float4 per thread
+    mv_norm_regs<FMT, NT, true, 4>(a, L, smem, cw, lane);
+    return;
+  }
   if (a.pro == PRO_NORM && K <= MV_NORM_MU * MV_NCW * 32 * 4) {
     mv_norm_regs<FMT, NT, true, MV_NORM_MU>(a, L, smem, cw, lane);
     return;
@@ -673,7 +701,7 @@ __global__ void __launch_bounds__(MV_THREADS, (NT <= 2 ? 2 : 1)) mv_kernel(MvArg
   const uint32_t nrs = (r_end - r_begin + RS - 1) / RS;
   const uint32_t nrounds = (nrs + G - 1) / G;
 
-  uint64_t* const trace = a.trace ? a.trace + (uint64_t)blockIdx.x * 4 : nullptr;
+  uint64_t* const trace = a.trace ? a.trace + (uint64_t)blockIdx.x * 8 : nullptr;
   if (trace && threadIdx.x == 0) trace[0] = globaltimer();
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
