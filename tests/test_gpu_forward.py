@@ -149,6 +149,31 @@ def test_long_context_decode_matches_oracle(yl, orc, model_factory, preset):
     assert dev_ids == host_ids
 
 
+def test_wide_ffn_dynamic_schedule_matches_oracle(yl, orc, model_factory):
+    """A feed-forward and vocabulary wide enough (32768 gate/up rows, 16384
+    logits) that single-token passes hand out 8-row sets dynamically: the
+    gate/up + SwiGLU + h-quantize launch (h blocks completed across CTAs) and
+    the lm_head + argmax launch, against the oracle and graph vs host loop."""
+    path = model_factory("tiny", hidden_dim=16384, vocab_size=16384)
+    prompt = yl.prompt_ids(16384, 9, 4321).tolist()
+    errs, gids, oids, _, _ = run_pair(yl, orc, path, prompt, 12, 256)
+    olg = run_pair.oracle_logits
+    sens = oracle_sensitivity(orc, path, prompt, oids, 256)
+    assert max(errs) < bound_for(sens), (errs, sens)
+    assert_ids_match(gids, oids, olg, bound_for(sens))
+    gm = yl.load_transformer(path, max_ctx_len=256)
+    s1 = gm.create_session()
+    _, first = gm.forward_x_full(prompt, 0, s1, want_logits=False)
+    dev_ids = gm.decode_greedy(s1, first, len(prompt), 24).tolist()
+    s2 = gm.create_session()
+    _, tok = gm.forward_x_full(prompt, 0, s2, want_logits=False)
+    host_ids = []
+    for i in range(24):
+        _, tok = gm.forward_x_full([tok], len(prompt) + i, s2, want_logits=False)
+        host_ids.append(tok)
+    assert dev_ids == host_ids
+
+
 def test_prefill_equals_stepwise_on_device(yl, model_factory):
     path = model_factory("tiny")
     gm = yl.load_transformer(path, max_ctx_len=256)

@@ -584,6 +584,9 @@ int session_create(const Model* m, Session** out) {
   s->n_splits = k::attention_decode_splits(sh.n_kv_heads, sh.head_size);
   if ((rc = salloc(s.get(), (uint64_t)sh.n_heads * s->n_splits * (sh.head_size + 2) * 4, &p))) return rc;
   s->part = (float*)p;
+  if ((rc = salloc(s.get(), ((uint64_t)sh.n_layers + 1) * 2 * 4, &p))) return rc;
+  s->work = (unsigned int*)p;
+  YL_CUDA_TRY(cudaMemset(s->work, 0, ((uint64_t)sh.n_layers + 1) * 2 * 4));
   if ((rc = salloc(s.get(), ((uint64_t)sh.ctx_len + 1) * 4, &p))) return rc;
   s->hist = (uint32_t*)p;
   const uint64_t am_slots = (uint64_t)m->num_sms * 8;
@@ -683,6 +686,7 @@ int run_matvec_ex(const DevWeight& w, bool f32act, const int8_t* xq, const float
     a.am_out = ex.am_out;
     a.state = ex.state;
     a.trace = ex.trace;
+    a.work = ex.work;
     cudaError_t e = k::matvec(a, fmt, w.sf16, epi, lc);
     if (e != cudaSuccess) return fail(YL_ERR_CUDA, std::string("matvec launch: ") + cudaGetErrorString(e));
     if (launches) ++*launches;
@@ -754,6 +758,7 @@ int enqueue_forward(Session* s, uint32_t n, uint32_t start_pos, bool from_state,
     norm.hs = nullptr;
     norm.hcount = nullptr;
     norm.trace = YL_TRACE();
+    norm.work = nullptr;
     if ((rc = run_matvec_ex(L.wqkv, f32act, nullptr, nullptr, nullptr, d, d / 32, n, s->qkv, att + 2 * kvd,
                             k::EPI_STORE, 0, s->err, s->stream, pdl, m->num_sms, norm, &nl)))
       return rc;
@@ -815,6 +820,7 @@ int enqueue_forward(Session* s, uint32_t n, uint32_t start_pos, bool from_state,
     norm.hs = f32act ? nullptr : s->hs;
     norm.hcount = f32act ? nullptr : s->hcount;
     norm.trace = YL_TRACE();
+    norm.work = decode ? s->work + 2ull * l : nullptr;  // one launch per step at this site
     if ((rc = run_matvec_ex(L.w13, f32act, nullptr, nullptr, nullptr, d, d / 32, n, s->h, f,
                             f32act ? k::EPI_SWIGLU : k::EPI_SWIGLU_Q8, 0, s->err, s->stream, pdl, m->num_sms, norm,
                             &nl)))
@@ -838,6 +844,7 @@ int enqueue_forward(Session* s, uint32_t n, uint32_t start_pos, bool from_state,
     fin.am_out = s->hist;
     fin.state = from_state ? s->state : nullptr;
     fin.trace = YL_TRACE();
+    fin.work = s->work + 2ull * sh.n_layers;  // lm_head: one launch per forward
     if ((rc = run_matvec_ex(m->lm, true, nullptr, nullptr, nullptr, d, 0, 1, s->logits, sh.vocab_size, k::EPI_ARGMAX,
                             0, s->err, s->stream, pdl, m->num_sms, fin, &nl)))
       return rc;

@@ -69,6 +69,7 @@ struct Session {
   int8_t* hq = nullptr;   // [cap][ffn] quantized h (SwiGLU epilogue)
   float* hs = nullptr;    // [cap][ffn/32]
   unsigned int* hcount = nullptr;  // [cap][ffn/32] arrival counters (zero between launches)
+  unsigned int* work = nullptr;    // [n_layers + 1][2] dynamic row-set counters (decode gate/up, lm_head)
   uint32_t* tok = nullptr;  // [cap]
   float* logits = nullptr;  // [vocab]
   float* part = nullptr;    // attention split partials (general path)
@@ -137,6 +138,7 @@ struct MvExtra {
   uint32_t* am_out = nullptr;
   k::StepState* state = nullptr;
   uint64_t* trace = nullptr;   // timeline stamps of this launch (nullable)
+  unsigned int* work = nullptr;  // dynamic row-set counters of this launch site (nullable)
 };
 int run_matvec_ex(const DevWeight& w, bool f32act, const int8_t* xq, const float* xs, const float* xf,
                   uint64_t x_stride, uint64_t xs_stride, uint32_t ntok, float* out, uint64_t out_stride, int epi,

@@ -86,6 +86,10 @@ struct MvArgs {
   unsigned int* am_count;
   uint32_t* am_out;
   StepState* state;
+  // Dynamic scheduling (nullable): [next row set, CTAs done] counters, zero
+  // between launches; CTAs claim 8-row sets from it instead of a static range.
+  // Used by the launcher only for single-token passes with >= 4 sets per CTA.
+  unsigned int* work;
   // timeline tracing (nullable): 8 slots per CTA in globaltimer nanoseconds:
   // entry, activations staged, wait released, consumers done, and for the
   // RMSNorm prologue: first token's rows loaded, norm factor ready, warp 0's

@@ -48,10 +48,16 @@ __host__ __device__ constexpr bool mv_swiglu(int epi) { return epi == EPI_SWIGLU
 // its ring is split into two groups of four warps to keep two stages in the
 // budget; every other epilogue uses one group of eight warps.
 __host__ __device__ constexpr int mv_groups(int epi) { return mv_swiglu(epi) ? 2 : 1; }
+// Rows per stage (MV_NCW / groups warps x rows per warp): 8 for every epilogue.
+constexpr uint32_t MV_RS = 8;
+// Dynamic SwiGLU+quantize: row sets one CTA may take (its h blocks are
+// quantized from this list at the end).
+constexpr uint32_t MV_LIST = 32;
+constexpr uint32_t MV_END = 0xFFFFFFFFu;  // stage info: no more row sets
 
 // Shared-memory layout, computed identically on host and device.
 struct MvLayout {
-  uint32_t bar_off, red_off, x_off, xs_off, xsum_off, ring_off;
+  uint32_t bar_off, info_off, red_off, x_off, xs_off, xsum_off, ring_off;
   uint32_t stage_q_row, stage_s_row, stage_bytes, total;
 };
 // ssz: weight scale element size (2 for f16, 4 for f32). A stage's scale row
@@ -64,8 +70,9 @@ __host__ __device__ inline MvLayout mv_layout(uint32_t K, uint32_t kc, int rpw, 
                                              int groups = 1) {
   MvLayout L;
   L.bar_off = 0;       // 2 x 16 mbarriers
-  L.red_off = 256;     // reductions / argmax / h staging ([2][8][32] floats)
-  uint32_t off = 256 + 2048 + 128;
+  L.info_off = 256;    // per slot: first row and row count; row-set list (dynamic SwiGLU)
+  L.red_off = 768;     // reductions / argmax / h staging ([2][8][32] floats)
+  uint32_t off = 768 + 2048 + 128;
   L.x_off = off;
   if (mv_f32_act<FMT>()) {
     off += NT * K * 4;
@@ -129,6 +136,13 @@ __device__ __forceinline__ bool am_better(float v, uint32_t i, float bv, uint32_
 // rmsnorm_quant_kernel and the same per-element operations as
 // quant_q8_lane, so the bits equal the standalone kernels'.
 // NORM = false: the rows are quantized as they are (y = x, PRO_QUANT).
+// Consumers wait here for the kernel that produced the activations
+// (programmatic dependent launch); everything before it overlaps that kernel.
+__device__ __forceinline__ void mv_wait_inputs(const MvArgs& a) {
+  yl::dev::grid_dep_wait();
+  if (a.trace && threadIdx.x == 32) a.trace[(uint64_t)blockIdx.x * 8 + 2] = yl::dev::globaltimer();
+}
+
 constexpr int MV_NORM_MU = 8;    // float4 per thread with a norm (K <= 8192)
 constexpr int MV_QUANT_MU = 16;  // float4 per thread without (K <= 16384)
 template <int FMT, int NT, bool NORM, int MU>
@@ -137,16 +151,26 @@ __device__ __forceinline__ void mv_norm_regs(const MvArgs& a, const MvLayout& L,
   const uint32_t K = a.K, nb = K / 32;
   const int ctid = cw * 32 + lane;
   float* red = reinterpret_cast<float*>(smem + L.red_off);
+  // the norm weight is a constant of the model: fetched before the wait on
+  // the kernel that produces the rows
+  float4 wv[NORM ? MU : 1];
+  if (NORM) {
+#pragma unroll
+    for (int u = 0; u < MU; ++u) {
+      const uint32_t i = ctid * 4 + u * MV_NCW * 32 * 4;
+      wv[u] = i < K ? *reinterpret_cast<const float4*>(a.norm_w + i) : make_float4(0, 0, 0, 0);
+    }
+  }
+  mv_wait_inputs(a);
   for (int t = 0; t < NT; ++t) {
     const bool valid = t < (int)a.ntok;
     const float* xr = a.xres + (uint64_t)t * a.x_tok_stride;
-    float4 xv[MU], wv[NORM ? MU : 1];
+    float4 xv[MU];
 #pragma unroll
     for (int u = 0; u < MU; ++u) {
       const uint32_t i = ctid * 4 + u * MV_NCW * 32 * 4;
       const bool in = valid && i < K;
       xv[u] = in ? *reinterpret_cast<const float4*>(xr + i) : make_float4(0, 0, 0, 0);
-      if (NORM) wv[u] = in ? *reinterpret_cast<const float4*>(a.norm_w + i) : make_float4(0, 0, 0, 0);
     }
     float r = 1.0f;
     if (NORM) {
@@ -195,7 +219,7 @@ __device__ __forceinline__ void mv_norm_regs(const MvArgs& a, const MvLayout& L,
 #pragma unroll
     for (int u0 = 0; u0 < MU; u0 += 4) {
       if (u0 * MV_NCW * 32 * 4 >= K) break;  // uniform across the CTA
-      float m[4], sc[4], isc[4];
+      float m[4], sc[4], isc[4], lim[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const float4 y = xv[u0 + j];
@@ -210,10 +234,21 @@ __device__ __forceinline__ void mv_norm_regs(const MvArgs& a, const MvLayout& L,
       for (int o = 4; o > 0; o >>= 1)
 #pragma unroll
         for (int j = 0; j < 4; ++j) m[j] = fmaxf(m[j], __shfl_xor_sync(FULL, m[j], o));
+      // the four blocks' scale divisions are shared out: lane g*8 + j of a
+      // block group divides for slot j (every lane of the group holds all four
+      // maxima), then the results are broadcast within the group
+      {
+        const int j8 = lane & 7, src = lane & ~7;
+        const float mj = j8 == 0 ? m[0] : j8 == 1 ? m[1] : j8 == 2 ? m[2] : m[3];
+        const float scj = __fdiv_rn(mj, 127.0f);
+        const float iscj = __frcp_rn(scj);
+        const float lij = FMT == FMT_Q8X ? __fdiv_rn(254.0f, scj) : 0.0f;  // limb factor
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        sc[j] = __fdiv_rn(m[j], 127.0f);
-        isc[j] = __frcp_rn(sc[j]);
+        for (int j = 0; j < 4; ++j) {
+          sc[j] = __shfl_sync(FULL, scj, src | j);
+          isc[j] = __shfl_sync(FULL, iscj, src | j);
+          if (FMT == FMT_Q8X) lim[j] = __shfl_sync(FULL, lij, src | j);
+        }
       }
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
@@ -240,7 +275,7 @@ __device__ __forceinline__ void mv_norm_regs(const MvArgs& a, const MvLayout& L,
           if (in && e0 == 0) reinterpret_cast<int*>(smem + L.xsum_off)[t * nb + b] = qs;
         } else if (FMT == FMT_Q8X) {
           // limbs 1 and 2 refine the Q8_0 value a: y - s*a = (s/254)*b + (s/254^2)*c + e
-          const float inv = __fdiv_rn(254.0f, sc[j]);  // +inf for an all-zero block: limbs become 0
+          const float inv = lim[j];  // 254 / sc: +inf for an all-zero block, limbs become 0
           const float s1 = sc[j] * (1.0f / 254.0f);
           uint32_t w1 = 0, w2 = 0;
 #pragma unroll
@@ -291,6 +326,7 @@ __device__ __forceinline__ void mv_stage_x(const MvArgs& a, const MvLayout& L, u
     mv_norm_regs<FMT, NT, false, MV_QUANT_MU>(a, L, smem, cw, lane);
     return;
   }
+  mv_wait_inputs(a);
   if (a.pro == PRO_NORM) {
     for (int t = 0; t < NT; ++t) {
       const bool valid = t < (int)a.ntok;
@@ -682,24 +718,32 @@ __global__ void __launch_bounds__(MV_THREADS, (NT <= 2 ? 2 : 1)) mv_kernel(MvArg
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar_off);
   uint64_t* empty = full + S;
 
-  // Row range of this CTA: row pairs for SwiGLU (gate/up together).
+  // Row range: static split (row pairs for SwiGLU, gate/up together), or with
+  // a.work the whole matrix, its row sets handed out by an atomic counter.
+  const bool dyn = a.work != nullptr;
   const uint32_t unit = mv_swiglu(EPI) ? 2u : 1u;
   const uint64_t units = a.rows / unit;
-  const uint32_t r_begin = (uint32_t)(units * blockIdx.x / gridDim.x) * unit;
-  const uint32_t r_end = (uint32_t)(units * (blockIdx.x + 1) / gridDim.x) * unit;
+  const uint32_t r_begin = dyn ? 0u : (uint32_t)(units * blockIdx.x / gridDim.x) * unit;
+  const uint32_t r_end = dyn ? a.rows : (uint32_t)(units * (blockIdx.x + 1) / gridDim.x) * unit;
+  // stage info written by the producer before it arrives on the stage's full
+  // barrier: first row and row count (0: no rows, MV_END: no more stages)
+  uint32_t* info_row = reinterpret_cast<uint32_t*>(smem + L.info_off);
+  uint32_t* info_n = info_row + 16;
+  uint32_t* list = info_row + 32;  // [MV_LIST] first rows of this CTA's row sets (dynamic SwiGLU)
+  uint32_t* list_n = info_row + 32 + MV_LIST;
   // Stages carry row sets of RS rows (one consumer group's rows) and K-chunks.
   // Stage order: round p, chunk ch, group g (row set p*G + g), so consecutive
   // stages go to different groups and all groups consume concurrently; the
   // producer and every consumer walk the same nest and count stages in q.
   constexpr int WPG = MV_NCW / G;  // warps per group
+  static_assert(WPG * RPW == MV_RS, "a stage holds MV_RS rows");
   if (S % G != 0 || S > 16) {  // the launcher never plans this (parity aliasing)
-    if (threadIdx.x == 0 && a.err) atomicExch(a.err, 1);
+    if (threadIdx.x == 0 && a.err) atomicExch(a.err, ERR_BAD_ARG);
     return;
   }
   const uint32_t RS = WPG * RPW;
   const uint32_t nch = (K + kc - 1) / kc;
   const uint32_t nrs = (r_end - r_begin + RS - 1) / RS;
-  const uint32_t nrounds = (nrs + G - 1) / G;
 
   uint64_t* const trace = a.trace ? a.trace + (uint64_t)blockIdx.x * 8 : nullptr;
   if (trace && threadIdx.x == 0) trace[0] = globaltimer();
@@ -708,6 +752,7 @@ __global__ void __launch_bounds__(MV_THREADS, (NT <= 2 ? 2 : 1)) mv_kernel(MvArg
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], WPG);
     }
+    *list_n = 0;
     mbar_fence_init();
   }
   __syncthreads();
@@ -721,45 +766,90 @@ __global__ void __launch_bounds__(MV_THREADS, (NT <= 2 ? 2 : 1)) mv_kernel(MvArg
       // a stage's rows are then one contiguous range in both places.
       const bool contig = nch == 1 && L.stage_q_row == a.row_bytes &&
                           (!mv_has_scales<FMT>() || L.stage_s_row == a.scale_row_bytes);
-      uint32_t issued = 0, q = 0;
+      // q counts stages issued; bit s of datamask: slot s's latest stage
+      // carries copies (a stage with no rows or the closing stage has none)
+      uint32_t q = 0, nlist = 0, datamask = 0;
       bool ok = true;
-      for (uint32_t p = 0; ok && p < nrounds; ++p)
-      for (uint32_t ch = 0; ok && ch < nch; ++ch)
-      for (int g = 0; g < G; ++g) {
-        const uint32_t rs = p * G + g;
-        if (rs >= nrs) break;
-        const int slot = q % S;
-        const uint32_t ph = (q / S) & 1;
-        ++q;
-        if (!mbar_wait(&empty[slot], ph ^ 1, a.err)) { ok = false; break; }
-        const uint32_t row0 = r_begin + rs * RS;
-        const uint32_t nrows = min(RS, r_end - row0);
-        const uint32_t k0 = ch * kc, kn = min(kc, K - k0);
-        const uint32_t qb = mv_qbytes<FMT>(kn);
-        const uint32_t ssz = SF16 ? 2u : 4u;
-        const uint32_t sb = mv_has_scales<FMT>() ? ((kn / 32 * ssz + 15u) & ~15u) : 0u;
-        uint8_t* stage = smem + L.ring_off + slot * L.stage_bytes;
-        mbar_arrive_expect_tx(&full[slot], nrows * (qb + sb));
-        if (contig) {  // full rows: one copy for the quants, one for the scales
-          bulk_g2s(stage, a.wq + (uint64_t)row0 * a.row_bytes, nrows * qb, &full[slot], pol);
-          if (sb) bulk_g2s(stage + RS * L.stage_q_row, a.ws + (uint64_t)row0 * a.scale_row_bytes, nrows * sb,
-                           &full[slot], pol);
-          issued = q;
-          continue;
+      const bool listed = dyn && EPI == EPI_SWIGLU_Q8;
+      // rounds of G row sets (one per group); dynamic rounds are claimed one
+      // round ahead so the atomic's latency hides behind the copies
+      uint32_t base = dyn ? atomicAdd(a.work, (unsigned)G) : 0u;
+      for (uint32_t p = 0; ok; ++p) {
+        if (!dyn) base = p * G;
+        if (base >= nrs) {  // no more row sets: one closing stage per group
+          for (int g = 0; g < G; ++g) {
+            const int slot = q % S;
+            const uint32_t ph = (q / S) & 1;
+            if (!mbar_wait(&empty[slot], ph ^ 1, a.err)) { ok = false; break; }
+            ++q;
+            datamask &= ~(1u << slot);
+            info_n[slot] = MV_END;
+            mbar_arrive(&full[slot]);
+          }
+          break;
         }
-        for (uint32_t r = 0; r < nrows; ++r) {
-          const uint64_t row = row0 + r;
-          bulk_g2s(stage + r * L.stage_q_row, a.wq + row * a.row_bytes + mv_qbytes<FMT>(k0), qb, &full[slot], pol);
-          if (sb)
-            bulk_g2s(stage + RS * L.stage_q_row + r * L.stage_s_row,
-                     a.ws + row * a.scale_row_bytes + (k0 / 32) * ssz, sb, &full[slot], pol);
+        uint32_t next = nrs;
+        if (dyn && (!listed || nlist + 2u * G <= MV_LIST)) next = atomicAdd(a.work, (unsigned)G);
+        for (uint32_t ch = 0; ok && ch < nch; ++ch)
+        for (int g = 0; g < G; ++g) {
+          const uint32_t rs = base + g;
+          const int slot = q % S;
+          const uint32_t ph = (q / S) & 1;
+          if (!mbar_wait(&empty[slot], ph ^ 1, a.err)) { ok = false; break; }
+          ++q;
+          if (rs >= nrs) {  // this group has no row set in the last round
+            datamask &= ~(1u << slot);
+            info_n[slot] = 0;
+            mbar_arrive(&full[slot]);
+            continue;
+          }
+          datamask |= 1u << slot;
+          const uint32_t row0 = r_begin + rs * RS;
+          const uint32_t nrows = min(RS, r_end - row0);
+          info_row[slot] = row0;
+          info_n[slot] = nrows;
+          if (listed && ch == 0) list[nlist++] = row0;
+          const uint32_t k0 = ch * kc, kn = min(kc, K - k0);
+          const uint32_t qb = mv_qbytes<FMT>(kn);
+          const uint32_t ssz = SF16 ? 2u : 4u;
+          const uint32_t sb = mv_has_scales<FMT>() ? ((kn / 32 * ssz + 15u) & ~15u) : 0u;
+          uint8_t* stage = smem + L.ring_off + slot * L.stage_bytes;
+          mbar_arrive_expect_tx(&full[slot], nrows * (qb + sb));
+          if (contig) {  // full rows: one copy for the quants, one for the scales
+            bulk_g2s(stage, a.wq + (uint64_t)row0 * a.row_bytes, nrows * qb, &full[slot], pol);
+            if (sb) bulk_g2s(stage + RS * L.stage_q_row, a.ws + (uint64_t)row0 * a.scale_row_bytes, nrows * sb,
+                             &full[slot], pol);
+            continue;
+          }
+          for (uint32_t r = 0; r < nrows; ++r) {
+            const uint64_t row = row0 + r;
+            bulk_g2s(stage + r * L.stage_q_row, a.wq + row * a.row_bytes + mv_qbytes<FMT>(k0), qb, &full[slot], pol);
+            if (sb)
+              bulk_g2s(stage + RS * L.stage_q_row + r * L.stage_s_row,
+                       a.ws + row * a.scale_row_bytes + (k0 / 32) * ssz, sb, &full[slot], pol);
+          }
         }
-        issued = q;
+        if (listed) *list_n = nlist;
+        base = next;
       }
-      // Drain: no bulk copy may still target this CTA's shared memory at exit.
-      // In a healthy run every issued stage was consumed, so this returns at once.
-      for (uint32_t it = issued > (uint32_t)S ? issued - S : 0; it < issued; ++it)
-        mbar_wait(&full[it % S], (it / S) & 1, a.err, 100000000ull);
+      if (dyn) {  // the last CTA to finish claiming resets the counters for the next launch
+        __threadfence();
+        if (atomicAdd(a.work + 1, 1u) == gridDim.x - 1) {
+          atomicExch(a.work, 0u);
+          atomicExch(a.work + 1, 0u);
+        }
+      }
+      // Drain: no bulk copy may still target this CTA's shared memory at exit
+      // (consumers that timed out may have left). A slot whose latest stage
+      // carries copies is waited on with that stage's parity (its latest
+      // phase, so the parity is unambiguous); a slot whose latest stage has
+      // none was released by its consumers before reuse, so its copies landed.
+      // In a healthy run every stage was consumed and this returns at once.
+      for (int s2 = 0; s2 < S; ++s2) {
+        if (!((datamask >> s2) & 1u)) continue;
+        const uint32_t ql = q - 1 - ((q - 1 - (uint32_t)s2) % (uint32_t)S);  // latest stage on slot s2
+        mbar_wait(&full[s2], (ql / S) & 1, a.err, 100000000ull);
+      }
     }
     grid_dep_wait();  // every thread of the grid waits before exit (keeps PDL chains transitive)
     return;
@@ -767,9 +857,7 @@ __global__ void __launch_bounds__(MV_THREADS, (NT <= 2 ? 2 : 1)) mv_kernel(MvArg
 
   // ---------------- consumers ----------------
   const int cw = warp - 1;
-  grid_dep_wait();
-  if (trace && threadIdx.x == 32) trace[2] = globaltimer();
-  mv_stage_x<FMT, NT>(a, L, smem, cw, lane);
+  mv_stage_x<FMT, NT>(a, L, smem, cw, lane);  // waits for the producing kernel inside
   named_bar_sync(1, MV_NCW * 32);
   if (trace && threadIdx.x == 32) trace[1] = globaltimer();
 
@@ -783,32 +871,34 @@ __global__ void __launch_bounds__(MV_THREADS, (NT <= 2 ? 2 : 1)) mv_kernel(MvArg
 
   // After a wait timeout the warp stops waiting and computing ("dead") but
   // keeps walking the loop so every named barrier below is still reached.
-  bool dead = false;
+  // A warp that times out on a wait stops (the error flag is set) and goes on
+  // to the named barriers below, which every consumer warp reaches.
   const int grp = cw / WPG, wi = cw % WPG;
   uint32_t q = 0;
-  for (uint32_t p = 0; p < nrounds; ++p)
-  for (uint32_t ch = 0; ch < nch; ++ch)
+  for (bool fin = false; !fin;)
+  for (uint32_t ch = 0; !fin && ch < nch; ++ch)
   for (int g = 0; g < G; ++g) {
-    const uint32_t rs = p * G + g;
-    if (rs >= nrs) break;
     const int slot = q % S;
     const uint32_t ph = (q / S) & 1;
     ++q;
     if (g != grp) continue;
-    if (!dead && !mbar_wait(&full[slot], ph, a.err)) dead = true;
-    const uint32_t row0 = r_begin + rs * RS;
+    if (!mbar_wait(&full[slot], ph, a.err)) { fin = true; break; }
+    const uint32_t n = info_n[slot];
+    if (n == MV_END) { fin = true; break; }
+    const uint32_t row0 = info_row[slot];
+    const uint32_t rend = row0 + n;  // rows of this stage: [row0, rend)
     const uint32_t k0 = ch * kc, kn = min(kc, K - k0);
     const uint8_t* stage = smem + L.ring_off + slot * L.stage_bytes;
 #pragma unroll
     for (int rr = 0; rr < RPW; ++rr) {
       const uint32_t rl = wi * RPW + rr;
-      if (dead || row0 + rl >= r_end) continue;
+      if (rl >= n) continue;
       mv_row_chunk<FMT, NT, SF16>(stage + rl * L.stage_q_row, stage + RS * L.stage_q_row + rl * L.stage_s_row, smem,
                                   L, K, k0, kn, lane, acc[rr]);
     }
     __syncwarp();
-    if (lane == 0 && !dead) mbar_arrive(&empty[slot]);
-    if (ch != nch - 1) continue;
+    if (lane == 0) mbar_arrive(&empty[slot]);
+    if (n == 0 || ch != nch - 1) continue;
 
     // ---- epilogue for this warp's rows of the finished row set ----
 #pragma unroll
@@ -817,7 +907,7 @@ __global__ void __launch_bounds__(MV_THREADS, (NT <= 2 ? 2 : 1)) mv_kernel(MvArg
       for (int rr = 0; rr < RPW; ++rr) acc[rr][t] = warp_sum(acc[rr][t]);
     if (mv_swiglu(EPI)) {
       const uint32_t r = row0 + wi * RPW;  // gate row (even), up row = r + 1
-      const bool have = r + 1 < r_end;
+      const bool have = r + 1 < rend;
       float hv[NT];
 #pragma unroll
       for (int t = 0; t < NT; ++t) hv[t] = have ? silu_mul(acc[0][t], acc[1][t]) : 0.0f;
@@ -830,7 +920,7 @@ __global__ void __launch_bounds__(MV_THREADS, (NT <= 2 ? 2 : 1)) mv_kernel(MvArg
 #pragma unroll
       for (int rr = 0; rr < RPW; ++rr) {
         const uint32_t r = row0 + wi * RPW + rr;
-        if (r >= r_end) continue;
+        if (r >= rend) continue;
         if (EPI == EPI_ARGMAX) {
           const float v = acc[rr][0];
           if (v == v && am_better(v, r, am_v, am_i)) {
@@ -857,40 +947,71 @@ __global__ void __launch_bounds__(MV_THREADS, (NT <= 2 ? 2 : 1)) mv_kernel(MvArg
   }
 
   if (EPI == EPI_SWIGLU_Q8) {
-    // Quantize h (quantization.rs:29-52, forward.rs:240) once, here: this
-    // CTA's h range [j0, j1) is in global memory. Blocks of 32 inside the
-    // range are quantized now; a block shared with a neighbouring CTA is
-    // quantized by whichever CTA completes it (arrival count reaches 32).
-    __shared__ int sw_last[2];
-    const uint32_t hn = a.rows / 2, j0 = r_begin / 2, j1 = r_end / 2;
-    const uint32_t b0 = j0 / 32, b1 = (j1 + 31) / 32;  // blocks touched
+    // Quantize h (quantization.rs:29-52, forward.rs:240) once, here, from the
+    // h values in global memory: a block of 32 is quantized by the CTA whose
+    // arrival completes it (per-block arrival counters, reset by that CTA).
+    const uint32_t hn = a.rows / 2;
     __threadfence();
     named_bar_sync(1, MV_NCW * 32);
-    for (int t = 0; t < (int)a.ntok && t < NT; ++t) {
-      if (cw == 0 && lane < 2) {
-        // boundary blocks: first (lane 0) and last (lane 1), when partial
-        const uint32_t b = lane == 0 ? b0 : b1 - 1;
-        const uint32_t lo = max(j0, b * 32), hi = min(j1, b * 32 + 32);
-        const bool partial = hi - lo < 32 && (lane == 0 || b1 - 1 != b0);
-        int last = 0;
-        if (partial) last = atomicAdd(a.hcount + (uint64_t)t * (hn / 32) + b, hi - lo) + (hi - lo) == 32;
-        sw_last[lane] = partial ? last : 1;
-      }
-      named_bar_sync(1, MV_NCW * 32);
-      for (uint32_t b = b0 + cw; b < b1; b += MV_NCW) {
-        const bool first = b == b0, lastb = b == b1 - 1;
-        if ((first && !sw_last[0]) || (lastb && !sw_last[1])) continue;  // a neighbour finishes it
-        if (first || lastb) __threadfence();  // see the neighbour's h values
-        const uint64_t hk = (uint64_t)t * hn + b * 32 + lane;
-        float sc;
-        const int8_t qv = quant_q8_lane(__ldcg(a.out + (uint64_t)t * a.out_tok_stride + b * 32 + lane), &sc);
-        a.hq[hk] = qv;
-        if (lane == 0) {
-          a.hs[hk / 32] = sc;
-          if (b * 32 < j0 || b * 32 + 32 > j1) a.hcount[(uint64_t)t * (hn / 32) + b] = 0u;  // for the next launch
+    if (dyn) {
+      // every listed row set holds RS/2 consecutive h values of one block
+      uint32_t* done_b = reinterpret_cast<uint32_t*>(smem + L.red_off);  // [MV_LIST]
+      const uint32_t nl = *list_n;
+      const int ctid = cw * 32 + lane;
+      for (int t = 0; t < (int)a.ntok && t < NT; ++t) {
+        if (ctid < (int)nl) {
+          const uint32_t b = list[ctid] / 64;
+          const unsigned prev = atomicAdd(a.hcount + (uint64_t)t * (hn / 32) + b, RS / 2);
+          done_b[ctid] = prev + RS / 2 == 32 ? b : MV_END;
         }
+        named_bar_sync(1, MV_NCW * 32);
+        for (uint32_t i = cw; i < nl; i += MV_NCW) {
+          const uint32_t b = done_b[i];
+          if (b == MV_END) continue;
+          __threadfence();  // see the other CTAs' h values
+          const uint64_t hk = (uint64_t)t * hn + b * 32 + lane;
+          float sc;
+          const int8_t qv = quant_q8_lane(__ldcg(a.out + (uint64_t)t * a.out_tok_stride + b * 32 + lane), &sc);
+          a.hq[hk] = qv;
+          if (lane == 0) {
+            a.hs[hk / 32] = sc;
+            a.hcount[(uint64_t)t * (hn / 32) + b] = 0u;  // for the next launch
+          }
+        }
+        named_bar_sync(1, MV_NCW * 32);
       }
-      named_bar_sync(1, MV_NCW * 32);
+    } else {
+      // this CTA's h range is [j0, j1): blocks inside it are quantized now, a
+      // block shared with a neighbouring CTA by whichever completes it
+      __shared__ int sw_last[2];
+      const uint32_t j0 = r_begin / 2, j1 = r_end / 2;
+      const uint32_t b0 = j0 / 32, b1 = (j1 + 31) / 32;  // blocks touched
+      for (int t = 0; t < (int)a.ntok && t < NT; ++t) {
+        if (cw == 0 && lane < 2) {
+          // boundary blocks: first (lane 0) and last (lane 1), when partial
+          const uint32_t b = lane == 0 ? b0 : b1 - 1;
+          const uint32_t lo = max(j0, b * 32), hi = min(j1, b * 32 + 32);
+          const bool partial = hi - lo < 32 && (lane == 0 || b1 - 1 != b0);
+          int last = 0;
+          if (partial) last = atomicAdd(a.hcount + (uint64_t)t * (hn / 32) + b, hi - lo) + (hi - lo) == 32;
+          sw_last[lane] = partial ? last : 1;
+        }
+        named_bar_sync(1, MV_NCW * 32);
+        for (uint32_t b = b0 + cw; b < b1; b += MV_NCW) {
+          const bool first = b == b0, lastb = b == b1 - 1;
+          if ((first && !sw_last[0]) || (lastb && !sw_last[1])) continue;  // a neighbour finishes it
+          if (first || lastb) __threadfence();  // see the neighbour's h values
+          const uint64_t hk = (uint64_t)t * hn + b * 32 + lane;
+          float sc;
+          const int8_t qv = quant_q8_lane(__ldcg(a.out + (uint64_t)t * a.out_tok_stride + b * 32 + lane), &sc);
+          a.hq[hk] = qv;
+          if (lane == 0) {
+            a.hs[hk / 32] = sc;
+            if (b * 32 < j0 || b * 32 + 32 > j1) a.hcount[(uint64_t)t * (hn / 32) + b] = 0u;  // for the next launch
+          }
+        }
+        named_bar_sync(1, MV_NCW * 32);
+      }
     }
   }
 
@@ -994,6 +1115,15 @@ cudaError_t mv_launch(const MvArgs& a0, int epi, const LaunchCfg& lc) {
   const uint32_t smem = L0.total + stages * L0.stage_bytes;
   if (smem > 227u * 1024u) return cudaErrorInvalidConfiguration;
   if (epi == EPI_ARGMAX && nt != 1) return cudaErrorInvalidValue;
+  {
+    // dynamic row sets pay off with several row sets per CTA; the SwiGLU+
+    // quantize tail needs every row set whole and at most MV_LIST per CTA
+    const uint32_t g = lc.grid ? lc.grid : 148;
+    const uint32_t nrs = (a.rows + MV_RS - 1) / MV_RS;
+    bool ok = a.work && nt == 1 && a.ntok == 1 && nrs >= 4 * g;
+    if (epi == EPI_SWIGLU_Q8) ok = ok && a.rows % MV_RS == 0 && nrs <= g * (MV_LIST / 2);
+    if (!ok) a.work = nullptr;
+  }
   if (epi == EPI_SWIGLU_Q8 && (a.rows % 64 || mv_f32_act<FMT>())) return cudaErrorInvalidValue;
   if (a.pro == PRO_QUANT && (a.K > MV_QUANT_MU * MV_NCW * 32 * 4 || mv_f32_act<FMT>())) return cudaErrorInvalidValue;
   // three-limb activations are produced only by the register RMSNorm prologue
