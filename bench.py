@@ -44,6 +44,7 @@ sys.path.insert(0, str(ROOT))
 PKG = "yallma3-mini-inference_b200"
 PROMPT_LEN = 512
 CONFIG = "c4"
+TRAFFIC_GATEUP_BYTES = 129.02e6
 
 
 def measured_peaks() -> dict:
@@ -221,6 +222,43 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def profile_case(case: str) -> None:
+    """Small fixed workloads for ncu captures (printed results are not bench
+    values). `matvec:ROWSxK`: three batch-1 Q8_0 matvecs of that shape with
+    random weights (the bench's dominant kernel at 28672x4096). `decode4`: a
+    4-layer config-4-shaped model, prompt 8, then 4 decode steps launched
+    kernel by kernel (no graph)."""
+    import torch
+    yl = importlib.import_module(PKG)
+    torch.cuda.set_device(0)
+    rng = np.random.default_rng(0)
+    if case.startswith("matvec:"):
+        o, n = (int(v) for v in case.split(":", 1)[1].split("x"))
+        w = yl.QuantizedTensor.weight(yl.WeightFormat.Q8_0, o, n, 32, 1)
+        w.upload(quant_vals=rng.integers(-127, 128, o * n, dtype=np.int8),
+                 scale_factor=(np.abs(rng.standard_normal(o * n // 32)) * 1e-3).astype(np.float32))
+        xa = yl.new_workspace_buffer(yl.WeightFormat.Q8_0, n, 32)
+        yl.quantize(yl.WeightFormat.Q8_0, xa, torch.tensor(rng.standard_normal(n).astype(np.float32), device="cuda"),
+                    n, 32)
+        out = torch.zeros(o, device="cuda")
+        for _ in range(3):
+            yl.matmul(out, xa, w, n, o, 32, batch=1, accumulate=False)
+    elif case == "decode4":
+        path = os.path.join(os.environ.get("YL_BENCH_DIR", "/tmp"), "yl_c4_4layers.gguf")
+        if not os.path.exists(path):
+            yl.synth_preset(CONFIG, path, n_layers=4)
+        m = yl.load_transformer(path, max_ctx_len=1024)
+        s = m.create_session()
+        prompt = yl.prompt_ids(yl.PRESETS[CONFIG]["vocab_size"], 8, 1).tolist()
+        _, tok = m.forward_x_full(prompt, 0, s, want_logits=False)
+        for i in range(4):
+            _, tok = m.forward_x_full([tok], len(prompt) + i, s, want_logits=False)
+    else:
+        raise SystemExit(f"unknown --case {case}")
+    torch.cuda.synchronize()
+    print(json.dumps({"case": case, "ok": True}))
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -230,7 +268,11 @@ def main() -> None:
     ap.add_argument("--e2e-steps", type=int, default=128)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-tokens", type=int, default=3)
+    ap.add_argument("--case", default=None, help="profiling workload (matvec:ROWSxK or decode4), no bench line")
     args = ap.parse_args()
+    if args.case:
+        profile_case(args.case)
+        return
     if args.impl == "reference":
         run_reference(args)
         return
@@ -317,7 +359,10 @@ def main() -> None:
                 "call": "yl_forward_x (Transformer::forward_x), logits + greedy id to host"},
         "roofline": {"bound": "hbm", "kernel": "mv_kernel<Q8,NT=1> gate/up 28672x4096",
                      "achieved": mv["gbs"], "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                     "frac": mv["gbs"] / peaks["hbm_gbs"], "peak_src": peaks["src"], "traffic": None,
+                     "frac": mv["gbs"] / peaks["hbm_gbs"], "peak_src": peaks["src"],
+                     # DRAM read + write bytes of one launch of this kernel and shape from
+                     # one ncu capture (profiles/mv_kernel_gateup_28672x4096.md)
+                     "traffic": TRAFFIC_GATEUP_BYTES, "traffic_unit": "bytes per launch",
                      "algorithmic_bytes": mv["bytes"], "launch_ms": mv["ms"]},
         "step_roofline": {"bytes_per_token": btok, "achieved_gbs": btok / (ms / args.steps * 1e-3) / 1e9,
                           "frac": btok / (ms / args.steps * 1e-3) / 1e9 / peaks["hbm_gbs"]},

@@ -235,7 +235,8 @@ int yl_profile_decode_step(const yl_model* m, yl_session* s, uint32_t token, uin
  * (attention: wait released), 2 wait on the preceding kernel released
  * (attention: partials visible), 3 done; RMSNorm prologues also 4 first
  * token's rows loaded, 5 norm factor ready, 6 warp 0's rows quantized, 7 the
- * last warp's (0 where not stamped). Launch order as yl_profile_decode_step;
+ * last warp's; attention also 4 q rotated, 5 first key tile in shared
+ * memory, 6 partial ready, 7 merge done (0 where not stamped). Launch order as yl_profile_decode_step;
  * the embedding launch (index 0) is not stamped. Writes up to cap values; *n_launches = launches. */
 int yl_trace_decode_step(const yl_model* m, yl_session* s, uint32_t token, uint32_t pos, uint64_t* out,
                          uint64_t cap, uint32_t* n_launches);

@@ -293,8 +293,12 @@ __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
 }
 
+// At most 96 registers a thread: then an attention CTA (8 warps) and a
+// matvec CTA (9 warps, 96 registers) fit one SM together, two plus three
+// warps per sub-partition within its 16K registers, so the next projection's
+// CTAs become resident and stream their weights while attention runs.
 template <int HD>
-__global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(AttnDecodeArgs a) {
+__global__ void __maxnreg__(96) attn_decode_kernel(AttnDecodeArgs a) {
   using Lo = AdLayout<HD>;
   extern __shared__ __align__(16) float sm[];
   cg::cluster_group cluster = cg::this_cluster();
@@ -359,6 +363,7 @@ __global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(AttnDecodeArgs 
     cr[tid] = 0.0f;
   }
   __syncthreads();  // an empty split goes straight to the merge
+  if (trace && tid == 0) trace[4] = globaltimer();
 
   const uint32_t ntiles = (p_end - p_begin + AD_TILE - 1) / AD_TILE;
   for (uint32_t ti = 0; ti < ntiles; ++ti) {
@@ -390,6 +395,7 @@ __global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(AttnDecodeArgs 
     }
     cp_async_wait_all();
     __syncthreads();
+    if (trace && tid == 0 && ti == 0) trace[5] = globaltimer();
     // scores (forward.rs:328-346): thread (position p, dim quarter dq) forms
     // the partial dots of all kv_mul heads; K rows are read once per quarter
     {
@@ -491,6 +497,7 @@ __global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(AttnDecodeArgs 
     __syncthreads();
   }
 
+  if (trace && tid == 0) trace[6] = globaltimer();
   // every split's partial is in its CTA's shared memory
   cluster.sync();
   if (trace && tid == 0) trace[2] = globaltimer();
@@ -530,6 +537,7 @@ __global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(AttnDecodeArgs 
       if (lane == 0) a.s8[k / 32] = sc;
     }
   }
+  if (trace && tid == 0) trace[7] = globaltimer();
   // peers may still be reading this CTA's shared memory
   cluster.sync();
   if (trace && tid == 0) trace[3] = globaltimer();

@@ -130,27 +130,35 @@ __device__ __forceinline__ int8_t rust_as_i8(float v) {
   const int i = __float2int_rz(v);
   return (int8_t)max(-128, min(127, i));
 }
-// roundf(x / d) with the quotient correctly rounded to f32 (the quantizer's
-// `(x / scale).round()`), from one multiply by inv = 1/d (correctly rounded).
-// |x*inv - x/d| <= 2^-23 |x/d| and the f32 quotient is within 2^-24 |x/d| of
-// x/d, so for |x/d| <= 128 the two differ by under 2.3e-5: when x*inv is
-// farther than 3.1e-5 from a half-integer, both round to the same integer.
-// Otherwise (a few in 1e5 of the inputs), and for NaN/inf, the exact quotient
-// decides. Bit-exact with roundf(__fdiv_rn(x, d)).
-__device__ __forceinline__ float round_quot(float x, float d, float inv) {
-  const float v = x * inv;
+// q = rust_as_i8(roundf(x / d)) with the quotient correctly rounded to f32
+// (the quantizer's `(x / scale).round() as i8`), from v = x * inv, inv = 1/d
+// correctly rounded. |v - x/d| <= 2^-23 |x/d| and the f32 quotient is within
+// 2^-24 |x/d| of x/d, so for |x/d| <= 128 the two differ by under 2.3e-5:
+// when v is farther than 3.1e-5 from a half-integer both round to the same
+// integer, which the 1.5*2^23 shift gives in two full-rate instructions.
+// Otherwise (a few in 1e5 of the inputs), and for NaN/inf, `exact` is set and
+// the caller takes quot_code_exact for the warp.
+__device__ __forceinline__ int quot_code_fast(float x, float inv, bool& exact) {
+  const float v = __fmul_rn(x, inv);
   const float a = fabsf(v);
-  const float fr = a - floorf(a);
-  if (a <= 128.0f && fabsf(fr - 0.5f) > 3.1e-5f) return roundf(v);
-  return roundf(__fdiv_rn(x, d));
+  exact |= !(a <= 128.0f && fabsf((a - floorf(a)) - 0.5f) > 3.1e-5f);
+  const int q = __float_as_int(__fadd_rn(v, 12582912.0f)) - 0x4B400000;
+  return min(q, 127);
+}
+__device__ __forceinline__ int quot_code_exact(float x, float d) { return rust_as_i8(roundf(__fdiv_rn(x, d))); }
+// Packs four int8 codes (low bytes of q0..q3) into one word, q0 lowest.
+__device__ __forceinline__ uint32_t pack4(int q0, int q1, int q2, int q3) {
+  return __byte_perm(__byte_perm(q0, q1, 0x0040), __byte_perm(q2, q3, 0x0040), 0x5410);
 }
 __device__ __forceinline__ int8_t quant_q8_lane(float x, float* scale_out) {
-  float a = fabsf(x);
-  a = (a > 0.0f) ? a : 0.0f;  // NaN -> 0 so it never becomes the max
-  float wmax = warp_max(a);
-  float scale = __fdiv_rn(wmax, 127.0f);
+  const float a = fmaxf(fabsf(x), 0.0f);  // NaN -> 0 so it never becomes the max
+  const float wmax = warp_max(a);
+  const float scale = __fdiv_rn(wmax, 127.0f);
   *scale_out = scale;
-  return rust_as_i8(round_quot(x, scale, __frcp_rn(scale)));
+  bool exact = false;
+  int q = quot_code_fast(x, __frcp_rn(scale), exact);
+  if (__any_sync(FULL, exact)) q = quot_code_exact(x, scale);
+  return (int8_t)q;
 }
 
 }  // namespace dev

@@ -176,7 +176,8 @@ struct AttnDecodeArgs {
   int8_t* q8;             // (nullable)
   float* s8;
   // timeline tracing (nullable): 8 slots per CTA in globaltimer nanoseconds:
-  // entry, wait released, partials visible, done
+  // entry, wait released, partials visible, done, q rotated, first key tile
+  // in shared memory, partial ready, merge done
   uint64_t* trace;
 };
 // Cluster size for the decode attention: 16 when n_kv_heads clusters of 16

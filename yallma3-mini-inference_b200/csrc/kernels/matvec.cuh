@@ -223,12 +223,8 @@ __device__ __forceinline__ void mv_norm_regs(const MvArgs& a, const MvLayout& L,
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const float4 y = xv[u0 + j];
-        float mm = 0.0f;
-        mm = fmaxf(mm, fabsf(y.x) > 0.0f ? fabsf(y.x) : 0.0f);  // NaN never becomes the max
-        mm = fmaxf(mm, fabsf(y.y) > 0.0f ? fabsf(y.y) : 0.0f);
-        mm = fmaxf(mm, fabsf(y.z) > 0.0f ? fabsf(y.z) : 0.0f);
-        mm = fmaxf(mm, fabsf(y.w) > 0.0f ? fabsf(y.w) : 0.0f);
-        m[j] = mm;
+        // fmaxf returns the other operand for a NaN: NaN never becomes the max
+        m[j] = fmaxf(fmaxf(fmaxf(0.0f, fabsf(y.x)), fmaxf(fabsf(y.y), fabsf(y.z))), fabsf(y.w));
       }
 #pragma unroll
       for (int o = 4; o > 0; o >>= 1)
@@ -250,20 +246,32 @@ __device__ __forceinline__ void mv_norm_regs(const MvArgs& a, const MvLayout& L,
           if (FMT == FMT_Q8X) lim[j] = __shfl_sync(FULL, lij, src | j);
         }
       }
+      int qv[4][4];
+      bool exact = false;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        qv[j][0] = quot_code_fast(xv[u0 + j].x, isc[j], exact);
+        qv[j][1] = quot_code_fast(xv[u0 + j].y, isc[j], exact);
+        qv[j][2] = quot_code_fast(xv[u0 + j].z, isc[j], exact);
+        qv[j][3] = quot_code_fast(xv[u0 + j].w, isc[j], exact);
+      }
+      if (__any_sync(FULL, exact)) {  // rare: a quotient next to a half-integer
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          qv[j][0] = quot_code_exact(xv[u0 + j].x, sc[j]);
+          qv[j][1] = quot_code_exact(xv[u0 + j].y, sc[j]);
+          qv[j][2] = quot_code_exact(xv[u0 + j].z, sc[j]);
+          qv[j][3] = quot_code_exact(xv[u0 + j].w, sc[j]);
+        }
+      }
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int u = u0 + j;
         const uint32_t i = ctid * 4 + u * MV_NCW * 32 * 4;
         const bool in = i < K;
         const float y[4] = {xv[u].x, xv[u].y, xv[u].z, xv[u].w};
-        uint32_t word = 0;
-        int qs = 0;
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int8_t q = rust_as_i8(round_quot(y[e], sc[j], isc[j]));
-          word |= (uint32_t)(uint8_t)q << (8 * e);
-          qs += q;
-        }
+        const uint32_t word = pack4(qv[j][0], qv[j][1], qv[j][2], qv[j][3]);
+        int qs = qv[j][0] + qv[j][1] + qv[j][2] + qv[j][3];
         const uint32_t b = i / 32, e0 = i % 32;  // block and first element within it
         int8_t* xq = reinterpret_cast<int8_t*>(smem + L.x_off) + t * K;
         if (FMT == FMT_Q4) {
@@ -866,6 +874,15 @@ __global__ void __launch_bounds__(MV_THREADS, (NT <= 2 ? 2 : 1)) mv_kernel(MvArg
   for (int r = 0; r < RPW; ++r)
 #pragma unroll
     for (int t = 0; t < NT; ++t) acc[r][t] = 0.0f;
+  // EPI_ADD, one token, static split: the residual values this warp will add
+  // to (rows r_begin + rs*RS + cw, one row set per lane) are fetched now, so
+  // the epilogues do not wait on a global read-modify-write
+  const bool pre_add = EPI == EPI_ADD && NT == 1 && G == 1 && !dyn && nrs <= 32;
+  float xpre = 0.0f;
+  if (pre_add && lane < (int)nrs) {
+    const uint32_t r = r_begin + lane * RS + cw;
+    if (r < r_end) xpre = a.out[r];
+  }
   float am_v = -INFINITY;  // EPI_ARGMAX: this warp's best (lane 0)
   uint32_t am_i = 0xFFFFFFFFu;
 
@@ -928,13 +945,14 @@ __global__ void __launch_bounds__(MV_THREADS, (NT <= 2 ? 2 : 1)) mv_kernel(MvArg
             am_i = r;
           }
         }
+        const float prev = pre_add ? __shfl_sync(FULL, xpre, (row0 - r_begin) / RS) : 0.0f;
         if (lane == 0) {
 #pragma unroll
           for (int t = 0; t < NT; ++t) {
             if (t >= (int)a.ntok) continue;
             float* o = a.out + (uint64_t)t * a.out_tok_stride + r;
             if (EPI == EPI_STORE || EPI == EPI_ARGMAX) *o = acc[rr][t];
-            else if (EPI == EPI_ADD) *o = __fadd_rn(*o, acc[rr][t]);
+            else if (EPI == EPI_ADD) *o = __fadd_rn(pre_add ? prev : *o, acc[rr][t]);
             else *o = (r < a.quirk_cols) ? __fadd_rn(*o, acc[rr][t]) : acc[rr][t];
           }
         }
