@@ -177,6 +177,29 @@ typedef struct yl_shape {
  * and uploaded to the current CUDA device. */
 int yl_load_transformer(const char* path, int sequential, uint32_t max_ctx_len, int fmt_override,
                         yl_model** out);
+/* Tensor parallelism (no counterpart in the reference, which runs on one
+ * CPU; this is the Megatron split of forward.rs:154-279 for one NVSwitch
+ * box). Rank tp_rank of tp_size (2..8, one process per GPU, the device
+ * current) loads its shard: q/k/v heads and gate/up rows by rank, wo and
+ * down along their inputs, lm_head by vocabulary rows; embeddings and norms
+ * whole. Needs KV heads, ffn/64 and vocabulary divisible by tp_size.
+ * Sessions of such a model exchange partial sums over NVLink peer memory
+ * after wo and down, and per-rank greedy winners after the lm_head: create
+ * the session on every rank, collect every rank's yl_session_tp_handle (64
+ * bytes) in rank order, and pass the array to yl_session_tp_connect. Every
+ * rank must then make the same forward/decode calls in the same order (the
+ * exchange waits for all ranks, bounded: a missing rank gives
+ * YL_ERR_TIMEOUT). */
+int yl_load_transformer_tp(const char* path, uint32_t max_ctx_len, int fmt_override, int tp_rank, int tp_size,
+                           yl_model** out);
+int yl_session_tp_handle(yl_session* s, void* handle_out);
+int yl_session_tp_connect(yl_session* s, const void* handles);
+/* The split itself, without a GPU: first row / row count of this rank's q
+ * rows, k (= v) rows, gate (= up) rows and vocabulary rows. */
+typedef struct yl_tp_split {
+  uint32_t q_rows0, q_rows, kv_rows0, kv_rows, ffn_rows0, ffn_rows, vocab0, vocab_rows;
+} yl_tp_split;
+int yl_tp_plan(const yl_shape* shape, int tp_rank, int tp_size, yl_tp_split* out);
 int yl_model_free(yl_model* m);
 const char* yl_model_name(const yl_model* m);            /* Transformer::name */
 uint64_t yl_model_vocab_size(const yl_model* m);         /* Transformer::vocab_size */

@@ -55,6 +55,11 @@ class ShapeC(C.Structure):
         ("_pad", C.c_int32)]
 
 
+class TpSplitC(C.Structure):
+    _fields_ = [(n, C.c_uint32) for n in ("q_rows0", "q_rows", "kv_rows0", "kv_rows", "ffn_rows0", "ffn_rows",
+                                          "vocab0", "vocab_rows")]
+
+
 class SynthC(C.Structure):
     _fields_ = [(n, C.c_uint32) for n in ("dim", "hidden_dim", "n_layers", "n_heads", "n_kv_heads", "vocab_size",
                                           "context_length")] + [
@@ -83,6 +88,10 @@ _sigs = {
     "yl_fused_attention_static": (C.c_int, [_P, _P, _P, _P, C.c_uint64, C.c_uint64, C.c_uint64, C.c_uint64,
                                             C.c_uint64, C.c_uint32, C.c_uint64, C.c_float, _P]),
     "yl_load_transformer": (C.c_int, [C.c_char_p, C.c_int, C.c_uint32, C.c_int, C.POINTER(_P)]),
+    "yl_load_transformer_tp": (C.c_int, [C.c_char_p, C.c_uint32, C.c_int, C.c_int, C.c_int, C.POINTER(_P)]),
+    "yl_session_tp_handle": (C.c_int, [_P, C.c_char_p]),
+    "yl_session_tp_connect": (C.c_int, [_P, C.c_char_p]),
+    "yl_tp_plan": (C.c_int, [C.POINTER(ShapeC), C.c_int, C.c_int, C.POINTER(TpSplitC)]),
     "yl_model_free": (C.c_int, [_P]),
     "yl_model_name": (C.c_char_p, [_P]),
     "yl_model_vocab_size": (C.c_uint64, [_P]),
@@ -293,6 +302,24 @@ class InferenceSession:
         _check(_lib.yl_session_reset(self._h))
         self.pos = 0
 
+    def tp_handle(self) -> bytes:
+        """This rank's exchange-region handle (tensor-parallel sessions)."""
+        buf = C.create_string_buffer(64)
+        _check(_lib.yl_session_tp_handle(self._h, buf))
+        return buf.raw
+
+    def tp_connect(self, handles: Sequence[bytes]) -> None:
+        """Maps every rank's exchange region (handles in rank order)."""
+        blob = b"".join(handles)
+        _check(_lib.yl_session_tp_connect(self._h, blob))
+
+    def tp_connect_group(self, group=None) -> None:
+        """Exchanges handles over torch.distributed (all ranks call this)."""
+        import torch.distributed as dist
+        hs = [None] * dist.get_world_size(group)
+        dist.all_gather_object(hs, self.tp_handle(), group=group)
+        self.tp_connect(hs)
+
     def kv_cache(self):
         k, v, n = _P(), _P(), C.c_uint64()
         _check(_lib.yl_session_kv(self._h, C.byref(k), C.byref(v), C.byref(n)))
@@ -406,7 +433,7 @@ class Transformer:
         released, wait released / partials visible, done, rows loaded, norm
         factor ready, -, -); zeros where a launch has fewer CTAs or a point
         is not stamped (the embedding launch has none)."""
-        n_max = 5 * self.shape().n_layers + 4
+        n_max = 7 * self.shape().n_layers + 6
         out = np.zeros(n_max * 8192, np.uint64)
         n = C.c_uint32()
         _check(_lib.yl_trace_decode_step(self._h, session._h, token, pos, _ptr(out), out.size, C.byref(n)))
@@ -436,6 +463,32 @@ def load_transformer(model_path: str, sequential: bool = False, max_ctx_len: int
     _check(_lib.yl_load_transformer(str(model_path).encode(), 1 if sequential else 0, max_ctx_len,
                                     -1 if fmt_override is None else int(fmt_override), C.byref(h)))
     return Transformer(h.value)
+
+
+def load_transformer_tp(model_path: str, tp_rank: int, tp_size: int, max_ctx_len: int = 0xFFFFFFFF,
+                        fmt_override: Optional[WeightFormat] = None) -> Transformer:
+    """Rank tp_rank's shard of a tensor-parallel model on the current device
+    (one process per GPU); its sessions need tp_connect / tp_connect_group."""
+    h = _P()
+    _check(_lib.yl_load_transformer_tp(str(model_path).encode(), max_ctx_len,
+                                       -1 if fmt_override is None else int(fmt_override), tp_rank, tp_size,
+                                       C.byref(h)))
+    return Transformer(h.value)
+
+
+def tp_plan(shape: ShapeC, tp_rank: int, tp_size: int) -> dict:
+    """The tensor-parallel split of a shape (no GPU needed)."""
+    out = TpSplitC()
+    _check(_lib.yl_tp_plan(C.byref(shape), tp_rank, tp_size, C.byref(out)))
+    return {n: getattr(out, n) for n, _ in TpSplitC._fields_}
+
+
+def shape_of(**kw) -> ShapeC:
+    """A ShapeC from keyword fields (others zero), e.g. for tp_plan."""
+    sc = ShapeC()
+    for k, v in kw.items():
+        setattr(sc, k, v)
+    return sc
 
 
 def load_transformer_ffi(model_path: Optional[str]) -> bool:

@@ -315,9 +315,50 @@ int yl_load_transformer(const char* path, int sequential, uint32_t max_ctx_len, 
   }
   if (fmt_override < -1 || fmt_override > YL_F16) return fail(YL_ERR_ARG, "bad format override");
   Model* m = nullptr;
-  int rc = model_load_gguf(path, max_ctx_len, fmt_override, &m);
+  int rc = model_load_gguf(path, max_ctx_len, fmt_override, 0, 1, &m);
   if (rc) return rc;
   *out = new yl_model{m};
+  return YL_OK;
+}
+
+int yl_load_transformer_tp(const char* path, uint32_t max_ctx_len, int fmt_override, int tp_rank, int tp_size,
+                           yl_model** out) {
+  if (!path || !out) return fail(YL_ERR_ARG, "null argument");
+  std::string p(path);
+  if (p.size() < 5 || p.substr(p.size() - 5) != ".gguf") return fail(YL_ERR_ARG, "tensor-parallel load needs a .gguf");
+  if (fmt_override < -1 || fmt_override > YL_F16) return fail(YL_ERR_ARG, "bad format override");
+  Model* m = nullptr;
+  int rc = model_load_gguf(path, max_ctx_len, fmt_override, tp_rank, tp_size, &m);
+  if (rc) return rc;
+  *out = new yl_model{m};
+  return YL_OK;
+}
+
+int yl_session_tp_handle(yl_session* sp, void* handle_out) {
+  if (!sp || !handle_out) return fail(YL_ERR_ARG, "null argument");
+  return session_tp_handle(sp->s, handle_out);
+}
+
+int yl_session_tp_connect(yl_session* sp, const void* handles) {
+  if (!sp || !handles) return fail(YL_ERR_ARG, "null argument");
+  return session_tp_connect(sp->s, handles);
+}
+
+int yl_tp_plan(const yl_shape* shape, int tp_rank, int tp_size, yl_tp_split* out) {
+  if (!shape || !out) return fail(YL_ERR_ARG, "null argument");
+  if (tp_size < 1 || tp_size > 8 || tp_rank < 0 || tp_rank >= tp_size) return fail(YL_ERR_ARG, "bad rank/size");
+  const uint32_t N = (uint32_t)tp_size, r = (uint32_t)tp_rank, hs = shape->head_size;
+  if (shape->n_kv_heads == 0 || shape->n_kv_heads % N || shape->n_heads % shape->n_kv_heads ||
+      shape->hidden_dim % (64 * N) || shape->vocab_size % N)
+    return fail(YL_ERR_UNSUPPORTED, "tensor parallelism needs KV heads, ffn/64 and vocabulary divisible by the ranks");
+  out->q_rows0 = r * (shape->n_heads / N) * hs;
+  out->q_rows = (shape->n_heads / N) * hs;
+  out->kv_rows0 = r * (shape->n_kv_heads / N) * hs;
+  out->kv_rows = (shape->n_kv_heads / N) * hs;
+  out->ffn_rows0 = r * (shape->hidden_dim / N);
+  out->ffn_rows = shape->hidden_dim / N;
+  out->vocab0 = r * (shape->vocab_size / N);
+  out->vocab_rows = shape->vocab_size / N;
   return YL_OK;
 }
 
@@ -465,16 +506,17 @@ int yl_forward_x(const yl_model* m, yl_session* sp, const uint32_t* tokens, uint
   if ((uint64_t)start_pos + n > sh.ctx_len) return fail(YL_ERR_RANGE, "position beyond ctx_len");
   YL_CUDA_TRY(cudaSetDevice(s->device));
   int rc;
+  const bool lg_graph = logits_out && m->m->tp_size > 1;
   if (n == 1) {  // batch-1 step through the captured decode graph
-    if ((rc = ensure_decode_graph(s))) return rc;
+    if ((rc = ensure_decode_graph(s, lg_graph))) return rc;
     s->state_h->pos = (int32_t)start_pos;
     s->state_h->token = (int32_t)tokens[0];
     s->state_h->next = 0;
     s->state_h->steps = 0;
     YL_CUDA_TRY(cudaMemcpyAsync(s->state, s->state_h, sizeof(k::StepState), cudaMemcpyHostToDevice, s->stream));
-    YL_CUDA_TRY(cudaGraphLaunch(s->graph, s->stream));
+    YL_CUDA_TRY(cudaGraphLaunch(lg_graph ? s->graph_lg : s->graph, s->stream));
   } else {
-    if ((rc = forward(s, tokens, (uint32_t)n, start_pos))) return rc;
+    if ((rc = forward(s, tokens, (uint32_t)n, start_pos, logits_out != nullptr))) return rc;
   }
   if (logits_out)
     YL_CUDA_TRY(cudaMemcpyAsync(s->logits_h, s->logits, (uint64_t)sh.vocab_size * 4, cudaMemcpyDeviceToHost, s->stream));

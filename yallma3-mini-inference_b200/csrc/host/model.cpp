@@ -306,7 +306,8 @@ const Tunables& tunables() {
   return t;
 }
 
-int model_load_gguf(const char* path, uint32_t max_ctx_len, int fmt_override, Model** out) {
+int model_load_gguf(const char* path, uint32_t max_ctx_len, int fmt_override, int tp_rank, int tp_size, Model** out) {
+  if (tp_size < 1 || tp_size > 8 || tp_rank < 0 || tp_rank >= tp_size) return fail(YL_ERR_ARG, "bad tensor-parallel rank/size");
   int fd = open(path, O_RDONLY);
   if (fd < 0) return fail(YL_ERR_IO, std::string("cannot open ") + path);
   struct stat stt;
@@ -380,8 +381,8 @@ int model_load_gguf(const char* path, uint32_t max_ctx_len, int fmt_override, Mo
   else if (file_type == 7) fmt = YL_Q8_0;
   else return fail(YL_ERR_FORMAT, "Unsupported GGUF file_type " + std::to_string(file_type));
   s.weight_format = fmt;
-  s.tp_rank = 0;
-  s.tp_size = 1;
+  s.tp_rank = tp_rank;
+  s.tp_size = tp_size;
   m->bos = meta_id(meta, "tokenizer.ggml.bos_token_id", 128000u);
   m->eos = meta_id(meta, "tokenizer.ggml.eos_token_id", 128009u);
   if (s.dim % 32 || s.hidden_dim % 32 || s.head_size % 32 || s.n_kv_heads == 0 || s.n_heads % s.n_kv_heads)
@@ -389,6 +390,19 @@ int model_load_gguf(const char* path, uint32_t max_ctx_len, int fmt_override, Mo
   if (s.head_size != 64 && s.head_size != 128) return fail(YL_ERR_UNSUPPORTED, "head_size must be 64 or 128");
   if (s.n_heads / s.n_kv_heads > 8) return fail(YL_ERR_UNSUPPORTED, "more than 8 query heads per KV head");
   if (s.ctx_len == 0) return fail(YL_ERR_ARG, "ctx_len is 0");
+  // Megatron split: heads (q and KV) and ffn rows by rank, wo/down along K,
+  // lm_head by vocabulary rows; activation and weight blocks of 32 never
+  // straddle ranks (the ffn slice is a multiple of 64 for the SwiGLU pairs)
+  const uint32_t N = (uint32_t)tp_size;
+  if (s.n_kv_heads % N || s.hidden_dim % (64 * N) || s.vocab_size % N)
+    return fail(YL_ERR_UNSUPPORTED, "tensor parallelism needs KV heads, ffn/64 and vocabulary divisible by the ranks");
+  m->tp_rank = tp_rank;
+  m->tp_size = tp_size;
+  m->l_heads = s.n_heads / N;
+  m->l_kv = s.n_kv_heads / N;
+  m->l_ffn = s.hidden_dim / N;
+  m->l_vocab = s.vocab_size / N;
+  m->vocab0 = m->l_vocab * (uint32_t)tp_rank;
 
   std::map<std::string, TInfo> tmap;
   for (uint64_t i = 0; i < n_tensors && c.ok; ++i) {
@@ -449,12 +463,16 @@ int model_load_gguf(const char* path, uint32_t max_ctx_len, int fmt_override, Mo
   if ((rc = get("token_embd.weight", &te))) return rc;
   if (te->n != (uint64_t)s.vocab_size * d) return fail(YL_ERR_FORMAT, "token_embd.weight shape mismatch");
   if ((rc = up.weight(te->type, s.vocab_size, d, [&](uint32_t r) { return row_ptr(te, d, r); }, &m->emb))) return rc;
-  m->lm = m->emb;
+  m->lm = m->emb;  // this rank's vocabulary rows of the tied table
+  m->lm.rows = m->l_vocab;
+  m->lm.q = m->emb.q + (uint64_t)m->vocab0 * m->emb.row_bytes;
+  if (m->emb.s) m->lm.s = m->emb.s + (uint64_t)m->vocab0 * m->emb.scale_row_bytes;
   auto out_it = tmap.find("output.weight");
   if (out_it != tmap.end()) {  // untied lm_head (resolved deviation D2)
     const TInfo* to = &out_it->second;
     if (to->n != (uint64_t)s.vocab_size * d) return fail(YL_ERR_FORMAT, "output.weight shape mismatch");
-    if ((rc = up.weight(to->type, s.vocab_size, d, [&](uint32_t r) { return row_ptr(to, d, r); }, &m->lm))) return rc;
+    if ((rc = up.weight(to->type, m->l_vocab, d, [&](uint32_t r) { return row_ptr(to, d, m->vocab0 + r); }, &m->lm)))
+      return rc;
     s.untied_lm_head = 1;
   }
   auto f32t = [&](const std::string& nm, uint64_t n, float** dst) -> int {
@@ -480,17 +498,24 @@ int model_load_gguf(const char* path, uint32_t max_ctx_len, int fmt_override, Mo
     if ((rc = check(tq, att, d)) || (rc = check(tk, kvd, d)) || (rc = check(tv, kvd, d)) || (rc = check(to, d, att)) ||
         (rc = check(tg, f, d)) || (rc = check(tu, f, d)) || (rc = check(tdn, d, f)))
       return rc;
-    rc = up.weight(want_type, att + 2 * kvd, d, [&](uint32_t r) {
-      if (r < att) return row_ptr(tq, d, r);
-      if (r < att + kvd) return row_ptr(tk, d, r - att);
-      return row_ptr(tv, d, r - att - kvd);
+    // this rank's rows / columns (the whole matrices at one rank)
+    const uint32_t hs = s.head_size, la = m->l_heads * hs, lk = m->l_kv * hs, lf = m->l_ffn;
+    const uint32_t qa0 = (uint32_t)tp_rank * la, kv0 = (uint32_t)tp_rank * lk, f0 = (uint32_t)tp_rank * lf;
+    rc = up.weight(want_type, la + 2 * lk, d, [&](uint32_t r) {
+      if (r < la) return row_ptr(tq, d, qa0 + r);
+      if (r < la + lk) return row_ptr(tk, d, kv0 + r - la);
+      return row_ptr(tv, d, kv0 + r - la - lk);
     }, &L.wqkv);
     if (rc) return rc;
-    if ((rc = up.weight(want_type, d, att, [&](uint32_t r) { return row_ptr(to, att, r); }, &L.wo))) return rc;
-    rc = up.weight(want_type, 2 * f, d, [&](uint32_t r) { return (r & 1) ? row_ptr(tu, d, r / 2) : row_ptr(tg, d, r / 2); },
-                   &L.w13);
+    if ((rc = up.weight(want_type, d, la, [&](uint32_t r) { return row_ptr(to, att, r) + bytes_of(want_type, qa0); },
+                        &L.wo)))
+      return rc;
+    rc = up.weight(want_type, 2 * lf, d,
+                   [&](uint32_t r) { return (r & 1) ? row_ptr(tu, d, f0 + r / 2) : row_ptr(tg, d, f0 + r / 2); }, &L.w13);
     if (rc) return rc;
-    if ((rc = up.weight(want_type, d, f, [&](uint32_t r) { return row_ptr(tdn, f, r); }, &L.w2))) return rc;
+    if ((rc = up.weight(want_type, d, lf, [&](uint32_t r) { return row_ptr(tdn, f, r) + bytes_of(want_type, f0); },
+                        &L.w2)))
+      return rc;
   }
   std::vector<float2> cs;
   rope_table(s, l3_factor, l3_low, l3_high, (float)s.rope_original_ctx_len, &cs);
@@ -507,6 +532,10 @@ int model_load_gguf(const char* path, uint32_t max_ctx_len, int fmt_override, Mo
 
 Session::~Session() {
   if (graph) cudaGraphExecDestroy(graph);
+  if (graph_lg) cudaGraphExecDestroy(graph_lg);
+  if (stream) cudaStreamSynchronize(stream);
+  for (void* p : tp_opened) cudaIpcCloseMemHandle(p);
+  if (tp_region) cudaFree(tp_region);
   if (stream) cudaStreamDestroy(stream);
   for (void* p : allocs) cudaFree(p);
   if (state_h) cudaFreeHost(state_h);
@@ -568,7 +597,7 @@ int session_create(const Model* m, Session** out) {
   YL_CUDA_TRY(cudaSetDevice(m->device));
   YL_CUDA_TRY(cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking));
   const yl_shape& sh = m->shape;
-  const uint64_t kvd = (uint64_t)sh.n_kv_heads * sh.head_size;
+  const uint64_t kvd = (uint64_t)m->l_kv * sh.head_size;  // this rank's KV heads
   s->kv_elems = (uint64_t)sh.n_layers * sh.ctx_len * kvd;
   void* p;
   int rc;
@@ -581,7 +610,7 @@ int session_create(const Model* m, Session** out) {
   if ((rc = salloc(s.get(), (uint64_t)sh.vocab_size * 4, &p))) return rc;
   s->logits = (float*)p;
   // decode attention: one cluster of n_splits CTAs per KV head
-  s->n_splits = k::attention_decode_splits(sh.n_kv_heads, sh.head_size);
+  s->n_splits = k::attention_decode_splits(m->l_kv, sh.head_size);
   if ((rc = salloc(s.get(), (uint64_t)sh.n_heads * s->n_splits * (sh.head_size + 2) * 4, &p))) return rc;
   s->part = (float*)p;
   if ((rc = salloc(s.get(), ((uint64_t)sh.n_layers + 1) * 2 * 4, &p))) return rc;
@@ -607,7 +636,62 @@ int session_create(const Model* m, Session** out) {
   YL_CUDA_TRY(cudaMallocHost(&s->logits_h, (uint64_t)sh.vocab_size * 4));
   YL_CUDA_TRY(cudaMallocHost(&s->hist_h, ((uint64_t)sh.ctx_len + 1) * 4));
   if ((rc = ensure_cap(s.get(), 8))) return rc;
+  if (m->tp_size > 1) {
+    // exchange region: flags [2 L + 1][world], partials [2][tp_cap][dim],
+    // the lm_head winner slot, and this rank's logits slice
+    s->tp_cap = 512;
+    const uint64_t world = (uint64_t)m->tp_size;
+    s->tp_flags_off = 0;
+    uint64_t off = round_up((2ull * sh.n_layers + 1) * world * 4, 256);
+    s->tp_part_off[0] = off;
+    off += round_up((uint64_t)s->tp_cap * sh.dim * 4, 256);
+    s->tp_part_off[1] = off;
+    off += round_up((uint64_t)s->tp_cap * sh.dim * 4, 256);
+    s->tp_lm_off = off;
+    off += 256;
+    s->tp_logit_off = off;
+    off += round_up((uint64_t)m->l_vocab * 4, 256);
+    s->tp_bytes = off;
+    YL_CUDA_TRY(cudaMalloc(&p, s->tp_bytes));  // plain cudaMalloc: exportable through CUDA IPC
+    s->tp_region = (uint8_t*)p;
+    YL_CUDA_TRY(cudaMemset(s->tp_region, 0, s->tp_bytes));
+    if ((rc = salloc(s.get(), 4, &p))) return rc;
+    s->tp_epoch = (uint32_t*)p;
+    YL_CUDA_TRY(cudaMemset(s->tp_epoch, 0, 4));
+  }
   *out = s.release();
+  return YL_OK;
+}
+
+int session_tp_handle(Session* s, void* handle_out) {
+  if (s->m->tp_size < 2) return fail(YL_ERR_ARG, "session is not tensor-parallel");
+  YL_CUDA_TRY(cudaSetDevice(s->device));
+  cudaIpcMemHandle_t h;
+  YL_CUDA_TRY(cudaIpcGetMemHandle(&h, s->tp_region));
+  memcpy(handle_out, &h, sizeof(h));
+  return YL_OK;
+}
+
+int session_tp_connect(Session* s, const void* handles) {
+  const Model* m = s->m;
+  if (m->tp_size < 2) return fail(YL_ERR_ARG, "session is not tensor-parallel");
+  if (s->tp_ready) return fail(YL_ERR_ARG, "session already connected");
+  YL_CUDA_TRY(cudaSetDevice(s->device));
+  for (int r = 0; r < m->tp_size; ++r) {
+    if (r == m->tp_rank) {
+      s->tp_base[r] = s->tp_region;
+      continue;
+    }
+    cudaIpcMemHandle_t h;
+    memcpy(&h, (const uint8_t*)handles + (size_t)r * sizeof(h), sizeof(h));
+    void* p = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return fail(YL_ERR_COMM, std::string("opening rank ") + std::to_string(r) +
+                                                       "'s exchange region: " + cudaGetErrorString(e));
+    s->tp_opened.push_back(p);
+    s->tp_base[r] = (uint8_t*)p;
+  }
+  s->tp_ready = true;
   return YL_OK;
 }
 
@@ -687,6 +771,8 @@ int run_matvec_ex(const DevWeight& w, bool f32act, const int8_t* xq, const float
     a.state = ex.state;
     a.trace = ex.trace;
     a.work = ex.work;
+    a.am_shard = ex.am_shard;
+    a.am_base = ex.am_base;
     cudaError_t e = k::matvec(a, fmt, w.sf16, epi, lc);
     if (e != cudaSuccess) return fail(YL_ERR_CUDA, std::string("matvec launch: ") + cudaGetErrorString(e));
     if (launches) ++*launches;
@@ -699,10 +785,24 @@ namespace {
 // Enqueues the full forward for n tokens (already on device in s->tok unless
 // from_state). from_state: batch-1 step whose token/pos live in s->state
 // (graph capture). pdl: launch with programmatic dependent launch.
-int enqueue_forward(Session* s, uint32_t n, uint32_t start_pos, bool from_state, bool pdl, uint32_t* launches) {
+int enqueue_forward(Session* s, uint32_t n, uint32_t start_pos, bool from_state, bool pdl, uint32_t* launches,
+                    bool want_logits = true) {
   const Model* m = s->m;
   const yl_shape& sh = m->shape;
-  const uint32_t d = sh.dim, att = sh.n_heads * sh.head_size, kvd = sh.n_kv_heads * sh.head_size, f = sh.hidden_dim;
+  // this rank's attention width, KV width and ffn rows (the whole model at one rank)
+  const uint32_t d = sh.dim, att = m->l_heads * sh.head_size, kvd = m->l_kv * sh.head_size, f = m->l_ffn;
+  const bool tp = m->tp_size > 1;
+  if (tp && !s->tp_ready) return fail(YL_ERR_ARG, "tensor-parallel session is not connected to its peers");
+  if (tp && n > s->tp_cap) return fail(YL_ERR_ARG, "too many tokens for the exchange buffers in one pass");
+  k::TpArgs tpa{};
+  if (tp) {
+    for (int r = 0; r < m->tp_size; ++r) tpa.base[r] = s->tp_base[r];
+    tpa.rank = (uint32_t)m->tp_rank;
+    tpa.world = (uint32_t)m->tp_size;
+    tpa.flags_off = s->tp_flags_off;
+    tpa.epoch = s->tp_epoch;
+    tpa.err = s->err;
+  }
   const bool f32act = sh.weight_format == YL_F16;
   const k::StepState* st = from_state ? s->state : nullptr;
   k::LaunchCfg lc;
@@ -771,8 +871,8 @@ int enqueue_forward(Session* s, uint32_t n, uint32_t start_pos, bool from_state,
       ad.rope_mode = sh.rope_mode;
       ad.kcache = kc;
       ad.vcache = vc;
-      ad.n_heads = sh.n_heads;
-      ad.n_kv_heads = sh.n_kv_heads;
+      ad.n_heads = m->l_heads;
+      ad.n_kv_heads = m->l_kv;
       ad.head_size = sh.head_size;
       ad.kv_dim = kvd;
       ad.state = st;
@@ -786,15 +886,15 @@ int enqueue_forward(Session* s, uint32_t n, uint32_t start_pos, bool from_state,
       ad.s8 = s->xs;
       YL_LAUNCH(k::attention_decode(ad, lc));
     } else {
-      YL_LAUNCH(k::rope_kv(s->qkv, n, sh.n_heads, sh.n_kv_heads, sh.head_size, sh.rope_mode, m->rope_cs, sh.ctx_len,
+      YL_LAUNCH(k::rope_kv(s->qkv, n, m->l_heads, m->l_kv, sh.head_size, sh.rope_mode, m->rope_cs, sh.ctx_len,
                            st, start_pos, s->q, kc, vc, lc));
       k::AttnArgs aa{};
       aa.q = s->q;
       aa.kcache = kc;
       aa.vcache = vc;
       aa.ntok = n;
-      aa.n_heads = sh.n_heads;
-      aa.n_kv_heads = sh.n_kv_heads;
+      aa.n_heads = m->l_heads;
+      aa.n_kv_heads = m->l_kv;
       aa.head_size = sh.head_size;
       aa.kv_dim = kvd;
       aa.state = st;
@@ -807,9 +907,17 @@ int enqueue_forward(Session* s, uint32_t n, uint32_t start_pos, bool from_state,
       aa.s8 = s->xs;
       YL_LAUNCH(k::attention(aa, lc));
     }
-    // wo projection + residual add
-    YL_MV(L.wo, f32act, s->xq, s->xs, s->xf, att, att / 32, n, s->x, d, k::EPI_ADD, 0, s->err, s->stream, pdl,
-          m->num_sms);
+    // wo projection + residual add (tensor-parallel: this rank's partial
+    // sums, all-reduced over peer memory into the replicated residual)
+    if (tp) {
+      YL_MV(L.wo, f32act, s->xq, s->xs, s->xf, att, att / 32, n, (float*)(s->tp_region + s->tp_part_off[0]), d,
+            k::EPI_STORE, 0, s->err, s->stream, pdl, m->num_sms);
+      tpa.site = 2 * l;
+      YL_LAUNCH(k::tp_allreduce_add(tpa, s->tp_part_off[0], n * d, s->x, lc));
+    } else {
+      YL_MV(L.wo, f32act, s->xq, s->xs, s->xf, att, att / 32, n, s->x, d, k::EPI_ADD, 0, s->err, s->stream, pdl,
+            m->num_sms);
+    }
     // ---- feed-forward block (forward.rs:206-253) ----
     // RMSNorm + quantize in the prologue, SwiGLU in the epilogue (row pairs:
     // any CTA split keeps gate and up together), which for quantized formats
@@ -827,8 +935,15 @@ int enqueue_forward(Session* s, uint32_t n, uint32_t start_pos, bool from_state,
       return rc;
     YL_MARK();
     // down projection + residual add
-    YL_MV(L.w2, f32act, s->hq, s->hs, s->h, f, f / 32, n, s->x, d, k::EPI_ADD, 0, s->err, s->stream, pdl,
-          m->num_sms);
+    if (tp) {
+      YL_MV(L.w2, f32act, s->hq, s->hs, s->h, f, f / 32, n, (float*)(s->tp_region + s->tp_part_off[1]), d,
+            k::EPI_STORE, 0, s->err, s->stream, pdl, m->num_sms);
+      tpa.site = 2 * l + 1;
+      YL_LAUNCH(k::tp_allreduce_add(tpa, s->tp_part_off[1], n * d, s->x, lc));
+    } else {
+      YL_MV(L.w2, f32act, s->hq, s->hs, s->h, f, f / 32, n, s->x, d, k::EPI_ADD, 0, s->err, s->stream, pdl,
+            m->num_sms);
+    }
   }
   // final norm (prologue), lm_head on the last token and greedy id
   // (forward.rs:256-279, sampler.rs:67-79)
@@ -841,14 +956,24 @@ int enqueue_forward(Session* s, uint32_t n, uint32_t start_pos, bool from_state,
     fin.am_val = s->am_val;
     fin.am_idx = s->am_idx;
     fin.am_count = s->am_count;
-    fin.am_out = s->hist;
-    fin.state = from_state ? s->state : nullptr;
+    fin.am_out = tp ? nullptr : s->hist;
+    fin.state = (from_state && !tp) ? s->state : nullptr;
     fin.trace = YL_TRACE();
     fin.work = s->work + 2ull * sh.n_layers;  // lm_head: one launch per forward
-    if ((rc = run_matvec_ex(m->lm, true, nullptr, nullptr, nullptr, d, 0, 1, s->logits, sh.vocab_size, k::EPI_ARGMAX,
-                            0, s->err, s->stream, pdl, m->num_sms, fin, &nl)))
+    // tensor-parallel: this rank's vocabulary rows; the winner is published
+    // in the exchange region and combined across ranks
+    fin.am_shard = tp ? (float*)(s->tp_region + s->tp_lm_off) : nullptr;
+    fin.am_base = m->vocab0;
+    float* lg = tp ? (float*)(s->tp_region + s->tp_logit_off) : s->logits;
+    if ((rc = run_matvec_ex(m->lm, true, nullptr, nullptr, nullptr, d, 0, 1, lg, m->l_vocab, k::EPI_ARGMAX, 0, s->err,
+                            s->stream, pdl, m->num_sms, fin, &nl)))
       return rc;
     YL_MARK();
+    if (tp) {
+      tpa.site = 2 * sh.n_layers;
+      YL_LAUNCH(k::tp_argmax(tpa, s->tp_lm_off, s->tp_logit_off, m->l_vocab, want_logits ? s->logits : nullptr,
+                             s->hist, from_state ? s->state : nullptr, s->tp_epoch, lc));
+    }
   }
 #undef YL_LAUNCH
 #undef YL_MV
@@ -860,16 +985,22 @@ int enqueue_forward(Session* s, uint32_t n, uint32_t start_pos, bool from_state,
 
 }  // namespace
 
-int forward(Session* s, const uint32_t* tokens_host, uint32_t n, uint32_t start_pos) {
+int forward(Session* s, const uint32_t* tokens_host, uint32_t n, uint32_t start_pos, bool want_logits) {
   const yl_shape& sh = s->m->shape;
   if (n == 0) return fail(YL_ERR_ARG, "empty token batch");
   if ((uint64_t)start_pos + n > sh.ctx_len) return fail(YL_ERR_RANGE, "position beyond ctx_len");
   YL_CUDA_TRY(cudaSetDevice(s->device));
-  int rc = ensure_cap(s, n);
-  if (rc) return rc;
-  YL_CUDA_TRY(cudaMemcpyAsync(s->tok, tokens_host, (uint64_t)n * 4, cudaMemcpyHostToDevice, s->stream));
-  rc = enqueue_forward(s, n, start_pos, false, tunables().pdl, nullptr);
-  if (rc) return rc;
+  // tensor-parallel passes are limited by the exchange buffers: a longer
+  // prompt runs in chunks (causal attention over the cache makes that exact)
+  const uint32_t chunk = s->m->tp_size > 1 ? s->tp_cap : n;
+  for (uint32_t t0 = 0; t0 < n; t0 += chunk) {
+    const uint32_t nc = std::min(chunk, n - t0);
+    int rc = ensure_cap(s, nc);
+    if (rc) return rc;
+    YL_CUDA_TRY(cudaMemcpyAsync(s->tok, tokens_host + t0, (uint64_t)nc * 4, cudaMemcpyHostToDevice, s->stream));
+    rc = enqueue_forward(s, nc, start_pos + t0, false, tunables().pdl, nullptr, want_logits && t0 + nc == n);
+    if (rc) return rc;
+  }
   return YL_OK;
 }
 
@@ -916,7 +1047,7 @@ int trace_step(Session* s, uint32_t token, uint32_t pos, uint64_t* out, uint64_t
   YL_CUDA_TRY(cudaSetDevice(s->device));
   int rc = ensure_cap(s, 8);
   if (rc) return rc;
-  const uint64_t n_max = 5ull * sh.n_layers + 4;
+  const uint64_t n_max = 7ull * sh.n_layers + 6;
   if (!s->trace) {
     void* p = nullptr;
     if ((rc = salloc(s, n_max * TRACE_STRIDE * 8, &p))) return rc;
@@ -950,7 +1081,22 @@ int trace_step(Session* s, uint32_t token, uint32_t pos, uint64_t* out, uint64_t
   return YL_OK;
 }
 
-int ensure_decode_graph(Session* s) {
+int ensure_decode_graph(Session* s, bool logits) {
+  // tensor-parallel: a second graph gathers the full logits for callers that
+  // read them (one model rank holds only its vocabulary slice)
+  if (logits && s->m->tp_size > 1) {
+    if (s->graph_lg) return YL_OK;
+    cudaGraphExec_t keep = s->graph;
+    s->graph = nullptr;
+    int rc = capture_decode_graph(s, true);
+    s->graph_lg = s->graph;
+    s->graph = keep;
+    return rc;
+  }
+  return capture_decode_graph(s, false);
+}
+
+int capture_decode_graph(Session* s, bool gather) {
   if (s->graph) return YL_OK;
   YL_CUDA_TRY(cudaSetDevice(s->device));
   int rc = ensure_cap(s, 8);
@@ -958,7 +1104,7 @@ int ensure_decode_graph(Session* s) {
   cudaGraph_t g = nullptr;
   YL_CUDA_TRY(cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal));
   uint32_t nl = 0;
-  rc = enqueue_forward(s, 1, 0, true, tunables().pdl, &nl);
+  rc = enqueue_forward(s, 1, 0, true, tunables().pdl, &nl, gather);
   cudaError_t e = cudaStreamEndCapture(s->stream, &g);
   if (rc) { if (g) cudaGraphDestroy(g); return rc; }
   if (e != cudaSuccess) return fail(YL_ERR_CUDA, std::string("graph capture: ") + cudaGetErrorString(e));

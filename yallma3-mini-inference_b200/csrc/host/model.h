@@ -46,6 +46,10 @@ struct Model {
   float2* rope_cs = nullptr;  // [ctx_len][head_size/2] (cos, sin)
   std::vector<void*> allocs;
   uint64_t device_bytes = 0;
+  // tensor parallelism (Megatron split over tp_size ranks): this rank's
+  // query heads, KV heads, ffn rows and vocabulary rows (all of them at 1)
+  int tp_rank = 0, tp_size = 1;
+  uint32_t l_heads = 0, l_kv = 0, l_ffn = 0, l_vocab = 0, vocab0 = 0;
   ~Model();
 };
 
@@ -88,22 +92,39 @@ struct Session {
   uint64_t* trace = nullptr;  // timeline tracing: [launch][TRACE_STRIDE] stamps
   bool trace_on = false;
   cudaGraphExec_t graph = nullptr;
+  cudaGraphExec_t graph_lg = nullptr;  // tensor-parallel decode step that also gathers logits
   uint32_t graph_launches = 0;
+  // tensor parallelism: this rank's exchange region (shared with the peers
+  // through CUDA IPC) and every rank's region as mapped here
+  uint8_t* tp_region = nullptr;
+  uint64_t tp_bytes = 0, tp_flags_off = 0, tp_part_off[2] = {0, 0}, tp_lm_off = 0, tp_logit_off = 0;
+  uint32_t tp_cap = 0;  // tokens per forward the partial buffers hold
+  uint8_t* tp_base[8] = {};
+  std::vector<void*> tp_opened;
+  bool tp_ready = false;
+  uint32_t* tp_epoch = nullptr;  // completed steps (device)
   std::vector<void*> allocs;
   ~Session();
 };
 
-int model_load_gguf(const char* path, uint32_t max_ctx_len, int fmt_override, Model** out);
+int model_load_gguf(const char* path, uint32_t max_ctx_len, int fmt_override, int tp_rank, int tp_size, Model** out);
+// Tensor-parallel sessions: export this rank's exchange-region handle (64
+// bytes, cudaIpcMemHandle_t), then map all ranks' regions (handles[rank]).
+int session_tp_handle(Session* s, void* handle_out);
+int session_tp_connect(Session* s, const void* handles);
 int session_create(const Model* m, Session** out);
 int session_reset(Session* s);
 // General forward over n tokens (prefill or decode); last-token logits stay in
 // s->logits (device), greedy id in s->hist[0].
-int forward(Session* s, const uint32_t* tokens_host, uint32_t n, uint32_t start_pos);
+int forward(Session* s, const uint32_t* tokens_host, uint32_t n, uint32_t start_pos, bool want_logits = true);
 // One batch-1 step launched kernel by kernel (no graph, no PDL) with events
 // between launches; writes per-launch device times in microseconds.
 int profile_step(Session* s, uint32_t token, uint32_t pos, float* us, uint32_t cap, uint32_t* n_out);
-// One batch-1 step through the captured graph (state already set on device).
-int ensure_decode_graph(Session* s);
+// The captured batch-1 decode step (state set on device before a launch):
+// s->graph, or with logits (tensor-parallel) s->graph_lg, which also gathers
+// the full logits.
+int ensure_decode_graph(Session* s, bool logits = false);
+int capture_decode_graph(Session* s, bool gather);  // into s->graph
 // One batch-1 step captured exactly like the decode graph (PDL, state on the
 // device) with every matvec / attention CTA stamping globaltimer at fixed
 // points: out[launch * TRACE_STRIDE + cta * 8 + i].
@@ -139,6 +160,8 @@ struct MvExtra {
   k::StepState* state = nullptr;
   uint64_t* trace = nullptr;   // timeline stamps of this launch (nullable)
   unsigned int* work = nullptr;  // dynamic row-set counters of this launch site (nullable)
+  float* am_shard = nullptr;     // EPI_ARGMAX over a vocabulary shard: published winner
+  uint32_t am_base = 0;          // first vocabulary row of the shard
 };
 int run_matvec_ex(const DevWeight& w, bool f32act, const int8_t* xq, const float* xs, const float* xf,
                   uint64_t x_stride, uint64_t xs_stride, uint32_t ntok, float* out, uint64_t out_stride, int epi,

@@ -86,6 +86,11 @@ struct MvArgs {
   unsigned int* am_count;
   uint32_t* am_out;
   StepState* state;
+  // EPI_ARGMAX over a vocabulary shard (nullable): the winner is published as
+  // {value f32, global index u32 (rows + am_base), first-logit-NaN u32}
+  // instead of updating am_out / state
+  float* am_shard;
+  uint32_t am_base;
   // Dynamic scheduling (nullable): [next row set, CTAs done] counters, zero
   // between launches; CTAs claim 8-row sets from it instead of a static range.
   // Used by the launcher only for single-token passes with >= 4 sets per CTA.
@@ -184,6 +189,29 @@ struct AttnDecodeArgs {
 // can be resident at once, else 8.
 uint32_t attention_decode_splits(uint32_t n_kv_heads, uint32_t head_size);
 cudaError_t attention_decode(const AttnDecodeArgs& a, const LaunchCfg& lc);
+
+// ---- tensor parallelism over peer memory --------------------------------
+// Every rank owns one "exchange region" (cudaMalloc, shared by CUDA IPC) with
+// the same layout; base[r] is rank r's region as mapped in this process.
+// Flags: [sites][world] u32, written by peers (flag[site][src] = epoch).
+struct TpArgs {
+  uint8_t* base[8];
+  uint32_t rank, world;
+  uint32_t site;
+  uint64_t flags_off;
+  const uint32_t* epoch;  // this rank's completed-step counter (the step's epoch is *epoch + 1)
+  int* err;
+};
+// All-reduce + residual add: x[i] += sum over ranks r (in rank order) of
+// rank r's partial [n] at byte offset part_off of its region.
+cudaError_t tp_allreduce_add(const TpArgs& t, uint64_t part_off, uint32_t n, float* x, const LaunchCfg& lc);
+// Vocabulary-parallel greedy id: combines the ranks' published winners
+// ({value, global index, first-logit NaN} at lm_off), writes the id to
+// hist[state ? state->steps : 0], advances state like EPI_ARGMAX, increments
+// *epoch (the step's last collective), and with logits != null gathers every
+// rank's slice [vl] (at logit_off) into logits[V].
+cudaError_t tp_argmax(const TpArgs& t, uint64_t lm_off, uint64_t logit_off, uint32_t vl, float* logits,
+                      uint32_t* hist, StepState* state, uint32_t* epoch, const LaunchCfg& lc);
 
 // Greedy argmax over n logits (sampler.rs:67-79: the lowest index among equal
 // maxima). Writes out[0]; with state != null also state->next/token/pos/steps

@@ -1079,6 +1079,13 @@ __global__ void __launch_bounds__(MV_THREADS, (NT <= 2 ? 2 : 1)) mv_kernel(MvArg
         if (lane == 0) {
           uint32_t res = bi == 0xFFFFFFFFu ? 0u : bi;
           const float l0 = __ldcg(a.out);
+          if (a.am_shard) {  // vocabulary shard: publish (value, global index, first-logit NaN)
+            a.am_shard[0] = bv;
+            reinterpret_cast<uint32_t*>(a.am_shard)[1] = bi == 0xFFFFFFFFu ? 0xFFFFFFFFu : bi + a.am_base;
+            reinterpret_cast<uint32_t*>(a.am_shard)[2] = l0 != l0 ? 1u : 0u;
+            *a.am_count = 0u;
+            return;
+          }
           if (l0 != l0) res = 0;  // reference: a NaN first logit is never beaten
           StepState* st = a.state;
           if (a.am_out) a.am_out[st ? st->steps : 0] = res;
