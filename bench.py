@@ -134,9 +134,9 @@ def ensure_model(yl, rank: int, world: int, dist) -> str:
     return str(path)
 
 
-def time_dominant_matvec(yl, torch, model, cfg: dict, iters: int) -> dict:
-    """Q8_0 gate/up matvec (rows 2*ffn, K = dim) alone, cycling over layers."""
-    L, d, f = cfg["n_layers"], cfg["dim"], cfg["hidden_dim"]
+def time_dominant_matvec(yl, torch, model, cfg: dict, iters: int, world: int = 1) -> dict:
+    """Q8_0 gate/up matvec (rows 2*ffn/world, K = dim) alone, cycling over layers."""
+    L, d, f = cfg["n_layers"], cfg["dim"], cfg["hidden_dim"] // world
     ws = [model.weight(layer, 4) for layer in range(L)]
     x = (torch.randn(d, device="cuda") * 1.0).contiguous()
     xa = yl.new_workspace_buffer(yl.WeightFormat.Q8_0, d, 32)
@@ -292,9 +292,16 @@ def main() -> None:
     cfg = yl.PRESETS[CONFIG]
     path = ensure_model(yl, rank, world, dist)
     t0 = time.time()
-    model = yl.load_transformer(path, max_ctx_len=4096)
+    # N > 1: tensor parallelism over the N GPUs (Megatron shards, exchanges
+    # over NVLink peer memory); one token stream, so N does not multiply value
+    if world > 1:
+        model = yl.load_transformer_tp(path, rank, world, max_ctx_len=4096)
+    else:
+        model = yl.load_transformer(path, max_ctx_len=4096)
     load_s = time.time() - t0
     sess = model.create_session()
+    if world > 1:
+        sess.tp_connect_group()
     prompt = yl.prompt_ids(cfg["vocab_size"], PROMPT_LEN, cfg["seed"] + 1000)
     torch.cuda.synchronize()
     t0 = time.perf_counter()
@@ -338,34 +345,37 @@ def main() -> None:
         t = torch.tensor([e2e_s], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
-    # dominant kernel roofline
-    mv = time_dominant_matvec(yl, torch, model, cfg, 96)
+    # dominant kernel roofline (this rank's gate/up shard)
+    mv = time_dominant_matvec(yl, torch, model, cfg, 96, world)
     peaks = measured_peaks()
     seq_avg = PROMPT_LEN + args.warmup + args.steps / 2.0
     btok = bytes_per_token(cfg, seq_avg)
-    tokps = world * args.steps / (ms * 1e-3)
+    tokps = args.steps / (ms * 1e-3)
     line = {
         "metric": "decode tokens/s (Llama-3-8B-shape Q8_0, batch 1)",
         "value": tokps, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
+        "vs_baseline": None,
         "dtype": "int8 dot / f32 accumulate", "data": "synthetic",
         "config": {"workload": "config 4: Llama-3-8B-shaped Q8_0 (random-init, seed 3), prompt 512, "
                                "batch-1 greedy decode from position 512",
-                   "model": "llama-3-8b-shape-q8_0", "global_batch": world, "seq_len": PROMPT_LEN,
-                   "parallelism": "replicas" if world > 1 else "single",
+                   "model": "llama-3-8b-shape-q8_0", "global_batch": 1, "seq_len": PROMPT_LEN,
+                   "parallelism": f"tp{world}" if world > 1 else "single",
                    "l2": "weights 8.1 GB per token > 126 MB L2 (no flush needed)"},
-        "e2e": {"value": world * e2e_steps / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": 16,
+        "e2e": {"value": e2e_steps / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": 16,
                 "d2h_bytes_per_step": 4 * cfg["vocab_size"] + 4,
                 "call": "yl_forward_x (Transformer::forward_x), logits + greedy id to host"},
-        "roofline": {"bound": "hbm", "kernel": "mv_kernel<Q8,NT=1> gate/up 28672x4096",
+        "roofline": {"bound": "hbm", "kernel": f"mv_kernel<Q8,NT=1> gate/up {2 * cfg['hidden_dim'] // world}x4096",
                      "achieved": mv["gbs"], "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": mv["gbs"] / peaks["hbm_gbs"], "peak_src": peaks["src"],
                      # DRAM read + write bytes of one launch of this kernel and shape from
                      # one ncu capture (profiles/mv_kernel_gateup_28672x4096.md)
-                     "traffic": TRAFFIC_GATEUP_BYTES, "traffic_unit": "bytes per launch",
+                     "traffic": TRAFFIC_GATEUP_BYTES if world == 1 else None, "traffic_unit": "bytes per launch",
                      "algorithmic_bytes": mv["bytes"], "launch_ms": mv["ms"]},
-        "step_roofline": {"bytes_per_token": btok, "achieved_gbs": btok / (ms / args.steps * 1e-3) / 1e9,
-                          "frac": btok / (ms / args.steps * 1e-3) / 1e9 / peaks["hbm_gbs"]},
+        # per GPU: each rank streams its shard (1/N of the weights) per token
+        "step_roofline": {"bytes_per_token": btok, "bytes_per_token_per_gpu": btok / world,
+                          "achieved_gbs_per_gpu": btok / world / (ms / args.steps * 1e-3) / 1e9,
+                          "frac": btok / world / (ms / args.steps * 1e-3) / 1e9 / peaks["hbm_gbs"]},
         "gpu_launches": model.decode_step_launches() * args.steps,
         "clocks": clk.summary(),
         "prefill": {"tokens": PROMPT_LEN, "s": prefill_s, "tokens_per_s": PROMPT_LEN / prefill_s},
