@@ -274,16 +274,16 @@ constexpr int AD_MAXCS = 16;     // largest cluster (non-portable size)
 template <int HD>
 struct AdLayout {
   static constexpr int ROW = HD + 4;             // padded row (floats): 16-byte aligned
-  static constexpr int NPH = AD_THREADS / HD;    // P.V position groups
   static constexpr int KS = 0;
   static constexpr int VS = KS + AD_TILE * ROW;
+  static constexpr int WO = KS;                             // [8 warps][AT_MAXKV][HD] warp partials (after the tiles)
   static constexpr int QS = VS + AD_TILE * ROW;             // [AT_MAXKV][HD] rotated q
-  static constexpr int SP = QS + AT_MAXKV * HD;             // [4][AT_MAXKV][AD_TILE] partial scores
-  static constexpr int PT = SP + 4 * AT_MAXKV * AD_TILE;    // [AD_TILE][AT_MAXKV] probabilities
-  static constexpr int PO = PT + AD_TILE * AT_MAXKV;        // [NPH][AT_MAXKV][HD] P.V partials
-  static constexpr int OS = PO + NPH * AT_MAXKV * HD;       // [AT_MAXKV][HD] unnormalized output
-  static constexpr int STAT = OS + AT_MAXKV * HD;           // m, l, corr [AT_MAXKV] each
-  static constexpr int TOTAL = STAT + 3 * AT_MAXKV;
+  static constexpr int NK = QS + AT_MAXKV * HD;             // owner: new key (rotated) and value rows [2][HD]
+  static constexpr int WS = NK + 2 * HD;                    // [8][AT_MAXKV] warp max, then [8][AT_MAXKV] warp sum
+  static constexpr int OS = WS + 2 * 8 * AT_MAXKV;          // [AT_MAXKV][HD] CTA partial, unnormalized
+  static constexpr int STAT = OS + AT_MAXKV * HD;           // m, l [AT_MAXKV] each
+  static constexpr int TOTAL = STAT + 2 * AT_MAXKV;
+  static_assert(8 * AT_MAXKV * HD <= 2 * AD_TILE * ROW, "warp partials fit the tile area");
 };
 
 __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
@@ -297,26 +297,33 @@ __device__ __forceinline__ void cp_async_wait_all() {
 // matvec CTA (9 warps, 96 registers) fit one SM together, two plus three
 // warps per sub-partition within its 16K registers, so the next projection's
 // CTAs become resident and stream their weights while attention runs.
-template <int HD>
+//
+// Per CTA: warp w takes the positions w, w+8, ... of each key tile; lane j
+// holds dims [j*E, j*E+E) of q, k, v and of its running output for all KVM
+// heads, so a position costs one k and one v load per lane, a butterfly
+// per head for the score, and an online-softmax update in registers
+// (forward.rs:328-399). The eight warp partials are combined once per CTA.
+template <int HD, int KVM>
 __global__ void __maxnreg__(96) attn_decode_kernel(AttnDecodeArgs a) {
   using Lo = AdLayout<HD>;
+  constexpr int E = HD / 32;
   extern __shared__ __align__(16) float sm[];
   cg::cluster_group cluster = cg::this_cluster();
   float* Ks = sm + Lo::KS;
   float* Vs = sm + Lo::VS;
   float* qs = sm + Lo::QS;
-  float* sp4 = sm + Lo::SP;
-  float* pt = sm + Lo::PT;
-  float* po = sm + Lo::PO;
+  float* nk = sm + Lo::NK;
+  float* wo = sm + Lo::WO;
+  float* wm = sm + Lo::WS;
+  float* wl = wm + 8 * AT_MAXKV;
   float* os = sm + Lo::OS;
   float* ms = sm + Lo::STAT;
   float* ls = ms + AT_MAXKV;
-  float* cr = ls + AT_MAXKV;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t cs = a.n_splits;
   const uint32_t rank = cluster.block_rank();
   const uint32_t kvh = blockIdx.x / cs;
-  const uint32_t kv_mul = a.n_heads / a.n_kv_heads;
+  constexpr uint32_t kv_mul = KVM;
   uint64_t* const trace = a.trace ? a.trace + (uint64_t)blockIdx.x * 8 : nullptr;
   if (trace && tid == 0) trace[0] = globaltimer();
   grid_dep_launch();
@@ -333,7 +340,7 @@ __global__ void __maxnreg__(96) attn_decode_kernel(AttnDecodeArgs a) {
   auto issue_tile = [&](uint32_t base, uint32_t n) {
     for (uint32_t i = tid; i < n * (HD / 4); i += AD_THREADS) {
       const uint32_t r = i / (HD / 4), c4 = i % (HD / 4);
-      if (base + r == pos) continue;  // the new row is placed below
+      if (base + r == pos) continue;  // the new row is placed from nk
       cp_async16(Ks + r * Lo::ROW + 4 * c4, kbase + (uint64_t)(base + r) * a.kv_dim + 4 * c4);
       cp_async16(Vs + r * Lo::ROW + 4 * c4, vbase + (uint64_t)(base + r) * a.kv_dim + 4 * c4);
     }
@@ -343,26 +350,43 @@ __global__ void __maxnreg__(96) attn_decode_kernel(AttnDecodeArgs a) {
   if (a.early_kv) grid_dep_wait();
   if (trace && tid == 0) trace[1] = globaltimer();
 
-  // rotated q of the kv_mul query heads; running statistics
+  // rotated q of the KVM query heads, and (owner) the new key and value rows,
+  // all from the fused projection output in one round of loads
   const float2* c = a.cs + (uint64_t)pos * half;
-  for (uint32_t i = tid; i < kv_mul * half; i += AD_THREADS) {
+  for (uint32_t i = tid; i < (kv_mul + (owner ? 1u : 0u)) * half; i += AD_THREADS) {
     const uint32_t hh = i / half, p = i % half;
     uint32_t i0, i1;
     pair_index(a.rope_mode, p, half, i0, i1);
-    const float* src = a.qkv + (kvh * kv_mul + hh) * HD;
+    const float* src = hh < kv_mul ? a.qkv + (kvh * kv_mul + hh) * HD : a.qkv + att + kvh * HD;
     float r0, r1;
     rotate(src[i0], src[i1], c[p], r0, r1);
-    qs[hh * HD + i0] = r0;
-    qs[hh * HD + i1] = r1;
+    float* dst = hh < kv_mul ? qs + hh * HD : nk;
+    dst[i0] = r0;
+    dst[i1] = r1;
   }
-  for (uint32_t i = tid; i < AT_MAXKV * HD; i += AD_THREADS) os[i] = 0.0f;
-  for (uint32_t i = tid; i < AD_TILE * AT_MAXKV; i += AD_THREADS) pt[i] = 0.0f;  // unused heads stay 0
-  if (tid < AT_MAXKV) {
-    ms[tid] = -INFINITY;
-    ls[tid] = 0.0f;
-    cr[tid] = 0.0f;
+  if (owner) {
+    for (uint32_t d = tid; d < HD; d += AD_THREADS) nk[HD + d] = a.qkv[att + a.kv_dim + kvh * HD + d];
   }
-  __syncthreads();  // an empty split goes straight to the merge
+  __syncthreads();
+  if (owner) {  // the new rows go to the cache
+    float* kdst = a.kcache + (uint64_t)pos * a.kv_dim + kvh * HD;
+    float* vdst = a.vcache + (uint64_t)pos * a.kv_dim + kvh * HD;
+    for (uint32_t d = tid; d < HD; d += AD_THREADS) {
+      kdst[d] = nk[d];
+      vdst[d] = nk[HD + d];
+    }
+  }
+  float qr[KVM][E], acc[KVM][E], m[KVM], l[KVM];
+#pragma unroll
+  for (int h = 0; h < KVM; ++h) {
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      qr[h][e] = qs[h * HD + lane * E + e];
+      acc[h][e] = 0.0f;
+    }
+    m[h] = -INFINITY;
+    l[h] = 0.0f;
+  }
   if (trace && tid == 0) trace[4] = globaltimer();
 
   const uint32_t ntiles = (p_end - p_begin + AD_TILE - 1) / AD_TILE;
@@ -371,133 +395,79 @@ __global__ void __maxnreg__(96) attn_decode_kernel(AttnDecodeArgs a) {
     tn = min((uint32_t)AD_TILE, p_end - t0);
     if (ti > 0) issue_tile(t0, tn);
     if (owner && pos >= t0 && pos < t0 + tn) {
-      // new key (rotated) and value rows: cache write + tile placement
-      const float* ksrc = a.qkv + att + kvh * HD;
-      const float* vsrc = a.qkv + att + a.kv_dim + kvh * HD;
-      float* kdst = a.kcache + (uint64_t)pos * a.kv_dim + kvh * HD;
-      float* vdst = a.vcache + (uint64_t)pos * a.kv_dim + kvh * HD;
       const uint32_t r = pos - t0;
-      for (uint32_t p = tid; p < half; p += AD_THREADS) {
-        uint32_t i0, i1;
-        pair_index(a.rope_mode, p, half, i0, i1);
-        float r0, r1;
-        rotate(ksrc[i0], ksrc[i1], c[p], r0, r1);
-        kdst[i0] = r0;
-        kdst[i1] = r1;
-        Ks[r * Lo::ROW + i0] = r0;
-        Ks[r * Lo::ROW + i1] = r1;
-      }
       for (uint32_t d = tid; d < HD; d += AD_THREADS) {
-        const float v = vsrc[d];
-        vdst[d] = v;
-        Vs[r * Lo::ROW + d] = v;
+        Ks[r * Lo::ROW + d] = nk[d];
+        Vs[r * Lo::ROW + d] = nk[HD + d];
       }
     }
     cp_async_wait_all();
     __syncthreads();
     if (trace && tid == 0 && ti == 0) trace[5] = globaltimer();
-    // scores (forward.rs:328-346): thread (position p, dim quarter dq) forms
-    // the partial dots of all kv_mul heads; K rows are read once per quarter
-    {
-      constexpr int DQ = HD / 4;
-      const uint32_t p = tid % AD_TILE, dq = tid / AD_TILE;
-      float s[AT_MAXKV];
+    for (uint32_t pp = warp; pp < tn; pp += AD_THREADS / 32) {
+      float k[E], v[E];
 #pragma unroll
-      for (int h = 0; h < AT_MAXKV; ++h) s[h] = 0.0f;
-      if (p < tn) {
-        const float* kr = Ks + p * Lo::ROW + dq * DQ;
-#pragma unroll 4
-        for (int j = 0; j < DQ; j += 4) {
-          const float4 k4 = *reinterpret_cast<const float4*>(kr + j);
+      for (int e = 0; e < E; ++e) {
+        k[e] = Ks[pp * Lo::ROW + lane * E + e];
+        v[e] = Vs[pp * Lo::ROW + lane * E + e];
+      }
+      float sc[KVM];
 #pragma unroll
-          for (int h = 0; h < AT_MAXKV; ++h) {
-            if (h >= (int)kv_mul) break;
-            const float4 q4 = *reinterpret_cast<const float4*>(qs + h * HD + dq * DQ + j);
-            s[h] = fmaf(q4.x, k4.x, s[h]);
-            s[h] = fmaf(q4.y, k4.y, s[h]);
-            s[h] = fmaf(q4.z, k4.z, s[h]);
-            s[h] = fmaf(q4.w, k4.w, s[h]);
-          }
-        }
+      for (int h = 0; h < KVM; ++h) {
+        float t = 0.0f;
+#pragma unroll
+        for (int e = 0; e < E; ++e) t = fmaf(qr[h][e], k[e], t);
+        sc[h] = t;
       }
 #pragma unroll
-      for (int h = 0; h < AT_MAXKV; ++h)
-        if (h < (int)kv_mul) sp4[(dq * AT_MAXKV + h) * AD_TILE + p] = s[h];
-    }
-    __syncthreads();
-    // online softmax update, warp per query head (forward.rs:348-366)
-    for (uint32_t hh = warp; hh < kv_mul; hh += AD_THREADS / 32) {
-      float sv[2];
-      float mx = -INFINITY;
+      for (int o = 16; o > 0; o >>= 1)
 #pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const uint32_t p = lane + 32 * u;
-        float v = -INFINITY;
-        if (p < tn) {
-          const float* b = sp4 + hh * AD_TILE + p;
-          v = __fmul_rn(b[0] + b[AT_MAXKV * AD_TILE] + b[2 * AT_MAXKV * AD_TILE] + b[3 * AT_MAXKV * AD_TILE],
-                        a.scale);
-        }
-        sv[u] = v;
-        mx = fmaxf(mx, v);
-      }
-      mx = warp_max(mx);
-      const float m_old = ms[hh];
-      const float m_new = fmaxf(m_old, mx);
-      float sum = 0.0f;
+        for (int h = 0; h < KVM; ++h) sc[h] += __shfl_xor_sync(FULL, sc[h], o);
 #pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const uint32_t p = lane + 32 * u;
-        const float e = p < tn ? expf(sv[u] - m_new) : 0.0f;
-        pt[p * AT_MAXKV + hh] = e;
-        sum += e;
-      }
-      sum = warp_sum(sum);
-      if (lane == 0) {
-        const float cf = expf(m_old - m_new);
-        cr[hh] = cf;
-        ls[hh] = ls[hh] * cf + sum;
-        ms[hh] = m_new;
+      for (int h = 0; h < KVM; ++h) {
+        const float s = __fmul_rn(sc[h], a.scale);  // (q.k) * scale (forward.rs:328-346)
+        const float mn = fmaxf(m[h], s);
+        const float cf = expf(m[h] - mn);  // 0 while m is -inf
+        const float p = expf(s - mn);
+        l[h] = fmaf(l[h], cf, p);
+#pragma unroll
+        for (int e = 0; e < E; ++e) acc[h][e] = fmaf(acc[h][e], cf, p * v[e]);
+        m[h] = mn;
       }
     }
-    __syncthreads();
-    // P.V (forward.rs:368-399): thread (dim d, position group g), all heads
-    {
-      constexpr int PPG = AD_TILE / Lo::NPH;
-      const uint32_t d = tid % HD, g = tid / HD;
-      float acc[AT_MAXKV];
-#pragma unroll
-      for (int h = 0; h < AT_MAXKV; ++h) acc[h] = 0.0f;
-      const uint32_t pe = min(tn, (g + 1) * PPG);
-      for (uint32_t pp = g * PPG; pp < pe; ++pp) {
-        const float v = Vs[pp * Lo::ROW + d];
-        const float4 pa = *reinterpret_cast<const float4*>(pt + pp * AT_MAXKV);
-        const float4 pb = *reinterpret_cast<const float4*>(pt + pp * AT_MAXKV + 4);
-        acc[0] = fmaf(pa.x, v, acc[0]);
-        acc[1] = fmaf(pa.y, v, acc[1]);
-        acc[2] = fmaf(pa.z, v, acc[2]);
-        acc[3] = fmaf(pa.w, v, acc[3]);
-        acc[4] = fmaf(pb.x, v, acc[4]);
-        acc[5] = fmaf(pb.y, v, acc[5]);
-        acc[6] = fmaf(pb.z, v, acc[6]);
-        acc[7] = fmaf(pb.w, v, acc[7]);
-      }
-#pragma unroll
-      for (int h = 0; h < AT_MAXKV; ++h)
-        if (h < (int)kv_mul) po[(g * AT_MAXKV + h) * HD + d] = acc[h];
-    }
-    __syncthreads();
-    for (uint32_t i = tid; i < kv_mul * HD; i += AD_THREADS) {
-      const uint32_t hh = i / HD, d = i % HD;
-      float o = os[hh * HD + d] * cr[hh];
-#pragma unroll
-      for (int g = 0; g < Lo::NPH; ++g) o += po[(g * AT_MAXKV + hh) * HD + d];
-      os[hh * HD + d] = o;
-    }
-    __syncthreads();
+    __syncthreads();  // the tile area is reloaded or reused below
   }
-
+  // warp partials -> CTA partial (unnormalized, with its max and sum)
+#pragma unroll
+  for (int h = 0; h < KVM; ++h) {
+#pragma unroll
+    for (int e = 0; e < E; ++e) wo[(warp * AT_MAXKV + h) * HD + lane * E + e] = acc[h][e];
+    if (lane == 0) {
+      wm[warp * AT_MAXKV + h] = m[h];
+      wl[warp * AT_MAXKV + h] = l[h];
+    }
+  }
+  __syncthreads();
   if (trace && tid == 0) trace[6] = globaltimer();
+  for (uint32_t i = tid; i < kv_mul * HD; i += AD_THREADS) {
+    const uint32_t hh = i / HD, d = i % HD;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) M = fmaxf(M, wm[w * AT_MAXKV + hh]);
+    float O = 0.0f, Lsum = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      const float mw = wm[w * AT_MAXKV + hh];
+      const float wgt = mw == -INFINITY ? 0.0f : expf(mw - M);
+      O = fmaf(wo[(w * AT_MAXKV + hh) * HD + d], wgt, O);
+      Lsum = fmaf(wl[w * AT_MAXKV + hh], wgt, Lsum);
+    }
+    os[hh * HD + d] = O;
+    if (d == 0) {
+      ms[hh] = M;
+      ls[hh] = Lsum;
+    }
+  }
   // every split's partial is in its CTA's shared memory
   cluster.sync();
   if (trace && tid == 0) trace[2] = globaltimer();
@@ -543,12 +513,14 @@ __global__ void __maxnreg__(96) attn_decode_kernel(AttnDecodeArgs a) {
   if (trace && tid == 0) trace[3] = globaltimer();
 }
 
-template <int HD>
+template <int HD, int KVM>
 static cudaError_t decode_config(uint32_t n_kv_heads, uint32_t cs, cudaStream_t st, bool pdl, cudaLaunchConfig_t& cfg,
                                  cudaLaunchAttribute (&attr)[2]) {
   const uint32_t smem = AdLayout<HD>::TOTAL * sizeof(float);
-  cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e == cudaSuccess) e = cudaFuncSetAttribute(attn_decode_kernel<HD>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  cudaError_t e =
+      cudaFuncSetAttribute(attn_decode_kernel<HD, KVM>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(attn_decode_kernel<HD, KVM>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
   if (e != cudaSuccess) return e;
   cfg = {};
   cfg.gridDim = dim3(n_kv_heads * cs);
@@ -566,37 +538,54 @@ static cudaError_t decode_config(uint32_t n_kv_heads, uint32_t cs, cudaStream_t 
   return cudaSuccess;
 }
 
-uint32_t attention_decode_splits(uint32_t n_kv_heads, uint32_t head_size) {
+template <int HD>
+static uint32_t decode_splits_hd(uint32_t n_kv_heads) {
   for (uint32_t cs : {16u, 8u}) {
     cudaLaunchConfig_t cfg;
     cudaLaunchAttribute attr[2];
     int n = 0;
-    cudaError_t e = head_size == 64 ? decode_config<64>(n_kv_heads, cs, nullptr, false, cfg, attr)
-                                    : decode_config<128>(n_kv_heads, cs, nullptr, false, cfg, attr);
-    if (e == cudaSuccess)
-      e = head_size == 64 ? cudaOccupancyMaxActiveClusters(&n, attn_decode_kernel<64>, &cfg)
-                          : cudaOccupancyMaxActiveClusters(&n, attn_decode_kernel<128>, &cfg);
+    cudaError_t e = decode_config<HD, 4>(n_kv_heads, cs, nullptr, false, cfg, attr);
+    if (e == cudaSuccess) e = cudaOccupancyMaxActiveClusters(&n, attn_decode_kernel<HD, 4>, &cfg);
     if (e != cudaSuccess) (void)cudaGetLastError();
     if (e == cudaSuccess && n >= (int)n_kv_heads) return cs;
   }
   return 8;
 }
 
+uint32_t attention_decode_splits(uint32_t n_kv_heads, uint32_t head_size) {
+  return head_size == 64 ? decode_splits_hd<64>(n_kv_heads) : decode_splits_hd<128>(n_kv_heads);
+}
+
+template <int HD, int KVM>
+static cudaError_t launch_decode(const AttnDecodeArgs& a, const LaunchCfg& lc) {
+  cudaLaunchConfig_t cfg;
+  cudaLaunchAttribute attr[2];
+  cudaError_t e = decode_config<HD, KVM>(a.n_kv_heads, a.n_splits, lc.stream, lc.pdl, cfg, attr);
+  if (e != cudaSuccess) return e;
+  return cudaLaunchKernelEx(&cfg, attn_decode_kernel<HD, KVM>, a);
+}
+
+template <int HD>
+static cudaError_t launch_decode_hd(const AttnDecodeArgs& a, const LaunchCfg& lc, uint32_t kv_mul) {
+  switch (kv_mul) {
+    case 1: return launch_decode<HD, 1>(a, lc);
+    case 2: return launch_decode<HD, 2>(a, lc);
+    case 3: return launch_decode<HD, 3>(a, lc);
+    case 4: return launch_decode<HD, 4>(a, lc);
+    case 5: return launch_decode<HD, 5>(a, lc);
+    case 6: return launch_decode<HD, 6>(a, lc);
+    case 7: return launch_decode<HD, 7>(a, lc);
+    case 8: return launch_decode<HD, 8>(a, lc);
+  }
+  return cudaErrorInvalidValue;
+}
+
 cudaError_t attention_decode(const AttnDecodeArgs& a, const LaunchCfg& lc) {
   const uint32_t kv_mul = a.n_kv_heads ? a.n_heads / a.n_kv_heads : 0;
   if (kv_mul == 0 || kv_mul > AT_MAXKV || a.n_splits == 0 || a.n_splits > AD_MAXCS) return cudaErrorInvalidValue;
   if (a.kv_dim % 4 || ((uintptr_t)a.kcache | (uintptr_t)a.vcache) % 16) return cudaErrorInvalidValue;
-  cudaLaunchConfig_t cfg;
-  cudaLaunchAttribute attr[2];
-  cudaError_t e;
-  if (a.head_size == 64) {
-    if ((e = decode_config<64>(a.n_kv_heads, a.n_splits, lc.stream, lc.pdl, cfg, attr)) != cudaSuccess) return e;
-    return cudaLaunchKernelEx(&cfg, attn_decode_kernel<64>, a);
-  }
-  if (a.head_size == 128) {
-    if ((e = decode_config<128>(a.n_kv_heads, a.n_splits, lc.stream, lc.pdl, cfg, attr)) != cudaSuccess) return e;
-    return cudaLaunchKernelEx(&cfg, attn_decode_kernel<128>, a);
-  }
+  if (a.head_size == 64) return launch_decode_hd<64>(a, lc, kv_mul);
+  if (a.head_size == 128) return launch_decode_hd<128>(a, lc, kv_mul);
   return cudaErrorInvalidValue;
 }
 
