@@ -258,18 +258,20 @@ cudaError_t attention(const AttnArgs& a, const LaunchCfg& lc) {
 // head; CTA `rank` of the cluster takes the rank-th slice of the keys:
 //  * the slice's K and V rows are fetched with cp.async in one round trip
 //    (before the wait on the preceding kernel when early_kv is set), while q
-//    is rotated (RoPE) from the fused projection output;
-//  * the CTA that owns position `pos` rotates the new key, writes the new
-//    K/V rows to the cache and places them in its tile directly;
-//  * scores: thread (position, dim quarter) over all kv_mul query heads at
-//    once; online softmax per head; P.V: thread (dim, position group);
-//  * the splits' (max, sum, unnormalized output) partials stay in shared
-//    memory; after a cluster barrier every CTA merges a share of the 32-blocks
-//    of the KV head's output from its peers' shared memory and quantizes them.
+//    (and, in the CTA owning position `pos`, the new key and value rows) is
+//    read from the fused projection output and rotated (RoPE);
+//  * the owner writes the new K/V rows to the cache and into its tile;
+//  * each warp runs attention over its positions in registers (see the
+//    kernel), the CTA combines its eight warp partials;
+//  * every CTA pushes its (max, sum, unnormalized output) partial of each
+//    32-block of the KV head's output into the CTA that merges that block
+//    (distributed shared memory); after one cluster barrier each CTA merges
+//    and quantizes its blocks from its own shared memory.
 namespace cg = cooperative_groups;
 constexpr int AD_TILE = 64;      // positions per shared-memory tile
 constexpr int AD_THREADS = 256;
 constexpr int AD_MAXCS = 16;     // largest cluster (non-portable size)
+constexpr int AD_MAXSLOT = 4;    // output 32-blocks a CTA merges: kv_mul*HD/32/cs <= 8*128/32/8
 
 template <int HD>
 struct AdLayout {
@@ -280,9 +282,8 @@ struct AdLayout {
   static constexpr int QS = VS + AD_TILE * ROW;             // [AT_MAXKV][HD] rotated q
   static constexpr int NK = QS + AT_MAXKV * HD;             // owner: new key (rotated) and value rows [2][HD]
   static constexpr int WS = NK + 2 * HD;                    // [8][AT_MAXKV] warp max, then [8][AT_MAXKV] warp sum
-  static constexpr int OS = WS + 2 * 8 * AT_MAXKV;          // [AT_MAXKV][HD] CTA partial, unnormalized
-  static constexpr int STAT = OS + AT_MAXKV * HD;           // m, l [AT_MAXKV] each
-  static constexpr int TOTAL = STAT + 2 * AT_MAXKV;
+  static constexpr int RECV = WS + 2 * 8 * AT_MAXKV;        // [AD_MAXSLOT][AD_MAXCS][34] pushed block partials
+  static constexpr int TOTAL = RECV + AD_MAXSLOT * AD_MAXCS * 34;
   static_assert(8 * AT_MAXKV * HD <= 2 * AD_TILE * ROW, "warp partials fit the tile area");
 };
 
@@ -316,16 +317,14 @@ __global__ void __maxnreg__(96) attn_decode_kernel(AttnDecodeArgs a) {
   float* wo = sm + Lo::WO;
   float* wm = sm + Lo::WS;
   float* wl = wm + 8 * AT_MAXKV;
-  float* os = sm + Lo::OS;
-  float* ms = sm + Lo::STAT;
-  float* ls = ms + AT_MAXKV;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t cs = a.n_splits;
   const uint32_t rank = cluster.block_rank();
   const uint32_t kvh = blockIdx.x / cs;
   constexpr uint32_t kv_mul = KVM;
   uint64_t* const trace = a.trace ? a.trace + (uint64_t)blockIdx.x * 8 : nullptr;
-  if (trace && tid == 0) trace[0] = globaltimer();
+  uint64_t ts[8] = {0, 0, 0, 0, 0, 0, 0, 0};  // timeline stamps, stored at the end
+  if (trace && tid == 0) ts[0] = globaltimer();
   grid_dep_launch();
   if (!a.early_kv) grid_dep_wait();
   const uint32_t pos = a.state ? (uint32_t)a.state->pos : a.pos0;
@@ -348,7 +347,7 @@ __global__ void __maxnreg__(96) attn_decode_kernel(AttnDecodeArgs a) {
   uint32_t t0 = p_begin, tn = min((uint32_t)AD_TILE, p_end - p_begin);
   if (tn) issue_tile(t0, tn);
   if (a.early_kv) grid_dep_wait();
-  if (trace && tid == 0) trace[1] = globaltimer();
+  if (trace && tid == 0) ts[1] = globaltimer();
 
   // rotated q of the KVM query heads, and (owner) the new key and value rows,
   // all from the fused projection output in one round of loads
@@ -368,14 +367,6 @@ __global__ void __maxnreg__(96) attn_decode_kernel(AttnDecodeArgs a) {
     for (uint32_t d = tid; d < HD; d += AD_THREADS) nk[HD + d] = a.qkv[att + a.kv_dim + kvh * HD + d];
   }
   __syncthreads();
-  if (owner) {  // the new rows go to the cache
-    float* kdst = a.kcache + (uint64_t)pos * a.kv_dim + kvh * HD;
-    float* vdst = a.vcache + (uint64_t)pos * a.kv_dim + kvh * HD;
-    for (uint32_t d = tid; d < HD; d += AD_THREADS) {
-      kdst[d] = nk[d];
-      vdst[d] = nk[HD + d];
-    }
-  }
   float qr[KVM][E], acc[KVM][E], m[KVM], l[KVM];
 #pragma unroll
   for (int h = 0; h < KVM; ++h) {
@@ -387,7 +378,7 @@ __global__ void __maxnreg__(96) attn_decode_kernel(AttnDecodeArgs a) {
     m[h] = -INFINITY;
     l[h] = 0.0f;
   }
-  if (trace && tid == 0) trace[4] = globaltimer();
+  if (trace && tid == 0) ts[4] = globaltimer();
 
   const uint32_t ntiles = (p_end - p_begin + AD_TILE - 1) / AD_TILE;
   for (uint32_t ti = 0; ti < ntiles; ++ti) {
@@ -403,35 +394,53 @@ __global__ void __maxnreg__(96) attn_decode_kernel(AttnDecodeArgs a) {
     }
     cp_async_wait_all();
     __syncthreads();
-    if (trace && tid == 0 && ti == 0) trace[5] = globaltimer();
-    for (uint32_t pp = warp; pp < tn; pp += AD_THREADS / 32) {
-      float k[E], v[E];
+    if (trace && tid == 0 && ti == 0) ts[5] = globaltimer();
+    // two positions per step (p0 and p0 + 8): their loads, dots and
+    // butterflies interleave, and one softmax update absorbs both. The
+    // exponentials use the hardware exp2 (__expf): a few ulp on weights in
+    // [0, 1], far inside the logit tolerance, and one instruction instead of
+    // a range-reduced sequence on this latency-bound chain.
+    for (uint32_t p0 = warp; p0 < tn; p0 += 2 * (AD_THREADS / 32)) {
+      const uint32_t p1 = p0 + AD_THREADS / 32;
+      const bool two = p1 < tn;  // warp-uniform
+      float k0[E], v0[E], k1[E], v1[E];
 #pragma unroll
       for (int e = 0; e < E; ++e) {
-        k[e] = Ks[pp * Lo::ROW + lane * E + e];
-        v[e] = Vs[pp * Lo::ROW + lane * E + e];
+        k0[e] = Ks[p0 * Lo::ROW + lane * E + e];
+        v0[e] = Vs[p0 * Lo::ROW + lane * E + e];
+        k1[e] = two ? Ks[p1 * Lo::ROW + lane * E + e] : 0.0f;
+        v1[e] = two ? Vs[p1 * Lo::ROW + lane * E + e] : 0.0f;
       }
-      float sc[KVM];
+      float s0[KVM], s1[KVM];
 #pragma unroll
       for (int h = 0; h < KVM; ++h) {
-        float t = 0.0f;
+        float t0v = 0.0f, t1v = 0.0f;
 #pragma unroll
-        for (int e = 0; e < E; ++e) t = fmaf(qr[h][e], k[e], t);
-        sc[h] = t;
+        for (int e = 0; e < E; ++e) {
+          t0v = fmaf(qr[h][e], k0[e], t0v);
+          t1v = fmaf(qr[h][e], k1[e], t1v);
+        }
+        s0[h] = t0v;
+        s1[h] = t1v;
       }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1)
 #pragma unroll
-        for (int h = 0; h < KVM; ++h) sc[h] += __shfl_xor_sync(FULL, sc[h], o);
+        for (int h = 0; h < KVM; ++h) {
+          s0[h] += __shfl_xor_sync(FULL, s0[h], o);
+          s1[h] += __shfl_xor_sync(FULL, s1[h], o);
+        }
 #pragma unroll
       for (int h = 0; h < KVM; ++h) {
-        const float s = __fmul_rn(sc[h], a.scale);  // (q.k) * scale (forward.rs:328-346)
-        const float mn = fmaxf(m[h], s);
-        const float cf = expf(m[h] - mn);  // 0 while m is -inf
-        const float p = expf(s - mn);
-        l[h] = fmaf(l[h], cf, p);
+        const float a0 = __fmul_rn(s0[h], a.scale);  // (q.k) * scale (forward.rs:328-346)
+        const float a1 = two ? __fmul_rn(s1[h], a.scale) : -INFINITY;
+        const float mn = fmaxf(m[h], fmaxf(a0, a1));
+        const float cf = __expf(m[h] - mn);  // 0 while m is -inf
+        const float e0 = __expf(a0 - mn);
+        const float e1 = two ? __expf(a1 - mn) : 0.0f;
+        l[h] = fmaf(l[h], cf, e0 + e1);
 #pragma unroll
-        for (int e = 0; e < E; ++e) acc[h][e] = fmaf(acc[h][e], cf, p * v[e]);
+        for (int e = 0; e < E; ++e) acc[h][e] = fmaf(acc[h][e], cf, fmaf(e0, v0[e], e1 * v1[e]));
         m[h] = mn;
       }
     }
@@ -448,7 +457,12 @@ __global__ void __maxnreg__(96) attn_decode_kernel(AttnDecodeArgs a) {
     }
   }
   __syncthreads();
-  if (trace && tid == 0) trace[6] = globaltimer();
+  if (trace && tid == 0) ts[6] = globaltimer();
+  // The KV head's kv_mul*HD outputs form 32-blocks; block b is merged by CTA
+  // b % cs. Each CTA pushes its partial of every block, with the head's max
+  // and sum, into the merging CTA's shared memory (distributed shared
+  // memory); one cluster barrier later every CTA merges its blocks locally.
+  float* recv = sm + Lo::RECV;  // [AD_MAXSLOT][AD_MAXCS][34]: 32 outputs, max, sum
   for (uint32_t i = tid; i < kv_mul * HD; i += AD_THREADS) {
     const uint32_t hh = i / HD, d = i % HD;
     float M = -INFINITY;
@@ -458,46 +472,33 @@ __global__ void __maxnreg__(96) attn_decode_kernel(AttnDecodeArgs a) {
 #pragma unroll
     for (int w = 0; w < 8; ++w) {
       const float mw = wm[w * AT_MAXKV + hh];
-      const float wgt = mw == -INFINITY ? 0.0f : expf(mw - M);
+      const float wgt = mw == -INFINITY ? 0.0f : __expf(mw - M);
       O = fmaf(wo[(w * AT_MAXKV + hh) * HD + d], wgt, O);
       Lsum = fmaf(wl[w * AT_MAXKV + hh], wgt, Lsum);
     }
-    os[hh * HD + d] = O;
-    if (d == 0) {
-      ms[hh] = M;
-      ls[hh] = Lsum;
+    const uint32_t b = i / 32, j = i % 32;
+    float* dst = cluster.map_shared_rank(recv, b % cs) + ((b / cs) * AD_MAXCS + rank) * 34;
+    dst[j] = O;
+    if (j == 0) {
+      dst[32] = M;
+      dst[33] = Lsum;
     }
   }
-  // every split's partial is in its CTA's shared memory
-  cluster.sync();
-  if (trace && tid == 0) trace[2] = globaltimer();
-  // merge: warp `warp` of CTA `rank` takes 32-blocks rank + cs*warp + ...;
-  // block b covers elements [32b, 32b+32) of the KV head's kv_mul*HD outputs
+  cluster.sync();  // release the pushes / acquire the peers' pushes
+  if (trace && tid == 0) ts[2] = globaltimer();
   const uint32_t nblk = kv_mul * HD / 32;
   for (uint32_t b = rank + cs * warp; b < nblk; b += cs * (AD_THREADS / 32)) {
-    const uint32_t hh = (b * 32) / HD, d = (b * 32) % HD + lane;
-    float m[AD_MAXCS], l[AD_MAXCS], o[AD_MAXCS];
-#pragma unroll
-    for (int s = 0; s < AD_MAXCS; ++s) {
-      if (s >= (int)cs) break;
-      const float* peer = cluster.map_shared_rank(sm, (unsigned)s);
-      m[s] = peer[Lo::STAT + hh];
-      l[s] = peer[Lo::STAT + AT_MAXKV + hh];
-      o[s] = peer[Lo::OS + hh * HD + d];
-    }
+    const float* src = recv + (b / cs) * AD_MAXCS * 34;
     float M = -INFINITY;
-#pragma unroll
-    for (int s = 0; s < AD_MAXCS; ++s)
-      if (s < (int)cs) M = fmaxf(M, m[s]);
-    float L = 0.0f, acc = 0.0f;
-#pragma unroll
-    for (int s = 0; s < AD_MAXCS; ++s) {
-      if (s >= (int)cs) break;
-      const float w = m[s] == -INFINITY ? 0.0f : expf(m[s] - M);
-      L = fmaf(l[s], w, L);
-      acc = fmaf(o[s], w, acc);
+    for (uint32_t r = 0; r < cs; ++r) M = fmaxf(M, src[r * 34 + 32]);
+    float L = 0.0f, accv = 0.0f;
+    for (uint32_t r = 0; r < cs; ++r) {
+      const float mr = src[r * 34 + 32];
+      const float w = mr == -INFINITY ? 0.0f : __expf(mr - M);
+      L = fmaf(src[r * 34 + 33], w, L);
+      accv = fmaf(src[r * 34 + lane], w, accv);
     }
-    const float v = L > 0.0f ? __fdiv_rn(acc, L) : 0.0f;
+    const float v = L > 0.0f ? __fdiv_rn(accv, L) : 0.0f;
     const uint64_t k = (uint64_t)kvh * kv_mul * HD + b * 32 + lane;
     if (a.out) a.out[k] = v;
     if (a.q8) {
@@ -507,10 +508,20 @@ __global__ void __maxnreg__(96) attn_decode_kernel(AttnDecodeArgs a) {
       if (lane == 0) a.s8[k / 32] = sc;
     }
   }
-  if (trace && tid == 0) trace[7] = globaltimer();
-  // peers may still be reading this CTA's shared memory
-  cluster.sync();
-  if (trace && tid == 0) trace[3] = globaltimer();
+  // The new rows go to the cache last: a global store before the cluster
+  // barrier would make every CTA's release wait for its acknowledgement.
+  if (owner) {
+    float* kdst = a.kcache + (uint64_t)pos * a.kv_dim + kvh * HD;
+    float* vdst = a.vcache + (uint64_t)pos * a.kv_dim + kvh * HD;
+    for (uint32_t d = tid; d < HD; d += AD_THREADS) {
+      kdst[d] = nk[d];
+      vdst[d] = nk[HD + d];
+    }
+  }
+  if (trace && tid == 0) {
+    ts[3] = globaltimer();
+    for (int i = 0; i < 8; ++i) trace[i] = ts[i];
+  }
 }
 
 template <int HD, int KVM>
