@@ -140,9 +140,11 @@ __device__ __forceinline__ int8_t rust_as_i8(float v) {
 // the caller takes quot_code_exact for the warp.
 __device__ __forceinline__ int quot_code_fast(float x, float inv, bool& exact) {
   const float v = __fmul_rn(x, inv);
-  const float a = fabsf(v);
-  exact |= !(a <= 128.0f && fabsf((a - floorf(a)) - 0.5f) > 3.1e-5f);
-  const int q = __float_as_int(__fadd_rn(v, 12582912.0f)) - 0x4B400000;
+  const float t = __fadd_rn(v, 12582912.0f);  // v rounded to an integer in the low mantissa bits
+  const float d = __fsub_rn(v, __fsub_rn(t, 12582912.0f));  // v minus that integer, exact
+  // |d| just below 1/2 means v is next to a half-integer; NaN/inf fail the test
+  exact |= !(fabsf(v) <= 128.0f && fabsf(d) < 0.5f - 3.1e-5f);
+  const int q = __float_as_int(t) - 0x4B400000;
   return min(q, 127);
 }
 __device__ __forceinline__ int quot_code_exact(float x, float d) { return rust_as_i8(roundf(__fdiv_rn(x, d))); }
