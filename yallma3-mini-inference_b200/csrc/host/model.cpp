@@ -649,15 +649,24 @@ int session_create(const Model* m, Session** out) {
     off += round_up((uint64_t)s->tp_cap * sh.dim * 4, 256);
     s->tp_lm_off = off;
     off += 256;
+    s->tp_inbox_off[0] = off;
+    off += round_up(world * sh.dim * 4, 256);
+    s->tp_inbox_off[1] = off;
+    off += round_up(world * sh.dim * 4, 256);
+    s->tp_cnt_off = off;
+    off += round_up(2ull * sh.n_layers * 4, 256);
     s->tp_logit_off = off;
     off += round_up((uint64_t)m->l_vocab * 4, 256);
     s->tp_bytes = off;
     YL_CUDA_TRY(cudaMalloc(&p, s->tp_bytes));  // plain cudaMalloc: exportable through CUDA IPC
     s->tp_region = (uint8_t*)p;
     YL_CUDA_TRY(cudaMemset(s->tp_region, 0, s->tp_bytes));
-    if ((rc = salloc(s.get(), 4, &p))) return rc;
+    if ((rc = salloc(s.get(), 8, &p))) return rc;
     s->tp_epoch = (uint32_t*)p;
-    YL_CUDA_TRY(cudaMemset(s->tp_epoch, 0, 4));
+    s->tp_pepoch = s->tp_epoch + 1;
+    YL_CUDA_TRY(cudaMemset(s->tp_epoch, 0, 8));
+    if ((rc = salloc(s.get(), (uint64_t)sh.dim * 4, &p))) return rc;
+    s->x2 = (float*)p;
   }
   *out = s.release();
   return YL_OK;
@@ -773,6 +782,17 @@ int run_matvec_ex(const DevWeight& w, bool f32act, const int8_t* xq, const float
     a.work = ex.work;
     a.am_shard = ex.am_shard;
     a.am_base = ex.am_base;
+    a.tp_mode = ex.tp_mode;
+    if (ex.tp_mode) {
+      for (int r = 0; r < 8; ++r) a.tp_base[r] = ex.tp->base[r];
+      a.tp_rank = ex.tp->rank;
+      a.tp_world = ex.tp->world;
+      a.tp_epoch = ex.tp_epoch;
+      a.tp_inbox_off = ex.tp_inbox_off;
+      a.tp_cnt_off = ex.tp_cnt_off;
+      a.tp_arrivals = ex.tp_arrivals;
+      a.tp_xout = ex.tp_xout;
+    }
     cudaError_t e = k::matvec(a, fmt, w.sf16, epi, lc);
     if (e != cudaSuccess) return fail(YL_ERR_CUDA, std::string("matvec launch: ") + cudaGetErrorString(e));
     if (launches) ++*launches;
@@ -847,6 +867,35 @@ int enqueue_forward(Session* s, uint32_t n, uint32_t start_pos, bool from_state,
   norm.pro = k::PRO_NORM;
   norm.xres = s->x;
   norm.eps = sh.rms_norm_eps;
+  // Tensor-parallel single-token steps: wo and down push their partial rows
+  // into every rank's inbox in their epilogue, and the next RMSNorm prologue
+  // all-reduces them into the residual, which alternates between two rows
+  // (xcur is read, the other written by CTA 0). Multi-token passes all-reduce
+  // with a separate exchange kernel instead.
+  const bool tp_push = tp && decode;
+  float* xcur = s->x;
+  float* xalt = s->x2;
+  const uint32_t tp_arrivals =
+      tp ? (uint32_t)m->tp_size * k::matvec_grid_of(d, k::EPI_STORE, (uint32_t)m->num_sms * tunables().grid_mult) : 0;
+  auto tp_pull = [&](MvExtra& ex, uint32_t site) {  // all-reduce prologue of the site's pushes
+    ex.tp_mode = 2;
+    ex.tp = &tpa;
+    ex.tp_epoch = s->tp_pepoch;
+    ex.tp_inbox_off = s->tp_inbox_off[site & 1];
+    ex.tp_cnt_off = s->tp_cnt_off + 4ull * site;
+    ex.tp_arrivals = tp_arrivals;
+    ex.tp_xout = xalt;
+  };
+  auto tp_push_ex = [&](MvExtra& ex, uint32_t site) {  // push epilogue into the site's inboxes
+    ex = MvExtra();
+    ex.tp_mode = 1;
+    ex.tp = &tpa;
+    ex.tp_inbox_off = s->tp_inbox_off[site & 1];
+    ex.tp_cnt_off = s->tp_cnt_off + 4ull * site;
+  };
+  auto own_inbox = [&](uint32_t site) {
+    return (float*)(s->tp_region + s->tp_inbox_off[site & 1]) + (uint64_t)m->tp_rank * d;
+  };
   for (uint32_t l = 0; l < sh.n_layers; ++l) {
     const Layer& L = m->layers[l];
     float* kc = s->kcache + (uint64_t)l * sh.ctx_len * kvd;
@@ -859,10 +908,14 @@ int enqueue_forward(Session* s, uint32_t n, uint32_t start_pos, bool from_state,
     norm.hcount = nullptr;
     norm.trace = YL_TRACE();
     norm.work = nullptr;
+    norm.xres = xcur;
+    norm.tp_mode = 0;
+    if (tp_push && l > 0) tp_pull(norm, 2 * (l - 1) + 1);
     if ((rc = run_matvec_ex(L.wqkv, f32act, nullptr, nullptr, nullptr, d, d / 32, n, s->qkv, att + 2 * kvd,
                             k::EPI_STORE, 0, s->err, s->stream, pdl, m->num_sms, norm, &nl)))
       return rc;
     YL_MARK();
+    if (norm.tp_mode == 2) std::swap(xcur, xalt);
     if (decode) {
       // RoPE, KV write, split attention, merge and quantize in one kernel
       k::AttnDecodeArgs ad{};
@@ -909,7 +962,15 @@ int enqueue_forward(Session* s, uint32_t n, uint32_t start_pos, bool from_state,
     }
     // wo projection + residual add (tensor-parallel: this rank's partial
     // sums, all-reduced over peer memory into the replicated residual)
-    if (tp) {
+    if (tp_push) {
+      MvExtra px;
+      tp_push_ex(px, 2 * l);
+      px.trace = YL_TRACE();
+      if ((rc = run_matvec_ex(L.wo, f32act, s->xq, s->xs, s->xf, att, att / 32, n, own_inbox(2 * l), d, k::EPI_STORE,
+                              0, s->err, s->stream, pdl, m->num_sms, px, &nl)))
+        return rc;
+      YL_MARK();
+    } else if (tp) {
       YL_MV(L.wo, f32act, s->xq, s->xs, s->xf, att, att / 32, n, (float*)(s->tp_region + s->tp_part_off[0]), d,
             k::EPI_STORE, 0, s->err, s->stream, pdl, m->num_sms);
       tpa.site = 2 * l;
@@ -929,13 +990,25 @@ int enqueue_forward(Session* s, uint32_t n, uint32_t start_pos, bool from_state,
     norm.hcount = f32act ? nullptr : s->hcount;
     norm.trace = YL_TRACE();
     norm.work = decode ? s->work + 2ull * l : nullptr;  // one launch per step at this site
+    norm.xres = xcur;
+    norm.tp_mode = 0;
+    if (tp_push) tp_pull(norm, 2 * l);
     if ((rc = run_matvec_ex(L.w13, f32act, nullptr, nullptr, nullptr, d, d / 32, n, s->h, f,
                             f32act ? k::EPI_SWIGLU : k::EPI_SWIGLU_Q8, 0, s->err, s->stream, pdl, m->num_sms, norm,
                             &nl)))
       return rc;
     YL_MARK();
+    if (norm.tp_mode == 2) std::swap(xcur, xalt);
     // down projection + residual add
-    if (tp) {
+    if (tp_push) {
+      MvExtra px;
+      tp_push_ex(px, 2 * l + 1);
+      px.trace = YL_TRACE();
+      if ((rc = run_matvec_ex(L.w2, f32act, s->hq, s->hs, s->h, f, f / 32, n, own_inbox(2 * l + 1), d, k::EPI_STORE, 0,
+                              s->err, s->stream, pdl, m->num_sms, px, &nl)))
+        return rc;
+      YL_MARK();
+    } else if (tp) {
       YL_MV(L.w2, f32act, s->hq, s->hs, s->h, f, f / 32, n, (float*)(s->tp_region + s->tp_part_off[1]), d,
             k::EPI_STORE, 0, s->err, s->stream, pdl, m->num_sms);
       tpa.site = 2 * l + 1;
@@ -950,7 +1023,8 @@ int enqueue_forward(Session* s, uint32_t n, uint32_t start_pos, bool from_state,
   {
     MvExtra fin;
     fin.pro = k::PRO_NORM;
-    fin.xres = s->x + (uint64_t)(n - 1) * d;
+    fin.xres = xcur + (uint64_t)(n - 1) * d;
+    if (tp_push) tp_pull(fin, 2 * sh.n_layers - 1);
     fin.norm_w = m->rms_final;
     fin.eps = sh.rms_norm_eps;
     fin.am_val = s->am_val;
@@ -972,7 +1046,8 @@ int enqueue_forward(Session* s, uint32_t n, uint32_t start_pos, bool from_state,
     if (tp) {
       tpa.site = 2 * sh.n_layers;
       YL_LAUNCH(k::tp_argmax(tpa, s->tp_lm_off, s->tp_logit_off, m->l_vocab, want_logits ? s->logits : nullptr,
-                             s->hist, from_state ? s->state : nullptr, s->tp_epoch, lc));
+                             s->hist, from_state ? s->state : nullptr, s->tp_epoch, tp_push ? s->tp_pepoch : nullptr,
+                             lc));
     }
   }
 #undef YL_LAUNCH

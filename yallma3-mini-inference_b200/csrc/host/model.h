@@ -103,6 +103,9 @@ struct Session {
   std::vector<void*> tp_opened;
   bool tp_ready = false;
   uint32_t* tp_epoch = nullptr;  // completed steps (device)
+  uint32_t* tp_pepoch = nullptr; // completed single-token steps (device): the push exchanges' epoch
+  uint64_t tp_inbox_off[2] = {0, 0}, tp_cnt_off = 0;  // push inboxes [2][world][dim], counters [2 L]
+  float* x2 = nullptr;           // second residual row (single-token tensor-parallel steps alternate)
   std::vector<void*> allocs;
   ~Session();
 };
@@ -162,6 +165,13 @@ struct MvExtra {
   unsigned int* work = nullptr;  // dynamic row-set counters of this launch site (nullable)
   float* am_shard = nullptr;     // EPI_ARGMAX over a vocabulary shard: published winner
   uint32_t am_base = 0;          // first vocabulary row of the shard
+  // tensor parallel, single token: 1 push epilogue, 2 all-reduce prologue
+  int tp_mode = 0;
+  const k::TpArgs* tp = nullptr;     // ranks' exchange regions (base, rank, world)
+  const uint32_t* tp_epoch = nullptr;
+  uint64_t tp_inbox_off = 0, tp_cnt_off = 0;
+  uint32_t tp_arrivals = 0;
+  float* tp_xout = nullptr;
 };
 int run_matvec_ex(const DevWeight& w, bool f32act, const int8_t* xq, const float* xs, const float* xf,
                   uint64_t x_stride, uint64_t xs_stride, uint32_t ntok, float* out, uint64_t out_stride, int epi,

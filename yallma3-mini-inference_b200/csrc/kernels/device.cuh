@@ -20,6 +20,11 @@ enum : int { ERR_NONE = 0, ERR_WAIT_TIMEOUT = 1, ERR_BAD_ARG = 2 };
 __device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 // Allow the next kernel in the stream to be scheduled (it still waits in
 // grid_dep_wait() for this grid to finish before reading our outputs).
+__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const unsigned int* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
 // Global nanosecond timer (timeline tracing of the decode step).
 __device__ __forceinline__ uint64_t globaltimer() {
   uint64_t t;

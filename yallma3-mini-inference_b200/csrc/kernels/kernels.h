@@ -91,6 +91,19 @@ struct MvArgs {
   // instead of updating am_out / state
   float* am_shard;
   uint32_t am_base;
+  // Tensor parallel, single-token passes (tp_mode): 1 = push epilogue: each
+  // output row is stored into every rank's inbox [world][rows] (slot of this
+  // rank) at byte offset tp_inbox_off of its exchange region, then each CTA
+  // adds one arrival to every rank's counter at tp_cnt_off; 2 = all-reduce
+  // prologue (with PRO_NORM): wait until the local counter reaches
+  // (*tp_epoch + 1) * tp_arrivals, take the rows as xres + the sum of the
+  // ranks' inbox rows (in rank order), CTA 0 stores them to tp_xout.
+  int tp_mode;
+  uint32_t tp_rank, tp_world, tp_arrivals;
+  uint8_t* tp_base[8];
+  uint64_t tp_inbox_off, tp_cnt_off;
+  const uint32_t* tp_epoch;
+  float* tp_xout;
   // Dynamic scheduling (nullable): [next row set, CTAs done] counters, zero
   // between launches; CTAs claim 8-row sets from it instead of a static range.
   // Used by the launcher only for single-token passes with >= 4 sets per CTA.
@@ -103,6 +116,8 @@ struct MvArgs {
 };
 // fmt: FMT_*; scale_f16: weight scale type. Chooses NT from a.ntok.
 cudaError_t matvec(const MvArgs& a, int fmt, bool scale_f16, int epi, const LaunchCfg& lc);
+// CTAs a matvec launch uses (the tensor-parallel arrival counts depend on it).
+uint32_t matvec_grid_of(uint32_t rows, int epi, uint32_t lc_grid);
 // Largest tokens-per-pass (1, 2, 4 or 8) whose shared-memory layout fits with
 // at least two ring stages.
 uint32_t matvec_max_ntok(int fmt, uint32_t K, uint32_t kc, int epi);
@@ -210,8 +225,10 @@ cudaError_t tp_allreduce_add(const TpArgs& t, uint64_t part_off, uint32_t n, flo
 // hist[state ? state->steps : 0], advances state like EPI_ARGMAX, increments
 // *epoch (the step's last collective), and with logits != null gathers every
 // rank's slice [vl] (at logit_off) into logits[V].
+// pepoch (nullable): the single-token step counter of the push exchanges,
+// incremented here after a decode step.
 cudaError_t tp_argmax(const TpArgs& t, uint64_t lm_off, uint64_t logit_off, uint32_t vl, float* logits,
-                      uint32_t* hist, StepState* state, uint32_t* epoch, const LaunchCfg& lc);
+                      uint32_t* hist, StepState* state, uint32_t* epoch, uint32_t* pepoch, const LaunchCfg& lc);
 
 // Greedy argmax over n logits (sampler.rs:67-79: the lowest index among equal
 // maxima). Writes out[0]; with state != null also state->next/token/pos/steps

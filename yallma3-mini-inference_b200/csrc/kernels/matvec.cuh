@@ -162,6 +162,23 @@ __device__ __forceinline__ void mv_norm_regs(const MvArgs& a, const MvLayout& L,
     }
   }
   mv_wait_inputs(a);
+  const bool tp_in = NT == 1 && a.tp_mode == 2;
+  if (tp_in) {
+    // tensor parallel: wait for every rank's pushed partial rows (bounded)
+    if (ctid == 0) {
+      const uint32_t target = (*a.tp_epoch + 1u) * a.tp_arrivals;
+      const unsigned int* cnt = reinterpret_cast<const unsigned int*>(a.tp_base[a.tp_rank] + a.tp_cnt_off);
+      const uint64_t t0 = clock64();
+      uint32_t it = 0;
+      while ((int32_t)(ld_acquire_sys_u32(cnt) - target) < 0) {
+        if ((++it & 255u) == 0 && (uint64_t)(clock64() - t0) > 4000000000ull) {
+          if (a.err) atomicExch(a.err, ERR_WAIT_TIMEOUT);
+          break;
+        }
+      }
+    }
+    named_bar_sync(1, MV_NCW * 32);
+  }
   for (int t = 0; t < NT; ++t) {
     const bool valid = t < (int)a.ntok;
     const float* xr = a.xres + (uint64_t)t * a.x_tok_stride;
@@ -171,6 +188,22 @@ __device__ __forceinline__ void mv_norm_regs(const MvArgs& a, const MvLayout& L,
       const uint32_t i = ctid * 4 + u * MV_NCW * 32 * 4;
       const bool in = valid && i < K;
       xv[u] = in ? *reinterpret_cast<const float4*>(xr + i) : make_float4(0, 0, 0, 0);
+      if (tp_in && in) {  // residual + the ranks' partials, summed in rank order
+        const float* ib = reinterpret_cast<const float*>(a.tp_base[a.tp_rank] + a.tp_inbox_off) + i;
+        float4 sum = __ldcv(reinterpret_cast<const float4*>(ib));
+        for (uint32_t q = 1; q < a.tp_world; ++q) {
+          const float4 p = __ldcv(reinterpret_cast<const float4*>(ib + (uint64_t)q * K));
+          sum.x = __fadd_rn(sum.x, p.x);
+          sum.y = __fadd_rn(sum.y, p.y);
+          sum.z = __fadd_rn(sum.z, p.z);
+          sum.w = __fadd_rn(sum.w, p.w);
+        }
+        xv[u].x = __fadd_rn(xv[u].x, sum.x);
+        xv[u].y = __fadd_rn(xv[u].y, sum.y);
+        xv[u].z = __fadd_rn(xv[u].z, sum.z);
+        xv[u].w = __fadd_rn(xv[u].w, sum.w);
+        if (blockIdx.x == 0) *reinterpret_cast<float4*>(a.tp_xout + i) = xv[u];
+      }
     }
     float r = 1.0f;
     if (NORM) {
@@ -955,6 +988,13 @@ __global__ void __launch_bounds__(MV_THREADS, (NT <= 2 ? 2 : 1)) mv_kernel(MvArg
             else if (EPI == EPI_ADD) *o = __fadd_rn(pre_add ? prev : *o, acc[rr][t]);
             else *o = (r < a.quirk_cols) ? __fadd_rn(*o, acc[rr][t]) : acc[rr][t];
           }
+          if (EPI == EPI_STORE && NT == 1 && a.tp_mode == 1) {
+            // tensor parallel: this rank's partial row into every other rank's
+            // inbox (a.out is this rank's own slot)
+            for (uint32_t q = 0; q < a.tp_world; ++q)
+              if (q != a.tp_rank)
+                reinterpret_cast<float*>(a.tp_base[q] + a.tp_inbox_off)[(uint64_t)a.tp_rank * a.rows + r] = acc[rr][0];
+          }
         }
       }
     }
@@ -964,6 +1004,13 @@ __global__ void __launch_bounds__(MV_THREADS, (NT <= 2 ? 2 : 1)) mv_kernel(MvArg
       for (int rr = 0; rr < RPW; ++rr) acc[rr][t] = 0.0f;
   }
 
+  if (EPI == EPI_STORE && NT == 1 && a.tp_mode == 1) {
+    // the CTA's rows are in every inbox: one arrival per rank (system scope,
+    // after a system fence, so a rank that sees the count sees the rows)
+    __threadfence_system();
+    named_bar_sync(1, MV_NCW * 32);
+    if (cw == 0 && lane < (int)a.tp_world) atomicAdd_system(reinterpret_cast<unsigned int*>(a.tp_base[lane] + a.tp_cnt_off), 1u);
+  }
   if (EPI == EPI_SWIGLU_Q8) {
     // Quantize h (quantization.rs:29-52, forward.rs:240) once, here, from the
     // h values in global memory: a block of 32 is quantized by the CTA whose
@@ -1103,6 +1150,13 @@ __global__ void __launch_bounds__(MV_THREADS, (NT <= 2 ? 2 : 1)) mv_kernel(MvArg
   if (trace && threadIdx.x == 32) trace[3] = globaltimer();
 }
 
+// CTAs of a matvec launch: lc.grid (0: 148), at most one per row (row pair).
+inline uint32_t matvec_grid(uint32_t rows, int epi, uint32_t lc_grid) {
+  uint32_t grid = lc_grid ? lc_grid : 148;
+  const uint32_t unit = mv_swiglu(epi) ? 2 : 1;
+  return grid > rows / unit ? rows / unit : grid;
+}
+
 // Host-side launcher for one (FMT, SF16) family; NT and EPI dispatched here.
 template <int FMT, bool SF16>
 cudaError_t mv_launch(const MvArgs& a0, int epi, const LaunchCfg& lc) {
@@ -1150,6 +1204,11 @@ cudaError_t mv_launch(const MvArgs& a0, int epi, const LaunchCfg& lc) {
     if (!ok) a.work = nullptr;
   }
   if (epi == EPI_SWIGLU_Q8 && (a.rows % 64 || mv_f32_act<FMT>())) return cudaErrorInvalidValue;
+  // tensor-parallel push / all-reduce: single token, store epilogue / register RMSNorm prologue
+  if (a.tp_mode == 1 && (nt != 1 || epi != EPI_STORE || a.tp_world < 2 || a.tp_world > 8)) return cudaErrorInvalidValue;
+  if (a.tp_mode == 2 && (nt != 1 || a.pro != PRO_NORM || a.K > (uint32_t)(MV_NORM_MU * MV_NCW * 32 * 4) ||
+                         a.tp_world < 2 || a.tp_world > 8))
+    return cudaErrorInvalidValue;
   if (a.pro == PRO_QUANT && (a.K > MV_QUANT_MU * MV_NCW * 32 * 4 || mv_f32_act<FMT>())) return cudaErrorInvalidValue;
   // three-limb activations are produced only by the register RMSNorm prologue
   if (FMT == FMT_Q8X && (a.pro != PRO_NORM || a.K > MV_NORM_MU * MV_NCW * 32 * 4)) return cudaErrorInvalidValue;
@@ -1177,9 +1236,7 @@ cudaError_t mv_launch(const MvArgs& a0, int epi, const LaunchCfg& lc) {
   if (!kern) return cudaErrorInvalidValue;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  uint32_t grid = lc.grid ? lc.grid : 148;
-  const uint32_t unit = mv_swiglu(epi) ? 2 : 1;
-  if (grid > a.rows / unit) grid = (uint32_t)(a.rows / unit);
+  const uint32_t grid = matvec_grid(a.rows, epi, lc.grid);
   if (grid == 0) return cudaSuccess;
   return launch_kernel(kern, dim3(grid), dim3(MV_THREADS), smem, lc, a);
 }

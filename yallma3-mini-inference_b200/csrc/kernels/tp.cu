@@ -76,7 +76,8 @@ __global__ void __launch_bounds__(256) tp_allreduce_add_kernel(TpArgs t, uint64_
 }
 
 __global__ void __launch_bounds__(256) tp_argmax_kernel(TpArgs t, uint64_t lm_off, uint64_t logit_off, uint32_t vl,
-                                                       float* logits, uint32_t* hist, StepState* state, uint32_t* epoch) {
+                                                       float* logits, uint32_t* hist, StepState* state, uint32_t* epoch,
+                                                       uint32_t* pepoch) {
   grid_dep_launch();
   grid_dep_wait();
   const uint32_t e = *t.epoch + 1;
@@ -118,7 +119,10 @@ __global__ void __launch_bounds__(256) tp_argmax_kernel(TpArgs t, uint64_t lm_of
     }
   }
   __syncthreads();
-  if (threadIdx.x == 0) *epoch = e;  // the step's collectives are done
+  if (threadIdx.x == 0) {
+    *epoch = e;  // the step's collectives are done
+    if (pepoch) *pepoch += 1;
+  }
 }
 
 cudaError_t tp_allreduce_add(const TpArgs& t, uint64_t part_off, uint32_t n, float* x, const LaunchCfg& lc) {
@@ -128,10 +132,10 @@ cudaError_t tp_allreduce_add(const TpArgs& t, uint64_t part_off, uint32_t n, flo
 }
 
 cudaError_t tp_argmax(const TpArgs& t, uint64_t lm_off, uint64_t logit_off, uint32_t vl, float* logits,
-                      uint32_t* hist, StepState* state, uint32_t* epoch, const LaunchCfg& lc) {
+                      uint32_t* hist, StepState* state, uint32_t* epoch, uint32_t* pepoch, const LaunchCfg& lc) {
   if (t.world < 2 || t.world > 8 || t.rank >= t.world) return cudaErrorInvalidValue;
   return launch_kernel(tp_argmax_kernel, dim3(1), dim3(256), 0, lc, t, lm_off, logit_off, vl, logits, hist, state,
-                       epoch);
+                       epoch, pepoch);
 }
 
 }  // namespace k
