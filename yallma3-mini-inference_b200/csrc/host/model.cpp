@@ -301,6 +301,7 @@ const Tunables& tunables() {
     if (const char* e = getenv("YL_PDL")) x.pdl = atoi(e) != 0;
     if (const char* e = getenv("YL_MV_GRID_MULT")) x.grid_mult = std::max(1, atoi(e));
     if (const char* e = getenv("YL_LM_LIMBS")) x.limbs = atoi(e) != 0;
+    if (const char* e = getenv("YL_TP_FUSED")) x.tp_fused = atoi(e) != 0;
     return x;
   }();
   return t;
@@ -650,11 +651,9 @@ int session_create(const Model* m, Session** out) {
     s->tp_lm_off = off;
     off += 256;
     s->tp_inbox_off[0] = off;
-    off += round_up(world * sh.dim * 4, 256);
+    off += round_up(world * sh.dim * 8, 256);
     s->tp_inbox_off[1] = off;
-    off += round_up(world * sh.dim * 4, 256);
-    s->tp_cnt_off = off;
-    off += round_up(2ull * sh.n_layers * 4, 256);
+    off += round_up(world * sh.dim * 8, 256);
     s->tp_logit_off = off;
     off += round_up((uint64_t)m->l_vocab * 4, 256);
     s->tp_bytes = off;
@@ -789,8 +788,8 @@ int run_matvec_ex(const DevWeight& w, bool f32act, const int8_t* xq, const float
       a.tp_world = ex.tp->world;
       a.tp_epoch = ex.tp_epoch;
       a.tp_inbox_off = ex.tp_inbox_off;
-      a.tp_cnt_off = ex.tp_cnt_off;
-      a.tp_arrivals = ex.tp_arrivals;
+      a.tp_site = ex.tp_site;
+      a.tp_nsites = ex.tp_nsites;
       a.tp_xout = ex.tp_xout;
     }
     cudaError_t e = k::matvec(a, fmt, w.sf16, epi, lc);
@@ -870,31 +869,31 @@ int enqueue_forward(Session* s, uint32_t n, uint32_t start_pos, bool from_state,
   // Tensor-parallel single-token steps: wo and down push their partial rows
   // into every rank's inbox in their epilogue, and the next RMSNorm prologue
   // all-reduces them into the residual, which alternates between two rows
-  // (xcur is read, the other written by CTA 0). Multi-token passes all-reduce
-  // with a separate exchange kernel instead.
-  const bool tp_push = tp && decode;
+  // (xcur is read, the other written by CTA 0). Multi-token passes (and
+  // YL_TP_FUSED=0) all-reduce with a separate exchange kernel instead.
+  const bool tp_push = tp && decode && tunables().tp_fused;
   float* xcur = s->x;
   float* xalt = s->x2;
-  const uint32_t tp_arrivals =
-      tp ? (uint32_t)m->tp_size * k::matvec_grid_of(d, k::EPI_STORE, (uint32_t)m->num_sms * tunables().grid_mult) : 0;
   auto tp_pull = [&](MvExtra& ex, uint32_t site) {  // all-reduce prologue of the site's pushes
     ex.tp_mode = 2;
     ex.tp = &tpa;
     ex.tp_epoch = s->tp_pepoch;
     ex.tp_inbox_off = s->tp_inbox_off[site & 1];
-    ex.tp_cnt_off = s->tp_cnt_off + 4ull * site;
-    ex.tp_arrivals = tp_arrivals;
+    ex.tp_site = site;
+    ex.tp_nsites = 2 * sh.n_layers;
     ex.tp_xout = xalt;
   };
   auto tp_push_ex = [&](MvExtra& ex, uint32_t site) {  // push epilogue into the site's inboxes
     ex = MvExtra();
     ex.tp_mode = 1;
     ex.tp = &tpa;
+    ex.tp_epoch = s->tp_pepoch;
     ex.tp_inbox_off = s->tp_inbox_off[site & 1];
-    ex.tp_cnt_off = s->tp_cnt_off + 4ull * site;
+    ex.tp_site = site;
+    ex.tp_nsites = 2 * sh.n_layers;
   };
   auto own_inbox = [&](uint32_t site) {
-    return (float*)(s->tp_region + s->tp_inbox_off[site & 1]) + (uint64_t)m->tp_rank * d;
+    return (float*)(s->tp_region + s->tp_inbox_off[site & 1]);  // not written: the entries are pushed
   };
   for (uint32_t l = 0; l < sh.n_layers; ++l) {
     const Layer& L = m->layers[l];

@@ -104,7 +104,7 @@ struct Session {
   bool tp_ready = false;
   uint32_t* tp_epoch = nullptr;  // completed steps (device)
   uint32_t* tp_pepoch = nullptr; // completed single-token steps (device): the push exchanges' epoch
-  uint64_t tp_inbox_off[2] = {0, 0}, tp_cnt_off = 0;  // push inboxes [2][world][dim], counters [2 L]
+  uint64_t tp_inbox_off[2] = {0, 0};  // push inboxes [2][world][dim] of {f32, flag} entries
   float* x2 = nullptr;           // second residual row (single-token tensor-parallel steps alternate)
   std::vector<void*> allocs;
   ~Session();
@@ -141,6 +141,7 @@ struct Tunables {
   bool pdl = true;
   uint32_t grid_mult = 2;    // matvec CTAs per SM
   bool limbs = true;         // Q8_0 lm_head on three-limb int8 activations
+  bool tp_fused = true;      // tensor-parallel decode: exchange fused into the projections (else exchange kernels)
 };
 const Tunables& tunables();
 // Launches the matvec for `ntok` tokens (groups of 8) with activations x*.
@@ -169,8 +170,8 @@ struct MvExtra {
   int tp_mode = 0;
   const k::TpArgs* tp = nullptr;     // ranks' exchange regions (base, rank, world)
   const uint32_t* tp_epoch = nullptr;
-  uint64_t tp_inbox_off = 0, tp_cnt_off = 0;
-  uint32_t tp_arrivals = 0;
+  uint64_t tp_inbox_off = 0;
+  uint32_t tp_site = 0, tp_nsites = 0;
   float* tp_xout = nullptr;
 };
 int run_matvec_ex(const DevWeight& w, bool f32act, const int8_t* xq, const float* xs, const float* xf,

@@ -20,10 +20,13 @@ enum : int { ERR_NONE = 0, ERR_WAIT_TIMEOUT = 1, ERR_BAD_ARG = 2 };
 __device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 // Allow the next kernel in the stream to be scheduled (it still waits in
 // grid_dep_wait() for this grid to finish before reading our outputs).
-__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const unsigned int* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
+// 8-byte {value, flag} exchange entries: one aligned 64-bit access each is
+// single-copy atomic, so a reader that sees the flag sees the value with it.
+__device__ __forceinline__ void st_volatile_u64(void* p, uint64_t v) {
+  asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ void ld_volatile_2u64(const void* p, uint64_t& a, uint64_t& b) {
+  asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
 }
 // Global nanosecond timer (timeline tracing of the decode step).
 __device__ __forceinline__ uint64_t globaltimer() {

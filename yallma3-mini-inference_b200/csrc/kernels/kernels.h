@@ -91,17 +91,19 @@ struct MvArgs {
   // instead of updating am_out / state
   float* am_shard;
   uint32_t am_base;
-  // Tensor parallel, single-token passes (tp_mode): 1 = push epilogue: each
-  // output row is stored into every rank's inbox [world][rows] (slot of this
-  // rank) at byte offset tp_inbox_off of its exchange region, then each CTA
-  // adds one arrival to every rank's counter at tp_cnt_off; 2 = all-reduce
-  // prologue (with PRO_NORM): wait until the local counter reaches
-  // (*tp_epoch + 1) * tp_arrivals, take the rows as xres + the sum of the
-  // ranks' inbox rows (in rank order), CTA 0 stores them to tp_xout.
+  // Tensor parallel, single-token passes (tp_mode). Inboxes are [world][rows]
+  // 8-byte entries {f32 value, u32 flag} at byte offset tp_inbox_off of every
+  // rank's exchange region; the flag of this pass is
+  // *tp_epoch * tp_nsites + tp_site + 1. 1 = push epilogue: each output row
+  // goes into every rank's inbox (slot of this rank) as one 8-byte store;
+  // 2 = all-reduce prologue (with PRO_NORM): each thread waits (bounded)
+  // until its entries of every rank carry the flag, takes the rows as
+  // xres + the sum of the ranks' values (in rank order), CTA 0 stores them to
+  // tp_xout.
   int tp_mode;
-  uint32_t tp_rank, tp_world, tp_arrivals;
+  uint32_t tp_rank, tp_world, tp_site, tp_nsites;
   uint8_t* tp_base[8];
-  uint64_t tp_inbox_off, tp_cnt_off;
+  uint64_t tp_inbox_off;
   const uint32_t* tp_epoch;
   float* tp_xout;
   // Dynamic scheduling (nullable): [next row set, CTAs done] counters, zero
@@ -116,8 +118,6 @@ struct MvArgs {
 };
 // fmt: FMT_*; scale_f16: weight scale type. Chooses NT from a.ntok.
 cudaError_t matvec(const MvArgs& a, int fmt, bool scale_f16, int epi, const LaunchCfg& lc);
-// CTAs a matvec launch uses (the tensor-parallel arrival counts depend on it).
-uint32_t matvec_grid_of(uint32_t rows, int epi, uint32_t lc_grid);
 // Largest tokens-per-pass (1, 2, 4 or 8) whose shared-memory layout fits with
 // at least two ring stages.
 uint32_t matvec_max_ntok(int fmt, uint32_t K, uint32_t kc, int epi);

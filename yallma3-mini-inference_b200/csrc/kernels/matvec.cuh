@@ -163,22 +163,8 @@ __device__ __forceinline__ void mv_norm_regs(const MvArgs& a, const MvLayout& L,
   }
   mv_wait_inputs(a);
   const bool tp_in = NT == 1 && a.tp_mode == 2;
-  if (tp_in) {
-    // tensor parallel: wait for every rank's pushed partial rows (bounded)
-    if (ctid == 0) {
-      const uint32_t target = (*a.tp_epoch + 1u) * a.tp_arrivals;
-      const unsigned int* cnt = reinterpret_cast<const unsigned int*>(a.tp_base[a.tp_rank] + a.tp_cnt_off);
-      const uint64_t t0 = clock64();
-      uint32_t it = 0;
-      while ((int32_t)(ld_acquire_sys_u32(cnt) - target) < 0) {
-        if ((++it & 255u) == 0 && (uint64_t)(clock64() - t0) > 4000000000ull) {
-          if (a.err) atomicExch(a.err, ERR_WAIT_TIMEOUT);
-          break;
-        }
-      }
-    }
-    named_bar_sync(1, MV_NCW * 32);
-  }
+  const uint32_t tp_flag = tp_in ? *a.tp_epoch * a.tp_nsites + a.tp_site + 1u : 0u;
+  const uint64_t tp_t0 = tp_in ? clock64() : 0;
   for (int t = 0; t < NT; ++t) {
     const bool valid = t < (int)a.ntok;
     const float* xr = a.xres + (uint64_t)t * a.x_tok_stride;
@@ -189,14 +175,32 @@ __device__ __forceinline__ void mv_norm_regs(const MvArgs& a, const MvLayout& L,
       const bool in = valid && i < K;
       xv[u] = in ? *reinterpret_cast<const float4*>(xr + i) : make_float4(0, 0, 0, 0);
       if (tp_in && in) {  // residual + the ranks' partials, summed in rank order
-        const float* ib = reinterpret_cast<const float*>(a.tp_base[a.tp_rank] + a.tp_inbox_off) + i;
-        float4 sum = __ldcv(reinterpret_cast<const float4*>(ib));
-        for (uint32_t q = 1; q < a.tp_world; ++q) {
-          const float4 p = __ldcv(reinterpret_cast<const float4*>(ib + (uint64_t)q * K));
-          sum.x = __fadd_rn(sum.x, p.x);
-          sum.y = __fadd_rn(sum.y, p.y);
-          sum.z = __fadd_rn(sum.z, p.z);
-          sum.w = __fadd_rn(sum.w, p.w);
+        const uint64_t* ib = reinterpret_cast<const uint64_t*>(a.tp_base[a.tp_rank] + a.tp_inbox_off) + i;
+        float4 sum = make_float4(0, 0, 0, 0);
+        for (uint32_t q = 0; q < a.tp_world; ++q) {
+          uint64_t e0, e1, e2, e3;
+          // wait (bounded, ~2 s) until the four entries carry this pass's flag
+          for (uint32_t it = 0;; ++it) {
+            ld_volatile_2u64(ib + (uint64_t)q * K, e0, e1);
+            ld_volatile_2u64(ib + (uint64_t)q * K + 2, e2, e3);
+            if ((uint32_t)(e0 >> 32) == tp_flag && (uint32_t)(e1 >> 32) == tp_flag &&
+                (uint32_t)(e2 >> 32) == tp_flag && (uint32_t)(e3 >> 32) == tp_flag)
+              break;
+            if ((it & 63u) == 63u && (uint64_t)(clock64() - tp_t0) > 4000000000ull) {
+              if (a.err) atomicExch(a.err, ERR_WAIT_TIMEOUT);
+              break;
+            }
+          }
+          const float p0 = __uint_as_float((uint32_t)e0), p1 = __uint_as_float((uint32_t)e1);
+          const float p2 = __uint_as_float((uint32_t)e2), p3 = __uint_as_float((uint32_t)e3);
+          if (q == 0) {
+            sum = make_float4(p0, p1, p2, p3);
+          } else {
+            sum.x = __fadd_rn(sum.x, p0);
+            sum.y = __fadd_rn(sum.y, p1);
+            sum.z = __fadd_rn(sum.z, p2);
+            sum.w = __fadd_rn(sum.w, p3);
+          }
         }
         xv[u].x = __fadd_rn(xv[u].x, sum.x);
         xv[u].y = __fadd_rn(xv[u].y, sum.y);
@@ -984,16 +988,17 @@ __global__ void __launch_bounds__(MV_THREADS, (NT <= 2 ? 2 : 1)) mv_kernel(MvArg
           for (int t = 0; t < NT; ++t) {
             if (t >= (int)a.ntok) continue;
             float* o = a.out + (uint64_t)t * a.out_tok_stride + r;
-            if (EPI == EPI_STORE || EPI == EPI_ARGMAX) *o = acc[rr][t];
+            if (EPI == EPI_STORE && NT == 1 && a.tp_mode == 1) {
+              // tensor parallel: this rank's partial row, flagged, into every
+              // rank's inbox (own one included)
+              const uint32_t flag = *a.tp_epoch * a.tp_nsites + a.tp_site + 1u;
+              const uint64_t e = ((uint64_t)flag << 32) | __float_as_uint(acc[rr][0]);
+              for (uint32_t q = 0; q < a.tp_world; ++q)
+                st_volatile_u64(reinterpret_cast<uint64_t*>(a.tp_base[q] + a.tp_inbox_off) +
+                                    (uint64_t)a.tp_rank * a.rows + r, e);
+            } else if (EPI == EPI_STORE || EPI == EPI_ARGMAX) *o = acc[rr][t];
             else if (EPI == EPI_ADD) *o = __fadd_rn(pre_add ? prev : *o, acc[rr][t]);
             else *o = (r < a.quirk_cols) ? __fadd_rn(*o, acc[rr][t]) : acc[rr][t];
-          }
-          if (EPI == EPI_STORE && NT == 1 && a.tp_mode == 1) {
-            // tensor parallel: this rank's partial row into every other rank's
-            // inbox (a.out is this rank's own slot)
-            for (uint32_t q = 0; q < a.tp_world; ++q)
-              if (q != a.tp_rank)
-                reinterpret_cast<float*>(a.tp_base[q] + a.tp_inbox_off)[(uint64_t)a.tp_rank * a.rows + r] = acc[rr][0];
           }
         }
       }
@@ -1004,13 +1009,6 @@ __global__ void __launch_bounds__(MV_THREADS, (NT <= 2 ? 2 : 1)) mv_kernel(MvArg
       for (int rr = 0; rr < RPW; ++rr) acc[rr][t] = 0.0f;
   }
 
-  if (EPI == EPI_STORE && NT == 1 && a.tp_mode == 1) {
-    // the CTA's rows are in every inbox: one arrival per rank (system scope,
-    // after a system fence, so a rank that sees the count sees the rows)
-    __threadfence_system();
-    named_bar_sync(1, MV_NCW * 32);
-    if (cw == 0 && lane < (int)a.tp_world) atomicAdd_system(reinterpret_cast<unsigned int*>(a.tp_base[lane] + a.tp_cnt_off), 1u);
-  }
   if (EPI == EPI_SWIGLU_Q8) {
     // Quantize h (quantization.rs:29-52, forward.rs:240) once, here, from the
     // h values in global memory: a block of 32 is quantized by the CTA whose
@@ -1205,9 +1203,12 @@ cudaError_t mv_launch(const MvArgs& a0, int epi, const LaunchCfg& lc) {
   }
   if (epi == EPI_SWIGLU_Q8 && (a.rows % 64 || mv_f32_act<FMT>())) return cudaErrorInvalidValue;
   // tensor-parallel push / all-reduce: single token, store epilogue / register RMSNorm prologue
-  if (a.tp_mode == 1 && (nt != 1 || epi != EPI_STORE || a.tp_world < 2 || a.tp_world > 8)) return cudaErrorInvalidValue;
+  if (a.tp_mode && (!a.tp_epoch || a.tp_site >= a.tp_nsites || a.tp_world < 2 || a.tp_world > 8 ||
+                    a.tp_rank >= a.tp_world || a.tp_inbox_off % 32))
+    return cudaErrorInvalidValue;
+  if (a.tp_mode == 1 && (nt != 1 || epi != EPI_STORE)) return cudaErrorInvalidValue;
   if (a.tp_mode == 2 && (nt != 1 || a.pro != PRO_NORM || a.K > (uint32_t)(MV_NORM_MU * MV_NCW * 32 * 4) ||
-                         a.tp_world < 2 || a.tp_world > 8))
+                         a.K % 32 || !a.tp_xout))
     return cudaErrorInvalidValue;
   if (a.pro == PRO_QUANT && (a.K > MV_QUANT_MU * MV_NCW * 32 * 4 || mv_f32_act<FMT>())) return cudaErrorInvalidValue;
   // three-limb activations are produced only by the register RMSNorm prologue

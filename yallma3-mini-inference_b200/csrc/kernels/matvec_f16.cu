@@ -18,7 +18,6 @@ static uint32_t max_ntok_fmt(uint32_t K, uint32_t kc, int rpw) {
   return 0;
 }
 
-uint32_t matvec_grid_of(uint32_t rows, int epi, uint32_t lc_grid) { return matvec_grid(rows, epi, lc_grid); }
 
 uint32_t matvec_max_ntok(int fmt, uint32_t K, uint32_t kc, int epi) {
   const int rpw = (epi == EPI_SWIGLU || epi == EPI_SWIGLU_Q8) ? 2 : 1;
