@@ -68,8 +68,12 @@ def bytes_per_token(cfg: dict, seq: float) -> float:
 
 
 class ClockSampler:
-    """nvidia-smi clocks/throttle sampling during the timed region."""
+    """SM clock and clock-event (throttle) reasons sampled every 20 ms during
+    the timed region, read-only through NVML (nvidia-smi polling at 200 ms as
+    the fallback); one sample is also taken at entry and one at exit."""
 
+    REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
+               ("sw_power_cap", 0x4))
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -77,9 +81,51 @@ class ClockSampler:
     def __init__(self, gpu_index: int):
         self.idx = gpu_index
         self.proc = None
+        self.nv = None
+        self.h = None
+        self.stop = threading.Event()
+        self.samples: list[tuple[float, float, set]] = []  # (sm MHz, max sm MHz, active reasons)
         self.lines: list[str] = []
 
+    def _nvml_open(self) -> bool:
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            h = None
+            try:
+                import torch
+                pr = torch.cuda.get_device_properties(self.idx)
+                bus = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+                h = nv.nvmlDeviceGetHandleByPciBusId(bus)
+            except Exception:
+                h = nv.nvmlDeviceGetHandleByIndex(self.idx)
+            self.nv, self.h = nv, h
+            self._nvml_sample()
+            return True
+        except Exception:
+            self.nv = None
+            return False
+
+    def _nvml_sample(self) -> None:
+        nv, h = self.nv, self.h
+        sm = float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+        mx = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+        get = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        bits = int(get(h))
+        self.samples.append((sm, mx, {nm for nm, b in self.REASONS if bits & b}))
+
+    def _nvml_loop(self) -> None:
+        while not self.stop.wait(0.02):
+            try:
+                self._nvml_sample()
+            except Exception:
+                return
+
     def __enter__(self):
+        if self._nvml_open():
+            self.t = threading.Thread(target=self._nvml_loop, daemon=True)
+            self.t.start()
+            return self
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
@@ -95,6 +141,13 @@ class ClockSampler:
             self.lines.append(line.strip())
 
     def __exit__(self, *a):
+        if self.nv is not None:
+            self.stop.set()
+            self.t.join(timeout=5)
+            try:
+                self._nvml_sample()
+            except Exception:
+                pass
         if self.proc:
             self.proc.terminate()
             try:
@@ -104,7 +157,11 @@ class ClockSampler:
 
     def summary(self) -> dict:
         sm, mx, reasons = [], 0.0, set()
-        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for f, m, r in self.samples:
+            sm.append(f)
+            mx = max(mx, m)
+            reasons |= r
+        names = [nm for nm, _ in self.REASONS]
         for ln in self.lines:
             p = [x.strip() for x in ln.split(",")]
             if len(p) < 9:
@@ -118,7 +175,8 @@ class ClockSampler:
                 if v.lower() == "active":
                     reasons.add(nm)
         return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx or None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm),
+                "source": "nvml 20 ms" if self.nv is not None else "nvidia-smi 200 ms"}
 
 
 def ensure_model(yl, rank: int, world: int, dist) -> str:
