@@ -283,7 +283,9 @@ def run_reference(args) -> None:
 def profile_case(case: str) -> None:
     """Small fixed workloads for ncu captures (printed results are not bench
     values). `matvec:ROWSxK`: three batch-1 Q8_0 matvecs of that shape with
-    random weights (the bench's dominant kernel at 28672x4096). `decode4`: a
+    random weights (the bench's dominant kernel at 28672x4096). `gemm:OxKxB`:
+    the Q8_0 matmul of B tokens (the tensor-core GEMM from 16 tokens), timed
+    over 10 launches with CUDA events after 3 untimed ones. `decode4`: a
     4-layer config-4-shaped model, prompt 8, then 4 decode steps launched
     kernel by kernel (no graph)."""
     import torch
@@ -301,6 +303,27 @@ def profile_case(case: str) -> None:
         out = torch.zeros(o, device="cuda")
         for _ in range(3):
             yl.matmul(out, xa, w, n, o, 32, batch=1, accumulate=False)
+    elif case.startswith("gemm:"):
+        o, n, b = (int(v) for v in case.split(":", 1)[1].split("x"))
+        w = yl.QuantizedTensor.weight(yl.WeightFormat.Q8_0, o, n, 32, 1)
+        w.upload(quant_vals=rng.integers(-127, 128, o * n, dtype=np.int8),
+                 scale_factor=(np.abs(rng.standard_normal(o * n // 32)) * 1e-3).astype(np.float32))
+        xa = yl.new_workspace_buffer(yl.WeightFormat.Q8_0, b * n, 32)
+        yl.quantize(yl.WeightFormat.Q8_0, xa, torch.tensor(rng.standard_normal(b * n).astype(np.float32),
+                                                           device="cuda"), b * n, 32)
+        out = torch.zeros(b * o, device="cuda")
+        for _ in range(3):
+            yl.matmul(out, xa, w, n, o, 32, batch=b, accumulate=False)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        torch.cuda.synchronize()
+        ev[0].record()
+        for _ in range(10):
+            yl.matmul(out, xa, w, n, o, 32, batch=b, accumulate=False)
+        ev[1].record()
+        torch.cuda.synchronize()
+        us = ev[0].elapsed_time(ev[1]) * 100.0
+        print(json.dumps({"case": case, "us_per_launch": us, "tops": 2.0 * o * n * b / us * 1e-6,
+                          "weight_gbs": o * n * 34 / 32 / us * 1e-3}))
     elif case == "decode4":
         path = os.path.join(os.environ.get("YL_BENCH_DIR", "/tmp"), "yl_c4_4layers.gguf")
         if not os.path.exists(path):
@@ -326,7 +349,7 @@ def main() -> None:
     ap.add_argument("--e2e-steps", type=int, default=128)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-tokens", type=int, default=3)
-    ap.add_argument("--case", default=None, help="profiling workload (matvec:ROWSxK or decode4), no bench line")
+    ap.add_argument("--case", default=None, help="profiling workload (matvec:ROWSxK, gemm:ROWSxKxTOKENS or decode4), no bench line")
     args = ap.parse_args()
     if args.case:
         profile_case(args.case)

@@ -106,6 +106,26 @@ def test_tiny_models_match_oracle(yl, orc, model_factory, preset, over):
     assert_ids_match(gids, oids, olg, bound_for(sens))
 
 
+@pytest.mark.parametrize("preset,over", [
+    ("tiny", {}),
+    ("tiny128", {"weight_format": 2}),
+    ("tiny", {"weight_format": 2, "llama3_scaling": True, "rope_theta": 5e5, "context_length": 131072}),
+])
+def test_gemm_prefill_matches_oracle(yl, orc, model_factory, preset, over):
+    """A 70-token prompt: every projection of the prefill runs on the int8
+    tensor-core GEMM (two token tiles, the second partial; RMSNorm as its own
+    kernel; SwiGLU + h quantization in the gate/up epilogue), then greedy
+    decode on the matvec path."""
+    path = model_factory(preset, **over)
+    vocab = yl.PRESETS[preset]["vocab_size"]
+    prompt = yl.prompt_ids(vocab, 70, 99).tolist()
+    errs, gids, oids, _, _ = run_pair(yl, orc, path, prompt, 8, 256)
+    olg = run_pair.oracle_logits
+    sens = oracle_sensitivity(orc, path, prompt, oids, 256)
+    assert max(errs) < bound_for(sens), (errs, sens)
+    assert_ids_match(gids, oids, olg, bound_for(sens))
+
+
 def test_decode_graph_matches_host_loop(yl, orc, model_factory):
     path = model_factory("tiny128")
     gm = yl.load_transformer(path, max_ctx_len=512)

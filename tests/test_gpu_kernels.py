@@ -211,6 +211,55 @@ def test_f32_weight_scales(yl, orc, torch_cuda):
     assert np.all(np.abs(got - ref) <= 1e-5 * term_bound(xq, xs, wq, ws, 2, n, o) + 1e-30)
 
 
+GEMM_CASES = [(260, 576, 17), (1000, 2048, 64), (128, 32, 65), (384, 2080, 130), (2048, 2048, 256)]
+
+
+@pytest.mark.parametrize("o,n,batch", GEMM_CASES)
+@pytest.mark.parametrize("fmt", ["Q8_0", "Q4_0"])
+@pytest.mark.parametrize("scale_type", [1, 0])
+def test_gemm_bit_exact_vs_oracle(yl, orc, torch_cuda, o, n, batch, fmt, scale_type):
+    """Batches of 16 or more tokens run on the int8 tensor-core GEMM. It folds
+    each 32-block's exact int32 dot as ((f32)isum * ws) * xs in group order,
+    the oracle's sequence (weight_type.rs:190-224), so into a zeroed output the
+    results are bit-identical. Cases cover row and token tails, a single
+    block, an odd block count (f16 scale pairs) and several K stages."""
+    rng = np.random.default_rng(o + n + batch)
+    f = getattr(yl.WeightFormat, fmt)
+    lo, hi = (-127, 128) if fmt == "Q8_0" else (-8, 8)
+    wq = rng.integers(lo, hi, o * n, dtype=np.int8)
+    ws = (np.abs(rng.standard_normal(o * n // 32)) * 1e-3 + 1e-5).astype(np.float32)
+    if scale_type == 1:
+        ws = ws.astype(np.float16).astype(np.float32)
+    x = rng.standard_normal(batch * n).astype(np.float32)
+    xq, xs = orc.quantize_q8(x)
+    w = upload_weight(yl, f, wq, ws, o, n, scale_type=scale_type)
+    got = run_matmul(yl, torch_cuda, upload_act(yl, f, xq, xs), w, n, o, batch, accumulate=False)
+    ref = np.zeros(batch * o, np.float32)
+    orc.matmul_q8(ref, xq, xs, wq, ws, n, o)
+    assert np.array_equal(got, ref), float(np.max(np.abs(got - ref)))
+
+
+@pytest.mark.parametrize("fmt", ["Q8_0", "Q4_0"])
+def test_gemm_accumulate_quirk(yl, orc, torch_cuda, fmt):
+    """The `+=` quirk through the GEMM: quad columns add into the initial
+    output, remainder columns overwrite it (weight_type.rs:190-224)."""
+    rng = np.random.default_rng(11)
+    o, n, batch = 262, 1024, 40
+    f = getattr(yl.WeightFormat, fmt)
+    lo, hi = (-127, 128) if fmt == "Q8_0" else (-8, 8)
+    wq = rng.integers(lo, hi, o * n, dtype=np.int8)
+    ws = (np.abs(rng.standard_normal(o * n // 32)) * 1e-3 + 1e-5).astype(np.float16).astype(np.float32)
+    xq, xs = orc.quantize_q8(rng.standard_normal(batch * n).astype(np.float32))
+    init = rng.standard_normal(batch * o).astype(np.float32)
+    w = upload_weight(yl, f, wq, ws, o, n)
+    got = run_matmul(yl, torch_cuda, upload_act(yl, f, xq, xs), w, n, o, batch, init=init, accumulate=True)
+    ref = init.copy()
+    orc.matmul_q8(ref, xq, xs, wq, ws, n, o)
+    quad = np.tile(np.arange(o) < o // 4 * 4, batch)
+    tb = term_bound(xq, xs, wq, ws, batch, n, o)
+    assert np.all(np.abs(got - ref) <= 1e-5 * (tb + np.abs(init) * quad) + 1e-30)
+
+
 def test_full_size_lm_head_rows_sampled(yl, orc, torch_cuda):
     """(128256, 4096) Q8_0 at N=1: every output row depends on its own weight
     row only, so a random sample of rows checked against the oracle covers the

@@ -302,6 +302,8 @@ const Tunables& tunables() {
     if (const char* e = getenv("YL_MV_GRID_MULT")) x.grid_mult = std::max(1, atoi(e));
     if (const char* e = getenv("YL_LM_LIMBS")) x.limbs = atoi(e) != 0;
     if (const char* e = getenv("YL_TP_FUSED")) x.tp_fused = atoi(e) != 0;
+    if (const char* e = getenv("YL_GEMM")) x.gemm = atoi(e) != 0;
+    if (const char* e = getenv("YL_GEMM_MIN")) x.gemm_min = (uint32_t)std::max(2, atoi(e));
     return x;
   }();
   return t;
@@ -743,6 +745,39 @@ int run_matvec_ex(const DevWeight& w, bool f32act, const int8_t* xq, const float
   lc.pdl = pdl;
   lc.grid = (uint32_t)num_sms * tu.grid_mult;
   lc.smem_budget = tu.smem;
+  // several tokens with int8 activations: the tensor-core GEMM (weights read
+  // once per 64 tokens), with the RMSNorm prologue as a separate kernel
+  if (!f32act && tu.gemm && ntok >= tu.gemm_min && ex.tp_mode == 0 && (fmt == k::FMT_Q8 || fmt == k::FMT_Q4) &&
+      (ex.pro == k::PRO_LOAD || (ex.pro == k::PRO_NORM && ex.gq && ex.gs && ex.xres && ex.norm_w))) {
+    k::GemmArgs g{};
+    g.wq = w.q;
+    g.ws = w.s;
+    g.rows = w.rows;
+    g.K = w.cols;
+    g.row_bytes = w.row_bytes;
+    g.scale_row_bytes = w.scale_row_bytes;
+    g.xq = ex.pro == k::PRO_NORM ? ex.gq : xq;
+    g.xs = ex.pro == k::PRO_NORM ? ex.gs : xs;
+    g.x_stride = ex.pro == k::PRO_NORM ? w.cols : x_stride;
+    g.xs_stride = ex.pro == k::PRO_NORM ? w.cols / 32 : xs_stride;
+    g.ntok = ntok;
+    g.out = out;
+    g.out_stride = out_stride;
+    g.quirk_cols = quirk_cols;
+    g.hq = ex.hq;
+    g.hs = ex.hs;
+    if (k::gemm_supported(g, fmt, w.sf16, epi)) {
+      if (ex.pro == k::PRO_NORM) {
+        cudaError_t e = k::rmsnorm_quant(ex.xres, ex.norm_w, ntok, w.cols, ex.eps, ex.gq, ex.gs, nullptr, lc);
+        if (e != cudaSuccess) return fail(YL_ERR_CUDA, std::string("rmsnorm_quant launch: ") + cudaGetErrorString(e));
+        if (launches) ++*launches;
+      }
+      cudaError_t e = k::gemm_q(g, fmt, w.sf16, epi, lc);
+      if (e != cudaSuccess) return fail(YL_ERR_CUDA, std::string("gemm launch: ") + cudaGetErrorString(e));
+      if (launches) ++*launches;
+      return YL_OK;
+    }
+  }
   const uint32_t kc_eff = std::min<uint32_t>(kc, (uint32_t)round_up(w.cols, 256));
   const uint32_t group = k::matvec_max_ntok(fmt, w.cols, kc_eff, epi);
   if (group == 0) return fail(YL_ERR_UNSUPPORTED, "matvec row length too large for shared memory");
@@ -866,6 +901,8 @@ int enqueue_forward(Session* s, uint32_t n, uint32_t start_pos, bool from_state,
   norm.pro = k::PRO_NORM;
   norm.xres = s->x;
   norm.eps = sh.rms_norm_eps;
+  norm.gq = decode ? nullptr : s->xq;  // multi-token passes: normalized rows for the GEMM
+  norm.gs = decode ? nullptr : s->xs;
   // Tensor-parallel single-token steps: wo and down push their partial rows
   // into every rank's inbox in their epilogue, and the next RMSNorm prologue
   // all-reduces them into the residual, which alternates between two rows

@@ -141,6 +141,8 @@ struct Tunables {
   bool pdl = true;
   uint32_t grid_mult = 2;    // matvec CTAs per SM
   bool limbs = true;         // Q8_0 lm_head on three-limb int8 activations
+  bool gemm = true;          // multi-token passes on the int8 tensor-core GEMM
+  uint32_t gemm_min = 16;    // from this many tokens
   bool tp_fused = true;      // tensor-parallel decode: exchange fused into the projections (else exchange kernels)
 };
 const Tunables& tunables();
@@ -152,6 +154,8 @@ int run_matvec(const DevWeight& w, bool f32act, const int8_t* xq, const float* x
 struct MvExtra {
   int pro = 0;                 // k::PRO_*
   const float* xres = nullptr; // PRO_NORM: residual rows (stride x_stride)
+  int8_t* gq = nullptr;        // PRO_NORM through the multi-token GEMM: the
+  float* gs = nullptr;         // normalized, quantized rows [ntok][K] / [ntok][K/32]
   const float* norm_w = nullptr;
   float eps = 0.f;
   int8_t* hq = nullptr;        // EPI_SWIGLU_Q8 outputs and block counters

@@ -20,6 +20,8 @@ enum : int { ERR_NONE = 0, ERR_WAIT_TIMEOUT = 1, ERR_BAD_ARG = 2 };
 __device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 // Allow the next kernel in the stream to be scheduled (it still waits in
 // grid_dep_wait() for this grid to finish before reading our outputs).
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // 8-byte {value, flag} exchange entries: one aligned 64-bit access each is
 // single-copy atomic, so a reader that sees the flag sees the value with it.
 __device__ __forceinline__ void st_volatile_u64(void* p, uint64_t v) {
@@ -34,7 +36,13 @@ __device__ __forceinline__ uint64_t globaltimer() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
-__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// SwiGLU of one gate/up pair.
+__device__ __forceinline__ float silu_mul(float g, float u) {
+  // forward.rs:230-235: g / (1 + exp(-g)) * u
+  float s = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
+  return __fmul_rn(s, u);
+}
 
 // ---- time ----------------------------------------------------------------
 __device__ __forceinline__ uint64_t global_ns() {

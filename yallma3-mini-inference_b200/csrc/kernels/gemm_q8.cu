@@ -1,0 +1,312 @@
+// Multi-token projections (prefill, batched matmul): an int8 tensor-core GEMM
+// over Q8_0 / Q4_0 weights with the reference's per-32-block fold
+// (weight_type.rs:122-226):
+//   out[t][r] = sum over groups g, in order, of ((f32)isum(r,t,g) * ws[r][g]) * xs[t][g]
+// One mma.sync m16n8k32 (s8 x s8 -> s32) covers exactly one 32-element block,
+// so every block's exact int32 dot is folded into the f32 accumulators right
+// after its instruction, in the reference's order. Q4_0 nibbles are widened to
+// int8 (q - 8) in registers.
+//
+// Tiles: 128 weight rows x 64 tokens per CTA, 8 warps as 4 (rows) x 2 (tokens),
+// 32 x 32 outputs per warp; K is staged 4 blocks at a time through a 3-stage
+// cp.async ring (rows padded by 16 bytes: fragment loads are bank-conflict
+// free). The grid walks token tiles fastest, so the CTAs sharing a weight tile
+// run together and the tile comes from HBM once.
+//
+// Epilogues: store, residual add, the reference's `+=` quirk on quad columns,
+// and SwiGLU + Q8_0 quantization of h (forward.rs:206-240) for interleaved
+// gate/up rows (gate j at 2j, up j at 2j+1): the loader puts gate rows in the
+// upper and up rows in the lower half of every 16-row MMA tile, so one thread
+// holds both values of a pair; a CTA's 64 h values per token are two whole
+// quantization blocks, quantized by the bit-exact warp quantizer.
+#include "device.cuh"
+#include "kernels.h"
+
+namespace yl {
+namespace k {
+using namespace yl::dev;
+
+namespace {
+constexpr int GB_M = 128, GB_N = 64, GB_KB = 4, GB_S = 3, GB_THREADS = 256;
+
+template <int FMT>
+struct GTile {
+  static constexpr int QB = FMT == FMT_Q4 ? 16 : 32;  // weight bytes per 32-block
+  static constexpr int WROW = GB_KB * QB + 16;         // padded shared-memory rows
+  static constexpr int XROW = GB_KB * 32 + 16;
+  static constexpr int W_BYTES = GB_M * WROW;
+  static constexpr int X_BYTES = GB_N * XROW;
+  static constexpr int WS_BYTES = GB_M * GB_KB * 4;
+  static constexpr int XS_BYTES = GB_N * GB_KB * 4;
+  static constexpr int STAGE = W_BYTES + X_BYTES + WS_BYTES + XS_BYTES;
+  static constexpr int SMEM = GB_S * STAGE;
+};
+static_assert(GTile<FMT_Q8>::STAGE % 16 == 0 && GTile<FMT_Q4>::STAGE % 16 == 0, "stage alignment");
+static_assert(GB_N * GB_M / 2 * 4 <= GTile<FMT_Q4>::SMEM, "SwiGLU staging fits the ring");
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void mma_s8(int (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
+  asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]), "r"(0));
+}
+
+// Exact int32 -> f32 for |v| < 2^22 (a block dot is at most 32 * 128 * 128 =
+// 2^19): the integer added to the bits of 1.5 * 2^23 lands in the mantissa.
+__device__ __forceinline__ float small_i2f(int v) {
+  return __fsub_rn(__int_as_float(v + 0x4B400000), 12582912.0f);
+}
+
+// Shared-memory row of weight row i of the tile: with PERM, in each aligned
+// group of 16 rows the even rows (gate) go to the first 8 slots and the odd
+// rows (up) to the last 8, in order.
+template <bool PERM>
+__device__ __forceinline__ uint32_t tile_row(uint32_t i) {
+  if (!PERM) return i;
+  const uint32_t w = i & 15u;
+  return (i & ~15u) + (w >> 1) + ((w & 1u) << 3);
+}
+
+template <int FMT, bool SF16, bool PERM>
+__device__ __forceinline__ void gemm_load(const GemmArgs& a, uint8_t* st, uint32_t m0, uint32_t n0, uint32_t g0,
+                                          uint32_t nb) {
+  using T = GTile<FMT>;
+  uint8_t* wt = st;
+  uint8_t* xt = wt + T::W_BYTES;
+  uint8_t* wsc = xt + T::X_BYTES;
+  uint8_t* xsc = wsc + T::WS_BYTES;
+  const uint32_t tid = threadIdx.x;
+  // rows / tokens past the end re-read the last one (in bounds); their
+  // results are never stored
+  const uint32_t wp = nb * T::QB / 16;  // 16-byte pieces per weight row
+  for (uint32_t i = tid; i < GB_M * wp; i += GB_THREADS) {
+    const uint32_t r = i / wp, p = i - r * wp;
+    const uint32_t gr = min(m0 + r, a.rows - 1);
+    cp_async16(wt + tile_row<PERM>(r) * T::WROW + p * 16,
+               a.wq + (uint64_t)gr * a.row_bytes + (uint64_t)g0 * T::QB + p * 16);
+  }
+  const uint32_t xp = nb * 2;
+  for (uint32_t i = tid; i < GB_N * xp; i += GB_THREADS) {
+    const uint32_t t = i / xp, p = i - t * xp;
+    const uint32_t gt = min(n0 + t, a.ntok - 1);
+    cp_async16(xt + t * T::XROW + p * 16, a.xq + (uint64_t)gt * a.x_stride + (uint64_t)g0 * 32 + p * 16);
+  }
+  if (SF16) {  // f16 scales in pairs (the launcher checks the row padding holds an odd tail's pair)
+    const uint32_t sp = (nb + 1) / 2;
+    for (uint32_t i = tid; i < GB_M * sp; i += GB_THREADS) {
+      const uint32_t r = i / sp, p = i - r * sp;
+      const uint32_t gr = min(m0 + r, a.rows - 1);
+      cp_async4(wsc + (tile_row<PERM>(r) * GB_KB + 2 * p) * 2,
+                a.ws + (uint64_t)gr * a.scale_row_bytes + (uint64_t)(g0 + 2 * p) * 2);
+    }
+  } else {
+    for (uint32_t i = tid; i < GB_M * nb; i += GB_THREADS) {
+      const uint32_t r = i / nb, b = i - r * nb;
+      const uint32_t gr = min(m0 + r, a.rows - 1);
+      cp_async4(wsc + (tile_row<PERM>(r) * GB_KB + b) * 4, a.ws + (uint64_t)gr * a.scale_row_bytes + (uint64_t)(g0 + b) * 4);
+    }
+  }
+  for (uint32_t i = tid; i < GB_N * nb; i += GB_THREADS) {
+    const uint32_t t = i / nb, b = i - t * nb;
+    const uint32_t gt = min(n0 + t, a.ntok - 1);
+    cp_async4(xsc + (t * GB_KB + b) * 4, a.xs + (uint64_t)gt * a.xs_stride + g0 + b);
+  }
+}
+
+template <int FMT, bool SF16, int EPI>
+__global__ void __launch_bounds__(GB_THREADS, 2) gemm_q_kernel(GemmArgs a) {
+  using T = GTile<FMT>;
+  constexpr bool PERM = EPI == EPI_SWIGLU_Q8;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const uint32_t n0 = blockIdx.x * GB_N, m0 = blockIdx.y * GB_M;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int gid = lane >> 2, tig = lane & 3;
+  const int wm = warp & 3, wn = warp >> 2;
+  const uint32_t G = a.K / 32, nch = (G + GB_KB - 1) / GB_KB;
+
+  grid_dep_wait();  // activations come from the preceding kernel
+#pragma unroll
+  for (int s = 0; s < GB_S - 1; ++s) {
+    if ((uint32_t)s < nch)
+      gemm_load<FMT, SF16, PERM>(a, smem + s * T::STAGE, m0, n0, s * GB_KB, min((uint32_t)GB_KB, G - s * GB_KB));
+    cp_async_commit();
+  }
+
+  float acc[2][4][4];
+#pragma unroll
+  for (int i = 0; i < 2; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[i][j][e] = 0.0f;
+
+  for (uint32_t c = 0; c < nch; ++c) {
+    cp_async_wait<GB_S - 2>();
+    __syncthreads();  // stage c landed for every thread; stage c-1 is free
+    const uint32_t cn = c + GB_S - 1;
+    if (cn < nch)
+      gemm_load<FMT, SF16, PERM>(a, smem + (cn % GB_S) * T::STAGE, m0, n0, cn * GB_KB,
+                                 min((uint32_t)GB_KB, G - cn * GB_KB));
+    cp_async_commit();
+
+    const uint8_t* wt = smem + (c % GB_S) * T::STAGE;
+    const uint8_t* xt = wt + T::W_BYTES;
+    const uint8_t* wsc = xt + T::X_BYTES;
+    const float* xsc = reinterpret_cast<const float*>(wsc + T::WS_BYTES);
+    const uint32_t nb = min((uint32_t)GB_KB, G - c * GB_KB);
+    for (uint32_t b = 0; b < nb; ++b) {
+      uint32_t af[2][4], bf[4][2];
+      float w0[2], w1[2], x0[4], x1[4];
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt) {
+        const int rr = wm * 32 + mt * 16 + gid;
+        const uint8_t* p = wt + rr * T::WROW + b * T::QB + tig * 4;
+        if (FMT == FMT_Q8) {
+          af[mt][0] = *reinterpret_cast<const uint32_t*>(p);
+          af[mt][1] = *reinterpret_cast<const uint32_t*>(p + 8 * T::WROW);
+          af[mt][2] = *reinterpret_cast<const uint32_t*>(p + 16);
+          af[mt][3] = *reinterpret_cast<const uint32_t*>(p + 8 * T::WROW + 16);
+        } else {  // element j: low nibble of byte j, element j + 16: high nibble; value q - 8
+          const uint32_t v0 = *reinterpret_cast<const uint32_t*>(p);
+          const uint32_t v1 = *reinterpret_cast<const uint32_t*>(p + 8 * T::WROW);
+          af[mt][0] = __vsub4(v0 & 0x0F0F0F0Fu, 0x08080808u);
+          af[mt][1] = __vsub4(v1 & 0x0F0F0F0Fu, 0x08080808u);
+          af[mt][2] = __vsub4((v0 >> 4) & 0x0F0F0F0Fu, 0x08080808u);
+          af[mt][3] = __vsub4((v1 >> 4) & 0x0F0F0F0Fu, 0x08080808u);
+        }
+        if (SF16) {
+          w0[mt] = __half2float(reinterpret_cast<const __half*>(wsc)[rr * GB_KB + b]);
+          w1[mt] = __half2float(reinterpret_cast<const __half*>(wsc)[(rr + 8) * GB_KB + b]);
+        } else {
+          w0[mt] = reinterpret_cast<const float*>(wsc)[rr * GB_KB + b];
+          w1[mt] = reinterpret_cast<const float*>(wsc)[(rr + 8) * GB_KB + b];
+        }
+      }
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) {
+        const uint8_t* q = xt + (wn * 32 + nt * 8 + gid) * T::XROW + b * 32 + tig * 4;
+        bf[nt][0] = *reinterpret_cast<const uint32_t*>(q);
+        bf[nt][1] = *reinterpret_cast<const uint32_t*>(q + 16);
+        const int tt = wn * 32 + nt * 8 + tig * 2;
+        x0[nt] = xsc[tt * GB_KB + b];
+        x1[nt] = xsc[(tt + 1) * GB_KB + b];
+      }
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt) {
+          int d[4];
+          mma_s8(d, af[mt], bf[nt]);
+          // ((f32)isum * w_scale) * x_scale, added in group order
+          acc[mt][nt][0] = __fadd_rn(acc[mt][nt][0], __fmul_rn(__fmul_rn(small_i2f(d[0]), w0[mt]), x0[nt]));
+          acc[mt][nt][1] = __fadd_rn(acc[mt][nt][1], __fmul_rn(__fmul_rn(small_i2f(d[1]), w0[mt]), x1[nt]));
+          acc[mt][nt][2] = __fadd_rn(acc[mt][nt][2], __fmul_rn(__fmul_rn(small_i2f(d[2]), w1[mt]), x0[nt]));
+          acc[mt][nt][3] = __fadd_rn(acc[mt][nt][3], __fmul_rn(__fmul_rn(small_i2f(d[3]), w1[mt]), x1[nt]));
+        }
+    }
+  }
+
+  if (EPI == EPI_SWIGLU_Q8) {
+    cp_async_wait<0>();
+    __syncthreads();  // the ring is free: it now stages h [64 tokens][64 pairs]
+    float* hb = reinterpret_cast<float*>(smem);
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) {
+        const int jl = wm * 16 + mt * 8 + gid;  // pair of this thread's rows gid (gate) and gid + 8 (up)
+        const int tl = wn * 32 + nt * 8 + tig * 2;
+        hb[tl * (GB_M / 2) + jl] = silu_mul(acc[mt][nt][0], acc[mt][nt][2]);
+        hb[(tl + 1) * (GB_M / 2) + jl] = silu_mul(acc[mt][nt][1], acc[mt][nt][3]);
+      }
+    __syncthreads();
+    const uint32_t f = a.rows / 2;
+    for (int pi = warp; pi < GB_N * 2; pi += GB_THREADS / 32) {
+      const int tl = pi >> 1, blk = pi & 1;
+      const uint32_t t = n0 + tl;
+      if (t >= a.ntok) continue;  // warp-uniform
+      const float v = hb[tl * (GB_M / 2) + blk * 32 + lane];
+      float sc;
+      const int8_t q = quant_q8_lane(v, &sc);
+      const uint32_t j = m0 / 2 + blk * 32 + lane;
+      a.hq[(uint64_t)t * f + j] = q;
+      if (lane == 0) a.hs[(uint64_t)t * (f / 32) + j / 32] = sc;
+      if (a.out) a.out[(uint64_t)t * a.out_stride + j] = v;
+    }
+    return;
+  }
+
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const uint32_t r = m0 + wm * 32 + mt * 16 + gid + (e >> 1) * 8;
+        const uint32_t t = n0 + wn * 32 + nt * 8 + tig * 2 + (e & 1);
+        if (r >= a.rows || t >= a.ntok) continue;
+        float* o = a.out + (uint64_t)t * a.out_stride + r;
+        const float v = acc[mt][nt][e];
+        if (EPI == EPI_STORE) *o = v;
+        else if (EPI == EPI_ADD) *o = __fadd_rn(*o, v);
+        else *o = r < a.quirk_cols ? __fadd_rn(*o, v) : v;
+      }
+}
+
+template <int FMT, bool SF16, int EPI>
+cudaError_t gemm_launch(const GemmArgs& a, const LaunchCfg& lc) {
+  using T = GTile<FMT>;
+  cudaError_t e =
+      cudaFuncSetAttribute(gemm_q_kernel<FMT, SF16, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, T::SMEM);
+  if (e != cudaSuccess) return e;
+  const dim3 grid((a.ntok + GB_N - 1) / GB_N, (a.rows + GB_M - 1) / GB_M);
+  return launch_kernel(gemm_q_kernel<FMT, SF16, EPI>, grid, dim3(GB_THREADS), (uint32_t)T::SMEM, lc, a);
+}
+
+template <int FMT, bool SF16>
+cudaError_t gemm_epi(const GemmArgs& a, int epi, const LaunchCfg& lc) {
+  switch (epi) {
+    case EPI_STORE: return gemm_launch<FMT, SF16, EPI_STORE>(a, lc);
+    case EPI_ADD: return gemm_launch<FMT, SF16, EPI_ADD>(a, lc);
+    case EPI_QUIRK: return gemm_launch<FMT, SF16, EPI_QUIRK>(a, lc);
+    case EPI_SWIGLU_Q8: return gemm_launch<FMT, SF16, EPI_SWIGLU_Q8>(a, lc);
+    default: return cudaErrorInvalidValue;
+  }
+}
+}  // namespace
+
+bool gemm_supported(const GemmArgs& a, int fmt, bool sf16, int epi) {
+  if (fmt != FMT_Q8 && fmt != FMT_Q4) return false;
+  if (epi != EPI_STORE && epi != EPI_ADD && epi != EPI_QUIRK && epi != EPI_SWIGLU_Q8) return false;
+  if (!a.wq || !a.ws || !a.xq || !a.xs || a.rows == 0 || a.ntok == 0 || a.K == 0 || a.K % 32) return false;
+  if ((a.rows + GB_M - 1) / GB_M > 65535u) return false;
+  const uint32_t G = a.K / 32;
+  const uint32_t qb = fmt == FMT_Q4 ? 16 : 32;
+  if ((uintptr_t)a.wq % 16 || a.row_bytes % 16 || a.row_bytes < G * qb) return false;
+  if ((uintptr_t)a.xq % 16 || a.x_stride % 16 || a.x_stride < a.K) return false;
+  if ((uintptr_t)a.xs % 4 || a.xs_stride < G) return false;
+  if ((uintptr_t)a.ws % 4 || a.scale_row_bytes % 4) return false;
+  if (sf16 ? a.scale_row_bytes < 2 * (G + (G & 1)) : a.scale_row_bytes < 4 * G) return false;
+  if (epi == EPI_SWIGLU_Q8) return a.rows % GB_M == 0 && a.hq && a.hs;
+  return a.out != nullptr;
+}
+
+cudaError_t gemm_q(const GemmArgs& a, int fmt, bool sf16, int epi, const LaunchCfg& lc) {
+  if (!gemm_supported(a, fmt, sf16, epi)) return cudaErrorInvalidValue;
+  if (fmt == FMT_Q8) return sf16 ? gemm_epi<FMT_Q8, true>(a, epi, lc) : gemm_epi<FMT_Q8, false>(a, epi, lc);
+  return sf16 ? gemm_epi<FMT_Q4, true>(a, epi, lc) : gemm_epi<FMT_Q4, false>(a, epi, lc);
+}
+
+}  // namespace k
+}  // namespace yl

@@ -122,6 +122,29 @@ cudaError_t matvec(const MvArgs& a, int fmt, bool scale_f16, int epi, const Laun
 // at least two ring stages.
 uint32_t matvec_max_ntok(int fmt, uint32_t K, uint32_t kc, int epi);
 
+// ---- multi-token projections (int8 tensor-core GEMM) ----------------------
+// out[t][r] = sum_g ((f32)isum * ws[r][g]) * xs[t][g] over Q8_0 / Q4_0 weight
+// rows (f16 or f32 scales) and Q8_0 activation rows; epi: EPI_STORE,
+// EPI_ADD, EPI_QUIRK (quirk_cols) or EPI_SWIGLU_Q8 (interleaved gate/up rows,
+// rows % 128 == 0: h quantized into hq [ntok][rows/2] / hs [ntok][rows/64],
+// and h as f32 into out when out is not null).
+struct GemmArgs {
+  const uint8_t* wq;
+  const uint8_t* ws;
+  uint32_t rows, K, row_bytes, scale_row_bytes;
+  const int8_t* xq;
+  const float* xs;
+  uint64_t x_stride, xs_stride;  // bytes / floats per token row
+  uint32_t ntok;
+  float* out;
+  uint64_t out_stride;
+  uint32_t quirk_cols;
+  int8_t* hq;
+  float* hs;
+};
+bool gemm_supported(const GemmArgs& a, int fmt, bool scale_f16, int epi);
+cudaError_t gemm_q(const GemmArgs& a, int fmt, bool scale_f16, int epi, const LaunchCfg& lc);
+
 // ---- activations ------------------------------------------------------------
 // Bit-exact Q8_0 quantization of nblocks 32-element blocks (warp per block).
 cudaError_t quantize_q8(const float* x, int8_t* q, float* s, uint64_t nblocks, const LaunchCfg& lc);

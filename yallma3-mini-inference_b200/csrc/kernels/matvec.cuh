@@ -102,11 +102,6 @@ __device__ __forceinline__ float ld_scale(const uint8_t* base, int idx) {
   return reinterpret_cast<const float*>(base)[idx];
 }
 
-__device__ __forceinline__ float silu_mul(float g, float u) {
-  // forward.rs:230-235: g / (1 + exp(-g)) * u
-  float s = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
-  return __fmul_rn(s, u);
-}
 
 // int8 -> f32 for 4 packed bytes without the (quarter-rate) I2F unit:
 // 0x4B000000 | (b ^ 0x80) is the float 2^23 + b + 128, exact.
