@@ -284,8 +284,9 @@ def profile_case(case: str) -> None:
     """Small fixed workloads for ncu captures (printed results are not bench
     values). `matvec:ROWSxK`: three batch-1 Q8_0 matvecs of that shape with
     random weights (the bench's dominant kernel at 28672x4096). `gemm:OxKxB`:
-    the Q8_0 matmul of B tokens (the tensor-core GEMM from 16 tokens), timed
-    over 10 launches with CUDA events after 3 untimed ones. `decode4`: a
+    the Q8_0 matmul of B tokens (the tensor-core GEMM from 32 tokens), timed
+    over 10 launches with CUDA events after 3 untimed ones. `prefill4`: the
+    4-layer model below, one 512-token prefill. `decode4`: a
     4-layer config-4-shaped model, prompt 8, then 4 decode steps launched
     kernel by kernel (no graph)."""
     import torch
@@ -324,6 +325,14 @@ def profile_case(case: str) -> None:
         us = ev[0].elapsed_time(ev[1]) * 100.0
         print(json.dumps({"case": case, "us_per_launch": us, "tops": 2.0 * o * n * b / us * 1e-6,
                           "weight_gbs": o * n * 34 / 32 / us * 1e-3}))
+        return
+    elif case == "prefill4":
+        path = os.path.join(os.environ.get("YL_BENCH_DIR", "/tmp"), "yl_c4_4layers.gguf")
+        if not os.path.exists(path):
+            yl.synth_preset(CONFIG, path, n_layers=4)
+        m = yl.load_transformer(path, max_ctx_len=1024)
+        prompt = yl.prompt_ids(yl.PRESETS[CONFIG]["vocab_size"], 512, 1).tolist()
+        m.forward_x_full(prompt, 0, m.create_session(), want_logits=False)
     elif case == "decode4":
         path = os.path.join(os.environ.get("YL_BENCH_DIR", "/tmp"), "yl_c4_4layers.gguf")
         if not os.path.exists(path):
@@ -349,7 +358,7 @@ def main() -> None:
     ap.add_argument("--e2e-steps", type=int, default=128)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-tokens", type=int, default=3)
-    ap.add_argument("--case", default=None, help="profiling workload (matvec:ROWSxK, gemm:ROWSxKxTOKENS or decode4), no bench line")
+    ap.add_argument("--case", default=None, help="profiling workload (matvec:ROWSxK, gemm:ROWSxKxTOKENS, prefill4 or decode4), no bench line")
     args = ap.parse_args()
     if args.case:
         profile_case(args.case)

@@ -9,8 +9,8 @@
 //
 // Tiles: 128 weight rows x 64 tokens per CTA, 8 warps as 4 (rows) x 2 (tokens),
 // 32 x 32 outputs per warp; K is staged 4 blocks at a time through a 3-stage
-// cp.async ring (rows padded by 16 bytes: fragment loads are bank-conflict
-// free). The grid walks token tiles fastest, so the CTAs sharing a weight tile
+// cp.async ring (rows padded by 16 bytes: the ldmatrix fragment loads are
+// bank-conflict free). The grid walks token tiles fastest, so the CTAs sharing a weight tile
 // run together and the tile comes from HBM once.
 //
 // Epilogues: store, residual add, the reference's `+=` quirk on quad columns,
@@ -62,10 +62,16 @@ __device__ __forceinline__ void mma_s8(int (&d)[4], const uint32_t (&a)[4], cons
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]), "r"(0));
 }
 
-// Exact int32 -> f32 for |v| < 2^22 (a block dot is at most 32 * 128 * 128 =
-// 2^19): the integer added to the bits of 1.5 * 2^23 lands in the mantissa.
-__device__ __forceinline__ float small_i2f(int v) {
-  return __fsub_rn(__int_as_float(v + 0x4B400000), 12582912.0f);
+// ldmatrix: four (two) 8x8 tiles of 16-bit elements; for int8 data a lane
+// receives 4 consecutive bytes of row lane/4 at byte (lane%4)*4 of each tile,
+// which is the m16n8k32 s8 fragment layout.
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void ldsm_x2(uint32_t& r0, uint32_t& r1, const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(smem_u32(p)));
 }
 
 // Shared-memory row of weight row i of the tile: with PERM, in each aligned
@@ -117,10 +123,10 @@ __device__ __forceinline__ void gemm_load(const GemmArgs& a, uint8_t* st, uint32
       cp_async4(wsc + (tile_row<PERM>(r) * GB_KB + b) * 4, a.ws + (uint64_t)gr * a.scale_row_bytes + (uint64_t)(g0 + b) * 4);
     }
   }
-  for (uint32_t i = tid; i < GB_N * nb; i += GB_THREADS) {
+  for (uint32_t i = tid; i < GB_N * nb; i += GB_THREADS) {  // stored [block][token]
     const uint32_t t = i / nb, b = i - t * nb;
     const uint32_t gt = min(n0 + t, a.ntok - 1);
-    cp_async4(xsc + (t * GB_KB + b) * 4, a.xs + (uint64_t)gt * a.xs_stride + g0 + b);
+    cp_async4(xsc + (b * GB_N + t) * 4, a.xs + (uint64_t)gt * a.xs_stride + g0 + b);
   }
 }
 
@@ -165,21 +171,21 @@ __global__ void __launch_bounds__(GB_THREADS, 2) gemm_q_kernel(GemmArgs a) {
     const uint8_t* wsc = xt + T::X_BYTES;
     const float* xsc = reinterpret_cast<const float*>(wsc + T::WS_BYTES);
     const uint32_t nb = min((uint32_t)GB_KB, G - c * GB_KB);
-    for (uint32_t b = 0; b < nb; ++b) {
+#pragma unroll
+    for (uint32_t b = 0; b < (uint32_t)GB_KB; ++b) {
+      if (b >= nb) break;
       uint32_t af[2][4], bf[4][2];
-      float w0[2], w1[2], x0[4], x1[4];
+      float w0[2], w1[2];
+      float2 xv[4];
 #pragma unroll
       for (int mt = 0; mt < 2; ++mt) {
         const int rr = wm * 32 + mt * 16 + gid;
-        const uint8_t* p = wt + rr * T::WROW + b * T::QB + tig * 4;
+        const int lr = wm * 32 + mt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;  // this lane's ldmatrix row
         if (FMT == FMT_Q8) {
-          af[mt][0] = *reinterpret_cast<const uint32_t*>(p);
-          af[mt][1] = *reinterpret_cast<const uint32_t*>(p + 8 * T::WROW);
-          af[mt][2] = *reinterpret_cast<const uint32_t*>(p + 16);
-          af[mt][3] = *reinterpret_cast<const uint32_t*>(p + 8 * T::WROW + 16);
+          ldsm_x4(af[mt], wt + lr * T::WROW + b * T::QB + (lane >> 4) * 16);
         } else {  // element j: low nibble of byte j, element j + 16: high nibble; value q - 8
-          const uint32_t v0 = *reinterpret_cast<const uint32_t*>(p);
-          const uint32_t v1 = *reinterpret_cast<const uint32_t*>(p + 8 * T::WROW);
+          uint32_t v0, v1;
+          ldsm_x2(v0, v1, wt + lr * T::WROW + b * T::QB);
           af[mt][0] = __vsub4(v0 & 0x0F0F0F0Fu, 0x08080808u);
           af[mt][1] = __vsub4(v1 & 0x0F0F0F0Fu, 0x08080808u);
           af[mt][2] = __vsub4((v0 >> 4) & 0x0F0F0F0Fu, 0x08080808u);
@@ -194,14 +200,18 @@ __global__ void __launch_bounds__(GB_THREADS, 2) gemm_q_kernel(GemmArgs a) {
         }
       }
 #pragma unroll
-      for (int nt = 0; nt < 4; ++nt) {
-        const uint8_t* q = xt + (wn * 32 + nt * 8 + gid) * T::XROW + b * 32 + tig * 4;
-        bf[nt][0] = *reinterpret_cast<const uint32_t*>(q);
-        bf[nt][1] = *reinterpret_cast<const uint32_t*>(q + 16);
-        const int tt = wn * 32 + nt * 8 + tig * 2;
-        x0[nt] = xsc[tt * GB_KB + b];
-        x1[nt] = xsc[(tt + 1) * GB_KB + b];
+      for (int np = 0; np < 2; ++np) {  // n-tiles 2np and 2np + 1
+        const int lt = wn * 32 + np * 16 + (lane & 7) + ((lane >> 4) & 1) * 8;
+        uint32_t r[4];
+        ldsm_x4(r, xt + lt * T::XROW + b * 32 + ((lane >> 3) & 1) * 16);
+        bf[2 * np][0] = r[0];
+        bf[2 * np][1] = r[1];
+        bf[2 * np + 1][0] = r[2];
+        bf[2 * np + 1][1] = r[3];
       }
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt)
+        xv[nt] = *reinterpret_cast<const float2*>(xsc + b * GB_N + wn * 32 + nt * 8 + tig * 2);
 #pragma unroll
       for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
@@ -209,10 +219,10 @@ __global__ void __launch_bounds__(GB_THREADS, 2) gemm_q_kernel(GemmArgs a) {
           int d[4];
           mma_s8(d, af[mt], bf[nt]);
           // ((f32)isum * w_scale) * x_scale, added in group order
-          acc[mt][nt][0] = __fadd_rn(acc[mt][nt][0], __fmul_rn(__fmul_rn(small_i2f(d[0]), w0[mt]), x0[nt]));
-          acc[mt][nt][1] = __fadd_rn(acc[mt][nt][1], __fmul_rn(__fmul_rn(small_i2f(d[1]), w0[mt]), x1[nt]));
-          acc[mt][nt][2] = __fadd_rn(acc[mt][nt][2], __fmul_rn(__fmul_rn(small_i2f(d[2]), w1[mt]), x0[nt]));
-          acc[mt][nt][3] = __fadd_rn(acc[mt][nt][3], __fmul_rn(__fmul_rn(small_i2f(d[3]), w1[mt]), x1[nt]));
+          acc[mt][nt][0] = __fadd_rn(acc[mt][nt][0], __fmul_rn(__fmul_rn(__int2float_rn(d[0]), w0[mt]), xv[nt].x));
+          acc[mt][nt][1] = __fadd_rn(acc[mt][nt][1], __fmul_rn(__fmul_rn(__int2float_rn(d[1]), w0[mt]), xv[nt].y));
+          acc[mt][nt][2] = __fadd_rn(acc[mt][nt][2], __fmul_rn(__fmul_rn(__int2float_rn(d[2]), w1[mt]), xv[nt].x));
+          acc[mt][nt][3] = __fadd_rn(acc[mt][nt][3], __fmul_rn(__fmul_rn(__int2float_rn(d[3]), w1[mt]), xv[nt].y));
         }
     }
   }
