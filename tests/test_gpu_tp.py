@@ -50,16 +50,18 @@ def run_tp(world, path, prompt, feed, n_graph):
 
 
 @pytest.mark.parametrize("fused", ["1", "0"])
-@pytest.mark.parametrize("preset,over", [("tiny", {}), ("tiny", {"hidden_dim": 16384, "vocab_size": 16384})])
-def test_tp2_matches_oracle(yl, orc, model_factory, monkeypatch, preset, over, fused):
+@pytest.mark.parametrize("preset,over,plen", [("tiny", {}, 9), ("tiny", {"hidden_dim": 16384, "vocab_size": 16384}, 9),
+                                              ("tiny", {}, 40)])
+def test_tp2_matches_oracle(yl, orc, model_factory, monkeypatch, preset, over, plen, fused):
     """fused "1": single-token steps exchange through the projections' pushes
     and the next RMSNorm prologue; "0": through the separate exchange kernel
-    (the path multi-token passes always take)."""
+    (the path multi-token passes always take). A 40-token prompt runs the
+    sharded prefill on the tensor-core GEMM."""
     need_gpus(2)
     monkeypatch.setenv("YL_TP_FUSED", fused)  # read by the spawned ranks
     path = model_factory(preset, **over)
     vocab = over.get("vocab_size", yl.PRESETS[preset]["vocab_size"])
-    prompt = yl.prompt_ids(vocab, 9, 1234).tolist()
+    prompt = yl.prompt_ids(vocab, plen, 1234).tolist()
     om = orc.Model(path, 256)
     os_ = om.create_session()
     olg = [om.forward_x(prompt, 0, os_)]
