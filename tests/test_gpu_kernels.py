@@ -294,10 +294,14 @@ def test_matmul_format_mismatch(yl, torch_cuda):
 @pytest.mark.parametrize("hd,nh,nkv,batch,start", [
     (128, 32, 8, 1, 700), (64, 9, 3, 1, 40), (64, 32, 8, 1, 0), (128, 4, 1, 1, 3000),
     (128, 32, 8, 7, 100), (64, 32, 8, 16, 0),
+    (128, 32, 8, 64, 0), (128, 32, 8, 100, 300), (64, 9, 3, 40, 17), (128, 4, 1, 33, 0), (64, 16, 2, 50, 5),
+    (128, 8, 8, 70, 2),
 ])
 def test_fused_attention_vs_oracle(yl, orc, torch_cuda, hd, nh, nkv, batch, start):
     """forward.rs:299-400 through yl_fused_attention (split-sequence partials
-    for single-token calls) against the oracle's restatement."""
+    for single-token calls; 32 or more query rows on the query-blocked kernel:
+    GQA ratios 1, 3, 4 and 8, partial last blocks, key offsets) against the
+    oracle's restatement."""
     rng = np.random.default_rng(hd + nh + batch + start)
     seq = start + batch
     kvd = nkv * hd

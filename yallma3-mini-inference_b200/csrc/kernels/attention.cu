@@ -241,6 +241,7 @@ cudaError_t attention(const AttnArgs& a, const LaunchCfg& lc) {
   if (a.ntok == 0) return cudaSuccess;
   const uint32_t kv_mul = a.n_heads / a.n_kv_heads;
   if (kv_mul > AT_MAXKV || a.n_splits == 0 || a.n_splits > 64) return cudaErrorInvalidValue;
+  if (a.n_splits == 1 && a.ntok >= 32 && attention_prefill_ok(a)) return attention_prefill(a, lc);
   dim3 g(a.n_kv_heads, a.ntok, a.n_splits);
   cudaError_t e;
   if (a.head_size == 64) e = launch_kernel(attn_kernel<64>, g, dim3(AT_THREADS), 0, lc, a);

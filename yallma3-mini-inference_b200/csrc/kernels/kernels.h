@@ -194,6 +194,10 @@ struct AttnArgs {
   float* s8;    // [ntok][n_heads*head_size/32]
 };
 cudaError_t attention(const AttnArgs& a, const LaunchCfg& lc);
+// The query-blocked kernel attention() uses for 32 or more tokens with one
+// split (64 query rows per CTA share every K/V tile).
+bool attention_prefill_ok(const AttnArgs& a);
+cudaError_t attention_prefill(const AttnArgs& a, const LaunchCfg& lc);
 
 // Batch-1 decode attention with RoPE and the KV-cache write fused in:
 // q and the new k/v rows are taken unrotated from `qkv` ([att | k | v]),
