@@ -518,12 +518,27 @@ int yl_forward_x(const yl_model* m, yl_session* sp, const uint32_t* tokens, uint
   } else {
     if ((rc = forward(s, tokens, (uint32_t)n, start_pos, logits_out != nullptr))) return rc;
   }
-  if (logits_out)
-    YL_CUDA_TRY(cudaMemcpyAsync(s->logits_h, s->logits, (uint64_t)sh.vocab_size * 4, cudaMemcpyDeviceToHost, s->stream));
+  // logits straight into a page-locked caller buffer, else through the
+  // session's page-locked staging buffer; the greedy id and the error word
+  // come back with the same synchronization (error word in the last slot of
+  // hist_h, which batch-1 calls never use for ids)
+  bool direct = false;
+  if (logits_out) {
+    cudaPointerAttributes pa{};
+    direct = cudaPointerGetAttributes(&pa, logits_out) == cudaSuccess && pa.type == cudaMemoryTypeHost;
+    cudaGetLastError();
+    YL_CUDA_TRY(cudaMemcpyAsync(direct ? logits_out : s->logits_h, s->logits, (uint64_t)sh.vocab_size * 4,
+                                cudaMemcpyDeviceToHost, s->stream));
+  }
   YL_CUDA_TRY(cudaMemcpyAsync(s->hist_h, s->hist, 4, cudaMemcpyDeviceToHost, s->stream));
+  YL_CUDA_TRY(cudaMemcpyAsync(s->hist_h + sh.ctx_len, s->err, 4, cudaMemcpyDeviceToHost, s->stream));
   YL_CUDA_TRY(cudaStreamSynchronize(s->stream));
-  if ((rc = check_err(s))) return rc;
-  if (logits_out) memcpy(logits_out, s->logits_h, (uint64_t)sh.vocab_size * 4);
+  if (const int herr = (int)s->hist_h[sh.ctx_len]) {
+    cudaMemsetAsync(s->err, 0, sizeof(int), s->stream);
+    cudaStreamSynchronize(s->stream);
+    return fail(YL_ERR_TIMEOUT, "a bounded device wait expired (error word " + std::to_string(herr) + ")");
+  }
+  if (logits_out && !direct) memcpy(logits_out, s->logits_h, (uint64_t)sh.vocab_size * 4);
   if (argmax_out) *argmax_out = s->hist_h[0];
   return YL_OK;
 }
