@@ -1,8 +1,8 @@
-"""Tensor parallelism on two GPUs (one spawned process per GPU): the sharded
+"""Tensor parallelism on two and four GPUs (one spawned process per GPU): the sharded
 forward (all-reduce after wo and down over NVLink peer memory, vocabulary-
 parallel lm_head with the combined greedy id) against the CPU oracle, with
 the same bar as the single-GPU tiny models, and the decode graph against the
-host loop. Skipped where fewer than two GPUs are visible."""
+host loop. Skipped where fewer GPUs than ranks are visible."""
 from __future__ import annotations
 
 import multiprocessing as mp
@@ -75,5 +75,30 @@ def test_tp2_matches_oracle(yl, orc, model_factory, monkeypatch, preset, over, p
     assert max(errs) < bound_for(sens), (errs, sens)
     for k, lg in enumerate(out["logits"]):  # the combined id is the gathered logits' argmax
         assert out["ids"][k] == int(np.argmax(lg))
+    assert_ids_match(out["ids"], oids, olg, bound_for(sens))
+    assert out["dev"] == out["host"]
+
+
+@pytest.mark.parametrize("plen", [9, 40])
+def test_tp4_matches_oracle(yl, orc, model_factory, plen):
+    """Four ranks (4 KV heads, one per rank; feed-forward and vocabulary in
+    quarters): fused decode exchange among four inboxes, the sharded GEMM
+    prefill at 40 tokens, combined greedy id. Skipped on fewer than 4 GPUs."""
+    need_gpus(4)
+    over = {"dim": 512, "n_heads": 8, "n_kv_heads": 4, "hidden_dim": 1024}
+    path = model_factory("tiny", **over)
+    vocab = yl.PRESETS["tiny"]["vocab_size"]
+    prompt = yl.prompt_ids(vocab, plen, 4321).tolist()
+    om = orc.Model(path, 256)
+    os_ = om.create_session()
+    olg = [om.forward_x(prompt, 0, os_)]
+    oids = [orc.argmax(olg[0])]
+    for i in range(12):
+        olg.append(om.forward_x([oids[-1]], len(prompt) + i, os_))
+        oids.append(orc.argmax(olg[-1]))
+    out = run_tp(4, path, prompt, oids[:-1], 16)
+    sens = oracle_sensitivity(orc, path, prompt, oids, 256)
+    errs = [close_logits(g, o) for g, o in zip(out["logits"], olg)]
+    assert max(errs) < bound_for(sens), (errs, sens)
     assert_ids_match(out["ids"], oids, olg, bound_for(sens))
     assert out["dev"] == out["host"]
