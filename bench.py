@@ -280,13 +280,64 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+SWEEP_MK = [(2048, 2048), (8192, 2048), (2048, 8192), (14336, 4096), (4096, 14336), (128256, 4096)]
+SWEEP_N = [1, 4, 16, 64, 512]
+
+
+def sweep_case(yl, torch, rng) -> None:
+    """The matvec / GEMM sweep: (M, K) x {Q8_0, Q4_0, F16} x N tokens through
+    yl_matmul, each launch timed alone with CUDA events after a 256 MB write
+    that evicts L2 (median of 7 after 2 untimed). One JSON line per case:
+    GB/s = (M*K*b_fmt + N*K*(1+4/32) + N*M*4) / t against the measured HBM
+    copy peak, and TOPS = 2*M*K*N / t."""
+    peaks = measured_peaks()
+    hbm = peaks.get("hbm_gbs") if isinstance(peaks, dict) else None
+    flush = torch.empty(64 << 20, dtype=torch.float32, device="cuda")
+    big = max(m * k for m, k in SWEEP_MK)
+    q8 = rng.integers(-127, 128, big, dtype=np.int8)
+    fmts = [("Q8_0", yl.WeightFormat.Q8_0, 34 / 32), ("Q4_0", yl.WeightFormat.Q4_0, 18 / 32),
+            ("F16", yl.WeightFormat.F16, 2.0)]
+    for m, k in SWEEP_MK:
+        for name, f, bf in fmts:
+            w = yl.QuantizedTensor.weight(f, m, k, 32, 1)
+            if name == "F16":
+                w.upload(values=q8[: m * k].astype(np.float32) * np.float32(1e-3))
+            else:
+                wq = q8[: m * k] if name == "Q8_0" else (q8[: m * k] >> 4).astype(np.int8)
+                w.upload(quant_vals=wq, scale_factor=np.full(m * k // 32, 1e-3, np.float32))
+            for n in SWEEP_N:
+                xa = yl.new_workspace_buffer(f, n * k, 32)
+                yl.quantize(f, xa, torch.randn(n * k, device="cuda"), n * k, 32)
+                out = torch.empty(n * m, device="cuda")
+                ts = []
+                for it in range(9):
+                    flush.fill_(float(it))
+                    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+                    ev[0].record()
+                    yl.matmul(out, xa, w, k, m, 32, batch=n, accumulate=False)
+                    ev[1].record()
+                    torch.cuda.synchronize()
+                    if it >= 2:
+                        ts.append(ev[0].elapsed_time(ev[1]) * 1e-3)
+                t = float(np.median(ts))
+                gbs = (m * k * bf + n * k * (1 + 4 / 32) + n * m * 4) / t * 1e-9
+                print(json.dumps({"case": "sweep", "M": m, "K": k, "fmt": name, "N": n, "us": t * 1e6,
+                                  "gbs": gbs, "hbm_frac": gbs / hbm if hbm else None,
+                                  "tops": 2.0 * m * k * n / t * 1e-12,
+                                  "path": "gemm" if n >= 32 and name != "F16" else "matvec"}), flush=True)
+                del xa, out
+            del w
+            torch.cuda.synchronize()
+
+
 def profile_case(case: str) -> None:
     """Small fixed workloads for ncu captures (printed results are not bench
     values). `matvec:ROWSxK`: three batch-1 Q8_0 matvecs of that shape with
     random weights (the bench's dominant kernel at 28672x4096). `gemm:OxKxB`:
     the Q8_0 matmul of B tokens (the tensor-core GEMM from 32 tokens), timed
     over 10 launches with CUDA events after 3 untimed ones. `prefill4`: the
-    4-layer model below, one 512-token prefill. `decode4`: a
+    4-layer model below, one 512-token prefill. `sweep`: the matvec / GEMM
+    sweep (sweep_case). `decode4`: a
     4-layer config-4-shaped model, prompt 8, then 4 decode steps launched
     kernel by kernel (no graph)."""
     import torch
@@ -326,6 +377,9 @@ def profile_case(case: str) -> None:
         print(json.dumps({"case": case, "us_per_launch": us, "tops": 2.0 * o * n * b / us * 1e-6,
                           "weight_gbs": o * n * 34 / 32 / us * 1e-3}))
         return
+    elif case == "sweep":
+        sweep_case(yl, torch, rng)
+        return
     elif case == "prefill4":
         path = os.path.join(os.environ.get("YL_BENCH_DIR", "/tmp"), "yl_c4_4layers.gguf")
         if not os.path.exists(path):
@@ -358,7 +412,7 @@ def main() -> None:
     ap.add_argument("--e2e-steps", type=int, default=128)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-tokens", type=int, default=3)
-    ap.add_argument("--case", default=None, help="profiling workload (matvec:ROWSxK, gemm:ROWSxKxTOKENS, prefill4 or decode4), no bench line")
+    ap.add_argument("--case", default=None, help="profiling workload (matvec:ROWSxK, gemm:ROWSxKxTOKENS, sweep, prefill4 or decode4), no bench line")
     args = ap.parse_args()
     if args.case:
         profile_case(args.case)
