@@ -324,7 +324,7 @@ def sweep_case(yl, torch, rng) -> None:
                 print(json.dumps({"case": "sweep", "M": m, "K": k, "fmt": name, "N": n, "us": t * 1e6,
                                   "gbs": gbs, "hbm_frac": gbs / hbm if hbm else None,
                                   "tops": 2.0 * m * k * n / t * 1e-12,
-                                  "path": "gemm" if n >= 32 and name != "F16" else "matvec"}), flush=True)
+                                  "path": "gemm" if n >= 16 and name != "F16" else "matvec"}), flush=True)
                 del xa, out
             del w
             torch.cuda.synchronize()
@@ -334,7 +334,7 @@ def profile_case(case: str) -> None:
     """Small fixed workloads for ncu captures (printed results are not bench
     values). `matvec:ROWSxK`: three batch-1 Q8_0 matvecs of that shape with
     random weights (the bench's dominant kernel at 28672x4096). `gemm:OxKxB`:
-    the Q8_0 matmul of B tokens (the tensor-core GEMM from 32 tokens), timed
+    the Q8_0 matmul of B tokens (the tensor-core GEMM from 16 tokens), timed
     over 10 launches with CUDA events after 3 untimed ones. `prefill4`: the
     4-layer model below, one 512-token prefill. `sweep`: the matvec / GEMM
     sweep (sweep_case). `decode4`: a

@@ -116,7 +116,7 @@ int yl_quantize(int fmt, yl_qtensor* dst, const float* x, uint64_t n, uint32_t g
  * [batch][o]. accumulate = 1 reproduces the reference's store semantics
  * exactly (columns < 4*floor(o/4) add into out, the rest overwrite,
  * weight_type.rs:243-276); accumulate = 0 overwrites every column. Batches
- * of 32 or more Q8_0 / Q4_0 rows run on the int8 tensor-core GEMM, whose
+ * of 16 or more Q8_0 / Q4_0 rows run on the int8 tensor-core GEMM, whose
  * overwrite results equal the reference's bit for bit; smaller batches run on
  * the matvec (within 1e-5 of the sum of |terms|). */
 int yl_matmul(float* out, const yl_qtensor* x, const yl_qtensor* w, uint64_t n, uint64_t o, uint64_t gs,

@@ -218,7 +218,7 @@ GEMM_CASES = [(260, 576, 33), (1000, 2048, 64), (128, 32, 65), (384, 2080, 130),
 @pytest.mark.parametrize("fmt", ["Q8_0", "Q4_0"])
 @pytest.mark.parametrize("scale_type", [1, 0])
 def test_gemm_bit_exact_vs_oracle(yl, orc, torch_cuda, o, n, batch, fmt, scale_type):
-    """Batches of 32 or more tokens run on the int8 tensor-core GEMM. It folds
+    """Batches of 16 or more tokens run on the int8 tensor-core GEMM. It folds
     each 32-block's exact int32 dot as ((f32)isum * ws) * xs in group order,
     the oracle's sequence (weight_type.rs:190-224), so into a zeroed output the
     results are bit-identical. Cases cover row and token tails, a single

@@ -142,7 +142,7 @@ struct Tunables {
   uint32_t grid_mult = 2;    // matvec CTAs per SM
   bool limbs = true;         // Q8_0 lm_head on three-limb int8 activations
   bool gemm = true;          // multi-token passes on the int8 tensor-core GEMM
-  uint32_t gemm_min = 32;    // from this many tokens (below, the matvec re-reading weights per 8 is faster)
+  uint32_t gemm_min = 16;    // from this many tokens (below, the matvec re-reading weights per 8 is faster)
   bool tp_fused = true;      // tensor-parallel decode: exchange fused into the projections (else exchange kernels)
 };
 const Tunables& tunables();
