@@ -49,7 +49,10 @@ enum yl_weight_format { YL_Q8_0 = 0, YL_Q4_0 = 1, YL_F16 = 2 };
 /* Scale element type of a yl_qtensor. */
 enum yl_scale_type { YL_SCALE_F32 = 0, YL_SCALE_F16 = 1 };
 
-/* Q4_0 decode semantics (see DESIGN.md "Resolved deviations"). */
+/* Q4_0 decode semantics: GGML order (element j is the low nibble of byte j,
+ * element j+16 the high nibble) with value (q - 8) * d. The reference's own
+ * decode (interleaved nibbles, no -8, transformer_llama_gguf.rs:394-405) is
+ * not GGML-conformant and exists only in the oracle as a documented mode. */
 enum yl_q4_mode { YL_Q4_GGML = 0 };
 
 /* RoPE variants: util.rs:653-718 `rope_gguf` (pairs 2k,2k+1) and
