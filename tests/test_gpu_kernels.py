@@ -211,7 +211,8 @@ def test_f32_weight_scales(yl, orc, torch_cuda):
     assert np.all(np.abs(got - ref) <= 1e-5 * term_bound(xq, xs, wq, ws, 2, n, o) + 1e-30)
 
 
-GEMM_CASES = [(260, 576, 33), (1000, 2048, 64), (128, 32, 65), (384, 2080, 130), (2048, 2048, 256)]
+GEMM_CASES = [(260, 576, 17), (1000, 2048, 32), (384, 2080, 20), (260, 576, 33), (1000, 2048, 64), (128, 32, 65),
+              (384, 2080, 130), (2048, 2048, 256)]
 
 
 @pytest.mark.parametrize("o,n,batch", GEMM_CASES)
@@ -221,8 +222,9 @@ def test_gemm_bit_exact_vs_oracle(yl, orc, torch_cuda, o, n, batch, fmt, scale_t
     """Batches of 16 or more tokens run on the int8 tensor-core GEMM. It folds
     each 32-block's exact int32 dot as ((f32)isum * ws) * xs in group order,
     the oracle's sequence (weight_type.rs:190-224), so into a zeroed output the
-    results are bit-identical. Cases cover row and token tails, a single
-    block, an odd block count (f16 scale pairs) and several K stages."""
+    results are bit-identical. Cases cover both token tiles (32 and 64), row
+    and token tails, a single block, an odd block count (f16 scale pairs) and
+    several K stages."""
     rng = np.random.default_rng(o + n + batch)
     f = getattr(yl.WeightFormat, fmt)
     lo, hi = (-127, 128) if fmt == "Q8_0" else (-8, 8)

@@ -8,7 +8,8 @@
 // int8 (q - 8) in registers.
 //
 // Tiles: 128 weight rows x 64 tokens per CTA, 8 warps as 4 (rows) x 2 (tokens),
-// 32 x 32 outputs per warp; K is staged 4 blocks at a time through a 3-stage
+// 32 x 32 outputs per warp (passes of up to 32 tokens: 128 x 32, 16 x 32 per
+// warp); K is staged 4 blocks at a time through a 3-stage
 // cp.async ring (rows padded by 16 bytes: the ldmatrix fragment loads are
 // bank-conflict free). The grid walks token tiles fastest, so the CTAs sharing a weight tile
 // run together and the tile comes from HBM once.
@@ -29,20 +30,22 @@ using namespace yl::dev;
 namespace {
 constexpr int GB_M = 128, GB_N = 64, GB_KB = 4, GB_S = 3, GB_THREADS = 256;
 
-template <int FMT>
+template <int FMT, int BN>
 struct GTile {
   static constexpr int QB = FMT == FMT_Q4 ? 16 : 32;  // weight bytes per 32-block
   static constexpr int WROW = GB_KB * QB + 16;         // padded shared-memory rows
   static constexpr int XROW = GB_KB * 32 + 16;
   static constexpr int W_BYTES = GB_M * WROW;
-  static constexpr int X_BYTES = GB_N * XROW;
+  static constexpr int X_BYTES = BN * XROW;
   static constexpr int WS_BYTES = GB_M * GB_KB * 4;
-  static constexpr int XS_BYTES = GB_N * GB_KB * 4;
+  static constexpr int XS_BYTES = BN * GB_KB * 4;
   static constexpr int STAGE = W_BYTES + X_BYTES + WS_BYTES + XS_BYTES;
   static constexpr int SMEM = GB_S * STAGE;
 };
-static_assert(GTile<FMT_Q8>::STAGE % 16 == 0 && GTile<FMT_Q4>::STAGE % 16 == 0, "stage alignment");
-static_assert(GB_N * GB_M / 2 * 4 <= GTile<FMT_Q4>::SMEM, "SwiGLU staging fits the ring");
+static_assert(GTile<FMT_Q8, 64>::STAGE % 16 == 0 && GTile<FMT_Q4, 64>::STAGE % 16 == 0, "stage alignment");
+static_assert(GTile<FMT_Q8, 32>::STAGE % 16 == 0 && GTile<FMT_Q4, 32>::STAGE % 16 == 0, "stage alignment");
+static_assert(32 * GB_M / 2 * 4 <= GTile<FMT_Q4, 32>::SMEM && GB_N * GB_M / 2 * 4 <= GTile<FMT_Q4, 64>::SMEM,
+              "SwiGLU staging fits the ring");
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
@@ -84,10 +87,10 @@ __device__ __forceinline__ uint32_t tile_row(uint32_t i) {
   return (i & ~15u) + (w >> 1) + ((w & 1u) << 3);
 }
 
-template <int FMT, bool SF16, bool PERM>
+template <int FMT, bool SF16, bool PERM, int BN>
 __device__ __forceinline__ void gemm_load(const GemmArgs& a, uint8_t* st, uint32_t m0, uint32_t n0, uint32_t g0,
                                           uint32_t nb) {
-  using T = GTile<FMT>;
+  using T = GTile<FMT, BN>;
   uint8_t* wt = st;
   uint8_t* xt = wt + T::W_BYTES;
   uint8_t* wsc = xt + T::X_BYTES;
@@ -103,7 +106,7 @@ __device__ __forceinline__ void gemm_load(const GemmArgs& a, uint8_t* st, uint32
                a.wq + (uint64_t)gr * a.row_bytes + (uint64_t)g0 * T::QB + p * 16);
   }
   const uint32_t xp = nb * 2;
-  for (uint32_t i = tid; i < GB_N * xp; i += GB_THREADS) {
+  for (uint32_t i = tid; i < BN * xp; i += GB_THREADS) {
     const uint32_t t = i / xp, p = i - t * xp;
     const uint32_t gt = min(n0 + t, a.ntok - 1);
     cp_async16(xt + t * T::XROW + p * 16, a.xq + (uint64_t)gt * a.x_stride + (uint64_t)g0 * 32 + p * 16);
@@ -123,35 +126,37 @@ __device__ __forceinline__ void gemm_load(const GemmArgs& a, uint8_t* st, uint32
       cp_async4(wsc + (tile_row<PERM>(r) * GB_KB + b) * 4, a.ws + (uint64_t)gr * a.scale_row_bytes + (uint64_t)(g0 + b) * 4);
     }
   }
-  for (uint32_t i = tid; i < GB_N * nb; i += GB_THREADS) {  // stored [block][token]
+  for (uint32_t i = tid; i < BN * nb; i += GB_THREADS) {  // stored [block][token]
     const uint32_t t = i / nb, b = i - t * nb;
     const uint32_t gt = min(n0 + t, a.ntok - 1);
-    cp_async4(xsc + (b * GB_N + t) * 4, a.xs + (uint64_t)gt * a.xs_stride + g0 + b);
+    cp_async4(xsc + (b * BN + t) * 4, a.xs + (uint64_t)gt * a.xs_stride + g0 + b);
   }
 }
 
-template <int FMT, bool SF16, int EPI>
+template <int FMT, bool SF16, int EPI, int BN>
 __global__ void __launch_bounds__(GB_THREADS, 2) gemm_q_kernel(GemmArgs a) {
-  using T = GTile<FMT>;
+  using T = GTile<FMT, BN>;
   constexpr bool PERM = EPI == EPI_SWIGLU_Q8;
+  // BN = 64: warps 4 (rows) x 2 (tokens), 32 x 32 each; BN = 32: 8 x 1, 16 x 32
+  constexpr int WN = BN / 32, MT = BN / 32, RW = 16 * MT;
   extern __shared__ __align__(128) uint8_t smem[];
-  const uint32_t n0 = blockIdx.x * GB_N, m0 = blockIdx.y * GB_M;
+  const uint32_t n0 = blockIdx.x * BN, m0 = blockIdx.y * GB_M;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int gid = lane >> 2, tig = lane & 3;
-  const int wm = warp & 3, wn = warp >> 2;
+  const int wm = warp % (8 / WN), wn = warp / (8 / WN);
   const uint32_t G = a.K / 32, nch = (G + GB_KB - 1) / GB_KB;
 
   grid_dep_wait();  // activations come from the preceding kernel
 #pragma unroll
   for (int s = 0; s < GB_S - 1; ++s) {
     if ((uint32_t)s < nch)
-      gemm_load<FMT, SF16, PERM>(a, smem + s * T::STAGE, m0, n0, s * GB_KB, min((uint32_t)GB_KB, G - s * GB_KB));
+      gemm_load<FMT, SF16, PERM, BN>(a, smem + s * T::STAGE, m0, n0, s * GB_KB, min((uint32_t)GB_KB, G - s * GB_KB));
     cp_async_commit();
   }
 
-  float acc[2][4][4];
+  float acc[MT][4][4];
 #pragma unroll
-  for (int i = 0; i < 2; ++i)
+  for (int i = 0; i < MT; ++i)
 #pragma unroll
     for (int j = 0; j < 4; ++j)
 #pragma unroll
@@ -162,7 +167,7 @@ __global__ void __launch_bounds__(GB_THREADS, 2) gemm_q_kernel(GemmArgs a) {
     __syncthreads();  // stage c landed for every thread; stage c-1 is free
     const uint32_t cn = c + GB_S - 1;
     if (cn < nch)
-      gemm_load<FMT, SF16, PERM>(a, smem + (cn % GB_S) * T::STAGE, m0, n0, cn * GB_KB,
+      gemm_load<FMT, SF16, PERM, BN>(a, smem + (cn % GB_S) * T::STAGE, m0, n0, cn * GB_KB,
                                  min((uint32_t)GB_KB, G - cn * GB_KB));
     cp_async_commit();
 
@@ -174,13 +179,13 @@ __global__ void __launch_bounds__(GB_THREADS, 2) gemm_q_kernel(GemmArgs a) {
 #pragma unroll
     for (uint32_t b = 0; b < (uint32_t)GB_KB; ++b) {
       if (b >= nb) break;
-      uint32_t af[2][4], bf[4][2];
-      float w0[2], w1[2];
+      uint32_t af[MT][4], bf[4][2];
+      float w0[MT], w1[MT];
       float2 xv[4];
 #pragma unroll
-      for (int mt = 0; mt < 2; ++mt) {
-        const int rr = wm * 32 + mt * 16 + gid;
-        const int lr = wm * 32 + mt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;  // this lane's ldmatrix row
+      for (int mt = 0; mt < MT; ++mt) {
+        const int rr = wm * RW + mt * 16 + gid;
+        const int lr = wm * RW + mt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;  // this lane's ldmatrix row
         if (FMT == FMT_Q8) {
           ldsm_x4(af[mt], wt + lr * T::WROW + b * T::QB + (lane >> 4) * 16);
         } else {  // element j: low nibble of byte j, element j + 16: high nibble; value q - 8
@@ -211,9 +216,9 @@ __global__ void __launch_bounds__(GB_THREADS, 2) gemm_q_kernel(GemmArgs a) {
       }
 #pragma unroll
       for (int nt = 0; nt < 4; ++nt)
-        xv[nt] = *reinterpret_cast<const float2*>(xsc + b * GB_N + wn * 32 + nt * 8 + tig * 2);
+        xv[nt] = *reinterpret_cast<const float2*>(xsc + b * BN + wn * 32 + nt * 8 + tig * 2);
 #pragma unroll
-      for (int mt = 0; mt < 2; ++mt)
+      for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
         for (int nt = 0; nt < 4; ++nt) {
           int d[4];
@@ -232,17 +237,17 @@ __global__ void __launch_bounds__(GB_THREADS, 2) gemm_q_kernel(GemmArgs a) {
     __syncthreads();  // the ring is free: it now stages h [64 tokens][64 pairs]
     float* hb = reinterpret_cast<float*>(smem);
 #pragma unroll
-    for (int mt = 0; mt < 2; ++mt)
+    for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
       for (int nt = 0; nt < 4; ++nt) {
-        const int jl = wm * 16 + mt * 8 + gid;  // pair of this thread's rows gid (gate) and gid + 8 (up)
+        const int jl = (wm * RW + mt * 16) / 2 + gid;  // pair of this thread's rows gid (gate) and gid + 8 (up)
         const int tl = wn * 32 + nt * 8 + tig * 2;
         hb[tl * (GB_M / 2) + jl] = silu_mul(acc[mt][nt][0], acc[mt][nt][2]);
         hb[(tl + 1) * (GB_M / 2) + jl] = silu_mul(acc[mt][nt][1], acc[mt][nt][3]);
       }
     __syncthreads();
     const uint32_t f = a.rows / 2;
-    for (int pi = warp; pi < GB_N * 2; pi += GB_THREADS / 32) {
+    for (int pi = warp; pi < BN * 2; pi += GB_THREADS / 32) {
       const int tl = pi >> 1, blk = pi & 1;
       const uint32_t t = n0 + tl;
       if (t >= a.ntok) continue;  // warp-uniform
@@ -258,12 +263,12 @@ __global__ void __launch_bounds__(GB_THREADS, 2) gemm_q_kernel(GemmArgs a) {
   }
 
 #pragma unroll
-  for (int mt = 0; mt < 2; ++mt)
+  for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
     for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const uint32_t r = m0 + wm * 32 + mt * 16 + gid + (e >> 1) * 8;
+        const uint32_t r = m0 + wm * RW + mt * 16 + gid + (e >> 1) * 8;
         const uint32_t t = n0 + wn * 32 + nt * 8 + tig * 2 + (e & 1);
         if (r >= a.rows || t >= a.ntok) continue;
         float* o = a.out + (uint64_t)t * a.out_stride + r;
@@ -274,14 +279,20 @@ __global__ void __launch_bounds__(GB_THREADS, 2) gemm_q_kernel(GemmArgs a) {
       }
 }
 
+template <int FMT, bool SF16, int EPI, int BN>
+cudaError_t gemm_launch_bn(const GemmArgs& a, const LaunchCfg& lc) {
+  using T = GTile<FMT, BN>;
+  cudaError_t e =
+      cudaFuncSetAttribute(gemm_q_kernel<FMT, SF16, EPI, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, T::SMEM);
+  if (e != cudaSuccess) return e;
+  const dim3 grid((a.ntok + BN - 1) / BN, (a.rows + GB_M - 1) / GB_M);
+  return launch_kernel(gemm_q_kernel<FMT, SF16, EPI, BN>, grid, dim3(GB_THREADS), (uint32_t)T::SMEM, lc, a);
+}
+
+// Up to 32 tokens: 32-token tiles (half the padded work of a 64-token tile).
 template <int FMT, bool SF16, int EPI>
 cudaError_t gemm_launch(const GemmArgs& a, const LaunchCfg& lc) {
-  using T = GTile<FMT>;
-  cudaError_t e =
-      cudaFuncSetAttribute(gemm_q_kernel<FMT, SF16, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, T::SMEM);
-  if (e != cudaSuccess) return e;
-  const dim3 grid((a.ntok + GB_N - 1) / GB_N, (a.rows + GB_M - 1) / GB_M);
-  return launch_kernel(gemm_q_kernel<FMT, SF16, EPI>, grid, dim3(GB_THREADS), (uint32_t)T::SMEM, lc, a);
+  return a.ntok <= 32 ? gemm_launch_bn<FMT, SF16, EPI, 32>(a, lc) : gemm_launch_bn<FMT, SF16, EPI, 64>(a, lc);
 }
 
 template <int FMT, bool SF16>
