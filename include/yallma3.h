@@ -248,7 +248,9 @@ int yl_forward_x(const yl_model* m, yl_session* s, const uint32_t* tokens, uint6
  * enqueueing when sync == 0 (tokens_out must then be NULL). */
 int yl_decode_greedy(const yl_model* m, yl_session* s, uint32_t first_token, uint32_t start_pos,
                      uint32_t n_steps, uint32_t* tokens_out, void* stream, int sync);
-/* Number of kernel launches one batch-1 decode step issues. */
+/* Number of kernel launches one batch-1 decode step issues (the decode
+ * graph's kernels: 5 per layer + 2, + 1 with tensor parallelism, + 2 per layer
+ * more when the tensor-parallel exchange runs as separate kernels). */
 int yl_decode_step_launches(const yl_model* m, uint32_t* out);
 /* Diagnostic: runs one batch-1 decode step of `token` at `pos` launch by
  * launch (no graph, no programmatic dependent launch) with CUDA events

@@ -572,12 +572,14 @@ int yl_decode_greedy(const yl_model* m, yl_session* sp, uint32_t first_token, ui
 
 int yl_decode_step_launches(const yl_model* m, uint32_t* out) {
   if (!m || !out) return fail(YL_ERR_ARG, "null argument");
-  const yl_shape& s = m->m->shape;
-  // per layer: norm, qkv, rope, attention (+combine), wo, norm, w13, quant (Q formats), w2
-  const uint32_t per_layer = 8 + (s.weight_format == YL_F16 ? 0 : 1);
-  uint32_t ns = (2 * (uint32_t)m->m->num_sms + s.n_kv_heads - 1) / s.n_kv_heads;
-  ns = std::max(1u, std::min(64u, ns));
-  *out = 1 + s.n_layers * (per_layer + (ns > 1 ? 1 : 0)) + 3;
+  const uint32_t L = m->m->shape.n_layers;
+  // embedding; per layer qkv (+ RMSNorm prologue), decode attention (RoPE,
+  // cache write, merge, quantize), wo, gate/up (+ RMSNorm, SwiGLU, quantize),
+  // down; lm_head (+ RMSNorm, argmax). Tensor parallel: the winners' combine,
+  // and two exchange kernels per layer unless the exchange is fused.
+  uint32_t n = 1 + 5 * L + 1;
+  if (m->m->tp_size > 1) n += 1 + (tunables().tp_fused ? 0 : 2 * L);
+  *out = n;
   return YL_OK;
 }
 
