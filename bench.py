@@ -1,4 +1,4 @@
-"""Decode benchmark: Llama-3-8B-shaped Q8_0, batch 1.
+"""Decode benchmark: Llama-3-8B-shaped Q8_0, batch 1 (benchmark configuration 4).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
@@ -18,11 +18,14 @@ timed steps continue the sequence from position 512.
          alone with CUDA events, cycling through the 32 layers' weights so no
          launch reuses L2; algorithmic bytes / duration vs measured HBM peak.
   cpu_baseline  the CPU oracle (C++ restatement of the reference CPU path) on
-         a bounded sample of the same decode, all host cores.
+         a bounded sample of the same decode, on all host cores and on the
+         reference's default thread count (half the cores, rounded up,
+         parallelism.rs:59-71), with the CPU model recorded.
 
-With N > 1 (torchrun), each rank runs an independent replica of the batch-1
-decode on its own GPU (no data-path collective); value = all ranks' tokens /
-max time.
+With N > 1 (torchrun), the model is tensor-parallel over the N GPUs (Megatron
+split: heads and ffn rows by rank, wo / down along their inputs, lm_head by
+vocabulary rows; partial sums exchanged over NVLink peer memory). There is one
+token stream, so value = tokens / max time over ranks (strong scaling).
 """
 from __future__ import annotations
 
@@ -225,11 +228,22 @@ def time_dominant_matvec(yl, torch, model, cfg: dict, iters: int, world: int = 1
     return {"ms": ms, "bytes": nbytes, "gbs": nbytes / (ms * 1e-3) / 1e9}
 
 
-def cpu_baseline(path: str, cfg: dict, n_tokens: int, threads: int) -> dict:
-    """Oracle decode of n_tokens at positions 512.. with a seeded KV prefix."""
+def cpu_model() -> str:
+    try:
+        for ln in Path("/proc/cpuinfo").read_text().splitlines():
+            if ln.startswith("model name"):
+                return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def cpu_baseline(path: str, n_tokens: int, threads: int, half_threads: int | None = None) -> dict:
+    """Oracle decode of n_tokens at positions 512.. with a seeded KV prefix,
+    on `threads` host threads; with half_threads also on that many (the
+    reference's default pool, parallelism.rs:59-71)."""
     sys.path.insert(0, str(ROOT / "oracle"))
     import pyoracle as orc
-    orc.set_threads(threads)
     t0 = time.time()
     m = orc.Model(path, 4096)
     load_s = time.time() - t0
@@ -242,33 +256,49 @@ def cpu_baseline(path: str, cfg: dict, n_tokens: int, threads: int) -> dict:
         base = layer * sh.ctx_len * kvd
         k[base:base + PROMPT_LEN * kvd] = rng.standard_normal(PROMPT_LEN * kvd).astype(np.float32)
         v[base:base + PROMPT_LEN * kvd] = rng.standard_normal(PROMPT_LEN * kvd).astype(np.float32)
-    tok = 1
-    m.forward_x([tok], PROMPT_LEN, s)  # warm-up (page-in)
-    t = time.perf_counter()
-    for i in range(n_tokens):
-        lg = m.forward_x([tok], PROMPT_LEN + 1 + i, s)
-        tok = orc.argmax(lg)
-    dt = time.perf_counter() - t
-    return {"value": n_tokens / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
-            "sample": f"{n_tokens} batch-1 decode tokens of config 4 at positions {PROMPT_LEN + 1}.. "
-                      f"(KV prefix 0..{PROMPT_LEN - 1} seeded instead of a CPU prefill), "
-                      f"oracle load {load_s:.0f}s untimed"}
+
+    def timed(nt: int) -> float:
+        orc.set_threads(nt)
+        tok = 1
+        m.forward_x([tok], PROMPT_LEN, s)  # warm-up (page-in)
+        t = time.perf_counter()
+        for i in range(n_tokens):
+            lg = m.forward_x([tok], PROMPT_LEN + 1 + i, s)
+            tok = orc.argmax(lg)
+        return n_tokens / (time.perf_counter() - t)
+
+    out = {"value": timed(threads), "unit": "tokens/s", "cores": threads, "kind": "port",
+           "cpu_model": cpu_model(), "host_cores": os.cpu_count(),
+           "sample": f"{n_tokens} batch-1 decode tokens of config 4 at positions {PROMPT_LEN + 1}.. "
+                     f"(KV prefix 0..{PROMPT_LEN - 1} seeded instead of a CPU prefill), "
+                     f"oracle load {load_s:.0f}s untimed"}
+    if half_threads and half_threads != threads:
+        out["reference_default_threads"] = {"cores": half_threads, "value": timed(half_threads),
+                                            "rule": "ceil(0.5 * cores), parallelism.rs:59-71"}
+    return out
+
+
+def write_model_in_subprocess(path: Path) -> None:
+    """Writes the config-4 GGUF from a child process, so the process that times
+    the reference arm never loads this repository's CUDA library."""
+    if path.with_suffix(".ok").exists():
+        return
+    code = (f"import sys, importlib; sys.path.insert(0, {str(ROOT)!r}); "
+            f"yl = importlib.import_module({PKG!r}); yl.synth_preset({CONFIG!r}, {str(path)!r})")
+    subprocess.run([sys.executable, "-c", code], check=True)
+    path.with_suffix(".ok").write_text("ok")
 
 
 def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    yl = importlib.import_module(PKG)
-    cfg = yl.PRESETS[CONFIG]
     cache = Path(os.environ.get("YL_BENCH_DIR", tempfile.gettempdir()))
     path = cache / "yl_bench_c4_q8_0.gguf"
-    if not path.with_suffix(".ok").exists():
-        yl.synth_preset(CONFIG, str(path))
-        path.with_suffix(".ok").write_text("ok")
+    write_model_in_subprocess(path)
     steps = max(1, min(args.steps, 8))
     threads = os.cpu_count() or 1
-    cb = cpu_baseline(str(path), cfg, steps, threads)
+    cb = cpu_baseline(str(path), steps, threads, half_threads=max(1, -(-threads // 2)))
     line = {"impl": "reference", "metric": "decode tokens/s (Llama-3-8B-shape Q8_0, batch 1)",
             "value": cb["value"], "unit": "tokens/s", "n_gpus": args.gpus, "steps": steps, "warmup": 1,
             "ms_per_step": 1000.0 / cb["value"], "higher_is_better": True, "scaling": "weak",
@@ -516,8 +546,8 @@ def main() -> None:
         "roofline": {"bound": "hbm", "kernel": f"mv_kernel<Q8,NT=1> gate/up {2 * cfg['hidden_dim'] // world}x4096",
                      "achieved": mv["gbs"], "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": mv["gbs"] / peaks["hbm_gbs"], "peak_src": peaks["src"],
-                     # DRAM read + write bytes of one launch of this kernel and shape from
-                     # one ncu capture (profiles/mv_kernel_gateup_28672x4096.md)
+                     # DRAM read + write bytes of one launch of this kernel and shape,
+                     # from one ncu capture of `bench.py --case matvec:28672x4096`
                      "traffic": TRAFFIC_GATEUP_BYTES if world == 1 else None, "traffic_unit": "bytes per launch",
                      "algorithmic_bytes": mv["bytes"], "launch_ms": mv["ms"]},
         # per GPU: each rank streams its shard (1/N of the weights) per token
@@ -532,7 +562,8 @@ def main() -> None:
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         del model, sess
         torch.cuda.empty_cache()
-        line["cpu_baseline"] = cpu_baseline(path, cfg, args.cpu_tokens, os.cpu_count() or 1)
+        nc = os.cpu_count() or 1
+        line["cpu_baseline"] = cpu_baseline(path, args.cpu_tokens, nc, half_threads=max(1, -(-nc // 2)))
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

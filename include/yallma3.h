@@ -34,7 +34,7 @@ enum yl_status {
   YL_ERR_ARG = -1,         /* bad argument (null pointer, size, range) */
   YL_ERR_IO = -2,          /* file cannot be opened / read */
   YL_ERR_FORMAT = -3,      /* malformed file, or format/variant mismatch
-                              (the reference panics: weight_type.rs:141,157) */
+                              (the reference panics: weight_type.rs:88,104) */
   YL_ERR_CUDA = -4,        /* CUDA runtime error */
   YL_ERR_OOM = -5,         /* device allocation failed */
   YL_ERR_RANGE = -6,       /* position beyond the session's ctx_len */
@@ -43,7 +43,7 @@ enum yl_status {
   YL_ERR_COMM = -9         /* tensor-parallel communicator error */
 };
 
-/* WeightFormat (weight_type.rs:70-75). */
+/* WeightFormat (weight_type.rs:17-22). */
 enum yl_weight_format { YL_Q8_0 = 0, YL_Q4_0 = 1, YL_F16 = 2 };
 
 /* Scale element type of a yl_qtensor. */
@@ -63,7 +63,7 @@ const char* yl_last_error(void);
 /* Library version string, e.g. "yallma3_b200 0.1 sm_100a". */
 const char* yl_version(void);
 
-/* ---- quantized tensors (weight_type.rs:77-120, quantization.rs:23-27) ----
+/* ---- quantized tensors (weight_type.rs:24-50, quantization.rs:23-27) -----
  *
  * Two kinds share one struct:
  *  - activation tensors (rows == 0): the reference's flat containers.
@@ -91,7 +91,7 @@ typedef struct yl_qtensor {
   int32_t _pad;
 } yl_qtensor;
 
-/* new_workspace_buffer (weight_type.rs:161-173): zeroed activation tensor. */
+/* new_workspace_buffer (weight_type.rs:108-120): zeroed activation tensor. */
 int yl_qtensor_alloc(int fmt, uint64_t len, uint64_t gs, yl_qtensor* out);
 /* Weight tensor [rows][cols] in the repacked layout (zeroed). */
 int yl_qtensor_alloc_weight(int fmt, int scale_type, uint64_t rows, uint64_t cols, uint64_t gs,
@@ -111,14 +111,15 @@ int yl_qtensor_download(const yl_qtensor* t, int8_t* q, float* scales, float* va
  * q = round-half-away(x/scale) saturated to int8, NaN -> 0. Bit-exact with the
  * reference. x, q, scale are device pointers; floor(n/gs) groups are written. */
 int yl_quantize_q8_0(const float* x, int8_t* q, float* scale, uint64_t n, uint32_t gs, void* stream);
-/* weight_type.rs:129-143 `quantize(fmt, dst, x, n, gs)`: format dispatch into
+/* weight_type.rs:76-90 `quantize(fmt, dst, x, n, gs)`: format dispatch into
  * an activation tensor (YL_ERR_FORMAT on a variant mismatch). */
 int yl_quantize(int fmt, yl_qtensor* dst, const float* x, uint64_t n, uint32_t gs, void* stream);
-/* weight_type.rs:145-159 `matmul(out, x, w, n, o, gs)` with the batch made
+/* weight_type.rs:92-106 `matmul(out, x, w, n, o, gs)` with the batch made
  * explicit (the reference infers it as out.len()/o). out: device f32
  * [batch][o]. accumulate = 1 reproduces the reference's store semantics
  * exactly (columns < 4*floor(o/4) add into out, the rest overwrite,
- * weight_type.rs:243-276); accumulate = 0 overwrites every column. Batches
+ * weight_type.rs:190-201 and :207-224, inside matmul_q8_slices :122-226);
+ * accumulate = 0 overwrites every column. Batches
  * of 16 or more Q8_0 / Q4_0 rows run on the int8 tensor-core GEMM, whose
  * overwrite results equal the reference's bit for bit; smaller batches run on
  * the matvec (within 1e-5 of the sum of |terms|). */
@@ -148,10 +149,12 @@ int yl_fused_attention(float* output, const float* sq, const float* key_cache, c
  * a fixed device array of YL_ATTN_STATIC_BYTES (1 MiB) that every GPU loading
  * this library holds until the process exits. A call whose partials would not
  * fit (n_heads * splits * (head_size + 2) * 4 bytes) fails with
- * YL_ERR_UNSUPPORTED. The first call on a device resolves the array's device
- * address (cudaGetSymbolAddress), so make that first call before any stream
- * capture. All calls share the array: calls that overlap on the GPU (other
- * streams, other threads) race on it; serialize them. */
+ * YL_ERR_UNSUPPORTED. Every call resolves the array's device address on the
+ * current device (cudaGetSymbolAddress, which allocates nothing), so calls
+ * after a cudaDeviceReset find the reloaded array; the first call on a device
+ * also loads this library's kernels there, so make that first call before
+ * any stream capture. All calls share the array: calls that overlap on the
+ * GPU (other streams, other threads) race on it; serialize them. */
 #define YL_ATTN_STATIC_BYTES (1u << 20)
 int yl_fused_attention_static(float* output, const float* sq, const float* key_cache, const float* value_cache,
                               uint64_t seq_len, uint64_t batch, uint64_t n_heads, uint64_t n_kv_heads,
@@ -252,6 +255,21 @@ int yl_decode_greedy(const yl_model* m, yl_session* s, uint32_t first_token, uin
  * graph's kernels: 5 per layer + 2, + 1 with tensor parallelism, + 2 per layer
  * more when the tensor-parallel exchange runs as separate kernels). */
 int yl_decode_step_launches(const yl_model* m, uint32_t* out);
+/* The decode step's attention kernel on its own, with the model's RoPE table,
+ * head layout and attention scale (no reference counterpart as one function:
+ * it fuses the batch-1 RoPE of q/k and the cache write of forward.rs:154-175
+ * with fused_attention, forward.rs:299-400). qkv: device [q (heads*hd) | k |
+ * v] of one token, unrotated; key_cache/value_cache: device [>= pos+1][kv_dim]
+ * (one layer); the new k/v rows are rotated and written at `pos`, then the
+ * token attends to positions 0..pos. out: f32 [heads*hd] and/or out_q/out_s:
+ * its Q8_0 blocks (either may be NULL, not both). */
+int yl_model_attention_decode(const yl_model* m, const float* qkv, float* key_cache, float* value_cache, uint32_t pos,
+                              float* out, int8_t* out_q, float* out_s, void* stream);
+/* Diagnostic (no reference counterpart): the kernel nodes of this session's
+ * captured decode graph, counted in the graph itself (builds the graph if
+ * needed; with_logits selects the tensor-parallel graph that also gathers
+ * the logits). Equals yl_decode_step_launches for the graph without logits. */
+int yl_session_decode_graph_launches(yl_session* s, int with_logits, uint32_t* out);
 /* Diagnostic: runs one batch-1 decode step of `token` at `pos` launch by
  * launch (no graph, no programmatic dependent launch) with CUDA events
  * between launches, and writes each launch's device time in microseconds to

@@ -115,7 +115,7 @@ void orc_quantize_q8(int8_t* q, float* scale_out, const float* x, size_t n, uint
   }
 }
 
-/* weight_type.rs:105-127 (`q4_0_quantize`, the reference's +-7 quantizer) */
+/* weight_type.rs:52-74 (`q4_0_quantize`, the reference's +-7 quantizer) */
 void orc_quantize_q4_ref(int8_t* q, float* scale_out, const float* x, size_t n, uint32_t gs) {
   uint32_t num_groups = (uint32_t)n / gs;
   const float q_max = 7.0f;
@@ -135,10 +135,10 @@ void orc_quantize_q4_ref(int8_t* q, float* scale_out, const float* x, size_t n, 
   }
 }
 
-/* weight_type.rs:176-279 (`matmul_q8_slices`). Quirks kept: quad columns use
- * `+=` into out (:243-254), remainder columns use `=` (:276); the quad path
- * only sees floor(remaining/8)*8 elements of a group (:201, no scalar tail);
- * batch rows = out_len / o (par_chunks_exact_mut). */
+/* weight_type.rs:122-226 (`matmul_q8_slices`). Quirks kept: quad columns use
+ * `+=` into out (:190-201), remainder columns use `=` (:207-224); the quad path
+ * only sees floor(remaining/8)*8 elements of a group (:147-155, no scalar
+ * tail); batch rows = out_len / o (par_chunks_exact_mut, :135). */
 void orc_matmul_q8_slices(float* xout, size_t out_len, const int8_t* x, const float* x_scale,
                           const int8_t* w, const float* w_scale, size_t n, size_t o, size_t gs) {
   if (o == 0) return;
@@ -192,7 +192,7 @@ void orc_matmul_q8_slices(float* xout, size_t out_len, const int8_t* x, const fl
   }
 }
 
-/* weight_type.rs:281-323 (`matmul_f32`): sequential f32 sums, `=` semantics. */
+/* weight_type.rs:228-270 (`matmul_f32`): sequential f32 sums, `=` semantics. */
 void orc_matmul_f32(float* xout, size_t out_len, const float* x, const float* w, size_t n, size_t o) {
   if (o == 0) return;
   size_t rows = out_len / o;
@@ -225,7 +225,7 @@ void orc_matmul_f32(float* xout, size_t out_len, const float* x, const float* w,
   }
 }
 
-/* Per-block int32 dot products Σ x_q·w_q of weight_type.rs:208-241 (the value
+/* Per-block int32 dot products Σ x_q·w_q of weight_type.rs:150-201 (the value
  * of `ival.reduce_add()`), laid out [batch][o][n/gs]. Checker for the
  * bit-exactness of the device block dots. */
 void orc_block_dots(int32_t* out, const int8_t* x, const int8_t* w, size_t batch, size_t n, size_t o,
@@ -450,7 +450,7 @@ uint32_t orc_argmax(const float* p, size_t n) {
 /* ======================= GGUF loader + model ============================== */
 namespace {
 
-struct QT { /* QuantizedTensor (weight_type.rs:83-88) */
+struct QT { /* QuantizedTensor (weight_type.rs:30-36) */
   std::vector<int8_t> q;
   std::vector<float> s;
   std::vector<float> f; /* F16 variant, stored as f32 */

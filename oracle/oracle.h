@@ -28,7 +28,8 @@ extern "C" {
 enum { ORC_Q8_0 = 0, ORC_Q4_0 = 1, ORC_F16 = 2 };
 
 /* Q4_0 decoding modes. GGML: element j = low nibble of byte j, element j+16 =
- * high nibble, value (q-8)*d, Q8_0 activations (the BASELINE semantics).
+ * high nibble, value (q-8)*d, Q8_0 activations (the GGML semantics the
+ * benchmark configurations define).
  * REF: the literal reference decode (transformer_llama_gguf.rs:394-405: lo->2j,
  * hi->2j+1, no -8) with the +-7 activation quantizer (weight_type.rs:52-74). */
 enum { ORC_Q4_GGML = 0, ORC_Q4_REF = 1 };

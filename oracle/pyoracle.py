@@ -167,6 +167,17 @@ def fused_attention(sq, key_cache, value_cache, seq_len: int, batch: int, n_head
     return out
 
 
+def rope(shape: "OrcShape", sq: np.ndarray, k: np.ndarray, pos: int):
+    """The model's RoPE of one token's q [heads*hd] and k [kv_heads*hd] at
+    `pos` (util.rs:589-635 `rope` for llama3 scaling, else util.rs:653-718
+    `rope_gguf`), as forward.rs:154-175 applies it. Returns rotated copies."""
+    q = np.array(sq, np.float32, copy=True)
+    kk = np.array(k, np.float32, copy=True)
+    fn = lib().orc_rope if shape.rope_mode == 1 else lib().orc_rope_gguf
+    fn(C.byref(shape), _p(q), _p(kk), pos)
+    return q, kk
+
+
 def argmax(p: np.ndarray) -> int:
     p = np.ascontiguousarray(p, np.float32)
     return int(lib().orc_argmax(_p(p), p.size))

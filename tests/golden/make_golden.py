@@ -5,7 +5,7 @@ quantized matmul, from an independent numpy restatement of the reference
 Restated here:
   * quantization.rs:29-52  `quantize`: absmax/127 f32 scale, IEEE x/scale,
     round half away from zero, Rust `as i8` (saturating, NaN -> 0);
-  * weight_type.rs:176-279 `matmul_q8_slices`: per output column, groups
+  * weight_type.rs:122-226 `matmul_q8_slices`: per output column, groups
     folded in order as out += ((f32)isum * w_scale) * x_scale; the first
     4*floor(o/4) columns add into `out`, the rest overwrite it; the quad path
     sees floor(remaining/8)*8 elements of a group;

@@ -1,8 +1,14 @@
 """GPU parity of the full forward (Transformer::forward_x) against the CPU
-oracle on seeded synthetic GGUF models.
+oracle on small seeded synthetic GGUF models (two layers, narrow shapes).
 
-Bar: logits within 1e-2 * max|logit| of the oracle at
-every step; greedy token ids identical over the whole run."""
+Bar: logits within 1e-2 * max|logit| of the oracle at every step; greedy
+token ids identical over the whole run. These narrow test models can be more
+sensitive to single activation-quantization flips than the bar allows, so two
+documented allowances exist here, and each prints a `RELAXED` line when it is
+used: the logit bar becomes twice the oracle's own one-ulp sensitivity when
+that sensitivity is already within a factor 2 of 1e-2, and an id may differ at
+a step whose oracle top-2 margin is inside the bar. The benchmark
+configurations (tests/test_gpu_configs.py) use no allowance."""
 from __future__ import annotations
 
 import numpy as np
@@ -57,6 +63,8 @@ def assert_ids_match(gids, oids, olg, bound):
         lo = olg[k]
         margin = float(lo[oids[k]] - lo[gids[k]]) / float(np.max(np.abs(lo)))
         assert 0.0 <= margin <= bound, (k, oids[k], gids[k], margin, bound)
+        print(f"RELAXED near-tie id difference at step {k}: oracle {oids[k]}, device {gids[k]}, "
+              f"margin {margin:.3e} <= bound {bound:.3e}", flush=True)
     assert len(flips) <= max(1, len(oids) // 32), flips
     return flips
 
@@ -84,7 +92,10 @@ def oracle_sensitivity(orc, path, prompt, ids, max_ctx) -> float:
 def bound_for(sens: float) -> float:
     """The 1e-2 bar, unless the test model's own one-ulp sensitivity is
     already within a factor 2 of it (then twice the sensitivity)."""
-    return LOGIT_TOL if sens < LOGIT_TOL / 2 else 2.0 * sens
+    if sens < LOGIT_TOL / 2:
+        return LOGIT_TOL
+    print(f"RELAXED logit bound {2.0 * sens:.3e} (oracle one-ulp sensitivity {sens:.3e})", flush=True)
+    return 2.0 * sens
 
 
 @pytest.mark.parametrize("preset,over", [
@@ -203,27 +214,6 @@ def test_prefill_equals_stepwise_on_device(yl, model_factory):
     for i, t in enumerate(toks):
         b, _ = gm.forward_x_full([t], i, s)
     assert close_logits(a, b) < 1e-4
-
-
-def test_c1_smollm_shape_128_steps(yl, orc, model_factory):
-    """SmolLM2-135M shape, Q8_0, seed 0, prompt of 16 random
-    ids, 128 greedy steps, max_ctx 512."""
-    path = model_factory("c1")
-    prompt = yl.prompt_ids(49152, 16, 1000).tolist()
-    errs, gids, oids, _, _ = run_pair(yl, orc, path, prompt, 128, 512)
-    olg = run_pair.oracle_logits
-    sens = oracle_sensitivity(orc, path, prompt, oids, 512)
-    assert max(errs) < bound_for(sens), (max(errs), sens)
-    flips = assert_ids_match(gids, oids, olg, bound_for(sens))
-    # free-running device decode (its own ids fed back) follows the oracle's
-    # sequence up to the first near-tie
-    gm = yl.load_transformer(path, max_ctx_len=512)
-    s = gm.create_session()
-    _, first = gm.forward_x_full(prompt, 0, s, want_logits=False)
-    assert first == gids[0]
-    dev = gm.decode_greedy(s, first, len(prompt), 128).tolist()
-    upto = flips[0] if flips else 128
-    assert dev[:upto] == gids[1:upto + 1]
 
 
 def test_embeddings_match_oracle(yl, orc, model_factory):

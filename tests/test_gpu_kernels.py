@@ -68,7 +68,7 @@ def test_quantize_dispatch_errors(yl, torch_cuda):
     dst = yl.new_workspace_buffer(yl.WeightFormat.Q8_0, 64, 32)
     with pytest.raises(yl.YlError) as e:
         yl.quantize(yl.WeightFormat.F16, dst, x, 64, 32)
-    assert e.value.code == -3  # format/variant mismatch (weight_type.rs:141)
+    assert e.value.code == -3  # format/variant mismatch (weight_type.rs:88)
     yl.quantize(yl.WeightFormat.Q8_0, dst, x, 64, 32)
 
 
@@ -221,7 +221,7 @@ GEMM_CASES = [(260, 576, 17), (1000, 2048, 32), (384, 2080, 20), (260, 576, 33),
 def test_gemm_bit_exact_vs_oracle(yl, orc, torch_cuda, o, n, batch, fmt, scale_type):
     """Batches of 16 or more tokens run on the int8 tensor-core GEMM. It folds
     each 32-block's exact int32 dot as ((f32)isum * ws) * xs in group order,
-    the oracle's sequence (weight_type.rs:190-224), so into a zeroed output the
+    the oracle's sequence (weight_type.rs:190-201, :207-224), so into a zeroed output the
     results are bit-identical. Cases cover both token tiles (32 and 64), row
     and token tails, a single block, an odd block count (f16 scale pairs) and
     several K stages."""
@@ -244,7 +244,7 @@ def test_gemm_bit_exact_vs_oracle(yl, orc, torch_cuda, o, n, batch, fmt, scale_t
 @pytest.mark.parametrize("fmt", ["Q8_0", "Q4_0"])
 def test_gemm_accumulate_quirk(yl, orc, torch_cuda, fmt):
     """The `+=` quirk through the GEMM: quad columns add into the initial
-    output, remainder columns overwrite it (weight_type.rs:190-224)."""
+    output, remainder columns overwrite it (weight_type.rs:190-201 vs :223)."""
     rng = np.random.default_rng(11)
     o, n, batch = 262, 1024, 40
     f = getattr(yl.WeightFormat, fmt)

@@ -43,7 +43,7 @@ def test_matmul_q8_remainder_columns(orc):
 
 
 def test_matmul_quad_accumulates_remainder_overwrites(orc):
-    # weight_type.rs:243-254 (+=) vs :276 (=)
+    # weight_type.rs:190-201 (+=) vs :223 (=)
     n, o = 32, 6
     out = np.full(o, 100.0, np.float32)
     orc.matmul_q8(out, np.ones(n, np.int8), np.ones(1, np.float32), np.ones(o * n, np.int8),

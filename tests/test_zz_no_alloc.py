@@ -65,6 +65,28 @@ def test_static_matches_allocating_entry_point_twice(hd, nh, nkv, start):
         assert np.max(np.abs(g - r)) <= 1e-5 * float(vc.abs().max())
 
 
+@pytest.mark.parametrize("batch,start", [(7, 100), (40, 17)])
+def test_static_multi_token_matches_allocating_entry_point(batch, start):
+    """Several query rows (one split, the query-blocked kernel from 32 rows):
+    the same result as yl_fused_attention, twice in a row."""
+    import torch
+    lib = _lib()
+    hd, nh, nkv = 128, 32, 8
+    scale = 1.0 / float(np.sqrt(hd))
+    for call in range(2):
+        rng = np.random.default_rng(7 * call + batch + start)
+        seq = start + batch
+        sq = torch.from_numpy(rng.standard_normal(batch * nh * hd).astype(np.float32)).cuda()
+        kc = torch.from_numpy(rng.standard_normal(seq * nkv * hd).astype(np.float32)).cuda()
+        vc = torch.from_numpy(rng.standard_normal(seq * nkv * hd).astype(np.float32)).cuda()
+        ref = torch.zeros(batch * nh * hd, device="cuda")
+        got = torch.full((batch * nh * hd,), float("nan"), device="cuda")
+        assert _call(lib.yl_fused_attention, torch, ref, sq, kc, vc, seq, batch, nh, nkv, hd, start, scale) == 0
+        rc = _call(lib.yl_fused_attention_static, torch, got, sq, kc, vc, seq, batch, nh, nkv, hd, start, scale)
+        assert rc == 0, lib.yl_last_error().decode()
+        assert np.max(np.abs(got.cpu().numpy() - ref.cpu().numpy())) <= 1e-5 * float(vc.abs().max())
+
+
 def test_static_rejects_oversized_request():
     import torch
     lib = _lib()

@@ -1,7 +1,7 @@
 """Python mirror of the reference's API for the quantized forward path.
 
 The reference crate (yallma3-mini-inference) exposes, for this path:
-  * weight_type.rs:70-173  WeightFormat, QuantizedTensor, quantize, matmul,
+  * weight_type.rs:17-120  WeightFormat, QuantizedTensor, quantize, matmul,
                            new_workspace_buffer
   * quantization.rs:23-52  MutableQuantizedTensorQ8, quantize
   * transformer.rs:19-69   the Transformer trait (load_model, name, vocab_size,
@@ -112,6 +112,8 @@ _sigs = {
     "yl_forward_x": (C.c_int, [_P, _P, _P, C.c_uint64, C.c_uint32, _P, _P]),
     "yl_decode_greedy": (C.c_int, [_P, _P, C.c_uint32, C.c_uint32, C.c_uint32, _P, _P, C.c_int]),
     "yl_decode_step_launches": (C.c_int, [_P, C.POINTER(C.c_uint32)]),
+    "yl_session_decode_graph_launches": (C.c_int, [_P, C.c_int, C.POINTER(C.c_uint32)]),
+    "yl_model_attention_decode": (C.c_int, [_P, _P, _P, _P, C.c_uint32, _P, _P, _P, _P]),
     "yl_profile_decode_step": (C.c_int, [_P, _P, C.c_uint32, C.c_uint32, _P, C.c_uint32, C.POINTER(C.c_uint32)]),
     "yl_trace_decode_step": (C.c_int, [_P, _P, C.c_uint32, C.c_uint32, _P, C.c_uint64, C.POINTER(C.c_uint32)]),
     "load_transformer_ffi": (C.c_bool, [C.c_char_p]),
@@ -181,7 +183,7 @@ def _stream(stream) -> Optional[int]:
 # ------------------------------------------------------ weight_type.rs ---
 
 class WeightFormat(enum.IntEnum):
-    """weight_type.rs:70-75"""
+    """weight_type.rs:17-22"""
     Q8_0 = 0
     Q4_0 = 1
     F16 = 2
@@ -199,7 +201,7 @@ SCALE_F32, SCALE_F16 = 0, 1
 
 
 class QuantizedTensor:
-    """A device-resident QuantizedTensor (weight_type.rs:83-103).
+    """A device-resident QuantizedTensor (weight_type.rs:30-50).
 
     Activation tensors (the reference's flat containers) come from
     `new_workspace_buffer`; weight matrices (repacked HBM layout) from
@@ -254,14 +256,14 @@ class QuantizedTensor:
 
 
 def new_workspace_buffer(fmt: WeightFormat, len: int, gs: int) -> QuantizedTensor:
-    """weight_type.rs:161-173"""
+    """weight_type.rs:108-120"""
     c = QTensorC()
     _check(_lib.yl_qtensor_alloc(int(fmt), len, gs, C.byref(c)))
     return QuantizedTensor(c)
 
 
 def quantize(fmt: WeightFormat, dst: QuantizedTensor, x, n: int, gs: int, stream=None) -> None:
-    """weight_type.rs:129-143: quantize n values of device tensor `x` into `dst`."""
+    """weight_type.rs:76-90: quantize n values of device tensor `x` into `dst`."""
     _check(_lib.yl_quantize(int(fmt), C.byref(dst.c), _ptr(x), n, gs, _stream(stream)))
 
 
@@ -272,7 +274,7 @@ def quantize_q8_0(x, q, scale, n: int, gs: int = 32, stream=None) -> None:
 
 def matmul(out, x: QuantizedTensor, w: QuantizedTensor, n: int, o: int, gs: int, batch: Optional[int] = None,
            accumulate: bool = True, stream=None) -> None:
-    """weight_type.rs:145-159. batch defaults to out.numel() // o like the
+    """weight_type.rs:92-106. batch defaults to out.numel() // o like the
     reference. accumulate=True reproduces the reference's `+=` on the first
     4*floor(o/4) columns."""
     if batch is None:
@@ -418,6 +420,20 @@ class Transformer:
         _check(_lib.yl_decode_step_launches(self._h, C.byref(n)))
         return n.value
 
+    def attention_decode(self, qkv, key_cache, value_cache, pos: int, out=None, out_q=None, out_s=None,
+                         stream=None) -> None:
+        """The decode step's fused RoPE + cache write + attention kernel for one
+        token (device tensors): k/v rows written at `pos`, output into out (f32)
+        and/or out_q/out_s (Q8_0 blocks)."""
+        _check(_lib.yl_model_attention_decode(self._h, _ptr(qkv), _ptr(key_cache), _ptr(value_cache), pos,
+                                              _ptr(out), _ptr(out_q), _ptr(out_s), _stream(stream)))
+
+    def decode_graph_launches(self, session: InferenceSession, with_logits: bool = False) -> int:
+        """Kernel nodes of the session's captured decode graph (counted in the graph)."""
+        n = C.c_uint32()
+        _check(_lib.yl_session_decode_graph_launches(session._h, 1 if with_logits else 0, C.byref(n)))
+        return n.value
+
     def profile_decode_step(self, session: InferenceSession, token: int, pos: int) -> np.ndarray:
         """Per-launch device microseconds of one decode step launched kernel
         by kernel: [embed, (qkv, attention, wo, gate/up, down) x layers, lm_head]."""
@@ -498,7 +514,7 @@ def load_transformer_ffi(model_path: Optional[str]) -> bool:
 
 # -------------------------------------------------- synthetic models ---
 
-# C1 SmolLM2-135M-shaped, C2/C3 Llama-3.2-1B-shaped (Q8_0 /
+# Benchmark configurations: C1 SmolLM2-135M-shaped, C2/C3 Llama-3.2-1B-shaped (Q8_0 /
 # Q4_0), C4 Llama-3-8B-shaped (untied lm_head); plus tiny shapes for tests.
 PRESETS = {
     "c1": dict(dim=576, hidden_dim=1536, n_layers=30, n_heads=9, n_kv_heads=3, vocab_size=49152,

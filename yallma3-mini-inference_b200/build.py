@@ -42,11 +42,18 @@ def _obj(src: Path) -> Path:
     return BUILD / str(rel).replace(os.sep, "__")
 
 
+def _extra() -> list[str]:
+    """YL_WITH_TRACE=1 in the environment builds the diagnostics variant whose
+    decode kernels stamp a timeline (yl_trace_decode_step); the default build
+    compiles those stamps out."""
+    return ["-DYL_WITH_TRACE=1"] if os.environ.get("YL_WITH_TRACE", "0") == "1" else []
+
+
 def _compile(src: Path) -> tuple[Path, str]:
     obj = _obj(src)
-    cmd = [NVCC, *ARCH, *COMMON, "-c", str(src), "-o", str(obj)]
+    cmd = [NVCC, *ARCH, *COMMON, *_extra(), "-c", str(src), "-o", str(obj)]
     if src.suffix == ".cpp":
-        cmd = [NVCC, *COMMON, "-Wno-deprecated-gpu-targets", "-x", "c++", "-c", str(src), "-o", str(obj)]
+        cmd = [NVCC, *COMMON, *_extra(), "-Wno-deprecated-gpu-targets", "-x", "c++", "-c", str(src), "-o", str(obj)]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"compile failed: {src}\n{' '.join(cmd)}\n{r.stdout}\n{r.stderr}")
@@ -57,14 +64,22 @@ def build(verbose: bool = False, jobs: int | None = None) -> Path:
     BUILD.mkdir(exist_ok=True)
     srcs = sources()
     newest_header = max((h.stat().st_mtime for h in headers()), default=0.0)
+    # objects built with other flags (trace on/off) are all stale
+    stamp = BUILD / "flags.txt"
+    flags = " ".join(_extra())
+    same_flags = stamp.exists() and stamp.read_text() == flags
     stale = [s for s in srcs
-             if not _obj(s).exists() or _obj(s).stat().st_mtime < max(s.stat().st_mtime, newest_header)]
+             if not same_flags or not _obj(s).exists()
+             or _obj(s).stat().st_mtime < max(s.stat().st_mtime, newest_header)]
+    if stamp.exists() and not same_flags:
+        stamp.unlink()  # written again only once every object carries the new flags
     if stale:
         jobs = jobs or min(len(stale), os.cpu_count() or 4)
         with cf.ThreadPoolExecutor(max_workers=jobs) as ex:
             for obj, log in ex.map(_compile, stale):
                 if verbose and log.strip():
                     print(log)
+    stamp.write_text(flags)
     objs = [_obj(s) for s in srcs]
     if stale or not LIB.exists() or LIB.stat().st_mtime < max(o.stat().st_mtime for o in objs):
         tmp = LIB.with_suffix(".so.tmp")

@@ -241,9 +241,13 @@ int yl_matmul(float* out, const yl_qtensor* x, const yl_qtensor* w, uint64_t n, 
                     false, sms);
 }
 
+}  // extern "C"
+
+namespace yl {
 // Split count for a single-token attention call: enough CTAs to cover the
-// SMs twice, never more splits than keys, at most 64.
-static uint32_t attention_splits(uint64_t seq_len, uint64_t n_kv_heads) {
+// SMs twice, never more splits than keys, at most 64. Shared by both
+// attention entry points so that they split (and so round) identically.
+uint32_t attention_splits(uint64_t seq_len, uint64_t n_kv_heads) {
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -253,9 +257,9 @@ static uint32_t attention_splits(uint64_t seq_len, uint64_t n_kv_heads) {
   return (uint32_t)std::max<uint64_t>(ns, 1);
 }
 
-static int check_attention_args(const float* output, const float* sq, const float* kc, const float* vc,
-                                uint64_t seq_len, uint64_t batch, uint64_t n_heads, uint64_t n_kv_heads,
-                                uint64_t head_size, uint32_t start_pos, uint64_t kv_dim) {
+int check_attention_args(const float* output, const float* sq, const float* kc, const float* vc, uint64_t seq_len,
+                         uint64_t batch, uint64_t n_heads, uint64_t n_kv_heads, uint64_t head_size,
+                         uint32_t start_pos, uint64_t kv_dim) {
   if (!output || !sq || !kc || !vc) return fail(YL_ERR_ARG, "null pointer");
   if (batch == 0) return fail(YL_ERR_ARG, "empty batch");
   if (head_size != 64 && head_size != 128) return fail(YL_ERR_UNSUPPORTED, "head_size must be 64 or 128");
@@ -266,6 +270,9 @@ static int check_attention_args(const float* output, const float* sq, const floa
   if (((uintptr_t)kc | (uintptr_t)vc) % 16 || kv_dim % 4) return fail(YL_ERR_ARG, "caches must be 16-byte aligned");
   return YL_OK;
 }
+}  // namespace yl
+
+extern "C" {
 
 int yl_fused_attention(float* output, const float* sq, const float* key_cache, const float* value_cache,
                        uint64_t seq_len, uint64_t batch, uint64_t n_heads, uint64_t n_kv_heads, uint64_t head_size,
@@ -509,11 +516,9 @@ int yl_forward_x(const yl_model* m, yl_session* sp, const uint32_t* tokens, uint
   const bool lg_graph = logits_out && m->m->tp_size > 1;
   if (n == 1) {  // batch-1 step through the captured decode graph
     if ((rc = ensure_decode_graph(s, lg_graph))) return rc;
-    s->state_h->pos = (int32_t)start_pos;
-    s->state_h->token = (int32_t)tokens[0];
-    s->state_h->next = 0;
-    s->state_h->steps = 0;
-    YL_CUDA_TRY(cudaMemcpyAsync(s->state, s->state_h, sizeof(k::StepState), cudaMemcpyHostToDevice, s->stream));
+    k::LaunchCfg lc;
+    lc.stream = s->stream;
+    YL_CUDA_TRY(k::set_step_state(s->state, (int32_t)start_pos, (int32_t)tokens[0], lc));
     YL_CUDA_TRY(cudaGraphLaunch(lg_graph ? s->graph_lg : s->graph, s->stream));
   } else {
     if ((rc = forward(s, tokens, (uint32_t)n, start_pos, logits_out != nullptr))) return rc;
@@ -555,11 +560,11 @@ int yl_decode_greedy(const yl_model* m, yl_session* sp, uint32_t first_token, ui
   int rc;
   if ((rc = ensure_decode_graph(s))) return rc;
   cudaStream_t st = stream ? (cudaStream_t)stream : s->stream;
-  s->state_h->pos = (int32_t)start_pos;
-  s->state_h->token = (int32_t)first_token;
-  s->state_h->next = 0;
-  s->state_h->steps = 0;
-  YL_CUDA_TRY(cudaMemcpyAsync(s->state, s->state_h, sizeof(k::StepState), cudaMemcpyHostToDevice, st));
+  // the start state is a launch argument, not a host staging buffer, so a
+  // second call made before this one's work ran cannot overwrite it
+  k::LaunchCfg lc;
+  lc.stream = st;
+  YL_CUDA_TRY(k::set_step_state(s->state, (int32_t)start_pos, (int32_t)first_token, lc));
   for (uint32_t i = 0; i < n_steps; ++i) YL_CUDA_TRY(cudaGraphLaunch(s->graph, st));
   if (!sync) return YL_OK;
   if (tokens_out)
@@ -580,6 +585,47 @@ int yl_decode_step_launches(const yl_model* m, uint32_t* out) {
   uint32_t n = 1 + 5 * L + 1;
   if (m->m->tp_size > 1) n += 1 + (tunables().tp_fused ? 0 : 2 * L);
   *out = n;
+  return YL_OK;
+}
+
+int yl_model_attention_decode(const yl_model* m, const float* qkv, float* key_cache, float* value_cache, uint32_t pos,
+                              float* out, int8_t* out_q, float* out_s, void* stream) {
+  if (!m || !qkv || !key_cache || !value_cache || (!out && !out_q)) return fail(YL_ERR_ARG, "null argument");
+  if (out_q && !out_s) return fail(YL_ERR_ARG, "quantized output needs its scales");
+  const Model* mm = m->m;
+  const yl_shape& sh = mm->shape;
+  if (pos >= sh.ctx_len) return fail(YL_ERR_RANGE, "position beyond the model's ctx_len (RoPE table rows)");
+  YL_CUDA_TRY(cudaSetDevice(mm->device));
+  k::AttnDecodeArgs ad{};
+  ad.qkv = qkv;
+  ad.cs = mm->rope_cs;
+  ad.rope_mode = sh.rope_mode;
+  ad.kcache = key_cache;
+  ad.vcache = value_cache;
+  ad.n_heads = mm->l_heads;
+  ad.n_kv_heads = mm->l_kv;
+  ad.head_size = sh.head_size;
+  ad.kv_dim = mm->l_kv * sh.head_size;
+  ad.pos0 = pos;
+  ad.scale = mm->attn_scale;
+  ad.n_splits = k::attention_decode_splits(mm->l_kv, sh.head_size);
+  ad.out = out;
+  ad.q8 = out_q;
+  ad.s8 = out_s;
+  k::LaunchCfg lc;
+  lc.stream = (cudaStream_t)stream;
+  cudaError_t e = k::attention_decode(ad, lc);
+  if (e != cudaSuccess) return fail(YL_ERR_CUDA, std::string("decode attention launch: ") + cudaGetErrorString(e));
+  return YL_OK;
+}
+
+int yl_session_decode_graph_launches(yl_session* sp, int with_logits, uint32_t* out) {
+  if (!sp || !out) return fail(YL_ERR_ARG, "null argument");
+  Session* s = sp->s;
+  const bool lg = with_logits && s->m->tp_size > 1;
+  int rc = ensure_decode_graph(s, lg);
+  if (rc) return rc;
+  *out = lg ? s->graph_launches_lg : s->graph_launches;
   return YL_OK;
 }
 

@@ -541,7 +541,6 @@ Session::~Session() {
   if (tp_region) cudaFree(tp_region);
   if (stream) cudaStreamDestroy(stream);
   for (void* p : allocs) cudaFree(p);
-  if (state_h) cudaFreeHost(state_h);
   if (logits_h) cudaFreeHost(logits_h);
   if (hist_h) cudaFreeHost(hist_h);
 }
@@ -635,7 +634,6 @@ int session_create(const Model* m, Session** out) {
   s->err = (int*)p;
   YL_CUDA_TRY(cudaMemset(s->err, 0, sizeof(int)));
   YL_CUDA_TRY(cudaMemset(s->state, 0, sizeof(k::StepState)));
-  YL_CUDA_TRY(cudaMallocHost(&s->state_h, sizeof(k::StepState)));
   YL_CUDA_TRY(cudaMallocHost(&s->logits_h, (uint64_t)sh.vocab_size * 4));
   YL_CUDA_TRY(cudaMallocHost(&s->hist_h, ((uint64_t)sh.ctx_len + 1) * 4));
   if ((rc = ensure_cap(s.get(), 8))) return rc;
@@ -1154,6 +1152,8 @@ int profile_step(Session* s, uint32_t token, uint32_t pos, float* us, uint32_t c
 
 int trace_step(Session* s, uint32_t token, uint32_t pos, uint64_t* out, uint64_t cap, uint32_t* n_launches) {
   const yl_shape& sh = s->m->shape;
+  if (!YL_WITH_TRACE)
+    return fail(YL_ERR_UNSUPPORTED, "timeline stamps are compiled in only by a diagnostics build (YL_WITH_TRACE=1)");
   if (pos >= sh.ctx_len) return fail(YL_ERR_RANGE, "position beyond ctx_len");
   YL_CUDA_TRY(cudaSetDevice(s->device));
   int rc = ensure_cap(s, 8);
@@ -1165,11 +1165,11 @@ int trace_step(Session* s, uint32_t token, uint32_t pos, uint64_t* out, uint64_t
     s->trace = (uint64_t*)p;
   }
   YL_CUDA_TRY(cudaMemsetAsync(s->trace, 0, n_max * TRACE_STRIDE * 8, s->stream));
-  s->state_h->pos = (int32_t)pos;
-  s->state_h->token = (int32_t)token;
-  s->state_h->next = 0;
-  s->state_h->steps = 0;
-  YL_CUDA_TRY(cudaMemcpyAsync(s->state, s->state_h, sizeof(k::StepState), cudaMemcpyHostToDevice, s->stream));
+  {
+    k::LaunchCfg lc;
+    lc.stream = s->stream;
+    YL_CUDA_TRY(k::set_step_state(s->state, (int32_t)pos, (int32_t)token, lc));
+  }
   YL_CUDA_TRY(cudaStreamSynchronize(s->stream));
   cudaGraph_t g = nullptr;
   cudaGraphExec_t ge = nullptr;
@@ -1219,10 +1219,25 @@ int capture_decode_graph(Session* s, bool gather) {
   cudaError_t e = cudaStreamEndCapture(s->stream, &g);
   if (rc) { if (g) cudaGraphDestroy(g); return rc; }
   if (e != cudaSuccess) return fail(YL_ERR_CUDA, std::string("graph capture: ") + cudaGetErrorString(e));
+  // the kernel nodes the capture recorded (the launch count of one step)
+  size_t nn = 0;
+  e = cudaGraphGetNodes(g, nullptr, &nn);
+  std::vector<cudaGraphNode_t> nodes(nn);
+  if (e == cudaSuccess && nn) e = cudaGraphGetNodes(g, nodes.data(), &nn);
+  uint32_t kernels = 0;
+  for (size_t i = 0; e == cudaSuccess && i < nn; ++i) {
+    cudaGraphNodeType t;
+    e = cudaGraphNodeGetType(nodes[i], &t);
+    if (e == cudaSuccess && t == cudaGraphNodeTypeKernel) ++kernels;
+  }
+  if (e != cudaSuccess) { cudaGraphDestroy(g); return fail(YL_ERR_CUDA, std::string("graph nodes: ") + cudaGetErrorString(e)); }
   e = cudaGraphInstantiate(&s->graph, g, 0);
   cudaGraphDestroy(g);
   if (e != cudaSuccess) { s->graph = nullptr; return fail(YL_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(e)); }
-  s->graph_launches = nl;
+  if (kernels != nl) return fail(YL_ERR_CUDA, "decode graph holds " + std::to_string(kernels) + " kernels, " +
+                                                  std::to_string(nl) + " were enqueued");
+  if (gather) s->graph_launches_lg = kernels;
+  else s->graph_launches = kernels;
   return YL_OK;
 }
 

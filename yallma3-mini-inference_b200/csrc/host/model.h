@@ -84,7 +84,6 @@ struct Session {
   k::StepState* state = nullptr;
   int* err = nullptr;
   // pinned host staging
-  k::StepState* state_h = nullptr;
   float* logits_h = nullptr;
   uint32_t* hist_h = nullptr;
   uint32_t n_splits = 1;
@@ -93,7 +92,8 @@ struct Session {
   bool trace_on = false;
   cudaGraphExec_t graph = nullptr;
   cudaGraphExec_t graph_lg = nullptr;  // tensor-parallel decode step that also gathers logits
-  uint32_t graph_launches = 0;
+  uint32_t graph_launches = 0;     // kernel nodes of `graph` (one decode step)
+  uint32_t graph_launches_lg = 0;  // kernel nodes of `graph_lg`
   // tensor parallelism: this rank's exchange region (shared with the peers
   // through CUDA IPC) and every rank's region as mapped here
   uint8_t* tp_region = nullptr;

@@ -174,5 +174,19 @@ cudaError_t argmax(const float* logits, uint32_t n, uint32_t* out, StepState* st
   return launch_kernel(argmax_kernel, dim3(1), dim3(1024), 0, lc, logits, n, out, state);
 }
 
+// The token and position travel as launch arguments, so back-to-back calls
+// that enqueue without synchronizing each start from their own values.
+__global__ void set_step_state_kernel(StepState* state, int32_t pos, int32_t token) {
+  grid_dep_wait();
+  state->pos = pos;
+  state->token = token;
+  state->next = 0;
+  state->steps = 0;
+}
+
+cudaError_t set_step_state(StepState* state, int32_t pos, int32_t token, const LaunchCfg& lc) {
+  return launch_kernel(set_step_state_kernel, dim3(1), dim3(1), 0, lc, state, pos, token);
+}
+
 }  // namespace k
 }  // namespace yl

@@ -323,7 +323,7 @@ __global__ void __maxnreg__(96) attn_decode_kernel(AttnDecodeArgs a) {
   const uint32_t rank = cluster.block_rank();
   const uint32_t kvh = blockIdx.x / cs;
   constexpr uint32_t kv_mul = KVM;
-  uint64_t* const trace = a.trace ? a.trace + (uint64_t)blockIdx.x * 8 : nullptr;
+  uint64_t* const trace = (kTrace && a.trace) ? a.trace + (uint64_t)blockIdx.x * 8 : nullptr;
   uint64_t ts[8] = {0, 0, 0, 0, 0, 0, 0, 0};  // timeline stamps, stored at the end
   if (trace && tid == 0) ts[0] = globaltimer();
   grid_dep_launch();

@@ -30,6 +30,13 @@ __device__ __forceinline__ void st_volatile_u64(void* p, uint64_t v) {
 __device__ __forceinline__ void ld_volatile_2u64(const void* p, uint64_t& a, uint64_t& b) {
   asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
 }
+// Timeline stamps of the decode step (yl_trace_decode_step) exist only in a
+// diagnostics build (YL_WITH_TRACE=1); the product build compiles every stamp
+// branch out.
+#ifndef YL_WITH_TRACE
+#define YL_WITH_TRACE 0
+#endif
+constexpr bool kTrace = YL_WITH_TRACE != 0;
 // Global nanosecond timer (timeline tracing of the decode step).
 __device__ __forceinline__ uint64_t globaltimer() {
   uint64_t t;

@@ -7,6 +7,11 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+// Diagnostics build switch (timeline stamps inside the decode kernels).
+#ifndef YL_WITH_TRACE
+#define YL_WITH_TRACE 0
+#endif
+
 namespace yl {
 namespace k {
 
@@ -262,6 +267,8 @@ cudaError_t tp_argmax(const TpArgs& t, uint64_t lm_off, uint64_t logit_off, uint
 // for the device-resident decode loop.
 cudaError_t argmax(const float* logits, uint32_t n, uint32_t* out, StepState* state, const LaunchCfg& lc);
 
-// Copies state->token/pos from a host-written staging struct (graph input).
+// Starts a device-resident decode run: state = {pos, token, next 0, steps 0}
+// (one thread; the values are launch arguments, so nothing is staged on the host).
+cudaError_t set_step_state(StepState* state, int32_t pos, int32_t token, const LaunchCfg& lc);
 }  // namespace k
 }  // namespace yl

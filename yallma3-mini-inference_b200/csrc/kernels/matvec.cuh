@@ -1,7 +1,7 @@
 // Weight-streaming matvec for decode and small batches (1..8 tokens per pass):
 //   out[t][r] = sum_g ((float)isum(t, r, g) * w_scale[r][g]) * x_scale[t][g]
-// with isum the exact int32 dot of one 32-element block (weight_type.rs:176-279,
-// `matmul_q8_slices`), or the f32 dot of matmul_f32 (weight_type.rs:281-323) for
+// with isum the exact int32 dot of one 32-element block (weight_type.rs:122-226,
+// `matmul_q8_slices`), or the f32 dot of matmul_f32 (weight_type.rs:228-270) for
 // F16 weights and for the f32-activation lm_head (forward.rs:261-279).
 //
 // Design (B200): the op is HBM-bound (one byte of weight per 2 int ops at
@@ -135,7 +135,7 @@ __device__ __forceinline__ bool am_better(float v, uint32_t i, float bv, uint32_
 // (programmatic dependent launch); everything before it overlaps that kernel.
 __device__ __forceinline__ void mv_wait_inputs(const MvArgs& a) {
   yl::dev::grid_dep_wait();
-  if (a.trace && threadIdx.x == 32) a.trace[(uint64_t)blockIdx.x * 8 + 2] = yl::dev::globaltimer();
+  if (yl::dev::kTrace && a.trace && threadIdx.x == 32) a.trace[(uint64_t)blockIdx.x * 8 + 2] = yl::dev::globaltimer();
 }
 
 constexpr int MV_NORM_MU = 8;    // float4 per thread with a norm (K <= 8192)
@@ -215,7 +215,7 @@ __device__ __forceinline__ void mv_norm_regs(const MvArgs& a, const MvLayout& L,
         ss = fmaf(xv[u].w, xv[u].w, ss);
       }
       ss = warp_sum(ss);
-      if (a.trace && t == 0 && ctid == 0) a.trace[(uint64_t)blockIdx.x * 8 + 4] = globaltimer();
+      if (kTrace && a.trace && t == 0 && ctid == 0) a.trace[(uint64_t)blockIdx.x * 8 + 4] = globaltimer();
       if (lane == 0) red[cw] = ss;
       named_bar_sync(1, MV_NCW * 32);
       float tot = 0.0f;
@@ -225,7 +225,7 @@ __device__ __forceinline__ void mv_norm_regs(const MvArgs& a, const MvLayout& L,
       r = __fadd_rn(r, a.eps);
       r = __fdiv_rn(1.0f, __fsqrt_rn(r));
       named_bar_sync(1, MV_NCW * 32);  // red[] reused by the next token
-      if (a.trace && t == 0 && ctid == 0) a.trace[(uint64_t)blockIdx.x * 8 + 5] = globaltimer();
+      if (kTrace && a.trace && t == 0 && ctid == 0) a.trace[(uint64_t)blockIdx.x * 8 + 5] = globaltimer();
     }
     // y = w * (r * x) in place
 #pragma unroll
@@ -339,7 +339,7 @@ __device__ __forceinline__ void mv_norm_regs(const MvArgs& a, const MvLayout& L,
         if (in && e0 == 0) reinterpret_cast<float*>(smem + L.xs_off)[t * nb + b] = sc[j];
       }
     }
-    if (a.trace && t == 0 && lane == 0) {  // this warp's rows quantized: warp 0, and the last warp
+    if (kTrace && a.trace && t == 0 && lane == 0) {  // this warp's rows quantized: warp 0, and the last warp
       const unsigned long long now = globaltimer();
       if (cw == 0) a.trace[(uint64_t)blockIdx.x * 8 + 6] = now;
       atomicMax(reinterpret_cast<unsigned long long*>(a.trace + (uint64_t)blockIdx.x * 8 + 7), now);
@@ -785,7 +785,7 @@ __global__ void __launch_bounds__(MV_THREADS, (NT <= 2 ? 2 : 1)) mv_kernel(MvArg
   const uint32_t nch = (K + kc - 1) / kc;
   const uint32_t nrs = (r_end - r_begin + RS - 1) / RS;
 
-  uint64_t* const trace = a.trace ? a.trace + (uint64_t)blockIdx.x * 8 : nullptr;
+  uint64_t* const trace = (kTrace && a.trace) ? a.trace + (uint64_t)blockIdx.x * 8 : nullptr;
   if (trace && threadIdx.x == 0) trace[0] = globaltimer();
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
