@@ -131,11 +131,14 @@ int yl_matmul(float* out, const yl_qtensor* x, const yl_qtensor* w, uint64_t n, 
  * [seq_len][kv_dim] (queries already rotated, caches already holding the new
  * rows, seq_len = start_pos + batch as in forward.rs:135). Scores use
  * attn_scale, masked positions are excluded, the softmax runs over the whole
- * visible row. sq/output: [batch][n_heads*head_size]. All device pointers.
- * The reference takes its softmax scratch from the caller (`scores`); here a
- * single-token call splits the keys across CTAs and keeps the split partials
- * in a workspace this function allocates and frees on `stream`.
- * head_size 64 or 128, n_heads/n_kv_heads <= 8. */
+ * visible row. sq/output: [batch][n_heads*head_size]. All device pointers,
+ * 16-byte aligned. The result is bit-identical to the reference's: the same
+ * f32 operations in the same order (8-lane dot products, the softmax sum in
+ * position order, 8-lane P.V sums split at seq_len/8, exp correctly rounded).
+ * seq_len must equal start_pos + batch. The reference takes its softmax
+ * scratch from the caller (`scores`); here the weights live in a workspace of
+ * batch * n_heads * round_up(seq_len, 4) floats that this function allocates
+ * and frees on `stream`. head_size 64 or 128, n_heads/n_kv_heads <= 8. */
 int yl_fused_attention(float* output, const float* sq, const float* key_cache, const float* value_cache,
                        uint64_t seq_len, uint64_t batch, uint64_t n_heads, uint64_t n_kv_heads, uint64_t head_size,
                        uint32_t start_pos, uint64_t kv_dim, float attn_scale, void* stream);
@@ -145,10 +148,10 @@ int yl_fused_attention(float* output, const float* sq, const float* key_cache, c
  * cudaMalloc or cudaMallocAsync where attention runs (an engine whose memory
  * manager owns all device memory, or a latency-critical loop that must not
  * risk the allocator's implicit synchronization or out-of-memory failures).
- * Same arguments and result as yl_fused_attention; the split partials live in
- * a fixed device array of YL_ATTN_STATIC_BYTES (1 MiB) that every GPU loading
- * this library holds until the process exits. A call whose partials would not
- * fit (n_heads * splits * (head_size + 2) * 4 bytes) fails with
+ * Same arguments and result as yl_fused_attention; its workspace lives in a
+ * fixed device array of YL_ATTN_STATIC_BYTES (1 MiB) that every GPU loading
+ * this library holds until the process exits. A call whose workspace would
+ * not fit (batch * n_heads * round_up(seq_len, 4) * 4 bytes) fails with
  * YL_ERR_UNSUPPORTED. Every call resolves the array's device address on the
  * current device (cudaGetSymbolAddress, which allocates nothing), so calls
  * after a cudaDeviceReset find the reloaded array; the first call on a device

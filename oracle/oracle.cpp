@@ -37,6 +37,22 @@ inline int8_t rust_f32_as_i8(float v) {
   return (int8_t)v;
 }
 
+/* e^x rounded to nearest float. The reference calls `f32::exp` in the
+ * softmax (forward.rs:358, the platform libm's expf) and wide's f32x8 exp in
+ * the SiLU (forward.rs:230, wide 0.7.33, not vendored; f32::exp for a scalar
+ * tail, :235). Neither is pinned
+ * to the bit: glibc's expf is within 0.502 ulp and, checked over all 2^32
+ * float inputs (tests/test_expf_exact.py), differs from the correctly rounded
+ * value by one ulp on 170,648 of them. The oracle defines exp as the correctly
+ * rounded value, computed through the C library's double exp (whose error is
+ * far below half a float ulp; the same test finds it equal to an x87
+ * long-double evaluation on every input). Probe bit 1 switches back to the
+ * C library's expf to measure what that choice moves. */
+inline float exp_f32(float x) {
+  if (g_probe & 2) return expf(x);
+  return (float)exp((double)x);
+}
+
 /* wide::f32x8::reduce_add (wide 0.7.33, not vendored; order unpinned).
  * Assumed: (lo4 + hi4) folded pairwise, the SSE horizontal-sum idiom. */
 inline float reduce_add8(const float l[8]) {
@@ -284,7 +300,7 @@ void orc_rms_norm_scalar(float* x, size_t n, const float* weight, float eps, int
 
 /* util.rs:446-450 */
 void orc_silu(float* x, size_t n) {
-  for (size_t i = 0; i < n; ++i) x[i] = x[i] / (1.0f + expf(-x[i]));
+  for (size_t i = 0; i < n; ++i) x[i] = x[i] / (1.0f + exp_f32(-x[i]));
 }
 
 /* util.rs:589-635 (`rope`, half-split pairs, llama3 scaling 32/1/4 hard-coded).
@@ -400,7 +416,7 @@ void orc_fused_attention(float* output, float* scores, const float* sq, const fl
     for (size_t t2 = max_t2 + 1; t2 < seq_len; ++t2) score_row[t2] = -1e10f;
     float sum_exp = 0.0f;
     for (size_t t2 = 0; t2 < seq_len; ++t2) {
-      float e = expf(score_row[t2] - max_score);
+      float e = exp_f32(score_row[t2] - max_score);
       score_row[t2] = e;
       sum_exp = sum_exp + e;
     }
@@ -873,9 +889,9 @@ extern "C" int orc_forward_x(const orc_model* m, orc_session* sess, const uint32
     std::fill(hu.begin(), hu.end(), 0.f);
     fk_matmul(sh, hg.data(), batch * hidden_dim, xq, m->w1[layer], dim, hidden_dim);
     fk_matmul(sh, hu.data(), batch * hidden_dim, xq, m->w3[layer], dim, hidden_dim);
-    for (size_t i = 0; i < batch * hidden_dim; ++i) { /* :221-237 (libm expf; wide exp unpinned) */
+    for (size_t i = 0; i < batch * hidden_dim; ++i) { /* :221-237 (correctly rounded exp; wide exp unpinned) */
       float g = hg[i];
-      float silu = g / (1.0f + expf(-g));
+      float silu = g / (1.0f + exp_f32(-g));
       hg[i] = silu * hu[i];
     }
     fk_quantize(sh, &xq, hg.data(), batch * hidden_dim);

@@ -57,9 +57,11 @@ typedef struct orc_shape {
 void orc_set_threads(int n);
 /* Sensitivity probe (test infrastructure): flags != 0 perturbs the oracle by
  * at most one rounding step. Bit 0: the rmsnorm sum of squares is accumulated
- * in double instead of the reference's 8-lane f32 fold. Used only to measure
- * how far a model's logits move under a 1-ulp change (how sensitive a test
- * model is to activation-quantization flips); 0 = the faithful restatement. */
+ * in double instead of the reference's 8-lane f32 fold. Bit 1: exp is the C
+ * library's expf (within 0.502 ulp) instead of the correctly rounded e^x.
+ * Used only to measure how far a model's logits move under a 1-ulp change
+ * (how sensitive a test model is to activation-quantization flips);
+ * 0 = the faithful restatement. */
 void orc_set_probe(int flags);
 int orc_get_threads(void);
 

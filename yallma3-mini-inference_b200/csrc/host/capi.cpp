@@ -244,19 +244,6 @@ int yl_matmul(float* out, const yl_qtensor* x, const yl_qtensor* w, uint64_t n, 
 }  // extern "C"
 
 namespace yl {
-// Split count for a single-token attention call: enough CTAs to cover the
-// SMs twice, never more splits than keys, at most 64. Shared by both
-// attention entry points so that they split (and so round) identically.
-uint32_t attention_splits(uint64_t seq_len, uint64_t n_kv_heads) {
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  uint64_t ns = (2 * (uint64_t)sms + n_kv_heads - 1) / n_kv_heads;
-  ns = std::min<uint64_t>(ns, 64);
-  ns = std::min<uint64_t>(ns, std::max<uint64_t>(seq_len, 1));
-  return (uint32_t)std::max<uint64_t>(ns, 1);
-}
-
 int check_attention_args(const float* output, const float* sq, const float* kc, const float* vc, uint64_t seq_len,
                          uint64_t batch, uint64_t n_heads, uint64_t n_kv_heads, uint64_t head_size,
                          uint32_t start_pos, uint64_t kv_dim) {
@@ -267,7 +254,11 @@ int check_attention_args(const float* output, const float* sq, const float* kc, 
     return fail(YL_ERR_UNSUPPORTED, "n_heads must be a multiple (at most 8x) of n_kv_heads");
   if (kv_dim < n_kv_heads * head_size) return fail(YL_ERR_ARG, "kv_dim smaller than n_kv_heads * head_size");
   if ((uint64_t)start_pos + batch > seq_len) return fail(YL_ERR_RANGE, "start_pos + batch exceeds seq_len");
-  if (((uintptr_t)kc | (uintptr_t)vc) % 16 || kv_dim % 4) return fail(YL_ERR_ARG, "caches must be 16-byte aligned");
+  // the reference calls it with seq_len = start_pos + batch (forward.rs:135),
+  // which also fixes its 8-lane / tail split of the P.V sums
+  if ((uint64_t)start_pos + batch != seq_len) return fail(YL_ERR_ARG, "seq_len must equal start_pos + batch");
+  if (((uintptr_t)kc | (uintptr_t)vc | (uintptr_t)sq) % 16 || kv_dim % 4)
+    return fail(YL_ERR_ARG, "queries and caches must be 16-byte aligned");
   return YL_OK;
 }
 }  // namespace yl
@@ -292,13 +283,11 @@ int yl_fused_attention(float* output, const float* sq, const float* key_cache, c
   a.kv_dim = (uint32_t)kv_dim;
   a.pos0 = start_pos;
   a.scale = attn_scale;
-  a.n_splits = batch == 1 ? attention_splits(seq_len, n_kv_heads) : 1;
+  a.n_splits = 1;
   a.out = output;
   void* ws = nullptr;
-  if (a.n_splits > 1) {
-    YL_CUDA_TRY(cudaMallocAsync(&ws, n_heads * a.n_splits * (head_size + 2) * 4, st));
-    a.part = (float*)ws;
-  }
+  YL_CUDA_TRY(cudaMallocAsync(&ws, k::attention_scratch_floats((uint32_t)batch, (uint32_t)n_heads, start_pos) * 4, st));
+  a.part = (float*)ws;
   k::LaunchCfg lc;
   lc.stream = st;
   cudaError_t e = k::attention(a, lc);
@@ -612,9 +601,14 @@ int yl_model_attention_decode(const yl_model* m, const float* qkv, float* key_ca
   ad.out = out;
   ad.q8 = out_q;
   ad.s8 = out_s;
+  ad.sc_stride = (uint32_t)round_up((uint64_t)pos + 1, 4);
   k::LaunchCfg lc;
   lc.stream = (cudaStream_t)stream;
+  void* ws = nullptr;
+  YL_CUDA_TRY(cudaMallocAsync(&ws, (uint64_t)mm->l_heads * ad.sc_stride * 4, lc.stream));
+  ad.sc = (float*)ws;
   cudaError_t e = k::attention_decode(ad, lc);
+  cudaFreeAsync(ws, lc.stream);
   if (e != cudaSuccess) return fail(YL_ERR_CUDA, std::string("decode attention launch: ") + cudaGetErrorString(e));
   return YL_OK;
 }

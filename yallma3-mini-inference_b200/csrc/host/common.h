@@ -62,13 +62,11 @@ inline uint16_t f32_to_f16(float f) {
 
 inline uint64_t round_up(uint64_t a, uint64_t b) { return (a + b - 1) / b * b; }
 
-// Argument checks and the single-token split count shared by
-// yl_fused_attention and yl_fused_attention_static (one definition, so the
-// two entry points accept the same requests and split them the same way).
+// Argument checks shared by yl_fused_attention and yl_fused_attention_static
+// (one definition, so the two entry points accept the same requests).
 int check_attention_args(const float* output, const float* sq, const float* kc, const float* vc, uint64_t seq_len,
                          uint64_t batch, uint64_t n_heads, uint64_t n_kv_heads, uint64_t head_size,
                          uint32_t start_pos, uint64_t kv_dim);
-uint32_t attention_splits(uint64_t seq_len, uint64_t n_kv_heads);
 
 }  // namespace yl
 

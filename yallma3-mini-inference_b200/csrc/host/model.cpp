@@ -304,6 +304,7 @@ const Tunables& tunables() {
     if (const char* e = getenv("YL_TP_FUSED")) x.tp_fused = atoi(e) != 0;
     if (const char* e = getenv("YL_GEMM")) x.gemm = atoi(e) != 0;
     if (const char* e = getenv("YL_GEMM_MIN")) x.gemm_min = (uint32_t)std::max(2, atoi(e));
+    if (const char* e = getenv("YL_PF_MB")) x.pf_bytes = (uint64_t)std::max(0, atoi(e)) << 20;
     return x;
   }();
   return t;
@@ -541,6 +542,7 @@ Session::~Session() {
   if (tp_region) cudaFree(tp_region);
   if (stream) cudaStreamDestroy(stream);
   for (void* p : allocs) cudaFree(p);
+  if (ascr) cudaFree(ascr);
   if (logits_h) cudaFreeHost(logits_h);
   if (hist_h) cudaFreeHost(hist_h);
 }
@@ -611,9 +613,11 @@ int session_create(const Model* m, Session** out) {
   YL_CUDA_TRY(cudaMemset(s->vcache, 0, s->kv_elems * 4));
   if ((rc = salloc(s.get(), (uint64_t)sh.vocab_size * 4, &p))) return rc;
   s->logits = (float*)p;
-  // decode attention: one cluster of n_splits CTAs per KV head
+  // decode attention: one cluster of n_splits CTAs per KV head; the scores /
+  // weights of every local query head over the context
   s->n_splits = k::attention_decode_splits(m->l_kv, sh.head_size);
-  if ((rc = salloc(s.get(), (uint64_t)sh.n_heads * s->n_splits * (sh.head_size + 2) * 4, &p))) return rc;
+  s->part_stride = (uint32_t)round_up(sh.ctx_len, 4);
+  if ((rc = salloc(s.get(), (uint64_t)m->l_heads * s->part_stride * 4, &p))) return rc;
   s->part = (float*)p;
   if ((rc = salloc(s.get(), ((uint64_t)sh.n_layers + 1) * 2 * 4, &p))) return rc;
   s->work = (unsigned int*)p;
@@ -814,6 +818,7 @@ int run_matvec_ex(const DevWeight& w, bool f32act, const int8_t* xq, const float
     a.work = ex.work;
     a.am_shard = ex.am_shard;
     a.am_base = ex.am_base;
+    if (t0 + group >= ntok) a.pf = ex.pf;  // the last pass of this site prefetches for the next one
     a.tp_mode = ex.tp_mode;
     if (ex.tp_mode) {
       for (int r = 0; r < 8; ++r) a.tp_base[r] = ex.tp->base[r];
@@ -895,6 +900,36 @@ int enqueue_forward(Session* s, uint32_t n, uint32_t start_pos, bool from_state,
   YL_LAUNCH(k::embed(m->emb.fmt == YL_Q8_0 ? k::FMT_Q8 : m->emb.fmt == YL_Q4_0 ? k::FMT_Q4 : k::FMT_F16, m->emb.q,
                      m->emb.s, m->emb.row_bytes, m->emb.scale_row_bytes, d, sh.vocab_size, s->tok, st, n, s->x, lc));
   const bool decode = n == 1;
+  // Decode streams every weight once per token. Each weight-streaming launch
+  // (and the attention kernel, during which HBM would idle) prefetches into
+  // L2 the first rows the next weight-streaming launch reads, aimed at that
+  // launch's own schedule (its CTAs' static ranges, or its first row sets).
+  const uint32_t mv_grid = (uint32_t)m->num_sms * tunables().grid_mult;
+  auto pf_for = [&](const DevWeight& w, int epi, bool has_work) {
+    k::L2Prefetch p;
+    const uint64_t budget = tunables().pf_bytes;
+    if (!decode || budget == 0 || !w.q || w.rows == 0) return p;
+    uint32_t g;
+    bool dyn;
+    k::matvec_schedule(w.rows, epi, mv_grid, 1, has_work, &g, &dyn);
+    if (g == 0) return p;
+    const uint64_t per_row = (uint64_t)w.row_bytes + w.scale_row_bytes;
+    const uint64_t rows = std::min<uint64_t>(w.rows, std::max<uint64_t>(1, budget / per_row));
+    p.q = w.q;
+    p.s = w.s;
+    p.rows = w.rows;
+    p.row_bytes = w.row_bytes;
+    p.srow_bytes = w.scale_row_bytes;
+    p.unit = (epi == k::EPI_SWIGLU || epi == k::EPI_SWIGLU_Q8) ? 2u : 1u;
+    p.dyn = dyn ? 1u : 0u;
+    p.slots = dyn ? mv_grid : g;
+    uint64_t each = (rows + p.slots - 1) / p.slots;
+    if (dyn) each = round_up(each, k::MV_ROWSET);
+    p.rows_each = (uint32_t)each;
+    return p;
+  };
+  const int epi_ffn = f32act ? k::EPI_SWIGLU : k::EPI_SWIGLU_Q8;
+  const int epi_res = tp ? k::EPI_STORE : k::EPI_ADD;
   MvExtra norm;
   norm.pro = k::PRO_NORM;
   norm.xres = s->x;
@@ -944,6 +979,7 @@ int enqueue_forward(Session* s, uint32_t n, uint32_t start_pos, bool from_state,
     norm.work = nullptr;
     norm.xres = xcur;
     norm.tp_mode = 0;
+    norm.pf = pf_for(L.wo, epi_res, false);
     if (tp_push && l > 0) tp_pull(norm, 2 * (l - 1) + 1);
     if ((rc = run_matvec_ex(L.wqkv, f32act, nullptr, nullptr, nullptr, d, d / 32, n, s->qkv, att + 2 * kvd,
                             k::EPI_STORE, 0, s->err, s->stream, pdl, m->num_sms, norm, &nl)))
@@ -966,8 +1002,11 @@ int enqueue_forward(Session* s, uint32_t n, uint32_t start_pos, bool from_state,
       ad.pos0 = start_pos;
       ad.scale = m->attn_scale;
       ad.n_splits = s->n_splits;
+      ad.sc = s->part;
+      ad.sc_stride = s->part_stride;
       ad.early_kv = from_state ? 1 : 0;
       ad.trace = YL_TRACE();
+      ad.pf = pf_for(L.w13, epi_ffn, true);
       ad.out = f32act ? s->xf : nullptr;
       ad.q8 = f32act ? nullptr : s->xq;
       ad.s8 = s->xs;
@@ -988,7 +1027,9 @@ int enqueue_forward(Session* s, uint32_t n, uint32_t start_pos, bool from_state,
       aa.pos0 = start_pos;
       aa.scale = m->attn_scale;
       aa.n_splits = 1;
-      aa.part = s->part;
+      if (s->ascr_floats < k::attention_scratch_floats(n, m->l_heads, start_pos))
+        return fail(YL_ERR_ARG, "attention scratch not sized for this pass");
+      aa.part = s->ascr;
       aa.out = f32act ? s->xf : nullptr;
       aa.q8 = f32act ? nullptr : s->xq;
       aa.s8 = s->xs;
@@ -996,10 +1037,12 @@ int enqueue_forward(Session* s, uint32_t n, uint32_t start_pos, bool from_state,
     }
     // wo projection + residual add (tensor-parallel: this rank's partial
     // sums, all-reduced over peer memory into the replicated residual)
+    plain.pf = pf_for(L.w13, epi_ffn, true);
     if (tp_push) {
       MvExtra px;
       tp_push_ex(px, 2 * l);
       px.trace = YL_TRACE();
+      px.pf = plain.pf;
       if ((rc = run_matvec_ex(L.wo, f32act, s->xq, s->xs, s->xf, att, att / 32, n, own_inbox(2 * l), d, k::EPI_STORE,
                               0, s->err, s->stream, pdl, m->num_sms, px, &nl)))
         return rc;
@@ -1026,6 +1069,7 @@ int enqueue_forward(Session* s, uint32_t n, uint32_t start_pos, bool from_state,
     norm.work = decode ? s->work + 2ull * l : nullptr;  // one launch per step at this site
     norm.xres = xcur;
     norm.tp_mode = 0;
+    norm.pf = pf_for(L.w2, epi_res, false);
     if (tp_push) tp_pull(norm, 2 * l);
     if ((rc = run_matvec_ex(L.w13, f32act, nullptr, nullptr, nullptr, d, d / 32, n, s->h, f,
                             f32act ? k::EPI_SWIGLU : k::EPI_SWIGLU_Q8, 0, s->err, s->stream, pdl, m->num_sms, norm,
@@ -1034,10 +1078,13 @@ int enqueue_forward(Session* s, uint32_t n, uint32_t start_pos, bool from_state,
     YL_MARK();
     if (norm.tp_mode == 2) std::swap(xcur, xalt);
     // down projection + residual add
+    plain.pf = l + 1 < sh.n_layers ? pf_for(m->layers[l + 1].wqkv, k::EPI_STORE, false)
+                                   : pf_for(m->lm, k::EPI_ARGMAX, true);
     if (tp_push) {
       MvExtra px;
       tp_push_ex(px, 2 * l + 1);
       px.trace = YL_TRACE();
+      px.pf = plain.pf;
       if ((rc = run_matvec_ex(L.w2, f32act, s->hq, s->hs, s->h, f, f / 32, n, own_inbox(2 * l + 1), d, k::EPI_STORE, 0,
                               s->err, s->stream, pdl, m->num_sms, px, &nl)))
         return rc;
@@ -1068,6 +1115,7 @@ int enqueue_forward(Session* s, uint32_t n, uint32_t start_pos, bool from_state,
     fin.state = (from_state && !tp) ? s->state : nullptr;
     fin.trace = YL_TRACE();
     fin.work = s->work + 2ull * sh.n_layers;  // lm_head: one launch per forward
+    fin.pf = pf_for(m->layers[0].wqkv, k::EPI_STORE, false);  // the next decode step starts there
     // tensor-parallel: this rank's vocabulary rows; the winner is published
     // in the exchange region and combined across ranks
     fin.am_shard = tp ? (float*)(s->tp_region + s->tp_lm_off) : nullptr;
@@ -1106,6 +1154,16 @@ int forward(Session* s, const uint32_t* tokens_host, uint32_t n, uint32_t start_
     const uint32_t nc = std::min(chunk, n - t0);
     int rc = ensure_cap(s, nc);
     if (rc) return rc;
+    // multi-token attention keeps every (row, head) weight row of the pass
+    const uint64_t need = nc > 1 ? k::attention_scratch_floats(nc, s->m->l_heads, start_pos + t0) : 0;
+    if (need > s->ascr_floats) {
+      YL_CUDA_TRY(cudaStreamSynchronize(s->stream));
+      if (s->ascr) cudaFree(s->ascr);
+      s->ascr = nullptr;
+      s->ascr_floats = 0;
+      YL_CUDA_TRY(cudaMalloc(&s->ascr, need * 4));
+      s->ascr_floats = need;
+    }
     YL_CUDA_TRY(cudaMemcpyAsync(s->tok, tokens_host + t0, (uint64_t)nc * 4, cudaMemcpyHostToDevice, s->stream));
     rc = enqueue_forward(s, nc, start_pos + t0, false, tunables().pdl, nullptr, want_logits && t0 + nc == n);
     if (rc) return rc;

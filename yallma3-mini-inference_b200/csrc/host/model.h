@@ -76,7 +76,10 @@ struct Session {
   unsigned int* work = nullptr;    // [n_layers + 1][2] dynamic row-set counters (decode gate/up, lm_head)
   uint32_t* tok = nullptr;  // [cap]
   float* logits = nullptr;  // [vocab]
-  float* part = nullptr;    // attention split partials (general path)
+  float* part = nullptr;    // decode attention scores / weights [local heads][part_stride]
+  uint32_t part_stride = 0;
+  float* ascr = nullptr;    // multi-token attention scores / weights (grown on demand)
+  uint64_t ascr_floats = 0;
   float* am_val = nullptr;            // lm_head per-CTA winners
   uint32_t* am_idx = nullptr;
   unsigned int* am_count = nullptr;
@@ -144,6 +147,7 @@ struct Tunables {
   bool gemm = true;          // multi-token passes on the int8 tensor-core GEMM
   uint32_t gemm_min = 16;    // from this many tokens (below, the matvec re-reading weights per 8 is faster)
   bool tp_fused = true;      // tensor-parallel decode: exchange fused into the projections (else exchange kernels)
+  uint64_t pf_bytes = 24ull << 20;  // decode: L2 prefetch of the next matrix's first bytes per launch (YL_PF_MB)
 };
 const Tunables& tunables();
 // Launches the matvec for `ntok` tokens (groups of 8) with activations x*.
@@ -177,6 +181,7 @@ struct MvExtra {
   uint64_t tp_inbox_off = 0;
   uint32_t tp_site = 0, tp_nsites = 0;
   float* tp_xout = nullptr;
+  k::L2Prefetch pf;              // the next weight-streaming launch's first rows (decode)
 };
 int run_matvec_ex(const DevWeight& w, bool f32act, const int8_t* xq, const float* xs, const float* xf,
                   uint64_t x_stride, uint64_t xs_stride, uint32_t ntok, float* out, uint64_t out_stride, int epi,

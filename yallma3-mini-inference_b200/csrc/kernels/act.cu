@@ -29,39 +29,28 @@ cudaError_t quantize_q8(const float* x, int8_t* q, float* s, uint64_t nblocks, c
 }
 
 // util.rs:389-426: ss = sum x^2; ss /= n; ss += eps; ss = 1/sqrt(ss);
-// y = w * (ss * x); then the Q8_0 quantizer on y (forward.rs:155-160). The
-// sum-of-squares order differs from the reference's 8-lane fold (f32
-// rounding only); everything after it is the same sequence of IEEE ops.
+// y = w * (ss * x); then the Q8_0 quantizer on y (forward.rs:155-160). Every
+// step is the reference's sequence of IEEE f32 operations, the sum of squares
+// in its 8-lane order (rms_factors_exact), so y and its Q8_0 blocks are
+// bit-identical. One CTA per 16 rows: warp 0 walks the 16 addition chains,
+// then all warps normalize and quantize.
+constexpr uint32_t RQ_ROWS = 16;
 __global__ void __launch_bounds__(256) rmsnorm_quant_kernel(const float* __restrict__ x, const float* __restrict__ w,
-                                                            uint32_t dim, float eps, int8_t* __restrict__ q,
-                                                            float* __restrict__ s, float* __restrict__ y) {
+                                                            uint32_t ntok, uint32_t dim, float eps,
+                                                            int8_t* __restrict__ q, float* __restrict__ s,
+                                                            float* __restrict__ y) {
   grid_dep_launch();
   grid_dep_wait();
-  __shared__ float red[8];
-  const uint32_t t = blockIdx.x;
-  const float* xr = x + (uint64_t)t * dim;
+  __shared__ float rf[RQ_ROWS];
+  const uint32_t t0 = blockIdx.x * RQ_ROWS, nt = min(RQ_ROWS, ntok - t0);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float ss = 0.0f;
-  for (uint32_t i = threadIdx.x * 4; i < dim; i += 256 * 4) {
-    const float4 v = *reinterpret_cast<const float4*>(xr + i);
-    ss = fmaf(v.x, v.x, ss);
-    ss = fmaf(v.y, v.y, ss);
-    ss = fmaf(v.z, v.z, ss);
-    ss = fmaf(v.w, v.w, ss);
-  }
-  ss = warp_sum(ss);
-  if (lane == 0) red[warp] = ss;
+  if (warp == 0) rms_factors_exact(x + (uint64_t)t0 * dim, dim, nt, dim, eps, rf, lane);
   __syncthreads();
-  float tot = 0.0f;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) tot += red[i];
-  float r = __fdiv_rn(tot, (float)dim);
-  r = __fadd_rn(r, eps);
-  r = __fdiv_rn(1.0f, __fsqrt_rn(r));
   const uint32_t nb = dim / 32;
-  for (uint32_t b = warp; b < nb; b += 8) {
+  for (uint32_t tb = warp; tb < nt * nb; tb += 8) {
+    const uint32_t t = t0 + tb / nb, b = tb % nb;
     const uint32_t k = b * 32 + lane;
-    const float yv = __fmul_rn(w[k], __fmul_rn(r, xr[k]));
+    const float yv = __fmul_rn(w[k], __fmul_rn(rf[tb / nb], x[(uint64_t)t * dim + k]));
     if (y) y[(uint64_t)t * dim + k] = yv;
     if (q) {
       float sc;
@@ -75,7 +64,9 @@ __global__ void __launch_bounds__(256) rmsnorm_quant_kernel(const float* __restr
 cudaError_t rmsnorm_quant(const float* x, const float* w, uint32_t ntok, uint32_t dim, float eps, int8_t* q,
                           float* s, float* y, const LaunchCfg& lc) {
   if (ntok == 0) return cudaSuccess;
-  return launch_kernel(rmsnorm_quant_kernel, dim3(ntok), dim3(256), 0, lc, x, w, dim, eps, q, s, y);
+  if (dim % 32) return cudaErrorInvalidValue;
+  return launch_kernel(rmsnorm_quant_kernel, dim3((ntok + RQ_ROWS - 1) / RQ_ROWS), dim3(256), 0, lc, x, w, ntok, dim,
+                       eps, q, s, y);
 }
 
 // Embedding gather: x[t][k] = value of row tokens[t] (exact: int8 * f16 scale

@@ -1,4 +1,22 @@
 // RoPE + KV-cache write and causal GQA attention over the f32 KV cache.
+//
+// Attention reproduces forward.rs:299-400 operation for operation, so its
+// output is bit-identical to the reference's (the model is chaotic enough
+// that any other rounding would eventually change a greedy token):
+//   score[t2] = dot8(q, k[t2]) * scale     eight lane accumulators, lane l
+//                                          taking q[8s+l]*k[8s+l] in order,
+//                                          folded ((l0+l4)+(l2+l6))+((l1+l5)+(l3+l7))
+//   max      = max(-1e10, scores)          order-free
+//   e[t2]    = exp(score[t2] - max)        the correctly rounded exp (yl_expf)
+//   sum      = ((0 + e[0]) + e[1]) + ...   one chain in position order
+//   p[t2]    = e[t2] * (sum > 0 ? 1/sum : 0)
+//   out[d]   = reduce(lanes), lane l summing p[8c+l]*v[8c+l][d] over
+//              c < seq_len/8 in order, then + p*v for the seq_len % 8 tail
+// Masked positions (t2 > the query's position) have e = 0 and p = 0 and add
+// exactly nothing, so they are skipped; the lane / tail split still follows
+// the batch's seq_len. The sequential sum and the P.V lanes are what the
+// kernels' latency is built around: every chain runs in one thread, and the
+// work around them is spread over the CTA (or the cluster, for decode).
 #include <cooperative_groups.h>
 #include <float.h>
 
@@ -59,234 +77,58 @@ cudaError_t rope_kv(const float* qkv, uint32_t ntok, uint32_t n_heads, uint32_t 
                        cs, state, pos0, q_out, kcache, vcache);
 }
 
-constexpr int AT_THREADS = 128;
-constexpr int AT_TILE = 64;
 constexpr int AT_MAXKV = 8;  // max query heads per KV head
 
-template <int HD>
-struct AttnSmem {
-  float qs[AT_MAXKV][HD];
-  float ps[AT_MAXKV][AT_TILE];
-  float os[AT_MAXKV][HD];
-  float ms[AT_MAXKV], ls[AT_MAXKV], cr[AT_MAXKV];
-};
+// wide::f32x8::reduce_add as the oracle restates it.
+__device__ __forceinline__ float reduce_add8(float l0, float l1, float l2, float l3, float l4, float l5, float l6,
+                                             float l7) {
+  const float a0 = __fadd_rn(l0, l4), a1 = __fadd_rn(l1, l5), a2 = __fadd_rn(l2, l6), a3 = __fadd_rn(l3, l7);
+  return __fadd_rn(__fadd_rn(a0, a2), __fadd_rn(a1, a3));
+}
 
-// Online-softmax attention of the kv_mul query heads in sm.qs over keys
-// [p_begin, p_end) of one KV head: s = (q.k)*scale (forward.rs:328-346),
-// exp(s - max), o = sum p*V (forward.rs:368-399), kept unnormalized in
-// (sm.ms, sm.ls, sm.os). The kv_mul heads share every K/V row read.
+// dot8 of forward.rs:332-343 over HD floats (both 16-byte aligned).
 template <int HD>
-__device__ __forceinline__ void attn_tiles(AttnSmem<HD>& sm, const float* kc, const float* vc, uint32_t kv_dim,
-                                           uint32_t kvh, uint32_t kv_mul, float scale, uint32_t p_begin,
-                                           uint32_t p_end) {
-  constexpr int E = HD / 32;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (uint32_t p0 = p_begin; p0 < p_end; p0 += AT_TILE) {
-    const uint32_t tn = min((uint32_t)AT_TILE, p_end - p0);
-    for (uint32_t pp = warp; pp < tn; pp += AT_THREADS / 32) {
-      const float* kr = kc + (uint64_t)(p0 + pp) * kv_dim + kvh * HD + lane * E;
-      float kv[E];
-      if (E == 4) {
-        const float4 v = *reinterpret_cast<const float4*>(kr);
-        kv[0] = v.x; kv[1] = v.y; kv[2] = v.z; kv[3] = v.w;
-      } else {
+__device__ __forceinline__ float dot8_exact(const float* q, const float* k) {
+  float l0 = 0.0f, l1 = 0.0f, l2 = 0.0f, l3 = 0.0f, l4 = 0.0f, l5 = 0.0f, l6 = 0.0f, l7 = 0.0f;
 #pragma unroll
-        for (int e = 0; e < E; ++e) kv[e] = kr[e];
-      }
-      for (uint32_t hh = 0; hh < kv_mul; ++hh) {
-        float s = 0.0f;
+  for (int s = 0; s < HD / 8; ++s) {
+    const float4 qa = *reinterpret_cast<const float4*>(q + 8 * s);
+    const float4 qb = *reinterpret_cast<const float4*>(q + 8 * s + 4);
+    const float4 ka = *reinterpret_cast<const float4*>(k + 8 * s);
+    const float4 kb = *reinterpret_cast<const float4*>(k + 8 * s + 4);
+    l0 = __fadd_rn(l0, __fmul_rn(qa.x, ka.x));
+    l1 = __fadd_rn(l1, __fmul_rn(qa.y, ka.y));
+    l2 = __fadd_rn(l2, __fmul_rn(qa.z, ka.z));
+    l3 = __fadd_rn(l3, __fmul_rn(qa.w, ka.w));
+    l4 = __fadd_rn(l4, __fmul_rn(qb.x, kb.x));
+    l5 = __fadd_rn(l5, __fmul_rn(qb.y, kb.y));
+    l6 = __fadd_rn(l6, __fmul_rn(qb.z, kb.z));
+    l7 = __fadd_rn(l7, __fmul_rn(qb.w, kb.w));
+  }
+  return reduce_add8(l0, l1, l2, l3, l4, l5, l6, l7);
+}
+
+// The softmax denominator chain over w[0..n) (global, 16-byte aligned),
+// returning 1/sum (0 when the sum is not positive). Loads run ahead of the
+// dependent additions.
+__device__ __forceinline__ float softmax_inv(const float* w, uint32_t n) {
+  float s = 0.0f;
+  uint32_t i = 0;
+  for (; i + 16 <= n; i += 16) {
+    float4 v[4];
 #pragma unroll
-        for (int e = 0; e < E; ++e) s = fmaf(sm.qs[hh][lane * E + e], kv[e], s);
-        s = warp_sum(s);
-        if (lane == 0) sm.ps[hh][pp] = __fmul_rn(s, scale);
-      }
-    }
-    __syncthreads();
-    for (uint32_t hh = warp; hh < kv_mul; hh += AT_THREADS / 32) {
-      float mx = -INFINITY;
-      for (uint32_t pp = lane; pp < tn; pp += 32) mx = fmaxf(mx, sm.ps[hh][pp]);
-      mx = warp_max(mx);
-      const float m_old = sm.ms[hh];
-      const float m_new = fmaxf(m_old, mx);
-      float sum = 0.0f;
-      for (uint32_t pp = lane; pp < tn; pp += 32) {
-        const float e = expf(sm.ps[hh][pp] - m_new);
-        sm.ps[hh][pp] = e;
-        sum += e;
-      }
-      sum = warp_sum(sum);
-      if (lane == 0) {
-        const float c = expf(m_old - m_new);
-        sm.cr[hh] = c;
-        sm.ls[hh] = sm.ls[hh] * c + sum;
-        sm.ms[hh] = m_new;
-      }
-    }
-    __syncthreads();
-    for (uint32_t i = threadIdx.x; i < kv_mul * HD; i += AT_THREADS) {
-      const uint32_t hh = i / HD, d = i % HD;
-      float o = sm.os[hh][d] * sm.cr[hh];
-      const float* vr = vc + (uint64_t)p0 * kv_dim + kvh * HD + d;
-      for (uint32_t pp = 0; pp < tn; ++pp) o = fmaf(sm.ps[hh][pp], vr[(uint64_t)pp * kv_dim], o);
-      sm.os[hh][d] = o;
-    }
-    __syncthreads();
-  }
-}
-
-// Writes one finished head: f32 and/or Q8_0 blocks (forward.rs:191 quantizes
-// the attention output; head_size is a multiple of 32, so a head's blocks
-// never straddle heads).
-template <int HD>
-__device__ __forceinline__ void attn_emit(float* out, int8_t* q8, float* s8, uint64_t base, const float* o_head) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int b = warp; b < HD / 32; b += AT_THREADS / 32) {
-    const float v = o_head[b * 32 + lane];
-    const uint64_t k = base + b * 32 + lane;
-    if (out) out[k] = v;
-    if (q8) {
-      float sc;
-      const int8_t qv = quant_q8_lane(v, &sc);
-      q8[k] = qv;
-      if (lane == 0) s8[k / 32] = sc;
-    }
-  }
-}
-
-// Prefill / general path. One CTA: KV head blockIdx.x, query token
-// blockIdx.y, key split blockIdx.z (q already rotated, cache already written).
-template <int HD>
-__global__ void __launch_bounds__(AT_THREADS) attn_kernel(AttnArgs a) {
-  grid_dep_launch();
-  grid_dep_wait();
-  __shared__ AttnSmem<HD> sm;
-  const uint32_t kvh = blockIdx.x, t = blockIdx.y, sp = blockIdx.z;
-  const uint32_t kv_mul = a.n_heads / a.n_kv_heads;
-  const uint32_t pos0 = a.state ? (uint32_t)a.state->pos : a.pos0;
-  const uint32_t nvis = pos0 + t + 1;  // causal: keys 0..abs_pos
-  const uint32_t chunk = (nvis + a.n_splits - 1) / a.n_splits;
-  const uint32_t p_begin = min(nvis, sp * chunk), p_end = min(nvis, p_begin + chunk);
-  const uint32_t att = a.n_heads * HD;
-  for (uint32_t i = threadIdx.x; i < kv_mul * HD; i += AT_THREADS) {
-    const uint32_t hh = i / HD, d = i % HD;
-    sm.qs[hh][d] = a.q[(uint64_t)t * att + (kvh * kv_mul + hh) * HD + d];
-    sm.os[hh][d] = 0.0f;
-  }
-  if (threadIdx.x < kv_mul) {
-    sm.ms[threadIdx.x] = -INFINITY;
-    sm.ls[threadIdx.x] = 0.0f;
-  }
-  __syncthreads();
-  attn_tiles<HD>(sm, a.kcache, a.vcache, a.kv_dim, kvh, kv_mul, a.scale, p_begin, p_end);
-  if (a.n_splits == 1) {
-    for (uint32_t hh = 0; hh < kv_mul; ++hh) {
-      const float inv = sm.ls[hh] > 0.0f ? 1.0f / sm.ls[hh] : 0.0f;
-      for (uint32_t d = threadIdx.x; d < HD; d += AT_THREADS) sm.os[hh][d] *= inv;
-      __syncthreads();
-      attn_emit<HD>(a.out, a.q8, a.s8, (uint64_t)t * att + (kvh * kv_mul + hh) * HD, sm.os[hh]);
-      __syncthreads();
-    }
-  } else {
-    for (uint32_t i = threadIdx.x; i < kv_mul * (HD + 2); i += AT_THREADS) {
-      const uint32_t hh = i / (HD + 2), j = i % (HD + 2);
-      const uint32_t h = kvh * kv_mul + hh;
-      float* dst = a.part + (((uint64_t)t * a.n_heads + h) * a.n_splits + sp) * (HD + 2);
-      dst[j] = j == 0 ? sm.ms[hh] : (j == 1 ? sm.ls[hh] : sm.os[hh][j - 2]);
-    }
-  }
-}
-
-// Merges the split partials of one (token, head) and emits the output.
-template <int HD>
-__global__ void __launch_bounds__(AT_THREADS) attn_combine_kernel(AttnArgs a) {
-  grid_dep_launch();
-  grid_dep_wait();
-  __shared__ float o[HD];
-  __shared__ float wgt[64];
-  __shared__ float inv_l;
-  const uint32_t h = blockIdx.x, t = blockIdx.y;
-  const float* base = a.part + ((uint64_t)t * a.n_heads + h) * a.n_splits * (HD + 2);
-  if (threadIdx.x < 32) {
-    float M = -INFINITY;
-    for (uint32_t s = threadIdx.x; s < a.n_splits; s += 32) M = fmaxf(M, base[s * (HD + 2)]);
-    M = warp_max(M);
-    float L = 0.0f;
-    for (uint32_t s = threadIdx.x; s < a.n_splits; s += 32) {
-      const float m = base[s * (HD + 2)];
-      const float w = m == -INFINITY ? 0.0f : expf(m - M);
-      wgt[s] = w;
-      L += base[s * (HD + 2) + 1] * w;
-    }
-    L = warp_sum(L);
-    if (threadIdx.x == 0) inv_l = L > 0.0f ? 1.0f / L : 0.0f;
-  }
-  __syncthreads();
-  for (uint32_t d = threadIdx.x; d < HD; d += AT_THREADS) {
-    float acc = 0.0f;
-    for (uint32_t s0 = 0; s0 < a.n_splits; s0 += 8) {  // 8 independent loads in flight
-      float v[8];
+    for (int u = 0; u < 4; ++u) v[u] = __ldcg(reinterpret_cast<const float4*>(w + i) + u);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) v[j] = s0 + j < a.n_splits ? base[(s0 + j) * (HD + 2) + 2 + d] : 0.0f;
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-        if (s0 + j < a.n_splits) acc = fmaf(v[j], wgt[s0 + j], acc);
+    for (int u = 0; u < 4; ++u) {
+      s = __fadd_rn(s, v[u].x);
+      s = __fadd_rn(s, v[u].y);
+      s = __fadd_rn(s, v[u].z);
+      s = __fadd_rn(s, v[u].w);
     }
-    o[d] = acc * inv_l;
   }
-  __syncthreads();
-  attn_emit<HD>(a.out, a.q8, a.s8, (uint64_t)t * a.n_heads * HD + h * HD, o);
+  for (; i < n; ++i) s = __fadd_rn(s, __ldcg(w + i));
+  return s > 0.0f ? __fdiv_rn(1.0f, s) : 0.0f;
 }
-
-cudaError_t attention(const AttnArgs& a, const LaunchCfg& lc) {
-  if (a.ntok == 0) return cudaSuccess;
-  const uint32_t kv_mul = a.n_heads / a.n_kv_heads;
-  if (kv_mul > AT_MAXKV || a.n_splits == 0 || a.n_splits > 64) return cudaErrorInvalidValue;
-  if (a.n_splits == 1 && a.ntok >= 32 && attention_prefill_ok(a)) return attention_prefill(a, lc);
-  dim3 g(a.n_kv_heads, a.ntok, a.n_splits);
-  cudaError_t e;
-  if (a.head_size == 64) e = launch_kernel(attn_kernel<64>, g, dim3(AT_THREADS), 0, lc, a);
-  else if (a.head_size == 128) e = launch_kernel(attn_kernel<128>, g, dim3(AT_THREADS), 0, lc, a);
-  else return cudaErrorInvalidValue;
-  if (e != cudaSuccess || a.n_splits == 1) return e;
-  dim3 gc(a.n_heads, a.ntok);
-  if (a.head_size == 64) return launch_kernel(attn_combine_kernel<64>, gc, dim3(AT_THREADS), 0, lc, a);
-  return launch_kernel(attn_combine_kernel<128>, gc, dim3(AT_THREADS), 0, lc, a);
-}
-
-// ---------------------------------------------------------------------------
-// Batch-1 decode, built for latency (the KV bytes of one decode step are a few
-// MB; the cost is the dependent chain). One cluster of n_splits CTAs per KV
-// head; CTA `rank` of the cluster takes the rank-th slice of the keys:
-//  * the slice's K and V rows are fetched with cp.async in one round trip
-//    (before the wait on the preceding kernel when early_kv is set), while q
-//    (and, in the CTA owning position `pos`, the new key and value rows) is
-//    read from the fused projection output and rotated (RoPE);
-//  * the owner writes the new K/V rows to the cache and into its tile;
-//  * each warp runs attention over its positions in registers (see the
-//    kernel), the CTA combines its eight warp partials;
-//  * every CTA pushes its (max, sum, unnormalized output) partial of each
-//    32-block of the KV head's output into the CTA that merges that block
-//    (distributed shared memory); after one cluster barrier each CTA merges
-//    and quantizes its blocks from its own shared memory.
-namespace cg = cooperative_groups;
-constexpr int AD_TILE = 64;      // positions per shared-memory tile
-constexpr int AD_THREADS = 256;
-constexpr int AD_MAXCS = 16;     // largest cluster (non-portable size)
-constexpr int AD_MAXSLOT = 4;    // output 32-blocks a CTA merges: kv_mul*HD/32/cs <= 8*128/32/8
-
-template <int HD>
-struct AdLayout {
-  static constexpr int ROW = HD + 4;             // padded row (floats): 16-byte aligned
-  static constexpr int KS = 0;
-  static constexpr int VS = KS + AD_TILE * ROW;
-  static constexpr int WO = KS;                             // [8 warps][AT_MAXKV][HD] warp partials (after the tiles)
-  static constexpr int QS = VS + AD_TILE * ROW;             // [AT_MAXKV][HD] rotated q
-  static constexpr int NK = QS + AT_MAXKV * HD;             // owner: new key (rotated) and value rows [2][HD]
-  static constexpr int WS = NK + 2 * HD;                    // [8][AT_MAXKV] warp max, then [8][AT_MAXKV] warp sum
-  static constexpr int RECV = WS + 2 * 8 * AT_MAXKV;        // [AD_MAXSLOT][AD_MAXCS][34] pushed block partials
-  static constexpr int TOTAL = RECV + AD_MAXSLOT * AD_MAXCS * 34;
-  static_assert(8 * AT_MAXKV * HD <= 2 * AD_TILE * ROW, "warp partials fit the tile area");
-};
 
 __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
@@ -295,38 +137,223 @@ __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
 }
 
-// At most 96 registers a thread: then an attention CTA (8 warps) and a
-// matvec CTA (9 warps, 96 registers) fit one SM together, two plus three
-// warps per sub-partition within its 16K registers, so the next projection's
-// CTAs become resident and stream their weights while attention runs.
-//
-// Per CTA: warp w takes the positions w, w+8, ... of each key tile; lane j
-// holds dims [j*E, j*E+E) of q, k, v and of its running output for all KVM
-// heads, so a position costs one k and one v load per lane, a butterfly
-// per head for the score, and an online-softmax update in registers
-// (forward.rs:328-399). The eight warp partials are combined once per CTA.
+// ---------------------------------------------------------------------------
+// General attention (any batch): one CTA per (query head, block of AE_QB
+// query rows); the rows share every K and V tile.
+constexpr int AE_QB = 16;
+constexpr int AE_TILE = 64;
+constexpr int AE_THREADS = 256;
+
+template <int HD>
+struct AeSmem {
+  float q[AE_QB][HD];
+  float kv[AE_TILE][HD + 4];  // K tile, then V tile, then the output rows
+  float w[AE_QB][AE_TILE];    // the tile's weights p
+  float wmax[AE_THREADS / 32][4];
+  float mx[AE_QB], inv[AE_QB];
+};
+
+template <int HD>
+__global__ void __launch_bounds__(AE_THREADS) attn_exact_kernel(AttnArgs a) {
+  extern __shared__ __align__(16) uint8_t ae_raw[];
+  AeSmem<HD>& sm = *reinterpret_cast<AeSmem<HD>*>(ae_raw);
+  grid_dep_launch();
+  grid_dep_wait();
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t qh = blockIdx.x, kv_mul = a.n_heads / a.n_kv_heads, kvh = qh / kv_mul;
+  const uint32_t pos0 = a.state ? (uint32_t)a.state->pos : a.pos0;
+  const uint32_t r0 = blockIdx.y * AE_QB, nr = min((uint32_t)AE_QB, a.ntok - r0);
+  const uint32_t seq = pos0 + a.ntok;           // the batch's seq_len
+  const uint32_t nvis = pos0 + r0 + nr;         // keys any row of this CTA sees
+  const uint32_t att = a.n_heads * HD;
+  const float* kb = a.kcache + kvh * HD;
+  const float* vb = a.vcache + kvh * HD;
+  const uint64_t sstride = attention_scratch_stride(a.ntok, pos0);
+  auto wrow = [&](uint32_t r) { return a.part + ((uint64_t)(r0 + r) * a.n_heads + qh) * sstride; };
+
+  for (uint32_t i = tid; i < nr * HD / 4; i += AE_THREADS) {
+    const uint32_t r = i / (HD / 4), c = i % (HD / 4);
+    reinterpret_cast<float4*>(sm.q[r])[c] = reinterpret_cast<const float4*>(a.q + (uint64_t)(r0 + r) * att + qh * HD)[c];
+  }
+  // ---- scores, running maxima (rows tid/64 + 4m, m = 0..3) ----
+  float rmax[4] = {-1e10f, -1e10f, -1e10f, -1e10f};
+  for (uint32_t t0 = 0; t0 < nvis; t0 += AE_TILE) {
+    const uint32_t tn = min((uint32_t)AE_TILE, nvis - t0);
+    __syncthreads();  // the tile area is free
+    for (uint32_t i = tid; i < tn * (HD / 4); i += AE_THREADS) {
+      const uint32_t j = i / (HD / 4), c = i % (HD / 4);
+      cp_async16(&sm.kv[j][4 * c], kb + (uint64_t)(t0 + j) * a.kv_dim + 4 * c);
+    }
+    cp_async_wait_all();
+    __syncthreads();
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      const uint32_t r = tid / AE_TILE + 4 * m, j = tid % AE_TILE;
+      const uint32_t t2 = t0 + j;
+      if (r < nr && j < tn && t2 <= pos0 + r0 + r) {
+        const float s = __fmul_rn(dot8_exact<HD>(sm.q[r], sm.kv[j]), a.scale);
+        wrow(r)[t2] = s;
+        rmax[m] = fmaxf(rmax[m], s);
+      }
+    }
+  }
+#pragma unroll
+  for (int m = 0; m < 4; ++m) {
+    const float v = warp_max(rmax[m]);
+    if (lane == 0) sm.wmax[warp][m] = v;
+  }
+  __syncthreads();
+  if (tid < AE_QB) {  // row r's maxima sit in warps 2(r%4), 2(r%4)+1, slot r/4
+    const uint32_t r = tid;
+    sm.mx[r] = fmaxf(sm.wmax[2 * (r % 4)][r / 4], sm.wmax[2 * (r % 4) + 1][r / 4]);
+  }
+  __syncthreads();
+  // ---- e = exp(s - max) ----
+  for (uint32_t r = 0; r < nr; ++r) {
+    float* w = wrow(r);
+    const uint32_t n = pos0 + r0 + r + 1;
+    for (uint32_t t2 = tid; t2 < n; t2 += AE_THREADS) w[t2] = yl_expf(__fsub_rn(w[t2], sm.mx[r]));
+  }
+  __syncthreads();
+  // ---- the sums, one chain per row ----
+  if (tid < (int)nr) sm.inv[tid] = softmax_inv(wrow(tid), pos0 + r0 + tid + 1);
+  __syncthreads();
+  // ---- P.V: thread (row tid/16, dims (tid%16)*DPT + j), eight lanes each ----
+  constexpr int DPT = HD / 16;
+  const uint32_t r = tid / 16, g = tid % 16;
+  const uint32_t lim = min(seq / 8 * 8, pos0 + r0 + r + 1);  // lane-range keys of this row
+  float acc[DPT][8];
+#pragma unroll
+  for (int j = 0; j < DPT; ++j)
+#pragma unroll
+    for (int l = 0; l < 8; ++l) acc[j][l] = 0.0f;
+  const uint32_t lane_end = min(seq / 8 * 8, nvis);
+  for (uint32_t t0 = 0; t0 < lane_end; t0 += AE_TILE) {
+    const uint32_t tn = min((uint32_t)AE_TILE, lane_end - t0);
+    __syncthreads();
+    for (uint32_t i = tid; i < tn * (HD / 4); i += AE_THREADS) {
+      const uint32_t j = i / (HD / 4), c = i % (HD / 4);
+      cp_async16(&sm.kv[j][4 * c], vb + (uint64_t)(t0 + j) * a.kv_dim + 4 * c);
+    }
+    for (uint32_t i = tid; i < AE_QB * AE_TILE; i += AE_THREADS) {
+      const uint32_t rr = i / AE_TILE, j = i % AE_TILE;
+      const uint32_t t2 = t0 + j;
+      sm.w[rr][j] = (rr < nr && j < tn && t2 <= pos0 + r0 + rr) ? __fmul_rn(__ldcg(wrow(rr) + t2), sm.inv[rr]) : 0.0f;
+    }
+    cp_async_wait_all();
+    __syncthreads();
+    if (r < nr) {
+      for (uint32_t j0 = 0; j0 < tn; j0 += 8) {  // t0 and tn are multiples of 8: key t0+j0+l is lane l
+#pragma unroll
+        for (int l = 0; l < 8; ++l) {
+          const uint32_t t2 = t0 + j0 + l;
+          if (t2 >= lim) break;
+          const float p = sm.w[r][j0 + l];
+          const float* vr = &sm.kv[j0 + l][g * DPT];
+#pragma unroll
+          for (int j = 0; j < DPT; ++j) acc[j][l] = __fadd_rn(acc[j][l], __fmul_rn(p, vr[j]));
+        }
+      }
+    }
+  }
+  __syncthreads();  // the tile area now holds the output rows
+  if (r < nr) {
+    const uint32_t pr = pos0 + r0 + r;
+    const float inv = sm.inv[r];
+    const float* w = wrow(r);
+#pragma unroll
+    for (int j = 0; j < DPT; ++j) {
+      float o = reduce_add8(acc[j][0], acc[j][1], acc[j][2], acc[j][3], acc[j][4], acc[j][5], acc[j][6], acc[j][7]);
+      const uint32_t d = g * DPT + j;
+      for (uint32_t t2 = seq / 8 * 8; t2 <= pr; ++t2)  // the seq_len % 8 tail, in order
+        o = __fadd_rn(o, __fmul_rn(__fmul_rn(__ldcg(w + t2), inv), vb[(uint64_t)t2 * a.kv_dim + d]));
+      sm.kv[r][d] = o;
+    }
+  }
+  __syncthreads();
+  for (uint32_t i = warp; i < nr * (HD / 32); i += AE_THREADS / 32) {
+    const uint32_t rr = i / (HD / 32), b = i % (HD / 32);
+    const float v = sm.kv[rr][b * 32 + lane];
+    const uint64_t k = (uint64_t)(r0 + rr) * att + qh * HD + b * 32 + lane;
+    if (a.out) a.out[k] = v;
+    if (a.q8) {
+      float sc;
+      const int8_t q = quant_q8_lane(v, &sc);
+      a.q8[k] = q;
+      if (lane == 0) a.s8[k / 32] = sc;
+    }
+  }
+}
+
+cudaError_t attention(const AttnArgs& a, const LaunchCfg& lc) {
+  if (a.ntok == 0) return cudaSuccess;
+  const uint32_t kv_mul = a.n_kv_heads ? a.n_heads / a.n_kv_heads : 0;
+  if (kv_mul == 0 || kv_mul > AT_MAXKV || !a.part) return cudaErrorInvalidValue;
+  if (a.kv_dim % 4 || ((uintptr_t)a.kcache | (uintptr_t)a.vcache | (uintptr_t)a.q) % 16) return cudaErrorInvalidValue;
+  const dim3 g(a.n_heads, (a.ntok + AE_QB - 1) / AE_QB);
+  if (a.head_size == 64) {
+    const uint32_t smem = sizeof(AeSmem<64>);
+    cudaError_t e = cudaFuncSetAttribute(attn_exact_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    return launch_kernel(attn_exact_kernel<64>, g, dim3(AE_THREADS), smem, lc, a);
+  }
+  if (a.head_size == 128) {
+    const uint32_t smem = sizeof(AeSmem<128>);
+    cudaError_t e = cudaFuncSetAttribute(attn_exact_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    return launch_kernel(attn_exact_kernel<128>, g, dim3(AE_THREADS), smem, lc, a);
+  }
+  return cudaErrorInvalidValue;
+}
+
+// ---------------------------------------------------------------------------
+// Batch-1 decode with RoPE and the KV-cache write fused in. One cluster of cs
+// CTAs per KV head:
+//  1. CTA `rank` takes the rank-th slice of the positions 0..pos: its K rows
+//     are fetched with cp.async (before the wait on the preceding kernel when
+//     early_kv is set: they were written by earlier steps), q of the KVM
+//     query heads is rotated, and the owner of `pos` rotates the new key and
+//     writes the new K/V rows; then the slice's scores go to sc and the
+//     slice's maxima to shared memory;
+//  2. (cluster barrier) every CTA takes the head maxima from its peers'
+//     shared memory and turns its slice's scores into exp(s - max);
+//  3. (cluster barrier) the KV head's KVM*HD outputs are 32-blocks; CTA rank
+//     takes blocks rank, rank + cs, ...: one thread per block walks the
+//     softmax sum chain, then warp l runs lane l of the P.V sums for the
+//     block's 32 dimensions, warp 0 folds the lanes, adds the tail and
+//     quantizes the block.
+namespace cg = cooperative_groups;
+constexpr int AD_TILE = 64;      // positions per shared-memory K tile
+constexpr int AD_THREADS = 256;
+constexpr int AD_MAXCS = 16;     // largest cluster (non-portable size)
+constexpr int AD_MAXSLOT = 4;    // output 32-blocks one CTA takes: KVM*HD/32/cs <= 8*128/32/8
+
+template <int HD>
+struct AdSmem {
+  float ks[AD_TILE][HD + 4];
+  float qs[AT_MAXKV][HD];
+  float nk[HD];                   // owner: the new key, rotated
+  float wmax[AD_THREADS / 32][2];
+  float cmax[AT_MAXKV];           // this CTA's slice maxima (read by the peers)
+  float gmax[AT_MAXKV];
+  float inv[AD_MAXSLOT];
+  float lanes[8][32];             // P.V lane partials of one block
+};
+
 template <int HD, int KVM>
-__global__ void __maxnreg__(96) attn_decode_kernel(AttnDecodeArgs a) {
-  using Lo = AdLayout<HD>;
-  constexpr int E = HD / 32;
-  extern __shared__ __align__(16) float sm[];
+__global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(AttnDecodeArgs a) {
+  extern __shared__ __align__(16) uint8_t ad_raw[];
+  AdSmem<HD>& sm = *reinterpret_cast<AdSmem<HD>*>(ad_raw);
   cg::cluster_group cluster = cg::this_cluster();
-  float* Ks = sm + Lo::KS;
-  float* Vs = sm + Lo::VS;
-  float* qs = sm + Lo::QS;
-  float* nk = sm + Lo::NK;
-  float* wo = sm + Lo::WO;
-  float* wm = sm + Lo::WS;
-  float* wl = wm + 8 * AT_MAXKV;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t cs = a.n_splits;
   const uint32_t rank = cluster.block_rank();
   const uint32_t kvh = blockIdx.x / cs;
-  constexpr uint32_t kv_mul = KVM;
   uint64_t* const trace = (kTrace && a.trace) ? a.trace + (uint64_t)blockIdx.x * 8 : nullptr;
   uint64_t ts[8] = {0, 0, 0, 0, 0, 0, 0, 0};  // timeline stamps, stored at the end
   if (trace && tid == 0) ts[0] = globaltimer();
   grid_dep_launch();
+  if (tid == 0) l2_prefetch_next(a.pf, blockIdx.x, gridDim.x);
   if (!a.early_kv) grid_dep_wait();
   const uint32_t pos = a.state ? (uint32_t)a.state->pos : a.pos0;
   const uint32_t nvis = pos + 1;
@@ -336,13 +363,13 @@ __global__ void __maxnreg__(96) attn_decode_kernel(AttnDecodeArgs a) {
   const bool owner = p_begin <= pos && pos < p_end;
   const float* kbase = a.kcache + kvh * HD;
   const float* vbase = a.vcache + kvh * HD;
+  float* const sc0 = a.sc + (uint64_t)kvh * KVM * a.sc_stride;  // this KV head's query heads
 
   auto issue_tile = [&](uint32_t base, uint32_t n) {
     for (uint32_t i = tid; i < n * (HD / 4); i += AD_THREADS) {
       const uint32_t r = i / (HD / 4), c4 = i % (HD / 4);
       if (base + r == pos) continue;  // the new row is placed from nk
-      cp_async16(Ks + r * Lo::ROW + 4 * c4, kbase + (uint64_t)(base + r) * a.kv_dim + 4 * c4);
-      cp_async16(Vs + r * Lo::ROW + 4 * c4, vbase + (uint64_t)(base + r) * a.kv_dim + 4 * c4);
+      cp_async16(&sm.ks[r][4 * c4], kbase + (uint64_t)(base + r) * a.kv_dim + 4 * c4);
     }
   };
   uint32_t t0 = p_begin, tn = min((uint32_t)AD_TILE, p_end - p_begin);
@@ -350,177 +377,136 @@ __global__ void __maxnreg__(96) attn_decode_kernel(AttnDecodeArgs a) {
   if (a.early_kv) grid_dep_wait();
   if (trace && tid == 0) ts[1] = globaltimer();
 
-  // rotated q of the KVM query heads, and (owner) the new key and value rows,
-  // all from the fused projection output in one round of loads
+  // rotated q of the KVM query heads and (owner) the new key; the owner also
+  // writes the new K/V rows to the cache, visible to the peers after the
+  // first cluster barrier
   const float2* c = a.cs + (uint64_t)pos * half;
-  for (uint32_t i = tid; i < (kv_mul + (owner ? 1u : 0u)) * half; i += AD_THREADS) {
+  for (uint32_t i = tid; i < (KVM + (owner ? 1u : 0u)) * half; i += AD_THREADS) {
     const uint32_t hh = i / half, p = i % half;
     uint32_t i0, i1;
     pair_index(a.rope_mode, p, half, i0, i1);
-    const float* src = hh < kv_mul ? a.qkv + (kvh * kv_mul + hh) * HD : a.qkv + att + kvh * HD;
+    const float* src = hh < KVM ? a.qkv + (kvh * KVM + hh) * HD : a.qkv + att + kvh * HD;
     float r0, r1;
     rotate(src[i0], src[i1], c[p], r0, r1);
-    float* dst = hh < kv_mul ? qs + hh * HD : nk;
+    float* dst = hh < KVM ? sm.qs[hh] : sm.nk;
     dst[i0] = r0;
     dst[i1] = r1;
-  }
-  if (owner) {
-    for (uint32_t d = tid; d < HD; d += AD_THREADS) nk[HD + d] = a.qkv[att + a.kv_dim + kvh * HD + d];
-  }
-  __syncthreads();
-  float qr[KVM][E], acc[KVM][E], m[KVM], l[KVM];
-#pragma unroll
-  for (int h = 0; h < KVM; ++h) {
-#pragma unroll
-    for (int e = 0; e < E; ++e) {
-      qr[h][e] = qs[h * HD + lane * E + e];
-      acc[h][e] = 0.0f;
+    if (hh == KVM) {
+      float* kd = a.kcache + (uint64_t)pos * a.kv_dim + kvh * HD;
+      kd[i0] = r0;
+      kd[i1] = r1;
     }
-    m[h] = -INFINITY;
-    l[h] = 0.0f;
   }
+  if (owner)
+    for (uint32_t d = tid; d < HD; d += AD_THREADS)
+      a.vcache[(uint64_t)pos * a.kv_dim + kvh * HD + d] = a.qkv[att + a.kv_dim + kvh * HD + d];
   if (trace && tid == 0) ts[4] = globaltimer();
 
+  // ---- 1. scores of the slice: thread (head tid/64 + 4m, key tid%64) ----
+  float rmax[2] = {-1e10f, -1e10f};
   const uint32_t ntiles = (p_end - p_begin + AD_TILE - 1) / AD_TILE;
   for (uint32_t ti = 0; ti < ntiles; ++ti) {
     t0 = p_begin + ti * AD_TILE;
     tn = min((uint32_t)AD_TILE, p_end - t0);
-    if (ti > 0) issue_tile(t0, tn);
-    if (owner && pos >= t0 && pos < t0 + tn) {
-      const uint32_t r = pos - t0;
-      for (uint32_t d = tid; d < HD; d += AD_THREADS) {
-        Ks[r * Lo::ROW + d] = nk[d];
-        Vs[r * Lo::ROW + d] = nk[HD + d];
-      }
+    if (ti > 0) {
+      __syncthreads();  // the previous tile is consumed
+      issue_tile(t0, tn);
     }
     cp_async_wait_all();
+    __syncthreads();  // rotated q / nk and the tile are in place
+    if (owner && pos >= t0 && pos < t0 + tn)
+      for (uint32_t d = tid; d < HD; d += AD_THREADS) sm.ks[pos - t0][d] = sm.nk[d];
     __syncthreads();
     if (trace && tid == 0 && ti == 0) ts[5] = globaltimer();
-    // two positions per step (p0 and p0 + 8): their loads, dots and
-    // butterflies interleave, and one softmax update absorbs both. The
-    // exponentials use the hardware exp2 (__expf): a few ulp on weights in
-    // [0, 1], far inside the logit tolerance, and one instruction instead of
-    // a range-reduced sequence on this latency-bound chain.
-    for (uint32_t p0 = warp; p0 < tn; p0 += 2 * (AD_THREADS / 32)) {
-      const uint32_t p1 = p0 + AD_THREADS / 32;
-      const bool two = p1 < tn;  // warp-uniform
-      float k0[E], v0[E], k1[E], v1[E];
 #pragma unroll
-      for (int e = 0; e < E; ++e) {
-        k0[e] = Ks[p0 * Lo::ROW + lane * E + e];
-        v0[e] = Vs[p0 * Lo::ROW + lane * E + e];
-        k1[e] = two ? Ks[p1 * Lo::ROW + lane * E + e] : 0.0f;
-        v1[e] = two ? Vs[p1 * Lo::ROW + lane * E + e] : 0.0f;
-      }
-      float s0[KVM], s1[KVM];
-#pragma unroll
-      for (int h = 0; h < KVM; ++h) {
-        float t0v = 0.0f, t1v = 0.0f;
-#pragma unroll
-        for (int e = 0; e < E; ++e) {
-          t0v = fmaf(qr[h][e], k0[e], t0v);
-          t1v = fmaf(qr[h][e], k1[e], t1v);
-        }
-        s0[h] = t0v;
-        s1[h] = t1v;
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-        for (int h = 0; h < KVM; ++h) {
-          s0[h] += __shfl_xor_sync(FULL, s0[h], o);
-          s1[h] += __shfl_xor_sync(FULL, s1[h], o);
-        }
-#pragma unroll
-      for (int h = 0; h < KVM; ++h) {
-        const float a0 = __fmul_rn(s0[h], a.scale);  // (q.k) * scale (forward.rs:328-346)
-        const float a1 = two ? __fmul_rn(s1[h], a.scale) : -INFINITY;
-        const float mn = fmaxf(m[h], fmaxf(a0, a1));
-        const float cf = __expf(m[h] - mn);  // 0 while m is -inf
-        const float e0 = __expf(a0 - mn);
-        const float e1 = two ? __expf(a1 - mn) : 0.0f;
-        l[h] = fmaf(l[h], cf, e0 + e1);
-#pragma unroll
-        for (int e = 0; e < E; ++e) acc[h][e] = fmaf(acc[h][e], cf, fmaf(e0, v0[e], e1 * v1[e]));
-        m[h] = mn;
+    for (int m = 0; m < 2; ++m) {
+      const uint32_t hh = tid / AD_TILE + 4 * m, j = tid % AD_TILE;
+      if (hh < KVM && j < tn) {
+        const float s = __fmul_rn(dot8_exact<HD>(sm.qs[hh], sm.ks[j]), a.scale);
+        sc0[(uint64_t)hh * a.sc_stride + t0 + j] = s;
+        rmax[m] = fmaxf(rmax[m], s);
       }
     }
-    __syncthreads();  // the tile area is reloaded or reused below
   }
-  // warp partials -> CTA partial (unnormalized, with its max and sum)
 #pragma unroll
-  for (int h = 0; h < KVM; ++h) {
-#pragma unroll
-    for (int e = 0; e < E; ++e) wo[(warp * AT_MAXKV + h) * HD + lane * E + e] = acc[h][e];
-    if (lane == 0) {
-      wm[warp * AT_MAXKV + h] = m[h];
-      wl[warp * AT_MAXKV + h] = l[h];
-    }
+  for (int m = 0; m < 2; ++m) {
+    const float v = warp_max(rmax[m]);
+    if (lane == 0) sm.wmax[warp][m] = v;
   }
   __syncthreads();
+  if (tid < KVM) {  // head h's maxima sit in warps 2(h%4), 2(h%4)+1, slot h/4
+    const uint32_t h = tid;
+    sm.cmax[h] = fmaxf(sm.wmax[2 * (h % 4)][h / 4], sm.wmax[2 * (h % 4) + 1][h / 4]);
+  }
   if (trace && tid == 0) ts[6] = globaltimer();
-  // The KV head's kv_mul*HD outputs form 32-blocks; block b is merged by CTA
-  // b % cs. Each CTA pushes its partial of every block, with the head's max
-  // and sum, into the merging CTA's shared memory (distributed shared
-  // memory); one cluster barrier later every CTA merges its blocks locally.
-  float* recv = sm + Lo::RECV;  // [AD_MAXSLOT][AD_MAXCS][34]: 32 outputs, max, sum
-  for (uint32_t i = tid; i < kv_mul * HD; i += AD_THREADS) {
-    const uint32_t hh = i / HD, d = i % HD;
-    float M = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < 8; ++w) M = fmaxf(M, wm[w * AT_MAXKV + hh]);
-    float O = 0.0f, Lsum = 0.0f;
-#pragma unroll
-    for (int w = 0; w < 8; ++w) {
-      const float mw = wm[w * AT_MAXKV + hh];
-      const float wgt = mw == -INFINITY ? 0.0f : __expf(mw - M);
-      O = fmaf(wo[(w * AT_MAXKV + hh) * HD + d], wgt, O);
-      Lsum = fmaf(wl[w * AT_MAXKV + hh], wgt, Lsum);
-    }
-    const uint32_t b = i / 32, j = i % 32;
-    float* dst = cluster.map_shared_rank(recv, b % cs) + ((b / cs) * AD_MAXCS + rank) * 34;
-    dst[j] = O;
-    if (j == 0) {
-      dst[32] = M;
-      dst[33] = Lsum;
-    }
+  cluster.sync();  // scores, cache rows and slice maxima visible to the cluster
+
+  // ---- 2. e = exp(s - max) over the slice ----
+  if (tid < KVM) {
+    float m = -1e10f;
+    for (uint32_t r = 0; r < cs; ++r) m = fmaxf(m, cluster.map_shared_rank(sm.cmax, r)[tid]);
+    sm.gmax[tid] = m;
   }
-  cluster.sync();  // release the pushes / acquire the peers' pushes
+  __syncthreads();
+  for (uint32_t i = tid; i < KVM * (p_end - p_begin); i += AD_THREADS) {
+    const uint32_t hh = i / (p_end - p_begin), t2 = p_begin + i % (p_end - p_begin);
+    float* w = sc0 + (uint64_t)hh * a.sc_stride + t2;
+    *w = yl_expf(__fsub_rn(*w, sm.gmax[hh]));
+  }
+  cluster.sync();  // the weights of every slice are in place (and no CTA
+                   // still reads a peer's cmax)
   if (trace && tid == 0) ts[2] = globaltimer();
-  const uint32_t nblk = kv_mul * HD / 32;
-  for (uint32_t b = rank + cs * warp; b < nblk; b += cs * (AD_THREADS / 32)) {
-    const float* src = recv + (b / cs) * AD_MAXCS * 34;
-    float M = -INFINITY;
-    for (uint32_t r = 0; r < cs; ++r) M = fmaxf(M, src[r * 34 + 32]);
-    float L = 0.0f, accv = 0.0f;
-    for (uint32_t r = 0; r < cs; ++r) {
-      const float mr = src[r * 34 + 32];
-      const float w = mr == -INFINITY ? 0.0f : __expf(mr - M);
-      L = fmaf(src[r * 34 + 33], w, L);
-      accv = fmaf(src[r * 34 + lane], w, accv);
-    }
-    const float v = L > 0.0f ? __fdiv_rn(accv, L) : 0.0f;
-    const uint64_t k = (uint64_t)kvh * kv_mul * HD + b * 32 + lane;
-    if (a.out) a.out[k] = v;
-    if (a.q8) {
-      float sc;
-      const int8_t qv = quant_q8_lane(v, &sc);
-      a.q8[k] = qv;
-      if (lane == 0) a.s8[k / 32] = sc;
-    }
+
+  // ---- 3. output blocks ----
+  constexpr uint32_t BPH = HD / 32;  // 32-blocks per head
+  const uint32_t nblk = KVM * BPH;
+  const uint32_t nmine = rank < nblk ? (nblk - rank + cs - 1) / cs : 0;
+  if (tid % 32 == 0 && (uint32_t)warp < nmine) {  // the softmax sums, one chain per block
+    const uint32_t hh = (rank + warp * cs) / BPH;
+    sm.inv[warp] = softmax_inv(sc0 + (uint64_t)hh * a.sc_stride, nvis);
   }
-  // The new rows go to the cache last: a global store before the cluster
-  // barrier would make every CTA's release wait for its acknowledgement.
-  if (owner) {
-    float* kdst = a.kcache + (uint64_t)pos * a.kv_dim + kvh * HD;
-    float* vdst = a.vcache + (uint64_t)pos * a.kv_dim + kvh * HD;
-    for (uint32_t d = tid; d < HD; d += AD_THREADS) {
-      kdst[d] = nk[d];
-      vdst[d] = nk[HD + d];
+  __syncthreads();
+  const uint32_t nsimd8 = nvis / 8 * 8;
+  for (uint32_t i = 0; i < nmine; ++i) {
+    const uint32_t b = rank + i * cs, hh = b / BPH, d = (b % BPH) * 32 + lane;
+    const float* w = sc0 + (uint64_t)hh * a.sc_stride;
+    const float inv = sm.inv[i];
+    const float* vcol = vbase + d;
+    float acc = 0.0f;  // lane `warp` of the P.V sums, positions warp, warp + 8, ...
+    uint32_t t2 = warp;
+    for (; t2 + 32 <= nsimd8; t2 += 32) {
+      float wv[4], vv[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        wv[u] = __ldcg(w + t2 + 8 * u);
+        vv[u] = __ldcg(vcol + (uint64_t)(t2 + 8 * u) * a.kv_dim);  // row pos: the owner's write
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) acc = __fadd_rn(acc, __fmul_rn(__fmul_rn(wv[u], inv), vv[u]));
     }
+    for (; t2 < nsimd8; t2 += 8)
+      acc = __fadd_rn(acc, __fmul_rn(__fmul_rn(__ldcg(w + t2), inv), __ldcg(vcol + (uint64_t)t2 * a.kv_dim)));
+    sm.lanes[warp][lane] = acc;
+    __syncthreads();
+    if (warp == 0) {
+      float o = reduce_add8(sm.lanes[0][lane], sm.lanes[1][lane], sm.lanes[2][lane], sm.lanes[3][lane],
+                            sm.lanes[4][lane], sm.lanes[5][lane], sm.lanes[6][lane], sm.lanes[7][lane]);
+      for (uint32_t tt = nsimd8; tt < nvis; ++tt)
+        o = __fadd_rn(o, __fmul_rn(__fmul_rn(__ldcg(w + tt), inv), __ldcg(vcol + (uint64_t)tt * a.kv_dim)));
+      const uint64_t k = (uint64_t)(kvh * KVM + hh) * HD + d;
+      if (a.out) a.out[k] = o;
+      if (a.q8) {
+        float scl;
+        const int8_t qv = quant_q8_lane(o, &scl);
+        a.q8[k] = qv;
+        if (lane == 0) a.s8[k / 32] = scl;
+      }
+    }
+    __syncthreads();  // lanes[] is rewritten by the next block
   }
   if (trace && tid == 0) {
     ts[3] = globaltimer();
+    ts[7] = ts[3];
     for (int i = 0; i < 8; ++i) trace[i] = ts[i];
   }
 }
@@ -528,7 +514,7 @@ __global__ void __maxnreg__(96) attn_decode_kernel(AttnDecodeArgs a) {
 template <int HD, int KVM>
 static cudaError_t decode_config(uint32_t n_kv_heads, uint32_t cs, cudaStream_t st, bool pdl, cudaLaunchConfig_t& cfg,
                                  cudaLaunchAttribute (&attr)[2]) {
-  const uint32_t smem = AdLayout<HD>::TOTAL * sizeof(float);
+  const uint32_t smem = sizeof(AdSmem<HD>);
   cudaError_t e =
       cudaFuncSetAttribute(attn_decode_kernel<HD, KVM>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e == cudaSuccess)
@@ -595,7 +581,9 @@ static cudaError_t launch_decode_hd(const AttnDecodeArgs& a, const LaunchCfg& lc
 cudaError_t attention_decode(const AttnDecodeArgs& a, const LaunchCfg& lc) {
   const uint32_t kv_mul = a.n_kv_heads ? a.n_heads / a.n_kv_heads : 0;
   if (kv_mul == 0 || kv_mul > AT_MAXKV || a.n_splits == 0 || a.n_splits > AD_MAXCS) return cudaErrorInvalidValue;
-  if (a.kv_dim % 4 || ((uintptr_t)a.kcache | (uintptr_t)a.vcache) % 16) return cudaErrorInvalidValue;
+  if (kv_mul * a.head_size / 32 > a.n_splits * AD_MAXSLOT) return cudaErrorInvalidValue;
+  if (a.kv_dim % 4 || ((uintptr_t)a.kcache | (uintptr_t)a.vcache | (uintptr_t)a.sc) % 16 || a.sc_stride % 4 || !a.sc)
+    return cudaErrorInvalidValue;
   if (a.head_size == 64) return launch_decode_hd<64>(a, lc, kv_mul);
   if (a.head_size == 128) return launch_decode_hd<128>(a, lc, kv_mul);
   return cudaErrorInvalidValue;

@@ -17,7 +17,8 @@
 
 namespace {
 
-// One slot of (max, sum, head_size values) per (query head, key split).
+// The weights row of every (query row, head): batch * n_heads rows of
+// seq_len floats (attention_scratch_floats).
 constexpr size_t kStaticBytes = YL_ATTN_STATIC_BYTES;
 static_assert(kStaticBytes % 256 == 0, "the static partials area is a whole number of 256-byte lines");
 static __device__ __align__(256) float g_attn_scratch[kStaticBytes / sizeof(float)];
@@ -48,12 +49,13 @@ extern "C" int yl_fused_attention_static(float* output, const float* sq, const f
   int rc = yl::check_attention_args(output, sq, key_cache, value_cache, seq_len, batch, n_heads, n_kv_heads,
                                     head_size, start_pos, kv_dim);
   if (rc) return rc;
-  // the split count of yl_fused_attention, so both give the same result
-  const uint64_t ns = batch == 1 ? yl::attention_splits(seq_len, n_kv_heads) : 1;
-  const uint64_t need = n_heads * ns * (head_size + 2) * sizeof(float);
-  if (ns > 1 && need > kStaticBytes)
+  // the same kernel and scratch layout as yl_fused_attention, so both give
+  // the same result
+  const uint64_t need =
+      yl::k::attention_scratch_floats((uint32_t)batch, (uint32_t)n_heads, start_pos) * sizeof(float);
+  if (need > kStaticBytes)
     return yl::fail(YL_ERR_UNSUPPORTED, "attention needs " + std::to_string(need) +
-                                            " bytes of split scratch; the static area holds " +
+                                            " bytes of scratch; the static area holds " +
                                             std::to_string(kStaticBytes));
   float* scratch = nullptr;
   if ((rc = scratch_for_current_device(&scratch))) return rc;
@@ -68,8 +70,8 @@ extern "C" int yl_fused_attention_static(float* output, const float* sq, const f
   a.kv_dim = (uint32_t)kv_dim;
   a.pos0 = start_pos;
   a.scale = attn_scale;
-  a.n_splits = (uint32_t)ns;
-  // Every partial slot the merge reads is written by the same call first, so
+  a.n_splits = 1;
+  // Every weight the kernel reads is written by the same call first, so
   // nothing in the array needs clearing between calls.
   a.part = scratch;
   a.out = output;

@@ -6,6 +6,9 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "expf_exact.h"
+#include "kernels.h"
+
 namespace yl {
 namespace dev {
 
@@ -44,10 +47,10 @@ __device__ __forceinline__ uint64_t globaltimer() {
   return t;
 }
 
-// SwiGLU of one gate/up pair.
+// SwiGLU of one gate/up pair: forward.rs:230-235, g / (1 + exp(-g)) * u, with
+// exp the correctly rounded e^x (yl_expf), each operation rounded as in f32.
 __device__ __forceinline__ float silu_mul(float g, float u) {
-  // forward.rs:230-235: g / (1 + exp(-g)) * u
-  float s = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
+  float s = __fdiv_rn(g, __fadd_rn(1.0f, yl::yl_expf(-g)));
   return __fmul_rn(s, u);
 }
 
@@ -120,6 +123,88 @@ __device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src, uint32
       "%4;" ::"r"(smem_u32(dst_smem)),
       "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
       : "memory");
+}
+
+// Bulk prefetch of [src, src+bytes) into L2 (no completion to wait on).
+// src 16-byte aligned, bytes a multiple of 16; issued in 64 KB pieces.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint64_t bytes) {
+  const uint8_t* p = static_cast<const uint8_t*>(src);
+  while (bytes) {
+    const uint32_t n = bytes > 65536u ? 65536u : (uint32_t)bytes;
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(n) : "memory");
+    p += n;
+    bytes -= n;
+  }
+}
+
+// RMSNorm factors 1/sqrt(sum(x^2)/n + eps) of up to 16 rows of n floats
+// (n % 8 == 0, rows 16-byte aligned), bit-identical to util.rs:389-426: the
+// sum of squares runs in eight lane accumulators, lane l adding x[8j+l]^2 for
+// j = 0, 1, 2, ... (each square rounded, then added), folded as
+// ((l0+l4)+(l2+l6)) + ((l1+l5)+(l3+l7)); then /n, +eps, 1/sqrt, all rounded
+// as IEEE f32 operations. Called by all 32 lanes of one warp: lanes 2t and
+// 2t+1 walk row t (lanes 0..3 and 4..7 of its accumulators, one float4 per
+// step), so the cost is the n/8-long addition chain, not n.
+__device__ __forceinline__ void rms_factors_exact(const float* x0, uint64_t stride, uint32_t nrows, uint32_t n,
+                                                  float eps, float* out, int lane) {
+  const uint32_t t = (uint32_t)lane >> 1, half = (uint32_t)lane & 1u;
+  float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  if (t < nrows) {
+    const float* x = x0 + (uint64_t)t * stride + 4 * half;
+    const uint32_t nj = n / 8;
+    uint32_t j = 0;
+    for (; j + 8 <= nj; j += 8) {
+      float4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = *reinterpret_cast<const float4*>(x + 8 * (j + u));
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        acc.x = __fadd_rn(acc.x, __fmul_rn(v[u].x, v[u].x));
+        acc.y = __fadd_rn(acc.y, __fmul_rn(v[u].y, v[u].y));
+        acc.z = __fadd_rn(acc.z, __fmul_rn(v[u].z, v[u].z));
+        acc.w = __fadd_rn(acc.w, __fmul_rn(v[u].w, v[u].w));
+      }
+    }
+    for (; j < nj; ++j) {
+      const float4 v = *reinterpret_cast<const float4*>(x + 8 * j);
+      acc.x = __fadd_rn(acc.x, __fmul_rn(v.x, v.x));
+      acc.y = __fadd_rn(acc.y, __fmul_rn(v.y, v.y));
+      acc.z = __fadd_rn(acc.z, __fmul_rn(v.z, v.z));
+      acc.w = __fadd_rn(acc.w, __fmul_rn(v.w, v.w));
+    }
+  }
+  const float h0 = __shfl_down_sync(FULL, acc.x, 1), h1 = __shfl_down_sync(FULL, acc.y, 1);
+  const float h2 = __shfl_down_sync(FULL, acc.z, 1), h3 = __shfl_down_sync(FULL, acc.w, 1);
+  if (half == 0 && t < nrows) {
+    const float a0 = __fadd_rn(acc.x, h0), a1 = __fadd_rn(acc.y, h1);
+    const float a2 = __fadd_rn(acc.z, h2), a3 = __fadd_rn(acc.w, h3);
+    const float ss = __fadd_rn(__fadd_rn(a0, a2), __fadd_rn(a1, a3));
+    float r = __fdiv_rn(ss, (float)n);
+    r = __fadd_rn(r, eps);
+    out[t] = __fdiv_rn(1.0f, __fsqrt_rn(r));
+  }
+}
+
+// Prefetches this CTA's share (slots cta, cta + ncta, ...) of the next
+// kernel's first rows (see L2Prefetch).
+__device__ __forceinline__ void l2_prefetch_next(const k::L2Prefetch& pf, uint32_t cta, uint32_t ncta) {
+  if (!pf.q || !pf.slots || !pf.rows_each) return;
+  const uint64_t units = pf.rows / pf.unit;
+  for (uint32_t c = cta; c < pf.slots; c += ncta) {
+    uint64_t r0, r1;
+    if (pf.dyn) {
+      r0 = (uint64_t)c * pf.rows_each;
+      r1 = r0 + pf.rows_each;
+    } else {
+      r0 = units * c / pf.slots * pf.unit;
+      r1 = units * (c + 1) / pf.slots * pf.unit;
+      if (r1 > r0 + pf.rows_each) r1 = r0 + pf.rows_each;
+    }
+    if (r1 > pf.rows) r1 = pf.rows;
+    if (r0 >= r1) continue;
+    bulk_prefetch_l2(pf.q + r0 * pf.row_bytes, (r1 - r0) * pf.row_bytes);
+    if (pf.s) bulk_prefetch_l2(pf.s + r0 * pf.srow_bytes, (r1 - r0) * pf.srow_bytes);
+  }
 }
 
 // ---- named barrier over a subset of warps ---------------------------------

@@ -57,6 +57,26 @@ inline cudaError_t launch_kernel(void (*kern)(KArgs...), dim3 grid, dim3 block, 
   return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
+// ---- L2 prefetch of the next kernel's weights ------------------------------
+// Batch-1 decode streams every weight once per token, and HBM idles while a
+// kernel drains, while the next one starts and during attention. A kernel
+// given this descriptor asks the TMA unit to prefetch into L2 the rows the
+// NEXT weight-streaming kernel reads first, so those gaps carry useful bytes.
+// Slots c = 0..slots-1 are spread over the prefetching kernel's CTAs:
+//  * static split (dyn = 0): slot c is next-kernel CTA c's contiguous row
+//    range (units = rows/unit split evenly over `slots` CTAs), of which the
+//    first rows_each rows are fetched;
+//  * dynamic row sets (dyn = 1): slot c is rows [c*rows_each, (c+1)*rows_each).
+struct L2Prefetch {
+  const uint8_t* q = nullptr;  // quants of the next matrix (null: nothing to prefetch)
+  const uint8_t* s = nullptr;  // its scales (nullable)
+  uint32_t rows = 0, row_bytes = 0, srow_bytes = 0;
+  uint32_t unit = 1;
+  uint32_t slots = 0;
+  uint32_t rows_each = 0;
+  uint32_t dyn = 0;
+};
+
 // ---- matvec -------------------------------------------------------------
 struct MvArgs {
   const uint8_t* wq;        // weight quants (row-major, row_bytes per row)
@@ -120,9 +140,27 @@ struct MvArgs {
   // RMSNorm prologue: first token's rows loaded, norm factor ready, warp 0's
   // and the last warp's rows quantized
   uint64_t* trace;
+  // issued by each CTA's producer once its own copies are all issued
+  L2Prefetch pf;
 };
 // fmt: FMT_*; scale_f16: weight scale type. Chooses NT from a.ntok.
 cudaError_t matvec(const MvArgs& a, int fmt, bool scale_f16, int epi, const LaunchCfg& lc);
+// The schedule matvec() picks: CTA count, and whether a single-token pass
+// given row-set counters (has_work) hands out 8-row sets dynamically (worth it
+// with 4 or more sets per CTA; the SwiGLU+quantize epilogue also needs whole
+// sets and at most 16 per CTA). Also used to aim L2Prefetch at a launch.
+constexpr uint32_t MV_ROWSET = 8;
+constexpr uint32_t MV_SWIGLU_LIST = 32;  // row sets one CTA may list for its h-quantize tail
+inline void matvec_schedule(uint32_t rows, int epi, uint32_t lc_grid, uint32_t ntok, bool has_work, uint32_t* grid,
+                            bool* dyn) {
+  const uint32_t g = lc_grid ? lc_grid : 148;
+  const uint32_t unit = (epi == EPI_SWIGLU || epi == EPI_SWIGLU_Q8) ? 2u : 1u;
+  *grid = g > rows / unit ? rows / unit : g;
+  const uint32_t nrs = (rows + MV_ROWSET - 1) / MV_ROWSET;
+  bool ok = has_work && ntok == 1 && nrs >= 4 * g;
+  if (epi == EPI_SWIGLU_Q8) ok = ok && rows % MV_ROWSET == 0 && nrs <= g * (MV_SWIGLU_LIST / 2);
+  *dyn = ok;
+}
 // Largest tokens-per-pass (1, 2, 4 or 8) whose shared-memory layout fits with
 // at least two ring stages.
 uint32_t matvec_max_ntok(int fmt, uint32_t K, uint32_t kc, int epi);
@@ -181,9 +219,13 @@ cudaError_t rope_kv(const float* qkv, uint32_t ntok, uint32_t n_heads, uint32_t 
                     float* q_out, float* kcache, float* vcache, const LaunchCfg& lc);
 
 // Causal GQA attention (forward.rs:299-400) for ntok queries at positions
-// pos0..pos0+ntok-1 over kcache/vcache [ctx][kv_dim]. Split-sequence with
-// partials in `part` when n_splits > 1; the combine also quantizes the output
-// per 32-block into q/s (Q8_0) and/or writes f32 into out.
+// pos0..pos0+ntok-1 over kcache/vcache [ctx][kv_dim], bit-identical to the
+// reference's sequence of f32 operations: 8-lane dot products, max, the
+// correctly rounded exp, the softmax sum in position order, 1/sum, and the
+// 8-lane P.V sums over the batch's seq_len = pos0 + ntok with the sequential
+// tail. The scores and weights go through `part` ([ntok][n_heads][seq_len]
+// floats, attention_scratch_floats). The output is quantized per 32-block into
+// q8/s8 (Q8_0) and/or written as f32 into out.
 struct AttnArgs {
   const float* q;
   const float* kcache;
@@ -192,23 +234,34 @@ struct AttnArgs {
   const StepState* state;
   uint32_t pos0;
   float scale;
-  uint32_t n_splits;
-  float* part;  // [ntok][n_heads][n_splits][head_size + 2]
+  uint32_t n_splits;  // unused (kept for the argument layout)
+  float* part;  // scores / weights scratch [ntok][n_heads][pos0 + ntok]
   float* out;   // [ntok][n_heads*head_size] f32 (nullable)
   int8_t* q8;   // [ntok][n_heads*head_size] (nullable)
   float* s8;    // [ntok][n_heads*head_size/32]
 };
 cudaError_t attention(const AttnArgs& a, const LaunchCfg& lc);
-// The query-blocked kernel attention() uses for 32 or more tokens with one
-// split (64 query rows per CTA share every K/V tile).
-bool attention_prefill_ok(const AttnArgs& a);
-cudaError_t attention_prefill(const AttnArgs& a, const LaunchCfg& lc);
+// Row stride (floats) and size of `part` for attention(): one row of
+// seq_len = pos0 + ntok weights per (query row, head), rows 16-byte aligned.
+#if defined(__CUDACC__)
+#define YL_KHD __host__ __device__
+#else
+#define YL_KHD
+#endif
+YL_KHD inline uint64_t attention_scratch_stride(uint32_t ntok, uint32_t pos0) {
+  return ((uint64_t)pos0 + ntok + 3) / 4 * 4;
+}
+YL_KHD inline uint64_t attention_scratch_floats(uint32_t ntok, uint32_t n_heads, uint32_t pos0) {
+  return (uint64_t)ntok * n_heads * attention_scratch_stride(ntok, pos0);
+}
 
 // Batch-1 decode attention with RoPE and the KV-cache write fused in:
 // q and the new k/v rows are taken unrotated from `qkv` ([att | k | v]),
 // rotated with cs[pos], the new k/v rows written at `pos`. One thread-block
-// cluster of n_splits CTAs per KV head splits the keys; the splits' partials
-// are merged through distributed shared memory, and the output is quantized
+// cluster of n_splits CTAs per KV head: the CTAs split the scores, then the
+// output 32-blocks; scores and weights of every query head go through
+// sc[head][sc_stride] (sc_stride >= pos + 1). Bit-identical to the
+// reference's operation sequence, like attention(); the output is quantized
 // per 32-block in the same kernel.
 struct AttnDecodeArgs {
   const float* qkv;
@@ -231,6 +284,11 @@ struct AttnDecodeArgs {
   // entry, wait released, partials visible, done, q rotated, first key tile
   // in shared memory, partial ready, merge done
   uint64_t* trace;
+  // issued by thread 0 of every CTA at entry (HBM is otherwise idle while
+  // attention runs)
+  L2Prefetch pf;
+  float* sc;           // scores / weights scratch [n_heads][sc_stride]
+  uint32_t sc_stride;
 };
 // Cluster size for the decode attention: 16 when n_kv_heads clusters of 16
 // can be resident at once, else 8.

@@ -39,6 +39,12 @@ __host__ __device__ constexpr uint32_t mv_qbytes(uint32_t kn) {
 }
 template <int FMT>
 __host__ __device__ constexpr bool mv_has_scales() { return FMT != FMT_F16; }
+// Int8-activation formats fold the block terms ((f32)isum * ws) * xs of a row
+// in group order into one f32 chain, as matmul_q8_slices does
+// (weight_type.rs:190-201), so their outputs equal the reference's bit for bit.
+template <int FMT>
+__host__ __device__ constexpr bool mv_exact_fold() { return FMT == FMT_Q8 || FMT == FMT_Q4; }
+constexpr uint32_t MV_TERMS = 64;  // block terms one warp pass produces per token
 template <int FMT>
 __host__ __device__ constexpr bool mv_f32_act() {
   return FMT == FMT_F16 || FMT == FMT_Q8F || FMT == FMT_Q4F;
@@ -57,7 +63,7 @@ constexpr uint32_t MV_END = 0xFFFFFFFFu;  // stage info: no more row sets
 
 // Shared-memory layout, computed identically on host and device.
 struct MvLayout {
-  uint32_t bar_off, info_off, red_off, x_off, xs_off, xsum_off, ring_off;
+  uint32_t bar_off, info_off, red_off, x_off, xs_off, xsum_off, terms_off, ring_off;
   uint32_t stage_q_row, stage_s_row, stage_bytes, total;
 };
 // ssz: weight scale element size (2 for f16, 4 for f32). A stage's scale row
@@ -87,6 +93,9 @@ __host__ __device__ inline MvLayout mv_layout(uint32_t K, uint32_t kc, int rpw, 
     L.xsum_off = off;
     if (FMT == FMT_Q4) off += NT * (K / 32) * 4;
   }
+  off = (off + 15) & ~15u;
+  L.terms_off = off;  // per consumer warp: [NT][MV_TERMS] block terms of one pass
+  if (mv_exact_fold<FMT>()) off += MV_NCW * NT * MV_TERMS * 4;
   off = (off + 127) & ~127u;
   L.ring_off = off;
   L.stage_q_row = mv_qbytes<FMT>(kc);
@@ -160,6 +169,14 @@ __device__ __forceinline__ void mv_norm_regs(const MvArgs& a, const MvLayout& L,
   const bool tp_in = NT == 1 && a.tp_mode == 2;
   const uint32_t tp_flag = tp_in ? *a.tp_epoch * a.tp_nsites + a.tp_site + 1u : 0u;
   const uint64_t tp_t0 = tp_in ? clock64() : 0;
+  // Norm factors of the resident rows in the reference's summation order (one
+  // warp, all tokens at once). Tensor-parallel rows exist only in registers
+  // (residual + the ranks' partials), so they keep the register-tree sum.
+  float* rfac = red + 32;
+  if (NORM && !tp_in) {
+    if (cw == 0) rms_factors_exact(a.xres, a.x_tok_stride, min((uint32_t)NT, a.ntok), K, a.eps, rfac, lane);
+    named_bar_sync(1, MV_NCW * 32);
+  }
   for (int t = 0; t < NT; ++t) {
     const bool valid = t < (int)a.ntok;
     const float* xr = a.xres + (uint64_t)t * a.x_tok_stride;
@@ -205,7 +222,9 @@ __device__ __forceinline__ void mv_norm_regs(const MvArgs& a, const MvLayout& L,
       }
     }
     float r = 1.0f;
-    if (NORM) {
+    if (NORM && !tp_in) {
+      r = valid ? rfac[t] : 1.0f;
+    } else if (NORM) {
       float ss = 0.0f;
 #pragma unroll
       for (int u = 0; u < MU; ++u) {
@@ -368,38 +387,13 @@ __device__ __forceinline__ void mv_stage_x(const MvArgs& a, const MvLayout& L, u
   }
   mv_wait_inputs(a);
   if (a.pro == PRO_NORM) {
+    // norm factors in the reference's summation order, all tokens at once
+    if (cw == 0) rms_factors_exact(a.xres, a.x_tok_stride, min((uint32_t)NT, a.ntok), K, a.eps, red + 32, lane);
+    named_bar_sync(1, MV_NCW * 32);
     for (int t = 0; t < NT; ++t) {
       const bool valid = t < (int)a.ntok;
       const float* xr = a.xres + (uint64_t)t * a.x_tok_stride;
-      // sum of squares, same order as rmsnorm_quant_kernel (256 threads,
-      // float4); the loads are issued four at a time so they overlap
-      float ss = 0.0f;
-      if (valid)
-        for (uint32_t i0 = ctid * 4; i0 < K; i0 += 4 * MV_NCW * 32 * 4) {
-          float4 v[4];
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const uint32_t i = i0 + u * MV_NCW * 32 * 4;
-            v[u] = i < K ? *reinterpret_cast<const float4*>(xr + i) : make_float4(0, 0, 0, 0);
-          }
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            ss = fmaf(v[u].x, v[u].x, ss);
-            ss = fmaf(v[u].y, v[u].y, ss);
-            ss = fmaf(v[u].z, v[u].z, ss);
-            ss = fmaf(v[u].w, v[u].w, ss);
-          }
-        }
-      ss = warp_sum(ss);
-      if (lane == 0) red[cw] = ss;
-      named_bar_sync(1, MV_NCW * 32);
-      float tot = 0.0f;
-#pragma unroll
-      for (int i = 0; i < MV_NCW; ++i) tot += red[i];
-      float r = __fdiv_rn(tot, (float)K);
-      r = __fadd_rn(r, a.eps);
-      r = __fdiv_rn(1.0f, __fsqrt_rn(r));
-      named_bar_sync(1, MV_NCW * 32);  // red[] reused by the next token
+      const float r = valid ? red[32 + t] : 1.0f;
       if (mv_f32_act<FMT>()) {
         float* xf = reinterpret_cast<float*>(smem + L.x_off) + t * K;
         for (uint32_t k = ctid; k < K; k += MV_NCW * 32)
@@ -485,11 +479,35 @@ __device__ __forceinline__ void mv_stage_x(const MvArgs& a, const MvLayout& L, u
 }
 
 // ---------------------------------------------------------------------------
-// One row's chunk [k0, k0+kn) from the stage, accumulated into acc[NT].
+// Lane t < NT adds token t's ng block terms of one pass, in group order, to
+// its chain (the reference's sequential `+=` over groups).
+template <int NT>
+__device__ __forceinline__ void mv_chain(const float* terms, uint32_t ng, int lane, float& chain) {
+  __syncwarp();
+  if (lane < NT) {
+    const float* tt = terms + lane * MV_TERMS;
+    float c = chain;
+    uint32_t i = 0;
+    for (; i + 4 <= ng; i += 4) {
+      const float4 q = *reinterpret_cast<const float4*>(tt + i);
+      c = __fadd_rn(c, q.x);
+      c = __fadd_rn(c, q.y);
+      c = __fadd_rn(c, q.z);
+      c = __fadd_rn(c, q.w);
+    }
+    for (; i < ng; ++i) c = __fadd_rn(c, tt[i]);
+    chain = c;
+  }
+  __syncwarp();  // the buffer is rewritten by the next pass
+}
+
+// One row's chunk [k0, k0+kn) from the stage, accumulated into acc[NT]; for
+// the exact-fold formats lane t's acc[0] is token t's chain and `terms` this
+// warp's buffer.
 template <int FMT, int NT, bool SF16>
 __device__ __forceinline__ void mv_row_chunk(const uint8_t* wrow, const uint8_t* srow, const uint8_t* smem,
                                              const MvLayout& L, uint32_t K, uint32_t k0, uint32_t kn, int lane,
-                                             float (&acc)[NT]) {
+                                             float (&acc)[NT], float* terms) {
   using namespace yl::dev;
   if (FMT == FMT_Q8) {
     const int8_t* xq = reinterpret_cast<const int8_t*>(smem + L.x_off);
@@ -524,11 +542,13 @@ __device__ __forceinline__ void mv_row_chunk(const uint8_t* wrow, const uint8_t*
         for (int u = 0; u < MV_U; ++u) {
           const uint32_t c = c0 + u * 32 + lane;
           if (v[u] && !(lane & 1)) {
+            // block term ((f32)isum * ws) * xs; group u*16 + lane/2 of this pass
             const float p = __fmul_rn(__fmul_rn((float)s[u], wsc[u]), xs[t * (K / 32) + (k0 >> 5) + (c >> 1)]);
-            acc[t] = __fadd_rn(acc[t], p);
+            terms[t * MV_TERMS + u * 16 + (lane >> 1)] = p;
           }
         }
       }
+      mv_chain<NT>(terms, min(MV_TERMS, (nck - c0) >> 1), lane, acc[0]);
     }
   } else if (FMT == FMT_Q4) {
     const int8_t* xq = reinterpret_cast<const int8_t*>(smem + L.x_off);
@@ -564,9 +584,10 @@ __device__ __forceinline__ void mv_row_chunk(const uint8_t* wrow, const uint8_t*
           s = dp4a((w[u].w >> 4) & 0x0F0F0F0F, xh.w, s);
           s -= 8 * xsum[t * nb + kb];  // sum (q-8)*x exactly
           const float p = __fmul_rn(__fmul_rn((float)s, wsc[u]), xs[t * nb + kb]);
-          acc[t] = __fadd_rn(acc[t], p);
+          terms[t * MV_TERMS + u * 32 + lane] = p;  // group u*32 + lane of this pass
         }
       }
+      mv_chain<NT>(terms, min(MV_TERMS, nbk - b0), lane, acc[0]);
     }
   } else if (FMT == FMT_F16) {
     const float* xf = reinterpret_cast<const float*>(smem + L.x_off);
@@ -879,6 +900,9 @@ __global__ void __launch_bounds__(MV_THREADS, (NT <= 2 ? 2 : 1)) mv_kernel(MvArg
           atomicExch(a.work + 1, 0u);
         }
       }
+      // every copy of this CTA is issued: the rest of its time HBM would idle
+      // on its account, so start fetching the next kernel's first rows
+      l2_prefetch_next(a.pf, blockIdx.x, gridDim.x);
       // Drain: no bulk copy may still target this CTA's shared memory at exit
       // (consumers that timed out may have left). A slot whose latest stage
       // carries copies is waited on with that stage's parity (its latest
@@ -938,22 +962,32 @@ __global__ void __launch_bounds__(MV_THREADS, (NT <= 2 ? 2 : 1)) mv_kernel(MvArg
     const uint32_t rend = row0 + n;  // rows of this stage: [row0, rend)
     const uint32_t k0 = ch * kc, kn = min(kc, K - k0);
     const uint8_t* stage = smem + L.ring_off + slot * L.stage_bytes;
+    float* terms = reinterpret_cast<float*>(smem + L.terms_off) + cw * NT * MV_TERMS;
 #pragma unroll
     for (int rr = 0; rr < RPW; ++rr) {
       const uint32_t rl = wi * RPW + rr;
       if (rl >= n) continue;
       mv_row_chunk<FMT, NT, SF16>(stage + rl * L.stage_q_row, stage + RS * L.stage_q_row + rl * L.stage_s_row, smem,
-                                  L, K, k0, kn, lane, acc[rr]);
+                                  L, K, k0, kn, lane, acc[rr], terms);
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[slot]);
     if (n == 0 || ch != nch - 1) continue;
 
     // ---- epilogue for this warp's rows of the finished row set ----
+    if (mv_exact_fold<FMT>()) {  // lane t holds token t's chain: broadcast
 #pragma unroll
-    for (int t = 0; t < NT; ++t)
+      for (int rr = 0; rr < RPW; ++rr) {
+        const float c = acc[rr][0];
 #pragma unroll
-      for (int rr = 0; rr < RPW; ++rr) acc[rr][t] = warp_sum(acc[rr][t]);
+        for (int t = 0; t < NT; ++t) acc[rr][t] = __shfl_sync(FULL, c, t);
+      }
+    } else {
+#pragma unroll
+      for (int t = 0; t < NT; ++t)
+#pragma unroll
+        for (int rr = 0; rr < RPW; ++rr) acc[rr][t] = warp_sum(acc[rr][t]);
+    }
     if (mv_swiglu(EPI)) {
       const uint32_t r = row0 + wi * RPW;  // gate row (even), up row = r + 1
       const bool have = r + 1 < rend;
@@ -1145,9 +1179,10 @@ __global__ void __launch_bounds__(MV_THREADS, (NT <= 2 ? 2 : 1)) mv_kernel(MvArg
 
 // CTAs of a matvec launch: lc.grid (0: 148), at most one per row (row pair).
 inline uint32_t matvec_grid(uint32_t rows, int epi, uint32_t lc_grid) {
-  uint32_t grid = lc_grid ? lc_grid : 148;
-  const uint32_t unit = mv_swiglu(epi) ? 2 : 1;
-  return grid > rows / unit ? rows / unit : grid;
+  uint32_t grid;
+  bool dyn;
+  matvec_schedule(rows, epi, lc_grid, 1, false, &grid, &dyn);
+  return grid;
 }
 
 // Host-side launcher for one (FMT, SF16) family; NT and EPI dispatched here.
@@ -1190,10 +1225,10 @@ cudaError_t mv_launch(const MvArgs& a0, int epi, const LaunchCfg& lc) {
   {
     // dynamic row sets pay off with several row sets per CTA; the SwiGLU+
     // quantize tail needs every row set whole and at most MV_LIST per CTA
-    const uint32_t g = lc.grid ? lc.grid : 148;
-    const uint32_t nrs = (a.rows + MV_RS - 1) / MV_RS;
-    bool ok = a.work && nt == 1 && a.ntok == 1 && nrs >= 4 * g;
-    if (epi == EPI_SWIGLU_Q8) ok = ok && a.rows % MV_RS == 0 && nrs <= g * (MV_LIST / 2);
+    static_assert(MV_RS == MV_ROWSET && MV_LIST == MV_SWIGLU_LIST, "one schedule rule for launcher and prefetch");
+    uint32_t g;
+    bool ok;
+    matvec_schedule(a.rows, epi, lc.grid, a.ntok, a.work != nullptr, &g, &ok);
     if (!ok) a.work = nullptr;
   }
   if (epi == EPI_SWIGLU_Q8 && (a.rows % 64 || mv_f32_act<FMT>())) return cudaErrorInvalidValue;
