@@ -147,7 +147,9 @@ struct Tunables {
   bool gemm = true;          // multi-token passes on the int8 tensor-core GEMM
   uint32_t gemm_min = 16;    // from this many tokens (below, the matvec re-reading weights per 8 is faster)
   bool tp_fused = true;      // tensor-parallel decode: exchange fused into the projections (else exchange kernels)
-  uint64_t pf_bytes = 24ull << 20;  // decode: L2 prefetch of the next matrix's first bytes per launch (YL_PF_MB)
+  // decode: L2 prefetch of the next matrix's first bytes per launch (YL_PF_MB).
+  // Off: measured slower at every size tried (16, 32, 48 MB).
+  uint64_t pf_bytes = 0;
 };
 const Tunables& tunables();
 // Launches the matvec for `ntok` tokens (groups of 8) with activations x*.

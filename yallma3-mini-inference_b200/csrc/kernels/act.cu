@@ -31,26 +31,34 @@ cudaError_t quantize_q8(const float* x, int8_t* q, float* s, uint64_t nblocks, c
 // util.rs:389-426: ss = sum x^2; ss /= n; ss += eps; ss = 1/sqrt(ss);
 // y = w * (ss * x); then the Q8_0 quantizer on y (forward.rs:155-160). Every
 // step is the reference's sequence of IEEE f32 operations, the sum of squares
-// in its 8-lane order (rms_factors_exact), so y and its Q8_0 blocks are
-// bit-identical. One CTA per 16 rows: warp 0 walks the 16 addition chains,
-// then all warps normalize and quantize.
-constexpr uint32_t RQ_ROWS = 16;
+// in its 8-lane order, so y and its Q8_0 blocks are bit-identical. One CTA
+// per 4 rows: the rows are staged in shared memory, lanes 8g..8g+7 of warp 0
+// walk row g's eight addition chains, then all warps normalize and quantize.
+constexpr uint32_t RQ_ROWS = 4;
 __global__ void __launch_bounds__(256) rmsnorm_quant_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                                             uint32_t ntok, uint32_t dim, float eps,
                                                             int8_t* __restrict__ q, float* __restrict__ s,
                                                             float* __restrict__ y) {
+  extern __shared__ __align__(16) float rq_stage[];  // [RQ_ROWS][dim]
   grid_dep_launch();
   grid_dep_wait();
   __shared__ float rf[RQ_ROWS];
   const uint32_t t0 = blockIdx.x * RQ_ROWS, nt = min(RQ_ROWS, ntok - t0);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (warp == 0) rms_factors_exact(x + (uint64_t)t0 * dim, dim, nt, dim, eps, rf, lane);
+  for (uint32_t i = threadIdx.x * 4; i < nt * dim; i += 256 * 4)
+    *reinterpret_cast<float4*>(rq_stage + i) = *reinterpret_cast<const float4*>(x + (uint64_t)t0 * dim + i);
+  __syncthreads();
+  if (warp == 0) {
+    const uint32_t g = (uint32_t)lane >> 3;
+    const float r = rms_factor_smem8(rq_stage + (g < nt ? g : 0) * dim, dim, eps, lane);
+    if ((lane & 7) == 0 && g < nt) rf[g] = r;
+  }
   __syncthreads();
   const uint32_t nb = dim / 32;
   for (uint32_t tb = warp; tb < nt * nb; tb += 8) {
     const uint32_t t = t0 + tb / nb, b = tb % nb;
     const uint32_t k = b * 32 + lane;
-    const float yv = __fmul_rn(w[k], __fmul_rn(rf[tb / nb], x[(uint64_t)t * dim + k]));
+    const float yv = __fmul_rn(w[k], __fmul_rn(rf[tb / nb], rq_stage[(tb / nb) * dim + k]));
     if (y) y[(uint64_t)t * dim + k] = yv;
     if (q) {
       float sc;
@@ -65,8 +73,12 @@ cudaError_t rmsnorm_quant(const float* x, const float* w, uint32_t ntok, uint32_
                           float* s, float* y, const LaunchCfg& lc) {
   if (ntok == 0) return cudaSuccess;
   if (dim % 32) return cudaErrorInvalidValue;
-  return launch_kernel(rmsnorm_quant_kernel, dim3((ntok + RQ_ROWS - 1) / RQ_ROWS), dim3(256), 0, lc, x, w, ntok, dim,
-                       eps, q, s, y);
+  const uint32_t smem = RQ_ROWS * dim * 4;
+  if (smem > 227u * 1024u) return cudaErrorInvalidValue;
+  cudaError_t e = cudaFuncSetAttribute(rmsnorm_quant_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  return launch_kernel(rmsnorm_quant_kernel, dim3((ntok + RQ_ROWS - 1) / RQ_ROWS), dim3(256), smem, lc, x, w, ntok,
+                       dim, eps, q, s, y);
 }
 
 // Embedding gather: x[t][k] = value of row tokens[t] (exact: int8 * f16 scale

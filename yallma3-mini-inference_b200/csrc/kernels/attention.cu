@@ -108,28 +108,6 @@ __device__ __forceinline__ float dot8_exact(const float* q, const float* k) {
   return reduce_add8(l0, l1, l2, l3, l4, l5, l6, l7);
 }
 
-// The softmax denominator chain over w[0..n) (global, 16-byte aligned),
-// returning 1/sum (0 when the sum is not positive). Loads run ahead of the
-// dependent additions.
-__device__ __forceinline__ float softmax_inv(const float* w, uint32_t n) {
-  float s = 0.0f;
-  uint32_t i = 0;
-  for (; i + 16 <= n; i += 16) {
-    float4 v[4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) v[u] = __ldcg(reinterpret_cast<const float4*>(w + i) + u);
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      s = __fadd_rn(s, v[u].x);
-      s = __fadd_rn(s, v[u].y);
-      s = __fadd_rn(s, v[u].z);
-      s = __fadd_rn(s, v[u].w);
-    }
-  }
-  for (; i < n; ++i) s = __fadd_rn(s, __ldcg(w + i));
-  return s > 0.0f ? __fdiv_rn(1.0f, s) : 0.0f;
-}
-
 __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
 }
@@ -144,10 +122,15 @@ constexpr int AE_QB = 16;
 constexpr int AE_TILE = 64;
 constexpr int AE_THREADS = 256;
 
+constexpr int AE_ECH = 256;  // positions of exp weights staged per chunk
+
 template <int HD>
 struct AeSmem {
   float q[AE_QB][HD];
-  float kv[AE_TILE][HD + 4];  // K tile, then V tile, then the output rows
+  union {
+    float kv[AE_TILE][HD + 4];   // K tile, then V tile, then the output rows
+    float ebuf[AE_QB][AE_ECH];   // exp weights of one chunk (softmax sums)
+  };
   float w[AE_QB][AE_TILE];    // the tile's weights p
   float wmax[AE_THREADS / 32][4];
   float mx[AE_QB], inv[AE_QB];
@@ -208,15 +191,37 @@ __global__ void __launch_bounds__(AE_THREADS) attn_exact_kernel(AttnArgs a) {
     sm.mx[r] = fmaxf(sm.wmax[2 * (r % 4)][r / 4], sm.wmax[2 * (r % 4) + 1][r / 4]);
   }
   __syncthreads();
-  // ---- e = exp(s - max) ----
-  for (uint32_t r = 0; r < nr; ++r) {
-    float* w = wrow(r);
-    const uint32_t n = pos0 + r0 + r + 1;
-    for (uint32_t t2 = tid; t2 < n; t2 += AE_THREADS) w[t2] = yl_expf(__fsub_rn(w[t2], sm.mx[r]));
+  // ---- e = exp(s - max), chunk by chunk into shared memory (and back into
+  // the scratch for the P.V pass); thread r extends row r's sum ----
+  float rsum = 0.0f;
+  for (uint32_t c0 = 0; c0 < nvis; c0 += AE_ECH) {
+    const uint32_t cn = min((uint32_t)AE_ECH, nvis - c0);
+    for (uint32_t i = tid; i < nr * cn; i += AE_THREADS) {
+      const uint32_t r = i / cn, j = i % cn, t2 = c0 + j;
+      float e = 0.0f;
+      if (t2 <= pos0 + r0 + r) {
+        e = yl_expf(__fsub_rn(wrow(r)[t2], sm.mx[r]));
+        wrow(r)[t2] = e;
+      }
+      sm.ebuf[r][j] = e;  // masked: 0, which leaves the sum as it is
+    }
+    __syncthreads();
+    if (tid < (int)nr) {
+      const uint32_t n = min(cn, pos0 + r0 + tid + 1 > c0 ? pos0 + r0 + tid + 1 - c0 : 0u);
+      const float* eb = sm.ebuf[tid];
+      uint32_t j = 0;
+      for (; j + 16 <= n; j += 16) {
+        float v[16];
+#pragma unroll
+        for (int u = 0; u < 16; ++u) v[u] = eb[j + u];
+#pragma unroll
+        for (int u = 0; u < 16; ++u) rsum = __fadd_rn(rsum, v[u]);
+      }
+      for (; j < n; ++j) rsum = __fadd_rn(rsum, eb[j]);
+    }
+    __syncthreads();  // ebuf is rewritten by the next chunk
   }
-  __syncthreads();
-  // ---- the sums, one chain per row ----
-  if (tid < (int)nr) sm.inv[tid] = softmax_inv(wrow(tid), pos0 + r0 + tid + 1);
+  if (tid < (int)nr) sm.inv[tid] = rsum > 0.0f ? __fdiv_rn(1.0f, rsum) : 0.0f;
   __syncthreads();
   // ---- P.V: thread (row tid/16, dims (tid%16)*DPT + j), eight lanes each ----
   constexpr int DPT = HD / 16;
@@ -328,15 +333,19 @@ constexpr int AD_THREADS = 256;
 constexpr int AD_MAXCS = 16;     // largest cluster (non-portable size)
 constexpr int AD_MAXSLOT = 4;    // output 32-blocks one CTA takes: KVM*HD/32/cs <= 8*128/32/8
 
+constexpr int AD_ECH = 2048;     // positions of exp weights staged per chunk (per block)
+
 template <int HD>
 struct AdSmem {
-  float ks[AD_TILE][HD + 4];
+  union {
+    float ks[AD_TILE][HD + 4];        // phase 1: the slice's K tile
+    float ebuf[AD_MAXSLOT][AD_ECH];   // phase 3: exp weights of a chunk, per output block
+  };
   float qs[AT_MAXKV][HD];
   float nk[HD];                   // owner: the new key, rotated
-  float wmax[AD_THREADS / 32][2];
-  float cmax[AT_MAXKV];           // this CTA's slice maxima (read by the peers)
-  float gmax[AT_MAXKV];
-  float inv[AD_MAXSLOT];
+  float wred[AD_THREADS / 32][AD_MAXSLOT];
+  float gmax[AD_MAXSLOT];
+  float sum[AD_MAXSLOT];
   float lanes[8][32];             // P.V lane partials of one block
 };
 
@@ -403,7 +412,6 @@ __global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(AttnDecodeArgs 
   if (trace && tid == 0) ts[4] = globaltimer();
 
   // ---- 1. scores of the slice: thread (head tid/64 + 4m, key tid%64) ----
-  float rmax[2] = {-1e10f, -1e10f};
   const uint32_t ntiles = (p_end - p_begin + AD_TILE - 1) / AD_TILE;
   for (uint32_t ti = 0; ti < ntiles; ++ti) {
     t0 = p_begin + ti * AD_TILE;
@@ -421,78 +429,123 @@ __global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(AttnDecodeArgs 
 #pragma unroll
     for (int m = 0; m < 2; ++m) {
       const uint32_t hh = tid / AD_TILE + 4 * m, j = tid % AD_TILE;
-      if (hh < KVM && j < tn) {
-        const float s = __fmul_rn(dot8_exact<HD>(sm.qs[hh], sm.ks[j]), a.scale);
-        sc0[(uint64_t)hh * a.sc_stride + t0 + j] = s;
-        rmax[m] = fmaxf(rmax[m], s);
-      }
+      if (hh < KVM && j < tn) sc0[(uint64_t)hh * a.sc_stride + t0 + j] = __fmul_rn(dot8_exact<HD>(sm.qs[hh], sm.ks[j]), a.scale);
     }
   }
-#pragma unroll
-  for (int m = 0; m < 2; ++m) {
-    const float v = warp_max(rmax[m]);
-    if (lane == 0) sm.wmax[warp][m] = v;
-  }
-  __syncthreads();
-  if (tid < KVM) {  // head h's maxima sit in warps 2(h%4), 2(h%4)+1, slot h/4
-    const uint32_t h = tid;
-    sm.cmax[h] = fmaxf(sm.wmax[2 * (h % 4)][h / 4], sm.wmax[2 * (h % 4) + 1][h / 4]);
-  }
   if (trace && tid == 0) ts[6] = globaltimer();
-  cluster.sync();  // scores, cache rows and slice maxima visible to the cluster
-
-  // ---- 2. e = exp(s - max) over the slice ----
-  if (tid < KVM) {
-    float m = -1e10f;
-    for (uint32_t r = 0; r < cs; ++r) m = fmaxf(m, cluster.map_shared_rank(sm.cmax, r)[tid]);
-    sm.gmax[tid] = m;
-  }
-  __syncthreads();
-  for (uint32_t i = tid; i < KVM * (p_end - p_begin); i += AD_THREADS) {
-    const uint32_t hh = i / (p_end - p_begin), t2 = p_begin + i % (p_end - p_begin);
-    float* w = sc0 + (uint64_t)hh * a.sc_stride + t2;
-    *w = yl_expf(__fsub_rn(*w, sm.gmax[hh]));
-  }
-  cluster.sync();  // the weights of every slice are in place (and no CTA
-                   // still reads a peer's cmax)
+  cluster.sync();  // every slice's scores and the new cache rows are visible to the cluster
   if (trace && tid == 0) ts[2] = globaltimer();
 
-  // ---- 3. output blocks ----
+  // ---- 2. the CTA's output blocks: block b = rank + i*cs, head b / BPH ----
   constexpr uint32_t BPH = HD / 32;  // 32-blocks per head
   const uint32_t nblk = KVM * BPH;
   const uint32_t nmine = rank < nblk ? (nblk - rank + cs - 1) / cs : 0;
-  if (tid % 32 == 0 && (uint32_t)warp < nmine) {  // the softmax sums, one chain per block
-    const uint32_t hh = (rank + warp * cs) / BPH;
-    sm.inv[warp] = softmax_inv(sc0 + (uint64_t)hh * a.sc_stride, nvis);
+  auto head_of = [&](uint32_t i) { return (rank + i * cs) / BPH; };
+  // max(-1e10, scores) of each block's head, the whole row at once
+  {
+    float m[AD_MAXSLOT];
+#pragma unroll
+    for (int i = 0; i < AD_MAXSLOT; ++i) {
+      m[i] = -1e10f;
+      if ((uint32_t)i < nmine) {
+        const float* w = sc0 + (uint64_t)head_of(i) * a.sc_stride;
+        for (uint32_t t2 = tid; t2 < nvis; t2 += AD_THREADS) m[i] = fmaxf(m[i], __ldcg(w + t2));
+      }
+      m[i] = warp_max(m[i]);
+      if (lane == 0) sm.wred[warp][i] = m[i];
+    }
+    __syncthreads();
+    if (tid < AD_MAXSLOT) {
+      float g = -1e10f;
+      for (int w = 0; w < AD_THREADS / 32; ++w) g = fmaxf(g, sm.wred[w][tid]);
+      sm.gmax[tid] = g;
+      sm.sum[tid] = 0.0f;
+    }
+    __syncthreads();
   }
-  __syncthreads();
+  // e = exp(s - max) chunk by chunk into shared memory; lane 0 of warp i
+  // extends block i's sum over the chunk. The scores in sc are only read:
+  // the CTAs sharing a head each keep their own weights.
+  const uint32_t nchunk = (nvis + AD_ECH - 1) / AD_ECH;
+  auto fill_chunk = [&](uint32_t c0, uint32_t cn) {
+    for (uint32_t i = 0; i < nmine; ++i) {
+      const float* w = sc0 + (uint64_t)head_of(i) * a.sc_stride + c0;
+      for (uint32_t j = tid; j < cn; j += AD_THREADS) sm.ebuf[i][j] = yl_expf(__fsub_rn(__ldcg(w + j), sm.gmax[i]));
+    }
+  };
+  for (uint32_t c = 0; c < nchunk; ++c) {
+    const uint32_t c0 = c * AD_ECH, cn = min((uint32_t)AD_ECH, nvis - c0);
+    fill_chunk(c0, cn);
+    __syncthreads();
+    if (lane == 0 && (uint32_t)warp < nmine) {
+      const float* eb = sm.ebuf[warp];
+      float s = sm.sum[warp];
+      uint32_t j = 0;
+      for (; j + 16 <= cn; j += 16) {
+        float4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) v[u] = *reinterpret_cast<const float4*>(eb + j + 4 * u);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          s = __fadd_rn(s, v[u].x);
+          s = __fadd_rn(s, v[u].y);
+          s = __fadd_rn(s, v[u].z);
+          s = __fadd_rn(s, v[u].w);
+        }
+      }
+      for (; j < cn; ++j) s = __fadd_rn(s, eb[j]);
+      sm.sum[warp] = s;
+    }
+    __syncthreads();  // ebuf is rewritten by the next chunk (or read below)
+  }
+  // P.V: warp l runs lane l of the sums (positions l, l + 8, ...) for every
+  // block of the CTA, chunk by chunk (a single chunk is still in ebuf); the
+  // lane chains carry over chunk boundaries, which are multiples of 8
   const uint32_t nsimd8 = nvis / 8 * 8;
+  float inv[AD_MAXSLOT], acc[AD_MAXSLOT];
+#pragma unroll
+  for (int i = 0; i < AD_MAXSLOT; ++i) {
+    inv[i] = sm.sum[i] > 0.0f ? __fdiv_rn(1.0f, sm.sum[i]) : 0.0f;
+    acc[i] = 0.0f;
+  }
+  for (uint32_t c = 0; c < nchunk; ++c) {
+    const uint32_t c0 = c * AD_ECH, cn = min((uint32_t)AD_ECH, nvis - c0);
+    if (nchunk > 1) {
+      __syncthreads();
+      fill_chunk(c0, cn);
+      __syncthreads();
+    }
+    const uint32_t cend = min(c0 + cn, nsimd8);
+#pragma unroll
+    for (int i = 0; i < AD_MAXSLOT; ++i) {
+      if ((uint32_t)i >= nmine) break;
+      const uint32_t b = rank + i * cs, d = (b % BPH) * 32 + lane;
+      const float* vcol = vbase + d;
+      const float* eb = sm.ebuf[i] - c0;
+      float s = acc[i];
+      uint32_t t2 = c0 + warp;
+      for (; t2 + 128 <= cend; t2 += 128) {  // sixteen positions' V loads in flight
+        float vv[16];
+#pragma unroll
+        for (int u = 0; u < 16; ++u) vv[u] = __ldcg(vcol + (uint64_t)(t2 + 8 * u) * a.kv_dim);  // row pos: the owner's write
+#pragma unroll
+        for (int u = 0; u < 16; ++u) s = __fadd_rn(s, __fmul_rn(__fmul_rn(eb[t2 + 8 * u], inv[i]), vv[u]));
+      }
+      for (; t2 < cend; t2 += 8) s = __fadd_rn(s, __fmul_rn(__fmul_rn(eb[t2], inv[i]), __ldcg(vcol + (uint64_t)t2 * a.kv_dim)));
+      acc[i] = s;
+    }
+  }
+  // fold the lanes, add the tail (positions nsimd8..pos, in the last chunk)
   for (uint32_t i = 0; i < nmine; ++i) {
     const uint32_t b = rank + i * cs, hh = b / BPH, d = (b % BPH) * 32 + lane;
-    const float* w = sc0 + (uint64_t)hh * a.sc_stride;
-    const float inv = sm.inv[i];
-    const float* vcol = vbase + d;
-    float acc = 0.0f;  // lane `warp` of the P.V sums, positions warp, warp + 8, ...
-    uint32_t t2 = warp;
-    for (; t2 + 32 <= nsimd8; t2 += 32) {
-      float wv[4], vv[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        wv[u] = __ldcg(w + t2 + 8 * u);
-        vv[u] = __ldcg(vcol + (uint64_t)(t2 + 8 * u) * a.kv_dim);  // row pos: the owner's write
-      }
-#pragma unroll
-      for (int u = 0; u < 4; ++u) acc = __fadd_rn(acc, __fmul_rn(__fmul_rn(wv[u], inv), vv[u]));
-    }
-    for (; t2 < nsimd8; t2 += 8)
-      acc = __fadd_rn(acc, __fmul_rn(__fmul_rn(__ldcg(w + t2), inv), __ldcg(vcol + (uint64_t)t2 * a.kv_dim)));
-    sm.lanes[warp][lane] = acc;
+    sm.lanes[warp][lane] = acc[i];
     __syncthreads();
     if (warp == 0) {
       float o = reduce_add8(sm.lanes[0][lane], sm.lanes[1][lane], sm.lanes[2][lane], sm.lanes[3][lane],
                             sm.lanes[4][lane], sm.lanes[5][lane], sm.lanes[6][lane], sm.lanes[7][lane]);
+      const uint32_t c0 = (nchunk - 1) * AD_ECH;
       for (uint32_t tt = nsimd8; tt < nvis; ++tt)
-        o = __fadd_rn(o, __fmul_rn(__fmul_rn(__ldcg(w + tt), inv), __ldcg(vcol + (uint64_t)tt * a.kv_dim)));
+        o = __fadd_rn(o, __fmul_rn(__fmul_rn(sm.ebuf[i][tt - c0], inv[i]), __ldcg(vbase + d + (uint64_t)tt * a.kv_dim)));
       const uint64_t k = (uint64_t)(kvh * KVM + hh) * HD + d;
       if (a.out) a.out[k] = o;
       if (a.q8) {

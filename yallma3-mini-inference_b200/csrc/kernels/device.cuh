@@ -185,6 +185,36 @@ __device__ __forceinline__ void rms_factors_exact(const float* x0, uint64_t stri
   }
 }
 
+// The same factor from a row staged in shared memory (n floats, n % 8 == 0),
+// computed by lanes 8g..8g+7 of a warp: lane 8g+l walks accumulator l, the
+// lanes fold with shuffles, and lane 8g returns the factor (other lanes return
+// garbage). Shared-memory latency instead of L2 latency on every step of the
+// n/8-long chains.
+__device__ __forceinline__ float rms_factor_smem8(const float* x, uint32_t n, float eps, int lane) {
+  const int l = lane & 7;
+  float acc = 0.0f;
+  const uint32_t nj = n / 8;
+  uint32_t j = 0;
+  for (; j + 16 <= nj; j += 16) {
+    float v[16];
+#pragma unroll
+    for (int u = 0; u < 16; ++u) v[u] = x[8 * (j + u) + l];
+#pragma unroll
+    for (int u = 0; u < 16; ++u) acc = __fadd_rn(acc, __fmul_rn(v[u], v[u]));
+  }
+  for (; j < nj; ++j) {
+    const float v = x[8 * j + l];
+    acc = __fadd_rn(acc, __fmul_rn(v, v));
+  }
+  // ((l0+l4)+(l2+l6)) + ((l1+l5)+(l3+l7)) within each group of eight lanes
+  const float a = __fadd_rn(acc, __shfl_down_sync(FULL, acc, 4));   // lane l<4: l_l + l_{l+4}
+  const float b = __fadd_rn(a, __shfl_down_sync(FULL, a, 2));       // lane 0: a0+a2, lane 1: a1+a3
+  const float ss = __fadd_rn(b, __shfl_down_sync(FULL, b, 1));      // lane 0: (a0+a2)+(a1+a3)
+  float r = __fdiv_rn(ss, (float)n);
+  r = __fadd_rn(r, eps);
+  return __fdiv_rn(1.0f, __fsqrt_rn(r));
+}
+
 // Prefetches this CTA's share (slots cta, cta + ncta, ...) of the next
 // kernel's first rows (see L2Prefetch).
 __device__ __forceinline__ void l2_prefetch_next(const k::L2Prefetch& pf, uint32_t cta, uint32_t ncta) {

@@ -45,6 +45,15 @@ __host__ __device__ constexpr bool mv_has_scales() { return FMT != FMT_F16; }
 template <int FMT>
 __host__ __device__ constexpr bool mv_exact_fold() { return FMT == FMT_Q8 || FMT == FMT_Q4; }
 constexpr uint32_t MV_TERMS = 64;  // block terms one warp pass produces per token
+// Single-token passes of those formats hand the fold to a tenth warp: the
+// consumer warps write each stage's block terms into the stage's fold slot
+// and move on; the fold warp walks the rows' addition chains (lane r = row r
+// of the stage) and runs the epilogue. Multi-token passes fold in-warp.
+template <int FMT, int NT>
+__host__ __device__ constexpr bool mv_fold_warp() { return mv_exact_fold<FMT>() && NT == 1; }
+template <int FMT, int NT>
+__host__ __device__ constexpr int mv_threads() { return 32 * (1 + MV_NCW + (mv_fold_warp<FMT, NT>() ? 1 : 0)); }
+constexpr int MV_FOLD_WARP = 1 + MV_NCW;  // warp index of the fold warp
 template <int FMT>
 __host__ __device__ constexpr bool mv_f32_act() {
   return FMT == FMT_F16 || FMT == FMT_Q8F || FMT == FMT_Q4F;
@@ -63,8 +72,11 @@ constexpr uint32_t MV_END = 0xFFFFFFFFu;  // stage info: no more row sets
 
 // Shared-memory layout, computed identically on host and device.
 struct MvLayout {
-  uint32_t bar_off, info_off, red_off, x_off, xs_off, xsum_off, terms_off, ring_off;
+  uint32_t bar_off, info_off, red_off, fbar_off, x_off, xs_off, xsum_off, terms_off, ring_off;
   uint32_t stage_q_row, stage_s_row, stage_bytes, total;
+  // fold warp: each stage slot carries, after its weight rows, a header
+  // {first row, row count} (16 bytes) and MV_RS rows of fold_row floats
+  uint32_t fold_off, fold_row;
 };
 // ssz: weight scale element size (2 for f16, 4 for f32). A stage's scale row
 // is the chunk's scales padded to 16 bytes, which for a full-row chunk equals
@@ -72,13 +84,18 @@ struct MvLayout {
 // groups: consumer groups; a stage holds the rows of one group (MV_NCW/groups
 // warps x rpw rows each).
 template <int FMT, int NT>
+// norm_stage: the RMSNorm prologue stages one f32 row (K floats) at x_off to
+// walk the reference-order sum-of-squares chains from shared memory; the
+// activation region is at least that large (the staged row is dead before
+// the quantized activations are written over it).
 __host__ __device__ inline MvLayout mv_layout(uint32_t K, uint32_t kc, int rpw, int stages, uint32_t ssz = 4,
-                                             int groups = 1) {
+                                             int groups = 1, bool norm_stage = false) {
   MvLayout L;
   L.bar_off = 0;       // 2 x 16 mbarriers
   L.info_off = 256;    // per slot: first row and row count; row-set list (dynamic SwiGLU)
   L.red_off = 768;     // reductions / argmax / h staging ([2][8][32] floats)
-  uint32_t off = 768 + 2048 + 128;
+  L.fbar_off = 2816;   // fold warp: 2 x 16 mbarriers (fold slot full / free)
+  uint32_t off = 2816 + 256 + 128;
   L.x_off = off;
   if (mv_f32_act<FMT>()) {
     off += NT * K * 4;
@@ -93,14 +110,24 @@ __host__ __device__ inline MvLayout mv_layout(uint32_t K, uint32_t kc, int rpw, 
     L.xsum_off = off;
     if (FMT == FMT_Q4) off += NT * (K / 32) * 4;
   }
+  if (norm_stage && off < L.x_off + K * 4) off = L.x_off + K * 4;
   off = (off + 15) & ~15u;
-  L.terms_off = off;  // per consumer warp: [NT][MV_TERMS] block terms of one pass
-  if (mv_exact_fold<FMT>()) off += MV_NCW * NT * MV_TERMS * 4;
+  L.terms_off = off;  // per consumer warp: [NT][MV_TERMS] block terms of one pass (in-warp fold)
+  if (mv_exact_fold<FMT>() && !mv_fold_warp<FMT, NT>()) off += MV_NCW * NT * MV_TERMS * 4;
   off = (off + 127) & ~127u;
   L.ring_off = off;
   L.stage_q_row = mv_qbytes<FMT>(kc);
   L.stage_s_row = mv_has_scales<FMT>() ? ((kc / 32 * ssz + 15u) & ~15u) : 0;
   L.stage_bytes = (uint32_t)(MV_NCW / groups * rpw) * (L.stage_q_row + L.stage_s_row);
+  L.fold_off = L.fold_row = 0;
+  if (mv_fold_warp<FMT, NT>()) {
+    // padded rows: lane r of the fold warp reads row r at a 16-byte offset
+    // from its neighbours, so the eight lanes' float4 loads are conflict-free
+    L.fold_off = (L.stage_bytes + 15u) & ~15u;
+    L.fold_row = kc / 32 + 4;
+    L.stage_bytes = L.fold_off + 16 + MV_RS * L.fold_row * 4;
+    L.stage_bytes = (L.stage_bytes + 127u) & ~127u;
+  }
   L.total = off + stages * L.stage_bytes;
   return L;
 }
@@ -174,8 +201,20 @@ __device__ __forceinline__ void mv_norm_regs(const MvArgs& a, const MvLayout& L,
   // (residual + the ranks' partials), so they keep the register-tree sum.
   float* rfac = red + 32;
   if (NORM && !tp_in) {
-    if (cw == 0) rms_factors_exact(a.xres, a.x_tok_stride, min((uint32_t)NT, a.ntok), K, a.eps, rfac, lane);
-    named_bar_sync(1, MV_NCW * 32);
+    // one token at a time: the row is staged in shared memory (coalesced,
+    // every consumer thread), then lanes 0..7 of warp 0 walk the chains
+    float* stg = reinterpret_cast<float*>(smem + L.x_off);
+    for (int t = 0; t < NT && t < (int)a.ntok; ++t) {
+      const float* xr = a.xres + (uint64_t)t * a.x_tok_stride;
+      for (uint32_t i = ctid * 4; i < K; i += MV_NCW * 32 * 4)
+        *reinterpret_cast<float4*>(stg + i) = *reinterpret_cast<const float4*>(xr + i);
+      named_bar_sync(1, MV_NCW * 32);
+      if (cw == 0) {
+        const float r = rms_factor_smem8(stg, K, a.eps, lane);
+        if (lane == 0) rfac[t] = r;
+      }
+      named_bar_sync(1, MV_NCW * 32);  // the staging area is reused / overwritten
+    }
   }
   for (int t = 0; t < NT; ++t) {
     const bool valid = t < (int)a.ntok;
@@ -387,9 +426,20 @@ __device__ __forceinline__ void mv_stage_x(const MvArgs& a, const MvLayout& L, u
   }
   mv_wait_inputs(a);
   if (a.pro == PRO_NORM) {
-    // norm factors in the reference's summation order, all tokens at once
-    if (cw == 0) rms_factors_exact(a.xres, a.x_tok_stride, min((uint32_t)NT, a.ntok), K, a.eps, red + 32, lane);
-    named_bar_sync(1, MV_NCW * 32);
+    // norm factors in the reference's summation order, each row staged in
+    // shared memory first (the layout reserves K floats at x_off)
+    float* stg = reinterpret_cast<float*>(smem + L.x_off);
+    for (int t = 0; t < NT && t < (int)a.ntok; ++t) {
+      const float* xr = a.xres + (uint64_t)t * a.x_tok_stride;
+      for (uint32_t i = ctid * 4; i < K; i += MV_NCW * 32 * 4)
+        *reinterpret_cast<float4*>(stg + i) = *reinterpret_cast<const float4*>(xr + i);
+      named_bar_sync(1, MV_NCW * 32);
+      if (cw == 0) {
+        const float r = rms_factor_smem8(stg, K, a.eps, lane);
+        if (lane == 0) red[32 + t] = r;
+      }
+      named_bar_sync(1, MV_NCW * 32);
+    }
     for (int t = 0; t < NT; ++t) {
       const bool valid = t < (int)a.ntok;
       const float* xr = a.xres + (uint64_t)t * a.x_tok_stride;
@@ -488,12 +538,17 @@ __device__ __forceinline__ void mv_chain(const float* terms, uint32_t ng, int la
     const float* tt = terms + lane * MV_TERMS;
     float c = chain;
     uint32_t i = 0;
-    for (; i + 4 <= ng; i += 4) {
-      const float4 q = *reinterpret_cast<const float4*>(tt + i);
-      c = __fadd_rn(c, q.x);
-      c = __fadd_rn(c, q.y);
-      c = __fadd_rn(c, q.z);
-      c = __fadd_rn(c, q.w);
+    for (; i + 32 <= ng; i += 32) {  // eight loads in flight, then the dependent adds
+      float4 q[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) q[u] = *reinterpret_cast<const float4*>(tt + i + 4 * u);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        c = __fadd_rn(c, q[u].x);
+        c = __fadd_rn(c, q[u].y);
+        c = __fadd_rn(c, q[u].z);
+        c = __fadd_rn(c, q[u].w);
+      }
     }
     for (; i < ng; ++i) c = __fadd_rn(c, tt[i]);
     chain = c;
@@ -503,8 +558,9 @@ __device__ __forceinline__ void mv_chain(const float* terms, uint32_t ng, int la
 
 // One row's chunk [k0, k0+kn) from the stage, accumulated into acc[NT]; for
 // the exact-fold formats lane t's acc[0] is token t's chain and `terms` this
-// warp's buffer.
-template <int FMT, int NT, bool SF16>
+// warp's buffer, or with FW (fold warp) the row's fold-slot row, which takes
+// the chunk's block terms in group order and no chain is walked here.
+template <int FMT, int NT, bool SF16, bool FW = false>
 __device__ __forceinline__ void mv_row_chunk(const uint8_t* wrow, const uint8_t* srow, const uint8_t* smem,
                                              const MvLayout& L, uint32_t K, uint32_t k0, uint32_t kn, int lane,
                                              float (&acc)[NT], float* terms) {
@@ -544,11 +600,12 @@ __device__ __forceinline__ void mv_row_chunk(const uint8_t* wrow, const uint8_t*
           if (v[u] && !(lane & 1)) {
             // block term ((f32)isum * ws) * xs; group u*16 + lane/2 of this pass
             const float p = __fmul_rn(__fmul_rn((float)s[u], wsc[u]), xs[t * (K / 32) + (k0 >> 5) + (c >> 1)]);
-            terms[t * MV_TERMS + u * 16 + (lane >> 1)] = p;
+            if (FW) terms[c >> 1] = p;
+            else terms[t * MV_TERMS + u * 16 + (lane >> 1)] = p;
           }
         }
       }
-      mv_chain<NT>(terms, min(MV_TERMS, (nck - c0) >> 1), lane, acc[0]);
+      if (!FW) mv_chain<NT>(terms, min(MV_TERMS, (nck - c0) >> 1), lane, acc[0]);
     }
   } else if (FMT == FMT_Q4) {
     const int8_t* xq = reinterpret_cast<const int8_t*>(smem + L.x_off);
@@ -584,10 +641,11 @@ __device__ __forceinline__ void mv_row_chunk(const uint8_t* wrow, const uint8_t*
           s = dp4a((w[u].w >> 4) & 0x0F0F0F0F, xh.w, s);
           s -= 8 * xsum[t * nb + kb];  // sum (q-8)*x exactly
           const float p = __fmul_rn(__fmul_rn((float)s, wsc[u]), xs[t * nb + kb]);
-          terms[t * MV_TERMS + u * 32 + lane] = p;  // group u*32 + lane of this pass
+          if (FW) terms[b0 + u * 32 + lane] = p;
+          else terms[t * MV_TERMS + u * 32 + lane] = p;  // group u*32 + lane of this pass
         }
       }
-      mv_chain<NT>(terms, min(MV_TERMS, nbk - b0), lane, acc[0]);
+      if (!FW) mv_chain<NT>(terms, min(MV_TERMS, nbk - b0), lane, acc[0]);
     }
   } else if (FMT == FMT_F16) {
     const float* xf = reinterpret_cast<const float*>(smem + L.x_off);
@@ -765,19 +823,22 @@ __device__ __forceinline__ void mv_row_chunk(const uint8_t* wrow, const uint8_t*
 }
 
 // ---------------------------------------------------------------------------
-// Batch-1/2 passes are capped at 112 registers so that two CTAs (2 x 288
-// threads) share an SM; larger token groups keep their accumulators unspilled.
+// Batch-1/2 passes are capped so that two CTAs share an SM; larger token
+// groups keep their accumulators unspilled.
 template <int FMT, int NT, int EPI, bool SF16, int RPW>
-__global__ void __launch_bounds__(MV_THREADS, (NT <= 2 ? 2 : 1)) mv_kernel(MvArgs a) {
+__global__ void __launch_bounds__(mv_threads<FMT, NT>(), (NT <= 2 ? 2 : 1)) mv_kernel(MvArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   using namespace yl::dev;
+  constexpr bool FW = mv_fold_warp<FMT, NT>();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t K = a.K, kc = a.kc;
   const int S = a.stages;
   constexpr int G = mv_groups(EPI);
-  const MvLayout L = mv_layout<FMT, NT>(K, kc, RPW, S, SF16 ? 2u : 4u, G);
+  const MvLayout L = mv_layout<FMT, NT>(K, kc, RPW, S, SF16 ? 2u : 4u, G, a.pro == PRO_NORM);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar_off);
   uint64_t* empty = full + S;
+  uint64_t* tfull = reinterpret_cast<uint64_t*>(smem + L.fbar_off);  // fold slot written (WPG arrivals)
+  uint64_t* tempty = tfull + S;                                        // fold slot consumed (fold warp)
 
   // Row range: static split (row pairs for SwiGLU, gate/up together), or with
   // a.work the whole matrix, its row sets handed out by an atomic counter.
@@ -812,12 +873,100 @@ __global__ void __launch_bounds__(MV_THREADS, (NT <= 2 ? 2 : 1)) mv_kernel(MvArg
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], WPG);
+      if (FW) {
+        mbar_init(&tfull[s], WPG);
+        mbar_init(&tempty[s], 1);
+      }
     }
     *list_n = 0;
     mbar_fence_init();
   }
   __syncthreads();
   grid_dep_launch();
+
+  if (FW && warp == MV_FOLD_WARP) {
+    // ---------------- fold warp ----------------
+    // Walks the stages in the consumers' order (stage q: group q % G, chunk
+    // (q / G) % nch). Lane r < MV_RS holds the chain of row r of each group's
+    // current row set: ((0 + t_0) + t_1) + ... over the row's block terms in
+    // group order (matmul_q8_slices' sequential `+=`, weight_type.rs:190-201);
+    // after a row set's last chunk it runs the epilogue for its rows.
+    float chain[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) chain[g] = 0.0f;
+    int ended = 0;
+    for (uint32_t q = 0;; ++q) {
+      const int slot = q % S;
+      const uint32_t ph = (q / S) & 1;
+      if (!mbar_wait(&tfull[slot], ph, a.err)) break;
+      const uint8_t* st = smem + L.ring_off + slot * L.stage_bytes + L.fold_off;
+      const uint32_t row0 = reinterpret_cast<const uint32_t*>(st)[0];
+      const uint32_t n = reinterpret_cast<const uint32_t*>(st)[1];
+      const int g = q % G;
+      const uint32_t ch = (q / G) % nch;
+      float v = 0.0f;
+      if (n != MV_END && n != 0 && (uint32_t)lane < n) {
+        const uint32_t kn = min(kc, K - ch * kc), ng = kn / 32;
+        const float* tt = reinterpret_cast<const float*>(st + 16) + lane * L.fold_row;
+#pragma unroll
+        for (int gg = 0; gg < G; ++gg) {
+          if (gg != g) continue;
+          float c = chain[gg];
+          uint32_t i = 0;
+          for (; i + 32 <= ng; i += 32) {  // eight loads in flight, then the dependent adds
+            float4 w4[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) w4[u] = *reinterpret_cast<const float4*>(tt + i + 4 * u);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+              c = __fadd_rn(c, w4[u].x);
+              c = __fadd_rn(c, w4[u].y);
+              c = __fadd_rn(c, w4[u].z);
+              c = __fadd_rn(c, w4[u].w);
+            }
+          }
+          for (; i < ng; ++i) c = __fadd_rn(c, tt[i]);
+          chain[gg] = c;
+          v = c;
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[slot]);  // the slot's terms are read
+      if (n == MV_END) {
+        if (++ended == G) break;
+        continue;
+      }
+      if (n == 0 || ch != nch - 1) continue;
+      // ---- epilogue of the row set: lane r -> row row0 + r ----
+#pragma unroll
+      for (int gg = 0; gg < G; ++gg)
+        if (gg == g) chain[gg] = 0.0f;
+      const uint32_t r = row0 + lane;
+      if (mv_swiglu(EPI)) {
+        const float up = __shfl_down_sync(FULL, v, 1);  // rows 2j (gate), 2j+1 (up)
+        if (!(lane & 1) && (uint32_t)lane + 1 < n) a.out[r / 2] = silu_mul(v, up);
+      } else if ((uint32_t)lane < n) {
+        float* o = a.out + r;
+        if (EPI == EPI_STORE && a.tp_mode == 1) {
+          // tensor parallel: this rank's partial row, flagged, into every
+          // rank's inbox (own one included)
+          const uint32_t flag = *a.tp_epoch * a.tp_nsites + a.tp_site + 1u;
+          const uint64_t e = ((uint64_t)flag << 32) | __float_as_uint(v);
+          for (uint32_t qq = 0; qq < a.tp_world; ++qq)
+            st_volatile_u64(reinterpret_cast<uint64_t*>(a.tp_base[qq] + a.tp_inbox_off) +
+                                (uint64_t)a.tp_rank * a.rows + r, e);
+        } else if (EPI == EPI_STORE) *o = v;
+        else if (EPI == EPI_ADD) *o = __fadd_rn(*o, v);
+        else if (EPI == EPI_QUIRK) *o = (r < a.quirk_cols) ? __fadd_rn(*o, v) : v;
+      }
+    }
+    if (EPI == EPI_SWIGLU_Q8) {  // h complete in global memory before the consumers quantize it
+      __threadfence();
+      named_bar_sync(2, (MV_NCW + 1) * 32);
+    }
+    grid_dep_wait();  // every thread of the grid waits before exit (keeps PDL chains transitive)
+    return;
+  }
 
   if (warp == 0) {
     // ---------------- producer ----------------
@@ -957,21 +1106,40 @@ __global__ void __launch_bounds__(MV_THREADS, (NT <= 2 ? 2 : 1)) mv_kernel(MvArg
     if (g != grp) continue;
     if (!mbar_wait(&full[slot], ph, a.err)) { fin = true; break; }
     const uint32_t n = info_n[slot];
-    if (n == MV_END) { fin = true; break; }
     const uint32_t row0 = info_row[slot];
+    uint8_t* const stage = smem + L.ring_off + slot * L.stage_bytes;
+    if (FW) {  // the slot's fold area is free once the fold warp read its previous use
+      if (!mbar_wait(&tempty[slot], ph ^ 1, a.err)) { fin = true; break; }
+      if (wi == 0 && lane == 0) {
+        reinterpret_cast<uint32_t*>(stage + L.fold_off)[0] = row0;
+        reinterpret_cast<uint32_t*>(stage + L.fold_off)[1] = n;
+      }
+    }
+    if (n == MV_END) {
+      if (FW) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tfull[slot]);
+      }
+      fin = true;
+      break;
+    }
     const uint32_t rend = row0 + n;  // rows of this stage: [row0, rend)
     const uint32_t k0 = ch * kc, kn = min(kc, K - k0);
-    const uint8_t* stage = smem + L.ring_off + slot * L.stage_bytes;
-    float* terms = reinterpret_cast<float*>(smem + L.terms_off) + cw * NT * MV_TERMS;
 #pragma unroll
     for (int rr = 0; rr < RPW; ++rr) {
       const uint32_t rl = wi * RPW + rr;
       if (rl >= n) continue;
-      mv_row_chunk<FMT, NT, SF16>(stage + rl * L.stage_q_row, stage + RS * L.stage_q_row + rl * L.stage_s_row, smem,
-                                  L, K, k0, kn, lane, acc[rr], terms);
+      float* terms = FW ? reinterpret_cast<float*>(stage + L.fold_off + 16) + rl * L.fold_row
+                        : reinterpret_cast<float*>(smem + L.terms_off) + cw * NT * MV_TERMS;
+      mv_row_chunk<FMT, NT, SF16, FW>(stage + rl * L.stage_q_row, stage + RS * L.stage_q_row + rl * L.stage_s_row,
+                                      smem, L, K, k0, kn, lane, acc[rr], terms);
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[slot]);
+    if (lane == 0) {
+      if (FW) mbar_arrive(&tfull[slot]);  // releases the terms (and the header) to the fold warp
+      mbar_arrive(&empty[slot]);
+    }
+    if (FW) continue;  // the fold warp walks the chains and runs the epilogue
     if (n == 0 || ch != nch - 1) continue;
 
     // ---- epilogue for this warp's rows of the finished row set ----
@@ -1044,7 +1212,8 @@ __global__ void __launch_bounds__(MV_THREADS, (NT <= 2 ? 2 : 1)) mv_kernel(MvArg
     // arrival completes it (per-block arrival counters, reset by that CTA).
     const uint32_t hn = a.rows / 2;
     __threadfence();
-    named_bar_sync(1, MV_NCW * 32);
+    if (FW) named_bar_sync(2, (MV_NCW + 1) * 32);  // with the fold warp, which wrote h
+    else named_bar_sync(1, MV_NCW * 32);
     if (dyn) {
       // every listed row set holds RS/2 consecutive h values of one block
       uint32_t* done_b = reinterpret_cast<uint32_t*>(smem + L.red_off);  // [MV_LIST]
@@ -1195,10 +1364,10 @@ cudaError_t mv_launch(const MvArgs& a0, int epi, const LaunchCfg& lc) {
   int stages = 0;
   auto layout = [&](int g) {
     switch (nt) {
-      case 1: return mv_layout<FMT, 1>(a.K, a.kc, rpw, 0, SF16 ? 2u : 4u, g);
-      case 2: return mv_layout<FMT, 2>(a.K, a.kc, rpw, 0, SF16 ? 2u : 4u, g);
-      case 4: return mv_layout<FMT, 4>(a.K, a.kc, rpw, 0, SF16 ? 2u : 4u, g);
-      default: return mv_layout<FMT, 8>(a.K, a.kc, rpw, 0, SF16 ? 2u : 4u, g);
+      case 1: return mv_layout<FMT, 1>(a.K, a.kc, rpw, 0, SF16 ? 2u : 4u, g, a.pro == PRO_NORM);
+      case 2: return mv_layout<FMT, 2>(a.K, a.kc, rpw, 0, SF16 ? 2u : 4u, g, a.pro == PRO_NORM);
+      case 4: return mv_layout<FMT, 4>(a.K, a.kc, rpw, 0, SF16 ? 2u : 4u, g, a.pro == PRO_NORM);
+      default: return mv_layout<FMT, 8>(a.K, a.kc, rpw, 0, SF16 ? 2u : 4u, g, a.pro == PRO_NORM);
     }
   };
   // Ring plan. The stage count S must be a multiple of the group count G:
@@ -1269,7 +1438,8 @@ cudaError_t mv_launch(const MvArgs& a0, int epi, const LaunchCfg& lc) {
   if (e != cudaSuccess) return e;
   const uint32_t grid = matvec_grid(a.rows, epi, lc.grid);
   if (grid == 0) return cudaSuccess;
-  return launch_kernel(kern, dim3(grid), dim3(MV_THREADS), smem, lc, a);
+  const int threads = nt == 1 ? mv_threads<FMT, 1>() : MV_THREADS;
+  return launch_kernel(kern, dim3(grid), dim3(threads), smem, lc, a);
 }
 
 }  // namespace k
