@@ -280,16 +280,19 @@ int yl_session_decode_graph_launches(yl_session* s, int with_logits, uint32_t* o
  * layer qkv, attention, wo, gate/up, down, then lm_head. */
 int yl_profile_decode_step(const yl_model* m, yl_session* s, uint32_t token, uint32_t pos, float* us_out,
                            uint32_t cap, uint32_t* n_out);
-/* Diagnostic: runs one batch-1 decode step of `token` at `pos` exactly as the
+/* Diagnostic, in a build with YL_WITH_TRACE=1 only (YL_ERR_UNSUPPORTED
+ * otherwise): runs one batch-1 decode step of `token` at `pos` exactly as the
  * decode graph does (one graph, programmatic dependent launch) while every
  * matvec and attention CTA stamps the GPU's nanosecond global timer:
  * out[launch * 8192 + cta * 8 + i], i = 0 entry, 1 activations staged
  * (attention: wait released), 2 wait on the preceding kernel released
- * (attention: partials visible), 3 done; RMSNorm prologues also 4 first
- * token's rows loaded, 5 norm factor ready, 6 warp 0's rows quantized, 7 the
- * last warp's; attention also 4 q rotated, 5 first key tile in shared
- * memory, 6 partial ready, 7 merge done (0 where not stamped). Launch order as yl_profile_decode_step;
- * the embedding launch (index 0) is not stamped. Writes up to cap values; *n_launches = launches. */
+ * (attention: every slice's scores visible), 3 done; RMSNorm prologues also 6
+ * warp 0's rows quantized, 7 the last warp's (4, 5: the tensor-parallel
+ * prologue's rows loaded, norm factor ready); attention also 4 q rotated,
+ * 5 first key tile in shared memory, 6 slice scores written, 7 softmax sums
+ * done (0 where not stamped). Launch order as yl_profile_decode_step; the
+ * embedding launch (index 0) is not stamped. Writes up to cap values;
+ * *n_launches = launches. */
 int yl_trace_decode_step(const yl_model* m, yl_session* s, uint32_t token, uint32_t pos, uint64_t* out,
                          uint64_t cap, uint32_t* n_launches);
 

@@ -114,6 +114,11 @@ __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
 __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
 }
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait_group() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
 
 // ---------------------------------------------------------------------------
 // General attention (any batch): one CTA per (query head, block of AE_QB
@@ -334,6 +339,7 @@ constexpr int AD_MAXCS = 16;     // largest cluster (non-portable size)
 constexpr int AD_MAXSLOT = 4;    // output 32-blocks one CTA takes: KVM*HD/32/cs <= 8*128/32/8
 
 constexpr int AD_ECH = 2048;     // positions of exp weights staged per chunk (per block)
+constexpr int AD_VROWS = 512;    // V rows (32 dims each) fetched into shared memory at entry, per CTA
 
 template <int HD>
 struct AdSmem {
@@ -341,6 +347,7 @@ struct AdSmem {
     float ks[AD_TILE][HD + 4];        // phase 1: the slice's K tile
     float ebuf[AD_MAXSLOT][AD_ECH];   // phase 3: exp weights of a chunk, per output block
   };
+  float vbuf[AD_VROWS * 32];       // V columns of the CTA's output blocks, first rows
   float qs[AT_MAXKV][HD];
   float nk[HD];                   // owner: the new key, rotated
   float wred[AD_THREADS / 32][AD_MAXSLOT];
@@ -383,6 +390,11 @@ __global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(AttnDecodeArgs 
   };
   uint32_t t0 = p_begin, tn = min((uint32_t)AD_TILE, p_end - p_begin);
   if (tn) issue_tile(t0, tn);
+  cp_async_commit();
+  constexpr uint32_t BPH = HD / 32;  // 32-blocks per head
+  const uint32_t nblk = KVM * BPH;
+  const uint32_t nmine = rank < nblk ? (nblk - rank + cs - 1) / cs : 0;
+  const uint32_t vrows = nmine ? min(nvis, (uint32_t)AD_VROWS / nmine) : 0;
   if (a.early_kv) grid_dep_wait();
   if (trace && tid == 0) ts[1] = globaltimer();
 
@@ -409,6 +421,20 @@ __global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(AttnDecodeArgs 
   if (owner)
     for (uint32_t d = tid; d < HD; d += AD_THREADS)
       a.vcache[(uint64_t)pos * a.kv_dim + kvh * HD + d] = a.qkv[att + a.kv_dim + kvh * HD + d];
+  // The V columns of this CTA's output blocks (blocks rank, rank + cs, ...,
+  // 32 dimensions each), first `vrows` positions, into shared memory: they
+  // do not depend on this step's scores, and rows below pos were written by
+  // earlier steps. Row pos (the new value row) is placed from qkv later.
+  for (uint32_t i = 0; i < nmine; ++i) {
+    const uint32_t d0 = ((rank + i * cs) % BPH) * 32;
+    float* vb = sm.vbuf + i * vrows * 32;
+    for (uint32_t e = tid; e < vrows * 8; e += AD_THREADS) {
+      const uint32_t r = e / 8, c4 = e % 8;
+      if (r == pos) continue;
+      cp_async16(vb + r * 32 + 4 * c4, vbase + (uint64_t)r * a.kv_dim + d0 + 4 * c4);
+    }
+  }
+  cp_async_commit();
   if (trace && tid == 0) ts[4] = globaltimer();
 
   // ---- 1. scores of the slice: thread (head tid/64 + 4m, key tid%64) ----
@@ -419,8 +445,11 @@ __global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(AttnDecodeArgs 
     if (ti > 0) {
       __syncthreads();  // the previous tile is consumed
       issue_tile(t0, tn);
+      cp_async_commit();
+      cp_async_wait_group<0>();
+    } else {
+      cp_async_wait_group<1>();  // the first tile; the V group may still be in flight
     }
-    cp_async_wait_all();
     __syncthreads();  // rotated q / nk and the tile are in place
     if (owner && pos >= t0 && pos < t0 + tn)
       for (uint32_t d = tid; d < HD; d += AD_THREADS) sm.ks[pos - t0][d] = sm.nk[d];
@@ -437,11 +466,18 @@ __global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(AttnDecodeArgs 
   if (trace && tid == 0) ts[2] = globaltimer();
 
   // ---- 2. the CTA's output blocks: block b = rank + i*cs, head b / BPH ----
-  constexpr uint32_t BPH = HD / 32;  // 32-blocks per head
-  const uint32_t nblk = KVM * BPH;
-  const uint32_t nmine = rank < nblk ? (nblk - rank + cs - 1) / cs : 0;
   auto head_of = [&](uint32_t i) { return (rank + i * cs) / BPH; };
-  // max(-1e10, scores) of each block's head, the whole row at once
+  // max(-1e10, scores), e = exp(s - max) and the sums of each block's head.
+  // Rows that fit one chunk are read once into shared memory; longer rows
+  // take a pass for the max, then chunk by chunk exp and sums (the scores in
+  // sc are only read: the CTAs sharing a head each keep their own weights).
+  const uint32_t nchunk = (nvis + AD_ECH - 1) / AD_ECH;
+  auto fill_chunk = [&](uint32_t c0, uint32_t cn) {
+    for (uint32_t i = 0; i < nmine; ++i) {
+      const float* w = sc0 + (uint64_t)head_of(i) * a.sc_stride + c0;
+      for (uint32_t j = tid; j < cn; j += AD_THREADS) sm.ebuf[i][j] = yl_expf(__fsub_rn(__ldcg(w + j), sm.gmax[i]));
+    }
+  };
   {
     float m[AD_MAXSLOT];
 #pragma unroll
@@ -449,7 +485,11 @@ __global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(AttnDecodeArgs 
       m[i] = -1e10f;
       if ((uint32_t)i < nmine) {
         const float* w = sc0 + (uint64_t)head_of(i) * a.sc_stride;
-        for (uint32_t t2 = tid; t2 < nvis; t2 += AD_THREADS) m[i] = fmaxf(m[i], __ldcg(w + t2));
+        for (uint32_t t2 = tid; t2 < nvis; t2 += AD_THREADS) {
+          const float v = __ldcg(w + t2);
+          if (nchunk == 1) sm.ebuf[i][t2] = v;
+          m[i] = fmaxf(m[i], v);
+        }
       }
       m[i] = warp_max(m[i]);
       if (lane == 0) sm.wred[warp][i] = m[i];
@@ -463,19 +503,14 @@ __global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(AttnDecodeArgs 
     }
     __syncthreads();
   }
-  // e = exp(s - max) chunk by chunk into shared memory; lane 0 of warp i
-  // extends block i's sum over the chunk. The scores in sc are only read:
-  // the CTAs sharing a head each keep their own weights.
-  const uint32_t nchunk = (nvis + AD_ECH - 1) / AD_ECH;
-  auto fill_chunk = [&](uint32_t c0, uint32_t cn) {
-    for (uint32_t i = 0; i < nmine; ++i) {
-      const float* w = sc0 + (uint64_t)head_of(i) * a.sc_stride + c0;
-      for (uint32_t j = tid; j < cn; j += AD_THREADS) sm.ebuf[i][j] = yl_expf(__fsub_rn(__ldcg(w + j), sm.gmax[i]));
-    }
-  };
   for (uint32_t c = 0; c < nchunk; ++c) {
     const uint32_t c0 = c * AD_ECH, cn = min((uint32_t)AD_ECH, nvis - c0);
-    fill_chunk(c0, cn);
+    if (nchunk == 1) {
+      for (uint32_t i = 0; i < nmine; ++i)
+        for (uint32_t j = tid; j < cn; j += AD_THREADS) sm.ebuf[i][j] = yl_expf(__fsub_rn(sm.ebuf[i][j], sm.gmax[i]));
+    } else {
+      fill_chunk(c0, cn);
+    }
     __syncthreads();
     if (lane == 0 && (uint32_t)warp < nmine) {
       const float* eb = sm.ebuf[warp];
@@ -498,6 +533,15 @@ __global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(AttnDecodeArgs 
     }
     __syncthreads();  // ebuf is rewritten by the next chunk (or read below)
   }
+  if (trace && tid == 0) ts[7] = globaltimer();
+  // the staged V columns have landed; the new value row goes in from qkv
+  cp_async_wait_group<0>();
+  if (pos < vrows)
+    for (uint32_t i = 0; i < nmine; ++i)
+      if (tid < 32)
+        sm.vbuf[(i * vrows + pos) * 32 + tid] =
+            a.qkv[att + a.kv_dim + kvh * HD + ((rank + i * cs) % BPH) * 32 + tid];
+  __syncthreads();
   // P.V: warp l runs lane l of the sums (positions l, l + 8, ...) for every
   // block of the CTA, chunk by chunk (a single chunk is still in ebuf); the
   // lane chains carry over chunk boundaries, which are multiples of 8
@@ -522,16 +566,27 @@ __global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(AttnDecodeArgs 
       const uint32_t b = rank + i * cs, d = (b % BPH) * 32 + lane;
       const float* vcol = vbase + d;
       const float* eb = sm.ebuf[i] - c0;
+      const float* vs = sm.vbuf + i * vrows * 32 + lane;
       float s = acc[i];
       uint32_t t2 = c0 + warp;
-      for (; t2 + 128 <= cend; t2 += 128) {  // sixteen positions' V loads in flight
+      const uint32_t send = min(cend, vrows);  // rows below send are in shared memory
+      for (; t2 + 64 <= send; t2 += 64) {
+        float vv[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) vv[u] = vs[(t2 + 8 * u) * 32];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) s = __fadd_rn(s, __fmul_rn(__fmul_rn(eb[t2 + 8 * u], inv[i]), vv[u]));
+      }
+      for (; t2 < send; t2 += 8) s = __fadd_rn(s, __fmul_rn(__fmul_rn(eb[t2], inv[i]), vs[t2 * 32]));
+      for (; t2 < cend; t2 += 128) {  // rows past the staged ones: sixteen positions' loads in flight
         float vv[16];
 #pragma unroll
-        for (int u = 0; u < 16; ++u) vv[u] = __ldcg(vcol + (uint64_t)(t2 + 8 * u) * a.kv_dim);  // row pos: the owner's write
+        for (int u = 0; u < 16; ++u)
+          vv[u] = t2 + 8 * u < cend ? __ldcg(vcol + (uint64_t)(t2 + 8 * u) * a.kv_dim) : 0.0f;  // row pos: the owner's write
 #pragma unroll
-        for (int u = 0; u < 16; ++u) s = __fadd_rn(s, __fmul_rn(__fmul_rn(eb[t2 + 8 * u], inv[i]), vv[u]));
+        for (int u = 0; u < 16; ++u)
+          if (t2 + 8 * u < cend) s = __fadd_rn(s, __fmul_rn(__fmul_rn(eb[t2 + 8 * u], inv[i]), vv[u]));
       }
-      for (; t2 < cend; t2 += 8) s = __fadd_rn(s, __fmul_rn(__fmul_rn(eb[t2], inv[i]), __ldcg(vcol + (uint64_t)t2 * a.kv_dim)));
       acc[i] = s;
     }
   }
@@ -544,8 +599,10 @@ __global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(AttnDecodeArgs 
       float o = reduce_add8(sm.lanes[0][lane], sm.lanes[1][lane], sm.lanes[2][lane], sm.lanes[3][lane],
                             sm.lanes[4][lane], sm.lanes[5][lane], sm.lanes[6][lane], sm.lanes[7][lane]);
       const uint32_t c0 = (nchunk - 1) * AD_ECH;
-      for (uint32_t tt = nsimd8; tt < nvis; ++tt)
-        o = __fadd_rn(o, __fmul_rn(__fmul_rn(sm.ebuf[i][tt - c0], inv[i]), __ldcg(vbase + d + (uint64_t)tt * a.kv_dim)));
+      for (uint32_t tt = nsimd8; tt < nvis; ++tt) {
+        const float vv = tt < vrows ? sm.vbuf[(i * vrows + tt) * 32 + lane] : __ldcg(vbase + d + (uint64_t)tt * a.kv_dim);
+        o = __fadd_rn(o, __fmul_rn(__fmul_rn(sm.ebuf[i][tt - c0], inv[i]), vv));
+      }
       const uint64_t k = (uint64_t)(kvh * KVM + hh) * HD + d;
       if (a.out) a.out[k] = o;
       if (a.q8) {
@@ -559,7 +616,6 @@ __global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(AttnDecodeArgs 
   }
   if (trace && tid == 0) {
     ts[3] = globaltimer();
-    ts[7] = ts[3];
     for (int i = 0; i < 8; ++i) trace[i] = ts[i];
   }
 }

@@ -195,10 +195,19 @@ __device__ __forceinline__ float rms_factor_smem8(const float* x, uint32_t n, fl
   float acc = 0.0f;
   const uint32_t nj = n / 8;
   uint32_t j = 0;
-  for (; j + 16 <= nj; j += 16) {
+  if (nj >= 16) {  // software-pipelined: the next 16 squares load while these 16 add
     float v[16];
 #pragma unroll
-    for (int u = 0; u < 16; ++u) v[u] = x[8 * (j + u) + l];
+    for (int u = 0; u < 16; ++u) v[u] = x[8 * u + l];
+    for (j = 16; j + 16 <= nj; j += 16) {
+      float nv[16];
+#pragma unroll
+      for (int u = 0; u < 16; ++u) nv[u] = x[8 * (j + u) + l];
+#pragma unroll
+      for (int u = 0; u < 16; ++u) acc = __fadd_rn(acc, __fmul_rn(v[u], v[u]));
+#pragma unroll
+      for (int u = 0; u < 16; ++u) v[u] = nv[u];
+    }
 #pragma unroll
     for (int u = 0; u < 16; ++u) acc = __fadd_rn(acc, __fmul_rn(v[u], v[u]));
   }

@@ -72,7 +72,7 @@ constexpr uint32_t MV_END = 0xFFFFFFFFu;  // stage info: no more row sets
 
 // Shared-memory layout, computed identically on host and device.
 struct MvLayout {
-  uint32_t bar_off, info_off, red_off, fbar_off, x_off, xs_off, xsum_off, terms_off, ring_off;
+  uint32_t bar_off, info_off, red_off, fbar_off, x_off, xs_off, xsum_off, nstage_off, terms_off, ring_off;
   uint32_t stage_q_row, stage_s_row, stage_bytes, total;
   // fold warp: each stage slot carries, after its weight rows, a header
   // {first row, row count} (16 bytes) and MV_RS rows of fold_row floats
@@ -84,10 +84,9 @@ struct MvLayout {
 // groups: consumer groups; a stage holds the rows of one group (MV_NCW/groups
 // warps x rpw rows each).
 template <int FMT, int NT>
-// norm_stage: the RMSNorm prologue stages one f32 row (K floats) at x_off to
-// walk the reference-order sum-of-squares chains from shared memory; the
-// activation region is at least that large (the staged row is dead before
-// the quantized activations are written over it).
+// norm_stage: the RMSNorm prologue stages one f32 row (K floats, at
+// nstage_off) to walk the reference-order sum-of-squares chains from shared
+// memory.
 __host__ __device__ inline MvLayout mv_layout(uint32_t K, uint32_t kc, int rpw, int stages, uint32_t ssz = 4,
                                              int groups = 1, bool norm_stage = false) {
   MvLayout L;
@@ -110,8 +109,16 @@ __host__ __device__ inline MvLayout mv_layout(uint32_t K, uint32_t kc, int rpw, 
     L.xsum_off = off;
     if (FMT == FMT_Q4) off += NT * (K / 32) * 4;
   }
-  if (norm_stage && off < L.x_off + K * 4) off = L.x_off + K * 4;
   off = (off + 15) & ~15u;
+  // RMSNorm prologue: one f32 row staged for the sum-of-squares chains. A
+  // single-token pass overlays it on the activation area (its chains finish
+  // before the quantized row is written there); several tokens need their
+  // own area (earlier tokens' quantized rows stay in place).
+  L.nstage_off = NT == 1 ? L.x_off : off;
+  if (norm_stage) {
+    if (NT == 1) off = off > L.x_off + K * 4 ? off : L.x_off + K * 4;
+    else off += K * 4;
+  }
   L.terms_off = off;  // per consumer warp: [NT][MV_TERMS] block terms of one pass (in-warp fold)
   if (mv_exact_fold<FMT>() && !mv_fold_warp<FMT, NT>()) off += MV_NCW * NT * MV_TERMS * 4;
   off = (off + 127) & ~127u;
@@ -199,23 +206,7 @@ __device__ __forceinline__ void mv_norm_regs(const MvArgs& a, const MvLayout& L,
   // Norm factors of the resident rows in the reference's summation order (one
   // warp, all tokens at once). Tensor-parallel rows exist only in registers
   // (residual + the ranks' partials), so they keep the register-tree sum.
-  float* rfac = red + 32;
-  if (NORM && !tp_in) {
-    // one token at a time: the row is staged in shared memory (coalesced,
-    // every consumer thread), then lanes 0..7 of warp 0 walk the chains
-    float* stg = reinterpret_cast<float*>(smem + L.x_off);
-    for (int t = 0; t < NT && t < (int)a.ntok; ++t) {
-      const float* xr = a.xres + (uint64_t)t * a.x_tok_stride;
-      for (uint32_t i = ctid * 4; i < K; i += MV_NCW * 32 * 4)
-        *reinterpret_cast<float4*>(stg + i) = *reinterpret_cast<const float4*>(xr + i);
-      named_bar_sync(1, MV_NCW * 32);
-      if (cw == 0) {
-        const float r = rms_factor_smem8(stg, K, a.eps, lane);
-        if (lane == 0) rfac[t] = r;
-      }
-      named_bar_sync(1, MV_NCW * 32);  // the staging area is reused / overwritten
-    }
-  }
+  float* const stg = reinterpret_cast<float*>(smem + L.nstage_off);
   for (int t = 0; t < NT; ++t) {
     const bool valid = t < (int)a.ntok;
     const float* xr = a.xres + (uint64_t)t * a.x_tok_stride;
@@ -262,7 +253,25 @@ __device__ __forceinline__ void mv_norm_regs(const MvArgs& a, const MvLayout& L,
     }
     float r = 1.0f;
     if (NORM && !tp_in) {
-      r = valid ? rfac[t] : 1.0f;
+      // the reference's 8-lane sum of squares (util.rs:389-426): the row,
+      // already in registers, is staged in shared memory and lanes 0..7 of
+      // warp 0 walk the eight addition chains from there
+      if (valid) {
+#pragma unroll
+        for (int u = 0; u < MU; ++u) {
+          const uint32_t i = ctid * 4 + u * MV_NCW * 32 * 4;
+          if (i < K) *reinterpret_cast<float4*>(stg + i) = xv[u];
+        }
+      }
+      named_bar_sync(1, MV_NCW * 32);
+      if (kTrace && a.trace && t == 0 && ctid == 0) a.trace[(uint64_t)blockIdx.x * 8 + 4] = globaltimer();
+      if (cw == 0 && valid) {
+        const float rv = rms_factor_smem8(stg, K, a.eps, lane);
+        if (lane == 0) red[32 + t] = rv;
+      }
+      named_bar_sync(1, MV_NCW * 32);  // the factor is published; stg is reused by the next token
+      if (kTrace && a.trace && t == 0 && ctid == 0) a.trace[(uint64_t)blockIdx.x * 8 + 5] = globaltimer();
+      r = valid ? red[32 + t] : 1.0f;
     } else if (NORM) {
       float ss = 0.0f;
 #pragma unroll
@@ -427,8 +436,8 @@ __device__ __forceinline__ void mv_stage_x(const MvArgs& a, const MvLayout& L, u
   mv_wait_inputs(a);
   if (a.pro == PRO_NORM) {
     // norm factors in the reference's summation order, each row staged in
-    // shared memory first (the layout reserves K floats at x_off)
-    float* stg = reinterpret_cast<float*>(smem + L.x_off);
+    // shared memory first (the layout reserves K floats at nstage_off)
+    float* stg = reinterpret_cast<float*>(smem + L.nstage_off);
     for (int t = 0; t < NT && t < (int)a.ntok; ++t) {
       const float* xr = a.xres + (uint64_t)t * a.x_tok_stride;
       for (uint32_t i = ctid * 4; i < K; i += MV_NCW * 32 * 4)
