@@ -421,20 +421,6 @@ __global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(AttnDecodeArgs 
   if (owner)
     for (uint32_t d = tid; d < HD; d += AD_THREADS)
       a.vcache[(uint64_t)pos * a.kv_dim + kvh * HD + d] = a.qkv[att + a.kv_dim + kvh * HD + d];
-  // The V columns of this CTA's output blocks (blocks rank, rank + cs, ...,
-  // 32 dimensions each), first `vrows` positions, into shared memory: they
-  // do not depend on this step's scores, and rows below pos were written by
-  // earlier steps. Row pos (the new value row) is placed from qkv later.
-  for (uint32_t i = 0; i < nmine; ++i) {
-    const uint32_t d0 = ((rank + i * cs) % BPH) * 32;
-    float* vb = sm.vbuf + i * vrows * 32;
-    for (uint32_t e = tid; e < vrows * 8; e += AD_THREADS) {
-      const uint32_t r = e / 8, c4 = e % 8;
-      if (r == pos) continue;
-      cp_async16(vb + r * 32 + 4 * c4, vbase + (uint64_t)r * a.kv_dim + d0 + 4 * c4);
-    }
-  }
-  cp_async_commit();
   if (trace && tid == 0) ts[4] = globaltimer();
 
   // ---- 1. scores of the slice: thread (head tid/64 + 4m, key tid%64) ----
@@ -446,10 +432,8 @@ __global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(AttnDecodeArgs 
       __syncthreads();  // the previous tile is consumed
       issue_tile(t0, tn);
       cp_async_commit();
-      cp_async_wait_group<0>();
-    } else {
-      cp_async_wait_group<1>();  // the first tile; the V group may still be in flight
     }
+    cp_async_wait_group<0>();
     __syncthreads();  // rotated q / nk and the tile are in place
     if (owner && pos >= t0 && pos < t0 + tn)
       for (uint32_t d = tid; d < HD; d += AD_THREADS) sm.ks[pos - t0][d] = sm.nk[d];
@@ -462,6 +446,21 @@ __global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(AttnDecodeArgs 
     }
   }
   if (trace && tid == 0) ts[6] = globaltimer();
+  // The V columns of this CTA's output blocks (blocks rank, rank + cs, ...,
+  // 32 dimensions each), first `vrows` positions, into shared memory: they
+  // do not depend on this step's scores, and rows below pos were written by
+  // earlier steps (issued here, they land while the cluster syncs and the
+  // softmax sums run). Row pos (the new value row) is placed from qkv later.
+  for (uint32_t i = 0; i < nmine; ++i) {
+    const uint32_t d0 = ((rank + i * cs) % BPH) * 32;
+    float* vb = sm.vbuf + i * vrows * 32;
+    for (uint32_t e = tid; e < vrows * 8; e += AD_THREADS) {
+      const uint32_t r = e / 8, c4 = e % 8;
+      if (r == pos) continue;
+      cp_async16(vb + r * 32 + 4 * c4, vbase + (uint64_t)r * a.kv_dim + d0 + 4 * c4);
+    }
+  }
+  cp_async_commit();
   cluster.sync();  // every slice's scores and the new cache rows are visible to the cluster
   if (trace && tid == 0) ts[2] = globaltimer();
 
@@ -516,10 +515,24 @@ __global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(AttnDecodeArgs 
       const float* eb = sm.ebuf[warp];
       float s = sm.sum[warp];
       uint32_t j = 0;
-      for (; j + 16 <= cn; j += 16) {
+      if (cn >= 16) {  // software-pipelined: the next 16 weights load while these 16 add
         float4 v[4];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) v[u] = *reinterpret_cast<const float4*>(eb + j + 4 * u);
+        for (int u = 0; u < 4; ++u) v[u] = *reinterpret_cast<const float4*>(eb + 4 * u);
+        for (j = 16; j + 16 <= cn; j += 16) {
+          float4 nv[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) nv[u] = *reinterpret_cast<const float4*>(eb + j + 4 * u);
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            s = __fadd_rn(s, v[u].x);
+            s = __fadd_rn(s, v[u].y);
+            s = __fadd_rn(s, v[u].z);
+            s = __fadd_rn(s, v[u].w);
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u) v[u] = nv[u];
+        }
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           s = __fadd_rn(s, v[u].x);
@@ -599,10 +612,17 @@ __global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(AttnDecodeArgs 
       float o = reduce_add8(sm.lanes[0][lane], sm.lanes[1][lane], sm.lanes[2][lane], sm.lanes[3][lane],
                             sm.lanes[4][lane], sm.lanes[5][lane], sm.lanes[6][lane], sm.lanes[7][lane]);
       const uint32_t c0 = (nchunk - 1) * AD_ECH;
-      for (uint32_t tt = nsimd8; tt < nvis; ++tt) {
-        const float vv = tt < vrows ? sm.vbuf[(i * vrows + tt) * 32 + lane] : __ldcg(vbase + d + (uint64_t)tt * a.kv_dim);
-        o = __fadd_rn(o, __fmul_rn(__fmul_rn(sm.ebuf[i][tt - c0], inv[i]), vv));
+      float vt[8];  // the tail's (at most 7) V values, loaded ahead of the chain
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const uint32_t tt = nsimd8 + u;
+        vt[u] = tt >= nvis ? 0.0f
+                           : tt < vrows ? sm.vbuf[(i * vrows + tt) * 32 + lane]
+                                        : __ldcg(vbase + d + (uint64_t)tt * a.kv_dim);
       }
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (nsimd8 + u < nvis) o = __fadd_rn(o, __fmul_rn(__fmul_rn(sm.ebuf[i][nsimd8 + u - c0], inv[i]), vt[u]));
       const uint64_t k = (uint64_t)(kvh * KVM + hh) * HD + d;
       if (a.out) a.out[k] = o;
       if (a.q8) {

@@ -200,16 +200,22 @@ __device__ __forceinline__ float rms_factor_smem8(const float* x, uint32_t n, fl
 #pragma unroll
     for (int u = 0; u < 16; ++u) v[u] = x[8 * u + l];
     for (j = 16; j + 16 <= nj; j += 16) {
-      float nv[16];
+      float nv[16], sq[16];
 #pragma unroll
       for (int u = 0; u < 16; ++u) nv[u] = x[8 * (j + u) + l];
+      // the squares first, so the adds issue back to back on the chain
 #pragma unroll
-      for (int u = 0; u < 16; ++u) acc = __fadd_rn(acc, __fmul_rn(v[u], v[u]));
+      for (int u = 0; u < 16; ++u) sq[u] = __fmul_rn(v[u], v[u]);
+#pragma unroll
+      for (int u = 0; u < 16; ++u) acc = __fadd_rn(acc, sq[u]);
 #pragma unroll
       for (int u = 0; u < 16; ++u) v[u] = nv[u];
     }
+    float sq[16];
 #pragma unroll
-    for (int u = 0; u < 16; ++u) acc = __fadd_rn(acc, __fmul_rn(v[u], v[u]));
+    for (int u = 0; u < 16; ++u) sq[u] = __fmul_rn(v[u], v[u]);
+#pragma unroll
+    for (int u = 0; u < 16; ++u) acc = __fadd_rn(acc, sq[u]);
   }
   for (; j < nj; ++j) {
     const float v = x[8 * j + l];
