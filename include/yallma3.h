@@ -183,10 +183,21 @@ typedef struct yl_shape {
 } yl_shape;
 
 /* lib.rs:107-133 `load_transformer(path, sequential, max_ctx_len, fmt_override)`.
- * Dispatch by extension: .gguf (architecture must be "llama"). fmt_override
- * = -1 keeps general.file_type; `sequential` selects nothing on the device
- * path (kept for signature parity). Weights are parsed on the host, repacked
- * and uploaded to the current CUDA device. */
+ * Dispatch by extension:
+ *  - .gguf (architecture must be "llama"; fmt_override = -1 keeps
+ *    general.file_type);
+ *  - .safetensors with config.json beside it (transformer_llama_st.rs): MLX
+ *    affine 8-bit weights are requantized to symmetric Q8 with f32 scales
+ *    (util.rs:451-518), F16 weights when config.json has no "quantization"
+ *    section; a "Q4_0" quant_type gives YL_ERR_UNSUPPORTED (the reference
+ *    runs its Q4_0 kernel on requantized Q8 tensors there). BOS/EOS come
+ *    from tokenizer.json, else tokenizer.bin;
+ *  - .lmrs (transformer_llama_lmrs.rs): Q8 with f32 scales whatever the
+ *    override; tokenizer.bin beside it supplies BOS/EOS.
+ * Quantized files must use groups of 32 (YL_ERR_UNSUPPORTED otherwise).
+ * `sequential` selects nothing on the device path: the forward is
+ * forward.rs's llama_forward_x for every format. Weights are parsed on the
+ * host, repacked and uploaded to the current CUDA device. */
 int yl_load_transformer(const char* path, int sequential, uint32_t max_ctx_len, int fmt_override,
                         yl_model** out);
 /* Tensor parallelism (no counterpart in the reference, which runs on one

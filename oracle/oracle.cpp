@@ -636,7 +636,7 @@ extern "C" {
 
 const char* orc_last_error(void) { return g_err.c_str(); }
 
-orc_model* orc_model_load(const char* path, uint32_t max_ctx_len, int fmt_override, int q4_mode) {
+static orc_model* load_gguf(const char* path, uint32_t max_ctx_len, int fmt_override, int q4_mode) {
   int fd = open(path, O_RDONLY);
   if (fd < 0) { g_err = std::string("cannot open ") + path; return nullptr; }
   struct stat st;
@@ -776,6 +776,23 @@ orc_model* orc_model_load(const char* path, uint32_t max_ctx_len, int fmt_overri
   return m.release();
 }
 
+/* Loaders of the other two model files (below): safetensors + config.json
+ * (transformer_llama_st.rs:41-372) and lm.rs (transformer_llama_lmrs.rs:56-439). */
+static orc_model* load_st(const char* path, uint32_t max_ctx_len, int fmt_override);
+static orc_model* load_lmrs(const char* path, uint32_t max_ctx_len);
+
+/* lib.rs:107-133: dispatch by file extension. */
+orc_model* orc_model_load(const char* path, uint32_t max_ctx_len, int fmt_override, int q4_mode) {
+  std::string p(path);
+  size_t dot = p.rfind('.'), slash = p.rfind('/');
+  std::string ext = (dot == std::string::npos || (slash != std::string::npos && dot < slash)) ? "" : p.substr(dot + 1);
+  if (ext == "gguf") return load_gguf(path, max_ctx_len, fmt_override, q4_mode);
+  if (ext == "safetensors") return load_st(path, max_ctx_len, fmt_override);
+  if (ext == "lmrs") return load_lmrs(path, max_ctx_len);
+  g_err = "Unsupported model extension for path: " + p;
+  return nullptr;
+}
+
 void orc_model_free(orc_model* m) { delete m; }
 
 int orc_model_shape(const orc_model* m, orc_shape* out) {
@@ -906,4 +923,482 @@ extern "C" int orc_forward_x(const orc_model* m, orc_session* sess, const uint32
   const std::vector<float>& E = m->lm_head.empty() ? m->token_embedding : m->lm_head;
   for (size_t vv = 0; vv < sh.vocab_size; ++vv) logits[vv] = dot8(last, &E[vv * dim], dim);
   return 0;
+}
+
+/* ===================== safetensors and lm.rs loaders ====================== */
+namespace {
+
+/* A JSON value: the subset the two loaders read (serde_json semantics for
+ * as_u64: non-negative integer literals only; as_f64: any number). */
+struct JV {
+  char t = 'n'; /* n null, b bool, d number, s string, a array, o object */
+  double num = 0;
+  bool uint_lit = false;
+  unsigned long long u = 0;
+  std::string s;
+  std::vector<JV> a;
+  std::vector<std::pair<std::string, JV>> o;
+  const JV* at(const char* k) const { /* last duplicate wins */
+    const JV* r = nullptr;
+    if (t == 'o')
+      for (auto& kv : o)
+        if (kv.first == k) r = &kv.second;
+    return r;
+  }
+};
+
+struct JP {
+  const char* p;
+  const char* e;
+  bool ok = true;
+  void sp() { while (p < e && (*p == ' ' || *p == '\n' || *p == '\r' || *p == '\t')) ++p; }
+  bool str(std::string* out) {
+    if (p >= e || *p != '"') return ok = false;
+    ++p;
+    while (p < e && *p != '"') {
+      if (*p == '\\') {
+        if (++p >= e) return ok = false;
+        char c = *p++;
+        if (c == 'u') {
+          if (e - p < 4) return ok = false;
+          unsigned cp = (unsigned)strtoul(std::string(p, 4).c_str(), nullptr, 16);
+          p += 4;
+          if (cp >= 0xD800 && cp < 0xDC00 && e - p >= 6 && p[0] == '\\' && p[1] == 'u') {
+            unsigned lo = (unsigned)strtoul(std::string(p + 2, 4).c_str(), nullptr, 16);
+            p += 6;
+            cp = 0x10000 + ((cp - 0xD800) << 10) + (lo - 0xDC00);
+          }
+          if (cp < 0x80) out->push_back((char)cp);
+          else if (cp < 0x800) { out->push_back((char)(0xC0 | (cp >> 6))); out->push_back((char)(0x80 | (cp & 63))); }
+          else if (cp < 0x10000) {
+            out->push_back((char)(0xE0 | (cp >> 12)));
+            out->push_back((char)(0x80 | ((cp >> 6) & 63)));
+            out->push_back((char)(0x80 | (cp & 63)));
+          } else {
+            out->push_back((char)(0xF0 | (cp >> 18)));
+            out->push_back((char)(0x80 | ((cp >> 12) & 63)));
+            out->push_back((char)(0x80 | ((cp >> 6) & 63)));
+            out->push_back((char)(0x80 | (cp & 63)));
+          }
+        } else {
+          const char* from = "\"\\/bfnrt";
+          const char* to = "\"\\/\b\f\n\r\t";
+          const char* f = strchr(from, c);
+          if (!f || !c) return ok = false;
+          out->push_back(to[f - from]);
+        }
+      } else {
+        out->push_back(*p++);
+      }
+    }
+    if (p >= e) return ok = false;
+    ++p;
+    return true;
+  }
+  JV val(int depth) {
+    JV v;
+    sp();
+    if (p >= e || depth > 64) { ok = false; return v; }
+    if (*p == '{') {
+      v.t = 'o';
+      ++p;
+      sp();
+      if (p < e && *p == '}') { ++p; return v; }
+      while (ok) {
+        sp();
+        std::string k;
+        if (!str(&k)) break;
+        sp();
+        if (p >= e || *p != ':') { ok = false; break; }
+        ++p;
+        JV x = val(depth + 1);
+        v.o.emplace_back(k, x);
+        sp();
+        if (p < e && *p == ',') { ++p; continue; }
+        if (p < e && *p == '}') { ++p; break; }
+        ok = false;
+      }
+    } else if (*p == '[') {
+      v.t = 'a';
+      ++p;
+      sp();
+      if (p < e && *p == ']') { ++p; return v; }
+      while (ok) {
+        v.a.push_back(val(depth + 1));
+        sp();
+        if (p < e && *p == ',') { ++p; continue; }
+        if (p < e && *p == ']') { ++p; break; }
+        ok = false;
+      }
+    } else if (*p == '"') {
+      v.t = 's';
+      str(&v.s);
+    } else if (e - p >= 4 && !strncmp(p, "true", 4)) {
+      v.t = 'b'; p += 4;
+    } else if (e - p >= 5 && !strncmp(p, "false", 5)) {
+      v.t = 'b'; p += 5;
+    } else if (e - p >= 4 && !strncmp(p, "null", 4)) {
+      p += 4;
+    } else {
+      const char* b = p;
+      while (p < e && strchr("+-0123456789.eE", *p)) ++p;
+      std::string tok(b, p - b);
+      if (tok.empty()) { ok = false; return v; }
+      v.t = 'd';
+      v.num = strtod(tok.c_str(), nullptr);
+      bool digits = tok.find_first_not_of("0123456789") == std::string::npos;
+      if (digits && tok.size() < 20) { v.uint_lit = true; v.u = strtoull(tok.c_str(), nullptr, 10); }
+    }
+    return v;
+  }
+};
+
+bool json_read(const char* p, size_t n, JV* out) {
+  JP jp{p, p + n};
+  *out = jp.val(0);
+  jp.sp();
+  return jp.ok && jp.p == jp.e;
+}
+
+bool read_file(const std::string& path, std::string* out) {
+  FILE* f = fopen(path.c_str(), "rb");
+  if (!f) return false;
+  char buf[65536];
+  size_t k;
+  while ((k = fread(buf, 1, sizeof buf, f)) > 0) out->append(buf, k);
+  fclose(f);
+  return true;
+}
+
+std::string parent_dir(const std::string& p) {
+  size_t k = p.rfind('/');
+  return k == std::string::npos ? "." : p.substr(0, k);
+}
+
+/* Tokenizer::new header (tokenizer.rs:223-228) / Tokenizer::from_json added
+ * tokens (tokenizer.rs:179-186): BOS and EOS only. */
+bool tokenizer_ids(const std::string& dir, bool try_json, uint32_t* bos, uint32_t* eos) {
+  std::string t;
+  if (try_json && read_file(dir + "/tokenizer.json", &t)) {
+    JV root;
+    if (!json_read(t.data(), t.size(), &root)) { g_err = "bad tokenizer.json"; return false; }
+    const JV* added = root.at("added_tokens");
+    if (!added || added->t != 'a') { g_err = "tokenizer.json: no added_tokens"; return false; }
+    *bos = 128000u;
+    *eos = 128009u;
+    for (auto& tk : added->a) {
+      const JV* c = tk.at("content");
+      const JV* id = tk.at("id");
+      if (!c || c->t != 's' || !id || !id->uint_lit) { g_err = "tokenizer.json: bad added token"; return false; }
+      if (c->s == "<|begin_of_text|>") *bos = (uint32_t)id->u;
+      if (c->s == "<|end_of_text|>" || c->s == "<|eot_id|>") *eos = (uint32_t)id->u;
+    }
+    return true;
+  }
+  t.clear();
+  if (!read_file(dir + "/tokenizer.bin", &t)) { g_err = "cannot open " + dir + "/tokenizer.bin"; return false; }
+  if (t.size() < 16) { g_err = "tokenizer.bin too short"; return false; }
+  memcpy(bos, t.data() + 8, 4);
+  memcpy(eos, t.data() + 12, 4);
+  return true;
+}
+
+/* Rust `f as i32`: NaN -> 0, saturating. */
+inline int32_t rust_f32_as_i32(float v) {
+  if (v != v) return 0;
+  if (v >= 2147483648.0f) return INT32_MAX;
+  if (v <= -2147483648.0f) return INT32_MIN;
+  return (int32_t)v;
+}
+
+/* util.rs:451-518 load_q8_tensor_st: unpack the u32-packed u8 quants, then
+ * per group: dequantize (q as u8) * scale + bias, symmetric requantize. */
+void load_q8_tensor_st(const uint8_t* data, size_t rows, size_t cols, size_t gs, size_t w_off, size_t s_off,
+                       size_t b_off, QT* out) {
+  size_t n = rows * cols, groups = n / gs, packed_cols = cols / 4;
+  std::vector<int8_t> vals(n);
+  for (size_t r = 0; r < rows; ++r)
+    for (size_t pc = 0; pc < packed_cols; ++pc) {
+      uint32_t packed;
+      memcpy(&packed, data + w_off + (r * packed_cols + pc) * 4, 4);
+      size_t dst = r * cols + pc * 4;
+      for (int b = 0; b < 4; ++b) vals[dst + b] = (int8_t)(uint8_t)(packed >> (8 * b));
+    }
+  out->q.assign(n, 0);
+  out->s.assign(groups, 0.0f);
+  std::vector<float> deq(gs);
+  for (size_t g = 0; g < groups; ++g) {
+    uint16_t sb, bb;
+    memcpy(&sb, data + s_off + g * 2, 2);
+    memcpy(&bb, data + b_off + g * 2, 2);
+    float scale = orc_f16_to_f32(sb), bias = orc_f16_to_f32(bb);
+    size_t start = g * gs, end = start + gs < n ? start + gs : n;
+    float max_abs = 0.0f;
+    for (size_t i = start; i < end; ++i) {
+      float f = (float)(uint8_t)vals[i] * scale + bias;
+      deq[i - start] = f;
+      float a = fabsf(f);
+      if (a > max_abs) max_abs = a;
+    }
+    float sym = max_abs == 0.0f ? 1.0f : max_abs / 127.0f;
+    out->s[g] = sym;
+    for (size_t i = start; i < end; ++i) {
+      int32_t q = rust_f32_as_i32(roundf(deq[i - start] / sym));
+      out->q[i] = (int8_t)(q < -128 ? -128 : q > 127 ? 127 : q);
+    }
+  }
+}
+
+struct StInfo {
+  std::string dtype;
+  size_t off = 0, len = 0;
+};
+
+}  // namespace
+
+static orc_model* load_st(const char* path, uint32_t max_ctx_len, int fmt_override) {
+  std::string dir = parent_dir(path), text;
+  if (!read_file(dir + "/config.json", &text)) { g_err = "cannot open " + dir + "/config.json"; return nullptr; }
+  JV cfg;
+  if (!json_read(text.data(), text.size(), &cfg)) { g_err = "bad config.json"; return nullptr; }
+  auto u = [&](const char* k, uint32_t* v) {
+    const JV* j = cfg.at(k);
+    if (!j || !j->uint_lit) { g_err = std::string("config.json: ") + k; return false; }
+    *v = (uint32_t)j->u;
+    return true;
+  };
+  auto f = [&](const char* k, float* v) {
+    const JV* j = cfg.at(k);
+    if (!j || j->t != 'd') { g_err = std::string("config.json: ") + k; return false; }
+    *v = (float)j->num;
+    return true;
+  };
+  orc_shape s;
+  memset(&s, 0, sizeof(s));
+  uint32_t max_seq_len;
+  /* transformer_llama_st.rs:50-59 */
+  if (!u("hidden_size", &s.dim) || !u("intermediate_size", &s.hidden_dim) || !u("num_attention_heads", &s.n_heads) ||
+      !u("num_key_value_heads", &s.n_kv_heads) || !u("head_dim", &s.head_size) ||
+      !u("num_hidden_layers", &s.n_layers) || !u("vocab_size", &s.vocab_size) || !f("rms_norm_eps", &s.rms_norm_eps) ||
+      !f("rope_theta", &s.rope_theta) || !u("max_position_embeddings", &max_seq_len))
+    return nullptr;
+  /* :62-91 */
+  const JV* q = cfg.at("quantization");
+  uint32_t gs = 32;
+  if (q && q->at("group_size") && q->at("group_size")->uint_lit) gs = (uint32_t)q->at("group_size")->u;
+  int fmt;
+  if (fmt_override >= 0) fmt = fmt_override;
+  else if (!q) fmt = ORC_F16;
+  else {
+    const JV* qt = q->at("quant_type");
+    fmt = (qt && qt->t == 's' && qt->s == "Q4_0") ? ORC_Q4_0 : ORC_Q8_0;
+  }
+  if (fmt == ORC_Q4_0) { g_err = "safetensors Q4_0 has no defined result (Q8 tensors under the Q4_0 kernel)"; return nullptr; }
+  if (fmt == ORC_F16) gs = 32;
+  /* :97-117 */
+  s.ctx_len = max_seq_len < max_ctx_len ? max_seq_len : max_ctx_len;
+  s.group_size = gs;
+  s.rope_freq_scale = 1.0f;
+  s.rope_ext_factor = 0.0f;
+  s.rope_attn_factor = 1.0f;
+  s.rope_original_ctx_len = s.ctx_len;
+  s.attention_scale = 0.0f;
+  s.weight_format = fmt;
+  s.rope_mode = ORC_ROPE_LLAMA3; /* the ST forward calls util::rope */
+  s.llama3_old_ctx = (float)s.ctx_len;
+  s.q4_mode = ORC_Q4_GGML;
+  /* :347-352 tokenizer.json, else tokenizer.bin */
+  if (!tokenizer_ids(dir, true, &s.bos, &s.eos)) return nullptr;
+  /* :122-157 safetensors header */
+  int fd = open(path, O_RDONLY);
+  if (fd < 0) { g_err = std::string("cannot open ") + path; return nullptr; }
+  struct stat st;
+  fstat(fd, &st);
+  size_t size = (size_t)st.st_size;
+  if (size < 8) { close(fd); g_err = "short safetensors file"; return nullptr; }
+  void* mp = mmap(nullptr, size, PROT_READ, MAP_PRIVATE, fd, 0);
+  close(fd);
+  if (mp == MAP_FAILED) { g_err = "mmap failed"; return nullptr; }
+  std::unique_ptr<void, std::function<void(void*)>> guard(mp, [size](void* x) { munmap(x, size); });
+  const uint8_t* data = (const uint8_t*)mp;
+  uint64_t hlen;
+  memcpy(&hlen, data, 8);
+  if (hlen > size - 8) { g_err = "bad safetensors header length"; return nullptr; }
+  JV hdr;
+  if (!json_read((const char*)data + 8, hlen, &hdr) || hdr.t != 'o') { g_err = "bad safetensors header"; return nullptr; }
+  size_t data_start = 8 + hlen;
+  std::map<std::string, StInfo> tensors;
+  for (auto& kv : hdr.o) {
+    if (kv.first == "__metadata__") continue;
+    const JV* dt = kv.second.at("dtype");
+    const JV* offs = kv.second.at("data_offsets");
+    if (!dt || dt->t != 's' || !offs || offs->t != 'a' || offs->a.size() != 2) { g_err = "bad entry " + kv.first; return nullptr; }
+    StInfo ti;
+    ti.dtype = dt->s;
+    ti.off = data_start + (size_t)offs->a[0].u;
+    ti.len = (size_t)(offs->a[1].u - offs->a[0].u);
+    if (ti.off + ti.len > size) { g_err = "tensor out of bounds " + kv.first; return nullptr; }
+    tensors[kv.first] = ti;
+  }
+  auto need = [&](const std::string& nm, size_t bytes, const char* dtype, size_t* off) {
+    auto it = tensors.find(nm);
+    if (it == tensors.end()) { g_err = "Missing tensor: " + nm; return false; }
+    if (dtype && it->second.dtype != dtype) { g_err = "dtype of " + nm; return false; }
+    if (it->second.len < bytes) { g_err = "short tensor " + nm; return false; }
+    *off = it->second.off;
+    return true;
+  };
+  auto f16vec = [&](size_t off, size_t n, std::vector<float>* out) { /* :162-170 load_f16_vec */
+    out->resize(n);
+    for (size_t i = 0; i < n; ++i) {
+      uint16_t h;
+      memcpy(&h, data + off + 2 * i, 2);
+      (*out)[i] = orc_f16_to_f32(h);
+    }
+  };
+  bool quant = fmt != ORC_F16;
+  /* :280-300 load_q: MLX affine (weight, scales, biases) or an F16 tensor */
+  auto load_q = [&](const std::string& stem, size_t rows, size_t cols, QT* out) {
+    size_t w, sc, bi;
+    if (!quant) {
+      if (!need(stem + ".weight", rows * cols * 2, "F16", &w)) return false;
+      f16vec(w, rows * cols, &out->f);
+      return true;
+    }
+    if (!need(stem + ".weight", rows * cols, nullptr, &w) || !need(stem + ".scales", rows * cols / gs * 2, nullptr, &sc) ||
+        !need(stem + ".biases", rows * cols / gs * 2, nullptr, &bi))
+      return false;
+    load_q8_tensor_st(data, rows, cols, gs, w, sc, bi, out);
+    return true;
+  };
+  std::unique_ptr<orc_model> m(new orc_model());
+  m->shape = s;
+  size_t dim = s.dim, qr = (size_t)s.n_heads * s.head_size, kvr = (size_t)s.n_kv_heads * s.head_size;
+  size_t off;
+  /* :172-178 final norm, :181-199 layer norms */
+  if (!need("model.norm.weight", dim * 2, "F16", &off)) return nullptr;
+  f16vec(off, dim, &m->w_rms_final);
+  size_t L = s.n_layers;
+  m->w_rms_att.resize(L); m->w_rms_post_att.resize(L);
+  for (size_t l = 0; l < L; ++l) {
+    std::string p = "model.layers." + std::to_string(l) + ".";
+    if (!need(p + "input_layernorm.weight", dim * 2, "F16", &off)) return nullptr;
+    f16vec(off, dim, &m->w_rms_att[l]);
+    if (!need(p + "post_attention_layernorm.weight", dim * 2, "F16", &off)) return nullptr;
+    f16vec(off, dim, &m->w_rms_post_att[l]);
+  }
+  /* :213-251 token embedding: F16 as is, else requantized and dequantized q * scale */
+  QT emb;
+  if (!load_q("model.embed_tokens", s.vocab_size, dim, &emb)) return nullptr;
+  m->token_embedding = dequant(emb, gs);
+  /* :280-316 */
+  m->wq.resize(L); m->wk.resize(L); m->wv.resize(L); m->wo.resize(L);
+  m->w1.resize(L); m->w2.resize(L); m->w3.resize(L);
+  for (size_t l = 0; l < L; ++l) {
+    std::string p = "model.layers." + std::to_string(l) + ".";
+    if (!load_q(p + "self_attn.q_proj", qr, dim, &m->wq[l]) || !load_q(p + "self_attn.k_proj", kvr, dim, &m->wk[l]) ||
+        !load_q(p + "self_attn.v_proj", kvr, dim, &m->wv[l]) || !load_q(p + "self_attn.o_proj", dim, qr, &m->wo[l]) ||
+        !load_q(p + "mlp.gate_proj", s.hidden_dim, dim, &m->w1[l]) ||
+        !load_q(p + "mlp.down_proj", dim, s.hidden_dim, &m->w2[l]) ||
+        !load_q(p + "mlp.up_proj", s.hidden_dim, dim, &m->w3[l]))
+      return nullptr;
+  }
+  return m.release();
+}
+
+static orc_model* load_lmrs(const char* path, uint32_t max_ctx_len) {
+  std::string dir = parent_dir(path);
+  orc_shape s;
+  memset(&s, 0, sizeof(s));
+  /* transformer_llama_lmrs.rs:62-66: the file must exist; tokenizer.bin first */
+  struct stat st;
+  if (stat(path, &st) != 0) { g_err = std::string("Model file does not exist: ") + path; return nullptr; }
+  if (!tokenizer_ids(dir, false, &s.bos, &s.eos)) return nullptr;
+  int fd = open(path, O_RDONLY);
+  if (fd < 0) { g_err = std::string("cannot open ") + path; return nullptr; }
+  size_t size = (size_t)st.st_size;
+  if (size < 256) { close(fd); g_err = "Model not in lm.rs format."; return nullptr; }
+  void* mp = mmap(nullptr, size, PROT_READ, MAP_PRIVATE, fd, 0);
+  close(fd);
+  if (mp == MAP_FAILED) { g_err = "mmap failed"; return nullptr; }
+  std::unique_ptr<void, std::function<void(void*)>> guard(mp, [size](void* x) { munmap(x, size); });
+  const uint8_t* raw = (const uint8_t*)mp;
+  /* :72-77 magic */
+  if (memcmp(raw, "lmrs", 4) != 0) { g_err = "Model not in lm.rs format."; return nullptr; }
+  /* :31-47, :81-88: packed TransformerArgs at 8..55 */
+  const uint8_t* c = raw + 8;
+  uint32_t seq_len;
+  memcpy(&s.dim, c + 0, 4);
+  memcpy(&s.hidden_dim, c + 4, 4);
+  memcpy(&s.n_layers, c + 8, 4);
+  memcpy(&s.n_heads, c + 12, 4);
+  memcpy(&s.head_size, c + 16, 4);
+  memcpy(&s.n_kv_heads, c + 20, 4);
+  memcpy(&s.vocab_size, c + 24, 4);
+  memcpy(&seq_len, c + 28, 4);
+  memcpy(&s.rms_norm_eps, c + 32, 4);
+  memcpy(&s.rope_theta, c + 36, 4);
+  memcpy(&s.group_size, c + 42, 4);
+  /* :111-120 */
+  if (s.dim == 0 || s.hidden_dim == 0 || s.n_heads == 0 || s.n_layers == 0) {
+    g_err = "Invalid model configuration: critical dimensions cannot be zero";
+    return nullptr;
+  }
+  if (seq_len == 0 || s.vocab_size == 0) {
+    g_err = "Invalid model configuration: sequence length and vocab size must be positive";
+    return nullptr;
+  }
+  if (s.group_size == 0) { g_err = "group_size 0"; return nullptr; }
+  /* :122-148 */
+  s.ctx_len = seq_len < max_ctx_len ? seq_len : max_ctx_len;
+  s.rope_freq_scale = 1.0f;
+  s.rope_ext_factor = 0.0f;
+  s.rope_attn_factor = 1.0f;
+  s.rope_original_ctx_len = s.ctx_len;
+  s.attention_scale = 0.0f;
+  s.weight_format = ORC_Q8_0; /* :101-109 */
+  s.rope_mode = ORC_ROPE_LLAMA3;
+  s.llama3_old_ctx = (float)s.ctx_len;
+  s.q4_mode = ORC_Q4_GGML;
+  size_t gs = s.group_size, dim = s.dim, hd = s.hidden_dim, L = s.n_layers;
+  size_t qsz = (size_t)s.n_heads * s.head_size * dim, kvsz = (size_t)s.n_kv_heads * s.head_size * dim;
+  /* total bytes the tensors need, so that a short file is an error */
+  size_t need = 256 + (size_t)s.vocab_size * dim + (size_t)s.vocab_size * dim / gs * 4 + 2 * L * dim * 4 + dim * 4 +
+                L * (2 * (qsz + qsz / gs * 4) + 2 * (kvsz + kvsz / gs * 4) + 3 * (hd * dim + hd * dim / gs * 4));
+  if (need > size) { g_err = "lm.rs file shorter than its tensors"; return nullptr; }
+  std::unique_ptr<orc_model> m(new orc_model());
+  m->shape = s;
+  size_t off = 256;
+  /* util.rs:547-573 load_q8_tenstor_lmrs: quants then f32 scales */
+  auto q8 = [&](size_t n, QT* out) {
+    out->q.resize(n);
+    memcpy(out->q.data(), raw + off, n);
+    off += n;
+    out->s.resize(n / gs);
+    memcpy(out->s.data(), raw + off, n / gs * 4);
+    off += n / gs * 4;
+  };
+  auto f32v = [&](std::vector<float>* out) {
+    out->resize(dim);
+    memcpy(out->data(), raw + off, dim * 4);
+    off += dim * 4;
+  };
+  QT emb;
+  q8((size_t)s.vocab_size * dim, &emb);
+  /* :176-181 emb_tab[i] = q[i] * scale[i / group_size] */
+  m->token_embedding = dequant(emb, gs);
+  m->w_rms_att.resize(L); m->w_rms_post_att.resize(L);
+  m->wq.resize(L); m->wk.resize(L); m->wv.resize(L); m->wo.resize(L);
+  m->w1.resize(L); m->w2.resize(L); m->w3.resize(L);
+  for (size_t l = 0; l < L; ++l) f32v(&m->w_rms_att[l]);
+  for (size_t l = 0; l < L; ++l) q8(qsz, &m->wq[l]);
+  for (size_t l = 0; l < L; ++l) q8(kvsz, &m->wk[l]);
+  for (size_t l = 0; l < L; ++l) q8(kvsz, &m->wv[l]);
+  for (size_t l = 0; l < L; ++l) q8(qsz, &m->wo[l]);
+  for (size_t l = 0; l < L; ++l) f32v(&m->w_rms_post_att[l]);
+  for (size_t l = 0; l < L; ++l) q8(hd * dim, &m->w1[l]);
+  for (size_t l = 0; l < L; ++l) q8(hd * dim, &m->w2[l]);
+  for (size_t l = 0; l < L; ++l) q8(hd * dim, &m->w3[l]);
+  f32v(&m->w_rms_final);
+  return m.release();
 }

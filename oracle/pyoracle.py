@@ -188,10 +188,12 @@ def f16_to_f32(h: int) -> float:
 
 
 Q4_GGML, Q4_REF = 0, 1
+Q8_0, Q4_0, F16 = 0, 1, 2  # WeightFormat (weight_type.rs:17-22)
+ROPE_GGUF, ROPE_LLAMA3 = 0, 1
 
 
 class Model:
-    """Oracle model loaded from a GGUF file (transformer_llama_gguf.rs)."""
+    """Oracle model loaded from a .gguf, .safetensors or .lmrs file (lib.rs:107-133 dispatch)."""
 
     def __init__(self, path: str, max_ctx_len: int = 0xFFFFFFFF, fmt_override: int = -1, q4_mode: int = Q4_GGML):
         self._h = lib().orc_model_load(str(path).encode(), max_ctx_len, fmt_override, q4_mode)

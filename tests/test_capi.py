@@ -40,9 +40,12 @@ def test_load_errors_without_gpu(yl, tmp_path):
     with pytest.raises(yl.YlError) as e:
         yl.load_transformer(str(tmp_path / "model.bin"))
     assert e.value.code == -1  # unsupported extension (lib.rs:131)
-    with pytest.raises(yl.YlError) as e:
+    with pytest.raises(yl.YlError) as e:  # no config.json beside it
         yl.load_transformer(str(tmp_path / "model.safetensors"))
-    assert e.value.code == -8
+    assert e.value.code == -2 and "config.json" in str(e.value)
+    with pytest.raises(yl.YlError) as e:
+        yl.load_transformer(str(tmp_path / "model.lmrs"))
+    assert e.value.code == -2
     bad = tmp_path / "bad.gguf"
     bad.write_bytes(b"NOTGGUF" + bytes(64))
     with pytest.raises(yl.YlError) as e:

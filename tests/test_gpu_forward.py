@@ -1,14 +1,14 @@
 """GPU parity of the full forward (Transformer::forward_x) against the CPU
 oracle on small seeded synthetic GGUF models (two layers, narrow shapes).
 
-Bar: logits within 1e-2 * max|logit| of the oracle at every step; greedy
-token ids identical over the whole run. These narrow test models can be more
-sensitive to single activation-quantization flips than the bar allows, so two
-documented allowances exist here, and each prints a `RELAXED` line when it is
-used: the logit bar becomes twice the oracle's own one-ulp sensitivity when
-that sensitivity is already within a factor 2 of 1e-2, and an id may differ at
-a step whose oracle top-2 margin is inside the bar. The benchmark
-configurations (tests/test_gpu_configs.py) use no allowance."""
+Bar, with nothing relaxed: logits within 1e-2 * max|logit| of the oracle at
+every step and greedy token ids identical over the whole run. The device
+forward reproduces the oracle's residual stream bit for bit (only the
+lm_head's logits are approximate, ~1e-7 relative), so these narrow models,
+whose logits move by up to 1% under a one-ulp perturbation of the oracle
+itself, pass the bar as written. The allowance helpers below
+(oracle_sensitivity, bound_for, assert_ids_match) serve only the
+tensor-parallel tests, whose all-reduce changes the summation order."""
 from __future__ import annotations
 
 import numpy as np
@@ -69,6 +69,13 @@ def assert_ids_match(gids, oids, olg, bound):
     return flips
 
 
+def assert_exact_path(errs, gids, oids) -> None:
+    """The strict bar: every step's logits within 1e-2 * max|logit|, every
+    greedy id equal."""
+    assert max(errs) < LOGIT_TOL, errs
+    assert gids == oids, [k for k in range(len(oids)) if gids[k] != oids[k]]
+
+
 def oracle_sensitivity(orc, path, prompt, ids, max_ctx) -> float:
     """Largest relative logit move of the oracle itself under a one-ulp
     perturbation (RMSNorm sum of squares in f64), fed the same tokens: how far
@@ -111,10 +118,7 @@ def test_tiny_models_match_oracle(yl, orc, model_factory, preset, over):
     vocab = yl.PRESETS[preset]["vocab_size"]
     prompt = yl.prompt_ids(vocab, 9, 1234).tolist()
     errs, gids, oids, _, _ = run_pair(yl, orc, path, prompt, 24, 256)
-    olg = run_pair.oracle_logits
-    sens = oracle_sensitivity(orc, path, prompt, oids, 256)
-    assert max(errs) < bound_for(sens), (errs, sens)
-    assert_ids_match(gids, oids, olg, bound_for(sens))
+    assert_exact_path(errs, gids, oids)
 
 
 @pytest.mark.parametrize("preset,over", [
@@ -131,10 +135,7 @@ def test_gemm_prefill_matches_oracle(yl, orc, model_factory, preset, over):
     vocab = yl.PRESETS[preset]["vocab_size"]
     prompt = yl.prompt_ids(vocab, 70, 99).tolist()
     errs, gids, oids, _, _ = run_pair(yl, orc, path, prompt, 8, 256)
-    olg = run_pair.oracle_logits
-    sens = oracle_sensitivity(orc, path, prompt, oids, 256)
-    assert max(errs) < bound_for(sens), (errs, sens)
-    assert_ids_match(gids, oids, olg, bound_for(sens))
+    assert_exact_path(errs, gids, oids)
 
 
 def test_decode_graph_matches_host_loop(yl, orc, model_factory):
@@ -163,10 +164,7 @@ def test_long_context_decode_matches_oracle(yl, orc, model_factory, preset):
     vocab = yl.PRESETS[preset]["vocab_size"]
     prompt = yl.prompt_ids(vocab, 1500, 77).tolist()
     errs, gids, oids, _, _ = run_pair(yl, orc, path, prompt, 6, 2048)
-    olg = run_pair.oracle_logits
-    sens = oracle_sensitivity(orc, path, prompt, oids, 2048)
-    assert max(errs) < bound_for(sens), (errs, sens)
-    assert_ids_match(gids, oids, olg, bound_for(sens))
+    assert_exact_path(errs, gids, oids)
     gm = yl.load_transformer(path, max_ctx_len=2048)
     s1 = gm.create_session()
     _, first = gm.forward_x_full(prompt, 0, s1, want_logits=False)
@@ -188,10 +186,7 @@ def test_wide_ffn_dynamic_schedule_matches_oracle(yl, orc, model_factory):
     path = model_factory("tiny", hidden_dim=16384, vocab_size=16384)
     prompt = yl.prompt_ids(16384, 9, 4321).tolist()
     errs, gids, oids, _, _ = run_pair(yl, orc, path, prompt, 12, 256)
-    olg = run_pair.oracle_logits
-    sens = oracle_sensitivity(orc, path, prompt, oids, 256)
-    assert max(errs) < bound_for(sens), (errs, sens)
-    assert_ids_match(gids, oids, olg, bound_for(sens))
+    assert_exact_path(errs, gids, oids)
     gm = yl.load_transformer(path, max_ctx_len=256)
     s1 = gm.create_session()
     _, first = gm.forward_x_full(prompt, 0, s1, want_logits=False)

@@ -27,6 +27,8 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-ccbin", "/usr/bin/g++",
           f"-I{INCLUDE}", "--expt-relaxed-constexpr", "-Xptxas", "-warn-spills"]
+# host code rounds every f32 operation on its own (no contraction into fused multiply-adds)
+HOST_FLAGS = ["-Xcompiler", "-ffp-contract=off"]
 
 
 def sources() -> list[Path]:
@@ -53,7 +55,7 @@ def _compile(src: Path) -> tuple[Path, str]:
     obj = _obj(src)
     cmd = [NVCC, *ARCH, *COMMON, *_extra(), "-c", str(src), "-o", str(obj)]
     if src.suffix == ".cpp":
-        cmd = [NVCC, *COMMON, *_extra(), "-Wno-deprecated-gpu-targets", "-x", "c++", "-c", str(src), "-o", str(obj)]
+        cmd = [NVCC, *COMMON, *HOST_FLAGS, *_extra(), "-Wno-deprecated-gpu-targets", "-x", "c++", "-c", str(src), "-o", str(obj)]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"compile failed: {src}\n{' '.join(cmd)}\n{r.stdout}\n{r.stderr}")

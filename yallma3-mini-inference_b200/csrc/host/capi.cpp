@@ -302,16 +302,15 @@ int yl_load_transformer(const char* path, int sequential, uint32_t max_ctx_len, 
   (void)sequential;
   if (!path || !out) return fail(YL_ERR_ARG, "null argument");
   std::string p(path);
-  const size_t dot = p.rfind('.');
-  const std::string ext = dot == std::string::npos ? "" : p.substr(dot + 1);
-  if (ext != "gguf") {
-    if (ext == "safetensors" || ext == "lmrs")
-      return fail(YL_ERR_UNSUPPORTED, "the device path loads .gguf files; " + ext + " upload is not built yet");
-    return fail(YL_ERR_ARG, "Unsupported model extension for path: " + p);
-  }
+  const size_t dot = p.rfind('.'), slash = p.rfind('/');
+  const std::string ext = dot == std::string::npos || (slash != std::string::npos && dot < slash) ? "" : p.substr(dot + 1);
   if (fmt_override < -1 || fmt_override > YL_F16) return fail(YL_ERR_ARG, "bad format override");
   Model* m = nullptr;
-  int rc = model_load_gguf(path, max_ctx_len, fmt_override, 0, 1, &m);
+  int rc;
+  if (ext == "gguf") rc = model_load_gguf(path, max_ctx_len, fmt_override, 0, 1, &m);
+  else if (ext == "safetensors") rc = model_load_st(path, max_ctx_len, fmt_override, &m);
+  else if (ext == "lmrs") rc = model_load_lmrs(path, max_ctx_len, fmt_override, &m);
+  else return fail(YL_ERR_ARG, "Unsupported model extension for path: " + p);
   if (rc) return rc;
   *out = new yl_model{m};
   return YL_OK;
@@ -390,7 +389,7 @@ int yl_get_embeddings_batch(const yl_model* m, const uint32_t* tokens, uint64_t 
   if (e == cudaSuccess) {
     k::LaunchCfg lc;
     e = k::embed(mm->emb.fmt == YL_Q8_0 ? k::FMT_Q8 : mm->emb.fmt == YL_Q4_0 ? k::FMT_Q4 : k::FMT_F16, mm->emb.q,
-                 mm->emb.s, mm->emb.row_bytes, mm->emb.scale_row_bytes, d, mm->shape.vocab_size, tk, nullptr,
+                 mm->emb.s, mm->emb.row_bytes, mm->emb.scale_row_bytes, mm->emb.sf16, d, mm->shape.vocab_size, tk, nullptr,
                  (uint32_t)n, x, lc);
   }
   if (e == cudaSuccess) e = cudaMemcpy(out, x, n * d * 4ull, cudaMemcpyDeviceToHost);

@@ -2,6 +2,7 @@
 // layout, sessions (base_transformer.rs:78-105) and the device forward
 // (forward.rs:119-297) with a CUDA-graph batch-1 decode step.
 #include "model.h"
+#include "upload.h"
 
 #include <fcntl.h>
 #include <sys/mman.h>
@@ -95,12 +96,6 @@ struct TInfo {
   uint64_t n = 0;
 };
 
-struct Mapped {
-  void* p = MAP_FAILED;
-  size_t size = 0;
-  ~Mapped() { if (p != MAP_FAILED) munmap(p, size); }
-};
-
 bool meta_u(const std::map<std::string, GVal>& m, const char* k, uint64_t* out) {
   auto it = m.find(k);
   if (it == m.end() || !(it->second.type == 4 || it->second.type == 10)) return false;
@@ -121,170 +116,6 @@ uint32_t meta_id(const std::map<std::string, GVal>& m, const char* k, uint32_t d
     case 5: case 11: return (uint32_t)it->second.i;
   }
   return dflt;
-}
-
-int parallel_for(uint64_t n, const std::function<void(uint64_t, uint64_t)>& fn) {
-  unsigned nt = std::max(1u, std::min(32u, std::thread::hardware_concurrency()));
-  if (n < 4096) nt = 1;
-  std::vector<std::thread> th;
-  uint64_t per = (n + nt - 1) / nt;
-  for (unsigned k = 0; k < nt; ++k) {
-    uint64_t a = k * per, b = std::min(n, a + per);
-    if (a >= b) break;
-    th.emplace_back(fn, a, b);
-  }
-  for (auto& t : th) t.join();
-  return 0;
-}
-
-// Repacks `nrows` rows coming from (possibly several) GGUF tensors into one
-// device weight. src_row(r) returns the file address of logical row r.
-struct Uploader {
-  Model* m;
-  uint8_t* stage = nullptr;
-  size_t stage_bytes = 0;
-  ~Uploader() { if (stage) cudaFreeHost(stage); }
-  int alloc(size_t bytes, void** out) {
-    void* p = nullptr;
-    cudaError_t e = cudaMalloc(&p, std::max<size_t>(bytes, 256));
-    if (e != cudaSuccess) return fail(YL_ERR_OOM, std::string("cudaMalloc: ") + cudaGetErrorString(e));
-    m->allocs.push_back(p);
-    m->device_bytes += bytes;
-    *out = p;
-    return YL_OK;
-  }
-  int ensure_stage(size_t bytes) {
-    if (bytes <= stage_bytes) return YL_OK;
-    if (stage) cudaFreeHost(stage);
-    stage = nullptr;
-    YL_CUDA_TRY(cudaMallocHost(&stage, bytes));
-    stage_bytes = bytes;
-    return YL_OK;
-  }
-  // ggml_type: 8 Q8_0, 2 Q4_0, 1 F16
-  int weight(uint32_t ggml_type, uint32_t rows, uint32_t cols, const std::function<const uint8_t*(uint32_t)>& src_row,
-             DevWeight* w) {
-    if (cols % 32) return fail(YL_ERR_FORMAT, "row length must be a multiple of 32");
-    w->rows = rows;
-    w->cols = cols;
-    w->sf16 = true;
-    const uint32_t nb = cols / 32;
-    uint32_t src_row_bytes;
-    if (ggml_type == 8) { w->fmt = YL_Q8_0; w->row_bytes = cols; src_row_bytes = nb * 34; }
-    else if (ggml_type == 2) { w->fmt = YL_Q4_0; w->row_bytes = cols / 2; src_row_bytes = nb * 18; }
-    else if (ggml_type == 1) { w->fmt = YL_F16; w->row_bytes = cols * 2; src_row_bytes = cols * 2; }
-    else return fail(YL_ERR_FORMAT, "unsupported tensor type " + std::to_string(ggml_type));
-    (void)src_row_bytes;
-    w->scale_row_bytes = w->fmt == YL_F16 ? 0 : (uint32_t)round_up(nb * 2, 16);
-    void* q;
-    int rc = alloc((size_t)rows * w->row_bytes, &q);
-    if (rc) return rc;
-    w->q = (uint8_t*)q;
-    if (w->scale_row_bytes) {
-      void* s;
-      rc = alloc((size_t)rows * w->scale_row_bytes, &s);
-      if (rc) return rc;
-      w->s = (uint8_t*)s;
-    }
-    const size_t per_row = (size_t)w->row_bytes + w->scale_row_bytes;
-    const uint32_t chunk_rows = (uint32_t)std::max<size_t>(1, (64u << 20) / per_row);
-    rc = ensure_stage((size_t)chunk_rows * per_row);
-    if (rc) return rc;
-    for (uint32_t r0 = 0; r0 < rows; r0 += chunk_rows) {
-      const uint32_t nr = std::min(chunk_rows, rows - r0);
-      uint8_t* sq = stage;
-      uint8_t* ss = stage + (size_t)nr * w->row_bytes;
-      parallel_for(nr, [&](uint64_t a, uint64_t b) {
-        for (uint64_t r = a; r < b; ++r) {
-          const uint8_t* src = src_row(r0 + (uint32_t)r);
-          uint8_t* dq = sq + r * w->row_bytes;
-          if (w->fmt == YL_F16) {
-            memcpy(dq, src, w->row_bytes);
-            continue;
-          }
-          uint8_t* ds = ss + r * w->scale_row_bytes;
-          memset(ds, 0, w->scale_row_bytes);
-          const uint32_t bsz = w->fmt == YL_Q8_0 ? 34 : 18, qb = w->fmt == YL_Q8_0 ? 32 : 16;
-          for (uint32_t b = 0; b < nb; ++b) {
-            const uint8_t* blk = src + (size_t)b * bsz;
-            ds[2 * b] = blk[0];
-            ds[2 * b + 1] = blk[1];
-            memcpy(dq + (size_t)b * qb, blk + 2, qb);
-          }
-        }
-      });
-      YL_CUDA_TRY(cudaMemcpy(w->q + (size_t)r0 * w->row_bytes, sq, (size_t)nr * w->row_bytes, cudaMemcpyHostToDevice));
-      if (w->scale_row_bytes)
-        YL_CUDA_TRY(cudaMemcpy(w->s + (size_t)r0 * w->scale_row_bytes, ss, (size_t)nr * w->scale_row_bytes,
-                               cudaMemcpyHostToDevice));
-    }
-    return YL_OK;
-  }
-  int f32(const float* src, uint64_t n, float** out) {
-    void* p;
-    int rc = alloc(n * 4, &p);
-    if (rc) return rc;
-    YL_CUDA_TRY(cudaMemcpy(p, src, n * 4, cudaMemcpyHostToDevice));
-    *out = (float*)p;
-    return YL_OK;
-  }
-};
-
-// RoPE (cos, sin) table per (position, pair), by the reference formulas:
-// util.rs:653-718 (rope_gguf, theta iterated by *= theta_scale) or
-// util.rs:589-635 (rope with llama3 frequency scaling).
-void rope_table(const yl_shape& s, float llama3_factor, float llama3_low, float llama3_high, float old_ctx,
-                std::vector<float2>* out) {
-  const uint32_t hs = s.head_size, half = hs / 2;
-  out->assign((size_t)s.ctx_len * half, float2{0.f, 0.f});
-  if (s.rope_mode == YL_ROPE_GGUF) {
-    const float theta_scale = powf(s.rope_theta, -2.0f / (float)hs);
-    const float n_ctx_orig = (float)s.rope_original_ctx_len;
-    const float beta_fast = 32.0f, beta_slow = 1.0f;
-    float corr_start = fmaf(logf(n_ctx_orig / (beta_fast * 2.0f * (float)M_PI)), (float)hs, 0.0f) /
-                       (2.0f * logf(s.rope_theta));
-    corr_start = fmaxf(floorf(corr_start), 0.0f);
-    const float corr_end = fmaf(logf(n_ctx_orig / (beta_slow * 2.0f * (float)M_PI)), (float)hs, 0.0f) /
-                           (2.0f * logf(s.rope_theta));
-    const float corr_dims_1 = fminf(corr_start, corr_end) + fminf(corr_end, (float)half) - fmaxf(corr_start, 0.0f);
-    parallel_for(s.ctx_len, [&](uint64_t a, uint64_t b) {
-      for (uint64_t pos = a; pos < b; ++pos) {
-        float theta = (float)pos;
-        for (uint32_t kp = 0; kp < half; ++kp) {
-          const float theta_interp = s.rope_freq_scale * theta / 1.0f;
-          float t = theta_interp;
-          if (s.rope_ext_factor != 0.0f) {
-            const float y = ((float)(kp * 2) * 0.5f - corr_start) / fmaxf(corr_dims_1 - corr_start, 0.001f);
-            const float ramp = (1.0f - fminf(1.0f, fmaxf(y, 0.0f))) * s.rope_ext_factor;
-            t = theta_interp * (1.0f - ramp) + theta / 1.0f * ramp;
-          }
-          (*out)[pos * half + kp] = float2{cosf(t) * s.rope_attn_factor, sinf(t) * s.rope_attn_factor};
-          theta = theta * theta_scale;
-        }
-      }
-    });
-  } else {
-    const float low_wl = old_ctx / llama3_low, high_wl = old_ctx / llama3_high;
-    std::vector<float> freq(half);
-    for (uint32_t j = 0; j < half; ++j) {
-      float f = powf(s.rope_theta, -((float)(j * 2)) / (float)hs);
-      const float wl = (2.0f * (float)M_PI) / f;
-      if (wl > low_wl) {
-        f = f / llama3_factor;
-      } else if (wl <= low_wl && wl >= high_wl) {
-        const float sm = (old_ctx / wl - llama3_low) / (llama3_high - llama3_low);
-        f = (1.0f - sm) * f / llama3_factor + sm * f;
-      }
-      freq[j] = f;
-    }
-    parallel_for(s.ctx_len, [&](uint64_t a, uint64_t b) {
-      for (uint64_t pos = a; pos < b; ++pos)
-        for (uint32_t j = 0; j < half; ++j) {
-          const float v = (float)pos * freq[j];
-          (*out)[pos * half + j] = float2{cosf(v), sinf(v)};
-        }
-    });
-  }
 }
 
 }  // namespace
@@ -312,17 +143,10 @@ const Tunables& tunables() {
 
 int model_load_gguf(const char* path, uint32_t max_ctx_len, int fmt_override, int tp_rank, int tp_size, Model** out) {
   if (tp_size < 1 || tp_size > 8 || tp_rank < 0 || tp_rank >= tp_size) return fail(YL_ERR_ARG, "bad tensor-parallel rank/size");
-  int fd = open(path, O_RDONLY);
-  if (fd < 0) return fail(YL_ERR_IO, std::string("cannot open ") + path);
-  struct stat stt;
-  if (fstat(fd, &stt) != 0) { close(fd); return fail(YL_ERR_IO, "fstat failed"); }
   Mapped mp;
-  mp.size = (size_t)stt.st_size;
-  mp.p = mmap(nullptr, mp.size, PROT_READ, MAP_PRIVATE, fd, 0);
-  close(fd);
-  if (mp.p == MAP_FAILED) return fail(YL_ERR_IO, "mmap failed");
-  madvise(mp.p, mp.size, MADV_SEQUENTIAL);
-  const uint8_t* base = (const uint8_t*)mp.p;
+  int rc = map_file(path, &mp);
+  if (rc) return rc;
+  const uint8_t* base = mp.data();
   Cursor c{base, mp.size, 0};
   if (c.rd(4) != 0x46554747u) return fail(YL_ERR_FORMAT, "Not a GGUF file (bad magic)");
   const uint64_t version = c.rd(4);
@@ -389,24 +213,8 @@ int model_load_gguf(const char* path, uint32_t max_ctx_len, int fmt_override, in
   s.tp_size = tp_size;
   m->bos = meta_id(meta, "tokenizer.ggml.bos_token_id", 128000u);
   m->eos = meta_id(meta, "tokenizer.ggml.eos_token_id", 128009u);
-  if (s.dim % 32 || s.hidden_dim % 32 || s.head_size % 32 || s.n_kv_heads == 0 || s.n_heads % s.n_kv_heads)
-    return fail(YL_ERR_UNSUPPORTED, "device path needs dim, ffn and head_size multiples of 32 and GQA grouping");
-  if (s.head_size != 64 && s.head_size != 128) return fail(YL_ERR_UNSUPPORTED, "head_size must be 64 or 128");
-  if (s.n_heads / s.n_kv_heads > 8) return fail(YL_ERR_UNSUPPORTED, "more than 8 query heads per KV head");
-  if (s.ctx_len == 0) return fail(YL_ERR_ARG, "ctx_len is 0");
-  // Megatron split: heads (q and KV) and ffn rows by rank, wo/down along K,
-  // lm_head by vocabulary rows; activation and weight blocks of 32 never
-  // straddle ranks (the ffn slice is a multiple of 64 for the SwiGLU pairs)
-  const uint32_t N = (uint32_t)tp_size;
-  if (s.n_kv_heads % N || s.hidden_dim % (64 * N) || s.vocab_size % N)
-    return fail(YL_ERR_UNSUPPORTED, "tensor parallelism needs KV heads, ffn/64 and vocabulary divisible by the ranks");
-  m->tp_rank = tp_rank;
-  m->tp_size = tp_size;
-  m->l_heads = s.n_heads / N;
-  m->l_kv = s.n_kv_heads / N;
-  m->l_ffn = s.hidden_dim / N;
-  m->l_vocab = s.vocab_size / N;
-  m->vocab0 = m->l_vocab * (uint32_t)tp_rank;
+  if ((rc = check_device_shape(s, tp_size))) return rc;
+  set_rank_split(m.get(), tp_rank, tp_size);
 
   std::map<std::string, TInfo> tmap;
   for (uint64_t i = 0; i < n_tensors && c.ok; ++i) {
@@ -454,7 +262,6 @@ int model_load_gguf(const char* path, uint32_t max_ctx_len, int fmt_override, in
   YL_CUDA_TRY(cudaDeviceGetAttribute(&m->num_sms, cudaDevAttrMultiProcessorCount, m->device));
   Uploader up{m.get()};
   const uint32_t d = s.dim, att = s.n_heads * s.head_size, kvd = s.n_kv_heads * s.head_size, f = s.hidden_dim;
-  int rc;
   auto row_ptr = [&](const TInfo* ti, uint32_t cols, uint32_t r) {
     return base + ti->off + bytes_of(ti->type, (uint64_t)r * cols);
   };
@@ -466,7 +273,7 @@ int model_load_gguf(const char* path, uint32_t max_ctx_len, int fmt_override, in
   const TInfo* te;
   if ((rc = get("token_embd.weight", &te))) return rc;
   if (te->n != (uint64_t)s.vocab_size * d) return fail(YL_ERR_FORMAT, "token_embd.weight shape mismatch");
-  if ((rc = up.weight(te->type, s.vocab_size, d, [&](uint32_t r) { return row_ptr(te, d, r); }, &m->emb))) return rc;
+  if ((rc = up.gguf(te->type, s.vocab_size, d, [&](uint32_t r) { return row_ptr(te, d, r); }, &m->emb))) return rc;
   m->lm = m->emb;  // this rank's vocabulary rows of the tied table
   m->lm.rows = m->l_vocab;
   m->lm.q = m->emb.q + (uint64_t)m->vocab0 * m->emb.row_bytes;
@@ -475,7 +282,7 @@ int model_load_gguf(const char* path, uint32_t max_ctx_len, int fmt_override, in
   if (out_it != tmap.end()) {  // untied lm_head (resolved deviation D2)
     const TInfo* to = &out_it->second;
     if (to->n != (uint64_t)s.vocab_size * d) return fail(YL_ERR_FORMAT, "output.weight shape mismatch");
-    if ((rc = up.weight(to->type, m->l_vocab, d, [&](uint32_t r) { return row_ptr(to, d, m->vocab0 + r); }, &m->lm)))
+    if ((rc = up.gguf(to->type, m->l_vocab, d, [&](uint32_t r) { return row_ptr(to, d, m->vocab0 + r); }, &m->lm)))
       return rc;
     s.untied_lm_head = 1;
   }
@@ -505,29 +312,23 @@ int model_load_gguf(const char* path, uint32_t max_ctx_len, int fmt_override, in
     // this rank's rows / columns (the whole matrices at one rank)
     const uint32_t hs = s.head_size, la = m->l_heads * hs, lk = m->l_kv * hs, lf = m->l_ffn;
     const uint32_t qa0 = (uint32_t)tp_rank * la, kv0 = (uint32_t)tp_rank * lk, f0 = (uint32_t)tp_rank * lf;
-    rc = up.weight(want_type, la + 2 * lk, d, [&](uint32_t r) {
+    rc = up.gguf(want_type, la + 2 * lk, d, [&](uint32_t r) {
       if (r < la) return row_ptr(tq, d, qa0 + r);
       if (r < la + lk) return row_ptr(tk, d, kv0 + r - la);
       return row_ptr(tv, d, kv0 + r - la - lk);
     }, &L.wqkv);
     if (rc) return rc;
-    if ((rc = up.weight(want_type, d, la, [&](uint32_t r) { return row_ptr(to, att, r) + bytes_of(want_type, qa0); },
+    if ((rc = up.gguf(want_type, d, la, [&](uint32_t r) { return row_ptr(to, att, r) + bytes_of(want_type, qa0); },
                         &L.wo)))
       return rc;
-    rc = up.weight(want_type, 2 * lf, d,
+    rc = up.gguf(want_type, 2 * lf, d,
                    [&](uint32_t r) { return (r & 1) ? row_ptr(tu, d, f0 + r / 2) : row_ptr(tg, d, f0 + r / 2); }, &L.w13);
     if (rc) return rc;
-    if ((rc = up.weight(want_type, d, lf, [&](uint32_t r) { return row_ptr(tdn, f, r) + bytes_of(want_type, f0); },
+    if ((rc = up.gguf(want_type, d, lf, [&](uint32_t r) { return row_ptr(tdn, f, r) + bytes_of(want_type, f0); },
                         &L.w2)))
       return rc;
   }
-  std::vector<float2> cs;
-  rope_table(s, l3_factor, l3_low, l3_high, (float)s.rope_original_ctx_len, &cs);
-  void* csd;
-  if ((rc = up.alloc(cs.size() * sizeof(float2), &csd))) return rc;
-  YL_CUDA_TRY(cudaMemcpy(csd, cs.data(), cs.size() * sizeof(float2), cudaMemcpyHostToDevice));
-  m->rope_cs = (float2*)csd;
-  m->attn_scale = s.attention_scale != 0.0f ? s.attention_scale : 1.0f / sqrtf((float)s.head_size);
+  if ((rc = finish_model(m.get(), up, l3_factor, l3_low, l3_high, (float)s.rope_original_ctx_len))) return rc;
   *out = m.release();
   return YL_OK;
 }
@@ -898,7 +699,7 @@ int enqueue_forward(Session* s, uint32_t n, uint32_t start_pos, bool from_state,
 
   YL_MARK();
   YL_LAUNCH(k::embed(m->emb.fmt == YL_Q8_0 ? k::FMT_Q8 : m->emb.fmt == YL_Q4_0 ? k::FMT_Q4 : k::FMT_F16, m->emb.q,
-                     m->emb.s, m->emb.row_bytes, m->emb.scale_row_bytes, d, sh.vocab_size, s->tok, st, n, s->x, lc));
+                     m->emb.s, m->emb.row_bytes, m->emb.scale_row_bytes, m->emb.sf16, d, sh.vocab_size, s->tok, st, n, s->x, lc));
   const bool decode = n == 1;
   // Decode streams every weight once per token. Each weight-streaming launch
   // (and the attention kernel, during which HBM would idle) prefetches into

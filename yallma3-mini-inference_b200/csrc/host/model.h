@@ -114,6 +114,10 @@ struct Session {
 };
 
 int model_load_gguf(const char* path, uint32_t max_ctx_len, int fmt_override, int tp_rank, int tp_size, Model** out);
+// safetensors + config.json beside it (MLX affine 8-bit requantized to Q8
+// with f32 scales, or F16), and lm.rs files (Q8 with f32 scales); one rank.
+int model_load_st(const char* path, uint32_t max_ctx_len, int fmt_override, Model** out);
+int model_load_lmrs(const char* path, uint32_t max_ctx_len, int fmt_override, Model** out);
 // Tensor-parallel sessions: export this rank's exchange-region handle (64
 // bytes, cudaIpcMemHandle_t), then map all ranks' regions (handles[rank]).
 int session_tp_handle(Session* s, void* handle_out);

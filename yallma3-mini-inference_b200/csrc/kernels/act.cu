@@ -81,12 +81,15 @@ cudaError_t rmsnorm_quant(const float* x, const float* w, uint32_t ntok, uint32_
                        dim, eps, q, s, y);
 }
 
-// Embedding gather: x[t][k] = value of row tokens[t] (exact: int8 * f16 scale
-// fits in f32), zeros for ids >= vocab (base_transformer.rs:148-158).
+// Embedding gather: x[t][k] = value of row tokens[t], q * scale rounded once
+// as the reference's dequantized table holds it (an int8 times an f16 scale
+// is exact in f32; f32 scales come from lm.rs files and requantized
+// safetensors), zeros for ids >= vocab (base_transformer.rs:148-158).
 __global__ void __launch_bounds__(256) embed_kernel(int fmt, const uint8_t* __restrict__ wq,
                                                     const uint8_t* __restrict__ ws, uint32_t row_bytes,
-                                                    uint32_t scale_row_bytes, uint32_t dim, uint32_t vocab,
-                                                    const uint32_t* __restrict__ tokens, const StepState* state,
+                                                    uint32_t scale_row_bytes, bool sf16, uint32_t dim,
+                                                    uint32_t vocab, const uint32_t* __restrict__ tokens,
+                                                    const StepState* state,
                                                     float* __restrict__ x) {
   grid_dep_launch();
   grid_dep_wait();
@@ -100,7 +103,9 @@ __global__ void __launch_bounds__(256) embed_kernel(int fmt, const uint8_t* __re
     if (fmt == FMT_F16) {
       v = __half2float(reinterpret_cast<const __half*>(row)[k]);
     } else {
-      const float sc = __half2float(reinterpret_cast<const __half*>(ws + (uint64_t)id * scale_row_bytes)[k / 32]);
+      const uint8_t* srow = ws + (uint64_t)id * scale_row_bytes;
+      const float sc = sf16 ? __half2float(reinterpret_cast<const __half*>(srow)[k / 32])
+                            : reinterpret_cast<const float*>(srow)[k / 32];
       int qv;
       if (fmt == FMT_Q8) {
         qv = (int8_t)row[k];
@@ -116,11 +121,11 @@ __global__ void __launch_bounds__(256) embed_kernel(int fmt, const uint8_t* __re
 }
 
 cudaError_t embed(int fmt, const uint8_t* wq, const uint8_t* ws, uint32_t row_bytes, uint32_t scale_row_bytes,
-                  uint32_t dim, uint32_t vocab, const uint32_t* tokens, const StepState* state, uint32_t ntok,
+                  bool sf16, uint32_t dim, uint32_t vocab, const uint32_t* tokens, const StepState* state, uint32_t ntok,
                   float* x, const LaunchCfg& lc) {
   if (ntok == 0) return cudaSuccess;
   return launch_kernel(embed_kernel, dim3((dim + 255) / 256, ntok), dim3(256), 0, lc, fmt, wq, ws, row_bytes,
-                       scale_row_bytes, dim, vocab, tokens, state, x);
+                       scale_row_bytes, sf16, dim, vocab, tokens, state, x);
 }
 
 // sampler.rs:67-79: index of the first strictly-greatest value. NaNs never

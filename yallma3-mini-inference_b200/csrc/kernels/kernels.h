@@ -207,7 +207,7 @@ struct StepState {
   int32_t steps;  // number of device steps executed
 };
 cudaError_t embed(int fmt, const uint8_t* wq, const uint8_t* ws, uint32_t row_bytes, uint32_t scale_row_bytes,
-                  uint32_t dim, uint32_t vocab, const uint32_t* tokens, const StepState* state, uint32_t ntok,
+                  bool sf16, uint32_t dim, uint32_t vocab, const uint32_t* tokens, const StepState* state, uint32_t ntok,
                   float* x, const LaunchCfg& lc);
 
 // RoPE + KV-cache write. qkv: [ntok][att_dim + 2 kv_dim] (q | k | v) from the
