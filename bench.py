@@ -367,7 +367,8 @@ def profile_case(case: str) -> None:
     the Q8_0 matmul of B tokens (the tensor-core GEMM from 16 tokens), timed
     over 10 launches with CUDA events after 3 untimed ones. `prefill4`: the
     4-layer model below, one 512-token prefill. `sweep`: the matvec / GEMM
-    sweep (sweep_case). `decode4`: a
+    sweep (sweep_case). `int8peak`: torch._int_mm on 8192^3 (the library
+    int8 GEMM, the denominator of the GEMM's tensor fraction). `decode4`: a
     4-layer config-4-shaped model, prompt 8, then 4 decode steps launched
     kernel by kernel (no graph)."""
     import torch
@@ -410,6 +411,22 @@ def profile_case(case: str) -> None:
     elif case == "sweep":
         sweep_case(yl, torch, rng)
         return
+    elif case == "int8peak":
+        # dense int8 tensor-core peak of the library GEMM (torch._int_mm, cuBLASLt), 8192^3
+        a8 = torch.randint(-127, 128, (8192, 8192), dtype=torch.int8, device="cuda")
+        b8 = torch.randint(-127, 128, (8192, 8192), dtype=torch.int8, device="cuda")
+        for _ in range(3):
+            torch._int_mm(a8, b8)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        torch.cuda.synchronize()
+        ev[0].record()
+        for _ in range(20):
+            torch._int_mm(a8, b8)
+        ev[1].record()
+        torch.cuda.synchronize()
+        us = ev[0].elapsed_time(ev[1]) * 50.0
+        print(json.dumps({"case": case, "us_per_launch": us, "tops": 2.0 * 8192 ** 3 / us * 1e-6}))
+        return
     elif case == "prefill4":
         path = os.path.join(os.environ.get("YL_BENCH_DIR", "/tmp"), "yl_c4_4layers.gguf")
         if not os.path.exists(path):
@@ -442,7 +459,7 @@ def main() -> None:
     ap.add_argument("--e2e-steps", type=int, default=128)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-tokens", type=int, default=3)
-    ap.add_argument("--case", default=None, help="profiling workload (matvec:ROWSxK, gemm:ROWSxKxTOKENS, sweep, prefill4 or decode4), no bench line")
+    ap.add_argument("--case", default=None, help="profiling workload (matvec:ROWSxK, gemm:ROWSxKxTOKENS, sweep, int8peak, prefill4 or decode4), no bench line")
     args = ap.parse_args()
     if args.case:
         profile_case(args.case)

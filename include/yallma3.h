@@ -88,7 +88,7 @@ typedef struct yl_qtensor {
   void* quant;
   void* scale;
   int32_t owned;       /* 1 if freed by yl_qtensor_free */
-  int32_t _pad;
+  int32_t flags;       /* bit 0: an f16 scale is +-inf (set by yl_qtensor_upload) */
 } yl_qtensor;
 
 /* new_workspace_buffer (weight_type.rs:108-120): zeroed activation tensor. */
@@ -181,6 +181,15 @@ typedef struct yl_shape {
   int32_t tp_rank, tp_size;
   int32_t _pad;
 } yl_shape;
+
+/* Process-wide options of the device path (no reference counterpart), read
+ * by launches made after the call:
+ *  "gemm"        1 = batches of 16+ tokens on the int8 tensor-core GEMM (default)
+ *  "gemm_tc"     1 = Q8_0 batches on the tcgen05 / tensor-memory kernel
+ *                (bit-identical, not faster; default 0, env YL_GEMM_TC)
+ *  "gemm_tc_min" token count from which gemm_tc applies (default 96)
+ * YL_ERR_ARG for an unknown key. */
+int yl_config_set(const char* key, int64_t value);
 
 /* lib.rs:107-133 `load_transformer(path, sequential, max_ctx_len, fmt_override)`.
  * Dispatch by extension:

@@ -138,6 +138,26 @@ def test_gemm_prefill_matches_oracle(yl, orc, model_factory, preset, over):
     assert_exact_path(errs, gids, oids)
 
 
+@pytest.mark.parametrize("preset,over", [
+    ("tiny", {}),
+    ("tiny128", {"llama3_scaling": True, "rope_theta": 5e5, "context_length": 131072}),
+])
+def test_tcgen05_prefill_matches_oracle(yl, orc, model_factory, preset, over):
+    """A 200-token Q8_0 prompt: every projection of the prefill runs on the
+    tcgen05 kernel (two 128-token tiles, the second partial): the q/k/v store,
+    the wo and down residual adds and the gate/up SwiGLU + h-quantize
+    epilogue; then greedy decode."""
+    path = model_factory(preset, **over)
+    vocab = yl.PRESETS[preset]["vocab_size"]
+    prompt = yl.prompt_ids(vocab, 200, 7).tolist()
+    yl.config_set("gemm_tc", 1)
+    try:
+        errs, gids, oids, _, _ = run_pair(yl, orc, path, prompt, 8, 256)
+    finally:
+        yl.config_set("gemm_tc", 0)
+    assert_exact_path(errs, gids, oids)
+
+
 def test_decode_graph_matches_host_loop(yl, orc, model_factory):
     path = model_factory("tiny128")
     gm = yl.load_transformer(path, max_ctx_len=512)

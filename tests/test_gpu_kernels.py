@@ -212,19 +212,36 @@ def test_f32_weight_scales(yl, orc, torch_cuda):
 
 
 GEMM_CASES = [(260, 576, 17), (1000, 2048, 32), (384, 2080, 20), (260, 576, 33), (1000, 2048, 64), (128, 32, 65),
-              (384, 2080, 130), (2048, 2048, 256)]
+              (384, 2080, 130), (2048, 2048, 256),
+              # from 96 tokens Q8_0 runs on the tcgen05 kernel (128 x 128 tiles, 4 blocks per stage):
+              # row / token tails, a single block, a partial last stage (65 blocks), several token tiles
+              (300, 1056, 129), (128, 32, 100), (1000, 2080, 96), (512, 4096, 384), (4096, 4096, 512)]
+
+
+@pytest.fixture
+def gemm_path(yl, request):
+    """Selects the Q8_0 GEMM kernel for the test: mma.sync (tc = 0) or the
+    tcgen05 / tensor-memory kernel (tc = 1, from 96 tokens)."""
+    tc = request.param
+    yl.config_set("gemm_tc", tc)
+    yield tc
+    yl.config_set("gemm_tc", 0)
 
 
 @pytest.mark.parametrize("o,n,batch", GEMM_CASES)
 @pytest.mark.parametrize("fmt", ["Q8_0", "Q4_0"])
 @pytest.mark.parametrize("scale_type", [1, 0])
-def test_gemm_bit_exact_vs_oracle(yl, orc, torch_cuda, o, n, batch, fmt, scale_type):
+@pytest.mark.parametrize("gemm_path", [0, 1], indirect=True)
+def test_gemm_bit_exact_vs_oracle(yl, orc, torch_cuda, o, n, batch, fmt, scale_type, gemm_path):
     """Batches of 16 or more tokens run on the int8 tensor-core GEMM. It folds
     each 32-block's exact int32 dot as ((f32)isum * ws) * xs in group order,
     the oracle's sequence (weight_type.rs:190-201, :207-224), so into a zeroed output the
     results are bit-identical. Cases cover both token tiles (32 and 64), row
     and token tails, a single block, an odd block count (f16 scale pairs) and
-    several K stages."""
+    several K stages. With gemm_path 1, Q8_0 batches of 96+ tokens run on the
+    tcgen05 kernel instead (the other cases are skipped there)."""
+    if gemm_path and (fmt != "Q8_0" or batch < 96):
+        pytest.skip("the tcgen05 kernel takes Q8_0 batches of 96 or more tokens")
     rng = np.random.default_rng(o + n + batch)
     f = getattr(yl.WeightFormat, fmt)
     lo, hi = (-127, 128) if fmt == "Q8_0" else (-8, 8)
@@ -242,11 +259,16 @@ def test_gemm_bit_exact_vs_oracle(yl, orc, torch_cuda, o, n, batch, fmt, scale_t
 
 
 @pytest.mark.parametrize("fmt", ["Q8_0", "Q4_0"])
-def test_gemm_accumulate_quirk(yl, orc, torch_cuda, fmt):
+@pytest.mark.parametrize("batch", [40, 140])
+@pytest.mark.parametrize("gemm_path", [0, 1], indirect=True)
+def test_gemm_accumulate_quirk(yl, orc, torch_cuda, fmt, batch, gemm_path):
     """The `+=` quirk through the GEMM: quad columns add into the initial
-    output, remainder columns overwrite it (weight_type.rs:190-201 vs :223)."""
+    output, remainder columns overwrite it (weight_type.rs:190-201 vs :223).
+    With gemm_path 1, 140 tokens of Q8_0 take the tcgen05 kernel."""
+    if gemm_path and (fmt != "Q8_0" or batch < 96):
+        pytest.skip("the tcgen05 kernel takes Q8_0 batches of 96 or more tokens")
     rng = np.random.default_rng(11)
-    o, n, batch = 262, 1024, 40
+    o, n = 262, 1024
     f = getattr(yl.WeightFormat, fmt)
     lo, hi = (-127, 128) if fmt == "Q8_0" else (-8, 8)
     wq = rng.integers(lo, hi, o * n, dtype=np.int8)

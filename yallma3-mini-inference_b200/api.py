@@ -42,7 +42,7 @@ _lib = C.CDLL(str(LIB_PATH))
 class QTensorC(C.Structure):
     _fields_ = [("fmt", C.c_int32), ("scale_type", C.c_int32), ("len", C.c_uint64), ("gs", C.c_uint64),
                 ("rows", C.c_uint64), ("cols", C.c_uint64), ("scale_stride", C.c_uint64),
-                ("quant", C.c_void_p), ("scale", C.c_void_p), ("owned", C.c_int32), ("_pad", C.c_int32)]
+                ("quant", C.c_void_p), ("scale", C.c_void_p), ("owned", C.c_int32), ("flags", C.c_int32)]
 
 
 class ShapeC(C.Structure):
@@ -112,6 +112,7 @@ _sigs = {
     "yl_forward_x": (C.c_int, [_P, _P, _P, C.c_uint64, C.c_uint32, _P, _P]),
     "yl_decode_greedy": (C.c_int, [_P, _P, C.c_uint32, C.c_uint32, C.c_uint32, _P, _P, C.c_int]),
     "yl_decode_step_launches": (C.c_int, [_P, C.POINTER(C.c_uint32)]),
+    "yl_config_set": (C.c_int, [C.c_char_p, C.c_int64]),
     "yl_session_decode_graph_launches": (C.c_int, [_P, C.c_int, C.POINTER(C.c_uint32)]),
     "yl_model_attention_decode": (C.c_int, [_P, _P, _P, _P, C.c_uint32, _P, _P, _P, _P]),
     "yl_profile_decode_step": (C.c_int, [_P, _P, C.c_uint32, C.c_uint32, _P, C.c_uint32, C.POINTER(C.c_uint32)]),
@@ -145,6 +146,11 @@ def _check(rc: int) -> None:
 
 def last_error() -> str:
     return _lib.yl_last_error().decode(errors="replace")
+
+
+def config_set(key: str, value: int) -> None:
+    """Process-wide device-path option (yl_config_set): gemm, gemm_tc, gemm_tc_min."""
+    _check(_lib.yl_config_set(key.encode(), int(value)))
 
 
 def version() -> str:

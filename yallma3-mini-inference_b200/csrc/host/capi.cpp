@@ -134,11 +134,17 @@ int yl_qtensor_upload(yl_qtensor* t, const int8_t* q, const float* scales, const
   YL_CUDA_TRY(cudaMemcpy(t->quant, hq.data(), hq.size(), cudaMemcpyHostToDevice));
   const uint64_t ssz = t->scale_type == YL_SCALE_F16 ? 2 : 4;
   std::vector<uint8_t> hs(rows * t->scale_stride * ssz, 0);
+  t->flags &= ~1;
   for (uint64_t r = 0; r < rows; ++r)
     for (uint64_t b = 0; b < nb; ++b) {
       const float sv = scales[r * nb + b];
-      if (ssz == 2) ((uint16_t*)hs.data())[r * t->scale_stride + b] = f32_to_f16(sv);
-      else ((float*)hs.data())[r * t->scale_stride + b] = sv;
+      if (ssz == 2) {
+        const uint16_t h = f32_to_f16(sv);
+        ((uint16_t*)hs.data())[r * t->scale_stride + b] = h;
+        if ((h & 0x7FFFu) == 0x7C00u) t->flags |= 1;
+      } else {
+        ((float*)hs.data())[r * t->scale_stride + b] = sv;
+      }
     }
   YL_CUDA_TRY(cudaMemcpy(t->scale, hs.data(), hs.size(), cudaMemcpyHostToDevice));
   return YL_OK;
@@ -231,6 +237,7 @@ int yl_matmul(float* out, const yl_qtensor* x, const yl_qtensor* w, uint64_t n, 
   dw.scale_row_bytes = w->fmt == YL_F16 ? 0 : (uint32_t)(w->scale_stride * (dw.sf16 ? 2 : 4));
   dw.q = (uint8_t*)w->quant;
   dw.s = (uint8_t*)w->scale;
+  dw.no_inf_scales = (w->flags & 1) == 0;
   const bool f32act = w->fmt == YL_F16;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
@@ -297,6 +304,11 @@ int yl_fused_attention(float* output, const float* sq, const float* key_cache, c
 }
 
 // ------------------------------- model -----------------------------------
+
+int yl_config_set(const char* key, int64_t value) {
+  if (!key) return fail(YL_ERR_ARG, "null key");
+  return set_tunable(key, value);
+}
 
 int yl_load_transformer(const char* path, int sequential, uint32_t max_ctx_len, int fmt_override, yl_model** out) {
   (void)sequential;

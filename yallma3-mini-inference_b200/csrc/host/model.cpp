@@ -124,7 +124,8 @@ Model::~Model() {
   for (void* p : allocs) cudaFree(p);
 }
 
-const Tunables& tunables() {
+namespace {
+Tunables& tunables_mut() {
   static Tunables t = [] {
     Tunables x;
     if (const char* e = getenv("YL_MV_KC_BYTES")) x.kc_bytes = (uint32_t)atoi(e);
@@ -135,10 +136,24 @@ const Tunables& tunables() {
     if (const char* e = getenv("YL_TP_FUSED")) x.tp_fused = atoi(e) != 0;
     if (const char* e = getenv("YL_GEMM")) x.gemm = atoi(e) != 0;
     if (const char* e = getenv("YL_GEMM_MIN")) x.gemm_min = (uint32_t)std::max(2, atoi(e));
+    if (const char* e = getenv("YL_GEMM_TC")) x.gemm_tc = atoi(e) != 0;
+    if (const char* e = getenv("YL_GEMM_TC_MIN")) x.gemm_tc_min = (uint32_t)std::max(1, atoi(e));
     if (const char* e = getenv("YL_PF_MB")) x.pf_bytes = (uint64_t)std::max(0, atoi(e)) << 20;
     return x;
   }();
   return t;
+}
+}  // namespace
+
+const Tunables& tunables() { return tunables_mut(); }
+
+int set_tunable(const std::string& key, int64_t value) {
+  Tunables& t = tunables_mut();
+  if (key == "gemm_tc") t.gemm_tc = value != 0;
+  else if (key == "gemm_tc_min") t.gemm_tc_min = (uint32_t)std::max<int64_t>(1, value);
+  else if (key == "gemm") t.gemm = value != 0;
+  else return fail(YL_ERR_ARG, "unknown option " + key);
+  return YL_OK;
 }
 
 int model_load_gguf(const char* path, uint32_t max_ctx_len, int fmt_override, int tp_rank, int tp_size, Model** out) {
@@ -569,13 +584,15 @@ int run_matvec_ex(const DevWeight& w, bool f32act, const int8_t* xq, const float
     g.quirk_cols = quirk_cols;
     g.hq = ex.hq;
     g.hs = ex.hs;
+    g.err = err;
     if (k::gemm_supported(g, fmt, w.sf16, epi)) {
       if (ex.pro == k::PRO_NORM) {
         cudaError_t e = k::rmsnorm_quant(ex.xres, ex.norm_w, ntok, w.cols, ex.eps, ex.gq, ex.gs, nullptr, lc);
         if (e != cudaSuccess) return fail(YL_ERR_CUDA, std::string("rmsnorm_quant launch: ") + cudaGetErrorString(e));
         if (launches) ++*launches;
       }
-      cudaError_t e = k::gemm_q(g, fmt, w.sf16, epi, lc);
+      const bool tc = tu.gemm_tc && ntok >= tu.gemm_tc_min && w.no_inf_scales && k::gemm_tc_supported(g, fmt, w.sf16, epi);
+      cudaError_t e = tc ? k::gemm_tc(g, w.sf16, epi, lc) : k::gemm_q(g, fmt, w.sf16, epi, lc);
       if (e != cudaSuccess) return fail(YL_ERR_CUDA, std::string("gemm launch: ") + cudaGetErrorString(e));
       if (launches) ++*launches;
       return YL_OK;

@@ -20,6 +20,7 @@ struct DevWeight {
   uint32_t row_bytes = 0, scale_row_bytes = 0;
   uint8_t* q = nullptr;
   uint8_t* s = nullptr;
+  bool no_inf_scales = true;  // no f16 scale is +-inf (the tcgen05 GEMM's fused fold needs that)
 };
 
 struct Layer {
@@ -150,12 +151,20 @@ struct Tunables {
   bool limbs = true;         // Q8_0 lm_head on three-limb int8 activations
   bool gemm = true;          // multi-token passes on the int8 tensor-core GEMM
   uint32_t gemm_min = 16;    // from this many tokens (below, the matvec re-reading weights per 8 is faster)
+  // Q8_0 GEMMs on the tcgen05 tensor-memory kernel (YL_GEMM_TC=1), from
+  // gemm_tc_min tokens (its tiles are 128 tokens wide). Off by default: it is
+  // bit-identical to the mma.sync kernel but measured no faster (both are
+  // bound by the exact per-block fold on the FP32 pipe, not by the tensor core).
+  bool gemm_tc = false;
+  uint32_t gemm_tc_min = 96;
   bool tp_fused = true;      // tensor-parallel decode: exchange fused into the projections (else exchange kernels)
   // decode: L2 prefetch of the next matrix's first bytes per launch (YL_PF_MB).
   // Off: measured slower at every size tried (16, 32, 48 MB).
   uint64_t pf_bytes = 0;
 };
 const Tunables& tunables();
+// Runtime override of a tunable (yl_config_set): gemm, gemm_tc, gemm_tc_min.
+int set_tunable(const std::string& key, int64_t value);
 // Launches the matvec for `ntok` tokens (groups of 8) with activations x*.
 int run_matvec(const DevWeight& w, bool f32act, const int8_t* xq, const float* xs, const float* xf,
                uint64_t x_stride, uint64_t xs_stride, uint32_t ntok, float* out, uint64_t out_stride, int epi,

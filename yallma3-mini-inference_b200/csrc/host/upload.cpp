@@ -8,6 +8,7 @@
 #include <unistd.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <thread>
 #include <vector>
@@ -85,6 +86,7 @@ int Uploader::rows(int fmt, bool sf16, uint32_t nrows, uint32_t cols, const RowF
     if ((rc = alloc((size_t)nrows * w->scale_row_bytes, &s))) return rc;
     w->s = (uint8_t*)s;
   }
+  std::atomic<bool> inf_scale{false};
   const size_t per_row = (size_t)w->row_bytes + w->scale_row_bytes;
   const uint32_t chunk_rows = (uint32_t)std::max<size_t>(1, (64u << 20) / per_row);
   if ((rc = ensure_stage((size_t)std::min(chunk_rows, std::max(nrows, 1u)) * per_row))) return rc;
@@ -97,6 +99,12 @@ int Uploader::rows(int fmt, bool sf16, uint32_t nrows, uint32_t cols, const RowF
         uint8_t* ds = w->scale_row_bytes ? ss + r * w->scale_row_bytes : nullptr;
         if (ds) memset(ds, 0, w->scale_row_bytes);  // the padding past cols/32 scales
         fill(r0 + (uint32_t)r, sq + r * w->row_bytes, ds);
+        if (ds && sf16)
+          for (uint32_t b = 0; b < nb; ++b) {
+            uint16_t h;
+            memcpy(&h, ds + 2 * b, 2);
+            if ((h & 0x7FFFu) == 0x7C00u) inf_scale = true;
+          }
       }
     });
     YL_CUDA_TRY(cudaMemcpy(w->q + (size_t)r0 * w->row_bytes, sq, (size_t)nr * w->row_bytes, cudaMemcpyHostToDevice));
@@ -104,6 +112,7 @@ int Uploader::rows(int fmt, bool sf16, uint32_t nrows, uint32_t cols, const RowF
       YL_CUDA_TRY(cudaMemcpy(w->s + (size_t)r0 * w->scale_row_bytes, ss, (size_t)nr * w->scale_row_bytes,
                              cudaMemcpyHostToDevice));
   }
+  w->no_inf_scales = !inf_scale;
   return YL_OK;
 }
 

@@ -184,9 +184,16 @@ struct GemmArgs {
   uint32_t quirk_cols;
   int8_t* hq;
   float* hs;
+  int* err;  // device error word (bounded waits of the tensor-memory GEMM)
+  float neg_zero;  // -0.0f, set by gemm_tc (an addend the compiler cannot see through)
 };
 bool gemm_supported(const GemmArgs& a, int fmt, bool scale_f16, int epi);
 cudaError_t gemm_q(const GemmArgs& a, int fmt, bool scale_f16, int epi, const LaunchCfg& lc);
+// The same contraction on the 5th-generation tensor cores (tcgen05.mma
+// kind::i8, TMA-fed, accumulators in tensor memory; Q8_0 weights, 128 x 128
+// tiles), bit-identical to gemm_q. Needs the 16-byte alignments of TMA.
+bool gemm_tc_supported(const GemmArgs& a, int fmt, bool scale_f16, int epi);
+cudaError_t gemm_tc(const GemmArgs& a, bool scale_f16, int epi, const LaunchCfg& lc);
 
 // ---- activations ------------------------------------------------------------
 // Bit-exact Q8_0 quantization of nblocks 32-element blocks (warp per block).
