@@ -540,6 +540,31 @@ def main() -> None:
         t = torch.tensor([e2e_s], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
+    # batched decode of independent sessions (yl_batch_forward): 8 sessions
+    # prefilled with the prompt, then greedy steps together; host call timed
+    batched = None
+    if world == 1:
+        nb, bsteps = 8, 16
+        bs = [model.create_session() for _ in range(nb)]
+        btok = []
+        for se in bs:
+            _, t1 = model.forward_x_full(prompt, 0, se, want_logits=False)
+            btok.append(t1)
+        batch = model.create_batch(nb)
+        bpos = [PROMPT_LEN] * nb
+        for _ in range(2):  # untimed
+            ids, _ = batch.forward(bs, btok, bpos)
+            btok, bpos = [int(i) for i in ids], [q + 1 for q in bpos]
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(bsteps):
+            ids, _ = batch.forward(bs, btok, bpos)
+            btok, bpos = [int(i) for i in ids], [q + 1 for q in bpos]
+        bsec = time.perf_counter() - t0
+        batched = {"sessions": nb, "steps": bsteps, "tokens_per_s": nb * bsteps / bsec,
+                   "ms_per_step": bsec / bsteps * 1e3, "call": "yl_batch_forward (host ids in and out each step)",
+                   "positions": f"{PROMPT_LEN + 2}..{PROMPT_LEN + 2 + bsteps}"}
+        del batch, bs
     # dominant kernel roofline (this rank's gate/up shard)
     mv = time_dominant_matvec(yl, torch, model, cfg, 96, world)
     peaks = measured_peaks()
@@ -576,6 +601,8 @@ def main() -> None:
         "prefill": {"tokens": PROMPT_LEN, "s": prefill_s, "tokens_per_s": PROMPT_LEN / prefill_s},
         "load_s": load_s,
     }
+    if batched:
+        line["batched"] = batched
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         del model, sess
         torch.cuda.empty_cache()

@@ -182,6 +182,24 @@ typedef struct yl_shape {
   int32_t _pad;
 } yl_shape;
 
+/* Batched decode of independent sessions (no reference counterpart: the
+ * reference serves one session per forward_x call, each user holding their
+ * own InferenceSession, main.rs:23-32, with Transformer: Send + Sync,
+ * transformer.rs:19). One yl_batch_forward call is one decode step for n
+ * distinct sessions of the batch's model: token tokens[i] at position
+ * positions[i] of sessions[i]. The projections run once over the n stacked
+ * rows (weights streamed once per 8 rows on the matvec, once per 64 on the
+ * GEMM from 16 rows) and the attention is one launch over every session's own
+ * KV cache and position; each session's results equal a yl_forward_x step of
+ * that session alone, bit for bit. logits_out (nullable): n x vocab floats,
+ * row i for session i; ids_out (nullable): the n greedy ids. Each session's
+ * pos becomes positions[i] + 1. n <= max_sessions <= 16; one GPU. */
+typedef struct yl_batch yl_batch;
+int yl_batch_create(const yl_model* m, uint32_t max_sessions, yl_batch** out);
+int yl_batch_free(yl_batch* b);
+int yl_batch_forward(yl_batch* b, yl_session* const* sessions, uint32_t n, const uint32_t* tokens,
+                     const uint32_t* positions, float* logits_out, uint32_t* ids_out);
+
 /* Process-wide options of the device path (no reference counterpart), read
  * by launches made after the call:
  *  "gemm"        1 = batches of 16+ tokens on the int8 tensor-core GEMM (default)

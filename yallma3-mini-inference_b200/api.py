@@ -113,6 +113,9 @@ _sigs = {
     "yl_decode_greedy": (C.c_int, [_P, _P, C.c_uint32, C.c_uint32, C.c_uint32, _P, _P, C.c_int]),
     "yl_decode_step_launches": (C.c_int, [_P, C.POINTER(C.c_uint32)]),
     "yl_config_set": (C.c_int, [C.c_char_p, C.c_int64]),
+    "yl_batch_create": (C.c_int, [_P, C.c_uint32, C.POINTER(_P)]),
+    "yl_batch_free": (C.c_int, [_P]),
+    "yl_batch_forward": (C.c_int, [_P, C.POINTER(_P), C.c_uint32, _P, _P, _P, _P]),
     "yl_session_decode_graph_launches": (C.c_int, [_P, C.c_int, C.POINTER(C.c_uint32)]),
     "yl_model_attention_decode": (C.c_int, [_P, _P, _P, _P, C.c_uint32, _P, _P, _P, _P]),
     "yl_profile_decode_step": (C.c_int, [_P, _P, C.c_uint32, C.c_uint32, _P, C.c_uint32, C.POINTER(C.c_uint32)]),
@@ -345,6 +348,47 @@ class InferenceSession:
             pass
 
 
+class SessionBatch:
+    """Batched decode of independent sessions (yl_batch_forward): one step
+    feeds one token to each of up to `max_sessions` sessions of one model."""
+
+    def __init__(self, model: "Transformer", max_sessions: int):
+        h = _P()
+        _check(_lib.yl_batch_create(model._h, int(max_sessions), C.byref(h)))
+        self._h = h.value
+        self._model = model
+        self.max_sessions = int(max_sessions)
+
+    def forward(self, sessions: Sequence["InferenceSession"], tokens: Sequence[int], positions: Sequence[int],
+                want_logits: bool = False):
+        """One decode step; returns (ids [n], logits [n, vocab] or None). Each
+        session's pos becomes positions[i] + 1."""
+        n = len(sessions)
+        hs = (_P * n)(*[se._h for se in sessions])
+        t = np.ascontiguousarray(tokens, np.uint32)
+        p = np.ascontiguousarray(positions, np.uint32)
+        if t.size != n or p.size != n:
+            raise ValueError("one token and one position per session")
+        ids = np.empty(n, np.uint32)
+        logits = np.empty((n, self._model.vocab_size()), np.float32) if want_logits else None
+        _check(_lib.yl_batch_forward(self._h, hs, n, _ptr(t), _ptr(p), _ptr(logits) if logits is not None else None,
+                                     _ptr(ids)))
+        for i, se in enumerate(sessions):
+            se.pos = int(p[i]) + 1
+        return ids, logits
+
+    def close(self) -> None:
+        if self._h:
+            _lib.yl_batch_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 class Transformer:
     """The Transformer trait (transformer.rs:19-69) over a device model."""
 
@@ -397,6 +441,10 @@ class Transformer:
         h = _P()
         _check(_lib.yl_create_session(self._h, C.byref(h)))
         return InferenceSession(h.value, self)
+
+    def create_batch(self, max_sessions: int) -> SessionBatch:
+        """Workspace for batched decode of up to max_sessions (<= 16) sessions."""
+        return SessionBatch(self, max_sessions)
 
     def forward_x(self, tokens: Sequence[int], start_pos: int, session: InferenceSession) -> np.ndarray:
         """Logits of the last token (length vocab_size), like forward.rs:261-279."""

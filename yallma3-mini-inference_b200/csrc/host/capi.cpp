@@ -12,6 +12,9 @@ struct yl_model {
 struct yl_session {
   yl::Session* s;
 };
+struct yl_batch {
+  yl::Batch* b;
+};
 
 namespace yl {
 namespace {
@@ -479,6 +482,50 @@ int yl_session_free(yl_session* s) {
   return YL_OK;
 }
 uint32_t yl_session_pos(const yl_session* s) { return s ? s->s->pos : 0; }
+
+int yl_batch_create(const yl_model* m, uint32_t max_sessions, yl_batch** out) {
+  if (!m || !out) return fail(YL_ERR_ARG, "null argument");
+  Batch* b = nullptr;
+  int rc = batch_create(m->m, max_sessions, &b);
+  if (rc) return rc;
+  *out = new yl_batch{b};
+  return YL_OK;
+}
+
+int yl_batch_free(yl_batch* b) {
+  if (!b) return fail(YL_ERR_ARG, "null batch");
+  delete b->b;
+  delete b;
+  return YL_OK;
+}
+
+int yl_batch_forward(yl_batch* bp, yl_session* const* sessions, uint32_t n, const uint32_t* tokens,
+                     const uint32_t* positions, float* logits_out, uint32_t* ids_out) {
+  if (!bp || !sessions || !tokens || !positions) return fail(YL_ERR_ARG, "null argument");
+  Batch* b = bp->b;
+  if (n == 0 || n > b->cap) return fail(YL_ERR_ARG, "batch size out of range");
+  Session* ss[k::YL_MAX_BATCH];
+  for (uint32_t i = 0; i < n; ++i) {
+    if (!sessions[i]) return fail(YL_ERR_ARG, "null session");
+    ss[i] = sessions[i]->s;
+  }
+  int rc = forward_batch(b, ss, n, tokens, positions);
+  if (rc) return rc;
+  Session* w = b->ws;
+  const uint64_t V = b->m->shape.vocab_size;
+  if (logits_out)
+    YL_CUDA_TRY(cudaMemcpyAsync(logits_out, b->logits, (uint64_t)n * V * 4, cudaMemcpyDeviceToHost, w->stream));
+  YL_CUDA_TRY(cudaMemcpyAsync(b->tok_h + b->cap, b->ids, (uint64_t)n * 4, cudaMemcpyDeviceToHost, w->stream));
+  YL_CUDA_TRY(cudaMemcpyAsync(b->tok_h + 2 * b->cap, w->err, 4, cudaMemcpyDeviceToHost, w->stream));
+  YL_CUDA_TRY(cudaStreamSynchronize(w->stream));
+  if (const int herr = (int)b->tok_h[2 * b->cap]) {
+    cudaMemsetAsync(w->err, 0, sizeof(int), w->stream);
+    cudaStreamSynchronize(w->stream);
+    return fail(YL_ERR_TIMEOUT, "a bounded device wait expired (error word " + std::to_string(herr) + ")");
+  }
+  if (ids_out) memcpy(ids_out, b->tok_h + b->cap, (uint64_t)n * 4);
+  return YL_OK;
+}
 int yl_session_set_pos(yl_session* s, uint32_t pos) {
   if (!s) return fail(YL_ERR_ARG, "null session");
   if (pos > s->s->m->shape.ctx_len) return fail(YL_ERR_RANGE, "position beyond ctx_len");

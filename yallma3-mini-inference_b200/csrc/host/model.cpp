@@ -410,7 +410,9 @@ int ensure_cap(Session* s, uint32_t n) {
 }
 }  // namespace
 
-int session_create(const Model* m, Session** out) {
+int session_create(const Model* m, Session** out) { return session_create_ex(m, true, out); }
+
+int session_create_ex(const Model* m, bool with_kv, Session** out) {
   std::unique_ptr<Session> s(new Session());
   s->m = m;
   s->device = m->device;
@@ -418,15 +420,17 @@ int session_create(const Model* m, Session** out) {
   YL_CUDA_TRY(cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking));
   const yl_shape& sh = m->shape;
   const uint64_t kvd = (uint64_t)m->l_kv * sh.head_size;  // this rank's KV heads
-  s->kv_elems = (uint64_t)sh.n_layers * sh.ctx_len * kvd;
+  s->kv_elems = with_kv ? (uint64_t)sh.n_layers * sh.ctx_len * kvd : 0;
   void* p;
   int rc;
-  if ((rc = salloc(s.get(), s->kv_elems * 4, &p))) return rc;
-  s->kcache = (float*)p;
-  if ((rc = salloc(s.get(), s->kv_elems * 4, &p))) return rc;
-  s->vcache = (float*)p;
-  YL_CUDA_TRY(cudaMemset(s->kcache, 0, s->kv_elems * 4));
-  YL_CUDA_TRY(cudaMemset(s->vcache, 0, s->kv_elems * 4));
+  if (with_kv) {
+    if ((rc = salloc(s.get(), s->kv_elems * 4, &p))) return rc;
+    s->kcache = (float*)p;
+    if ((rc = salloc(s.get(), s->kv_elems * 4, &p))) return rc;
+    s->vcache = (float*)p;
+    YL_CUDA_TRY(cudaMemset(s->kcache, 0, s->kv_elems * 4));
+    YL_CUDA_TRY(cudaMemset(s->vcache, 0, s->kv_elems * 4));
+  }
   if ((rc = salloc(s.get(), (uint64_t)sh.vocab_size * 4, &p))) return rc;
   s->logits = (float*)p;
   // decode attention: one cluster of n_splits CTAs per KV head; the scores /
@@ -986,6 +990,146 @@ int forward(Session* s, const uint32_t* tokens_host, uint32_t n, uint32_t start_
     rc = enqueue_forward(s, nc, start_pos + t0, false, tunables().pdl, nullptr, want_logits && t0 + nc == n);
     if (rc) return rc;
   }
+  return YL_OK;
+}
+
+// ------------------------------ batched sessions ---------------------------
+
+Batch::~Batch() {
+  if (ws) {
+    cudaStreamSynchronize(ws->stream);
+    delete ws;
+  }
+  if (tok_h) cudaFreeHost(tok_h);
+}
+
+int batch_create(const Model* m, uint32_t cap, Batch** out) {
+  if (cap == 0 || cap > k::YL_MAX_BATCH)
+    return fail(YL_ERR_ARG, "a batch carries 1 to " + std::to_string(k::YL_MAX_BATCH) + " sessions");
+  if (m->tp_size > 1) return fail(YL_ERR_UNSUPPORTED, "batched decode runs on one GPU (not tensor parallel)");
+  YL_CUDA_TRY(cudaSetDevice(m->device));
+  std::unique_ptr<Batch> b(new Batch());
+  b->m = m;
+  b->cap = cap;
+  int rc = session_create_ex(m, false, &b->ws);
+  if (rc) return rc;
+  Session* w = b->ws;
+  if ((rc = ensure_cap(w, cap))) return rc;
+  const yl_shape& sh = m->shape;
+  void* p;
+  if ((rc = salloc(w, (uint64_t)cap * m->l_heads * w->part_stride * 4, &p))) return rc;
+  b->sc = (float*)p;
+  if ((rc = salloc(w, (uint64_t)cap * sh.vocab_size * 4, &p))) return rc;
+  b->logits = (float*)p;
+  if ((rc = salloc(w, (uint64_t)cap * 4, &p))) return rc;
+  b->ids = (uint32_t*)p;
+  YL_CUDA_TRY(cudaMallocHost(&b->tok_h, (uint64_t)(2 * cap + 1) * 4));
+  *out = b.release();
+  return YL_OK;
+}
+
+int forward_batch(Batch* b, Session* const* ss, uint32_t n, const uint32_t* tokens, const uint32_t* pos) {
+  const Model* m = b->m;
+  const yl_shape& sh = m->shape;
+  if (n == 0 || n > b->cap) return fail(YL_ERR_ARG, "batch of " + std::to_string(n) + " sessions, capacity " + std::to_string(b->cap));
+  for (uint32_t i = 0; i < n; ++i) {
+    if (!ss[i] || ss[i]->m != m) return fail(YL_ERR_ARG, "session missing or of another model");
+    if (pos[i] >= sh.ctx_len) return fail(YL_ERR_RANGE, "position beyond ctx_len");
+    for (uint32_t j = 0; j < i; ++j)
+      if (ss[j] == ss[i]) return fail(YL_ERR_ARG, "a session appears twice in one batch");
+  }
+  Session* w = b->ws;
+  YL_CUDA_TRY(cudaSetDevice(m->device));
+  for (uint32_t i = 0; i < n; ++i) YL_CUDA_TRY(cudaStreamSynchronize(ss[i]->stream));  // their caches are settled
+  memcpy(b->tok_h, tokens, (uint64_t)n * 4);
+  YL_CUDA_TRY(cudaMemcpyAsync(w->tok, b->tok_h, (uint64_t)n * 4, cudaMemcpyHostToDevice, w->stream));
+  const uint32_t d = sh.dim, att = m->l_heads * sh.head_size, kvd = m->l_kv * sh.head_size, f = m->l_ffn;
+  const bool f32act = sh.weight_format == YL_F16;
+  const bool pdl = tunables().pdl;
+  k::LaunchCfg lc;
+  lc.stream = w->stream;
+  lc.pdl = pdl;
+  int rc;
+  cudaError_t e = k::embed(m->emb.fmt == YL_Q8_0 ? k::FMT_Q8 : m->emb.fmt == YL_Q4_0 ? k::FMT_Q4 : k::FMT_F16, m->emb.q,
+                           m->emb.s, m->emb.row_bytes, m->emb.scale_row_bytes, m->emb.sf16, d, sh.vocab_size, w->tok,
+                           nullptr, n, w->x, lc);
+  if (e != cudaSuccess) return fail(YL_ERR_CUDA, std::string("embed launch: ") + cudaGetErrorString(e));
+  MvExtra norm, plain;
+  norm.pro = k::PRO_NORM;
+  norm.xres = w->x;
+  norm.eps = sh.rms_norm_eps;
+  norm.gq = w->xq;  // 16+ rows: normalized rows for the GEMM
+  norm.gs = w->xs;
+  for (uint32_t l = 0; l < sh.n_layers; ++l) {
+    const Layer& L = m->layers[l];
+    // attention block: the stacked rows' projections, then every session's
+    // RoPE, cache write and attention over its own cache in one launch
+    norm.norm_w = L.rms_att;
+    norm.hq = nullptr;
+    norm.hs = nullptr;
+    norm.hcount = nullptr;
+    if ((rc = run_matvec_ex(L.wqkv, f32act, nullptr, nullptr, nullptr, d, d / 32, n, w->qkv, att + 2 * kvd,
+                            k::EPI_STORE, 0, w->err, w->stream, pdl, m->num_sms, norm, nullptr)))
+      return rc;
+    k::AttnDecodeArgs ad{};
+    ad.qkv = w->qkv;
+    ad.cs = m->rope_cs;
+    ad.rope_mode = sh.rope_mode;
+    ad.n_heads = m->l_heads;
+    ad.n_kv_heads = m->l_kv;
+    ad.head_size = sh.head_size;
+    ad.kv_dim = kvd;
+    ad.scale = m->attn_scale;
+    ad.n_splits = w->n_splits;
+    ad.sc = b->sc;
+    ad.sc_stride = w->part_stride;
+    ad.early_kv = 0;
+    ad.out = f32act ? w->xf : nullptr;
+    ad.q8 = f32act ? nullptr : w->xq;
+    ad.s8 = w->xs;
+    ad.nseq = n;
+    for (uint32_t i = 0; i < n; ++i) {
+      ad.kseq[i] = ss[i]->kcache + (uint64_t)l * sh.ctx_len * kvd;
+      ad.vseq[i] = ss[i]->vcache + (uint64_t)l * sh.ctx_len * kvd;
+      ad.pseq[i] = pos[i];
+    }
+    ad.qkv_stride = att + 2 * kvd;
+    ad.sc_seq_stride = (uint64_t)m->l_heads * w->part_stride;
+    if ((e = k::attention_decode(ad, lc)) != cudaSuccess)
+      return fail(YL_ERR_CUDA, std::string("batched attention launch: ") + cudaGetErrorString(e));
+    if ((rc = run_matvec_ex(L.wo, f32act, w->xq, w->xs, w->xf, att, att / 32, n, w->x, d, k::EPI_ADD, 0, w->err,
+                            w->stream, pdl, m->num_sms, plain, nullptr)))
+      return rc;
+    // feed-forward block
+    norm.norm_w = L.rms_ffn;
+    norm.hq = f32act ? nullptr : w->hq;
+    norm.hs = f32act ? nullptr : w->hs;
+    norm.hcount = f32act ? nullptr : w->hcount;
+    if ((rc = run_matvec_ex(L.w13, f32act, nullptr, nullptr, nullptr, d, d / 32, n, w->h, f,
+                            f32act ? k::EPI_SWIGLU : k::EPI_SWIGLU_Q8, 0, w->err, w->stream, pdl, m->num_sms, norm,
+                            nullptr)))
+      return rc;
+    if ((rc = run_matvec_ex(L.w2, f32act, w->hq, w->hs, w->h, f, f / 32, n, w->x, d, k::EPI_ADD, 0, w->err, w->stream,
+                            pdl, m->num_sms, plain, nullptr)))
+      return rc;
+  }
+  // every row's final norm, lm_head and greedy id (forward.rs:256-279)
+  for (uint32_t i = 0; i < n; ++i) {
+    MvExtra fin;
+    fin.pro = k::PRO_NORM;
+    fin.xres = w->x + (uint64_t)i * d;
+    fin.norm_w = m->rms_final;
+    fin.eps = sh.rms_norm_eps;
+    fin.am_val = w->am_val;
+    fin.am_idx = w->am_idx;
+    fin.am_count = w->am_count;
+    fin.am_out = b->ids + i;
+    fin.work = w->work + 2ull * sh.n_layers;
+    if ((rc = run_matvec_ex(m->lm, true, nullptr, nullptr, nullptr, d, 0, 1, b->logits + (uint64_t)i * sh.vocab_size,
+                            m->l_vocab, k::EPI_ARGMAX, 0, w->err, w->stream, pdl, m->num_sms, fin, nullptr)))
+      return rc;
+  }
+  for (uint32_t i = 0; i < n; ++i) ss[i]->pos = pos[i] + 1;
   return YL_OK;
 }
 

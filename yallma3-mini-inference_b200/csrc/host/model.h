@@ -124,6 +124,8 @@ int model_load_lmrs(const char* path, uint32_t max_ctx_len, int fmt_override, Mo
 int session_tp_handle(Session* s, void* handle_out);
 int session_tp_connect(Session* s, const void* handles);
 int session_create(const Model* m, Session** out);
+// with_kv = false: a workspace session without a KV cache (batched decode)
+int session_create_ex(const Model* m, bool with_kv, Session** out);
 int session_reset(Session* s);
 // General forward over n tokens (prefill or decode); last-token logits stay in
 // s->logits (device), greedy id in s->hist[0].
@@ -162,6 +164,25 @@ struct Tunables {
   // Off: measured slower at every size tried (16, 32, 48 MB).
   uint64_t pf_bytes = 0;
 };
+// Batched decode of independent sessions (one token each per step): the
+// projections run once over the stacked rows, the attention is one launch
+// over every session's own cache and position. Holds the workspace.
+struct Batch {
+  const Model* m = nullptr;
+  Session* ws = nullptr;     // workspace: activations of up to `cap` rows, no KV cache
+  uint32_t cap = 0;
+  float* sc = nullptr;       // decode attention scores [cap][local heads][part_stride]
+  float* logits = nullptr;   // [cap][vocab]
+  uint32_t* ids = nullptr;   // [cap] greedy ids
+  uint32_t* tok_h = nullptr; // page-locked staging: tokens in, ids and the error word out
+  ~Batch();
+};
+int batch_create(const Model* m, uint32_t cap, Batch** out);
+// One decode step for n sessions: token i at position pos[i] of session ss[i]
+// (distinct sessions of b's model). Logits and ids stay in b->logits / b->ids;
+// the caller synchronizes b->ws->stream.
+int forward_batch(Batch* b, Session* const* ss, uint32_t n, const uint32_t* tokens, const uint32_t* pos);
+
 const Tunables& tunables();
 // Runtime override of a tunable (yl_config_set): gemm, gemm_tc, gemm_tc_min.
 int set_tunable(const std::string& key, int64_t value);

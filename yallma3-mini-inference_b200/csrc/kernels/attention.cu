@@ -357,7 +357,7 @@ struct AdSmem {
 };
 
 template <int HD, int KVM>
-__global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(AttnDecodeArgs a) {
+__global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(const __grid_constant__ AttnDecodeArgs a) {
   extern __shared__ __align__(16) uint8_t ad_raw[];
   AdSmem<HD>& sm = *reinterpret_cast<AdSmem<HD>*>(ad_raw);
   cg::cluster_group cluster = cg::this_cluster();
@@ -365,21 +365,30 @@ __global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(AttnDecodeArgs 
   const uint32_t cs = a.n_splits;
   const uint32_t rank = cluster.block_rank();
   const uint32_t kvh = blockIdx.x / cs;
-  uint64_t* const trace = (kTrace && a.trace) ? a.trace + (uint64_t)blockIdx.x * 8 : nullptr;
+  // this CTA's sequence: the single one, or grid row y of a batched launch
+  const uint32_t sq = a.nseq ? blockIdx.y : 0u;
+  float* const kcache = a.nseq ? a.kseq[sq] : a.kcache;
+  float* const vcache = a.nseq ? a.vseq[sq] : a.vcache;
+  const float* const qkv = a.qkv + (uint64_t)sq * a.qkv_stride;
+  const uint64_t orow = (uint64_t)sq * a.n_heads * HD;
+  float* const outp = a.out ? a.out + orow : nullptr;
+  int8_t* const q8p = a.q8 ? a.q8 + orow : nullptr;
+  float* const s8p = a.q8 ? a.s8 + orow / 32 : nullptr;
+  uint64_t* const trace = (kTrace && a.trace && blockIdx.y == 0) ? a.trace + (uint64_t)blockIdx.x * 8 : nullptr;
   uint64_t ts[8] = {0, 0, 0, 0, 0, 0, 0, 0};  // timeline stamps, stored at the end
   if (trace && tid == 0) ts[0] = globaltimer();
   grid_dep_launch();
   if (tid == 0) l2_prefetch_next(a.pf, blockIdx.x, gridDim.x);
   if (!a.early_kv) grid_dep_wait();
-  const uint32_t pos = a.state ? (uint32_t)a.state->pos : a.pos0;
+  const uint32_t pos = a.nseq ? a.pseq[sq] : a.state ? (uint32_t)a.state->pos : a.pos0;
   const uint32_t nvis = pos + 1;
   const uint32_t chunk = (nvis + cs - 1) / cs;
   const uint32_t p_begin = min(nvis, rank * chunk), p_end = min(nvis, p_begin + chunk);
   const uint32_t att = a.n_heads * HD, half = HD / 2;
   const bool owner = p_begin <= pos && pos < p_end;
-  const float* kbase = a.kcache + kvh * HD;
-  const float* vbase = a.vcache + kvh * HD;
-  float* const sc0 = a.sc + (uint64_t)kvh * KVM * a.sc_stride;  // this KV head's query heads
+  const float* kbase = kcache + kvh * HD;
+  const float* vbase = vcache + kvh * HD;
+  float* const sc0 = a.sc + (uint64_t)sq * a.sc_seq_stride + (uint64_t)kvh * KVM * a.sc_stride;  // this KV head's query heads
 
   auto issue_tile = [&](uint32_t base, uint32_t n) {
     for (uint32_t i = tid; i < n * (HD / 4); i += AD_THREADS) {
@@ -406,21 +415,21 @@ __global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(AttnDecodeArgs 
     const uint32_t hh = i / half, p = i % half;
     uint32_t i0, i1;
     pair_index(a.rope_mode, p, half, i0, i1);
-    const float* src = hh < KVM ? a.qkv + (kvh * KVM + hh) * HD : a.qkv + att + kvh * HD;
+    const float* src = hh < KVM ? qkv + (kvh * KVM + hh) * HD : qkv + att + kvh * HD;
     float r0, r1;
     rotate(src[i0], src[i1], c[p], r0, r1);
     float* dst = hh < KVM ? sm.qs[hh] : sm.nk;
     dst[i0] = r0;
     dst[i1] = r1;
     if (hh == KVM) {
-      float* kd = a.kcache + (uint64_t)pos * a.kv_dim + kvh * HD;
+      float* kd = kcache + (uint64_t)pos * a.kv_dim + kvh * HD;
       kd[i0] = r0;
       kd[i1] = r1;
     }
   }
   if (owner)
     for (uint32_t d = tid; d < HD; d += AD_THREADS)
-      a.vcache[(uint64_t)pos * a.kv_dim + kvh * HD + d] = a.qkv[att + a.kv_dim + kvh * HD + d];
+      vcache[(uint64_t)pos * a.kv_dim + kvh * HD + d] = qkv[att + a.kv_dim + kvh * HD + d];
   if (trace && tid == 0) ts[4] = globaltimer();
 
   // ---- 1. scores of the slice: thread (head tid/64 + 4m, key tid%64) ----
@@ -553,7 +562,7 @@ __global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(AttnDecodeArgs 
     for (uint32_t i = 0; i < nmine; ++i)
       if (tid < 32)
         sm.vbuf[(i * vrows + pos) * 32 + tid] =
-            a.qkv[att + a.kv_dim + kvh * HD + ((rank + i * cs) % BPH) * 32 + tid];
+            qkv[att + a.kv_dim + kvh * HD + ((rank + i * cs) % BPH) * 32 + tid];
   __syncthreads();
   // P.V: warp l runs lane l of the sums (positions l, l + 8, ...) for every
   // block of the CTA, chunk by chunk (a single chunk is still in ebuf); the
@@ -624,12 +633,12 @@ __global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(AttnDecodeArgs 
       for (int u = 0; u < 8; ++u)
         if (nsimd8 + u < nvis) o = __fadd_rn(o, __fmul_rn(__fmul_rn(sm.ebuf[i][nsimd8 + u - c0], inv[i]), vt[u]));
       const uint64_t k = (uint64_t)(kvh * KVM + hh) * HD + d;
-      if (a.out) a.out[k] = o;
-      if (a.q8) {
+      if (outp) outp[k] = o;
+      if (q8p) {
         float scl;
         const int8_t qv = quant_q8_lane(o, &scl);
-        a.q8[k] = qv;
-        if (lane == 0) a.s8[k / 32] = scl;
+        q8p[k] = qv;
+        if (lane == 0) s8p[k / 32] = scl;
       }
     }
     __syncthreads();  // lanes[] is rewritten by the next block
@@ -642,7 +651,7 @@ __global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(AttnDecodeArgs 
 
 template <int HD, int KVM>
 static cudaError_t decode_config(uint32_t n_kv_heads, uint32_t cs, cudaStream_t st, bool pdl, cudaLaunchConfig_t& cfg,
-                                 cudaLaunchAttribute (&attr)[2]) {
+                                 cudaLaunchAttribute (&attr)[2], uint32_t nseq = 0) {
   const uint32_t smem = sizeof(AdSmem<HD>);
   cudaError_t e =
       cudaFuncSetAttribute(attn_decode_kernel<HD, KVM>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -650,7 +659,7 @@ static cudaError_t decode_config(uint32_t n_kv_heads, uint32_t cs, cudaStream_t 
     e = cudaFuncSetAttribute(attn_decode_kernel<HD, KVM>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
   if (e != cudaSuccess) return e;
   cfg = {};
-  cfg.gridDim = dim3(n_kv_heads * cs);
+  cfg.gridDim = dim3(n_kv_heads * cs, nseq ? nseq : 1u);
   cfg.blockDim = dim3(AD_THREADS);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
@@ -687,7 +696,7 @@ template <int HD, int KVM>
 static cudaError_t launch_decode(const AttnDecodeArgs& a, const LaunchCfg& lc) {
   cudaLaunchConfig_t cfg;
   cudaLaunchAttribute attr[2];
-  cudaError_t e = decode_config<HD, KVM>(a.n_kv_heads, a.n_splits, lc.stream, lc.pdl, cfg, attr);
+  cudaError_t e = decode_config<HD, KVM>(a.n_kv_heads, a.n_splits, lc.stream, lc.pdl, cfg, attr, a.nseq);
   if (e != cudaSuccess) return e;
   return cudaLaunchKernelEx(&cfg, attn_decode_kernel<HD, KVM>, a);
 }
@@ -711,7 +720,12 @@ cudaError_t attention_decode(const AttnDecodeArgs& a, const LaunchCfg& lc) {
   const uint32_t kv_mul = a.n_kv_heads ? a.n_heads / a.n_kv_heads : 0;
   if (kv_mul == 0 || kv_mul > AT_MAXKV || a.n_splits == 0 || a.n_splits > AD_MAXCS) return cudaErrorInvalidValue;
   if (kv_mul * a.head_size / 32 > a.n_splits * AD_MAXSLOT) return cudaErrorInvalidValue;
-  if (a.kv_dim % 4 || ((uintptr_t)a.kcache | (uintptr_t)a.vcache | (uintptr_t)a.sc) % 16 || a.sc_stride % 4 || !a.sc)
+  if (a.kv_dim % 4 || (uintptr_t)a.sc % 16 || a.sc_stride % 4 || !a.sc || a.nseq > YL_MAX_BATCH)
+    return cudaErrorInvalidValue;
+  if (a.nseq == 0 && ((uintptr_t)a.kcache | (uintptr_t)a.vcache) % 16) return cudaErrorInvalidValue;
+  for (uint32_t i = 0; i < a.nseq; ++i)
+    if (!a.kseq[i] || !a.vseq[i] || ((uintptr_t)a.kseq[i] | (uintptr_t)a.vseq[i]) % 16) return cudaErrorInvalidValue;
+  if (a.nseq && (a.qkv_stride % 4 || a.sc_seq_stride % 4 || a.sc_seq_stride < (uint64_t)a.n_heads * a.sc_stride))
     return cudaErrorInvalidValue;
   if (a.head_size == 64) return launch_decode_hd<64>(a, lc, kv_mul);
   if (a.head_size == 128) return launch_decode_hd<128>(a, lc, kv_mul);

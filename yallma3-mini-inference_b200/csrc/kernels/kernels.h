@@ -15,6 +15,9 @@
 namespace yl {
 namespace k {
 
+// Sessions one batched decode step can carry (yl_batch_forward).
+constexpr uint32_t YL_MAX_BATCH = 16;
+
 // FMT_Q8X: Q8_0 weights against f32 activations held as three int8 limbs per
 // 32-block, y = s * (a + b/254 + c/254^2) (|error| <= s/2/254^2, about 6e-8 of
 // the block's absmax), so the f32-activation lm_head runs on dp4a.
@@ -296,6 +299,16 @@ struct AttnDecodeArgs {
   L2Prefetch pf;
   float* sc;           // scores / weights scratch [n_heads][sc_stride]
   uint32_t sc_stride;
+  // Independent sequences in one launch (batched decode of several
+  // sessions): when nseq > 0, the CTAs of grid row y serve sequence y: its
+  // layer caches kseq[y] / vseq[y], its position pseq[y], row y of qkv
+  // (qkv_stride floats apart), out / q8 / s8 (n_heads*head_size apart) and
+  // scratch sc + y * sc_seq_stride. kcache, vcache, state and pos0 are unused.
+  uint32_t nseq;
+  float* kseq[YL_MAX_BATCH];
+  float* vseq[YL_MAX_BATCH];
+  uint32_t pseq[YL_MAX_BATCH];
+  uint64_t qkv_stride, sc_seq_stride;
 };
 // Cluster size for the decode attention: 16 when n_kv_heads clusters of 16
 // can be resident at once, else 8.
