@@ -339,6 +339,79 @@ int yl_trace_decode_step(const yl_model* m, yl_session* s, uint32_t token, uint3
  * the reference). Returns false on any error. */
 bool load_transformer_ffi(const char* model_path);
 
+/* infer_ffi / free_string as the reference documents them (README.md:88-92,
+ * PoC_Bun_load.js:12-38; the reference declares but never implements them).
+ * infer_ffi runs one fresh conversation on the model load_transformer_ffi
+ * loaded, the way the reference's console does (main.rs:149-214): the prompt
+ * is tokenized with the model's tokenizer into the no-template chat format
+ * (empty system prompt, the user turn, an empty assistant header), prefilled,
+ * and tokens are sampled on the device and decoded one at a time until EOS,
+ * the context length or the token limit. The reply (the decoded pieces
+ * concatenated, each piece decoded on its own as the console prints it) is
+ * returned as a malloc'ed UTF-8 string to be released with free_string.
+ * NULL on any error (no model loaded, empty or non-UTF-8 prompt, prompt longer
+ * than the context; yl_last_error() says which). Calls are serialized by a
+ * mutex; the session and the sampler persist across calls like the console's
+ * (the session is reset at each call, the sampler keeps its state). */
+const char* infer_ffi(const char* prompt);
+void free_string(const char* s);
+/* Sampling of infer_ffi. Defaults are the console's Sampler::new(vocab, 0.7,
+ * 0.9, 42) (main.rs:135) and no token limit (max_tokens 0). Takes effect at the
+ * next infer_ffi call (a changed setting starts a fresh sampler). */
+int yl_infer_config(float temperature, float top_p, uint64_t seed, uint32_t max_tokens);
+
+/* ---- tokenizer (tokenizer.rs) -------------------------------------------- */
+/* Host-side byte-level BPE tokenizer, loaded from the files the reference's
+ * loaders read: a .gguf file's tokenizer.ggml.* metadata
+ * (Tokenizer::from_gguf_parts, tokenizer.rs:78-132), tokenizer.json
+ * (from_json, :134-217) else tokenizer.bin (new, :219-262) beside a
+ * .safetensors file, tokenizer.bin beside a .lmrs file. Needs no GPU.
+ * A Jinja chat template (tokenizer.chat_template) is recorded but not
+ * rendered: yl_tokenizer_chat_prompt builds the no-template format for every
+ * tokenizer. */
+typedef struct yl_tokenizer yl_tokenizer;
+int yl_tokenizer_load(const char* model_path, yl_tokenizer** out);
+int yl_tokenizer_free(yl_tokenizer* t);
+/* Transformer::tokenizer(): the model's tokenizer, loaded from the model's
+ * file at the first call and owned by the model. */
+int yl_model_tokenizer(const yl_model* m, const yl_tokenizer** out);
+/* vocabulary size, BOS, EOS, whether a chat template is present */
+int yl_tokenizer_info(const yl_tokenizer* t, uint32_t* vocab_size, uint32_t* bos, uint32_t* eos, int* has_template);
+/* Tokenizer::encode(text, bos, eos) (tokenizer.rs:338-392). text: non-empty
+ * UTF-8 (YL_ERR_ARG otherwise). Writes up to cap ids; *n_out = the full count
+ * (YL_ERR_RANGE when it exceeds cap). */
+int yl_tokenizer_encode(const yl_tokenizer* t, const char* text, int bos, int eos, uint32_t* ids, uint64_t cap,
+                        uint64_t* n_out);
+/* Tokenizer::decode (tokenizer.rs:523-551): UTF-8 bytes (invalid sequences
+ * replaced by U+FFFD), NUL-terminated when it fits; *n_out = byte count
+ * without the terminator (YL_ERR_RANGE when n_out + 1 exceeds cap). */
+int yl_tokenizer_decode(const yl_tokenizer* t, const uint32_t* ids, uint64_t n, char* out, uint64_t cap,
+                        uint64_t* n_out);
+/* The console's prompt of a fresh conversation: apply_system_template(system)
+ * then apply_turn_template(user, true) (tokenizer.rs:453-521, no-template
+ * branches; main.rs:149-153,177). YL_ERR_FORMAT when a Llama-3 vocabulary does
+ * not encode "user" / "assistant" as single tokens (a panic in the reference). */
+int yl_tokenizer_chat_prompt(const yl_tokenizer* t, const char* system, const char* user, uint32_t* ids,
+                             uint64_t cap, uint64_t* n_out);
+
+/* ---- device sampler (sampler.rs:41-180) ---------------------------------- */
+/* Sampler::new(vocab_size, temperature, top_p, seed): device state (the
+ * persistent (prob, index) array, zeroed) on the current CUDA device. */
+typedef struct yl_sampler yl_sampler;
+int yl_sampler_create(uint32_t vocab_size, float temperature, float top_p, uint64_t seed, yl_sampler** out);
+int yl_sampler_free(yl_sampler* s);
+/* Sampler::sample(&mut logits): logits is a DEVICE row of vocab_size floats
+ * and is overwritten as the reference overwrites its slice (divided by the
+ * temperature, then the probabilities; untouched at temperature 0). The id is
+ * written to *id_out (host) after the stream synchronizes; with id_out NULL
+ * the call returns once the work is enqueued and yl_sampler_result() reads the
+ * id later. stream NULL: the legacy default stream. */
+int yl_sampler_sample(yl_sampler* s, float* logits, uint32_t* id_out, void* stream);
+int yl_sampler_result(yl_sampler* s, uint32_t* id_out);
+/* The session's logits row on the device after its latest yl_forward_x (the
+ * last token's logits; single-GPU models). */
+int yl_session_logits(const yl_session* s, float** logits);
+
 /* ---- synthetic model files (test and bench inputs) ----------------------- */
 typedef struct yl_synth_config {
   uint32_t dim, hidden_dim, n_layers, n_heads, n_kv_heads, vocab_size, context_length;

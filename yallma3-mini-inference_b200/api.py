@@ -121,6 +121,22 @@ _sigs = {
     "yl_profile_decode_step": (C.c_int, [_P, _P, C.c_uint32, C.c_uint32, _P, C.c_uint32, C.POINTER(C.c_uint32)]),
     "yl_trace_decode_step": (C.c_int, [_P, _P, C.c_uint32, C.c_uint32, _P, C.c_uint64, C.POINTER(C.c_uint32)]),
     "load_transformer_ffi": (C.c_bool, [C.c_char_p]),
+    "infer_ffi": (C.c_void_p, [C.c_char_p]),
+    "free_string": (None, [C.c_void_p]),
+    "yl_infer_config": (C.c_int, [C.c_float, C.c_float, C.c_uint64, C.c_uint32]),
+    "yl_tokenizer_load": (C.c_int, [C.c_char_p, C.POINTER(_P)]),
+    "yl_tokenizer_free": (C.c_int, [_P]),
+    "yl_model_tokenizer": (C.c_int, [_P, C.POINTER(_P)]),
+    "yl_tokenizer_info": (C.c_int, [_P, C.POINTER(C.c_uint32), C.POINTER(C.c_uint32), C.POINTER(C.c_uint32),
+                                    C.POINTER(C.c_int)]),
+    "yl_tokenizer_encode": (C.c_int, [_P, C.c_char_p, C.c_int, C.c_int, _P, C.c_uint64, C.POINTER(C.c_uint64)]),
+    "yl_tokenizer_decode": (C.c_int, [_P, _P, C.c_uint64, _P, C.c_uint64, C.POINTER(C.c_uint64)]),
+    "yl_tokenizer_chat_prompt": (C.c_int, [_P, C.c_char_p, C.c_char_p, _P, C.c_uint64, C.POINTER(C.c_uint64)]),
+    "yl_sampler_create": (C.c_int, [C.c_uint32, C.c_float, C.c_float, C.c_uint64, C.POINTER(_P)]),
+    "yl_sampler_free": (C.c_int, [_P]),
+    "yl_sampler_sample": (C.c_int, [_P, _P, _P, _P]),
+    "yl_sampler_result": (C.c_int, [_P, C.POINTER(C.c_uint32)]),
+    "yl_session_logits": (C.c_int, [_P, C.POINTER(_P)]),
     "yl_synth_write_gguf": (C.c_int, [C.c_char_p, C.POINTER(SynthC)]),
 }
 for _name, (_res, _args) in _sigs.items():
@@ -414,8 +430,11 @@ class Transformer:
     def bos_token(self) -> int:
         return int(_lib.yl_model_bos_token(self._h))
 
-    def tokenizer(self):
-        return None
+    def tokenizer(self) -> "Tokenizer":
+        """Transformer::tokenizer(): loaded from the model file at the first call."""
+        h = _P()
+        _check(_lib.yl_model_tokenizer(self._h, C.byref(h)))
+        return Tokenizer(h.value, owned=False, keep=self)
 
     def shape(self) -> ShapeC:
         s = ShapeC()
@@ -525,6 +544,116 @@ class Transformer:
         except Exception:
             pass
 
+
+
+class Tokenizer:
+    """tokenizer.rs's Tokenizer (byte-level BPE) through the C-ABI (host only)."""
+
+    def __init__(self, handle: int, owned: bool = True, keep=None):
+        self._h = handle
+        self._owned = owned
+        self._keep = keep  # the model that owns a borrowed tokenizer
+
+    @classmethod
+    def load(cls, model_path: str) -> "Tokenizer":
+        h = _P()
+        _check(_lib.yl_tokenizer_load(model_path.encode(), C.byref(h)))
+        return cls(h.value)
+
+    def info(self) -> dict:
+        v, b, e, t = C.c_uint32(), C.c_uint32(), C.c_uint32(), C.c_int()
+        _check(_lib.yl_tokenizer_info(self._h, C.byref(v), C.byref(b), C.byref(e), C.byref(t)))
+        return {"vocab_size": v.value, "bos": b.value, "eos": e.value, "has_template": bool(t.value)}
+
+    def _ids(self, fn, *args) -> list:
+        n = C.c_uint64()
+        cap = 256
+        while True:
+            buf = np.zeros(cap, np.uint32)
+            rc = fn(self._h, *args, _ptr(buf), cap, C.byref(n))
+            if rc == -6 and n.value > cap:  # YL_ERR_RANGE: retry with the reported size
+                cap = n.value
+                continue
+            _check(rc)
+            return [int(x) for x in buf[: n.value]]
+
+    def encode(self, text: str, bos: bool = False, eos: bool = False) -> list:
+        return self._ids(_lib.yl_tokenizer_encode, text.encode(), 1 if bos else 0, 1 if eos else 0)
+
+    def decode(self, ids: Sequence[int]) -> str:
+        t = np.ascontiguousarray(ids, dtype=np.uint32)
+        n = C.c_uint64()
+        cap = 64 + 16 * len(t)
+        while True:
+            buf = C.create_string_buffer(cap)
+            rc = _lib.yl_tokenizer_decode(self._h, _ptr(t) if len(t) else None, len(t), buf, cap, C.byref(n))
+            if rc == -6 and n.value + 1 > cap:
+                cap = n.value + 1
+                continue
+            _check(rc)
+            return buf.raw[: n.value].decode("utf-8")
+
+    def chat_prompt(self, user: str, system: str = "") -> list:
+        return self._ids(_lib.yl_tokenizer_chat_prompt, system.encode(), user.encode())
+
+    def close(self) -> None:
+        if self._h and self._owned:
+            _lib.yl_tokenizer_free(self._h)
+        self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Sampler:
+    """sampler.rs's Sampler on the device: sample() takes a CUDA logits row."""
+
+    def __init__(self, vocab_size: int, temperature: float, top_p: float, seed: int):
+        h = _P()
+        _check(_lib.yl_sampler_create(vocab_size, temperature, top_p, seed, C.byref(h)))
+        self._h = h.value
+
+    def sample(self, logits, stream=None) -> int:
+        """Sampler::sample(&mut logits): logits (device, float32) is overwritten like the reference's slice."""
+        out = C.c_uint32()
+        _check(_lib.yl_sampler_sample(self._h, _ptr(logits), C.byref(out), _stream(stream)))
+        return out.value
+
+    def close(self) -> None:
+        if self._h:
+            _lib.yl_sampler_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def session_logits(session: InferenceSession) -> int:
+    """Device address of the session's logits row (single-GPU models)."""
+    p = _P()
+    _check(_lib.yl_session_logits(session._h, C.byref(p)))
+    return p.value
+
+
+def infer_config(temperature: float = 0.7, top_p: float = 0.9, seed: int = 42, max_tokens: int = 0) -> None:
+    _check(_lib.yl_infer_config(temperature, top_p, seed, max_tokens))
+
+
+def infer_ffi(prompt: str) -> Optional[str]:
+    """infer_ffi + free_string as a C host binds them (PoC_Bun_load.js:12-38)."""
+    p = _lib.infer_ffi(prompt.encode())
+    if not p:
+        return None
+    try:
+        return C.string_at(p).decode("utf-8")
+    finally:
+        _lib.free_string(p)
 
 def load_transformer(model_path: str, sequential: bool = False, max_ctx_len: int = 0xFFFFFFFF,
                      fmt_override: Optional[WeightFormat] = None) -> Transformer:

@@ -1,9 +1,11 @@
 // extern "C" entry points declared in include/yallma3.h.
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 #include <string>
 #include <vector>
 
+#include "generate.h"
 #include "model.h"
 
 struct yl_model {
@@ -699,6 +701,19 @@ int yl_trace_decode_step(const yl_model* m, yl_session* sp, uint32_t token, uint
 
 static std::mutex g_ffi_mu;
 static yl_model* g_current = nullptr;  // CURRENT_TRANSFORMER (lib.rs:48)
+// infer_ffi's conversation state on g_current, and its sampling settings
+static yl_session* g_ffi_sess = nullptr;
+static yl_sampler* g_ffi_smp = nullptr;
+static float g_ffi_temp = 0.7f, g_ffi_topp = 0.9f;  // Sampler::new(vocab, 0.7, 0.9, 42) (main.rs:135)
+static uint64_t g_ffi_seed = 42;
+static uint32_t g_ffi_max_tokens = 0;  // 0: no limit (the console's default)
+
+static void ffi_drop_state() {
+  if (g_ffi_sess) yl_session_free(g_ffi_sess);
+  if (g_ffi_smp) yl_sampler_free(g_ffi_smp);
+  g_ffi_sess = nullptr;
+  g_ffi_smp = nullptr;
+}
 
 bool load_transformer_ffi(const char* model_path) {
   if (!model_path) return false;
@@ -706,9 +721,94 @@ bool load_transformer_ffi(const char* model_path) {
   // lib.rs:143: load_transformer(path, false, u32::MAX, None)
   if (yl_load_transformer(model_path, 0, 0xFFFFFFFFu, -1, &m) != YL_OK) return false;
   std::lock_guard<std::mutex> lk(g_ffi_mu);
+  ffi_drop_state();
   if (g_current) yl_model_free(g_current);
   g_current = m;
   return true;
 }
+
+int yl_infer_config(float temperature, float top_p, uint64_t seed, uint32_t max_tokens) {
+  if (!(temperature >= 0.0f)) return fail(YL_ERR_ARG, "temperature must be >= 0");
+  std::lock_guard<std::mutex> lk(g_ffi_mu);
+  if (temperature != g_ffi_temp || top_p != g_ffi_topp || seed != g_ffi_seed) {
+    if (g_ffi_smp) yl_sampler_free(g_ffi_smp);
+    g_ffi_smp = nullptr;
+  }
+  g_ffi_temp = temperature;
+  g_ffi_topp = top_p;
+  g_ffi_seed = seed;
+  g_ffi_max_tokens = max_tokens;
+  return YL_OK;
+}
+
+int yl_model_tokenizer(const yl_model* m, const yl_tokenizer** out) {
+  if (!m || !out) return fail(YL_ERR_ARG, "null argument");
+  std::lock_guard<std::mutex> lk(m->m->tok_mu);
+  if (!m->m->tok) {
+    yl_tokenizer* t = nullptr;
+    int rc = yl_tokenizer_load(m->m->path.c_str(), &t);
+    if (rc) return rc;
+    m->m->tok.reset(t);
+  }
+  *out = m->m->tok.get();
+  return YL_OK;
+}
+
+int yl_session_logits(const yl_session* s, float** logits) {
+  if (!s || !logits) return fail(YL_ERR_ARG, "null argument");
+  if (s->s->m->tp_size > 1) return fail(YL_ERR_UNSUPPORTED, "the logits row of a tensor-parallel session is a shard");
+  *logits = s->s->logits;
+  return YL_OK;
+}
+
+// One conversation turn of the console (main.rs:186-214) on the device.
+static int ffi_generate(const char* prompt, std::string* reply) {
+  if (!g_current) return fail(YL_ERR_ARG, "no model loaded (load_transformer_ffi)");
+  if (!prompt || !*prompt) return fail(YL_ERR_ARG, "empty prompt");
+  const Model* mm = g_current->m;
+  if (mm->tp_size > 1) return fail(YL_ERR_UNSUPPORTED, "infer_ffi runs single-GPU models");
+  const yl_tokenizer* tk = nullptr;
+  int rc = yl_model_tokenizer(g_current, &tk);
+  if (rc) return rc;
+  std::vector<uint32_t> ids;
+  if ((rc = tok_chat_prompt(tk->t, "", prompt, &ids))) return rc;
+  const uint32_t ctx = mm->shape.ctx_len;
+  if (ids.empty() || ids.size() > ctx) return fail(YL_ERR_RANGE, "prompt longer than the context");
+  YL_CUDA_TRY(cudaSetDevice(mm->device));
+  if (!g_ffi_sess && (rc = yl_create_session(g_current, &g_ffi_sess))) return rc;
+  if (!g_ffi_smp && (rc = yl_sampler_create(mm->shape.vocab_size, g_ffi_temp, g_ffi_topp, g_ffi_seed, &g_ffi_smp)))
+    return rc;
+  if ((rc = yl_session_reset(g_ffi_sess))) return rc;
+  Session* s = g_ffi_sess->s;
+  // prefill, then sample from the last token's logits (they stay on the device)
+  if ((rc = yl_forward_x(g_current, g_ffi_sess, ids.data(), ids.size(), 0, nullptr, nullptr))) return rc;
+  uint32_t pos = (uint32_t)ids.size(), next = 0, gen = 0;
+  if ((rc = sampler_run(g_ffi_smp, s->logits, s->stream)) || (rc = sampler_wait(g_ffi_smp, &next))) return rc;
+  const uint32_t max_gen = g_ffi_max_tokens ? g_ffi_max_tokens : 0xFFFFFFFFu;
+  while (next != mm->eos && pos < ctx && gen < max_gen) {
+    *reply += tok_decode(tk->t, &next, 1);
+    if ((rc = yl_forward_x(g_current, g_ffi_sess, &next, 1, pos, nullptr, nullptr))) return rc;
+    ++pos;
+    ++gen;
+    if ((rc = sampler_run(g_ffi_smp, s->logits, s->stream)) || (rc = sampler_wait(g_ffi_smp, &next))) return rc;
+  }
+  return YL_OK;
+}
+
+const char* infer_ffi(const char* prompt) {
+  std::lock_guard<std::mutex> lk(g_ffi_mu);
+  std::string reply;
+  if (ffi_generate(prompt, &reply) != YL_OK) return nullptr;
+  char* out = (char*)malloc(reply.size() + 1);
+  if (!out) {
+    fail(YL_ERR_OOM, "reply buffer");
+    return nullptr;
+  }
+  memcpy(out, reply.data(), reply.size());
+  out[reply.size()] = '\0';
+  return out;
+}
+
+void free_string(const char* s) { free((void*)s); }
 
 }  // extern "C"

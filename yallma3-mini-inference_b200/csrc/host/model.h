@@ -8,6 +8,7 @@
 
 #include "../kernels/kernels.h"
 #include "common.h"
+#include "tokenizer.h"
 
 namespace yl {
 
@@ -51,6 +52,9 @@ struct Model {
   // query heads, KV heads, ffn rows and vocabulary rows (all of them at 1)
   int tp_rank = 0, tp_size = 1;
   uint32_t l_heads = 0, l_kv = 0, l_ffn = 0, l_vocab = 0, vocab0 = 0;
+  // Transformer::tokenizer(): loaded from `path` at the first request
+  mutable std::mutex tok_mu;
+  mutable std::unique_ptr<yl_tokenizer> tok;
   ~Model();
 };
 

@@ -348,5 +348,34 @@ cudaError_t argmax(const float* logits, uint32_t n, uint32_t* out, StepState* st
 // Starts a device-resident decode run: state = {pos, token, next 0, steps 0}
 // (one thread; the values are launch arguments, so nothing is staged on the host).
 cudaError_t set_step_state(StepState* state, int32_t pos, int32_t token, const LaunchCfg& lc);
+
+// ---- device sampler (sampler.rs:117-180) ----------------------------------
+struct SampleArgs {
+  float* logits = nullptr;  // [V] on the device; overwritten (x/T, then probabilities) like Sampler::sample
+  uint32_t V = 0, ntiles = 0;  // ntiles = sample_tiles(V)
+  float temperature = 0.f, top_p = 0.f;
+  float cutoff = 0.f;  // (1 - top_p) / (V - 1), computed in f32 as the reference does
+  float rand = 0.f;    // random_f32(seed); the reference's generator never advances
+  int topp = 0;        // 1: sample_topp, 0: sample_mult
+  float* tile_val = nullptr;     // [ntiles]
+  uint32_t* tile_cnt = nullptr;  // [ntiles]
+  float* misc = nullptr;         // [0] softmax sum, [1] kept count (bits)
+  float* prefix = nullptr;       // [V] cumulative sums of the sorted entries
+  uint32_t* out = nullptr;       // sampled id (device)
+  int* err = nullptr;
+  // the persistent probability_idx array (prob, index) of the sampler, two
+  // buffers for the radix sort; zero at creation
+  float* sbuf_prob[2] = {nullptr, nullptr};
+  uint32_t* sbuf_idx[2] = {nullptr, nullptr};
+  float* sprob = nullptr;        // the current buffer (set by sample())
+  uint32_t* sidx = nullptr;
+  void* sort_temp = nullptr;
+  size_t sort_temp_bytes = 0;
+};
+uint32_t sample_tiles(uint32_t V);
+size_t sample_sort_temp_bytes(uint32_t V);
+// Enqueues one Sampler::sample; *cur selects the current persistent buffer
+// and is updated by the sort.
+cudaError_t sample(SampleArgs& a, int* cur, const LaunchCfg& lc);
 }  // namespace k
 }  // namespace yl
