@@ -206,9 +206,6 @@ int yl_batch_forward(yl_batch* b, yl_session* const* sessions, uint32_t n, const
  *  "gemm_tc"     1 = Q8_0 batches on the tcgen05 / tensor-memory kernel
  *                (bit-identical, not faster; default 0, env YL_GEMM_TC)
  *  "gemm_tc_min" token count from which gemm_tc applies (default 96)
- *  "mv2"         single-token Q8_0 projections on the per-lane-chain matvec
- *                (matvec2.cu; default 0, env YL_MV2; bit-identical to the
- *                fold-warp matvec)
  * YL_ERR_ARG for an unknown key. */
 int yl_config_set(const char* key, int64_t value);
 

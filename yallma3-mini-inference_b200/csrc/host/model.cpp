@@ -139,10 +139,6 @@ Tunables& tunables_mut() {
     if (const char* e = getenv("YL_GEMM_TC")) x.gemm_tc = atoi(e) != 0;
     if (const char* e = getenv("YL_GEMM_TC_MIN")) x.gemm_tc_min = (uint32_t)std::max(1, atoi(e));
     if (const char* e = getenv("YL_PF_MB")) x.pf_bytes = (uint64_t)std::max(0, atoi(e)) << 20;
-    if (const char* e = getenv("YL_MV2")) x.mv2 = atoi(e) != 0;
-    if (const char* e = getenv("YL_MV2_CPS")) x.mv2_cps = (uint32_t)std::max(1, atoi(e));
-    if (const char* e = getenv("YL_MV2_SMEM")) x.mv2_smem = (uint32_t)std::max(16384, atoi(e));
-    if (const char* e = getenv("YL_MV2_KC")) x.mv2_kc = (uint32_t)std::max(0, atoi(e));
     return x;
   }();
   return t;
@@ -156,7 +152,6 @@ int set_tunable(const std::string& key, int64_t value) {
   if (key == "gemm_tc") t.gemm_tc = value != 0;
   else if (key == "gemm_tc_min") t.gemm_tc_min = (uint32_t)std::max<int64_t>(1, value);
   else if (key == "gemm") t.gemm = value != 0;
-  else if (key == "mv2") t.mv2 = value != 0;
   else return fail(YL_ERR_ARG, "unknown option " + key);
   return YL_OK;
 }
@@ -657,18 +652,7 @@ int run_matvec_ex(const DevWeight& w, bool f32act, const int8_t* xq, const float
       a.tp_nsites = ex.tp_nsites;
       a.tp_xout = ex.tp_xout;
     }
-    cudaError_t e;
-    if (tu.mv2 && k::matvec2_supported(a, fmt, w.sf16, epi)) {
-      k::LaunchCfg l2 = lc;
-      l2.grid = (uint32_t)num_sms;
-      l2.smem_budget = tu.mv2_smem;
-      e = k::matvec2(a, w.sf16, epi, tu.mv2_cps, tu.mv2_kc, l2);
-      // a plan it cannot make (tensor map refused, shared memory) enqueues
-      // nothing: the fold-warp matvec takes the pass
-      if (e == cudaErrorInvalidValue || e == cudaErrorInvalidConfiguration) e = k::matvec(a, fmt, w.sf16, epi, lc);
-    } else {
-      e = k::matvec(a, fmt, w.sf16, epi, lc);
-    }
+    cudaError_t e = k::matvec(a, fmt, w.sf16, epi, lc);
     if (e != cudaSuccess) return fail(YL_ERR_CUDA, std::string("matvec launch: ") + cudaGetErrorString(e));
     if (launches) ++*launches;
   }

@@ -167,14 +167,6 @@ struct Tunables {
   // decode: L2 prefetch of the next matrix's first bytes per launch (YL_PF_MB).
   // Off: measured slower at every size tried (16, 32, 48 MB).
   uint64_t pf_bytes = 0;
-  // Single-token Q8_0 projections on the per-lane-chain matvec (matvec2.cu,
-  // YL_MV2=1 / yl_config_set("mv2", 1)); CTAs per SM, the shared-memory
-  // budget of each and the K bytes per stage (YL_MV2_CPS, YL_MV2_SMEM,
-  // YL_MV2_KC; 0 lets the launcher pick).
-  bool mv2 = false;
-  uint32_t mv2_cps = 2;
-  uint32_t mv2_smem = 100 * 1024;
-  uint32_t mv2_kc = 0;
 };
 // Batched decode of independent sessions (one token each per step): the
 // projections run once over the stacked rows, the attention is one launch

@@ -349,31 +349,6 @@ cudaError_t argmax(const float* logits, uint32_t n, uint32_t* out, StepState* st
 // (one thread; the values are launch arguments, so nothing is staged on the host).
 cudaError_t set_step_state(StepState* state, int32_t pos, int32_t token, const LaunchCfg& lc);
 
-
-// ---- decode matvec, one token, Q8_0 weights (matvec2.cu) --------------------
-struct Mv2Args {
-  uint32_t rows = 0, K = 0;
-  uint32_t kc = 0;    // K bytes per stage (set by the launcher)
-  int stages = 0;     // ring depth (set by the launcher)
-  const int8_t* xq = nullptr;   // PRO_LOAD: int8 activations [K], scales [K/32]
-  const float* xs = nullptr;
-  const float* xres = nullptr;  // PRO_NORM: residual row [K] and norm weight
-  const float* norm_w = nullptr;
-  float eps = 0.f;
-  float* out = nullptr;
-  int8_t* hq = nullptr;         // EPI_SWIGLU_Q8
-  float* hs = nullptr;
-  unsigned int* hcount = nullptr;
-  int* err = nullptr;
-};
-// Whether matvec2 takes this pass (one token, Q8_0, store / add / SwiGLU+Q8
-// epilogues, load / RMSNorm prologues, no tensor parallelism).
-bool matvec2_supported(const MvArgs& a, int fmt, bool sf16, int epi);
-// lc.grid = SM count; ctas_per_sm CTAs per SM within lc.smem_budget each;
-// kc_pref: K bytes per stage (1024, 512 or 256; 0 picks).
-cudaError_t matvec2(const MvArgs& a, bool sf16, int epi, uint32_t ctas_per_sm, uint32_t kc_pref,
-                    const LaunchCfg& lc);
-
 // ---- device sampler (sampler.rs:117-180) ----------------------------------
 struct SampleArgs {
   float* logits = nullptr;  // [V] on the device; overwritten (x/T, then probabilities) like Sampler::sample
