@@ -83,10 +83,14 @@ __global__ void __launch_bounds__(SMP_THREADS) smp_exp(SampleArgs a) {
   }
 }
 
-// One thread walks the chain s = ((init + v0) + v1) + ... over v[0, n), the
-// loads of the next 32 values in flight while the current 32 are added.
-// Writes every partial sum to pre (when given); stops after the first index
-// whose sum exceeds `stop_above` (when finite) and returns it in *stopped.
+// One thread walks the chain s = ((0 + v0) + v1) + ... over v[0, n): blocks
+// of 32 values, the next block's loads in flight while the current one is
+// added, no branch between the dependent additions. With PRE every partial
+// sum is stored to pre[]. The values are >= 0, so the partial sums never
+// decrease: the first index whose sum exceeds `stop_above` lies in the first
+// block whose last sum does, which is then walked again (same additions from
+// the same start) to find it; *stopped gets that index, or 0xFFFFFFFF.
+template <bool PRE>
 __device__ float smp_chain(const float* v, uint32_t n, float* pre, float stop_above, uint32_t* stopped) {
   float s = 0.0f;
   float cur[32], nxt[32];
@@ -95,14 +99,28 @@ __device__ float smp_chain(const float* v, uint32_t n, float* pre, float stop_ab
   for (uint32_t i0 = 0; i0 < n; i0 += 32) {
 #pragma unroll
     for (int u = 0; u < 32; ++u) nxt[u] = i0 + 32 + u < n ? __ldcg(v + i0 + 32 + u) : 0.0f;
+    const float start = s;
+    const uint32_t m = n - i0 < 32u ? n - i0 : 32u;
+    if (m == 32u) {
 #pragma unroll
-    for (int u = 0; u < 32; ++u) {
-      if (i0 + u >= n) break;
-      s = __fadd_rn(s, cur[u]);
-      if (pre) pre[i0 + u] = s;
-      if (s > stop_above) {
-        *stopped = i0 + u;
-        return s;
+      for (int u = 0; u < 32; ++u) {
+        s = __fadd_rn(s, cur[u]);
+        if (PRE) pre[i0 + u] = s;
+      }
+    } else {
+      for (uint32_t u = 0; u < m; ++u) {
+        s = __fadd_rn(s, cur[u]);
+        if (PRE) pre[i0 + u] = s;
+      }
+    }
+    if (s > stop_above) {
+      float t = start;
+      for (uint32_t u = 0; u < m; ++u) {
+        t = __fadd_rn(t, cur[u]);
+        if (t > stop_above) {
+          *stopped = i0 + u;
+          return t;
+        }
       }
     }
 #pragma unroll
@@ -116,7 +134,7 @@ __device__ float smp_chain(const float* v, uint32_t n, float* pre, float stop_ab
 __global__ void smp_sum(SampleArgs a) {
   if (threadIdx.x != 0) return;
   uint32_t dummy;
-  a.misc[0] = smp_chain(a.logits, a.V, nullptr, INFINITY, &dummy);
+  a.misc[0] = smp_chain<false>(a.logits, a.V, nullptr, INFINITY, &dummy);
 }
 
 // p = e / sum; top-p: per-tile count of entries with p >= cutoff
@@ -205,7 +223,7 @@ __global__ void smp_topp_pick(SampleArgs a) {
   }
   if (lane == 0) {
     uint32_t stop;
-    const float cum = smp_chain(a.sprob, n0, a.prefix, a.top_p, &stop);
+    const float cum = smp_chain<true>(a.sprob, n0, a.prefix, a.top_p, &stop);
     s_last = stop == 0xFFFFFFFFu ? n0 - 1 : stop;
     s_r = __fmul_rn(a.rand, cum);
   }
@@ -229,7 +247,7 @@ __global__ void smp_mult_pick(SampleArgs a) {
   if (threadIdx.x != 0) return;
   uint32_t stop;
   // rand < cdf  <=>  cdf > rand
-  smp_chain(a.logits, a.V, nullptr, a.rand, &stop);
+  smp_chain<false>(a.logits, a.V, nullptr, a.rand, &stop);
   *a.out = stop == 0xFFFFFFFFu ? a.V - 1 : stop;
 }
 
