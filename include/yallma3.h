@@ -120,7 +120,7 @@ int yl_quantize(int fmt, yl_qtensor* dst, const float* x, uint64_t n, uint32_t g
  * exactly (columns < 4*floor(o/4) add into out, the rest overwrite,
  * weight_type.rs:190-201 and :207-224, inside matmul_q8_slices :122-226);
  * accumulate = 0 overwrites every column. Batches
- * of 16 or more Q8_0 / Q4_0 rows run on the int8 tensor-core GEMM, whose
+ * of 5 or more Q8_0 / Q4_0 rows run on the int8 tensor-core GEMM, whose
  * overwrite results equal the reference's bit for bit; smaller batches run on
  * the matvec (within 1e-5 of the sum of |terms|). */
 int yl_matmul(float* out, const yl_qtensor* x, const yl_qtensor* w, uint64_t n, uint64_t o, uint64_t gs,
@@ -202,7 +202,7 @@ int yl_batch_forward(yl_batch* b, yl_session* const* sessions, uint32_t n, const
 
 /* Process-wide options of the device path (no reference counterpart), read
  * by launches made after the call:
- *  "gemm"        1 = batches of 16+ tokens on the int8 tensor-core GEMM (default)
+ *  "gemm"        1 = batches of 5+ tokens on the int8 tensor-core GEMM (default)
  *  "gemm_tc"     1 = Q8_0 batches on the tcgen05 / tensor-memory kernel
  *                (bit-identical, not faster; default 0, env YL_GEMM_TC)
  *  "gemm_tc_min" token count from which gemm_tc applies (default 96)

@@ -156,7 +156,9 @@ struct Tunables {
   uint32_t grid_mult = 2;    // matvec CTAs per SM
   bool limbs = true;         // Q8_0 lm_head on three-limb int8 activations
   bool gemm = true;          // multi-token passes on the int8 tensor-core GEMM
-  uint32_t gemm_min = 16;    // from this many tokens (below, the matvec re-reading weights per 8 is faster)
+  // from this many tokens: measured on B200, 8-token passes run 2.1x faster on
+  // the GEMM than on the 8-token matvec, 4-token passes 9 % slower
+  uint32_t gemm_min = 5;
   // Q8_0 GEMMs on the tcgen05 tensor-memory kernel (YL_GEMM_TC=1), from
   // gemm_tc_min tokens (its tiles are 128 tokens wide). Off by default: it is
   // bit-identical to the mma.sync kernel but measured no faster (both are

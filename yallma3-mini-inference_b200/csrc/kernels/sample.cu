@@ -83,58 +83,86 @@ __global__ void __launch_bounds__(SMP_THREADS) smp_exp(SampleArgs a) {
   }
 }
 
-// One thread walks the chain s = ((0 + v0) + v1) + ... over v[0, n): blocks
-// of 32 values, the next block's loads in flight while the current one is
-// added, no branch between the dependent additions. With PRE every partial
-// sum is stored to pre[]. The values are >= 0, so the partial sums never
-// decrease: the first index whose sum exceeds `stop_above` lies in the first
-// block whose last sum does, which is then walked again (same additions from
-// the same start) to find it; *stopped gets that index, or 0xFFFFFFFF.
+// The chain s = ((0 + v0) + v1) + ... over v[0, n), walked by thread 0 of a
+// block of SMP_THREADS threads: the block stages the values through shared
+// memory in tiles of SMP_CT (double-buffered, every thread loading the next
+// tile while thread 0 adds the current one), and thread 0 keeps the next 32
+// values in registers ahead of its dependent additions, so the chain runs at
+// the latency of the additions rather than of global loads. With PRE every
+// partial sum is stored to pre[]. The values are >= 0, so the partial sums
+// never decrease: the first index whose sum exceeds `stop_above` lies in the
+// first group of 32 whose last sum does, which is walked again (the same
+// additions from the same start) to find it. Every thread returns the final
+// (or stopping) sum; *stopped (thread 0's) is that index, or 0xFFFFFFFF.
+constexpr uint32_t SMP_CT = 4096;
+
 template <bool PRE>
-__device__ float smp_chain(const float* v, uint32_t n, float* pre, float stop_above, uint32_t* stopped) {
+__device__ float smp_chain_block(const float* v, uint32_t n, float* pre, float stop_above, uint32_t* stopped) {
+  __shared__ __align__(16) float tile[2][SMP_CT];
+  __shared__ uint32_t s_stop;
+  __shared__ float s_sum;
+  const uint32_t tid = threadIdx.x, nt = (n + SMP_CT - 1) / SMP_CT;
+  for (uint32_t i = tid; i < SMP_CT && i < n; i += SMP_THREADS) tile[0][i] = __ldcg(v + i);
+  if (tid == 0) s_stop = 0xFFFFFFFFu;
+  __syncthreads();
   float s = 0.0f;
-  float cur[32], nxt[32];
+  for (uint32_t t = 0; t < nt; ++t) {
+    const uint32_t base = t * SMP_CT;
+    if (t + 1 < nt)
+      for (uint32_t i = tid; i < SMP_CT && base + SMP_CT + i < n; i += SMP_THREADS)
+        tile[(t + 1) & 1][i] = __ldcg(v + base + SMP_CT + i);
+    if (tid == 0) {
+      const float* tv = tile[t & 1];
+      const uint32_t m = n - base < SMP_CT ? n - base : SMP_CT;
+      float cur[32], nxt[32];
 #pragma unroll
-  for (int u = 0; u < 32; ++u) cur[u] = u < (int)n ? __ldcg(v + u) : 0.0f;
-  for (uint32_t i0 = 0; i0 < n; i0 += 32) {
+      for (int u = 0; u < 32; ++u) cur[u] = (uint32_t)u < m ? tv[u] : 0.0f;
+      for (uint32_t i0 = 0; i0 < m; i0 += 32) {
 #pragma unroll
-    for (int u = 0; u < 32; ++u) nxt[u] = i0 + 32 + u < n ? __ldcg(v + i0 + 32 + u) : 0.0f;
-    const float start = s;
-    const uint32_t m = n - i0 < 32u ? n - i0 : 32u;
-    if (m == 32u) {
+        for (int u = 0; u < 32; ++u) nxt[u] = i0 + 32 + u < m ? tv[i0 + 32 + u] : 0.0f;
+        const float start = s;
+        const uint32_t k = m - i0 < 32u ? m - i0 : 32u;
+        if (k == 32u) {
 #pragma unroll
-      for (int u = 0; u < 32; ++u) {
-        s = __fadd_rn(s, cur[u]);
-        if (PRE) pre[i0 + u] = s;
-      }
-    } else {
-      for (uint32_t u = 0; u < m; ++u) {
-        s = __fadd_rn(s, cur[u]);
-        if (PRE) pre[i0 + u] = s;
-      }
-    }
-    if (s > stop_above) {
-      float t = start;
-      for (uint32_t u = 0; u < m; ++u) {
-        t = __fadd_rn(t, cur[u]);
-        if (t > stop_above) {
-          *stopped = i0 + u;
-          return t;
+          for (int u = 0; u < 32; ++u) {
+            s = __fadd_rn(s, cur[u]);
+            if (PRE) pre[base + i0 + u] = s;
+          }
+        } else {  // the tail (from shared memory: no dynamic register index)
+          for (uint32_t u = 0; u < k; ++u) {
+            s = __fadd_rn(s, tv[i0 + u]);
+            if (PRE) pre[base + i0 + u] = s;
+          }
         }
-      }
-    }
+        if (s > stop_above) {
+          float r = start;
+          for (uint32_t u = 0; u < k; ++u) {
+            r = __fadd_rn(r, tv[i0 + u]);
+            if (r > stop_above) {
+              s_stop = base + i0 + u;
+              break;
+            }
+          }
+          s = r;
+          break;
+        }
 #pragma unroll
-    for (int u = 0; u < 32; ++u) cur[u] = nxt[u];
+        for (int u = 0; u < 32; ++u) cur[u] = nxt[u];
+      }
+      s_sum = s;
+    }
+    __syncthreads();  // the next tile is staged; thread 0 is done with this one
+    if (s_stop != 0xFFFFFFFFu) break;
   }
-  *stopped = 0xFFFFFFFFu;
-  return s;
+  *stopped = s_stop;
+  return s_sum;
 }
 
 // the softmax denominator, summed in index order (the reference's f32 Sum)
-__global__ void smp_sum(SampleArgs a) {
-  if (threadIdx.x != 0) return;
+__global__ void __launch_bounds__(SMP_THREADS) smp_sum(SampleArgs a) {
   uint32_t dummy;
-  a.misc[0] = smp_chain<false>(a.logits, a.V, nullptr, INFINITY, &dummy);
+  const float sum = smp_chain_block<false>(a.logits, a.V, nullptr, INFINITY, &dummy);
+  if (threadIdx.x == 0) a.misc[0] = sum;
 }
 
 // p = e / sum; top-p: per-tile count of entries with p >= cutoff
@@ -206,33 +234,28 @@ __global__ void __launch_bounds__(SMP_THREADS) smp_compact(SampleArgs a) {
   if (blockIdx.x == gridDim.x - 1 && threadIdx.x == 0) a.misc[1] = __uint_as_float(tile_off + run);
 }
 
-// The cumulative chain over the sorted entries (lane 0), then the draw,
-// located by the warp in the same prefix sums (the reference's cdf loop over
-// 0..=last adds the same values in the same order from 0).
-__global__ void smp_topp_pick(SampleArgs a) {
-  __shared__ uint32_t s_last;
-  __shared__ float s_r;
-  const int lane = threadIdx.x;
+// The cumulative chain over the sorted entries, then the draw, located by
+// warp 0 in the same prefix sums (the reference's cdf loop over 0..=last adds
+// the same values in the same order from 0).
+__global__ void __launch_bounds__(SMP_THREADS) smp_topp_pick(SampleArgs a) {
+  const int lane = threadIdx.x & 31;
   const uint32_t n0 = __float_as_uint(a.misc[1]);
   if (n0 == 0) {  // the reference underflows n0 - 1 (a panic)
-    if (lane == 0) {
+    if (threadIdx.x == 0) {
       if (a.err) atomicExch(a.err, dev::ERR_BAD_ARG);
       *a.out = 0u;
     }
     return;
   }
-  if (lane == 0) {
-    uint32_t stop;
-    const float cum = smp_chain<true>(a.sprob, n0, a.prefix, a.top_p, &stop);
-    s_last = stop == 0xFFFFFFFFu ? n0 - 1 : stop;
-    s_r = __fmul_rn(a.rand, cum);
-  }
-  __syncwarp();
-  const uint32_t last = s_last;
-  const float r = s_r;
+  uint32_t stop;
+  const float cum = smp_chain_block<true>(a.sprob, n0, a.prefix, a.top_p, &stop);
+  if (threadIdx.x >= 32) return;
+  __threadfence_block();  // thread 0's prefix stores, before warp 0 reads them
+  const uint32_t last = stop == 0xFFFFFFFFu ? n0 - 1 : stop;
+  const float r = __fmul_rn(a.rand, cum);
   for (uint32_t i0 = 0; i0 <= last; i0 += 32) {
     const uint32_t i = i0 + lane;
-    const bool hit = i <= last && r < a.prefix[i];
+    const bool hit = i <= last && r < __ldcg(a.prefix + i);
     const uint32_t bal = __ballot_sync(0xFFFFFFFFu, hit);
     if (bal) {
       if (lane == 0) *a.out = a.sidx[i0 + __ffs(bal) - 1];
@@ -243,12 +266,11 @@ __global__ void smp_topp_pick(SampleArgs a) {
 }
 
 // sample_mult: first index whose cdf (index order) exceeds rand
-__global__ void smp_mult_pick(SampleArgs a) {
-  if (threadIdx.x != 0) return;
+__global__ void __launch_bounds__(SMP_THREADS) smp_mult_pick(SampleArgs a) {
   uint32_t stop;
   // rand < cdf  <=>  cdf > rand
-  smp_chain<false>(a.logits, a.V, nullptr, a.rand, &stop);
-  *a.out = stop == 0xFFFFFFFFu ? a.V - 1 : stop;
+  smp_chain_block<false>(a.logits, a.V, nullptr, a.rand, &stop);
+  if (threadIdx.x == 0) *a.out = stop == 0xFFFFFFFFu ? a.V - 1 : stop;
 }
 
 // sample_argmax: lowest index among the maxima; a NaN first value is never
@@ -304,10 +326,10 @@ cudaError_t sample(SampleArgs& a, int* cur, const LaunchCfg& lc) {
   }
   smp_scale_max<<<a.ntiles, SMP_THREADS, 0, st>>>(a);
   smp_exp<<<a.ntiles, SMP_THREADS, 0, st>>>(a);
-  smp_sum<<<1, 32, 0, st>>>(a);
+  smp_sum<<<1, SMP_THREADS, 0, st>>>(a);
   smp_norm<<<a.ntiles, SMP_THREADS, 0, st>>>(a);
   if (!a.topp) {
-    smp_mult_pick<<<1, 32, 0, st>>>(a);
+    smp_mult_pick<<<1, SMP_THREADS, 0, st>>>(a);
     return cudaGetLastError();
   }
   SampleArgs b = a;
@@ -326,7 +348,7 @@ cudaError_t sample(SampleArgs& a, int* cur, const LaunchCfg& lc) {
   if (keys.Current() != a.sbuf_prob[*cur] || vals.Current() != a.sbuf_idx[*cur]) return cudaErrorUnknown;
   b.sprob = a.sbuf_prob[*cur];
   b.sidx = a.sbuf_idx[*cur];
-  smp_topp_pick<<<1, 32, 0, st>>>(b);
+  smp_topp_pick<<<1, SMP_THREADS, 0, st>>>(b);
   return cudaGetLastError();
 }
 
