@@ -211,7 +211,7 @@ def test_f32_weight_scales(yl, orc, torch_cuda):
     assert np.all(np.abs(got - ref) <= 1e-5 * term_bound(xq, xs, wq, ws, 2, n, o) + 1e-30)
 
 
-GEMM_CASES = [(260, 576, 17), (1000, 2048, 32), (384, 2080, 20), (260, 576, 33), (1000, 2048, 64), (128, 32, 65),
+GEMM_CASES = [(260, 576, 5), (1000, 2048, 8), (384, 2080, 12), (128, 32, 16), (260, 576, 17), (1000, 2048, 32), (384, 2080, 20), (260, 576, 33), (1000, 2048, 64), (128, 32, 65),
               (384, 2080, 130), (2048, 2048, 256),
               # from 96 tokens Q8_0 runs on the tcgen05 kernel (128 x 128 tiles, 4 blocks per stage):
               # row / token tails, a single block, a partial last stage (65 blocks), several token tiles

@@ -137,8 +137,12 @@ template <int FMT, bool SF16, int EPI, int BN>
 __global__ void __launch_bounds__(GB_THREADS, 2) gemm_q_kernel(GemmArgs a) {
   using T = GTile<FMT, BN>;
   constexpr bool PERM = EPI == EPI_SWIGLU_Q8;
-  // BN = 64: warps 4 (rows) x 2 (tokens), 32 x 32 each; BN = 32: 8 x 1, 16 x 32
-  constexpr int WN = BN / 32, MT = BN / 32, RW = 16 * MT;
+  // BN = 64: warps 4 (rows) x 2 (tokens), 32 x 32 each; BN = 32: 8 x 1,
+  // 16 x 32; BN = 16 / 8: 8 x 1, 16 x 16 / 16 x 8 (fewer padded tokens folded
+  // for small batches). NTW: 8-token n-tiles per warp.
+  constexpr int WN = BN >= 64 ? 2 : 1, MT = BN >= 64 ? 2 : 1, RW = 16 * MT;
+  constexpr int NTW = BN >= 32 ? 4 : BN / 8;
+  static_assert(BN == 8 || BN == 16 || BN == 32 || BN == 64, "token tile");
   extern __shared__ __align__(128) uint8_t smem[];
   const uint32_t n0 = blockIdx.x * BN, m0 = blockIdx.y * GB_M;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -154,11 +158,11 @@ __global__ void __launch_bounds__(GB_THREADS, 2) gemm_q_kernel(GemmArgs a) {
     cp_async_commit();
   }
 
-  float acc[MT][4][4];
+  float acc[MT][NTW][4];
 #pragma unroll
   for (int i = 0; i < MT; ++i)
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
+    for (int j = 0; j < NTW; ++j)
 #pragma unroll
       for (int e = 0; e < 4; ++e) acc[i][j][e] = 0.0f;
 
@@ -179,9 +183,9 @@ __global__ void __launch_bounds__(GB_THREADS, 2) gemm_q_kernel(GemmArgs a) {
 #pragma unroll
     for (uint32_t b = 0; b < (uint32_t)GB_KB; ++b) {
       if (b >= nb) break;
-      uint32_t af[MT][4], bf[4][2];
+      uint32_t af[MT][4], bf[NTW][2];
       float w0[MT], w1[MT];
-      float2 xv[4];
+      float2 xv[NTW];
 #pragma unroll
       for (int mt = 0; mt < MT; ++mt) {
         const int rr = wm * RW + mt * 16 + gid;
@@ -204,23 +208,28 @@ __global__ void __launch_bounds__(GB_THREADS, 2) gemm_q_kernel(GemmArgs a) {
           w1[mt] = reinterpret_cast<const float*>(wsc)[(rr + 8) * GB_KB + b];
         }
       }
+      if (NTW == 1) {  // one n-tile: lanes 0..15 address its two 8x8 matrices
+        const int lt = lane & 7;
+        ldsm_x2(bf[0][0], bf[0][1], xt + lt * T::XROW + b * 32 + ((lane >> 3) & 1) * 16);
+      } else {
 #pragma unroll
-      for (int np = 0; np < 2; ++np) {  // n-tiles 2np and 2np + 1
-        const int lt = wn * 32 + np * 16 + (lane & 7) + ((lane >> 4) & 1) * 8;
-        uint32_t r[4];
-        ldsm_x4(r, xt + lt * T::XROW + b * 32 + ((lane >> 3) & 1) * 16);
-        bf[2 * np][0] = r[0];
-        bf[2 * np][1] = r[1];
-        bf[2 * np + 1][0] = r[2];
-        bf[2 * np + 1][1] = r[3];
+        for (int np = 0; np < NTW / 2; ++np) {  // n-tiles 2np and 2np + 1
+          const int lt = wn * 32 + np * 16 + (lane & 7) + ((lane >> 4) & 1) * 8;
+          uint32_t r[4];
+          ldsm_x4(r, xt + lt * T::XROW + b * 32 + ((lane >> 3) & 1) * 16);
+          bf[2 * np][0] = r[0];
+          bf[2 * np][1] = r[1];
+          bf[(2 * np + 1) % NTW][0] = r[2];
+          bf[(2 * np + 1) % NTW][1] = r[3];
+        }
       }
 #pragma unroll
-      for (int nt = 0; nt < 4; ++nt)
+      for (int nt = 0; nt < NTW; ++nt)
         xv[nt] = *reinterpret_cast<const float2*>(xsc + b * BN + wn * 32 + nt * 8 + tig * 2);
 #pragma unroll
       for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-        for (int nt = 0; nt < 4; ++nt) {
+        for (int nt = 0; nt < NTW; ++nt) {
           int d[4];
           mma_s8(d, af[mt], bf[nt]);
           // ((f32)isum * w_scale) * x_scale, added in group order
@@ -239,7 +248,7 @@ __global__ void __launch_bounds__(GB_THREADS, 2) gemm_q_kernel(GemmArgs a) {
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-      for (int nt = 0; nt < 4; ++nt) {
+      for (int nt = 0; nt < NTW; ++nt) {
         const int jl = (wm * RW + mt * 16) / 2 + gid;  // pair of this thread's rows gid (gate) and gid + 8 (up)
         const int tl = wn * 32 + nt * 8 + tig * 2;
         hb[tl * (GB_M / 2) + jl] = silu_mul(acc[mt][nt][0], acc[mt][nt][2]);
@@ -265,7 +274,7 @@ __global__ void __launch_bounds__(GB_THREADS, 2) gemm_q_kernel(GemmArgs a) {
 #pragma unroll
   for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-    for (int nt = 0; nt < 4; ++nt)
+    for (int nt = 0; nt < NTW; ++nt)
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const uint32_t r = m0 + wm * RW + mt * 16 + gid + (e >> 1) * 8;
@@ -289,9 +298,12 @@ cudaError_t gemm_launch_bn(const GemmArgs& a, const LaunchCfg& lc) {
   return launch_kernel(gemm_q_kernel<FMT, SF16, EPI, BN>, grid, dim3(GB_THREADS), (uint32_t)T::SMEM, lc, a);
 }
 
-// Up to 32 tokens: 32-token tiles (half the padded work of a 64-token tile).
+// Token tiles of 8, 16, 32 or 64: a small batch folds no more padded tokens
+// than it must (the fold, not the tensor core, bounds this kernel).
 template <int FMT, bool SF16, int EPI>
 cudaError_t gemm_launch(const GemmArgs& a, const LaunchCfg& lc) {
+  if (a.ntok <= 8) return gemm_launch_bn<FMT, SF16, EPI, 8>(a, lc);
+  if (a.ntok <= 16) return gemm_launch_bn<FMT, SF16, EPI, 16>(a, lc);
   return a.ntok <= 32 ? gemm_launch_bn<FMT, SF16, EPI, 32>(a, lc) : gemm_launch_bn<FMT, SF16, EPI, 64>(a, lc);
 }
 
