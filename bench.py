@@ -47,7 +47,7 @@ sys.path.insert(0, str(ROOT))
 PKG = "yallma3-mini-inference_b200"
 PROMPT_LEN = 512
 CONFIG = "c4"
-TRAFFIC_GATEUP_BYTES = 129.02e6
+TRAFFIC_GATEUP_BYTES = 128.22e6
 
 
 def measured_peaks() -> dict:
