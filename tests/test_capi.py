@@ -101,3 +101,24 @@ def test_synth_weight_statistics(yl, orc, model_factory):
     m = orc.Model(model_factory("tiny128"), 512)
     e = np.concatenate([m.get_embeddings(t) for t in range(64)])
     assert abs(float(e.std()) - 0.02) < 0.002 and abs(float(e.mean())) < 0.002
+
+
+def test_infer_ffi_error_paths_without_gpu(tmp_path):
+    """infer_ffi before any load_transformer_ffi returns NULL (no abort),
+    free_string accepts NULL, yl_infer_config rejects a negative temperature.
+    Run in a fresh process: the loaded-model slot is process-global."""
+    import subprocess
+    import sys
+    code = (
+        "import importlib, sys, ctypes as C\n"
+        f"sys.path.insert(0, {str(ROOT)!r})\n"
+        "yl = importlib.import_module('yallma3-mini-inference_b200')\n"
+        "lib = yl.raw_lib()\n"
+        "assert lib.infer_ffi(b'hello') is None\n"
+        "assert 'no model loaded' in yl.last_error()\n"
+        "lib.free_string(None)\n"
+        "assert lib.yl_infer_config(C.c_float(-1.0), C.c_float(0.9), 42, 0) == -1\n"
+        "assert lib.yl_infer_config(C.c_float(0.0), C.c_float(0.9), 42, 8) == 0\n"
+        "print('ok')\n")
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stdout + r.stderr
