@@ -230,51 +230,6 @@ __device__ __forceinline__ float rms_factor_smem8(const float* x, uint32_t n, fl
   return __fdiv_rn(1.0f, __fsqrt_rn(r));
 }
 
-// The same factor from the row's squares x[i]^2 (each rounded, as above)
-// staged transposed in shared memory: row l (stride n/8 + 4 floats, so the
-// eight lanes' 16-byte loads fall in different banks) holds the squares of
-// x[8j + l], j = 0, 1, ... Lanes 8g..8g+7 walk the eight chains four values
-// per load, so each step is one dependent addition; lane 8g returns the
-// factor (other lanes return garbage). Bit-identical to rms_factor_smem8.
-__host__ __device__ constexpr uint32_t rms_sq8_stride(uint32_t n) { return n / 8 + 4; }
-__device__ __forceinline__ float rms_factor_sq8(const float* sq, uint32_t n, float eps, int lane) {
-  const int l = lane & 7;
-  const float4* row = reinterpret_cast<const float4*>(sq + (uint32_t)l * rms_sq8_stride(n));
-  const uint32_t nq = n / 32;  // float4 per chain
-  float acc = 0.0f;
-  uint32_t j = 0;
-  float4 cur[8];
-#pragma unroll
-  for (int u = 0; u < 8; ++u) cur[u] = (uint32_t)u < nq ? row[u] : make_float4(0.f, 0.f, 0.f, 0.f);
-  for (; j + 8 <= nq; j += 8) {
-    float4 nxt[8];
-#pragma unroll
-    for (int u = 0; u < 8; ++u) nxt[u] = j + 8 + u < nq ? row[j + 8 + u] : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      acc = __fadd_rn(acc, cur[u].x);
-      acc = __fadd_rn(acc, cur[u].y);
-      acc = __fadd_rn(acc, cur[u].z);
-      acc = __fadd_rn(acc, cur[u].w);
-    }
-#pragma unroll
-    for (int u = 0; u < 8; ++u) cur[u] = nxt[u];
-  }
-  for (uint32_t u = 0; j + u < nq; ++u) {  // fewer than 8 float4 left (still in cur)
-    const float4 v = row[j + u];
-    acc = __fadd_rn(acc, v.x);
-    acc = __fadd_rn(acc, v.y);
-    acc = __fadd_rn(acc, v.z);
-    acc = __fadd_rn(acc, v.w);
-  }
-  const float a = __fadd_rn(acc, __shfl_down_sync(FULL, acc, 4));
-  const float b = __fadd_rn(a, __shfl_down_sync(FULL, a, 2));
-  const float ss = __fadd_rn(b, __shfl_down_sync(FULL, b, 1));
-  float r = __fdiv_rn(ss, (float)n);
-  r = __fadd_rn(r, eps);
-  return __fdiv_rn(1.0f, __fsqrt_rn(r));
-}
-
 // Prefetches this CTA's share (slots cta, cta + ncta, ...) of the next
 // kernel's first rows (see L2Prefetch).
 __device__ __forceinline__ void l2_prefetch_next(const k::L2Prefetch& pf, uint32_t cta, uint32_t ncta) {

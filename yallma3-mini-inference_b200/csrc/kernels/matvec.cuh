@@ -115,10 +115,9 @@ __host__ __device__ inline MvLayout mv_layout(uint32_t K, uint32_t kc, int rpw, 
   // before the quantized row is written there); several tokens need their
   // own area (earlier tokens' quantized rows stay in place).
   L.nstage_off = NT == 1 ? L.x_off : off;
-  if (norm_stage) {  // the row (K floats), or its squares transposed (8 padded rows)
-    const uint32_t nb = 8 * yl::dev::rms_sq8_stride(K) * 4 > K * 4 ? 8 * yl::dev::rms_sq8_stride(K) * 4 : K * 4;
-    if (NT == 1) off = off > L.x_off + nb ? off : L.x_off + nb;
-    else off += nb;
+  if (norm_stage) {
+    if (NT == 1) off = off > L.x_off + K * 4 ? off : L.x_off + K * 4;
+    else off += K * 4;
   }
   L.terms_off = off;  // per consumer warp: [NT][MV_TERMS] block terms of one pass (in-warp fold)
   if (mv_exact_fold<FMT>() && !mv_fold_warp<FMT, NT>()) off += MV_NCW * NT * MV_TERMS * 4;
@@ -254,28 +253,20 @@ __device__ __forceinline__ void mv_norm_regs(const MvArgs& a, const MvLayout& L,
     }
     float r = 1.0f;
     if (NORM && !tp_in) {
-      // the reference's 8-lane sum of squares (util.rs:389-426): every
-      // thread stages the rounded squares of its values, transposed (chain
-      // l = elements 8j + l in one padded row), and lanes 0..7 of warp 0 walk
-      // the eight addition chains from there, one dependent add per step
+      // the reference's 8-lane sum of squares (util.rs:389-426): the row,
+      // already in registers, is staged in shared memory and lanes 0..7 of
+      // warp 0 walk the eight addition chains from there
       if (valid) {
-        const uint32_t rs = rms_sq8_stride(K);
 #pragma unroll
         for (int u = 0; u < MU; ++u) {
           const uint32_t i = ctid * 4 + u * MV_NCW * 32 * 4;
-          if (i < K) {
-            const uint32_t l0 = i & 7u, jj = i >> 3;  // i % 8 is 0 or 4: lanes l0..l0+3, column jj
-            stg[(l0 + 0) * rs + jj] = __fmul_rn(xv[u].x, xv[u].x);
-            stg[(l0 + 1) * rs + jj] = __fmul_rn(xv[u].y, xv[u].y);
-            stg[(l0 + 2) * rs + jj] = __fmul_rn(xv[u].z, xv[u].z);
-            stg[(l0 + 3) * rs + jj] = __fmul_rn(xv[u].w, xv[u].w);
-          }
+          if (i < K) *reinterpret_cast<float4*>(stg + i) = xv[u];
         }
       }
       named_bar_sync(1, MV_NCW * 32);
       if (kTrace && a.trace && t == 0 && ctid == 0) a.trace[(uint64_t)blockIdx.x * 8 + 4] = globaltimer();
       if (cw == 0 && valid) {
-        const float rv = rms_factor_sq8(stg, K, a.eps, lane);
+        const float rv = rms_factor_smem8(stg, K, a.eps, lane);
         if (lane == 0) red[32 + t] = rv;
       }
       named_bar_sync(1, MV_NCW * 32);  // the factor is published; stg is reused by the next token
