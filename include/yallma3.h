@@ -396,7 +396,8 @@ int yl_tokenizer_chat_prompt(const yl_tokenizer* t, const char* system, const ch
 
 /* ---- device sampler (sampler.rs:41-180) ---------------------------------- */
 /* Sampler::new(vocab_size, temperature, top_p, seed): device state (the
- * persistent (prob, index) array, zeroed) on the current CUDA device. */
+ * persistent (prob, index) array, zeroed) on the current CUDA device. A
+ * sampler is used by one thread at a time (the reference's `&mut self`). */
 typedef struct yl_sampler yl_sampler;
 int yl_sampler_create(uint32_t vocab_size, float temperature, float top_p, uint64_t seed, yl_sampler** out);
 int yl_sampler_free(yl_sampler* s);
