@@ -2,6 +2,8 @@
 // quantize, embedding gather and the greedy argmax.
 #include <float.h>
 
+#include <algorithm>
+
 #include "device.cuh"
 #include "kernels.h"
 
@@ -31,34 +33,36 @@ cudaError_t quantize_q8(const float* x, int8_t* q, float* s, uint64_t nblocks, c
 // util.rs:389-426: ss = sum x^2; ss /= n; ss += eps; ss = 1/sqrt(ss);
 // y = w * (ss * x); then the Q8_0 quantizer on y (forward.rs:155-160). Every
 // step is the reference's sequence of IEEE f32 operations, the sum of squares
-// in its 8-lane order, so y and its Q8_0 blocks are bit-identical. One CTA
-// per 4 rows: the rows are staged in shared memory, lanes 8g..8g+7 of warp 0
-// walk row g's eight addition chains, then all warps normalize and quantize.
-constexpr uint32_t RQ_ROWS = 4;
+// in its 8-lane order, so y and its Q8_0 blocks are bit-identical. CTA
+// (sx, t) stages row t in shared memory, lanes 0..7 of warp 0 walk its eight
+// addition chains (every CTA of the row computes the same factor), then the
+// CTA's warps normalize and quantize its share sx of the row's 32-blocks: a
+// few rows still fill the GPU, and no warp quantizes more than a few blocks.
 __global__ void __launch_bounds__(256) rmsnorm_quant_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                                             uint32_t ntok, uint32_t dim, float eps,
                                                             int8_t* __restrict__ q, float* __restrict__ s,
                                                             float* __restrict__ y) {
-  extern __shared__ __align__(16) float rq_stage[];  // [RQ_ROWS][dim]
+  extern __shared__ __align__(16) float rq_stage[];  // [dim]
   grid_dep_launch();
   grid_dep_wait();
-  __shared__ float rf[RQ_ROWS];
-  const uint32_t t0 = blockIdx.x * RQ_ROWS, nt = min(RQ_ROWS, ntok - t0);
+  __shared__ float rf;
+  const uint32_t t = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (uint32_t i = threadIdx.x * 4; i < nt * dim; i += 256 * 4)
-    *reinterpret_cast<float4*>(rq_stage + i) = *reinterpret_cast<const float4*>(x + (uint64_t)t0 * dim + i);
+  const float* xr = x + (uint64_t)t * dim;
+  for (uint32_t i = threadIdx.x * 4; i < dim; i += 256 * 4)
+    *reinterpret_cast<float4*>(rq_stage + i) = *reinterpret_cast<const float4*>(xr + i);
   __syncthreads();
   if (warp == 0) {
-    const uint32_t g = (uint32_t)lane >> 3;
-    const float r = rms_factor_smem8(rq_stage + (g < nt ? g : 0) * dim, dim, eps, lane);
-    if ((lane & 7) == 0 && g < nt) rf[g] = r;
+    const float r = rms_factor_smem8(rq_stage, dim, eps, lane);
+    if (lane == 0) rf = r;
   }
   __syncthreads();
   const uint32_t nb = dim / 32;
-  for (uint32_t tb = warp; tb < nt * nb; tb += 8) {
-    const uint32_t t = t0 + tb / nb, b = tb % nb;
+  const uint32_t b0 = (uint32_t)((uint64_t)nb * blockIdx.x / gridDim.x);
+  const uint32_t b1 = (uint32_t)((uint64_t)nb * (blockIdx.x + 1) / gridDim.x);
+  for (uint32_t b = b0 + warp; b < b1; b += 8) {
     const uint32_t k = b * 32 + lane;
-    const float yv = __fmul_rn(w[k], __fmul_rn(rf[tb / nb], rq_stage[(tb / nb) * dim + k]));
+    const float yv = __fmul_rn(w[k], __fmul_rn(rf, rq_stage[k]));
     if (y) y[(uint64_t)t * dim + k] = yv;
     if (q) {
       float sc;
@@ -72,13 +76,18 @@ __global__ void __launch_bounds__(256) rmsnorm_quant_kernel(const float* __restr
 cudaError_t rmsnorm_quant(const float* x, const float* w, uint32_t ntok, uint32_t dim, float eps, int8_t* q,
                           float* s, float* y, const LaunchCfg& lc) {
   if (ntok == 0) return cudaSuccess;
-  if (dim % 32) return cudaErrorInvalidValue;
-  const uint32_t smem = RQ_ROWS * dim * 4;
+  if (dim % 32 || ntok > 65535u) return cudaErrorInvalidValue;
+  const uint32_t smem = dim * 4;
   if (smem > 227u * 1024u) return cudaErrorInvalidValue;
   cudaError_t e = cudaFuncSetAttribute(rmsnorm_quant_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  return launch_kernel(rmsnorm_quant_kernel, dim3((ntok + RQ_ROWS - 1) / RQ_ROWS), dim3(256), smem, lc, x, w, ntok,
-                       dim, eps, q, s, y);
+  // shares of a row: enough CTAs for the SMs when the rows are few, one warp
+  // pass (8 blocks) per share at least
+  const uint32_t nb = dim / 32, sms = lc.grid ? lc.grid : 148u;
+  uint32_t split = (2 * sms + ntok - 1) / ntok;
+  split = std::max<uint32_t>(1u, std::min<uint32_t>(split, (nb + 7) / 8));
+  return launch_kernel(rmsnorm_quant_kernel, dim3(split, ntok), dim3(256), smem, lc, x, w, ntok, dim, eps, q, s,
+                       y);
 }
 
 // Embedding gather: x[t][k] = value of row tokens[t], q * scale rounded once
