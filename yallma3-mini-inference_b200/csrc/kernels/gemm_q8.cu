@@ -28,16 +28,16 @@ namespace k {
 using namespace yl::dev;
 
 namespace {
-constexpr int GB_M = 128, GB_N = 64, GB_KB = 4, GB_S = 3, GB_THREADS = 256;
+constexpr int GB_M = 128, GB_N = 64, GB_KB = 4, GB_S = 3;
 
-template <int FMT, int BN>
+template <int FMT, int BN, int BM = 128>
 struct GTile {
   static constexpr int QB = FMT == FMT_Q4 ? 16 : 32;  // weight bytes per 32-block
   static constexpr int WROW = GB_KB * QB + 16;         // padded shared-memory rows
   static constexpr int XROW = GB_KB * 32 + 16;
-  static constexpr int W_BYTES = GB_M * WROW;
+  static constexpr int W_BYTES = BM * WROW;
   static constexpr int X_BYTES = BN * XROW;
-  static constexpr int WS_BYTES = GB_M * GB_KB * 4;
+  static constexpr int WS_BYTES = BM * GB_KB * 4;
   static constexpr int XS_BYTES = BN * GB_KB * 4;
   static constexpr int STAGE = W_BYTES + X_BYTES + WS_BYTES + XS_BYTES;
   static constexpr int SMEM = GB_S * STAGE;
@@ -87,10 +87,10 @@ __device__ __forceinline__ uint32_t tile_row(uint32_t i) {
   return (i & ~15u) + (w >> 1) + ((w & 1u) << 3);
 }
 
-template <int FMT, bool SF16, bool PERM, int BN>
+template <int FMT, bool SF16, bool PERM, int BN, int BM, int NTH>
 __device__ __forceinline__ void gemm_load(const GemmArgs& a, uint8_t* st, uint32_t m0, uint32_t n0, uint32_t g0,
                                           uint32_t nb) {
-  using T = GTile<FMT, BN>;
+  using T = GTile<FMT, BN, BM>;
   uint8_t* wt = st;
   uint8_t* xt = wt + T::W_BYTES;
   uint8_t* wsc = xt + T::X_BYTES;
@@ -99,43 +99,48 @@ __device__ __forceinline__ void gemm_load(const GemmArgs& a, uint8_t* st, uint32
   // rows / tokens past the end re-read the last one (in bounds); their
   // results are never stored
   const uint32_t wp = nb * T::QB / 16;  // 16-byte pieces per weight row
-  for (uint32_t i = tid; i < GB_M * wp; i += GB_THREADS) {
+  for (uint32_t i = tid; i < BM * wp; i += NTH) {
     const uint32_t r = i / wp, p = i - r * wp;
     const uint32_t gr = min(m0 + r, a.rows - 1);
     cp_async16(wt + tile_row<PERM>(r) * T::WROW + p * 16,
                a.wq + (uint64_t)gr * a.row_bytes + (uint64_t)g0 * T::QB + p * 16);
   }
   const uint32_t xp = nb * 2;
-  for (uint32_t i = tid; i < BN * xp; i += GB_THREADS) {
+  for (uint32_t i = tid; i < BN * xp; i += NTH) {
     const uint32_t t = i / xp, p = i - t * xp;
     const uint32_t gt = min(n0 + t, a.ntok - 1);
     cp_async16(xt + t * T::XROW + p * 16, a.xq + (uint64_t)gt * a.x_stride + (uint64_t)g0 * 32 + p * 16);
   }
   if (SF16) {  // f16 scales in pairs (the launcher checks the row padding holds an odd tail's pair)
     const uint32_t sp = (nb + 1) / 2;
-    for (uint32_t i = tid; i < GB_M * sp; i += GB_THREADS) {
+    for (uint32_t i = tid; i < BM * sp; i += NTH) {
       const uint32_t r = i / sp, p = i - r * sp;
       const uint32_t gr = min(m0 + r, a.rows - 1);
       cp_async4(wsc + (tile_row<PERM>(r) * GB_KB + 2 * p) * 2,
                 a.ws + (uint64_t)gr * a.scale_row_bytes + (uint64_t)(g0 + 2 * p) * 2);
     }
   } else {
-    for (uint32_t i = tid; i < GB_M * nb; i += GB_THREADS) {
+    for (uint32_t i = tid; i < BM * nb; i += NTH) {
       const uint32_t r = i / nb, b = i - r * nb;
       const uint32_t gr = min(m0 + r, a.rows - 1);
       cp_async4(wsc + (tile_row<PERM>(r) * GB_KB + b) * 4, a.ws + (uint64_t)gr * a.scale_row_bytes + (uint64_t)(g0 + b) * 4);
     }
   }
-  for (uint32_t i = tid; i < BN * nb; i += GB_THREADS) {  // stored [block][token]
+  for (uint32_t i = tid; i < BN * nb; i += NTH) {  // stored [block][token]
     const uint32_t t = i / nb, b = i - t * nb;
     const uint32_t gt = min(n0 + t, a.ntok - 1);
     cp_async4(xsc + (b * BN + t) * 4, a.xs + (uint64_t)gt * a.xs_stride + g0 + b);
   }
 }
 
-template <int FMT, bool SF16, int EPI, int BN>
-__global__ void __launch_bounds__(GB_THREADS, 2) gemm_q_kernel(GemmArgs a) {
-  using T = GTile<FMT, BN>;
+// Threads of a CTA: 8 warps for 64-token tiles, else one warp per 16 rows.
+template <int BN, int BM>
+__host__ __device__ constexpr int gemm_threads() { return (BN >= 64 ? 8 : BM / 16) * 32; }
+
+template <int FMT, bool SF16, int EPI, int BN, int BM>
+__global__ void __launch_bounds__(gemm_threads<BN, BM>(), 512 / gemm_threads<BN, BM>()) gemm_q_kernel(GemmArgs a) {
+  using T = GTile<FMT, BN, BM>;
+  constexpr int NTH = gemm_threads<BN, BM>(), NW = NTH / 32;
   constexpr bool PERM = EPI == EPI_SWIGLU_Q8;
   // BN = 64: warps 4 (rows) x 2 (tokens), 32 x 32 each; BN = 32: 8 x 1,
   // 16 x 32; BN = 16 / 8: 8 x 1, 16 x 16 / 16 x 8 (fewer padded tokens folded
@@ -143,18 +148,20 @@ __global__ void __launch_bounds__(GB_THREADS, 2) gemm_q_kernel(GemmArgs a) {
   constexpr int WN = BN >= 64 ? 2 : 1, MT = BN >= 64 ? 2 : 1, RW = 16 * MT;
   constexpr int NTW = BN >= 32 ? 4 : BN / 8;
   static_assert(BN == 8 || BN == 16 || BN == 32 || BN == 64, "token tile");
+  static_assert((BN == 64 && BM == 128) || (BN < 64 && BM % 16 == 0 && BM <= 128), "row tile");
+  static_assert(EPI != EPI_SWIGLU_Q8 || BM % 64 == 0, "a SwiGLU tile holds whole 32-value h blocks");
   extern __shared__ __align__(128) uint8_t smem[];
-  const uint32_t n0 = blockIdx.x * BN, m0 = blockIdx.y * GB_M;
+  const uint32_t n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int gid = lane >> 2, tig = lane & 3;
-  const int wm = warp % (8 / WN), wn = warp / (8 / WN);
+  const int wm = warp % (NW / WN), wn = warp / (NW / WN);
   const uint32_t G = a.K / 32, nch = (G + GB_KB - 1) / GB_KB;
 
   grid_dep_wait();  // activations come from the preceding kernel
 #pragma unroll
   for (int s = 0; s < GB_S - 1; ++s) {
     if ((uint32_t)s < nch)
-      gemm_load<FMT, SF16, PERM, BN>(a, smem + s * T::STAGE, m0, n0, s * GB_KB, min((uint32_t)GB_KB, G - s * GB_KB));
+      gemm_load<FMT, SF16, PERM, BN, BM, NTH>(a, smem + s * T::STAGE, m0, n0, s * GB_KB, min((uint32_t)GB_KB, G - s * GB_KB));
     cp_async_commit();
   }
 
@@ -171,7 +178,7 @@ __global__ void __launch_bounds__(GB_THREADS, 2) gemm_q_kernel(GemmArgs a) {
     __syncthreads();  // stage c landed for every thread; stage c-1 is free
     const uint32_t cn = c + GB_S - 1;
     if (cn < nch)
-      gemm_load<FMT, SF16, PERM, BN>(a, smem + (cn % GB_S) * T::STAGE, m0, n0, cn * GB_KB,
+      gemm_load<FMT, SF16, PERM, BN, BM, NTH>(a, smem + (cn % GB_S) * T::STAGE, m0, n0, cn * GB_KB,
                                  min((uint32_t)GB_KB, G - cn * GB_KB));
     cp_async_commit();
 
@@ -251,16 +258,18 @@ __global__ void __launch_bounds__(GB_THREADS, 2) gemm_q_kernel(GemmArgs a) {
       for (int nt = 0; nt < NTW; ++nt) {
         const int jl = (wm * RW + mt * 16) / 2 + gid;  // pair of this thread's rows gid (gate) and gid + 8 (up)
         const int tl = wn * 32 + nt * 8 + tig * 2;
-        hb[tl * (GB_M / 2) + jl] = silu_mul(acc[mt][nt][0], acc[mt][nt][2]);
-        hb[(tl + 1) * (GB_M / 2) + jl] = silu_mul(acc[mt][nt][1], acc[mt][nt][3]);
+        hb[tl * (BM / 2) + jl] = silu_mul(acc[mt][nt][0], acc[mt][nt][2]);
+        hb[(tl + 1) * (BM / 2) + jl] = silu_mul(acc[mt][nt][1], acc[mt][nt][3]);
       }
     __syncthreads();
     const uint32_t f = a.rows / 2;
-    for (int pi = warp; pi < BN * 2; pi += GB_THREADS / 32) {
-      const int tl = pi >> 1, blk = pi & 1;
+    constexpr int HB = BM >= 64 ? BM / 64 : 1;  // h blocks of 32 per token in this tile
+    static_assert(BN * (BM / 2) * 4 <= T::SMEM, "the h staging fits the ring");
+    for (int pi = warp; pi < BN * HB; pi += NW) {
+      const int tl = pi / HB, blk = pi % HB;
       const uint32_t t = n0 + tl;
       if (t >= a.ntok) continue;  // warp-uniform
-      const float v = hb[tl * (GB_M / 2) + blk * 32 + lane];
+      const float v = hb[tl * (BM / 2) + blk * 32 + lane];
       float sc;
       const int8_t q = quant_q8_lane(v, &sc);
       const uint32_t j = m0 / 2 + blk * 32 + lane;
@@ -288,23 +297,28 @@ __global__ void __launch_bounds__(GB_THREADS, 2) gemm_q_kernel(GemmArgs a) {
       }
 }
 
-template <int FMT, bool SF16, int EPI, int BN>
+template <int FMT, bool SF16, int EPI, int BN, int BM>
 cudaError_t gemm_launch_bn(const GemmArgs& a, const LaunchCfg& lc) {
-  using T = GTile<FMT, BN>;
-  cudaError_t e =
-      cudaFuncSetAttribute(gemm_q_kernel<FMT, SF16, EPI, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, T::SMEM);
+  using T = GTile<FMT, BN, BM>;
+  cudaError_t e = cudaFuncSetAttribute(gemm_q_kernel<FMT, SF16, EPI, BN, BM>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, T::SMEM);
   if (e != cudaSuccess) return e;
-  const dim3 grid((a.ntok + BN - 1) / BN, (a.rows + GB_M - 1) / GB_M);
-  return launch_kernel(gemm_q_kernel<FMT, SF16, EPI, BN>, grid, dim3(GB_THREADS), (uint32_t)T::SMEM, lc, a);
+  const dim3 grid((a.ntok + BN - 1) / BN, (a.rows + BM - 1) / BM);
+  return launch_kernel(gemm_q_kernel<FMT, SF16, EPI, BN, BM>, grid, dim3(gemm_threads<BN, BM>()), (uint32_t)T::SMEM,
+                       lc, a);
 }
 
 // Token tiles of 8, 16, 32 or 64: a small batch folds no more padded tokens
-// than it must (the fold, not the tensor core, bounds this kernel).
+// than it must (the fold, not the tensor core, bounds this kernel). Up to 16
+// tokens the row tiles shrink to 32 rows (64 with the SwiGLU epilogue, whose
+// tile holds whole 32-value h blocks), so a 4096-row projection still spreads
+// over 128 CTAs.
 template <int FMT, bool SF16, int EPI>
 cudaError_t gemm_launch(const GemmArgs& a, const LaunchCfg& lc) {
-  if (a.ntok <= 8) return gemm_launch_bn<FMT, SF16, EPI, 8>(a, lc);
-  if (a.ntok <= 16) return gemm_launch_bn<FMT, SF16, EPI, 16>(a, lc);
-  return a.ntok <= 32 ? gemm_launch_bn<FMT, SF16, EPI, 32>(a, lc) : gemm_launch_bn<FMT, SF16, EPI, 64>(a, lc);
+  constexpr int SBM = EPI == EPI_SWIGLU_Q8 ? 64 : 32;
+  if (a.ntok <= 8) return gemm_launch_bn<FMT, SF16, EPI, 8, SBM>(a, lc);
+  if (a.ntok <= 16) return gemm_launch_bn<FMT, SF16, EPI, 16, SBM>(a, lc);
+  return a.ntok <= 32 ? gemm_launch_bn<FMT, SF16, EPI, 32, 128>(a, lc) : gemm_launch_bn<FMT, SF16, EPI, 64, 128>(a, lc);
 }
 
 template <int FMT, bool SF16>
@@ -323,7 +337,7 @@ bool gemm_supported(const GemmArgs& a, int fmt, bool sf16, int epi) {
   if (fmt != FMT_Q8 && fmt != FMT_Q4) return false;
   if (epi != EPI_STORE && epi != EPI_ADD && epi != EPI_QUIRK && epi != EPI_SWIGLU_Q8) return false;
   if (!a.wq || !a.ws || !a.xq || !a.xs || a.rows == 0 || a.ntok == 0 || a.K == 0 || a.K % 32) return false;
-  if ((a.rows + GB_M - 1) / GB_M > 65535u) return false;
+  if ((a.rows + 31) / 32 > 65535u) return false;
   const uint32_t G = a.K / 32;
   const uint32_t qb = fmt == FMT_Q4 ? 16 : 32;
   if ((uintptr_t)a.wq % 16 || a.row_bytes % 16 || a.row_bytes < G * qb) return false;
@@ -331,7 +345,7 @@ bool gemm_supported(const GemmArgs& a, int fmt, bool sf16, int epi) {
   if ((uintptr_t)a.xs % 4 || a.xs_stride < G) return false;
   if ((uintptr_t)a.ws % 4 || a.scale_row_bytes % 4) return false;
   if (sf16 ? a.scale_row_bytes < 2 * (G + (G & 1)) : a.scale_row_bytes < 4 * G) return false;
-  if (epi == EPI_SWIGLU_Q8) return a.rows % GB_M == 0 && a.hq && a.hs;
+  if (epi == EPI_SWIGLU_Q8) return a.rows % (a.ntok <= 16 ? 64u : (uint32_t)GB_M) == 0 && a.hq && a.hs;
   return a.out != nullptr;
 }
 
