@@ -119,10 +119,11 @@ int yl_quantize(int fmt, yl_qtensor* dst, const float* x, uint64_t n, uint32_t g
  * [batch][o]. accumulate = 1 reproduces the reference's store semantics
  * exactly (columns < 4*floor(o/4) add into out, the rest overwrite,
  * weight_type.rs:190-201 and :207-224, inside matmul_q8_slices :122-226);
- * accumulate = 0 overwrites every column. Batches
- * of 5 or more Q8_0 / Q4_0 rows run on the int8 tensor-core GEMM, whose
- * overwrite results equal the reference's bit for bit; smaller batches run on
- * the matvec (within 1e-5 of the sum of |terms|). */
+ * accumulate = 0 overwrites every column. Q8_0 / Q4_0: batches of 5 or more
+ * rows run on the int8 tensor-core GEMM, smaller ones on the matvec; both
+ * fold the per-block int32 dots in the reference's order, so the results
+ * equal the reference's bit for bit. F16 weights run on the matvec with f32
+ * products summed in lane-parallel order (within 1e-5 of the sum of |terms|). */
 int yl_matmul(float* out, const yl_qtensor* x, const yl_qtensor* w, uint64_t n, uint64_t o, uint64_t gs,
               uint64_t batch, int accumulate, void* stream);
 
