@@ -121,9 +121,13 @@ int yl_quantize(int fmt, yl_qtensor* dst, const float* x, uint64_t n, uint32_t g
  * weight_type.rs:190-201 and :207-224, inside matmul_q8_slices :122-226);
  * accumulate = 0 overwrites every column. Q8_0 / Q4_0: batches of 5 or more
  * rows run on the int8 tensor-core GEMM, smaller ones on the matvec; both
- * fold the per-block int32 dots in the reference's order, so the results
- * equal the reference's bit for bit. F16 weights run on the matvec with f32
- * products summed in lane-parallel order (within 1e-5 of the sum of |terms|). */
+ * fold the per-block int32 dots in the reference's order, so with
+ * accumulate = 0 the results equal the reference's bit for bit. With
+ * accumulate = 1 a quad column gets its initial value plus the folded row
+ * (the reference adds every block term into the initial value in turn):
+ * within 1e-5 of the sum of |terms| and |initial value|. F16 weights run on
+ * the matvec with f32 products summed in lane-parallel order (within 1e-5 of
+ * the sum of |terms|). */
 int yl_matmul(float* out, const yl_qtensor* x, const yl_qtensor* w, uint64_t n, uint64_t o, uint64_t gs,
               uint64_t batch, int accumulate, void* stream);
 
