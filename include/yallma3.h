@@ -371,9 +371,11 @@ int yl_infer_config(float temperature, float top_p, uint64_t seed, uint32_t max_
  * (Tokenizer::from_gguf_parts, tokenizer.rs:78-132), tokenizer.json
  * (from_json, :134-217) else tokenizer.bin (new, :219-262) beside a
  * .safetensors file, tokenizer.bin beside a .lmrs file. Needs no GPU.
- * A Jinja chat template (tokenizer.chat_template) is recorded but not
- * rendered: yl_tokenizer_chat_prompt builds the no-template format for every
- * tokenizer. */
+ * A GGUF file's chat template (tokenizer.chat_template) is parsed at load
+ * (set_chat_template, tokenizer.rs:408-416) and rendered by the prompts
+ * below with minijinja's semantics (the reference's template engine); a
+ * template that does not parse makes those calls fail with the parse error
+ * (the reference panics at load). */
 typedef struct yl_tokenizer yl_tokenizer;
 int yl_tokenizer_load(const char* model_path, yl_tokenizer** out);
 int yl_tokenizer_free(yl_tokenizer* t);
@@ -392,12 +394,38 @@ int yl_tokenizer_encode(const yl_tokenizer* t, const char* text, int bos, int eo
  * without the terminator (YL_ERR_RANGE when n_out + 1 exceeds cap). */
 int yl_tokenizer_decode(const yl_tokenizer* t, const uint32_t* ids, uint64_t n, char* out, uint64_t cap,
                         uint64_t* n_out);
-/* The console's prompt of a fresh conversation: apply_system_template(system)
- * then apply_turn_template(user, true) (tokenizer.rs:453-521, no-template
- * branches; main.rs:149-153,177). YL_ERR_FORMAT when a Llama-3 vocabulary does
- * not encode "user" / "assistant" as single tokens (a panic in the reference). */
+/* The console's prompt of a fresh conversation (main.rs:149-153,177).
+ * Without a chat template: apply_system_template(system) then
+ * apply_turn_template(user, true), no-template branches (tokenizer.rs:475-521);
+ * YL_ERR_FORMAT when a Llama-3 vocabulary does not encode "user" /
+ * "assistant" as single tokens (a panic in the reference). With a template:
+ * [BOS] when add_bos_token, the rendered system turn when system is non-empty
+ * (apply_system_template), the rendered turn of [user, empty assistant] with
+ * add_generation_prompt, less a trailing <|eot_id|> (apply_turn_template).
+ * Template errors as yl_chat_template_render. */
 int yl_tokenizer_chat_prompt(const yl_tokenizer* t, const char* system, const char* user, uint32_t* ids,
                              uint64_t cap, uint64_t* n_out);
+/* Tokenizer::render_chat_template (tokenizer.rs:418-436): the chat template
+ * rendered with {messages: [{role, content}] x n_messages,
+ * add_generation_prompt}, then encode_template_output (:438-473): at each '<'
+ * the longest vocabulary entry matching there is one id, the text up to the
+ * next '<' goes through encode(text, false, false). *n_out = 0 when the
+ * tokenizer has no template or the text is empty. */
+int yl_tokenizer_render_chat(const yl_tokenizer* t, const char* const* roles, const char* const* contents,
+                             uint64_t n_messages, int add_generation_prompt, uint32_t* ids, uint64_t cap,
+                             uint64_t* n_out);
+/* The text step alone: renders template source with the same context
+ * (minijinja 2.20 at default settings: no trim_blocks / lstrip_blocks, one
+ * trailing newline of the source dropped, lenient undefined values, no
+ * Python-style string methods). Output as yl_tokenizer_decode. Errors:
+ * YL_ERR_FORMAT where minijinja fails (syntax; an undefined value under
+ * attribute access or arithmetic; an unknown filter, test, function or method;
+ * a type error), YL_ERR_UNSUPPORTED for a construct this renderer does not
+ * implement (floats, macros, call / filter / with / raw blocks, includes, the
+ * less common builtin filters), YL_ERR_ARG for text that is not UTF-8. */
+int yl_chat_template_render(const char* tmpl, const char* const* roles, const char* const* contents,
+                            uint64_t n_messages, int add_generation_prompt, char* out, uint64_t cap,
+                            uint64_t* n_out);
 
 /* ---- device sampler (sampler.rs:41-180) ---------------------------------- */
 /* Sampler::new(vocab_size, temperature, top_p, seed): device state (the

@@ -5,7 +5,11 @@ product imports this file.
 
 The GPT-2 pre-tokenizer split uses the `regex` module with the reference's
 pattern (tokenizer.rs:28-30), an implementation independent of the product's
-hand-written matcher. Sums the reference chains in f32 (softmax denominator,
+hand-written matcher. Chat templates: the reference renders them with
+minijinja 2.20.0 (Cargo.lock), which is not installed here; jinja2 3.1.6
+stands in, set to minijinja's defaults where the two differ on the cases the
+tests render (see _MiniJinjaDefaults), so the C++ renderer is checked against
+an independent Jinja implementation rather than against minijinja itself. Sums the reference chains in f32 (softmax denominator,
 top-p cumulative sum, cdf) are taken with numpy's sequential float32
 accumulate, which rounds after every addition like the reference's loops.
 """
@@ -15,8 +19,10 @@ import json
 import struct
 from pathlib import Path
 
+import jinja2
 import numpy as np
 import regex
+from jinja2.sandbox import SandboxedEnvironment
 
 GPT2_PATTERN = r"'(?:[sdmt]|ll|ve|re)| ?\p{L}+| ?\p{N}+| ?[^\s\p{L}\p{N}]+|\s+"
 _GPT2 = regex.compile(GPT2_PATTERN)
@@ -121,12 +127,14 @@ class Tokenizer:
     @classmethod
     def from_gguf(cls, path: str):
         kv = read_gguf_metadata(path)
-        return cls.from_gguf_parts(kv["tokenizer.ggml.tokens"], kv.get("tokenizer.ggml.merges", []),
-                                   kv.get("tokenizer.ggml.bos_token_id", 128000),
-                                   kv.get("tokenizer.ggml.eos_token_id", 128009),
-                                   kv.get("tokenizer.ggml.pre", "default"),
-                                   kv.get("tokenizer.ggml.add_bos_token", True),
-                                   kv.get("tokenizer.ggml.add_space_prefix", False))
+        tok = cls.from_gguf_parts(kv["tokenizer.ggml.tokens"], kv.get("tokenizer.ggml.merges", []),
+                                  kv.get("tokenizer.ggml.bos_token_id", 128000),
+                                  kv.get("tokenizer.ggml.eos_token_id", 128009),
+                                  kv.get("tokenizer.ggml.pre", "default"),
+                                  kv.get("tokenizer.ggml.add_bos_token", True),
+                                  kv.get("tokenizer.ggml.add_space_prefix", False))
+        tok.chat_template = kv.get("tokenizer.chat_template")  # transformer_llama_gguf.rs:634-641
+        return tok
 
     # ---- encode / decode ----
     def has_llama_tokens(self) -> bool:
@@ -208,8 +216,57 @@ class Tokenizer:
             t += [271, 128009]
         return t
 
+    chat_template = None
+
+    def encode_template_output(self, text: str) -> list[int]:
+        """tokenizer.rs:438-473, literally: every vocabulary entry containing
+        '<' (a later equal text replacing an earlier one), the longest that
+        matches at each '<', the text up to the next '<' through encode()."""
+        text_to_id = {}
+        for tid, t in enumerate(self.vocab):
+            if "<" in t:
+                text_to_id[t] = tid
+        entries = [(t.encode(), tid) for t, tid in text_to_id.items()]
+        b = text.encode()
+        out, pos = [], 0
+        while pos < len(b):
+            if b[pos] == 0x3C:
+                best, best_len = None, 0
+                for tb, tid in entries:
+                    if b.startswith(tb, pos) and len(tb) > best_len:
+                        best, best_len = tid, len(tb)
+                if best is not None:
+                    out.append(best)
+                    pos += best_len
+                    continue
+            start = pos
+            pos += 1
+            while pos < len(b) and b[pos] != 0x3C:
+                pos += 1
+            out += self.encode(b[start:pos].decode())
+        return out
+
+    def render_chat(self, messages, add_generation_prompt: bool) -> list[int]:
+        """render_chat_template (tokenizer.rs:418-436)"""
+        if self.chat_template is None:
+            return []
+        text = render_chat_template_text(self.chat_template, messages, add_generation_prompt)
+        return self.encode_template_output(text) if text else []
+
     def chat_prompt(self, user: str, system: str = "") -> list[int]:
-        """apply_system_template + apply_turn_template(user, true), no template (tokenizer.rs:453-521)"""
+        """The console's fresh prompt (main.rs:149-153, :177): with a chat
+        template, [bos] then apply_turn_template(user, true) (tokenizer.rs:496-508)
+        (a given system prompt rendered in between, apply_system_template
+        :476-482); without one, apply_system_template + apply_turn_template,
+        no-template branches (tokenizer.rs:453-521)"""
+        if self.chat_template is not None:
+            t = [self.bos] if self.add_bos_token else []
+            if system:
+                t += self.render_chat([("system", system)], False)
+            turn = self.render_chat([("user", user), ("assistant", "")], True)
+            if turn and turn[-1] == 128009:
+                turn.pop()
+            return t + turn
         if self.has_llama_tokens():
             t = self._wrap_n_header(system, "system", True)
         else:
@@ -224,6 +281,39 @@ class Tokenizer:
                 t.append(self.bos)
             t += self.encode(user)
         return t
+
+
+class _MiniJinjaDefaults(SandboxedEnvironment):
+    """jinja2 set to minijinja's default behaviour (the reference's renderer,
+    tokenizer.rs:408-430) where the two differ: no Python methods on strings,
+    lists and maps (minijinja without pycompat: an error when called, an
+    undefined value when only looked up), and booleans / none printed as
+    true / false / none. Undefined values, whitespace control, the dropped
+    trailing newline and autoescape off are jinja2's defaults already."""
+
+    def is_safe_attribute(self, obj, attr, value):
+        if isinstance(obj, (str, list, tuple, dict)) and callable(value):
+            return False
+        return super().is_safe_attribute(obj, attr, value)
+
+
+def _finalize(v):
+    if v is True:
+        return "true"
+    if v is False:
+        return "false"
+    if v is None:
+        return "none"
+    return v
+
+
+def render_chat_template_text(template: str, messages, add_generation_prompt: bool) -> str:
+    """The render of tokenizer.rs:418-428: context {messages: [{role,
+    content}], add_generation_prompt}; serde_json's map keeps the keys sorted,
+    so each message iterates content before role."""
+    env = _MiniJinjaDefaults(finalize=_finalize, undefined=jinja2.Undefined)
+    msgs = [{"content": c, "role": r} for r, c in messages]
+    return env.from_string(template).render(messages=msgs, add_generation_prompt=add_generation_prompt)
 
 
 def utf8_lossy(b: bytes) -> str:

@@ -132,6 +132,9 @@ _sigs = {
     "yl_tokenizer_encode": (C.c_int, [_P, C.c_char_p, C.c_int, C.c_int, _P, C.c_uint64, C.POINTER(C.c_uint64)]),
     "yl_tokenizer_decode": (C.c_int, [_P, _P, C.c_uint64, _P, C.c_uint64, C.POINTER(C.c_uint64)]),
     "yl_tokenizer_chat_prompt": (C.c_int, [_P, C.c_char_p, C.c_char_p, _P, C.c_uint64, C.POINTER(C.c_uint64)]),
+    "yl_tokenizer_render_chat": (C.c_int, [_P, _P, _P, C.c_uint64, C.c_int, _P, C.c_uint64, C.POINTER(C.c_uint64)]),
+    "yl_chat_template_render": (C.c_int, [C.c_char_p, _P, _P, C.c_uint64, C.c_int, _P, C.c_uint64,
+                                          C.POINTER(C.c_uint64)]),
     "yl_sampler_create": (C.c_int, [C.c_uint32, C.c_float, C.c_float, C.c_uint64, C.POINTER(_P)]),
     "yl_sampler_free": (C.c_int, [_P]),
     "yl_sampler_sample": (C.c_int, [_P, _P, _P, _P]),
@@ -596,6 +599,12 @@ class Tokenizer:
     def chat_prompt(self, user: str, system: str = "") -> list:
         return self._ids(_lib.yl_tokenizer_chat_prompt, system.encode(), user.encode())
 
+    def render_chat(self, messages: Sequence[tuple], add_generation_prompt: bool) -> list:
+        """Tokenizer::render_chat_template: messages are (role, content) pairs."""
+        roles, contents, keep = _message_arrays(messages)
+        return self._ids(_lib.yl_tokenizer_render_chat, roles, contents, len(messages),
+                         1 if add_generation_prompt else 0)
+
     def close(self) -> None:
         if self._h and self._owned:
             _lib.yl_tokenizer_free(self._h)
@@ -632,6 +641,30 @@ class Sampler:
             self.close()
         except Exception:
             pass
+
+
+def _message_arrays(messages: Sequence[tuple]):
+    enc = [(r.encode(), c.encode()) for r, c in messages]
+    roles = (C.c_char_p * max(1, len(enc)))(*[r for r, _ in enc])
+    contents = (C.c_char_p * max(1, len(enc)))(*[c for _, c in enc])
+    return C.cast(roles, C.c_void_p), C.cast(contents, C.c_void_p), (roles, contents, enc)
+
+
+def render_chat_template(template: str, messages: Sequence[tuple], add_generation_prompt: bool) -> str:
+    """Renders chat-template source with {messages, add_generation_prompt}
+    (the text step of Tokenizer::render_chat_template)."""
+    roles, contents, keep = _message_arrays(messages)
+    n = C.c_uint64()
+    cap = 256 + 2 * len(template)
+    while True:
+        buf = C.create_string_buffer(cap)
+        rc = _lib.yl_chat_template_render(template.encode(), roles, contents, len(messages),
+                                          1 if add_generation_prompt else 0, buf, cap, C.byref(n))
+        if rc == -6 and n.value + 1 > cap:
+            cap = n.value + 1
+            continue
+        _check(rc)
+        return buf.raw[: n.value].decode("utf-8")
 
 
 def session_logits(session: InferenceSession) -> int:

@@ -8,6 +8,7 @@
 #include <vector>
 
 #include "../kernels/kernels.h"
+#include "chat_template.h"
 #include "common.h"
 #include "generate.h"
 #include "tokenizer.h"
@@ -206,6 +207,48 @@ int yl_tokenizer_chat_prompt(const yl_tokenizer* t, const char* system, const ch
   int rc = yl::tok_chat_prompt(t->t, system ? system : "", user, &v);
   if (rc) return rc;
   return copy_ids(v, ids, cap, n_out);
+}
+
+static int gather_messages(const char* const* roles, const char* const* contents, uint64_t n,
+                           yl::ChatMessages* out) {
+  if (n && (!roles || !contents)) return fail(YL_ERR_ARG, "null message arrays");
+  for (uint64_t i = 0; i < n; ++i) {
+    if (!roles[i] || !contents[i]) return fail(YL_ERR_ARG, "null message");
+    out->push_back({roles[i], contents[i]});
+  }
+  return YL_OK;
+}
+
+int yl_tokenizer_render_chat(const yl_tokenizer* t, const char* const* roles, const char* const* contents,
+                             uint64_t n_messages, int add_generation_prompt, uint32_t* ids, uint64_t cap,
+                             uint64_t* n_out) {
+  if (!t) return fail(YL_ERR_ARG, "null tokenizer");
+  yl::ChatMessages msgs;
+  int rc = gather_messages(roles, contents, n_messages, &msgs);
+  if (rc) return rc;
+  std::vector<uint32_t> v;
+  if ((rc = yl::tok_render_chat(t->t, msgs, add_generation_prompt != 0, &v))) return rc;
+  return copy_ids(v, ids, cap, n_out);
+}
+
+int yl_chat_template_render(const char* tmpl, const char* const* roles, const char* const* contents,
+                            uint64_t n_messages, int add_generation_prompt, char* out, uint64_t cap,
+                            uint64_t* n_out) {
+  if (!tmpl) return fail(YL_ERR_ARG, "null template");
+  yl::ChatMessages msgs;
+  int rc = gather_messages(roles, contents, n_messages, &msgs);
+  if (rc) return rc;
+  std::shared_ptr<const yl::ChatTemplate> t;
+  if ((rc = yl::chat_template_parse(tmpl, &t))) return rc;
+  std::string s;
+  if ((rc = yl::chat_template_render(*t, msgs, add_generation_prompt != 0, &s))) return rc;
+  if (n_out) *n_out = s.size();
+  if (s.size() + 1 > cap) return fail(YL_ERR_RANGE, "output buffer too small");
+  if (out) {
+    memcpy(out, s.data(), s.size());
+    out[s.size()] = '\0';
+  }
+  return YL_OK;
 }
 
 }  // extern "C"

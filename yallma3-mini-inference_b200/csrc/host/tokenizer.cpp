@@ -10,6 +10,7 @@
 #include <map>
 #include <sstream>
 
+#include "chat_template.h"
 #include "common.h"
 #include "json.h"
 #include "unicode_tables.h"
@@ -164,6 +165,15 @@ void finish_tables(Tokenizer* t, bool byte_level) {
   t->index.clear();
   t->index.reserve(t->vocab.size() * 2);
   for (uint32_t i = 0; i < t->vocab.size(); ++i) t->index[t->vocab[i]] = i;  // the last equal text wins
+  // encode_template_output's map of the entries containing '<' (tokenizer.rs:439-444; a later equal text
+  // replaces an earlier one); only those that start with '<' can match at a '<'
+  t->lt_index.clear();
+  t->lt_max_len = 0;
+  for (uint32_t i = 0; i < t->vocab.size(); ++i)
+    if (!t->vocab[i].empty() && t->vocab[i][0] == '<') {
+      t->lt_index[t->vocab[i]] = i;
+      t->lt_max_len = std::max(t->lt_max_len, t->vocab[i].size());
+    }
   t->byte_level = byte_level;
   if (!byte_level) {  // tokenizer.bin: byte b is token b + 3 (tokenizer.rs:255)
     for (int b = 0; b < 256; ++b) t->byte_to_token[b] = (uint32_t)b + 3;
@@ -332,6 +342,10 @@ int load_gguf_tok(const std::string& path, Tokenizer* t) {
   tokenizer_from_parts(t, std::move(tokens), merges, (uint32_t)bos, (uint32_t)eos, pre, add_bos, add_space);
   t->has_template = have_tmpl;
   t->chat_template = tmpl;
+  if (have_tmpl) {  // set_chat_template (tokenizer.rs:408-416) parses it at load
+    t->tmpl_rc = chat_template_parse(tmpl, &t->tmpl);
+    if (t->tmpl_rc) t->tmpl_err = yl_last_error();
+  }
   return YL_OK;
 }
 
@@ -446,6 +460,11 @@ bool exists(const std::string& p) {
 }
 
 }  // namespace
+
+bool utf8_code_points(const std::string& s, std::vector<uint32_t>* cps, std::vector<size_t>* offs) {
+  return utf8_decode(s, cps, offs);
+}
+bool is_white_space(uint32_t cp) { return in_ranges(kUniSpace, kUniSpace_N, cp); }
 
 void tokenizer_from_parts(Tokenizer* t, std::vector<std::string> vocab, const std::vector<std::string>& merges,
                           uint32_t bos, uint32_t eos, const std::string& pre, bool add_bos, bool add_space_prefix) {
@@ -589,11 +608,60 @@ int wrap_n_header(const Tokenizer& t, const std::string& text, const std::string
 }
 }  // namespace
 
+int tok_encode_template_output(const Tokenizer& t, const std::string& text, std::vector<uint32_t>* out) {
+  out->clear();
+  std::vector<uint32_t> e;
+  size_t pos = 0;
+  while (pos < text.size()) {
+    if (text[pos] == '<') {  // the longest entry that matches here (one text per length can)
+      bool hit = false;
+      for (size_t len = std::min(t.lt_max_len, text.size() - pos); len > 0 && !hit; --len) {
+        auto it = t.lt_index.find(text.substr(pos, len));
+        if (it != t.lt_index.end()) {
+          out->push_back(it->second);
+          pos += len;
+          hit = true;
+        }
+      }
+      if (hit) continue;
+    }
+    const size_t start = pos++;
+    while (pos < text.size() && text[pos] != '<') ++pos;
+    const int rc = tok_encode(t, text.substr(start, pos - start), false, false, &e);
+    if (rc) return rc;
+    out->insert(out->end(), e.begin(), e.end());
+  }
+  return YL_OK;
+}
+
+int tok_render_chat(const Tokenizer& t, const std::vector<std::pair<std::string, std::string>>& messages,
+                    bool add_generation_prompt, std::vector<uint32_t>* out) {
+  out->clear();
+  if (!t.has_template) return YL_OK;
+  if (!t.tmpl) return fail(t.tmpl_rc, t.tmpl_err);
+  std::string text;
+  const int rc = chat_template_render(*t.tmpl, messages, add_generation_prompt, &text);
+  if (rc) return rc;
+  if (text.empty()) return YL_OK;
+  return tok_encode_template_output(t, text, out);
+}
+
 int tok_chat_prompt(const Tokenizer& t, const std::string& system, const std::string& user,
                     std::vector<uint32_t>* out) {
   out->clear();
   int rc;
   std::vector<uint32_t> e;
+  if (t.has_template) {
+    if (t.add_bos_token) out->push_back(t.bos);
+    if (!system.empty()) {
+      if ((rc = tok_render_chat(t, {{"system", system}}, false, &e))) return rc;
+      out->insert(out->end(), e.begin(), e.end());
+    }
+    if ((rc = tok_render_chat(t, {{"user", user}, {"assistant", ""}}, true, &e))) return rc;
+    if (!e.empty() && e.back() == 128009u) e.pop_back();  // Tokenizer::EOT
+    out->insert(out->end(), e.begin(), e.end());
+    return YL_OK;
+  }
   // apply_system_template, no-template branch (tokenizer.rs:453-471)
   if (t.has_llama_tokens()) {
     if ((rc = wrap_n_header(t, system, "system", true, out))) return rc;

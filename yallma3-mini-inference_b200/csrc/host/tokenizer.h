@@ -8,9 +8,12 @@
 #include <memory>
 #include <string>
 #include <unordered_map>
+#include <utility>
 #include <vector>
 
 namespace yl {
+
+struct ChatTemplate;
 
 struct Tokenizer {
   std::vector<std::string> vocab;
@@ -26,8 +29,15 @@ struct Tokenizer {
   uint32_t bos = 0, eos = 0;
   std::string pre = "default";
   bool add_bos_token = true, add_space_prefix = false;
-  bool has_template = false;  // a Jinja chat template was found (kept, not rendered)
+  bool has_template = false;  // the GGUF metadata held tokenizer.chat_template
   std::string chat_template;
+  std::shared_ptr<const ChatTemplate> tmpl;  // the parsed template (null if it did not parse)
+  int tmpl_rc = 0;                           // why it did not parse
+  std::string tmpl_err;
+  // vocabulary entries that start with '<' -> the highest id of that text,
+  // and their longest length in bytes (encode_template_output)
+  std::unordered_map<std::string, uint32_t> lt_index;
+  size_t lt_max_len = 0;
 
   bool has_llama_tokens() const { return vocab.size() > 128009; }  // tokenizer.rs:264-266
 };
@@ -45,13 +55,31 @@ void tokenizer_from_parts(Tokenizer* t, std::vector<std::string> vocab, const st
 int tok_encode(const Tokenizer& t, const std::string& text, bool bos, bool eos, std::vector<uint32_t>* out);
 // Tokenizer::decode (tokenizer.rs:523-551), String::from_utf8_lossy included.
 std::string tok_decode(const Tokenizer& t, const uint32_t* ids, size_t n);
-// The prompt of one fresh conversation as the reference's console builds it
-// (main.rs:149-153 and :177): the system template of an empty system prompt,
-// then the user turn with an empty assistant header (tokenizer.rs:453-521,
-// the no-template branches). Jinja templates are not rendered: a tokenizer
-// that carries one is prompted with the same built-in format.
+// Tokenizer::render_chat_template (tokenizer.rs:418-436): the chat template
+// rendered with {messages, add_generation_prompt}, then encoded as
+// encode_template_output does (:438-473). No template: an empty result.
+int tok_render_chat(const Tokenizer& t, const std::vector<std::pair<std::string, std::string>>& messages,
+                    bool add_generation_prompt, std::vector<uint32_t>* out);
+// encode_template_output (tokenizer.rs:438-473): at each '<' the longest
+// vocabulary entry that matches there becomes one id; the text up to the next
+// '<' goes through encode(text, false, false).
+int tok_encode_template_output(const Tokenizer& t, const std::string& text, std::vector<uint32_t>* out);
+// The prompt of one fresh conversation as the reference's console builds it.
+// Without a chat template (main.rs:149-153, :177): apply_system_template of
+// the system prompt, then apply_turn_template(user, true), no-template
+// branches (tokenizer.rs:475-521). With one: [BOS] when add_bos_token
+// (main.rs:149-153), the rendered system turn when a system prompt is given
+// (apply_system_template, tokenizer.rs:476-482), then the rendered user turn
+// with an empty assistant message and add_generation_prompt, less a trailing
+// <|eot_id|> (apply_turn_template, tokenizer.rs:496-508).
 int tok_chat_prompt(const Tokenizer& t, const std::string& system, const std::string& user,
                     std::vector<uint32_t>* out);
+
+// UTF-8 helpers shared with the chat-template renderer: the code points of s
+// (false if s is not well-formed UTF-8) with their byte offsets plus s.size(),
+// and the Unicode White_Space property.
+bool utf8_code_points(const std::string& s, std::vector<uint32_t>* cps, std::vector<size_t>* offs);
+bool is_white_space(uint32_t cp);
 
 }  // namespace yl
 
