@@ -54,10 +54,29 @@ def chat_models(tmp_path_factory, yl):
     small_vocab = vocab + [f"<|pad_{i}|>" for i in range(1000 - len(vocab))]
     base = yl.synth_preset("tiny128", str(root / "base_small.gguf"))
     out["small"] = tf.retokenize_gguf(base, root / "small.gguf", small_vocab, merges, 1, 2, pre="gpt2")
+    # the same models carrying chat templates (GGUF tokenizer.chat_template)
+    tmpl_vocab = vocab + ["<|im_start|>", "<|im_end|>"] + [f"<|pad_{i}|>" for i in range(998 - len(vocab))]
+    out["small_tmpl"] = tf.retokenize_gguf(base, root / "small_tmpl.gguf", tmpl_vocab, merges, 1, 2, pre="gpt2",
+                                           template=BLOCKS_TEMPLATE)
     base = yl.synth_preset("tiny128", str(root / "base_big.gguf"), vocab_size=128256)
     out["llama"] = tf.retokenize_gguf(base, root / "llama.gguf", tf.llama_vocab(vocab), merges, 128000, 128009,
                                       pre="gpt2")
+    out["llama_tmpl"] = tf.retokenize_gguf(base, root / "llama_tmpl.gguf", tf.llama_vocab(vocab), merges, 128000,
+                                           128009, pre="gpt2", template=HEADERS_TEMPLATE)
     return out
+
+
+BLOCKS_TEMPLATE = """{%- for m in messages -%}
+<|im_start|>{{ m.role }}
+{{ m.content }}<|im_end|>
+{% endfor -%}
+{%- if add_generation_prompt %}<|im_start|>assistant
+{% endif %}"""
+
+HEADERS_TEMPLATE = """{%- for m in messages %}
+    {{- '<|start_header_id|>' + m['role'] + '<|end_header_id|>\n\n' + m['content'] | trim + '<|eot_id|>' }}
+{%- endfor %}
+{%- if add_generation_prompt %}{{ '<|start_header_id|>assistant<|end_header_id|>\n\n' }}{% endif %}"""
 
 
 def host_console_loop(yl, path, prompt, temp, top_p, seed, max_tokens):
@@ -83,7 +102,7 @@ def host_console_loop(yl, path, prompt, temp, top_p, seed, max_tokens):
     return reply, ids, toks
 
 
-@pytest.mark.parametrize("kind", ["small", "llama"])
+@pytest.mark.parametrize("kind", ["small", "llama", "small_tmpl", "llama_tmpl"])
 def test_infer_ffi_matches_console_loop(yl, torch_cuda, chat_models, kind):
     path = chat_models[kind]
     assert yl.load_transformer_ffi(path)
