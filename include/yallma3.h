@@ -422,7 +422,10 @@ int yl_tokenizer_render_chat(const yl_tokenizer* t, const char* const* roles, co
  * attribute access or arithmetic; an unknown filter, test, function or method;
  * a type error), YL_ERR_UNSUPPORTED for a construct this renderer does not
  * implement (floats, macros, call / filter / with / raw blocks, includes, the
- * less common builtin filters), YL_ERR_ARG for text that is not UTF-8. */
+ * less common builtin filters), YL_ERR_ARG for text that is not UTF-8.
+ * Parsing and rendering run on an internal thread with an 8 MiB stack and
+ * bound nesting (more than ~250 nested parentheses, expressions deeper than
+ * 1000 nodes, blocks nested more than 200 deep: YL_ERR_FORMAT). */
 int yl_chat_template_render(const char* tmpl, const char* const* roles, const char* const* contents,
                             uint64_t n_messages, int add_generation_prompt, char* out, uint64_t cap,
                             uint64_t* n_out);

@@ -153,6 +153,57 @@ def test_render_errors(yl, template, code):
             tr.render_chat_template_text(template, msgs, True)
 
 
+def test_render_bounds_nesting(yl):
+    """Template text comes from model files: nesting that would exhaust a thread's stack fails cleanly."""
+    msgs = [("user", "hi")]
+    deep = [
+        "{{ " + "(" * 5000 + "1" + ")" * 5000 + " }}",
+        "{{ " + "-" * 5000 + "1 }}",
+        "{{ " + "not " * 5000 + "true }}",
+        "{{ " + " ~ ".join(["'a'"] * 3000) + " }}",
+        "{{ 'a'" + " | trim" * 3000 + " }}",
+        "{% if true %}" * 300 + "x" + "{% endif %}" * 300,
+    ]
+    for t in deep:
+        with pytest.raises(yl.YlError) as ei:
+            yl.render_chat_template(t, msgs, True)
+        assert ei.value.code == FORMAT
+        assert "too deep" in str(ei.value)  # the message reaches the calling thread
+    # well inside the limits
+    assert yl.render_chat_template("{{ " + "(" * 150 + "1" + ")" * 150 + " }}", msgs, True) == "1"
+    assert yl.render_chat_template("{% if true %}" * 150 + "x" + "{% endif %}" * 150, msgs, True) == "x"
+    assert yl.render_chat_template("{{ " + " ~ ".join(["'a'"] * 900) + " }}", msgs, True) == "a" * 900
+
+
+def test_render_on_a_small_thread_stack(tmp_path):
+    """Parsing and rendering run on a thread of their own: templates at the
+    nesting limits render from a caller thread with a 128 KiB stack."""
+    import subprocess
+    import sys
+    from pathlib import Path
+    script = tmp_path / "small_stack.py"
+    script.write_text(f"""
+import sys, threading
+sys.path.insert(0, {str(Path(__file__).parent)!r})
+from conftest import load_package
+yl = load_package()
+threading.stack_size(128 * 1024)
+m = [("user", "hi")]
+T = ["{{{{ " + "(" * 249 + "1" + ")" * 249 + " }}}}",
+     "{{{{ " + " ~ ".join(["'a'"] * 999) + " }}}}",
+     "{{% if true %}}" * 200 + "x" + "{{% endif %}}" * 200,
+     "{{{{ 'a'" + " | trim" * 999 + " }}}}"]
+out = []
+t = threading.Thread(target=lambda: out.extend(len(yl.render_chat_template(x, m, True)) for x in T))
+t.start()
+t.join()
+print(out)
+""")
+    r = subprocess.run([sys.executable, str(script)], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, r.stderr[-2000:]
+    assert r.stdout.strip() == "[1, 999, 1, 1]"
+
+
 def test_render_rejects_non_utf8_message(yl):
     import ctypes as C
     lib = yl.raw_lib()

@@ -24,6 +24,8 @@
 // YL_ERR_UNSUPPORTED.
 #include "chat_template.h"
 
+#include <pthread.h>
+
 #include <algorithm>
 #include <cctype>
 #include <climits>
@@ -332,6 +334,13 @@ std::vector<Tk> lex(const std::string& s) {
 // Jinja's expression grammar, loosest binding first: `x if c else y`, or,
 // and, not, comparisons / in / not in, + -, ~, * / // %, **, unary minus,
 // then a primary with its postfix subscripts and calls, filters and tests.
+// Nesting limits keep the recursive parser, evaluator and block runner
+// within about 1 MiB of stack whatever the template holds (they run on a
+// thread of their own with 8 MiB, run_on_own_stack).
+constexpr int kMaxNest = 500;     // nested sub-expressions (a parenthesised level counts two)
+constexpr int kMaxEval = 1000;    // expression tree depth when evaluated (long filter or operator chains)
+constexpr int kMaxBlocks = 200;   // nested for / if blocks
+
 class Parser {
  public:
   explicit Parser(std::vector<Tk> t) : t_(std::move(t)) {}
@@ -360,6 +369,14 @@ class Parser {
  private:
   std::vector<Tk> t_;
   size_t p_ = 0;
+  int depth_ = 0;
+  struct Nest {
+    int* d;
+    explicit Nest(int* depth) : d(depth) {
+      if (++*d > kMaxNest) bad("expression nested too deeply");
+    }
+    ~Nest() { --*d; }
+  };
 
   ExprP bin(const std::string& o, ExprP l, ExprP r) {
     auto e = mk(Expr::BIN);
@@ -368,6 +385,7 @@ class Parser {
     return e;
   }
   ExprP cond_() {
+    Nest guard(&depth_);
     ExprP e = or_();
     while (kw("if")) {
       ++p_;
@@ -392,6 +410,7 @@ class Parser {
   }
   ExprP not_() {
     if (kw("not")) {
+      Nest guard(&depth_);
       ++p_;
       auto e = mk(Expr::NOT);
       e->a = {not_()};
@@ -431,6 +450,7 @@ class Parser {
     return e;
   }
   ExprP unary_(bool with_filter) {
+    Nest guard(&depth_);
     ExprP e;
     if (op("-")) {
       ++p_;
@@ -693,7 +713,8 @@ std::vector<Piece> split_template(std::string src) {
 // keyword met ("" at the end of the pieces) and hands its statement's parser
 // to *stop_p.
 std::string parse_body(const std::vector<Piece>& ps, size_t* i, const std::vector<std::string>& stops, Body* body,
-                       std::unique_ptr<Parser>* stop_p) {
+                       std::unique_ptr<Parser>* stop_p, int depth = 0) {
+  if (depth > kMaxBlocks) bad("blocks nested too deeply");
   static const char* kUnsupported[] = {"macro", "endmacro", "call", "endcall", "filter", "endfilter", "with",
                                        "endwith", "raw", "endraw", "include", "import", "from", "extends", "block",
                                        "endblock", "autoescape", "endautoescape", "do", "break", "continue",
@@ -735,9 +756,10 @@ std::string parse_body(const std::vector<Piece>& ps, size_t* i, const std::vecto
       if (P.kw("if")) { P.skip(); n->filter = P.expr(); }
       if (P.kw("recursive")) unsup("recursive loops");
       P.end();
-      const std::string w = parse_body(ps, i, {"endfor", "else"}, &n->body, nullptr);
+      const std::string w = parse_body(ps, i, {"endfor", "else"}, &n->body, nullptr, depth + 1);
       if (w.empty()) bad("missing endfor");
-      if (w == "else" && parse_body(ps, i, {"endfor"}, &n->else_body, nullptr) != "endfor") bad("missing endfor");
+      if (w == "else" && parse_body(ps, i, {"endfor"}, &n->else_body, nullptr, depth + 1) != "endfor")
+        bad("missing endfor");
     } else if (word == "if") {
       n->k = Node::IF;
       ExprP cond = P.expr();
@@ -745,14 +767,14 @@ std::string parse_body(const std::vector<Piece>& ps, size_t* i, const std::vecto
       for (;;) {
         Body b;
         std::unique_ptr<Parser> sp;
-        const std::string w = parse_body(ps, i, {"elif", "else", "endif"}, &b, &sp);
+        const std::string w = parse_body(ps, i, {"elif", "else", "endif"}, &b, &sp, depth + 1);
         if (w.empty()) bad("missing endif");
         n->branches.push_back({cond, std::move(b)});
         if (w == "endif") { sp->end(); break; }
         if (w == "elif") { cond = sp->expr(); sp->end(); continue; }
         sp->end();
         Body eb;
-        if (parse_body(ps, i, {"endif"}, &eb, nullptr) != "endif") bad("missing endif");
+        if (parse_body(ps, i, {"endif"}, &eb, nullptr, depth + 1) != "endif") bad("missing endif");
         n->branches.push_back({nullptr, std::move(eb)});
         break;
       }
@@ -786,6 +808,7 @@ std::string parse_body(const std::vector<Piece>& ps, size_t* i, const std::vecto
 
 struct Ctx {
   std::vector<std::unordered_map<std::string, Val>> frames;
+  int depth = 0;  // eval recursion
   Val lookup(const std::string& n) const {
     for (auto it = frames.rbegin(); it != frames.rend(); ++it) {
       auto f = it->find(n);
@@ -1147,7 +1170,16 @@ Val call(const Expr& e, Ctx& c) {
   bad("value is not callable");
 }
 
+Val eval_node(const Expr& e, Ctx& c);
+
 Val eval(const Expr& e, Ctx& c) {
+  if (++c.depth > kMaxEval) bad("expression too deep to evaluate");
+  Val v = eval_node(e, c);
+  --c.depth;
+  return v;
+}
+
+Val eval_node(const Expr& e, Ctx& c) {
   switch (e.k) {
     case Expr::CONST: return e.c;
     case Expr::NAME: return c.lookup(e.name);
@@ -1307,47 +1339,80 @@ struct ChatTemplate {
   Body body;
 };
 
+namespace {
+
+// Runs body (which throws TplError / bad_alloc on failure) on a thread with
+// an 8 MiB stack, so the nesting limits above hold whatever stack the
+// caller's thread has, and reports the outcome on the caller's thread (the
+// last-error message is thread-local).
+template <class Body>
+int run_on_own_stack(Body&& body) {
+  struct Job {
+    Body* body = nullptr;
+    int code = YL_OK;
+    std::string msg;
+  } job;
+  job.body = &body;
+  auto work = [](void* p) -> void* {
+    Job* j = static_cast<Job*>(p);
+    try {
+      (*j->body)();
+    } catch (const TplError& e) {
+      j->code = e.code;
+      j->msg = std::string("chat template: ") + e.what();
+    } catch (const std::bad_alloc&) {
+      j->code = YL_ERR_OOM;
+      j->msg = "chat template: out of memory";
+    }
+    return nullptr;
+  };
+  pthread_attr_t attr;
+  pthread_t th;
+  bool started = pthread_attr_init(&attr) == 0;
+  if (started) {
+    started = pthread_attr_setstacksize(&attr, 8u << 20) == 0 && pthread_create(&th, &attr, work, &job) == 0;
+    pthread_attr_destroy(&attr);
+  }
+  if (!started) return fail(YL_ERR_OOM, "chat template: cannot start the rendering thread");
+  pthread_join(th, nullptr);
+  return job.code == YL_OK ? YL_OK : fail(job.code, job.msg);
+}
+
+}  // namespace
+
 int chat_template_parse(const std::string& src, std::shared_ptr<const ChatTemplate>* out) {
-  try {
-    std::vector<uint32_t> cps;
-    if (!utf8_code_points(src, &cps, nullptr)) return fail(YL_ERR_FORMAT, "chat template: not UTF-8");
-    auto t = std::make_shared<ChatTemplate>();
+  std::vector<uint32_t> cps;
+  if (!utf8_code_points(src, &cps, nullptr)) return fail(YL_ERR_FORMAT, "chat template: not UTF-8");
+  auto t = std::make_shared<ChatTemplate>();
+  const int rc = run_on_own_stack([&] {
     const std::vector<Piece> ps = split_template(src);
     size_t i = 0;
     parse_body(ps, &i, {}, &t->body, nullptr);
-    *out = t;
-  } catch (const TplError& e) {
-    return fail(e.code, std::string("chat template: ") + e.what());
-  } catch (const std::bad_alloc&) {
-    return fail(YL_ERR_OOM, "chat template: out of memory");
-  }
-  return YL_OK;
+  });
+  if (rc == YL_OK) *out = t;
+  return rc;
 }
 
 int chat_template_render(const ChatTemplate& t, const ChatMessages& messages, bool add_generation_prompt,
                          std::string* out) {
-  try {
+  for (const auto& m : messages) {
+    std::vector<uint32_t> cps;
+    if (!utf8_code_points(m.first, &cps, nullptr) || !utf8_code_points(m.second, &cps, nullptr))
+      return fail(YL_ERR_ARG, "chat message is not UTF-8");
+  }
+  std::string r;
+  const int rc = run_on_own_stack([&] {
     ValList msgs;
-    for (const auto& m : messages) {
-      std::vector<uint32_t> cps;
-      if (!utf8_code_points(m.first, &cps, nullptr) || !utf8_code_points(m.second, &cps, nullptr))
-        return fail(YL_ERR_ARG, "chat message is not UTF-8");
-      // serde_json's map keeps its keys sorted: content before role
+    for (const auto& m : messages)  // serde_json's map keeps its keys sorted: content before role
       msgs.push_back(v_map({{"content", v_str(m.second)}, {"role", v_str(m.first)}}));
-    }
     Ctx c;
     c.frames.emplace_back();
     c.frames.back()["messages"] = v_list(std::move(msgs));
     c.frames.back()["add_generation_prompt"] = v_bool(add_generation_prompt);
-    std::string r;
     exec(t.body, c, &r);
-    *out = std::move(r);
-  } catch (const TplError& e) {
-    return fail(e.code, std::string("chat template: ") + e.what());
-  } catch (const std::bad_alloc&) {
-    return fail(YL_ERR_OOM, "chat template: out of memory");
-  }
-  return YL_OK;
+  });
+  if (rc == YL_OK) *out = std::move(r);
+  return rc;
 }
 
 }  // namespace yl

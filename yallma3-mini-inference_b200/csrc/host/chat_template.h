@@ -13,6 +13,11 @@ namespace yl {
 struct ChatTemplate;                                                   // a parsed template
 using ChatMessages = std::vector<std::pair<std::string, std::string>>;  // (role, content)
 
+// Both calls run on an internal thread with an 8 MiB stack (the caller's
+// stack size does not matter) and bound nesting: more than ~250 nested
+// parentheses, expressions deeper than 1000 nodes or blocks nested more than
+// 200 deep give YL_ERR_FORMAT; YL_ERR_OOM if the thread cannot start.
+
 // Parses a template (Environment::add_template_owned, tokenizer.rs:411-413).
 // YL_ERR_FORMAT for a syntax error (where minijinja rejects the template),
 // YL_ERR_UNSUPPORTED for a statement this renderer does not implement.
