@@ -354,7 +354,7 @@ def sweep_case(yl, torch, rng) -> None:
                 print(json.dumps({"case": "sweep", "M": m, "K": k, "fmt": name, "N": n, "us": t * 1e6,
                                   "gbs": gbs, "hbm_frac": gbs / hbm if hbm else None,
                                   "tops": 2.0 * m * k * n / t * 1e-12,
-                                  "path": "gemm" if n >= 16 and name != "F16" else "matvec"}), flush=True)
+                                  "path": "gemm" if n >= 16 else "matvec"}), flush=True)
                 del xa, out
             del w
             torch.cuda.synchronize()

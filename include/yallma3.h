@@ -125,9 +125,11 @@ int yl_quantize(int fmt, yl_qtensor* dst, const float* x, uint64_t n, uint32_t g
  * accumulate = 0 the results equal the reference's bit for bit. With
  * accumulate = 1 a quad column gets its initial value plus the folded row
  * (the reference adds every block term into the initial value in turn):
- * within 1e-5 of the sum of |terms| and |initial value|. F16 weights run on
- * the matvec with f32 products summed in lane-parallel order (within 1e-5 of
- * the sum of |terms|). */
+ * within 1e-5 of the sum of |terms| and |initial value|. F16 weights: below
+ * 16 rows the matvec with f32 products summed in lane-parallel order; from 16
+ * rows the f16 tensor-core GEMM on the activations split into two f16 parts
+ * (stream-ordered scratch of 4 bytes per activation element; the matvec when
+ * it cannot be had). Both within 1e-5 of the sum of |terms|. */
 int yl_matmul(float* out, const yl_qtensor* x, const yl_qtensor* w, uint64_t n, uint64_t o, uint64_t gs,
               uint64_t batch, int accumulate, void* stream);
 
@@ -211,6 +213,8 @@ int yl_batch_forward(yl_batch* b, yl_session* const* sessions, uint32_t n, const
  *  "gemm_tc"     1 = Q8_0 batches on the tcgen05 / tensor-memory kernel
  *                (bit-identical, not faster; default 0, env YL_GEMM_TC)
  *  "gemm_tc_min" token count from which gemm_tc applies (default 96)
+ *  "gemm_f16_min" F16 passes of this many tokens on the f16 tensor-core GEMM
+ *                (default 16, env YL_GEMM_F16_MIN; 0 = the matvec at every N)
  * YL_ERR_ARG for an unknown key. */
 int yl_config_set(const char* key, int64_t value);
 

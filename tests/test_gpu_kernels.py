@@ -181,7 +181,7 @@ def test_sweep_vs_oracle(yl, orc, torch_cuda, mk, batch, fmt):
 
 
 @pytest.mark.parametrize("mk", [(2048, 2048), (1000, 4096)])
-@pytest.mark.parametrize("batch", [1, 5])
+@pytest.mark.parametrize("batch", [1, 5, 16, 33, 64])  # 16+: the f16 tensor-core GEMM (all three tiles)
 def test_f16_vs_oracle(yl, orc, torch_cuda, mk, batch):
     o, n = mk
     rng = np.random.default_rng(o + n + batch)
@@ -194,6 +194,30 @@ def test_f16_vs_oracle(yl, orc, torch_cuda, mk, batch):
     orc.matmul_f32(ref, x, wv, n, o)
     bound = (np.abs(x.reshape(batch, 1, n)) * np.abs(wv.reshape(1, o, n))).sum(axis=2).reshape(-1)
     assert np.all(np.abs(got - ref) <= 1e-5 * bound + 1e-30)
+
+
+@pytest.mark.parametrize("batch", [16, 40])
+def test_f16_gemm_matches_matvec_accumulate(yl, torch_cuda, batch):
+    """yl_matmul(accumulate) on F16: the tensor-core GEMM (16+ rows) and the
+    matvec (gemm_f16_min 0) give the same results within the F16 bound, quad
+    columns added and the tail stored alike."""
+    o, n = 1030, 1024
+    rng = np.random.default_rng(batch)
+    wv = (rng.standard_normal(o * n) * 0.02).astype(np.float16).astype(np.float32)
+    x = (rng.standard_normal(batch * n) * 30).astype(np.float32)
+    init = rng.standard_normal(batch * o).astype(np.float32)
+    w = upload_weight(yl, yl.WeightFormat.F16, None, None, o, n, values=wv)
+    xa = upload_act(yl, yl.WeightFormat.F16, None, None, values=x)
+    got = run_matmul(yl, torch_cuda, xa, w, n, o, batch, init=init, accumulate=True)
+    yl.config_set("gemm_f16_min", 0)
+    try:
+        mv = run_matmul(yl, torch_cuda, xa, w, n, o, batch, init=init, accumulate=True)
+    finally:
+        yl.config_set("gemm_f16_min", 16)
+    bound = (np.abs(x.reshape(batch, 1, n)) * np.abs(wv.reshape(1, o, n))).sum(axis=2).reshape(-1)
+    assert np.all(np.abs(got - mv) <= 2e-5 * bound + 1e-6)
+    tail = (np.arange(batch * o) % o) >= o // 4 * 4  # stored, not added (weight_type.rs:207-224)
+    assert np.all(np.abs(got[tail] - mv[tail]) <= 2e-5 * bound[tail])
 
 
 def test_f32_weight_scales(yl, orc, torch_cuda):

@@ -171,7 +171,7 @@ def last_error() -> str:
 
 
 def config_set(key: str, value: int) -> None:
-    """Process-wide device-path option (yl_config_set): gemm, gemm_tc, gemm_tc_min."""
+    """Process-wide device-path option (yl_config_set): gemm, gemm_tc, gemm_tc_min, gemm_f16_min."""
     _check(_lib.yl_config_set(key.encode(), int(value)))
 
 

@@ -223,6 +223,31 @@ int yl_quantize(int fmt, yl_qtensor* dst, const float* x, uint64_t n, uint32_t g
   return yl_quantize_q8_0(x, (int8_t*)dst->quant, (float*)dst->scale, n, gs, stream);
 }
 
+// The library's own stream-ordered memory pool per device (yl_matmul's F16
+// scratch): it keeps freed blocks (no release threshold), so repeated calls
+// reuse them instead of mapping memory every time. Null if it cannot be made.
+static cudaMemPool_t scratch_pool(int dev) {
+  static std::mutex mu;
+  static std::vector<std::pair<int, cudaMemPool_t>> pools;
+  std::lock_guard<std::mutex> lk(mu);
+  for (const auto& p : pools)
+    if (p.first == dev) return p.second;
+  cudaMemPoolProps props = {};
+  props.allocType = cudaMemAllocationTypePinned;
+  props.location.type = cudaMemLocationTypeDevice;
+  props.location.id = dev;
+  cudaMemPool_t pool = nullptr;
+  if (cudaMemPoolCreate(&pool, &props) == cudaSuccess) {
+    uint64_t keep = UINT64_MAX;
+    cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+  } else {
+    (void)cudaGetLastError();
+    pool = nullptr;
+  }
+  pools.push_back({dev, pool});
+  return pool;
+}
+
 int yl_matmul(float* out, const yl_qtensor* x, const yl_qtensor* w, uint64_t n, uint64_t o, uint64_t gs,
               uint64_t batch, int accumulate, void* stream) {
   if (!out || !x || !w) return fail(YL_ERR_ARG, "null pointer");
@@ -247,10 +272,25 @@ int yl_matmul(float* out, const yl_qtensor* x, const yl_qtensor* w, uint64_t n, 
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  return run_matvec(dw, f32act, f32act ? nullptr : (const int8_t*)x->quant, f32act ? nullptr : (const float*)x->scale,
-                    f32act ? (const float*)x->quant : nullptr, n, n / 32, (uint32_t)batch, out, o,
-                    accumulate ? k::EPI_QUIRK : k::EPI_STORE, (uint32_t)(o / 4 * 4), nullptr, (cudaStream_t)stream,
-                    false, sms);
+  cudaStream_t st = (cudaStream_t)stream;
+  MvExtra ex;
+  // F16 batches for the f16 tensor-core GEMM: its split rows in stream-ordered
+  // scratch from the library's pool (without it, the matvec runs)
+  const Tunables& tu = tunables();
+  if (f32act && tu.gemm && tu.gemm_f16_min && batch >= tu.gemm_f16_min && batch <= 0xFFFFFFFFull) {
+    cudaMemPool_t pool = scratch_pool(dev);
+    if (!pool || cudaMallocFromPoolAsync(&ex.f16ws, k::gemm_f16_workspace_bytes((uint32_t)batch, (uint32_t)n), pool,
+                                         st) != cudaSuccess) {
+      (void)cudaGetLastError();
+      ex.f16ws = nullptr;
+    }
+  }
+  const int rc = run_matvec_ex(dw, f32act, f32act ? nullptr : (const int8_t*)x->quant,
+                               f32act ? nullptr : (const float*)x->scale, f32act ? (const float*)x->quant : nullptr, n,
+                               n / 32, (uint32_t)batch, out, o, accumulate ? k::EPI_QUIRK : k::EPI_STORE,
+                               (uint32_t)(o / 4 * 4), nullptr, st, false, sms, ex, nullptr);
+  if (ex.f16ws) cudaFreeAsync(ex.f16ws, st);
+  return rc;
 }
 
 }  // extern "C"

@@ -138,6 +138,7 @@ Tunables& tunables_mut() {
     if (const char* e = getenv("YL_GEMM_MIN")) x.gemm_min = (uint32_t)std::max(2, atoi(e));
     if (const char* e = getenv("YL_GEMM_TC")) x.gemm_tc = atoi(e) != 0;
     if (const char* e = getenv("YL_GEMM_TC_MIN")) x.gemm_tc_min = (uint32_t)std::max(1, atoi(e));
+    if (const char* e = getenv("YL_GEMM_F16_MIN")) x.gemm_f16_min = (uint32_t)std::max(0, atoi(e));
     if (const char* e = getenv("YL_PF_MB")) x.pf_bytes = (uint64_t)std::max(0, atoi(e)) << 20;
     return x;
   }();
@@ -152,6 +153,7 @@ int set_tunable(const std::string& key, int64_t value) {
   if (key == "gemm_tc") t.gemm_tc = value != 0;
   else if (key == "gemm_tc_min") t.gemm_tc_min = (uint32_t)std::max<int64_t>(1, value);
   else if (key == "gemm") t.gemm = value != 0;
+  else if (key == "gemm_f16_min") t.gemm_f16_min = (uint32_t)std::max<int64_t>(0, value);
   else return fail(YL_ERR_ARG, "unknown option " + key);
   return YL_OK;
 }
@@ -405,6 +407,10 @@ int ensure_cap(Session* s, uint32_t n) {
   YL_CUDA_TRY(cudaMemset(s->hcount, 0, cap * (uint64_t)(sh.hidden_dim / 32) * 4ull));
   if ((rc = salloc(s, cap * 4ull, &p))) return rc;
   s->tok = (uint32_t*)p;
+  if (sh.weight_format == YL_F16 && s->m->tp_size == 1) {
+    if ((rc = salloc(s, k::gemm_f16_workspace_bytes(cap, (uint32_t)wmax), &p))) return rc;
+    s->f16ws = p;
+  }
   s->cap = cap;
   return YL_OK;
 }
@@ -567,6 +573,33 @@ int run_matvec_ex(const DevWeight& w, bool f32act, const int8_t* xq, const float
   lc.pdl = pdl;
   lc.grid = (uint32_t)num_sms * tu.grid_mult;
   lc.smem_budget = tu.smem;
+  // several tokens of an F16 model: the f16 tensor-core GEMM, its activation
+  // split (with the RMSNorm prologue) as a separate kernel
+  if (f32act && fmt == k::FMT_F16 && tu.gemm && tu.gemm_f16_min && ntok >= tu.gemm_f16_min && ex.tp_mode == 0 &&
+      ex.f16ws && (ex.pro == k::PRO_LOAD || (ex.pro == k::PRO_NORM && ex.xres && ex.norm_w))) {
+    k::GemmF16Args g{};
+    g.w = w.q;
+    g.rows = w.rows;
+    g.K = w.cols;
+    g.row_bytes = w.row_bytes;
+    g.x = ex.pro == k::PRO_NORM ? ex.xres : xf;
+    g.x_stride = x_stride;
+    g.norm_w = ex.pro == k::PRO_NORM ? ex.norm_w : nullptr;
+    g.eps = ex.eps;
+    g.ntok = ntok;
+    g.hi = static_cast<uint16_t*>(ex.f16ws);
+    g.lo = g.hi + (uint64_t)ntok * w.cols;
+    g.exps = reinterpret_cast<int*>(g.lo + (uint64_t)ntok * w.cols);
+    g.out = out;
+    g.out_stride = out_stride;
+    g.quirk_cols = quirk_cols;
+    if (k::gemm_f16_supported(g, epi)) {
+      cudaError_t e = k::gemm_f16(g, epi, lc);
+      if (e != cudaSuccess) return fail(YL_ERR_CUDA, std::string("f16 gemm launch: ") + cudaGetErrorString(e));
+      if (launches) *launches += 2;
+      return YL_OK;
+    }
+  }
   // several tokens with int8 activations: the tensor-core GEMM (weights read
   // once per 64 tokens), with the RMSNorm prologue as a separate kernel
   if (!f32act && tu.gemm && ntok >= tu.gemm_min && ex.tp_mode == 0 && (fmt == k::FMT_Q8 || fmt == k::FMT_Q4) &&
@@ -758,6 +791,8 @@ int enqueue_forward(Session* s, uint32_t n, uint32_t start_pos, bool from_state,
   norm.eps = sh.rms_norm_eps;
   norm.gq = decode ? nullptr : s->xq;  // multi-token passes: normalized rows for the GEMM
   norm.gs = decode ? nullptr : s->xs;
+  norm.f16ws = decode ? nullptr : s->f16ws;  // F16 models: split rows for the f16 GEMM
+  plain.f16ws = norm.f16ws;
   // Tensor-parallel single-token steps: wo and down push their partial rows
   // into every rank's inbox in their epilogue, and the next RMSNorm prologue
   // all-reduces them into the residual, which alternates between two rows
@@ -1060,6 +1095,8 @@ int forward_batch(Batch* b, Session* const* ss, uint32_t n, const uint32_t* toke
   norm.eps = sh.rms_norm_eps;
   norm.gq = w->xq;  // 16+ rows: normalized rows for the GEMM
   norm.gs = w->xs;
+  norm.f16ws = w->f16ws;
+  plain.f16ws = w->f16ws;
   for (uint32_t l = 0; l < sh.n_layers; ++l) {
     const Layer& L = m->layers[l];
     // attention block: the stacked rows' projections, then every session's

@@ -79,6 +79,7 @@ struct Session {
   float* hs = nullptr;    // [cap][ffn/32]
   unsigned int* hcount = nullptr;  // [cap][ffn/32] arrival counters (zero between launches)
   unsigned int* work = nullptr;    // [n_layers + 1][2] dynamic row-set counters (decode gate/up, lm_head)
+  void* f16ws = nullptr;  // F16 models: the f16 GEMM's split rows for cap tokens (single-GPU models)
   uint32_t* tok = nullptr;  // [cap]
   float* logits = nullptr;  // [vocab]
   float* part = nullptr;    // decode attention scores / weights [local heads][part_stride]
@@ -165,6 +166,9 @@ struct Tunables {
   // bound by the exact per-block fold on the FP32 pipe, not by the tensor core).
   bool gemm_tc = false;
   uint32_t gemm_tc_min = 96;
+  // F16 passes of this many tokens on the f16 tensor-core GEMM (YL_GEMM_F16_MIN;
+  // 0 turns it off; the matvec below)
+  uint32_t gemm_f16_min = 16;
   bool tp_fused = true;      // tensor-parallel decode: exchange fused into the projections (else exchange kernels)
   // decode: L2 prefetch of the next matrix's first bytes per launch (YL_PF_MB).
   // Off: measured slower at every size tried (16, 32, 48 MB).
@@ -190,7 +194,7 @@ int batch_create(const Model* m, uint32_t cap, Batch** out);
 int forward_batch(Batch* b, Session* const* ss, uint32_t n, const uint32_t* tokens, const uint32_t* pos);
 
 const Tunables& tunables();
-// Runtime override of a tunable (yl_config_set): gemm, gemm_tc, gemm_tc_min.
+// Runtime override of a tunable (yl_config_set): gemm, gemm_tc, gemm_tc_min, gemm_f16_min.
 int set_tunable(const std::string& key, int64_t value);
 // Launches the matvec for `ntok` tokens (groups of 8) with activations x*.
 int run_matvec(const DevWeight& w, bool f32act, const int8_t* xq, const float* xs, const float* xf,
@@ -224,6 +228,9 @@ struct MvExtra {
   uint32_t tp_site = 0, tp_nsites = 0;
   float* tp_xout = nullptr;
   k::L2Prefetch pf;              // the next weight-streaming launch's first rows (decode)
+  // F16 multi-token passes: workspace of the f16 tensor-core GEMM, at least
+  // gemm_f16_workspace_bytes(ntok, K) (nullable: the matvec runs instead)
+  void* f16ws = nullptr;
 };
 int run_matvec_ex(const DevWeight& w, bool f32act, const int8_t* xq, const float* xs, const float* xf,
                   uint64_t x_stride, uint64_t xs_stride, uint32_t ntok, float* out, uint64_t out_stride, int epi,

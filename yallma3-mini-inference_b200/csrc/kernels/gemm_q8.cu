@@ -21,6 +21,7 @@
 // holds both values of a pair; a CTA's 64 h values per token are two whole
 // quantization blocks, quantized by the bit-exact warp quantizer.
 #include "device.cuh"
+#include "gemm_util.cuh"
 #include "kernels.h"
 
 namespace yl {
@@ -28,6 +29,7 @@ namespace k {
 using namespace yl::dev;
 
 namespace {
+using namespace gu;
 constexpr int GB_M = 128, GB_N = 64, GB_KB = 4, GB_S = 3;
 
 template <int FMT, int BN, int BM = 128>
@@ -47,44 +49,10 @@ static_assert(GTile<FMT_Q8, 32>::STAGE % 16 == 0 && GTile<FMT_Q4, 32>::STAGE % 1
 static_assert(32 * GB_M / 2 * 4 <= GTile<FMT_Q4, 32>::SMEM && GB_N * GB_M / 2 * 4 <= GTile<FMT_Q4, 64>::SMEM,
               "SwiGLU staging fits the ring");
 
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-
 __device__ __forceinline__ void mma_s8(int (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
   asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
       : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]), "r"(0));
-}
-
-// ldmatrix: four (two) 8x8 tiles of 16-bit elements; for int8 data a lane
-// receives 4 consecutive bytes of row lane/4 at byte (lane%4)*4 of each tile,
-// which is the m16n8k32 s8 fragment layout.
-__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(smem_u32(p)));
-}
-__device__ __forceinline__ void ldsm_x2(uint32_t& r0, uint32_t& r1, const void* p) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(smem_u32(p)));
-}
-
-// Shared-memory row of weight row i of the tile: with PERM, in each aligned
-// group of 16 rows the even rows (gate) go to the first 8 slots and the odd
-// rows (up) to the last 8, in order.
-template <bool PERM>
-__device__ __forceinline__ uint32_t tile_row(uint32_t i) {
-  if (!PERM) return i;
-  const uint32_t w = i & 15u;
-  return (i & ~15u) + (w >> 1) + ((w & 1u) << 3);
 }
 
 template <int FMT, bool SF16, bool PERM, int BN, int BM, int NTH>

@@ -198,6 +198,37 @@ cudaError_t gemm_q(const GemmArgs& a, int fmt, bool scale_f16, int epi, const La
 bool gemm_tc_supported(const GemmArgs& a, int fmt, bool scale_f16, int epi);
 cudaError_t gemm_tc(const GemmArgs& a, bool scale_f16, int epi, const LaunchCfg& lc);
 
+// Multi-token F16 projections on the tensor cores (matmul_f32,
+// weight_type.rs:228-270: out[t][r] = sum_k (f32)w[r][k] * x[t][k]). f16_split
+// writes each token's f32 row (or its RMSNorm, norm_w non-null, computed as
+// the matvec prologue computes it) as x * 2^e = hi + lo, two f16 rows, with e
+// the power of two that puts the row's max |x| in [2^14, 2^15); the GEMM runs
+// mma.sync m16n8k16 (f16 x f16 -> f32) on w*hi and w*lo into one f32
+// accumulator and scales by 2^-e. Epilogues: EPI_STORE, EPI_ADD, EPI_QUIRK,
+// EPI_SWIGLU (interleaved gate/up rows, f32 h [ntok][rows/2]).
+struct GemmF16Args {
+  const uint8_t* w;          // f16 weight rows
+  uint32_t rows, K, row_bytes;
+  const float* x;            // f32 activation rows (the residual rows when norm_w is set)
+  uint64_t x_stride;         // floats per token row
+  const float* norm_w;       // nullable: RMSNorm weights
+  float eps;
+  uint32_t ntok;
+  uint16_t* hi;              // workspace [ntok][K] f16 each
+  uint16_t* lo;
+  int* exps;                 // workspace [ntok]
+  float* out;
+  uint64_t out_stride;
+  uint32_t quirk_cols;
+};
+// Workspace bytes of a pass: hi and lo rows plus the exponents.
+inline uint64_t gemm_f16_workspace_bytes(uint32_t ntok, uint32_t K) {
+  return (uint64_t)ntok * K * 4 + (uint64_t)ntok * 4 + 256;
+}
+bool gemm_f16_supported(const GemmF16Args& a, int epi);
+// f16_split then the GEMM: two launches.
+cudaError_t gemm_f16(const GemmF16Args& a, int epi, const LaunchCfg& lc);
+
 // ---- activations ------------------------------------------------------------
 // Bit-exact Q8_0 quantization of nblocks 32-element blocks (warp per block).
 cudaError_t quantize_q8(const float* x, int8_t* q, float* s, uint64_t nblocks, const LaunchCfg& lc);
