@@ -127,10 +127,11 @@ def test_tiny_models_match_oracle(yl, orc, model_factory, preset, over):
     ("tiny", {"weight_format": 2, "llama3_scaling": True, "rope_theta": 5e5, "context_length": 131072}),
 ])
 def test_gemm_prefill_matches_oracle(yl, orc, model_factory, preset, over):
-    """A 70-token prompt: every projection of the prefill runs on the int8
-    tensor-core GEMM (two token tiles, the second partial; RMSNorm as its own
-    kernel; SwiGLU + h quantization in the gate/up epilogue), then greedy
-    decode on the matvec path."""
+    """A 70-token prompt: every projection of the prefill runs on a
+    tensor-core GEMM (two token tiles, the second partial): the int8 GEMM for
+    Q8_0 (RMSNorm + quantize as its own kernel; SwiGLU + h quantization in the
+    gate/up epilogue), the f16 GEMM for F16 (RMSNorm + hi/lo split as its own
+    kernel; SwiGLU in the epilogue); then greedy decode on the matvec path."""
     path = model_factory(preset, **over)
     vocab = yl.PRESETS[preset]["vocab_size"]
     prompt = yl.prompt_ids(vocab, 70, 99).tolist()
