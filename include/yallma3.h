@@ -351,14 +351,16 @@ bool load_transformer_ffi(const char* model_path);
 /* infer_ffi / free_string as the reference documents them (README.md:88-92,
  * PoC_Bun_load.js:12-38; the reference declares but never implements them).
  * infer_ffi runs one fresh conversation on the model load_transformer_ffi
- * loaded, the way the reference's console does (main.rs:149-214): the prompt
- * is tokenized with the model's tokenizer into the no-template chat format
- * (empty system prompt, the user turn, an empty assistant header), prefilled,
+ * loaded, the way the reference's console does (main.rs:149-214): the prompt,
+ * trimmed of Unicode white space at both ends as the console trims its line,
+ * is tokenized with the model's tokenizer into the chat prompt of
+ * yl_tokenizer_chat_prompt with an empty system prompt (the GGUF file's chat
+ * template when it has one, else the built-in format), prefilled,
  * and tokens are sampled on the device and decoded one at a time until EOS,
  * the context length or the token limit. The reply (the decoded pieces
  * concatenated, each piece decoded on its own as the console prints it) is
  * returned as a malloc'ed UTF-8 string to be released with free_string.
- * NULL on any error (no model loaded, empty or non-UTF-8 prompt, prompt longer
+ * NULL on any error (no model loaded, empty (after trimming) or non-UTF-8 prompt, prompt longer
  * than the context; yl_last_error() says which). Calls are serialized by a
  * mutex; the session and the sampler persist across calls like the console's
  * (the session is reset at each call, the sampler keeps its state). */

@@ -112,6 +112,9 @@ def test_infer_ffi_matches_console_loop(yl, torch_cuda, chat_models, kind):
         want, _, _ = host_console_loop(yl, path, prompt, temp, top_p, 42, 24)
         assert got == want, (kind, prompt, got, want)
     assert yl.infer_ffi("") is None  # empty prompt: NULL, no abort
+    assert yl.infer_ffi(" \t\n") is None  # empty once trimmed (the console skips the line)
+    yl.infer_config(0.0, 0.9, 42, 8)  # greedy: the same reply whatever the sampler's state
+    assert yl.infer_ffi(" \thello world\n") == yl.infer_ffi("hello world")  # trimmed as main.rs:173
 
 
 def test_infer_ffi_greedy_matches_oracle(yl, orc, torch_cuda, chat_models):

@@ -801,10 +801,25 @@ int yl_session_logits(const yl_session* s, float** logits) {
   return YL_OK;
 }
 
-// One conversation turn of the console (main.rs:186-214) on the device.
-static int ffi_generate(const char* prompt, std::string* reply) {
+// The prompt as the console takes it: str::trim (Unicode White_Space at both
+// ends, main.rs:165,173); a prompt that is not UTF-8 is left to the
+// tokenizer's error.
+static std::string trim_prompt(const std::string& p) {
+  std::vector<uint32_t> cps;
+  std::vector<size_t> offs;
+  if (!utf8_code_points(p, &cps, &offs)) return p;
+  size_t a = 0, b = cps.size();
+  while (a < b && is_white_space(cps[a])) ++a;
+  while (b > a && is_white_space(cps[b - 1])) --b;
+  return p.substr(offs[a], offs[b] - offs[a]);
+}
+
+// One conversation turn of the console (main.rs:163-214) on the device.
+static int ffi_generate(const char* prompt_in, std::string* reply) {
   if (!g_current) return fail(YL_ERR_ARG, "no model loaded (load_transformer_ffi)");
-  if (!prompt || !*prompt) return fail(YL_ERR_ARG, "empty prompt");
+  if (!prompt_in) return fail(YL_ERR_ARG, "null prompt");
+  const std::string prompt = trim_prompt(prompt_in);
+  if (prompt.empty()) return fail(YL_ERR_ARG, "empty prompt");  // the console skips such a line
   const Model* mm = g_current->m;
   if (mm->tp_size > 1) return fail(YL_ERR_UNSUPPORTED, "infer_ffi runs single-GPU models");
   const yl_tokenizer* tk = nullptr;
