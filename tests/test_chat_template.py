@@ -272,6 +272,22 @@ def test_encode_template_output_longest_match(yl, tmp_path, bpe):
     assert ours.render_chat([], False) == []  # empty render: no ids
 
 
+def test_encode_template_output_fuzz(yl, tmp_path, bpe):
+    """Random texts dense in '<', special-token fragments and near misses:
+    the indexed longest match equals the literal scan of every entry."""
+    import random
+    vocab, merges = bpe
+    extra = ["<|im_start|>", "<|im_end|>", "<|im", "<|", "<s>", "</s>", "<s", "<|im_start|>x", "<|im_end|>"]
+    path = tf.write_gguf_tokenizer(tmp_path / "f.gguf", vocab + extra, merges, 1, 2,
+                                   template="{% for m in messages %}{{ m.content }}{% endfor %}")
+    ours, ref = yl.Tokenizer.load(path), tr.Tokenizer.from_gguf(path)
+    r = random.Random(11)
+    pieces = extra + ["<", "<<", "|", ">", "im", " ", "\n", "hello", "é", "日本", "x", "/s", "s>", "<|im_st"]
+    for _ in range(150):
+        text = "".join(r.choice(pieces) for _ in range(r.randint(1, 14)))
+        assert ours.render_chat([("user", text)], False) == ref.render_chat([("user", text)], False), text
+
+
 def test_template_that_does_not_parse(yl, tmp_path, bpe):
     vocab, merges = bpe
     path = tf.write_gguf_tokenizer(tmp_path / "b.gguf", vocab, merges, 1, 2, template="{% if %}")
