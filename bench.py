@@ -238,10 +238,10 @@ def cpu_model() -> str:
     return "unknown"
 
 
-def cpu_baseline(path: str, n_tokens: int, threads: int, half_threads: int | None = None) -> dict:
+def cpu_baseline(path: str, n_tokens: int, threads: int, half_threads: int | None = None, warmup: int = 1) -> dict:
     """Oracle decode of n_tokens at positions 512.. with a seeded KV prefix,
-    on `threads` host threads; with half_threads also on that many (the
-    reference's default pool, parallelism.rs:59-71)."""
+    after `warmup` untimed steps, on `threads` host threads; with half_threads
+    also on that many (the reference's default pool, parallelism.rs:59-71)."""
     sys.path.insert(0, str(ROOT / "oracle"))
     import pyoracle as orc
     t0 = time.time()
@@ -260,7 +260,8 @@ def cpu_baseline(path: str, n_tokens: int, threads: int, half_threads: int | Non
     def timed(nt: int) -> float:
         orc.set_threads(nt)
         tok = 1
-        m.forward_x([tok], PROMPT_LEN, s)  # warm-up (page-in)
+        for _ in range(max(1, warmup)):  # untimed (page-in, caches)
+            m.forward_x([tok], PROMPT_LEN, s)
         t = time.perf_counter()
         for i in range(n_tokens):
             lg = m.forward_x([tok], PROMPT_LEN + 1 + i, s)
@@ -297,10 +298,11 @@ def run_reference(args) -> None:
     path = cache / "yl_bench_c4_q8_0.gguf"
     write_model_in_subprocess(path)
     steps = max(1, min(args.steps, 8))
+    warmup = max(3, min(args.warmup, 5))  # at least 3 untimed steps; bounded CPU time
     threads = os.cpu_count() or 1
-    cb = cpu_baseline(str(path), steps, threads, half_threads=max(1, -(-threads // 2)))
+    cb = cpu_baseline(str(path), steps, threads, half_threads=max(1, -(-threads // 2)), warmup=warmup)
     line = {"impl": "reference", "metric": "decode tokens/s (Llama-3-8B-shape Q8_0, batch 1)",
-            "value": cb["value"], "unit": "tokens/s", "n_gpus": args.gpus, "steps": steps, "warmup": 1,
+            "value": cb["value"], "unit": "tokens/s", "n_gpus": args.gpus, "steps": steps, "warmup": warmup,
             "ms_per_step": 1000.0 / cb["value"], "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int8 dot / f32 accumulate", "data": "synthetic",
             "config": {"workload": "config 4: Llama-3-8B-shaped Q8_0, prompt 512, batch-1 greedy decode",
