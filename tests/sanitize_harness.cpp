@@ -3,8 +3,11 @@
 // AddressSanitizer and UBSan, run over inputs the test writes.
 //   sanitize_harness templates <file>            templates separated by "\n<<<SEP>>>\n"
 //   sanitize_harness tokenizer <gguf> <file>     texts separated by byte 0x01
+//   sanitize_harness load <file>                 model paths, one per line: tokenizer_load
+//                                                 (errors expected), then one encode
 #include <cstdio>
 #include <cstring>
+#include <exception>
 #include <fstream>
 #include <memory>
 #include <random>
@@ -80,6 +83,30 @@ int main(int argc, char** argv) {
     printf("texts %d ok %d\n", n, ok);
     return 0;
   }
-  fprintf(stderr, "usage: sanitize_harness templates <file> | tokenizer <gguf> <file>\n");
+  if (argc >= 3 && !strcmp(argv[1], "load")) {
+    int n = 0, loaded = 0;
+    for (const std::string& path : split(read_file(argv[2]), "\n")) {
+      if (path.empty()) continue;
+      std::unique_ptr<yl::Tokenizer> t;
+      ++n;
+      try {
+        if (yl::tokenizer_load(path, &t) != 0) continue;
+      } catch (const std::exception& e) {
+        printf("exception escaped tokenizer_load (%s): %s\n", e.what(), path.c_str());
+        return 3;
+      } catch (...) {
+        printf("exception escaped tokenizer_load: %s\n", path.c_str());
+        return 3;
+      }
+      ++loaded;
+      std::vector<uint32_t> ids;
+      yl::tok_encode(*t, "hello world, it's 3.14", true, false, &ids);
+      yl::tok_chat_prompt(*t, "", "hi", &ids);
+      if (!ids.empty()) yl::tok_decode(*t, ids.data(), ids.size());
+    }
+    printf("files %d loaded %d\n", n, loaded);
+    return 0;
+  }
+  fprintf(stderr, "usage: sanitize_harness templates <file> | tokenizer <gguf> <file> | load <file>\n");
   return 2;
 }

@@ -94,3 +94,51 @@ def test_tokenizer_under_sanitizers(harness, tmp_path):
     f.write_bytes(b"\x01".join(texts))
     out = run(harness, "tokenizer", path, f)
     assert int(out.split()[1]) == len(texts)
+
+
+def _mutations(data: bytes, r: random.Random, n: int) -> list:
+    out = []
+    for _ in range(n):
+        b = bytearray(data)
+        op = r.randint(0, 3)
+        if op == 0:  # truncate
+            b = b[:r.randrange(len(b))]
+        elif op == 1:  # flip bytes
+            for _ in range(r.randint(1, 8)):
+                b[r.randrange(len(b))] = r.randrange(256)
+        elif op == 2:  # a huge or off-by-some little-endian length somewhere
+            i = r.randrange(max(1, len(b) - 8))
+            b[i:i + 8] = r.choice([b"\xff" * 8, b"\x00\x00\x00\x80\x00\x00\x00\x00",
+                                   (len(b) + r.randint(-3, 3)).to_bytes(8, "little", signed=True)])
+        else:  # cut a span out
+            i = r.randrange(len(b))
+            del b[i:i + r.randint(1, 64)]
+        out.append(bytes(b))
+    return out
+
+
+def test_tokenizer_files_under_sanitizers(harness, tmp_path):
+    """Corrupted GGUF metadata, tokenizer.json and tokenizer.bin files: every
+    load returns (an error or a tokenizer), nothing reads out of bounds."""
+    vocab, merges = tf.learn_bpe(tf.corpus(7), 200)
+    gguf = Path(tf.write_gguf_tokenizer(tmp_path / "ok.gguf", vocab, merges, 1, 2, template=tct.T_BLOCKS))
+    (tmp_path / "j").mkdir()
+    jpath = Path(tf.write_tokenizer_json(tmp_path / "j" / "tokenizer.json", vocab, merges, {len(vocab): "<|eot_id|>"}))
+    (tmp_path / "b").mkdir()
+    bpath = Path(tf.write_tokenizer_bin_vocab(tmp_path / "b" / "tokenizer.bin", vocab, [0.0] * len(vocab), 1, 2))
+    r = random.Random(21)
+    paths = [gguf]
+    for i, data in enumerate(_mutations(gguf.read_bytes(), r, 300)):
+        p = tmp_path / f"m{i}.gguf"
+        p.write_bytes(data)
+        paths.append(p)
+    for kind, src, name, ext in (("j", jpath, "tokenizer.json", ".safetensors"), ("b", bpath, "tokenizer.bin", ".lmrs")):
+        for i, data in enumerate(_mutations(src.read_bytes(), r, 150)):
+            d = tmp_path / f"{kind}{i}"
+            d.mkdir()
+            (d / name).write_bytes(data)
+            paths.append(d / f"model{ext}")
+    lst = tmp_path / "paths.txt"
+    lst.write_text("\n".join(str(p) for p in paths))
+    out = run(harness, "load", lst)
+    assert int(out.split()[1]) == len(paths) and int(out.split()[3]) >= 1

@@ -266,7 +266,7 @@ int load_gguf_tok(const std::string& path, Tokenizer* t) {
   };
   auto str = [&]() -> std::string {
     const uint64_t n = rd(8);
-    if (!ok || off + n > size) { ok = false; return std::string(); }
+    if (!ok || n > size - off) { ok = false; return std::string(); }  // (off + n could wrap)
     std::string s((const char*)p + off, n);
     off += n;
     return s;
