@@ -15,6 +15,7 @@ import pytest
 
 import test_chat_template as tct
 import tokenizer_files as tf
+from test_loader_fuzz import gguf_fields, mutate_gguf_field
 
 ROOT = Path(__file__).resolve().parents[1]
 HOST = ROOT / "yallma3-mini-inference_b200" / "csrc" / "host"
@@ -128,7 +129,10 @@ def test_tokenizer_files_under_sanitizers(harness, tmp_path):
     bpath = Path(tf.write_tokenizer_bin_vocab(tmp_path / "b" / "tokenizer.bin", vocab, [0.0] * len(vocab), 1, 2))
     r = random.Random(21)
     paths = [gguf]
-    for i, data in enumerate(_mutations(gguf.read_bytes(), r, 300)):
+    raw = gguf.read_bytes()
+    fields = gguf_fields(raw)
+    muts = _mutations(raw, r, 300) + [mutate_gguf_field(raw, fields, r) for _ in range(300)]
+    for i, data in enumerate(muts):
         p = tmp_path / f"m{i}.gguf"
         p.write_bytes(data)
         paths.append(p)

@@ -44,14 +44,14 @@ struct Cursor {
   }
   std::string str() {
     uint64_t n = rd(8);
-    if (!ok || off + n > size) { ok = false; return ""; }
+    if (!ok || n > size - off) { ok = false; return ""; }  // (off + n could wrap)
     std::string s((const char*)p + off, n);
     off += n;
     return s;
   }
   void skip_str() {
     uint64_t n = rd(8);
-    if (!ok || off + n > size) { ok = false; return; }
+    if (!ok || n > size - off) { ok = false; return; }
     off += n;
   }
   // GGUF value of type t (transformer_llama_gguf.rs:80-107). Arrays keep only
@@ -265,7 +265,8 @@ int model_load_gguf(const char* path, uint32_t max_ctx_len, int fmt_override, in
   };
   for (auto& kv : tmap) {
     const uint64_t nb = bytes_of(kv.second.type, kv.second.n);
-    if (nb == 0 || kv.second.off + nb > mp.size) return fail(YL_ERR_FORMAT, "tensor out of file bounds: " + kv.first);
+    if (nb == 0 || kv.second.off > mp.size || nb > mp.size - kv.second.off)  // (off + nb could wrap)
+      return fail(YL_ERR_FORMAT, "tensor out of file bounds: " + kv.first);
   }
   auto get = [&](const std::string& nm, const TInfo** out_ti) -> int {
     auto it = tmap.find(nm);

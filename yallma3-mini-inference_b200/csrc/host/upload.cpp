@@ -151,6 +151,12 @@ int Uploader::f32(const float* src, uint64_t n, float** out) {
 }
 
 int check_device_shape(const yl_shape& s, int tp_size) {
+  // bounds far above any real model that keep every size the loaders compute
+  // from a file's header (sums of rows x cols over the layers) clear of
+  // 64-bit overflow
+  if (s.dim > (1u << 20) || s.hidden_dim > (1u << 22) || s.vocab_size > (1u << 23) || s.n_layers > 4096 ||
+      s.n_heads > 4096)
+    return fail(YL_ERR_UNSUPPORTED, "model shape beyond the supported bounds (dim, ffn, vocabulary, layers, heads)");
   if (s.dim % 32 || s.hidden_dim % 32 || s.head_size % 32 || s.n_kv_heads == 0 || s.n_heads % s.n_kv_heads)
     return fail(YL_ERR_UNSUPPORTED, "device path needs dim, ffn and head_size multiples of 32 and GQA grouping");
   if (s.head_size != 64 && s.head_size != 128) return fail(YL_ERR_UNSUPPORTED, "head_size must be 64 or 128");
