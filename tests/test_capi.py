@@ -122,3 +122,31 @@ def test_infer_ffi_error_paths_without_gpu(tmp_path):
         "print('ok')\n")
     r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=300)
     assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stdout + r.stderr
+
+
+def test_matmul_size_checks_do_not_wrap(tmp_path):
+    """yl_matmul checks batch * n against the activation length without 64-bit
+    wrap-around and refuses batches beyond 32 bits, before any CUDA call: a
+    batch whose product with n wraps to a small number gets YL_ERR_ARG. Run
+    with no visible GPU on descriptors whose device pointers are placeholders
+    (never dereferenced on this path)."""
+    import os
+    import subprocess
+    import sys
+    code = (
+        "import importlib, sys, ctypes as C\n"
+        f"sys.path.insert(0, {str(ROOT)!r})\n"
+        "yl = importlib.import_module('yallma3-mini-inference_b200')\n"
+        "lib = yl.raw_lib()\n"
+        "n, o = 96, 64\n"
+        "w = yl.QTensorC(fmt=0, scale_type=1, len=o * n, gs=32, rows=o, cols=n, scale_stride=n // 32,\n"
+        "                quant=0x1000, scale=0x2000, owned=0, flags=0)\n"
+        "x = yl.QTensorC(fmt=0, scale_type=1, len=4 * n, gs=32, rows=0, cols=0, scale_stride=0,\n"
+        "                quant=0x3000, scale=0x4000, owned=0, flags=0)\n"
+        "for batch in ((1 << 64) // n + 1, 1 << 32, (1 << 63) + 3, 5):\n"
+        "    rc = lib.yl_matmul(C.c_void_p(0x5000), C.byref(x), C.byref(w), n, o, 32, batch, 0, None)\n"
+        "    assert rc == -1, (batch, rc, yl.last_error())\n"
+        "print('ok')\n")
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="")
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=300, env=env)
+    assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stdout + r.stderr

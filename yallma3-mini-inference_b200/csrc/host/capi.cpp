@@ -256,8 +256,9 @@ int yl_matmul(float* out, const yl_qtensor* x, const yl_qtensor* w, uint64_t n, 
   if (x->rows != 0) return fail(YL_ERR_ARG, "x must be an activation tensor");
   if (w->rows != o || w->cols != n) return fail(YL_ERR_ARG, "w shape does not match (o, n)");
   if (gs != 32 || w->gs != 32) return fail(YL_ERR_UNSUPPORTED, "device matmul uses group size 32");
-  if (batch * n > x->len) return fail(YL_ERR_ARG, "x is shorter than batch * n");
   if (batch == 0 || o == 0) return YL_OK;
+  if (n == 0 || batch > 0xFFFFFFFFull) return fail(YL_ERR_ARG, "n must be positive and batch below 2^32");
+  if (batch > x->len / n) return fail(YL_ERR_ARG, "x is shorter than batch * n");  // (batch * n could wrap)
   DevWeight dw;
   dw.fmt = w->fmt;
   dw.sf16 = w->scale_type == YL_SCALE_F16;
@@ -301,6 +302,8 @@ int check_attention_args(const float* output, const float* sq, const float* kc, 
                          uint32_t start_pos, uint64_t kv_dim) {
   if (!output || !sq || !kc || !vc) return fail(YL_ERR_ARG, "null pointer");
   if (batch == 0) return fail(YL_ERR_ARG, "empty batch");
+  if (batch > 0xFFFFFFFFull || seq_len > 0xFFFFFFFFull || n_heads > 0xFFFFull || kv_dim > 0xFFFFFFFFull)
+    return fail(YL_ERR_ARG, "batch, seq_len or kv_dim beyond 32 bits, or more than 65535 heads");
   if (head_size != 64 && head_size != 128) return fail(YL_ERR_UNSUPPORTED, "head_size must be 64 or 128");
   if (n_kv_heads == 0 || n_heads % n_kv_heads || n_heads / n_kv_heads > 8)
     return fail(YL_ERR_UNSUPPORTED, "n_heads must be a multiple (at most 8x) of n_kv_heads");
