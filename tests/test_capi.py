@@ -146,6 +146,9 @@ def test_matmul_size_checks_do_not_wrap(tmp_path):
         "for batch in ((1 << 64) // n + 1, 1 << 32, (1 << 63) + 3, 5):\n"
         "    rc = lib.yl_matmul(C.c_void_p(0x5000), C.byref(x), C.byref(w), n, o, 32, batch, 0, None)\n"
         "    assert rc == -1, (batch, rc, yl.last_error())\n"
+        "t = yl.QTensorC()\n"
+        "for fmt in (0, 2):  # an activation length whose byte count would wrap\n"
+        "    assert lib.yl_qtensor_alloc(fmt, (1 << 62) + 4, 32, C.byref(t)) == -1, yl.last_error()\n"
         "print('ok')\n")
     env = dict(os.environ, CUDA_VISIBLE_DEVICES="")
     r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=300, env=env)

@@ -45,6 +45,7 @@ static uint64_t w_row_bytes(int fmt, uint64_t cols) {
 int yl_qtensor_alloc(int fmt, uint64_t len, uint64_t gs, yl_qtensor* out) {
   if (!out || gs == 0) return fail(YL_ERR_ARG, "null output or zero group size");
   if (fmt != YL_Q8_0 && fmt != YL_Q4_0 && fmt != YL_F16) return fail(YL_ERR_ARG, "unknown format");
+  if (len > (1ull << 40)) return fail(YL_ERR_ARG, "len too large");  // (len * 4 must not wrap)
   yl_qtensor t{};
   t.fmt = fmt;
   t.scale_type = YL_SCALE_F32;
