@@ -439,6 +439,7 @@ uint64_t yl_model_device_bytes(const yl_model* m) { return m ? m->m->device_byte
 int yl_get_embeddings_batch(const yl_model* m, const uint32_t* tokens, uint64_t n, float* out) {
   if (!m || (!tokens && n) || (!out && n)) return fail(YL_ERR_ARG, "null argument");
   if (n == 0) return YL_OK;
+  if (n > 0xFFFFFFFFull) return fail(YL_ERR_ARG, "more than 2^32 - 1 tokens");
   const Model* mm = m->m;
   const uint32_t d = mm->shape.dim;
   YL_CUDA_TRY(cudaSetDevice(mm->device));
