@@ -153,3 +153,16 @@ def test_matmul_size_checks_do_not_wrap(tmp_path):
     env = dict(os.environ, CUDA_VISIBLE_DEVICES="")
     r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=300, env=env)
     assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stdout + r.stderr
+
+
+def test_config_set_keys(yl):
+    """yl_config_set: the documented keys are accepted (and restored), an
+    unknown key is YL_ERR_ARG; no GPU needed."""
+    for key, value, default in (("gemm", 0, 1), ("gemm_tc", 1, 0), ("gemm_tc_min", 128, 96),
+                                ("gemm_f16_min", 0, 16), ("gemm_f16_min", 32, 16)):
+        yl.config_set(key, value)
+        yl.config_set(key, default)
+    import pytest
+    with pytest.raises(yl.YlError) as e:
+        yl.config_set("no_such_option", 1)
+    assert e.value.code == -1
