@@ -427,8 +427,8 @@ int yl_tokenizer_render_chat(const yl_tokenizer* t, const char* const* roles, co
  * YL_ERR_FORMAT where minijinja fails (syntax; an undefined value under
  * attribute access or arithmetic; an unknown filter, test, function or method;
  * a type error), YL_ERR_UNSUPPORTED for a construct this renderer does not
- * implement (floats, macros, call / filter / with / raw blocks, includes, the
- * less common builtin filters), YL_ERR_ARG for text that is not UTF-8.
+ * implement (floats, macros, call / filter / with blocks, includes, the less
+ * common builtin filters), YL_ERR_ARG for text that is not UTF-8.
  * Parsing and rendering run on an internal thread with an 8 MiB stack and
  * bound nesting (more than ~250 nested parentheses, expressions deeper than
  * 1000 nodes, blocks nested more than 200 deep: YL_ERR_FORMAT). */

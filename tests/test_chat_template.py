@@ -113,6 +113,17 @@ def test_render_matches_jinja(yl, name):
     assert sum(r is not None and r != "" for r in rendered) >= 4  # most cases render something
 
 
+@pytest.mark.parametrize("template", [
+    "a {% raw %}{{ x }} {% if %}{# c #}{% endraw %} b",
+    "a {%- raw -%}  {{ y }}  {%- endraw -%}  b",
+    "{% raw %}{% endraw %}|{% raw %} {% endraw %}|",
+    "{% for m in messages %}{% raw %}<{{ m }}>{% endraw %}{{ m.role }}{% endfor %}",
+    "x {% raw %}  {%- if -%}  {% endraw -%}   y",  # markers inside the raw text are text
+])
+def test_raw_blocks_match_jinja(yl, template):
+    _both(yl, template, [("user", "hi"), ("assistant", "ok")], True)
+
+
 def test_render_known_values(yl):
     r = yl.render_chat_template(T_BLOCKS, [("user", "hi")], True)
     assert r == "<|im_start|>user\nhi<|im_end|>\n<|im_start|>assistant\n"
@@ -140,7 +151,8 @@ def test_render_known_values(yl):
     ("{{ 7 / 2 }}", UNSUPPORTED),
     ("{% macro f() %}x{% endmacro %}{{ f() }}", UNSUPPORTED),
     ("{{ messages | tojson }}", UNSUPPORTED),
-    ("{% raw %}{{ x }}{% endraw %}", UNSUPPORTED),
+    ("{% raw %}never closed", FORMAT),
+    ("{% endraw %}", FORMAT),
     ("{{ 'É' | lower }}", UNSUPPORTED),
 ])
 def test_render_errors(yl, template, code):

@@ -50,7 +50,7 @@ def run(harness, *args):
 def test_chat_templates_under_sanitizers(harness, tmp_path):
     base = [tct.T_BLOCKS, tct.T_HEADERS, tct.T_HEADERS_NO_GEN, tct.T_EXPR, tct.T_SPACE]
     base += [t for t, _ in [("{{ bos_token + 'x' }}", 0), ("{{ messages[0].content.strip() }}", 0),
-                            ("{% if true %}open", 0), ("{{ 'unterminated }}", 0), ("{% raw %}{{ x }}{% endraw %}", 0)]]
+                            ("{% if true %}open", 0), ("{{ 'unterminated }}", 0), ("{% raw %}{{ x }}{% endraw %}", 0), ("{%- raw -%} a {%- endraw %}", 0)]]
     base += [tct._Gen(s).template() for s in range(600)]
     r = random.Random(5)
     junk = ["{{", "}}", "{%", "%}", "{#", "#}", "-", "+", "'", '"', "\\", "(", ")", "[", "]", "|", ".", ":",

@@ -19,8 +19,8 @@
 // tuple and map literals; names, attributes, subscripts, slices with steps,
 // calls of range / namespace / dict; operators `if else`, or, and, not,
 // comparisons, in, not in, + - * // % ** ~, unary minus; filters and tests as
-// listed in apply_filter / run_test. Floats, macros, call / filter / with /
-// raw blocks, includes and the remaining builtin filters give
+// listed in apply_filter / run_test; raw blocks. Floats, macros, call /
+// filter / with blocks, includes and the remaining builtin filters give
 // YL_ERR_UNSUPPORTED.
 #include "chat_template.h"
 
@@ -703,9 +703,39 @@ std::vector<Piece> split_template(std::string src) {
     std::string inner = src.substr(j, end - j);
     if (!inner.empty() && inner.back() == '-') { inner.pop_back(); lstrip_next = true; }
     else if (!inner.empty() && inner.back() == '+') inner.pop_back();
+    p = end + 2;
+    if (kind == '%' && trim_ws(inner, true, true) == "raw") {
+      // {% raw %}: the text up to the next {% endraw %} is literal
+      size_t e = p, e_end = std::string::npos;
+      bool e_lstrip = false, e_rstrip = false;
+      while ((e = src.find("{%", e)) != std::string::npos) {
+        size_t k = e + 2;
+        const bool ls = k < src.size() && src[k] == '-';
+        if (k < src.size() && (src[k] == '-' || src[k] == '+')) ++k;
+        const size_t c = src.find("%}", k);
+        if (c == std::string::npos) break;
+        std::string w = src.substr(k, c - k);
+        const bool rs = !w.empty() && w.back() == '-';
+        if (!w.empty() && (w.back() == '-' || w.back() == '+')) w.pop_back();
+        if (trim_ws(w, true, true) == "endraw") {
+          e_end = c + 2;
+          e_lstrip = ls;
+          e_rstrip = rs;
+          break;
+        }
+        e += 2;
+      }
+      if (e_end == std::string::npos) bad("missing endraw");
+      std::string body = src.substr(p, e - p);
+      if (lstrip_next) body = trim_ws(body, true, false);
+      if (e_lstrip) body = trim_ws(body, false, true);
+      if (!body.empty()) out.push_back({Piece::TEXT, body});
+      lstrip_next = e_rstrip;
+      p = e_end;
+      continue;
+    }
     if (kind == '{') out.push_back({Piece::VAR, inner});
     else if (kind == '%') out.push_back({Piece::STMT, inner});
-    p = end + 2;
   }
 }
 
@@ -716,7 +746,7 @@ std::string parse_body(const std::vector<Piece>& ps, size_t* i, const std::vecto
                        std::unique_ptr<Parser>* stop_p, int depth = 0) {
   if (depth > kMaxBlocks) bad("blocks nested too deeply");
   static const char* kUnsupported[] = {"macro", "endmacro", "call", "endcall", "filter", "endfilter", "with",
-                                       "endwith", "raw", "endraw", "include", "import", "from", "extends", "block",
+                                       "endwith", "include", "import", "from", "extends", "block",
                                        "endblock", "autoescape", "endautoescape", "do", "break", "continue",
                                        "endset"};
   while (*i < ps.size()) {
