@@ -114,6 +114,7 @@ def test_render_matches_jinja(yl, name):
 
 
 @pytest.mark.parametrize("template", [
+    "{% for m in messages %}{{ loop.cycle('odd', 'even') }}-{{ loop.cycle(1, 2, 3) }} {% endfor %}",
     "a {% raw %}{{ x }} {% if %}{# c #}{% endraw %} b",
     "a {%- raw -%}  {{ y }}  {%- endraw -%}  b",
     "{% raw %}{% endraw %}|{% raw %} {% endraw %}|",
@@ -121,7 +122,7 @@ def test_render_matches_jinja(yl, name):
     "x {% raw %}  {%- if -%}  {% endraw -%}   y",  # markers inside the raw text are text
 ])
 def test_raw_blocks_match_jinja(yl, template):
-    _both(yl, template, [("user", "hi"), ("assistant", "ok")], True)
+    _both(yl, template, [("user", "hi"), ("assistant", "ok"), ("user", "again")], True)
 
 
 def test_render_known_values(yl):

@@ -1165,7 +1165,11 @@ Val call(const Expr& e, Ctx& c) {
   if (f.k == Expr::ATTR) {
     const Val obj = eval(*f.a[0], c);
     if (obj.k == Val::UNDEF) bad("method '" + f.name + "' of an undefined value");
-    if (obj.tag == Val::LOOP && (f.name == "cycle" || f.name == "changed")) unsup("loop." + f.name);
+    if (obj.tag == Val::LOOP && f.name == "cycle") {  // the argument at index0 modulo their count
+      if (args.empty()) bad("loop.cycle needs arguments");
+      return args[(size_t)map_find(*obj.m, "index0")->i % args.size()];
+    }
+    if (obj.tag == Val::LOOP && f.name == "changed") unsup("loop.changed");
     bad(std::string("unknown method ") + kind_name(obj) + "." + f.name + "()");
   }
   if (f.k == Expr::NAME && c.lookup(f.name).k == Val::UNDEF) {
