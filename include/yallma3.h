@@ -411,6 +411,24 @@ int yl_tokenizer_decode(const yl_tokenizer* t, const uint32_t* ids, uint64_t n, 
  * Template errors as yl_chat_template_render. */
 int yl_tokenizer_chat_prompt(const yl_tokenizer* t, const char* system, const char* user, uint32_t* ids,
                              uint64_t cap, uint64_t* n_out);
+/* The pieces the prompt above is made of, as the reference's Tokenizer has
+ * them. encode_wrap_n_header (tokenizer.rs:277-297): with a Llama-3 vocabulary
+ * [<|begin_of_text|>] if wrap, the header in <|start_header_id|> ..
+ * <|end_header_id|> "\n\n" if non-empty, the text, ["\n\n", <|eot_id|>] if
+ * wrap; otherwise [BOS] if wrap and add_bos_token, then the text. */
+int yl_tokenizer_encode_wrap_n_header(const yl_tokenizer* t, const char* text, const char* header,
+                                      int begin_of_text_wrap, uint32_t* ids, uint64_t cap, uint64_t* n_out);
+/* set_chat_template (tokenizer.rs:408-416): parses and installs a chat
+ * template (errors as yl_chat_template_render's parse step; on an error the
+ * tokenizer is unchanged, where the reference panics). Not concurrently with
+ * other calls on the same tokenizer. */
+int yl_tokenizer_set_chat_template(yl_tokenizer* t, const char* tmpl);
+/* apply_system_template (tokenizer.rs:477-495) and
+ * apply_turn_template(user, add_empty_assistant) (:497-539). */
+int yl_tokenizer_apply_system_template(const yl_tokenizer* t, const char* system, uint32_t* ids, uint64_t cap,
+                                       uint64_t* n_out);
+int yl_tokenizer_apply_turn_template(const yl_tokenizer* t, const char* user, int add_empty_assistant, uint32_t* ids,
+                                     uint64_t cap, uint64_t* n_out);
 /* Tokenizer::render_chat_template (tokenizer.rs:418-436): the chat template
  * rendered with {messages: [{role, content}] x n_messages,
  * add_generation_prompt}, then encode_template_output (:438-473): at each '<'

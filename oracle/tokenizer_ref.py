@@ -253,34 +253,50 @@ class Tokenizer:
         text = render_chat_template_text(self.chat_template, messages, add_generation_prompt)
         return self.encode_template_output(text) if text else []
 
-    def chat_prompt(self, user: str, system: str = "") -> list[int]:
-        """The console's fresh prompt (main.rs:149-153, :177): with a chat
-        template, [bos] then apply_turn_template(user, true) (tokenizer.rs:496-508)
-        (a given system prompt rendered in between, apply_system_template
-        :476-482); without one, apply_system_template + apply_turn_template,
-        no-template branches (tokenizer.rs:453-521)"""
+    def encode_wrap_n_header(self, text: str, header: str, wrap: bool) -> list[int]:
+        """tokenizer.rs:277-297"""
+        return self._wrap_n_header(text, header, wrap)
+
+    def set_chat_template(self, template: str) -> None:
+        """tokenizer.rs:408-416 (jinja2 parses it here, as minijinja would)"""
+        render_chat_template_text(template, [], False)
+        self.chat_template = template
+
+    def apply_system_template(self, system: str) -> list[int]:
+        """tokenizer.rs:477-495"""
         if self.chat_template is not None:
-            t = [self.bos] if self.add_bos_token else []
-            if system:
-                t += self.render_chat([("system", system)], False)
-            turn = self.render_chat([("user", user), ("assistant", "")], True)
-            if turn and turn[-1] == 128009:
-                turn.pop()
-            return t + turn
+            return self.render_chat([("system", system)], False)
         if self.has_llama_tokens():
-            t = self._wrap_n_header(system, "system", True)
-        else:
-            t = self.encode(system) if system else []
+            return self._wrap_n_header(system, "system", True)
+        return self.encode(system) if system else []
+
+    def apply_turn_template(self, user: str, add_empty_assistant: bool) -> list[int]:
+        """tokenizer.rs:497-539"""
+        if self.chat_template is not None:
+            msgs = [("user", user)] + ([("assistant", "")] if add_empty_assistant else [])
+            out = self.render_chat(msgs, add_empty_assistant)
+            if add_empty_assistant and out and out[-1] == 128009:
+                out.pop()
+            return out
         if self.has_llama_tokens():
             u, a = self.encode("user"), self.encode("assistant")
             assert len(u) == 1 and len(a) == 1
-            t += [128006, u[0], 128007, 271] + self._wrap_n_header(user, "", False) + [128009]
-            t += [128006, a[0], 128007, 271]
+            t = [128006, u[0], 128007, 271] + self._wrap_n_header(user, "", False) + [128009]
+            return t + ([128006, a[0], 128007, 271] if add_empty_assistant else [])
+        return ([self.bos] if self.add_bos_token else []) + self.encode(user)
+
+    def chat_prompt(self, user: str, system: str = "") -> list[int]:
+        """The console's fresh prompt (main.rs:149-153, :173): with a chat
+        template [bos] (and a given system prompt's apply_system_template),
+        without one apply_system_template(system); then
+        apply_turn_template(user, true)"""
+        if self.chat_template is not None:
+            t = [self.bos] if self.add_bos_token else []
+            if system:
+                t += self.apply_system_template(system)
         else:
-            if self.add_bos_token:
-                t.append(self.bos)
-            t += self.encode(user)
-        return t
+            t = self.apply_system_template(system)
+        return t + self.apply_turn_template(user, True)
 
 
 class _MiniJinjaDefaults(SandboxedEnvironment):

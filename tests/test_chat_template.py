@@ -462,3 +462,41 @@ def test_random_expressions_match_jinja(yl):
             assert gerr is None and got == want, (seed, t, want, got, gerr)
             agreed += 1
     assert agreed > 300, (agreed, errors)
+
+
+@pytest.mark.parametrize("big", [False, True])
+def test_tokenizer_template_pieces_match_restatement(yl, tmp_path, bpe, big):
+    """encode_wrap_n_header, apply_system_template, apply_turn_template (with
+    and without the empty assistant turn) and set_chat_template, each against
+    the restatement of tokenizer.rs:277-539, on a tokenizer without and then
+    with a template."""
+    vocab, merges = bpe
+    if big:
+        path = tf.write_gguf_tokenizer(tmp_path / "b.gguf", tf.llama_vocab(vocab), merges, 128000, 128009)
+        template = T_HEADERS_NO_GEN
+    else:
+        path = tf.write_gguf_tokenizer(tmp_path / "s.gguf", vocab + ["<|im_start|>", "<|im_end|>"], merges, 1, 2,
+                                       add_bos=True)
+        template = T_BLOCKS
+    ours, ref = yl.Tokenizer.load(path), tr.Tokenizer.from_gguf(path)
+
+    def compare():
+        for text in ["hello world", "what's 3.14?", "日本 <b>"]:
+            for header in ["", "system", "user"]:
+                for wrap in (False, True):
+                    assert ours.encode_wrap_n_header(text, header, wrap) == ref.encode_wrap_n_header(text, header, wrap)
+            assert ours.apply_system_template(text) == ref.apply_system_template(text)
+            for add in (False, True):
+                assert ours.apply_turn_template(text, add) == ref.apply_turn_template(text, add), (text, add)
+            assert ours.chat_prompt(text, system="sys") == ref.chat_prompt(text, system="sys")
+        assert ours.apply_system_template("") == ref.apply_system_template("")
+
+    compare()
+    assert not ours.info()["has_template"]
+    with pytest.raises(yl.YlError) as e:
+        ours.set_chat_template("{% if %}")  # does not parse: the tokenizer stays as it was
+    assert e.value.code == FORMAT and not ours.info()["has_template"]
+    ours.set_chat_template(template)
+    ref.set_chat_template(template)
+    assert ours.info()["has_template"]
+    compare()

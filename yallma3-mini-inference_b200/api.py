@@ -133,6 +133,11 @@ _sigs = {
     "yl_tokenizer_decode": (C.c_int, [_P, _P, C.c_uint64, _P, C.c_uint64, C.POINTER(C.c_uint64)]),
     "yl_tokenizer_chat_prompt": (C.c_int, [_P, C.c_char_p, C.c_char_p, _P, C.c_uint64, C.POINTER(C.c_uint64)]),
     "yl_tokenizer_render_chat": (C.c_int, [_P, _P, _P, C.c_uint64, C.c_int, _P, C.c_uint64, C.POINTER(C.c_uint64)]),
+    "yl_tokenizer_encode_wrap_n_header": (C.c_int, [_P, C.c_char_p, C.c_char_p, C.c_int, _P, C.c_uint64,
+                                                    C.POINTER(C.c_uint64)]),
+    "yl_tokenizer_set_chat_template": (C.c_int, [_P, C.c_char_p]),
+    "yl_tokenizer_apply_system_template": (C.c_int, [_P, C.c_char_p, _P, C.c_uint64, C.POINTER(C.c_uint64)]),
+    "yl_tokenizer_apply_turn_template": (C.c_int, [_P, C.c_char_p, C.c_int, _P, C.c_uint64, C.POINTER(C.c_uint64)]),
     "yl_chat_template_render": (C.c_int, [C.c_char_p, _P, _P, C.c_uint64, C.c_int, _P, C.c_uint64,
                                           C.POINTER(C.c_uint64)]),
     "yl_sampler_create": (C.c_int, [C.c_uint32, C.c_float, C.c_float, C.c_uint64, C.POINTER(_P)]),
@@ -598,6 +603,19 @@ class Tokenizer:
 
     def chat_prompt(self, user: str, system: str = "") -> list:
         return self._ids(_lib.yl_tokenizer_chat_prompt, system.encode(), user.encode())
+
+    def encode_wrap_n_header(self, text: str, header: str, begin_of_text_wrap: bool) -> list:
+        return self._ids(_lib.yl_tokenizer_encode_wrap_n_header, text.encode(), header.encode(),
+                         1 if begin_of_text_wrap else 0)
+
+    def set_chat_template(self, template: str) -> None:
+        _check(_lib.yl_tokenizer_set_chat_template(self._h, template.encode()))
+
+    def apply_system_template(self, system: str) -> list:
+        return self._ids(_lib.yl_tokenizer_apply_system_template, system.encode())
+
+    def apply_turn_template(self, user: str, add_empty_assistant: bool) -> list:
+        return self._ids(_lib.yl_tokenizer_apply_turn_template, user.encode(), 1 if add_empty_assistant else 0)
 
     def render_chat(self, messages: Sequence[tuple], add_generation_prompt: bool) -> list:
         """Tokenizer::render_chat_template: messages are (role, content) pairs."""

@@ -209,6 +209,38 @@ int yl_tokenizer_chat_prompt(const yl_tokenizer* t, const char* system, const ch
   return copy_ids(v, ids, cap, n_out);
 }
 
+int yl_tokenizer_encode_wrap_n_header(const yl_tokenizer* t, const char* text, const char* header,
+                                      int begin_of_text_wrap, uint32_t* ids, uint64_t cap, uint64_t* n_out) {
+  if (!t || !text || !header) return fail(YL_ERR_ARG, "null argument");
+  std::vector<uint32_t> v;
+  int rc = yl::tok_encode_wrap_n_header(t->t, text, header, begin_of_text_wrap != 0, &v);
+  if (rc) return rc;
+  return copy_ids(v, ids, cap, n_out);
+}
+
+int yl_tokenizer_set_chat_template(yl_tokenizer* t, const char* tmpl) {
+  if (!t || !tmpl) return fail(YL_ERR_ARG, "null argument");
+  return yl::tok_set_chat_template(&t->t, tmpl);
+}
+
+int yl_tokenizer_apply_system_template(const yl_tokenizer* t, const char* system, uint32_t* ids, uint64_t cap,
+                                       uint64_t* n_out) {
+  if (!t || !system) return fail(YL_ERR_ARG, "null argument");
+  std::vector<uint32_t> v;
+  int rc = yl::tok_apply_system_template(t->t, system, &v);
+  if (rc) return rc;
+  return copy_ids(v, ids, cap, n_out);
+}
+
+int yl_tokenizer_apply_turn_template(const yl_tokenizer* t, const char* user, int add_empty_assistant, uint32_t* ids,
+                                     uint64_t cap, uint64_t* n_out) {
+  if (!t || !user) return fail(YL_ERR_ARG, "null argument");
+  std::vector<uint32_t> v;
+  int rc = yl::tok_apply_turn_template(t->t, user, add_empty_assistant != 0, &v);
+  if (rc) return rc;
+  return copy_ids(v, ids, cap, n_out);
+}
+
 static int gather_messages(const char* const* roles, const char* const* contents, uint64_t n,
                            yl::ChatMessages* out) {
   if (n && (!roles || !contents)) return fail(YL_ERR_ARG, "null message arrays");

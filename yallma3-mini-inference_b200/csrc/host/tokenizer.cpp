@@ -646,30 +646,44 @@ int tok_render_chat(const Tokenizer& t, const std::vector<std::pair<std::string,
   return tok_encode_template_output(t, text, out);
 }
 
-int tok_chat_prompt(const Tokenizer& t, const std::string& system, const std::string& user,
-                    std::vector<uint32_t>* out) {
+int tok_encode_wrap_n_header(const Tokenizer& t, const std::string& text, const std::string& header, bool wrap,
+                             std::vector<uint32_t>* out) {
+  out->clear();
+  return wrap_n_header(t, text, header, wrap, out);
+}
+
+int tok_set_chat_template(Tokenizer* t, const std::string& tmpl) {
+  std::shared_ptr<const ChatTemplate> ct;
+  const int rc = chat_template_parse(tmpl, &ct);
+  if (rc) return rc;  // the reference panics here; the tokenizer is left as it was
+  t->has_template = true;
+  t->chat_template = tmpl;
+  t->tmpl = ct;
+  t->tmpl_rc = 0;
+  t->tmpl_err.clear();
+  return YL_OK;
+}
+
+int tok_apply_system_template(const Tokenizer& t, const std::string& system, std::vector<uint32_t>* out) {
+  out->clear();
+  if (t.has_template) return tok_render_chat(t, {{"system", system}}, false, out);
+  if (t.has_llama_tokens()) return wrap_n_header(t, system, "system", true, out);
+  if (system.empty()) return YL_OK;
+  return tok_encode(t, system, false, false, out);
+}
+
+int tok_apply_turn_template(const Tokenizer& t, const std::string& user, bool add_empty_assistant,
+                            std::vector<uint32_t>* out) {
   out->clear();
   int rc;
-  std::vector<uint32_t> e;
   if (t.has_template) {
-    if (t.add_bos_token) out->push_back(t.bos);
-    if (!system.empty()) {
-      if ((rc = tok_render_chat(t, {{"system", system}}, false, &e))) return rc;
-      out->insert(out->end(), e.begin(), e.end());
-    }
-    if ((rc = tok_render_chat(t, {{"user", user}, {"assistant", ""}}, true, &e))) return rc;
-    if (!e.empty() && e.back() == 128009u) e.pop_back();  // Tokenizer::EOT
-    out->insert(out->end(), e.begin(), e.end());
+    std::vector<std::pair<std::string, std::string>> msgs = {{"user", user}};
+    if (add_empty_assistant) msgs.push_back({"assistant", ""});
+    if ((rc = tok_render_chat(t, msgs, add_empty_assistant, out))) return rc;
+    if (add_empty_assistant && !out->empty() && out->back() == 128009u) out->pop_back();  // Tokenizer::EOT
     return YL_OK;
   }
-  // apply_system_template, no-template branch (tokenizer.rs:453-471)
-  if (t.has_llama_tokens()) {
-    if ((rc = wrap_n_header(t, system, "system", true, out))) return rc;
-  } else if (!system.empty()) {
-    if ((rc = tok_encode(t, system, false, false, &e))) return rc;
-    out->insert(out->end(), e.begin(), e.end());
-  }
-  // apply_turn_template(user, true), no-template branch (tokenizer.rs:492-520)
+  std::vector<uint32_t> e;
   if (t.has_llama_tokens()) {
     std::vector<uint32_t> uid, aid;
     if ((rc = tok_encode(t, "user", false, false, &uid))) return rc;
@@ -679,12 +693,31 @@ int tok_chat_prompt(const Tokenizer& t, const std::string& system, const std::st
     out->insert(out->end(), {128006u, uid[0], 128007u, 271u});
     if ((rc = wrap_n_header(t, user, "", false, out))) return rc;
     out->push_back(128009u);
-    out->insert(out->end(), {128006u, aid[0], 128007u, 271u});
-  } else {
-    if (t.add_bos_token) out->push_back(t.bos);
-    if ((rc = tok_encode(t, user, false, false, &e))) return rc;
-    out->insert(out->end(), e.begin(), e.end());
+    if (add_empty_assistant) out->insert(out->end(), {128006u, aid[0], 128007u, 271u});
+    return YL_OK;
   }
+  if (t.add_bos_token) out->push_back(t.bos);
+  if ((rc = tok_encode(t, user, false, false, &e))) return rc;
+  out->insert(out->end(), e.begin(), e.end());
+  return YL_OK;
+}
+
+int tok_chat_prompt(const Tokenizer& t, const std::string& system, const std::string& user,
+                    std::vector<uint32_t>* out) {
+  out->clear();
+  int rc;
+  std::vector<uint32_t> e;
+  if (t.has_template) {  // main.rs:149-153: [BOS] instead of the system template
+    if (t.add_bos_token) out->push_back(t.bos);
+    if (!system.empty()) {
+      if ((rc = tok_apply_system_template(t, system, &e))) return rc;
+      out->insert(out->end(), e.begin(), e.end());
+    }
+  } else if ((rc = tok_apply_system_template(t, system, out))) {
+    return rc;
+  }
+  if ((rc = tok_apply_turn_template(t, user, true, &e))) return rc;  // main.rs:173
+  out->insert(out->end(), e.begin(), e.end());
   return YL_OK;
 }
 

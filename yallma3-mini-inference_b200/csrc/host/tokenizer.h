@@ -64,6 +64,18 @@ int tok_render_chat(const Tokenizer& t, const std::vector<std::pair<std::string,
 // vocabulary entry that matches there becomes one id; the text up to the next
 // '<' goes through encode(text, false, false).
 int tok_encode_template_output(const Tokenizer& t, const std::string& text, std::vector<uint32_t>* out);
+// Tokenizer::encode_wrap_n_header (tokenizer.rs:277-297).
+int tok_encode_wrap_n_header(const Tokenizer& t, const std::string& text, const std::string& header, bool wrap,
+                             std::vector<uint32_t>* out);
+// Tokenizer::set_chat_template (tokenizer.rs:408-416): parses and installs a
+// template; on a parse error the tokenizer is left unchanged (the reference
+// panics).
+int tok_set_chat_template(Tokenizer* t, const std::string& tmpl);
+// Tokenizer::apply_system_template (tokenizer.rs:477-495).
+int tok_apply_system_template(const Tokenizer& t, const std::string& system, std::vector<uint32_t>* out);
+// Tokenizer::apply_turn_template (tokenizer.rs:497-539).
+int tok_apply_turn_template(const Tokenizer& t, const std::string& user, bool add_empty_assistant,
+                            std::vector<uint32_t>* out);
 // The prompt of one fresh conversation as the reference's console builds it.
 // Without a chat template (main.rs:149-153, :177): apply_system_template of
 // the system prompt, then apply_turn_template(user, true), no-template
