@@ -5,6 +5,7 @@
 //   sanitize_harness tokenizer <gguf> <file>     texts separated by byte 0x01
 //   sanitize_harness load <file>                 model paths, one per line: tokenizer_load
 //                                                 (errors expected), then one encode
+//   sanitize_harness json <file>                 JSON documents separated by byte 0x01
 #include <cstdio>
 #include <cstring>
 #include <exception>
@@ -16,6 +17,7 @@
 #include <vector>
 
 #include "../yallma3-mini-inference_b200/csrc/host/chat_template.h"
+#include "../yallma3-mini-inference_b200/csrc/host/json.h"
 #include "../yallma3-mini-inference_b200/csrc/host/tokenizer.h"
 
 namespace yl {
@@ -107,6 +109,17 @@ int main(int argc, char** argv) {
     printf("files %d loaded %d\n", n, loaded);
     return 0;
   }
-  fprintf(stderr, "usage: sanitize_harness templates <file> | tokenizer <gguf> <file> | load <file>\n");
+  if (argc >= 3 && !strcmp(argv[1], "json")) {
+    int n = 0, parsed = 0;
+    for (const std::string& doc : split(read_file(argv[2]), std::string(1, '\x01'))) {
+      yl::Json j;
+      std::string err;
+      parsed += yl::json_parse(doc.data(), doc.size(), &j, &err);
+      ++n;
+    }
+    printf("documents %d parsed %d\n", n, parsed);
+    return 0;
+  }
+  fprintf(stderr, "usage: sanitize_harness templates <file> | tokenizer <gguf> <file> | load <file> | json <file>\n");
   return 2;
 }

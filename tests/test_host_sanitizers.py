@@ -146,3 +146,32 @@ def test_tokenizer_files_under_sanitizers(harness, tmp_path):
     lst.write_text("\n".join(str(p) for p in paths))
     out = run(harness, "load", lst)
     assert int(out.split()[1]) == len(paths) and int(out.split()[3]) >= 1
+
+
+def test_json_under_sanitizers(harness, tmp_path):
+    """The JSON reader (config.json, tokenizer.json, safetensors headers) on
+    valid documents and mutations of them: escapes, surrogate pairs and lone
+    surrogates, numbers at the edges, nesting past the reader's limit."""
+    import json
+    r = random.Random(31)
+    base = [json.dumps({"a": [1, 2.5, -3e-7, True, None, "x\u00e9\ud83d\ude00"], "b": {"c": "\\\"/\b\f\n\r\t"}}),
+            '{"hidden_size": 4096, "rope_scaling": {"factor": 8.0, "rope_type": "llama3"}, "x": 1e308, "y": -0}',
+            "[" * 70 + "]" * 70, "[" * 20 + "{}" + "]" * 20, '"\\ud800"', '"\\udc00x"', "18446744073709551616",
+            "-9223372036854775809", "1.7976931348623157e309", '{"a":1,"a":2}', "[1,]", "{,}", '"unterminated']
+    docs = list(base)
+    junk = ["{", "}", "[", "]", ",", ":", '"', "\\", "\\u", "\\ud83d", "e", "-", ".", "0", "9", "null", "tru"]
+    for _ in range(3000):
+        t = r.choice(base)
+        i = r.randrange(len(t) + 1)
+        op = r.randint(0, 2)
+        if op == 0:
+            t = t[:i]
+        elif op == 1:
+            t = t[:i] + r.choice(junk) + t[i:]
+        else:
+            t = t[:i] + t[i + 1:]
+        docs.append(t)
+    f = tmp_path / "docs.bin"
+    f.write_bytes(b"\x01".join(d.encode("utf-8", "surrogatepass") for d in docs))
+    out = run(harness, "json", f)
+    assert int(out.split()[1]) == len(docs) and int(out.split()[3]) >= 3
