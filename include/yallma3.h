@@ -362,8 +362,10 @@ bool load_transformer_ffi(const char* model_path);
  * returned as a malloc'ed UTF-8 string to be released with free_string.
  * NULL on any error (no model loaded, empty (after trimming) or non-UTF-8 prompt, prompt longer
  * than the context; yl_last_error() says which). Calls are serialized by a
- * mutex; the session and the sampler persist across calls like the console's
- * (the session is reset at each call, the sampler keeps its state). */
+ * mutex. Every call is a fresh conversation: the session's buffers persist
+ * but its cache is reset, whereas the console continues one conversation
+ * across turns (main.rs:223-226 never resets its only session); the sampler
+ * keeps its state across calls, as the console's does. */
 const char* infer_ffi(const char* prompt);
 void free_string(const char* s);
 /* Sampling of infer_ffi. Defaults are the console's Sampler::new(vocab, 0.7,
