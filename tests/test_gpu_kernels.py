@@ -181,7 +181,7 @@ def test_sweep_vs_oracle(yl, orc, torch_cuda, mk, batch, fmt):
 
 
 @pytest.mark.parametrize("mk", [(2048, 2048), (1000, 4096)])
-@pytest.mark.parametrize("batch", [1, 5, 16, 33, 64])  # 16+: the f16 tensor-core GEMM (all three tiles)
+@pytest.mark.parametrize("batch", [1, 5, 16, 24, 33, 64])  # 16+: the f16 tensor-core GEMM (16-, 32- and 64-token tiles)
 def test_f16_vs_oracle(yl, orc, torch_cuda, mk, batch):
     o, n = mk
     rng = np.random.default_rng(o + n + batch)
