@@ -368,9 +368,9 @@ int yl_load_transformer(const char* path, int sequential, uint32_t max_ctx_len, 
   if (fmt_override < -1 || fmt_override > YL_F16) return fail(YL_ERR_ARG, "bad format override");
   Model* m = nullptr;
   int rc;
-  if (ext == "gguf") rc = model_load_gguf(path, max_ctx_len, fmt_override, 0, 1, &m);
-  else if (ext == "safetensors") rc = model_load_st(path, max_ctx_len, fmt_override, &m);
-  else if (ext == "lmrs") rc = model_load_lmrs(path, max_ctx_len, fmt_override, &m);
+  if (ext == "gguf") rc = guarded([&] { return model_load_gguf(path, max_ctx_len, fmt_override, 0, 1, &m); });
+  else if (ext == "safetensors") rc = guarded([&] { return model_load_st(path, max_ctx_len, fmt_override, &m); });
+  else if (ext == "lmrs") rc = guarded([&] { return model_load_lmrs(path, max_ctx_len, fmt_override, &m); });
   else return fail(YL_ERR_ARG, "Unsupported model extension for path: " + p);
   if (rc) return rc;
   *out = new yl_model{m};
@@ -384,7 +384,7 @@ int yl_load_transformer_tp(const char* path, uint32_t max_ctx_len, int fmt_overr
   if (p.size() < 5 || p.substr(p.size() - 5) != ".gguf") return fail(YL_ERR_ARG, "tensor-parallel load needs a .gguf");
   if (fmt_override < -1 || fmt_override > YL_F16) return fail(YL_ERR_ARG, "bad format override");
   Model* m = nullptr;
-  int rc = model_load_gguf(path, max_ctx_len, fmt_override, tp_rank, tp_size, &m);
+  int rc = guarded([&] { return model_load_gguf(path, max_ctx_len, fmt_override, tp_rank, tp_size, &m); });
   if (rc) return rc;
   *out = new yl_model{m};
   return YL_OK;
@@ -858,7 +858,7 @@ static int ffi_generate(const char* prompt_in, std::string* reply) {
 const char* infer_ffi(const char* prompt) {
   std::lock_guard<std::mutex> lk(g_ffi_mu);
   std::string reply;
-  if (ffi_generate(prompt, &reply) != YL_OK) return nullptr;
+  if (guarded([&] { return ffi_generate(prompt, &reply); }) != YL_OK) return nullptr;
   char* out = (char*)malloc(reply.size() + 1);
   if (!out) {
     fail(YL_ERR_OOM, "reply buffer");

@@ -4,6 +4,8 @@
 
 #include <cstdint>
 #include <cstring>
+#include <exception>
+#include <new>
 #include <string>
 
 #include "../../../include/yallma3.h"
@@ -13,6 +15,22 @@ namespace yl {
 // Thread-local message behind yl_last_error().
 void set_error(const std::string& msg);
 int fail(int code, const std::string& msg);
+
+// Runs f (which returns a yl status) so that no C++ exception crosses the
+// C-ABI into the host: a failed host allocation becomes YL_ERR_OOM, any other
+// exception YL_ERR_FORMAT.
+template <class F>
+int guarded(F&& f) {
+  try {
+    return f();
+  } catch (const std::bad_alloc&) {
+    return fail(YL_ERR_OOM, "host memory allocation failed");
+  } catch (const std::exception& e) {
+    return fail(YL_ERR_FORMAT, std::string("unexpected error: ") + e.what());
+  } catch (...) {
+    return fail(YL_ERR_FORMAT, "unexpected error");
+  }
+}
 
 // IEEE binary16 <-> binary32 (round to nearest even on narrowing).
 inline float f16_to_f32(uint16_t h) {

@@ -14,6 +14,7 @@
 #include "tokenizer.h"
 
 using yl::fail;
+using yl::guarded;
 
 struct yl_sampler {
   int device = 0;
@@ -149,7 +150,7 @@ int yl_sampler_result(yl_sampler* s, uint32_t* id_out) {
 int yl_tokenizer_load(const char* model_path, yl_tokenizer** out) {
   if (!model_path || !out) return fail(YL_ERR_ARG, "null argument");
   std::unique_ptr<yl::Tokenizer> t;
-  int rc = yl::tokenizer_load(model_path, &t);
+  int rc = guarded([&] { return yl::tokenizer_load(model_path, &t); });
   if (rc) return rc;
   auto* h = new yl_tokenizer();
   h->t = std::move(*t);
@@ -182,7 +183,7 @@ int yl_tokenizer_encode(const yl_tokenizer* t, const char* text, int bos, int eo
                         uint64_t* n_out) {
   if (!t || !text) return fail(YL_ERR_ARG, "null argument");
   std::vector<uint32_t> v;
-  int rc = yl::tok_encode(t->t, text, bos != 0, eos != 0, &v);
+  int rc = guarded([&] { return yl::tok_encode(t->t, text, bos != 0, eos != 0, &v); });
   if (rc) return rc;
   return copy_ids(v, ids, cap, n_out);
 }
@@ -190,7 +191,12 @@ int yl_tokenizer_encode(const yl_tokenizer* t, const char* text, int bos, int eo
 int yl_tokenizer_decode(const yl_tokenizer* t, const uint32_t* ids, uint64_t n, char* out, uint64_t cap,
                         uint64_t* n_out) {
   if (!t || (!ids && n)) return fail(YL_ERR_ARG, "null argument");
-  const std::string s = yl::tok_decode(t->t, ids, (size_t)n);
+  std::string s;
+  const int rc = guarded([&] {
+    s = yl::tok_decode(t->t, ids, (size_t)n);
+    return YL_OK;
+  });
+  if (rc) return rc;
   if (n_out) *n_out = s.size();
   if (s.size() + 1 > cap) return fail(YL_ERR_RANGE, "output buffer too small");
   if (out) {
@@ -204,7 +210,7 @@ int yl_tokenizer_chat_prompt(const yl_tokenizer* t, const char* system, const ch
                              uint64_t cap, uint64_t* n_out) {
   if (!t || !user) return fail(YL_ERR_ARG, "null argument");
   std::vector<uint32_t> v;
-  int rc = yl::tok_chat_prompt(t->t, system ? system : "", user, &v);
+  int rc = guarded([&] { return yl::tok_chat_prompt(t->t, system ? system : "", user, &v); });
   if (rc) return rc;
   return copy_ids(v, ids, cap, n_out);
 }
