@@ -513,7 +513,7 @@ int yl_model_weight(const yl_model* m, uint32_t layer, int which, yl_qtensor* ou
 int yl_create_session(const yl_model* m, yl_session** out) {
   if (!m || !out) return fail(YL_ERR_ARG, "null argument");
   Session* s = nullptr;
-  int rc = session_create(m->m, &s);
+  int rc = guarded([&] { return session_create(m->m, &s); });
   if (rc) return rc;
   *out = new yl_session{s};
   return YL_OK;
@@ -533,7 +533,7 @@ uint32_t yl_session_pos(const yl_session* s) { return s ? s->s->pos : 0; }
 int yl_batch_create(const yl_model* m, uint32_t max_sessions, yl_batch** out) {
   if (!m || !out) return fail(YL_ERR_ARG, "null argument");
   Batch* b = nullptr;
-  int rc = batch_create(m->m, max_sessions, &b);
+  int rc = guarded([&] { return batch_create(m->m, max_sessions, &b); });
   if (rc) return rc;
   *out = new yl_batch{b};
   return YL_OK;

@@ -219,21 +219,21 @@ int yl_tokenizer_encode_wrap_n_header(const yl_tokenizer* t, const char* text, c
                                       int begin_of_text_wrap, uint32_t* ids, uint64_t cap, uint64_t* n_out) {
   if (!t || !text || !header) return fail(YL_ERR_ARG, "null argument");
   std::vector<uint32_t> v;
-  int rc = yl::tok_encode_wrap_n_header(t->t, text, header, begin_of_text_wrap != 0, &v);
+  int rc = guarded([&] { return yl::tok_encode_wrap_n_header(t->t, text, header, begin_of_text_wrap != 0, &v); });
   if (rc) return rc;
   return copy_ids(v, ids, cap, n_out);
 }
 
 int yl_tokenizer_set_chat_template(yl_tokenizer* t, const char* tmpl) {
   if (!t || !tmpl) return fail(YL_ERR_ARG, "null argument");
-  return yl::tok_set_chat_template(&t->t, tmpl);
+  return guarded([&] { return yl::tok_set_chat_template(&t->t, tmpl); });
 }
 
 int yl_tokenizer_apply_system_template(const yl_tokenizer* t, const char* system, uint32_t* ids, uint64_t cap,
                                        uint64_t* n_out) {
   if (!t || !system) return fail(YL_ERR_ARG, "null argument");
   std::vector<uint32_t> v;
-  int rc = yl::tok_apply_system_template(t->t, system, &v);
+  int rc = guarded([&] { return yl::tok_apply_system_template(t->t, system, &v); });
   if (rc) return rc;
   return copy_ids(v, ids, cap, n_out);
 }
@@ -242,7 +242,7 @@ int yl_tokenizer_apply_turn_template(const yl_tokenizer* t, const char* user, in
                                      uint64_t cap, uint64_t* n_out) {
   if (!t || !user) return fail(YL_ERR_ARG, "null argument");
   std::vector<uint32_t> v;
-  int rc = yl::tok_apply_turn_template(t->t, user, add_empty_assistant != 0, &v);
+  int rc = guarded([&] { return yl::tok_apply_turn_template(t->t, user, add_empty_assistant != 0, &v); });
   if (rc) return rc;
   return copy_ids(v, ids, cap, n_out);
 }
@@ -265,7 +265,7 @@ int yl_tokenizer_render_chat(const yl_tokenizer* t, const char* const* roles, co
   int rc = gather_messages(roles, contents, n_messages, &msgs);
   if (rc) return rc;
   std::vector<uint32_t> v;
-  if ((rc = yl::tok_render_chat(t->t, msgs, add_generation_prompt != 0, &v))) return rc;
+  if ((rc = guarded([&] { return yl::tok_render_chat(t->t, msgs, add_generation_prompt != 0, &v); }))) return rc;
   return copy_ids(v, ids, cap, n_out);
 }
 
