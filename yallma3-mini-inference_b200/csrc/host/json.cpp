@@ -228,7 +228,9 @@ struct Parser {
 }  // namespace
 
 bool json_parse(const char* text, size_t n, Json* out, std::string* err) {
-  Parser ps{text, n};
+  Parser ps;
+  ps.p = text;
+  ps.n = n;
   *out = Json();
   bool ok = ps.value(out);
   if (ok) {
